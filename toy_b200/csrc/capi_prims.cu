@@ -1,0 +1,64 @@
+// C ABI for the device-pointer primitives (tb2_gemm, tb2_split_f32, ...).
+#include "toy_b200.h"
+#include "gemm.cuh"
+#include "kernels.cuh"
+#include "runtime.cuh"
+
+namespace {
+tb2::Operand to_op(const tb2_operand* o) {
+  tb2::Operand r;
+  r.hi = static_cast<const __nv_bfloat16*>(o->hi);
+  r.lo = static_cast<const __nv_bfloat16*>(o->lo);
+  r.mn_major = o->mn_major;
+  r.ld = o->ld;
+  r.rows = o->rows;
+  r.cols = o->cols;
+  r.batch_stride = o->batch_stride;
+  r.nbatch = o->nbatch;
+  r.bdiv1 = o->bdiv1 > 0 ? o->bdiv1 : 1;
+  r.bmul1 = o->bmul1;
+  r.bdiv2 = o->bdiv2 > 0 ? o->bdiv2 : 1;
+  r.bmul2 = o->bmul2;
+  return r;
+}
+}  // namespace
+
+extern "C" {
+
+int tb2_gemm(int M, int N, int K, int batch, int split, const tb2_operand* a, const tb2_operand* b,
+             const tb2_epilogue* epi, void* stream) {
+  if (!a || !b || !epi) return -1;
+  tb2::GemmDesc d;
+  d.M = M; d.N = N; d.K = K; d.batch = batch; d.split = split != 0;
+  d.a = to_op(a);
+  d.b = to_op(b);
+  tb2::Epilogue& e = d.epi;
+  e.mode = epi->mode;
+  e.alpha = epi->alpha;
+  e.out = epi->out;
+  e.res = epi->res;
+  e.out_hi = static_cast<__nv_bfloat16*>(epi->out_hi);
+  e.out_lo = static_cast<__nv_bfloat16*>(epi->out_lo);
+  e.bstride = epi->bstride;
+  e.m_div = epi->m_div > 0 ? epi->m_div : (1 << 30);
+  e.m_s1 = epi->m_s1;
+  e.m_s0 = epi->m_s0;
+  e.n_div = epi->n_div > 0 ? epi->n_div : (1 << 30);
+  e.n_s1 = epi->n_s1;
+  int* err = tb2::device_error_word();
+  if (!err) return -3;
+  const int rc = tb2::gemm_launch(d, err, static_cast<cudaStream_t>(stream));
+  return rc == 0 ? 0 : (rc <= -10 ? -3 : -1);
+}
+
+int tb2_split_f32(const float* x, void* hi, void* lo, size_t n, void* stream) {
+  if (!x || !hi || !lo) return -1;
+  return tb2::launch_split_f32(x, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo), (long long)n,
+                               static_cast<cudaStream_t>(stream));
+}
+
+int tb2_device_error(void) { return tb2::read_and_clear_device_error(); }
+
+const char* tb2_version(void) { return "toy_b200 0.1 (sm_100a)"; }
+
+}  // extern "C"
