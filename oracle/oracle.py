@@ -350,7 +350,9 @@ def cross_entropy_loss(logits, labels):
 
 
 def cross_entropy_loss_back(logits, labels, dloss=1.0):
-    """tinynn/ab_smoke_cegrad.rb:1-3: dz = (softmax(z) - y) * dloss / N."""
+    """tinynn/ab_smoke_cegrad.rb:1-3: dz = (softmax(z) - y) * dloss / N, for every
+    row: a row with no target (label -1, an all-zero one-hot row) still gets
+    softmax(z) / N, exactly as ggml's CROSS_ENTROPY_LOSS_BACK computes it."""
     N = logits.shape[0]
     p = softmax(logits)
     if labels.ndim == 1:
