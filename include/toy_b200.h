@@ -49,7 +49,8 @@ typedef struct tb2_operand {
 
 /* Epilogue: mode 0 store f32, 1 accumulate f32, 2 residual (out = res + acc),
  * 3 store split-bf16 planes, 4 store f32 and split planes. Output element
- * (z, m, n) is at z*bstride + (m/m_div)*m_s1 + (m%m_div)*m_s0 + (n/n_div)*n_s1 + n%n_div. */
+ * (z, m, n) is at (z/z_div)*z_s1 + (z%z_div)*bstride + (m/m_div)*m_s1 + (m%m_div)*m_s0
+ * + (n/n_div)*n_s1 + n%n_div (a divisor <= 0 means "no split"). */
 typedef struct tb2_epilogue {
   int mode;
   float alpha;
@@ -58,6 +59,8 @@ typedef struct tb2_epilogue {
   void *out_hi;
   void *out_lo;
   long long bstride;
+  int z_div;
+  long long z_s1;
   int m_div;
   long long m_s1, m_s0;
   int n_div;
@@ -75,12 +78,137 @@ int tb2_gemm(int M, int N, int K, int batch, int split, const tb2_operand *a, co
 /* hi = rn_bf16(x), lo = rn_bf16(x - hi) for n f32 values. */
 int tb2_split_f32(const float *x, void *hi, void *lo, size_t n, void *stream);
 
+/* f32 [rows][K] -> Q8_0 blocks [rows][K/32*34] (ggml quantize_row_q8_0_ref:
+ * d = amax/127 as fp16, q = round-half-away(x * (1/d)); bit-exact).
+ * The quantiser behind tnn_cpy into a Q8_0 tensor (tinynn/ab_smoke_q8_kv.rb). */
+int tb2_q8_0_quantize(const float *x, void *q, long long rows, int K, void *stream);
+/* Q8_0 blocks -> split-bf16 planes (and exact f32 values when f32 != NULL). */
+int tb2_q8_0_dequantize(const void *q, void *hi, void *lo, float *f32, long long rows, int K, void *stream);
+
 /* Read and clear the device-side error word of the current device
  * (non-zero when a kernel's bounded wait gave up). Synchronises the device. */
 int tb2_device_error(void);
 
 /* Library version string. */
 const char *tb2_version(void);
+
+/* ===================================================================== */
+/* Sessions (tinynn/tinynn_ggml.h:47-66)                                 */
+/* ===================================================================== */
+
+/* backend_kind must be 1 (CUDA); this library has no CPU path and returns
+ * NULL (with a message on stderr) for any other kind instead of falling back.
+ * Replaces tnn_session_new / tnn_session_new_on (tinynn/tinynn_ggml.h:47,60). */
+void *tnn_session_new(int backend_kind);
+void *tnn_session_new_on(int backend_kind, int device);
+/* tinynn/tinynn_ggml.h:63 */
+int tnn_cuda_get_device_count(void);
+/* Frees every tensor and device buffer of the session (tinynn/tinynn_ggml.h:64). */
+void tnn_session_free(void *sess);
+/* tinynn/tinynn_ggml.h:89 */
+const char *tnn_backend_name(void *sess);
+/* Returns 73 (tinynn/tinynn_ggml.h:90). */
+int tnn_link_check(void);
+
+/* ===================================================================== */
+/* Training engine: the graph LlamaSeqEngine builds (llama_seq_engine.rb) */
+/* ===================================================================== */
+
+#define TB2_MODE_FULL_FINETUNE 0 /* every weight trainable f32 (FromScratch / full fine-tune) */
+#define TB2_MODE_QLORA 1         /* frozen Q8_0 base + trainable LoRA adapters (LoRA / QLoRA) */
+
+#define TB2_LORA_Q (1 << 0)
+#define TB2_LORA_K (1 << 1)
+#define TB2_LORA_V (1 << 2)
+#define TB2_LORA_O (1 << 3)
+#define TB2_LORA_GATE (1 << 4)
+#define TB2_LORA_UP (1 << 5)
+#define TB2_LORA_DOWN (1 << 6)
+
+typedef struct tb2_llama_config {
+  int vocab, d_model, n_heads, n_kv, d_head, d_ff, n_layers;
+  double rope_base, rms_eps, freq_scale;
+  int tied, qkv_bias;
+  int t_seq, t_batch;
+  int mode;
+  int lora_rank;
+  double lora_alpha;
+  int lora_targets;
+  const double *rope_freq_factors; /* d_head/2 llama3 factors or NULL */
+} tb2_llama_config;
+
+/* Realize the forward + cross-entropy + backward + AdamW program for a Llama
+ * decoder on the session's GPU: allocates weights, Adam moments, activations.
+ * Coarse replacement for LlamaSeqEngine#realize_for_random_init / realize_for_mmap
+ * + build_training_step (lib/toy/llm/engine/llama_seq_engine.rb:932,713,1786). */
+int tb2_llama_realize(void *sess, const tb2_llama_config *cfg);
+
+/* Seeded weights in the reference's draw order (upload_random_init!,
+ * llama_seq_engine.rb:1161-1340). std_all > 0 draws every tensor from N(0, std_all)
+ * (the frozen base of a QLoRA config, quantised to Q8_0 on upload); LoRA A/B
+ * follow from the same stream with the given standard deviations. */
+int tb2_llama_init_random(void *sess, long long seed, double init_scale, double std_all, double lora_a_std,
+                          double lora_b_std);
+
+#define TB2_IO_TOKEN_IDS 0
+#define TB2_IO_POSITIONS 1
+#define TB2_IO_LABELS 2
+#define TB2_IO_HP 3
+#define TB2_IO_LOSS 4
+#define TB2_IO_COUNT 5
+/* The step's input/output tensors (the handles build_training_step returns and
+ * the engine's t_seq_token_ids / t_seq_positions, llama_seq_engine.rb:1786-1958). */
+void *tb2_llama_io(void *sess, int which);
+/* Parameter tensor view by GGUF-style name (e.g. "blk.0.attn_q.weight",
+ * "blk.3.attn_v.lora_a"); upload/download through the tnn_* I/O calls. */
+void *tb2_llama_param(void *sess, const char *name);
+int tb2_llama_n_params(void *sess);
+const char *tb2_llama_param_name(void *sess, int i);
+int tb2_llama_param_trainable(void *sess, const char *name);
+long long tb2_llama_n_trainable(void *sess);
+int tb2_param_grad_to_f64(void *sess, const char *name, double *dst, size_t n);
+/* which = 0: first moment m, 1: second moment v. */
+int tb2_param_moment_to_f64(void *sess, const char *name, int which, double *dst, size_t n);
+/* Raw Q8_0 blocks (34 bytes per 32 values) of a frozen projection, byte-exact
+ * (the bytes tinynn/tinynn_gguf.c copies verbatim from a GGUF file). */
+int tb2_param_upload_q8_0(void *sess, const char *name, const void *blocks, size_t nbytes);
+int tb2_param_download_q8_0(void *sess, const char *name, void *blocks, size_t nbytes);
+/* Index fast path for the labels tensor: one target id per token, -1 = none.
+ * Equivalent to uploading the one-hot [T*B, vocab] matrix. */
+int tb2_upload_label_ids(void *sess, void *labels_tensor, const long *ids, size_t n);
+/* Kernels launched by the last eagerly enqueued step (a graph replay launches the same set). */
+int tb2_step_launches(void *sess);
+int tb2_set_use_graph(void *sess, int on);
+int tb2_forward_only(void *sess);
+int tb2_sync(void *sess);
+/* Copy a saved activation of the last step to host f32 (for layer-by-layer
+ * parity checks): which = 0 x_in, 1 x_after_attn, 2 attn_norm out, 3 Q (head-major,
+ * roped), 4 K, 5 V, 6 softmax probs, 7 attention out, 8 gate|up, 9 swiglu out,
+ * 10 logits, 11 ffn_norm out. Returns the element count (cap too small: nothing copied). */
+long long tb2_debug_activation(void *sess, int which, int layer, float *dst, long long cap);
+
+/* tinynn/tinynn_ggml.h:424 — the next tnn_compute_backward zeroes the Adam moments. */
+int tnn_graph_reset(void *sess);
+/* tinynn/tinynn_ggml.h:419 — gradients are overwritten by every backward; no-op. */
+int tnn_graph_reset_grads_only(void *sess);
+/* tinynn/tinynn_ggml.h:425 — forward, CE, backward and AdamW in one call. */
+int tnn_compute_backward(void *sess);
+
+/* ===================================================================== */
+/* Tensor I/O (tinynn/tinynn_ggml.h:486-537)                             */
+/* ===================================================================== */
+int tnn_upload_from_float_array(void *sess, void *tensor, const double *data, size_t n);
+int tnn_upload_from_int_array(void *sess, void *tensor, const long *data, size_t n);
+int tnn_download_to_f64_array(void *sess, void *tensor, double *dst, size_t n);
+int tnn_tensor_ne0(void *t);
+int tnn_tensor_ne1(void *t);
+int tnn_tensor_ne2(void *t);
+int tnn_tensor_ne3(void *t);
+size_t tnn_tensor_nbytes(void *t);
+int tnn_tensor_nelements(void *t);
+const char *tnn_tensor_name(void *t);
+void tnn_tensor_set_name(void *t, const char *name);
+int tnn_tensor_dtype(void *t);
 
 #ifdef __cplusplus
 }

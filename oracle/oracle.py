@@ -472,9 +472,10 @@ def _lora_back(mdl: Model, l: int, p: str, h1, u, dy, grads):
 
 
 def forward_backward(mdl: Model, ids: np.ndarray, pos: np.ndarray, labels: np.ndarray, T: int, B: int,
-                     want_grads: bool = True):
+                     want_grads: bool = True, trace: Optional[dict] = None):
     """Loss and gradients (float64) of one step. ids/pos/labels have T*B entries,
-    token (b, t) at b*T + t; labels are ids (-1 = none) or a dense [N, V] array."""
+    token (b, t) at b*T + t; labels are ids (-1 = none) or a dense [N, V] array.
+    When `trace` is a dict it receives the per-layer forward caches and logits."""
     cfg, P = mdl.cfg, mdl.params
     N, d, H, KV, dh, G = T * B, cfg.d_model, cfg.n_heads, cfg.n_kv, cfg.d_head, cfg.group
     eps = cfg.rms_eps
@@ -544,6 +545,8 @@ def forward_backward(mdl: Model, ids: np.ndarray, pos: np.ndarray, labels: np.nd
     W_out = E if cfg.tied else f64("output.weight")
     logits = xf @ W_out.T
     loss = cross_entropy_loss(logits, labels)
+    if trace is not None:
+        trace.update(layers=caches, logits=logits, x_final=x)
     if not want_grads:
         return loss, {}, logits
     grads: Dict[str, np.ndarray] = {}

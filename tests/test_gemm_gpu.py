@@ -38,7 +38,7 @@ def _epi(mode, out=None, ldc=0, res=None, hi=None, lo=None, bstride=0, alpha=1.0
     e.res = res.data_ptr() if res is not None else None
     e.out_hi = hi.data_ptr() if hi is not None else None
     e.out_lo = lo.data_ptr() if lo is not None else None
-    e.bstride, e.m_div, e.m_s1, e.m_s0, e.n_div, e.n_s1 = bstride, 0, 0, ldc, 0, 0
+    e.bstride, e.z_div, e.z_s1, e.m_div, e.m_s1, e.m_s0, e.n_div, e.n_s1 = bstride, 0, 0, 0, 0, ldc, 0, 0
     return e
 
 
@@ -57,7 +57,8 @@ def _relerr(x, ref):
 
 
 @pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (1, 0), (0, 1), (1, 1)])
-@pytest.mark.parametrize("M,N,K", [(256, 384, 320), (200, 576, 576), (128, 64, 4096), (384, 960, 64)])
+@pytest.mark.parametrize("M,N,K", [(256, 384, 320), (200, 576, 576), (128, 64, 4096), (384, 960, 64),
+                                   (128, 512, 128), (256, 1536, 576), (128, 256, 64), (64, 32, 32), (128, 128, 96)])
 def test_gemm_majors(cuda, a_mn, b_mn, M, N, K):
     import torch
     g = torch.Generator(device="cuda").manual_seed(M * 7 + N * 3 + K)

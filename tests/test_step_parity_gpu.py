@@ -1,0 +1,145 @@
+"""Whole-step parity of the CUDA path (through the C ABI) against the oracle.
+
+Tolerances (the training-step contract): loss within 1e-4 relative; per-tensor
+gradients, post-AdamW weights and Adam moments within 1e-3 relative L2; Q8_0
+bytes, token/label indexing and the seeded init streams bit-exact.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+LOSS_TOL = 1e-4
+REL_L2 = 1e-3
+
+
+def rel(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    nb = np.linalg.norm(b)
+    return np.linalg.norm(a - b) / (nb if nb > 0 else 1.0)
+
+
+def tiny_cfgs():
+    from toy_b200 import LlamaConfig
+    oc = O.LlamaCfg(vocab=512, d_model=128, n_heads=4, n_kv=2, d_head=32, d_ff=256, n_layers=2, rope_base=1e4)
+    gc = LlamaConfig(512, 128, 4, 2, 32, 256, 2, 1e4, 1e-5)
+    return oc, gc
+
+
+def inputs(cfg, T, B, seed=5):
+    ids = O.token_ids(seed, T * B, cfg.vocab)
+    return ids, O.positions(T, B), O.next_token_labels(ids, T, B, cfg.vocab)
+
+
+def compare_step(eng, mdl, loss_gpu, loss_ref, grads_ref, check_grads=True):
+    assert abs(loss_gpu - loss_ref) <= LOSS_TOL * abs(loss_ref), (loss_gpu, loss_ref)
+    worst = []
+    for k in mdl.trainable:
+        if check_grads:
+            r = rel(eng.grad(k), grads_ref[k].reshape(eng.grad(k).shape))
+            worst.append((r, "grad " + k))
+            assert r < REL_L2, ("grad", k, r)
+        rp = rel(eng.param(k), mdl.params[k].reshape(eng.param(k).shape))
+        assert rp < REL_L2, ("param", k, rp)
+        for w, ref in ((0, mdl.m[k]), (1, mdl.v[k])):
+            rm = rel(eng.moment(k, w), ref.reshape(eng.moment(k, w).shape))
+            assert rm < REL_L2, ("moment", w, k, rm)
+    return sorted(worst)[-3:]
+
+
+@pytest.fixture(scope="module")
+def full_pair(cuda):
+    from toy_b200 import FromScratch, RecipeOptions
+    oc, gc = tiny_cfgs()
+    T, B = 64, 2
+    rec = FromScratch()
+    rec.realize(gc, RecipeOptions(t_seq=T, t_batch=B, seed=3, init_scale=1.0))
+    mdl = O.full_ft_model(oc, seed=3, init_scale=1.0)
+    return rec, mdl, oc, T, B
+
+
+def test_full_ft_init_bit_exact(full_pair):
+    rec, mdl, oc, T, B = full_pair
+    eng = rec.fs_cache
+    for k, v in mdl.params.items():
+        got = eng.param(k).astype(np.float32).reshape(v.shape)
+        assert np.array_equal(got.view(np.uint32), v.view(np.uint32)), k
+
+
+def test_full_ft_two_steps(full_pair):
+    rec, mdl, oc, T, B = full_pair
+    eng = rec.fs_cache
+    ids, pos, lab = inputs(oc, T, B)
+    hp1 = O.hp_lora(1e-3, 1, wd=0.01)
+    loss_g = rec.step(ids, pos, lab, hp1, True)
+    loss_r, grads = O.train_step(mdl, ids, pos, lab, T, B, hp1, True)
+    compare_step(eng, mdl, loss_g, loss_r, grads)
+    ids2, pos2, lab2 = inputs(oc, T, B, seed=9)
+    lab2[7] = -1
+    hp2 = O.hp_lora(1e-3, 2, wd=0.01)
+    loss_g = rec.step(ids2, pos2, lab2, hp2, False)
+    loss_r, grads = O.train_step(mdl, ids2, pos2, lab2, T, B, hp2, False)
+    compare_step(eng, mdl, loss_g, loss_r, grads)
+
+
+@pytest.mark.parametrize("targets", [("q", "v"), ("q", "k", "v", "o", "gate", "up", "down")])
+def test_qlora_step(cuda, targets):
+    from toy_b200 import LoRA, LoraOptions, RecipeOptions
+    oc, gc = tiny_cfgs()
+    T, B = 64, 2
+    rec = LoRA()
+    lo = LoraOptions(rank=8, alpha=16.0, targets=targets, a_std=0.125, b_std=0.01, base_std=0.02)
+    rec.realize(gc, 8, RecipeOptions(t_seq=T, t_batch=B, seed=11), lo)
+    mdl = O.qlora_model(oc, O.LoraCfg(rank=8, alpha=16.0, targets=targets, a_std=0.125, b_std=0.01), seed=11,
+                        base_std=0.02)
+    eng = rec.lora_cache
+    # Q8_0 blocks of the frozen base and the adapter init are bit-exact
+    for k, blocks in mdl.q8.items():
+        assert np.array_equal(eng.q8_0_blocks(k).reshape(-1), blocks.reshape(-1)), k
+    for k in mdl.trainable:
+        got = eng.param(k).astype(np.float32).reshape(mdl.params[k].shape)
+        assert np.array_equal(got, mdl.params[k]), k
+    ids, pos, lab = inputs(oc, T, B)
+    for step in (1, 2):
+        hp = O.hp_lora(1e-4, step, wd=0.01)
+        loss_g = rec.step(ids, pos, lab, hp, step == 1)
+        loss_r, grads = O.train_step(mdl, ids, pos, lab, T, B, hp, step == 1)
+        compare_step(eng, mdl, loss_g, loss_r, grads)
+
+
+def test_dense_labels_match_index_labels(cuda):
+    from toy_b200 import FromScratch, RecipeOptions
+    oc, gc = tiny_cfgs()
+    T, B = 64, 1
+    ids, pos, lab = inputs(oc, T, B)
+    lab[3] = -1
+    onehot = np.zeros((T * B, oc.vocab))
+    for i, t in enumerate(lab):
+        if t >= 0:
+            onehot[i, t] = 1.0
+    out = []
+    for labels in (lab, onehot):
+        rec = FromScratch()
+        rec.realize(gc, RecipeOptions(t_seq=T, t_batch=B, seed=3))
+        loss = rec.step(ids, pos, labels, O.hp_lora(1e-3, 1), True)
+        out.append((loss, rec.fs_cache.grad("blk.1.ffn_down.weight")))
+    assert abs(out[0][0] - out[1][0]) <= 1e-6 * abs(out[0][0])
+    assert rel(out[1][1], out[0][1]) < 1e-6
+
+
+def test_run_twice_deterministic(cuda):
+    """Graph replay and eager execution give bit-identical results."""
+    from toy_b200 import FromScratch, RecipeOptions
+    oc, gc = tiny_cfgs()
+    T, B = 64, 2
+    ids, pos, lab = inputs(oc, T, B)
+    res = []
+    for _ in range(2):
+        rec = FromScratch()
+        rec.realize(gc, RecipeOptions(t_seq=T, t_batch=B, seed=3))
+        losses = [rec.step(ids, pos, lab, O.hp_lora(1e-3, s + 1), s == 0) for s in range(3)]
+        res.append((losses, rec.fs_cache.param("token_embd.weight"), rec.fs_cache.param("blk.0.attn_q.weight")))
+    assert res[0][0] == res[1][0]
+    assert np.array_equal(res[0][1], res[1][1]) and np.array_equal(res[0][2], res[1][2])

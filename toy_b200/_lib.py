@@ -20,18 +20,72 @@ class Operand(C.Structure):
 
 class Epilogue(C.Structure):
     _fields_ = [("mode", C.c_int), ("alpha", C.c_float), ("out", C.c_void_p), ("res", C.c_void_p),
-                ("out_hi", C.c_void_p), ("out_lo", C.c_void_p), ("bstride", C.c_longlong), ("m_div", C.c_int),
+                ("out_hi", C.c_void_p), ("out_lo", C.c_void_p), ("bstride", C.c_longlong), ("z_div", C.c_int),
+                ("z_s1", C.c_longlong), ("m_div", C.c_int),
                 ("m_s1", C.c_longlong), ("m_s0", C.c_longlong), ("n_div", C.c_int), ("n_s1", C.c_longlong)]
 
 
+class LlamaConfigC(C.Structure):
+    _fields_ = [("vocab", C.c_int), ("d_model", C.c_int), ("n_heads", C.c_int), ("n_kv", C.c_int),
+                ("d_head", C.c_int), ("d_ff", C.c_int), ("n_layers", C.c_int), ("rope_base", C.c_double),
+                ("rms_eps", C.c_double), ("freq_scale", C.c_double), ("tied", C.c_int), ("qkv_bias", C.c_int),
+                ("t_seq", C.c_int), ("t_batch", C.c_int), ("mode", C.c_int), ("lora_rank", C.c_int),
+                ("lora_alpha", C.c_double), ("lora_targets", C.c_int),
+                ("rope_freq_factors", C.POINTER(C.c_double))]
+
+
 _lib = None
+VP, D, DP, LP, SZ, I, LL = C.c_void_p, C.c_double, C.POINTER(C.c_double), C.POINTER(C.c_long), C.c_size_t, C.c_int, \
+    C.c_longlong
 
 # (name, restype, argtypes) for every exported symbol this module binds.
 _SIGS = [
+    ("tnn_session_new", VP, [I]),
+    ("tnn_session_new_on", VP, [I, I]),
+    ("tnn_cuda_get_device_count", I, []),
+    ("tnn_session_free", None, [VP]),
+    ("tnn_backend_name", C.c_char_p, [VP]),
+    ("tnn_link_check", I, []),
+    ("tb2_llama_realize", I, [VP, C.POINTER(LlamaConfigC)]),
+    ("tb2_llama_init_random", I, [VP, LL, D, D, D, D]),
+    ("tb2_llama_io", VP, [VP, I]),
+    ("tb2_llama_param", VP, [VP, C.c_char_p]),
+    ("tb2_llama_n_params", I, [VP]),
+    ("tb2_llama_param_name", C.c_char_p, [VP, I]),
+    ("tb2_llama_param_trainable", I, [VP, C.c_char_p]),
+    ("tb2_llama_n_trainable", LL, [VP]),
+    ("tb2_param_grad_to_f64", I, [VP, C.c_char_p, DP, SZ]),
+    ("tb2_param_moment_to_f64", I, [VP, C.c_char_p, I, DP, SZ]),
+    ("tb2_param_upload_q8_0", I, [VP, C.c_char_p, VP, SZ]),
+    ("tb2_param_download_q8_0", I, [VP, C.c_char_p, VP, SZ]),
+    ("tb2_upload_label_ids", I, [VP, VP, LP, SZ]),
+    ("tb2_step_launches", I, [VP]),
+    ("tb2_set_use_graph", I, [VP, I]),
+    ("tb2_forward_only", I, [VP]),
+    ("tb2_sync", I, [VP]),
+    ("tb2_debug_activation", LL, [VP, I, I, C.POINTER(C.c_float), LL]),
+    ("tnn_graph_reset", I, [VP]),
+    ("tnn_graph_reset_grads_only", I, [VP]),
+    ("tnn_compute_backward", I, [VP]),
+    ("tnn_upload_from_float_array", I, [VP, VP, DP, SZ]),
+    ("tnn_upload_from_int_array", I, [VP, VP, LP, SZ]),
+    ("tnn_download_to_f64_array", I, [VP, VP, DP, SZ]),
+    ("tnn_tensor_ne0", I, [VP]),
+    ("tnn_tensor_ne1", I, [VP]),
+    ("tnn_tensor_ne2", I, [VP]),
+    ("tnn_tensor_ne3", I, [VP]),
+    ("tnn_tensor_nbytes", SZ, [VP]),
+    ("tnn_tensor_nelements", I, [VP]),
+    ("tnn_tensor_name", C.c_char_p, [VP]),
+    ("tnn_tensor_set_name", None, [VP, C.c_char_p]),
+    ("tnn_tensor_dtype", I, [VP]),
     ("tb2_gemm", C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(Operand), C.POINTER(Operand),
                            C.POINTER(Epilogue), C.c_void_p]),
     ("tb2_split_f32", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
     ("tb2_device_error", C.c_int, []),
+    ("tb2_q8_0_quantize", C.c_int, [C.c_void_p, C.c_void_p, C.c_longlong, C.c_int, C.c_void_p]),
+    ("tb2_q8_0_dequantize", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_longlong, C.c_int,
+                                      C.c_void_p]),
     ("tb2_version", C.c_char_p, []),
 ]
 

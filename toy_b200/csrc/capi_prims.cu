@@ -40,6 +40,8 @@ int tb2_gemm(int M, int N, int K, int batch, int split, const tb2_operand* a, co
   e.out_hi = static_cast<__nv_bfloat16*>(epi->out_hi);
   e.out_lo = static_cast<__nv_bfloat16*>(epi->out_lo);
   e.bstride = epi->bstride;
+  e.z_div = epi->z_div > 0 ? epi->z_div : (1 << 30);
+  e.z_s1 = epi->z_s1;
   e.m_div = epi->m_div > 0 ? epi->m_div : (1 << 30);
   e.m_s1 = epi->m_s1;
   e.m_s0 = epi->m_s0;
@@ -55,6 +57,18 @@ int tb2_split_f32(const float* x, void* hi, void* lo, size_t n, void* stream) {
   if (!x || !hi || !lo) return -1;
   return tb2::launch_split_f32(x, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo), (long long)n,
                                static_cast<cudaStream_t>(stream));
+}
+
+int tb2_q8_0_quantize(const float* x, void* q, long long rows, int K, void* stream) {
+  if (!x || !q || rows <= 0 || K <= 0) return -1;
+  return tb2::launch_q8_0_quantize(x, static_cast<uint8_t*>(q), rows, K, static_cast<cudaStream_t>(stream));
+}
+
+int tb2_q8_0_dequantize(const void* q, void* hi, void* lo, float* f32, long long rows, int K, void* stream) {
+  if (!q || !hi || !lo || rows <= 0 || K <= 0) return -1;
+  tb2::Planes p{static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo)};
+  return tb2::launch_q8_0_to_planes(static_cast<const uint8_t*>(q), p, f32, rows, K,
+                                    static_cast<cudaStream_t>(stream));
 }
 
 int tb2_device_error(void) { return tb2::read_and_clear_device_error(); }

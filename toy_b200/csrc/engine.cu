@@ -1,0 +1,998 @@
+// LlamaEngine: allocation, parameter I/O, seeded init and the step program.
+#include "engine.cuh"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <thread>
+
+#include "runtime.cuh"
+
+namespace tb2 {
+
+#define CK(x)                  \
+  do {                         \
+    const int rc_ = (x);       \
+    if (rc_ != 0) return rc_;  \
+  } while (0)
+#define CU(x)                                 \
+  do {                                        \
+    if ((x) != cudaSuccess) return -3;        \
+  } while (0)
+
+namespace {
+
+Operand op(Planes p, int rows, int cols, long long ld, int mn) {
+  Operand o;
+  o.hi = p.hi; o.lo = p.lo; o.mn_major = mn; o.ld = ld; o.rows = rows; o.cols = cols;
+  o.batch_stride = (long long)rows * ld; o.nbatch = 1; o.bdiv1 = 1; o.bmul1 = 0; o.bdiv2 = 1; o.bmul2 = 0;
+  return o;
+}
+
+Operand bop(Planes p, int rows, int cols, long long ld, int nbatch, int mn, int d1 = 1, int m1 = 1, int d2 = 1,
+            int m2 = 0) {
+  Operand o = op(p, rows, cols, ld, mn);
+  o.nbatch = nbatch; o.bdiv1 = d1; o.bmul1 = m1; o.bdiv2 = d2; o.bmul2 = m2;
+  return o;
+}
+
+Planes offset(Planes p, long long off) { return Planes{p.hi + off, p.lo + off}; }
+
+// ---- the reference's host init streams (llama_seq_engine.rb:1383-1428) ----
+constexpr uint64_t kA = 1103515245ULL, kC = 12345ULL, kMask = 0x7FFFFFFFULL;
+
+struct Affine {
+  uint64_t a, c;
+};
+Affine compose(Affine f, Affine g) {  // g after f
+  return Affine{(g.a * f.a) & kMask, (g.a * f.c + g.c) & kMask};
+}
+uint64_t lcg_skip(uint64_t s, unsigned long long k) {
+  Affine acc{1, 0}, step{kA, kC};
+  while (k) {
+    if (k & 1) acc = compose(acc, step);
+    step = compose(step, step);
+    k >>= 1;
+  }
+  return (acc.a * s + acc.c) & kMask;
+}
+uint64_t lcg_next(uint64_t s) { return (s * kA + kC) & kMask; }
+
+uint64_t lcg_seed_state(long long seed) {
+  __int128 v = ((__int128)seed + 104729) * (__int128)2654435761LL;
+  __int128 m = v % 2147483647;
+  if (m < 0) m += 2147483647;
+  long long s = (long long)m;
+  if (s <= 0) s = seed + 104729;
+  uint64_t st = (uint64_t)s;
+  for (int w = 0; w < 8; ++w) st = lcg_next(st);
+  return st;
+}
+
+// upload_gaussian: pairs of uniforms -> Box-Muller (cos, then sin); returns the new state.
+uint64_t gaussian_fill(uint64_t state, float* out, long long n, double stdv) {
+  const long long pairs = (n + 1) / 2;
+  const int nth = (int)std::min<long long>(16, std::max<long long>(1, pairs / 200000));
+  auto work = [&](long long p0, long long p1) {
+    uint64_t s = lcg_skip(state, 2ULL * (unsigned long long)p0);
+    for (long long p = p0; p < p1; ++p) {
+      s = lcg_next(s);
+      double u1 = ((double)s + 1.0) / 2147483648.0;
+      s = lcg_next(s);
+      const double u2 = ((double)s + 1.0) / 2147483648.0;
+      if (u1 < 1.0e-300) u1 = 1.0e-300;
+      const double r = std::sqrt(-2.0 * std::log(u1));
+      const double th = 2.0 * M_PI * u2;
+      out[2 * p] = (float)(r * std::cos(th) * stdv);
+      if (2 * p + 1 < n) out[2 * p + 1] = (float)(r * std::sin(th) * stdv);
+    }
+  };
+  if (nth <= 1) {
+    work(0, pairs);
+  } else {
+    std::vector<std::thread> ts;
+    for (int t = 0; t < nth; ++t) ts.emplace_back(work, pairs * t / nth, pairs * (t + 1) / nth);
+    for (auto& t : ts) t.join();
+  }
+  return lcg_skip(state, 2ULL * (unsigned long long)pairs);
+}
+
+const char* kProjName[kLoraCount] = {"attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"};
+
+}  // namespace
+
+LlamaEngine::LlamaEngine(const LlamaConfig& cfg, int device) : cfg_(cfg), device_(device) {}
+
+LlamaEngine::~LlamaEngine() {
+  cudaSetDevice(device_);
+  if (graph_) cudaGraphExecDestroy(graph_);
+  for (DeviceBuf* b : {&p32_, &phi_, &plo_, &g_, &m_, &v_, &q8_})
+    if (b->p) cudaFree(b->p);
+  for (auto& b : bufs_)
+    if (b.p) cudaFree(b.p);
+  if (stage_) cudaFreeHost(stage_);
+  if (stream_) cudaStreamDestroy(stream_);
+}
+
+int LlamaEngine::alloc(DeviceBuf& b, size_t bytes) {
+  bytes = (bytes + 255) / 256 * 256;
+  if (bytes == 0) bytes = 256;
+  if (cudaMalloc(&b.p, bytes) != cudaSuccess) return -3;
+  b.bytes = bytes;
+  if (cudaMemsetAsync(b.p, 0, bytes, stream_) != cudaSuccess) return -3;
+  return 0;
+}
+
+int LlamaEngine::add_param(const std::string& name, int rows, int cols, bool trainable, bool q8) {
+  Param p;
+  p.name = name; p.rows = rows; p.cols = cols; p.trainable = trainable; p.q8 = q8;
+  pidx_[name] = (int)params_.size();
+  params_.push_back(p);
+  return 0;
+}
+
+const Param* LlamaEngine::find(const std::string& name) const {
+  auto it = pidx_.find(name);
+  return it == pidx_.end() ? nullptr : &params_[it->second];
+}
+
+const Param& LlamaEngine::P(const std::string& n) const { return params_[pidx_.at(n)]; }
+
+int LlamaEngine::realize() {
+  if (realized_) return -2;
+  const LlamaConfig& c = cfg_;
+  if (c.vocab <= 0 || c.d_model <= 0 || c.n_heads <= 0 || c.n_kv <= 0 || c.d_head <= 0 || c.d_ff <= 0 ||
+      c.n_layers <= 0 || c.T <= 0 || c.B <= 0)
+    return -1;
+  if (c.n_heads % c.n_kv || c.d_model % 64 || c.d_ff % 64 || c.d_head % 32 || c.T % 64 || c.vocab % 8) return -1;
+  if (c.mode == 1 && (c.lora_rank <= 0 || c.lora_rank % 8 || c.lora_targets == 0)) return -1;
+  CU(cudaSetDevice(device_));
+  CU(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+  err_ = device_error_word();
+  if (!err_) return -3;
+  const bool full = c.mode == 0;
+  const int d = c.d_model, H = c.n_heads, KV = c.n_kv, dh = c.d_head, ff = c.d_ff, V = c.vocab, r = c.lora_rank;
+  // Trainable parameters first so the optimiser walks one contiguous range.
+  if (full) {
+    add_param("token_embd.weight", V, d, true, false);
+    if (!c.tied) add_param("output.weight", V, d, true, false);
+    add_param("output_norm.weight", 1, d, true, false);
+  } else {
+    for (int l = 0; l < c.n_layers; ++l)
+      for (int t = 0; t < kLoraCount; ++t) {
+        if (!(c.lora_targets & (1 << t))) continue;
+        const int rows_out = t == kLoraQ ? H * dh : (t == kLoraK || t == kLoraV) ? KV * dh
+                             : (t == kLoraO || t == kLoraDown) ? d : ff;
+        const int cols_in = t == kLoraO ? H * dh : t == kLoraDown ? ff : d;
+        const std::string pre = "blk." + std::to_string(l) + "." + kProjName[t];
+        add_param(pre + ".lora_a", r, cols_in, true, false);
+        add_param(pre + ".lora_b", rows_out, r, true, false);
+      }
+  }
+  for (int l = 0; l < c.n_layers; ++l) {
+    const std::string pre = "blk." + std::to_string(l) + ".";
+    const bool q8 = !full;
+    add_param(pre + "attn_norm.weight", 1, d, full, false);
+    add_param(pre + "attn_q.weight", H * dh, d, full, q8);   // q | k | v contiguous: one fused GEMM operand
+    add_param(pre + "attn_k.weight", KV * dh, d, full, q8);
+    add_param(pre + "attn_v.weight", KV * dh, d, full, q8);
+    if (c.qkv_bias) {
+      add_param(pre + "attn_q.bias", 1, H * dh, full, false);
+      add_param(pre + "attn_k.bias", 1, KV * dh, full, false);
+      add_param(pre + "attn_v.bias", 1, KV * dh, full, false);
+    }
+    add_param(pre + "attn_output.weight", d, H * dh, full, q8);
+    add_param(pre + "ffn_norm.weight", 1, d, full, false);
+    add_param(pre + "ffn_gate.weight", ff, d, full, q8);      // gate | up contiguous
+    add_param(pre + "ffn_up.weight", ff, d, full, q8);
+    add_param(pre + "ffn_down.weight", d, ff, full, q8);
+  }
+  if (!full) {
+    add_param("token_embd.weight", V, d, false, false);
+    if (!c.tied) add_param("output.weight", V, d, false, false);
+    add_param("output_norm.weight", 1, d, false, false);
+  }
+  long long off = 0, qoff = 0;
+  for (auto& p : params_) {
+    if (p.trainable && off != n_train_) return -1;
+    p.offset = off;
+    off += (p.numel() + 63) / 64 * 64;
+    if (p.trainable) n_train_ = off;
+    if (p.q8) {
+      p.q8_offset = qoff;
+      qoff += p.numel() / 32 * 34;
+    }
+  }
+  n_total_ = off;
+  q8_bytes_ = qoff;
+  // fused operands must be contiguous
+  for (int l = 0; l < c.n_layers; ++l) {
+    const std::string pre = "blk." + std::to_string(l) + ".";
+    if (P(pre + "attn_k.weight").offset != P(pre + "attn_q.weight").offset + (long long)H * dh * d) return -1;
+    if (P(pre + "attn_v.weight").offset != P(pre + "attn_k.weight").offset + (long long)KV * dh * d) return -1;
+    if (P(pre + "ffn_up.weight").offset != P(pre + "ffn_gate.weight").offset + (long long)ff * d) return -1;
+  }
+  CK(alloc(p32_, n_total_ * 4));
+  CK(alloc(phi_, n_total_ * 2));
+  CK(alloc(plo_, n_total_ * 2));
+  CK(alloc(g_, std::max<long long>(n_train_, 64) * 4));
+  CK(alloc(m_, std::max<long long>(n_train_, 64) * 4));
+  CK(alloc(v_, std::max<long long>(n_train_, 64) * 4));
+  if (q8_bytes_) CK(alloc(q8_, q8_bytes_));
+
+  const int N = this->N(), T = c.T, B = c.B, W = (H + 2 * KV) * dh;
+  auto f32 = [&](long long n) -> float* {
+    bufs_.emplace_back();
+    if (alloc(bufs_.back(), n * 4)) return nullptr;
+    return static_cast<float*>(bufs_.back().p);
+  };
+  auto pl = [&](long long n) -> Planes {   // hi and lo planes, each padded to 128 elements
+    const long long np = (n + 127) / 128 * 128;
+    bufs_.emplace_back();
+    if (alloc(bufs_.back(), np * 4)) return Planes{};
+    bf16* base = static_cast<bf16*>(bufs_.back().p);
+    return Planes{base, base + np};
+  };
+  const long long att = (long long)B * H * T * T;
+  for (int l = 0; l <= c.n_layers; ++l) x_.push_back(f32((long long)N * d));
+  lora_u_.resize(c.n_layers);
+  for (int l = 0; l < c.n_layers; ++l) {
+    x1_.push_back(f32((long long)N * d));
+    gu_.push_back(f32((long long)N * 2 * ff));
+    h1_.push_back(pl((long long)N * d));
+    h2_.push_back(pl((long long)N * d));
+    a_.push_back(pl((long long)N * ff));
+    Qh_.push_back(pl((long long)N * H * dh));
+    Kh_.push_back(pl((long long)N * KV * dh));
+    Vh_.push_back(pl((long long)N * KV * dh));
+    Pm_.push_back(pl(att));
+    O_.push_back(pl((long long)N * H * dh));
+    lora_u_[l].resize(kLoraCount);
+    for (int t = 0; t < kLoraCount; ++t)
+      if (!full && (c.lora_targets & (1 << t))) lora_u_[l][t] = pl((long long)N * r);
+  }
+  qkv_ = f32((long long)N * W);
+  S_ = f32(att);
+  logits_ = f32((long long)N * V);
+  loss_rows_ = f32(N);
+  loss_ = f32(64);
+  dx_ = f32((long long)N * d);
+  dh_ = f32((long long)N * d);
+  da_ = f32((long long)N * ff);
+  dO32_ = f32((long long)N * H * dh);
+  dQ_ = f32((long long)N * H * dh);
+  dK_ = f32((long long)N * KV * dh);
+  dV_ = f32((long long)N * KV * dh);
+  gpart_ = f32((long long)rmsnorm_bwd_blocks() * d);
+  xf_ = pl((long long)N * d);
+  dlog_ = pl((long long)N * V);
+  dxp_ = pl((long long)N * d);
+  dgu_ = pl((long long)N * 2 * ff);
+  dO_ = pl((long long)N * H * dh);
+  dS_ = pl(att);
+  dqkv_ = pl((long long)N * W);
+  if (!full) {
+    u32_ = f32((long long)N * r);
+    du32_ = f32((long long)N * r);
+    du_ = pl((long long)N * r);
+  }
+  hp_ = f32(8);
+  bufs_.emplace_back();
+  CK(alloc(bufs_.back(), (size_t)N * 4 * 5 + 64));
+  int* ib = static_cast<int*>(bufs_.back().p);
+  ids_ = ib; pos_ = ib + N; labels_ = ib + 2 * N; ord_ = ib + 3 * N; seg_id_ = ib + 4 * N;
+  bufs_.emplace_back();
+  CK(alloc(bufs_.back(), (size_t)(N + 2) * 4));
+  seg_start_ = static_cast<int*>(bufs_.back().p);
+  nseg_dev_ = seg_start_ + N + 1;
+  for (const auto& b : bufs_)
+    if (!b.p) return -3;
+  // RoPE cos/sin table, ggml's rope cache: theta starts at float(pos), times
+  // theta_scale = powf(base, -2/n_dims) per pair, divided by the freq factor.
+  cs_rows_ = std::max(T, 4096);
+  const int half = dh / 2;
+  std::vector<float> tab((size_t)cs_rows_ * half * 2);
+  const float ts = powf(c.rope_base, -2.0f / (float)dh);
+  for (int p = 0; p < cs_rows_; ++p) {
+    float theta = (float)p;
+    for (int i = 0; i < half; ++i) {
+      const float f = c.freq_factors.empty() ? 1.0f : c.freq_factors[i];
+      const float th = c.freq_scale * (theta / f);
+      tab[((size_t)p * half + i) * 2] = (float)std::cos((double)th);
+      tab[((size_t)p * half + i) * 2 + 1] = (float)std::sin((double)th);
+      theta = theta * ts;
+    }
+  }
+  cs_ = f32((long long)cs_rows_ * half * 2);
+  if (!cs_) return -3;
+  CU(cudaMemcpyAsync(cs_, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice, stream_));
+  // default ids/positions: 0 and 0..T-1
+  std::vector<long long> pos0(N);
+  for (int i = 0; i < N; ++i) pos0[i] = i % T;
+  realized_ = true;
+  CK(set_positions(pos0.data(), N));
+  std::vector<long long> z(N, 0);
+  CK(set_tokens(z.data(), N));
+  CK(set_label_ids(z.data(), N));
+  CU(cudaStreamSynchronize(stream_));
+  return 0;
+}
+
+int LlamaEngine::staged(size_t bytes) {
+  if (bytes <= stage_bytes_) return 0;
+  if (stage_) {
+    cudaStreamSynchronize(stream_);
+    cudaFreeHost(stage_);
+  }
+  stage_bytes_ = std::max(bytes, (size_t)1 << 20);
+  if (cudaMallocHost(&stage_, stage_bytes_) != cudaSuccess) {
+    stage_ = nullptr;
+    stage_bytes_ = 0;
+    return -3;
+  }
+  return 0;
+}
+
+int LlamaEngine::refresh_planes(const Param& p) {
+  return launch_split_f32(P32(p), PP(p).hi, PP(p).lo, p.numel(), stream_);
+}
+
+int LlamaEngine::set_param(const std::string& name, const float* host, long long n) {
+  const Param* p = find(name);
+  if (!p || !host) return -1;
+  if (n != p->numel()) return -1;
+  // Stream-ordered copy: a plain cudaMemcpy from pageable memory may return
+  // before its DMA lands, and stream_ does not order against the legacy stream.
+  CU(cudaStreamSynchronize(stream_));
+  CU(cudaMemcpyAsync(P32(*p), host, n * 4, cudaMemcpyHostToDevice, stream_));
+  if (p->q8) {
+    CK(launch_q8_0_quantize(P32(*p), static_cast<uint8_t*>(q8_.p) + p->q8_offset, p->rows, p->cols, stream_));
+    CK(launch_q8_0_to_planes(static_cast<uint8_t*>(q8_.p) + p->q8_offset, PP(*p), P32(*p), p->rows, p->cols,
+                             stream_));
+  } else {
+    CK(refresh_planes(*p));
+  }
+  CU(cudaStreamSynchronize(stream_));
+  return 0;
+}
+
+int LlamaEngine::set_param_q8(const std::string& name, const uint8_t* blocks, long long nbytes) {
+  const Param* p = find(name);
+  if (!p || !p->q8 || !blocks || nbytes != p->numel() / 32 * 34) return -1;
+  CU(cudaStreamSynchronize(stream_));
+  uint8_t* dst = static_cast<uint8_t*>(q8_.p) + p->q8_offset;
+  CU(cudaMemcpyAsync(dst, blocks, nbytes, cudaMemcpyHostToDevice, stream_));
+  CK(launch_q8_0_to_planes(dst, PP(*p), P32(*p), p->rows, p->cols, stream_));
+  CU(cudaStreamSynchronize(stream_));
+  return 0;
+}
+
+int LlamaEngine::get_param_q8(const std::string& name, uint8_t* blocks, long long nbytes) {
+  const Param* p = find(name);
+  if (!p || !p->q8 || !blocks || nbytes != p->numel() / 32 * 34) return -1;
+  CU(cudaStreamSynchronize(stream_));
+  CU(cudaMemcpy(blocks, static_cast<uint8_t*>(q8_.p) + p->q8_offset, nbytes, cudaMemcpyDeviceToHost));
+  return 0;
+}
+
+int LlamaEngine::get_param(const std::string& name, float* host, long long n) {
+  const Param* p = find(name);
+  if (!p || !host || n != p->numel()) return -1;
+  CU(cudaStreamSynchronize(stream_));
+  CU(cudaMemcpy(host, P32(*p), n * 4, cudaMemcpyDeviceToHost));
+  return 0;
+}
+
+int LlamaEngine::get_grad(const std::string& name, float* host, long long n) {
+  const Param* p = find(name);
+  if (!p || !host || n != p->numel() || !p->trainable) return -1;
+  CU(cudaStreamSynchronize(stream_));
+  CU(cudaMemcpy(host, G32(*p), n * 4, cudaMemcpyDeviceToHost));
+  return 0;
+}
+
+int LlamaEngine::get_moment(const std::string& name, int which, float* host, long long n) {
+  const Param* p = find(name);
+  if (!p || !host || n != p->numel() || !p->trainable) return -1;
+  CU(cudaStreamSynchronize(stream_));
+  const float* src = static_cast<float*>(which == 0 ? m_.p : v_.p) + p->offset;
+  CU(cudaMemcpy(host, src, n * 4, cudaMemcpyDeviceToHost));
+  return 0;
+}
+
+// Seeded init in the reference's draw order (upload_random_init!,
+// llama_seq_engine.rb:1161-1340); std_all > 0 replaces every std (the synthetic
+// N(0, std) frozen base of the QLoRA configs, then quantised to Q8_0); LoRA
+// adapters follow from the same stream, per layer and target, A then B.
+int LlamaEngine::init_random(long long seed, double init_scale, double std_all, double lora_a_std,
+                             double lora_b_std) {
+  if (!realized_) return -2;
+  const LlamaConfig& c = cfg_;
+  const int d = c.d_model, H = c.n_heads, KV = c.n_kv, dh = c.d_head, ff = c.d_ff, V = c.vocab;
+  const bool all = std_all > 0.0;
+  const double s_emb = all ? std_all : 0.02;
+  const double s_d = all ? std_all : init_scale / std::sqrt((double)d);
+  const double s_ff = all ? std_all : init_scale / std::sqrt((double)ff);
+  uint64_t st = lcg_seed_state(seed);
+  std::vector<float> buf;
+  auto fill = [&](const std::string& name, double stdv) -> int {
+    const Param& p = P(name);
+    buf.resize(p.numel());
+    st = gaussian_fill(st, buf.data(), p.numel(), stdv);
+    return set_param(name, buf.data(), p.numel());
+  };
+  auto ones = [&](const std::string& name) -> int {
+    const Param& p = P(name);
+    buf.assign(p.numel(), 1.0f);
+    return set_param(name, buf.data(), p.numel());
+  };
+  CK(fill("token_embd.weight", s_emb));
+  CK(ones("output_norm.weight"));
+  if (!c.tied) CK(fill("output.weight", s_emb));
+  for (int l = 0; l < c.n_layers; ++l) {
+    const std::string pre = "blk." + std::to_string(l) + ".";
+    CK(ones(pre + "attn_norm.weight"));
+    CK(ones(pre + "ffn_norm.weight"));
+    // per-head draws, stored into the fused row blocks
+    std::vector<float> wq((size_t)H * dh * d), wk((size_t)KV * dh * d), wv((size_t)KV * dh * d);
+    for (int h = 0; h < H; ++h) st = gaussian_fill(st, wq.data() + (size_t)h * dh * d, (long long)dh * d, s_d);
+    for (int j = 0; j < KV; ++j) {
+      st = gaussian_fill(st, wk.data() + (size_t)j * dh * d, (long long)dh * d, s_d);
+      st = gaussian_fill(st, wv.data() + (size_t)j * dh * d, (long long)dh * d, s_d);
+    }
+    CK(set_param(pre + "attn_q.weight", wq.data(), (long long)wq.size()));
+    CK(set_param(pre + "attn_k.weight", wk.data(), (long long)wk.size()));
+    CK(set_param(pre + "attn_v.weight", wv.data(), (long long)wv.size()));
+    CK(fill(pre + "attn_output.weight", s_d));
+    CK(fill(pre + "ffn_gate.weight", s_d));
+    CK(fill(pre + "ffn_up.weight", s_d));
+    CK(fill(pre + "ffn_down.weight", s_ff));
+    if (c.qkv_bias) {
+      const double sb = all ? std_all : 0.02;
+      CK(fill(pre + "attn_q.bias", sb));
+      CK(fill(pre + "attn_k.bias", sb));
+      CK(fill(pre + "attn_v.bias", sb));
+    }
+  }
+  if (c.mode == 1) {
+    for (int l = 0; l < c.n_layers; ++l)
+      for (int t = 0; t < kLoraCount; ++t) {
+        if (!(c.lora_targets & (1 << t))) continue;
+        const std::string pre = "blk." + std::to_string(l) + "." + kProjName[t];
+        CK(fill(pre + ".lora_a", lora_a_std));
+        CK(fill(pre + ".lora_b", lora_b_std));
+      }
+  }
+  (void)V;
+  return 0;
+}
+
+// ------------------------------------------------------------------ inputs
+int LlamaEngine::set_tokens(const long long* ids, int n) {
+  if (!realized_ || !ids || n != N()) return -1;
+  const int V = cfg_.vocab;
+  CK(staged((size_t)n * 4 * 4 + 64));
+  int* h = static_cast<int*>(stage_);   // ids | order | seg ids | seg starts (+ count)
+  CU(cudaStreamSynchronize(stream_));
+  for (int i = 0; i < n; ++i) {
+    if (ids[i] < 0 || ids[i] >= V) return -1;
+    h[i] = (int)ids[i];
+  }
+  // rows grouped by id (stable), for the deterministic embedding scatter-add
+  std::vector<int> cnt;
+  std::vector<std::pair<int, int>> kv(n);
+  for (int i = 0; i < n; ++i) kv[i] = {h[i], i};
+  std::stable_sort(kv.begin(), kv.end(), [](auto a, auto b) { return a.first < b.first; });
+  int* ord = h + n;
+  int* sid = h + 2 * n;
+  int* sst = h + 3 * n;
+  int ns = 0;
+  for (int i = 0; i < n; ++i) {
+    ord[i] = kv[i].second;
+    if (i == 0 || kv[i].first != kv[i - 1].first) {
+      sid[ns] = kv[i].first;
+      sst[ns] = i;
+      ++ns;
+    }
+  }
+  sst[ns] = n;
+  nseg_ = ns;
+  CU(cudaMemcpyAsync(ids_, h, (size_t)n * 4, cudaMemcpyHostToDevice, stream_));
+  CU(cudaMemcpyAsync(ord_, ord, (size_t)n * 4, cudaMemcpyHostToDevice, stream_));
+  CU(cudaMemcpyAsync(seg_id_, sid, (size_t)ns * 4, cudaMemcpyHostToDevice, stream_));
+  CU(cudaMemcpyAsync(seg_start_, sst, (size_t)(ns + 1) * 4, cudaMemcpyHostToDevice, stream_));
+  sst[ns + 1] = ns;
+  CU(cudaMemcpyAsync(nseg_dev_, sst + ns + 1, 4, cudaMemcpyHostToDevice, stream_));
+  CU(cudaStreamSynchronize(stream_));
+  return 0;
+}
+
+int LlamaEngine::set_positions(const long long* pos, int n) {
+  if (!realized_ || !pos || n != N()) return -1;
+  CK(staged((size_t)n * 4));
+  CU(cudaStreamSynchronize(stream_));
+  int* h = static_cast<int*>(stage_);
+  for (int i = 0; i < n; ++i) {
+    if (pos[i] < 0 || pos[i] >= cs_rows_) return -1;
+    h[i] = (int)pos[i];
+  }
+  CU(cudaMemcpyAsync(pos_, h, (size_t)n * 4, cudaMemcpyHostToDevice, stream_));
+  CU(cudaStreamSynchronize(stream_));
+  return 0;
+}
+
+int LlamaEngine::set_label_ids(const long long* ids, int n) {
+  if (!realized_ || !ids || n != N()) return -1;
+  CK(staged((size_t)n * 4));
+  CU(cudaStreamSynchronize(stream_));
+  int* h = static_cast<int*>(stage_);
+  for (int i = 0; i < n; ++i) h[i] = (ids[i] >= 0 && ids[i] < cfg_.vocab) ? (int)ids[i] : -1;
+  CU(cudaMemcpyAsync(labels_, h, (size_t)n * 4, cudaMemcpyHostToDevice, stream_));
+  CU(cudaStreamSynchronize(stream_));
+  dense_labels_ = false;
+  return 0;
+}
+
+int LlamaEngine::set_labels_dense(const double* lab, long long n) {
+  const long long want = (long long)N() * cfg_.vocab;
+  if (!realized_ || !lab || n != want) return -1;
+  if (!labels_dense_) {
+    bufs_.emplace_back();
+    CK(alloc(bufs_.back(), (size_t)want * 4));
+    labels_dense_ = static_cast<float*>(bufs_.back().p);
+  }
+  const long long chunk = 4 << 20;
+  CK(staged((size_t)chunk * 4));
+  float* h = static_cast<float*>(stage_);
+  for (long long o = 0; o < want; o += chunk) {
+    const long long k = std::min(chunk, want - o);
+    CU(cudaStreamSynchronize(stream_));
+    for (long long i = 0; i < k; ++i) h[i] = (float)lab[o + i];
+    CU(cudaMemcpyAsync(labels_dense_ + o, h, (size_t)k * 4, cudaMemcpyHostToDevice, stream_));
+  }
+  CU(cudaStreamSynchronize(stream_));
+  dense_labels_ = true;
+  return 0;
+}
+
+int LlamaEngine::set_hp(const double* hp, int n) {
+  if (!realized_ || !hp || n != 7) return -1;
+  CK(staged(64));
+  CU(cudaStreamSynchronize(stream_));
+  float* h = static_cast<float*>(stage_);
+  for (int i = 0; i < 7; ++i) h[i] = (float)hp[i];
+  CU(cudaMemcpyAsync(hp_, h, 7 * 4, cudaMemcpyHostToDevice, stream_));
+  CU(cudaStreamSynchronize(stream_));
+  return 0;
+}
+
+// ------------------------------------------------------------------ step program
+int LlamaEngine::gemm(const GemmDesc& d) {
+  ++counting_;
+  const int rc = gemm_launch(d, err_, stream_);
+  if (rc) fprintf(stderr, "[toy_b200] gemm launch rejected (%d): M=%d N=%d K=%d batch=%d\n", rc, d.M, d.N, d.K, d.batch);
+  return rc;
+}
+
+#define KL(x)              \
+  do {                     \
+    ++counting_;           \
+    CK(x);                 \
+  } while (0)
+
+// Y[:, col_off : col_off + d_out] += s * (X A^T) B^T, saving u = X A^T (planes) for backward.
+int LlamaEngine::lora_forward(int l, int t, Planes X, int d_in, float* Y, long long ldy, int col_off, int d_out) {
+  const LlamaConfig& c = cfg_;
+  const int N = this->N(), r = c.lora_rank;
+  const std::string pre = "blk." + std::to_string(l) + "." + kProjName[t];
+  const Param& A = P(pre + ".lora_a");
+  const Param& Bp = P(pre + ".lora_b");
+  Planes u = lora_u_[l][t];
+  GemmDesc g1;
+  g1.M = N; g1.N = r; g1.K = d_in;
+  g1.a = op(X, N, d_in, d_in, 0);
+  g1.b = op(PP(A), r, d_in, d_in, 0);
+  g1.epi.mode = kEpiStoreSplit; g1.epi.out_hi = u.hi; g1.epi.out_lo = u.lo; g1.epi.m_s0 = r;
+  CK(gemm(g1));
+  GemmDesc g2;
+  g2.M = N; g2.N = d_out; g2.K = r;
+  g2.a = op(u, N, r, r, 0);
+  g2.b = op(PP(Bp), d_out, r, r, 0);
+  g2.epi = epi_rowmajor(kEpiAccumF32, Y + col_off, ldy, c.lora_alpha / (float)r);
+  return gemm(g2);
+}
+
+// Gradients of the adapter on projection (l, t): dB, dA into the gradient
+// arena, and dX += s * (dY B) A (row-major [N][d_in] or the given scatter).
+int LlamaEngine::lora_backward(int l, int t, Planes X, int d_in, Planes dY, long long ld_dy, int col_off, int d_out,
+                               float* dX, const Epilogue* dx_scatter) {
+  const LlamaConfig& c = cfg_;
+  const int N = this->N(), r = c.lora_rank;
+  const float s = c.lora_alpha / (float)r;
+  const std::string pre = "blk." + std::to_string(l) + "." + kProjName[t];
+  const Param& A = P(pre + ".lora_a");
+  const Param& Bp = P(pre + ".lora_b");
+  Planes u = lora_u_[l][t];
+  Planes dYo = offset(dY, col_off);
+  // dB = s * dY^T u   [d_out][r]
+  GemmDesc g3;
+  g3.M = d_out; g3.N = r; g3.K = N;
+  g3.a = op(dYo, N, d_out, ld_dy, 1);
+  g3.b = op(u, N, r, r, 1);
+  g3.epi = epi_rowmajor(kEpiStoreF32, G32(Bp), r, s);
+  CK(gemm(g3));
+  // du = s * dY B   [N][r]
+  GemmDesc g4;
+  g4.M = N; g4.N = r; g4.K = d_out;
+  g4.a = op(dYo, N, d_out, ld_dy, 0);
+  g4.b = op(PP(Bp), d_out, r, r, 1);
+  g4.epi.mode = kEpiStoreSplit; g4.epi.alpha = s; g4.epi.out_hi = du_.hi; g4.epi.out_lo = du_.lo; g4.epi.m_s0 = r;
+  CK(gemm(g4));
+  // dA = du^T X   [r][d_in]
+  GemmDesc g5;
+  g5.M = r; g5.N = d_in; g5.K = N;
+  g5.a = op(du_, N, r, r, 1);
+  g5.b = op(X, N, d_in, d_in, 1);
+  g5.epi = epi_rowmajor(kEpiStoreF32, G32(A), d_in);
+  CK(gemm(g5));
+  // dX += du A   [N][d_in]
+  GemmDesc g6;
+  g6.M = N; g6.N = d_in; g6.K = r;
+  g6.a = op(du_, N, r, r, 0);
+  g6.b = op(PP(A), r, d_in, d_in, 1);
+  if (dx_scatter) {
+    g6.epi = *dx_scatter;
+    g6.epi.mode = kEpiAccumF32;
+  } else {
+    g6.epi = epi_rowmajor(kEpiAccumF32, dX, d_in);
+  }
+  return gemm(g6);
+}
+
+int LlamaEngine::enqueue_forward() {
+  const LlamaConfig& c = cfg_;
+  const int N = this->N(), d = c.d_model, H = c.n_heads, KV = c.n_kv, dh = c.d_head, ff = c.d_ff, T = c.T, B = c.B;
+  const int W = (H + 2 * KV) * dh, G = H / KV, V = c.vocab;
+  const float scale = 1.0f / std::sqrt((float)dh);
+  const bool lora = c.mode == 1;
+  const Param& E = P("token_embd.weight");
+  KL(launch_embed_gather(P32(E), ids_, x_[0], N, d, stream_));
+  for (int l = 0; l < c.n_layers; ++l) {
+    const std::string pre = "blk." + std::to_string(l) + ".";
+    KL(launch_rmsnorm_fwd(x_[l], P32(P(pre + "attn_norm.weight")), h1_[l], N, d, c.rms_eps, stream_));
+    GemmDesc g;
+    g.M = N; g.N = W; g.K = d;
+    g.a = op(h1_[l], N, d, d, 0);
+    g.b = op(PP(P(pre + "attn_q.weight")), W, d, d, 0);
+    g.epi = epi_rowmajor(kEpiStoreF32, qkv_, W);
+    CK(gemm(g));
+    if (lora) {
+      if (c.lora_targets & (1 << kLoraQ)) CK(lora_forward(l, kLoraQ, h1_[l], d, qkv_, W, 0, H * dh));
+      if (c.lora_targets & (1 << kLoraK)) CK(lora_forward(l, kLoraK, h1_[l], d, qkv_, W, H * dh, KV * dh));
+      if (c.lora_targets & (1 << kLoraV)) CK(lora_forward(l, kLoraV, h1_[l], d, qkv_, W, (H + KV) * dh, KV * dh));
+    }
+    const float* bias = c.qkv_bias ? P32(P(pre + "attn_q.bias")) : nullptr;
+    KL(launch_rope_qkv_fwd(qkv_, bias, pos_, cs_, cs_rows_, Qh_[l], Kh_[l], Vh_[l], B, T, H, KV, dh, stream_));
+    // scores S = scale * Q K^T per (sequence, head)
+    GemmDesc gs;
+    gs.M = T; gs.N = T; gs.K = dh; gs.batch = B * H;
+    gs.a = bop(Qh_[l], T, dh, dh, B * H, 0);
+    gs.b = bop(Kh_[l], T, dh, dh, B * KV, 0, H, KV, G, 1);
+    gs.epi.mode = kEpiStoreF32; gs.epi.out = S_; gs.epi.alpha = scale; gs.epi.m_s0 = T;
+    gs.epi.bstride = (long long)T * T;
+    CK(gemm(gs));
+    KL(launch_softmax_causal_fwd(S_, Pm_[l], (long long)B * H, T, stream_));
+    // O = P V, written token-major [N][H*dh]
+    GemmDesc go;
+    go.M = T; go.N = dh; go.K = T; go.batch = B * H;
+    go.a = bop(Pm_[l], T, T, T, B * H, 0);
+    go.b = bop(Vh_[l], T, dh, dh, B * KV, 1, H, KV, G, 1);
+    go.epi.mode = kEpiStoreSplit; go.epi.out_hi = O_[l].hi; go.epi.out_lo = O_[l].lo;
+    go.epi.z_div = H; go.epi.z_s1 = (long long)T * H * dh; go.epi.bstride = dh; go.epi.m_s0 = (long long)H * dh;
+    CK(gemm(go));
+    // x1 = x + O Wo^T
+    GemmDesc gw;
+    gw.M = N; gw.N = d; gw.K = H * dh;
+    gw.a = op(O_[l], N, H * dh, H * dh, 0);
+    gw.b = op(PP(P(pre + "attn_output.weight")), d, H * dh, H * dh, 0);
+    gw.epi = epi_rowmajor(kEpiResidF32, x1_[l], d);
+    gw.epi.res = x_[l];
+    CK(gemm(gw));
+    if (lora && (c.lora_targets & (1 << kLoraO))) CK(lora_forward(l, kLoraO, O_[l], H * dh, x1_[l], d, 0, d));
+    KL(launch_rmsnorm_fwd(x1_[l], P32(P(pre + "ffn_norm.weight")), h2_[l], N, d, c.rms_eps, stream_));
+    GemmDesc gg;
+    gg.M = N; gg.N = 2 * ff; gg.K = d;
+    gg.a = op(h2_[l], N, d, d, 0);
+    gg.b = op(PP(P(pre + "ffn_gate.weight")), 2 * ff, d, d, 0);
+    gg.epi = epi_rowmajor(kEpiStoreF32, gu_[l], 2 * ff);
+    CK(gemm(gg));
+    if (lora && (c.lora_targets & (1 << kLoraGate))) CK(lora_forward(l, kLoraGate, h2_[l], d, gu_[l], 2 * ff, 0, ff));
+    if (lora && (c.lora_targets & (1 << kLoraUp))) CK(lora_forward(l, kLoraUp, h2_[l], d, gu_[l], 2 * ff, ff, ff));
+    KL(launch_swiglu_fwd(gu_[l], a_[l], N, ff, stream_));
+    GemmDesc gd;
+    gd.M = N; gd.N = d; gd.K = ff;
+    gd.a = op(a_[l], N, ff, ff, 0);
+    gd.b = op(PP(P(pre + "ffn_down.weight")), d, ff, ff, 0);
+    gd.epi = epi_rowmajor(kEpiResidF32, x_[l + 1], d);
+    gd.epi.res = x1_[l];
+    CK(gemm(gd));
+    if (lora && (c.lora_targets & (1 << kLoraDown))) CK(lora_forward(l, kLoraDown, a_[l], ff, x_[l + 1], d, 0, d));
+  }
+  KL(launch_rmsnorm_fwd(x_[c.n_layers], P32(P("output_norm.weight")), xf_, N, d, c.rms_eps, stream_));
+  const Param& Wout = c.tied ? E : P("output.weight");
+  GemmDesc gl;
+  gl.M = N; gl.N = V; gl.K = d;
+  gl.a = op(xf_, N, d, d, 0);
+  gl.b = op(PP(Wout), V, d, d, 0);
+  gl.epi = epi_rowmajor(kEpiStoreF32, logits_, V);
+  CK(gemm(gl));
+  KL(launch_cross_entropy(logits_, labels_, dense_labels_ ? labels_dense_ : nullptr, loss_rows_, dlog_, N, V, stream_));
+  KL(launch_loss_reduce(loss_rows_, N, loss_, stream_));
+  return 0;
+}
+
+int LlamaEngine::enqueue_backward() {
+  const LlamaConfig& c = cfg_;
+  const int N = this->N(), d = c.d_model, H = c.n_heads, KV = c.n_kv, dh = c.d_head, ff = c.d_ff, T = c.T, B = c.B;
+  const int W = (H + 2 * KV) * dh, G = H / KV, V = c.vocab;
+  const float scale = 1.0f / std::sqrt((float)dh);
+  const bool full = c.mode == 0, lora = c.mode == 1;
+  const int nblk = rmsnorm_bwd_blocks();
+  const Param& E = P("token_embd.weight");
+  const Param& Wout = c.tied ? E : P("output.weight");
+  // dxf = dlogits W_out   ([N][V] x [V][d])
+  GemmDesc g;
+  g.M = N; g.N = d; g.K = V;
+  g.a = op(dlog_, N, V, V, 0);
+  g.b = op(PP(Wout), V, d, d, 1);
+  g.epi = epi_rowmajor(kEpiStoreF32, dh_, d);
+  CK(gemm(g));
+  if (full) {
+    GemmDesc ge;
+    ge.M = V; ge.N = d; ge.K = N;
+    ge.a = op(dlog_, N, V, V, 1);
+    ge.b = op(xf_, N, d, d, 1);
+    ge.epi = epi_rowmajor(kEpiStoreF32, G32(Wout), d);
+    CK(gemm(ge));
+  }
+  const Param& gf = P("output_norm.weight");
+  KL(launch_rmsnorm_bwd(x_[c.n_layers], dh_, P32(gf), nullptr, dx_, dxp_, gpart_, nblk, N, d, c.rms_eps, stream_));
+  if (full) KL(launch_colsum(gpart_, nblk, d, G32(gf), 0, stream_));
+  for (int l = c.n_layers - 1; l >= 0; --l) {
+    const std::string pre = "blk." + std::to_string(l) + ".";
+    const Param& Wd = P(pre + "ffn_down.weight");
+    const Param& Wg = P(pre + "ffn_gate.weight");
+    const Param& Wo = P(pre + "attn_output.weight");
+    const Param& Wq = P(pre + "attn_q.weight");
+    // ---- FFN
+    GemmDesc gda;
+    gda.M = N; gda.N = ff; gda.K = d;
+    gda.a = op(dxp_, N, d, d, 0);
+    gda.b = op(PP(Wd), d, ff, ff, 1);
+    gda.epi = epi_rowmajor(kEpiStoreF32, da_, ff);
+    CK(gemm(gda));
+    if (full) {
+      GemmDesc gw;
+      gw.M = d; gw.N = ff; gw.K = N;
+      gw.a = op(dxp_, N, d, d, 1);
+      gw.b = op(a_[l], N, ff, ff, 1);
+      gw.epi = epi_rowmajor(kEpiStoreF32, G32(Wd), ff);
+      CK(gemm(gw));
+    }
+    if (lora && (c.lora_targets & (1 << kLoraDown)))
+      CK(lora_backward(l, kLoraDown, a_[l], ff, dxp_, d, 0, d, da_, nullptr));
+    KL(launch_swiglu_bwd(gu_[l], da_, dgu_, N, ff, stream_));
+    GemmDesc gh;
+    gh.M = N; gh.N = d; gh.K = 2 * ff;
+    gh.a = op(dgu_, N, 2 * ff, 2 * ff, 0);
+    gh.b = op(PP(Wg), 2 * ff, d, d, 1);
+    gh.epi = epi_rowmajor(kEpiStoreF32, dh_, d);
+    CK(gemm(gh));
+    if (full) {
+      GemmDesc gw;
+      gw.M = 2 * ff; gw.N = d; gw.K = N;
+      gw.a = op(dgu_, N, 2 * ff, 2 * ff, 1);
+      gw.b = op(h2_[l], N, d, d, 1);
+      gw.epi = epi_rowmajor(kEpiStoreF32, G32(Wg), d);
+      CK(gemm(gw));
+    }
+    if (lora && (c.lora_targets & (1 << kLoraGate)))
+      CK(lora_backward(l, kLoraGate, h2_[l], d, dgu_, 2 * ff, 0, ff, dh_, nullptr));
+    if (lora && (c.lora_targets & (1 << kLoraUp)))
+      CK(lora_backward(l, kLoraUp, h2_[l], d, dgu_, 2 * ff, ff, ff, dh_, nullptr));
+    const Param& g2 = P(pre + "ffn_norm.weight");
+    KL(launch_rmsnorm_bwd(x1_[l], dh_, P32(g2), dx_, dx_, dxp_, gpart_, nblk, N, d, c.rms_eps, stream_));
+    if (full) KL(launch_colsum(gpart_, nblk, d, G32(g2), 0, stream_));
+    // ---- attention output projection: dO (head-major f32), dWo
+    Epilogue hm;
+    hm.mode = kEpiStoreF32; hm.out = dO32_;
+    hm.m_div = T; hm.m_s1 = (long long)H * T * dh; hm.m_s0 = dh; hm.n_div = dh; hm.n_s1 = (long long)T * dh;
+    GemmDesc gdo;
+    gdo.M = N; gdo.N = H * dh; gdo.K = d;
+    gdo.a = op(dxp_, N, d, d, 0);
+    gdo.b = op(PP(Wo), d, H * dh, H * dh, 1);
+    gdo.epi = hm;
+    CK(gemm(gdo));
+    if (full) {
+      GemmDesc gw;
+      gw.M = d; gw.N = H * dh; gw.K = N;
+      gw.a = op(dxp_, N, d, d, 1);
+      gw.b = op(O_[l], N, H * dh, H * dh, 1);
+      gw.epi = epi_rowmajor(kEpiStoreF32, G32(Wo), H * dh);
+      CK(gemm(gw));
+    }
+    if (lora && (c.lora_targets & (1 << kLoraO)))
+      CK(lora_backward(l, kLoraO, O_[l], H * dh, dxp_, d, 0, d, dO32_, &hm));
+    KL(launch_split_f32(dO32_, dO_.hi, dO_.lo, (long long)N * H * dh, stream_));
+    // ---- attention core
+    GemmDesc gp;
+    gp.M = T; gp.N = T; gp.K = dh; gp.batch = B * H;
+    gp.a = bop(dO_, T, dh, dh, B * H, 0);
+    gp.b = bop(Vh_[l], T, dh, dh, B * KV, 0, H, KV, G, 1);
+    gp.epi.mode = kEpiStoreF32; gp.epi.out = S_; gp.epi.m_s0 = T; gp.epi.bstride = (long long)T * T;
+    CK(gemm(gp));
+    KL(launch_softmax_causal_bwd(Pm_[l], S_, dS_, (long long)B * H, T, scale, stream_));
+    GemmDesc gq;
+    gq.M = T; gq.N = dh; gq.K = T; gq.batch = B * H;
+    gq.a = bop(dS_, T, T, T, B * H, 0);
+    gq.b = bop(Kh_[l], T, dh, dh, B * KV, 1, H, KV, G, 1);
+    gq.epi.mode = kEpiStoreF32; gq.epi.out = dQ_; gq.epi.m_s0 = dh; gq.epi.bstride = (long long)T * dh;
+    CK(gemm(gq));
+    GemmDesc gk;
+    gk.M = T; gk.N = dh; gk.K = G * T; gk.batch = B * KV;
+    gk.a = bop(dS_, G * T, T, T, B * KV, 1);
+    gk.b = bop(Qh_[l], G * T, dh, dh, B * KV, 1);
+    gk.epi.mode = kEpiStoreF32; gk.epi.out = dK_; gk.epi.m_s0 = dh; gk.epi.bstride = (long long)T * dh;
+    CK(gemm(gk));
+    GemmDesc gv;
+    gv.M = T; gv.N = dh; gv.K = G * T; gv.batch = B * KV;
+    gv.a = bop(Pm_[l], G * T, T, T, B * KV, 1);
+    gv.b = bop(dO_, G * T, dh, dh, B * KV, 1);
+    gv.epi.mode = kEpiStoreF32; gv.epi.out = dV_; gv.epi.m_s0 = dh; gv.epi.bstride = (long long)T * dh;
+    CK(gemm(gv));
+    KL(launch_rope_qkv_bwd(dQ_, dK_, dV_, pos_, cs_, cs_rows_, dqkv_, c.qkv_bias ? qkv_ : nullptr, B, T, H, KV, dh,
+                           stream_));
+    if (c.qkv_bias && full) KL(launch_colsum_rows(qkv_, N, W, G32(P(pre + "attn_q.bias")), stream_));
+    // ---- QKV projection
+    GemmDesc gx;
+    gx.M = N; gx.N = d; gx.K = W;
+    gx.a = op(dqkv_, N, W, W, 0);
+    gx.b = op(PP(Wq), W, d, d, 1);
+    gx.epi = epi_rowmajor(kEpiStoreF32, dh_, d);
+    CK(gemm(gx));
+    if (full) {
+      GemmDesc gw;
+      gw.M = W; gw.N = d; gw.K = N;
+      gw.a = op(dqkv_, N, W, W, 1);
+      gw.b = op(h1_[l], N, d, d, 1);
+      gw.epi = epi_rowmajor(kEpiStoreF32, G32(Wq), d);
+      CK(gemm(gw));
+    }
+    if (lora && (c.lora_targets & (1 << kLoraQ)))
+      CK(lora_backward(l, kLoraQ, h1_[l], d, dqkv_, W, 0, H * dh, dh_, nullptr));
+    if (lora && (c.lora_targets & (1 << kLoraK)))
+      CK(lora_backward(l, kLoraK, h1_[l], d, dqkv_, W, H * dh, KV * dh, dh_, nullptr));
+    if (lora && (c.lora_targets & (1 << kLoraV)))
+      CK(lora_backward(l, kLoraV, h1_[l], d, dqkv_, W, (H + KV) * dh, KV * dh, dh_, nullptr));
+    const Param& g1 = P(pre + "attn_norm.weight");
+    KL(launch_rmsnorm_bwd(x_[l], dh_, P32(g1), dx_, dx_, dxp_, gpart_, nblk, N, d, c.rms_eps, stream_));
+    if (full) KL(launch_colsum(gpart_, nblk, d, G32(g1), 0, stream_));
+  }
+  if (full) KL(launch_embed_scatter(dx_, ord_, seg_start_, seg_id_, nseg_dev_, N, G32(E), d, stream_));
+  return 0;
+}
+
+int LlamaEngine::enqueue_optimizer() {
+  if (allreduce_fn_) CK(allreduce_fn_(allreduce_ctx_, grad_arena(), n_train_, stream_));
+  Planes pp{static_cast<bf16*>(phi_.p), static_cast<bf16*>(plo_.p)};
+  KL(launch_adamw(static_cast<float*>(p32_.p), static_cast<float*>(g_.p), static_cast<float*>(m_.p),
+                  static_cast<float*>(v_.p), pp, n_train_, hp_, grad_scale_, stream_));
+  return 0;
+}
+
+int LlamaEngine::enqueue_step(bool run_optimizer) {
+  counting_ = 0;
+  CK(enqueue_forward());
+  CK(enqueue_backward());
+  if (run_optimizer) CK(enqueue_optimizer());
+  launches_ = counting_;
+  return 0;
+}
+
+int LlamaEngine::step(bool is_first, bool run_optimizer) {
+  if (!realized_) return -2;
+  CU(cudaSetDevice(device_));
+  if (is_first) {
+    CU(cudaMemsetAsync(m_.p, 0, m_.bytes, stream_));
+    CU(cudaMemsetAsync(v_.p, 0, v_.bytes, stream_));
+  }
+  // The embedding scatter's segment count is baked into a captured graph.
+  const bool can_graph = use_graph_ && run_optimizer;
+  if (can_graph && graph_valid_ && graph_dense_ == dense_labels_) {
+    CU(cudaGraphLaunch(graph_, stream_));
+    return 0;
+  }
+  if (!can_graph) return enqueue_step(run_optimizer);
+  // First use of this configuration: run eagerly once (validates every launch),
+  // then capture the same program for replay.
+  CK(enqueue_step(run_optimizer));
+  cudaGraph_t g = nullptr;
+  CU(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+  const int rc = enqueue_step(run_optimizer);
+  cudaError_t ce = cudaStreamEndCapture(stream_, &g);
+  if (rc || ce != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    return rc ? rc : -3;
+  }
+  if (graph_) cudaGraphExecDestroy(graph_);
+  graph_ = nullptr;
+  ce = cudaGraphInstantiate(&graph_, g, 0);
+  cudaGraphDestroy(g);
+  CU(ce);
+  graph_valid_ = true;
+  graph_dense_ = dense_labels_;
+  return 0;
+}
+
+int LlamaEngine::forward_only() {
+  if (!realized_) return -2;
+  counting_ = 0;
+  return enqueue_forward();
+}
+
+float LlamaEngine::last_loss() {
+  float h = NAN;
+  cudaStreamSynchronize(stream_);
+  cudaMemcpy(&h, loss_, 4, cudaMemcpyDeviceToHost);
+  return h;
+}
+
+int LlamaEngine::sync() {
+  CU(cudaStreamSynchronize(stream_));
+  return 0;
+}
+
+}  // namespace tb2
+
+namespace tb2 {
+
+long long LlamaEngine::debug_activation(int which, int layer, float* dst, long long cap) {
+  if (!realized_) return -2;
+  const LlamaConfig& c = cfg_;
+  const long long N = this->N(), d = c.d_model, H = c.n_heads, KV = c.n_kv, dh = c.d_head, ff = c.d_ff;
+  const long long W = (H + 2 * KV) * dh;
+  if (layer < 0 || layer > c.n_layers || (layer == c.n_layers && which != 0)) return -1;
+  const float* f = nullptr;
+  Planes p{};
+  long long n = 0;
+  switch (which) {
+    case 0: f = x_[layer]; n = N * d; break;
+    case 1: f = x1_[layer]; n = N * d; break;
+    case 2: p = h1_[layer]; n = N * d; break;
+    case 3: p = Qh_[layer]; n = N * H * dh; break;
+    case 4: p = Kh_[layer]; n = N * KV * dh; break;
+    case 5: p = Vh_[layer]; n = N * KV * dh; break;
+    case 6: p = Pm_[layer]; n = (long long)c.B * H * c.T * c.T; break;
+    case 7: p = O_[layer]; n = N * H * dh; break;
+    case 8: f = gu_[layer]; n = N * 2 * ff; break;
+    case 9: p = a_[layer]; n = N * ff; break;
+    case 10: f = logits_; n = N * c.vocab; break;
+    case 11: p = h2_[layer]; n = N * d; break;
+    case 12: f = qkv_; n = N * W; break;
+    default: return -1;
+  }
+  if (!dst || cap < n) return n;
+  CU(cudaStreamSynchronize(stream_));
+  if (f) {
+    CU(cudaMemcpy(dst, f, n * 4, cudaMemcpyDeviceToHost));
+    return n;
+  }
+  std::vector<bf16> hi(n), lo(n);
+  CU(cudaMemcpy(hi.data(), p.hi, n * 2, cudaMemcpyDeviceToHost));
+  CU(cudaMemcpy(lo.data(), p.lo, n * 2, cudaMemcpyDeviceToHost));
+  for (long long i = 0; i < n; ++i) dst[i] = __bfloat162float(hi[i]) + __bfloat162float(lo[i]);
+  return n;
+}
+
+}  // namespace tb2

@@ -1,0 +1,159 @@
+// The Llama training step on one GPU: the program LlamaSeqEngine#build_training_step
+// (lib/toy/llm/engine/llama_seq_engine.rb:1786-1958) builds as a ggml graph,
+// expressed here as a fixed sequence of sm_100a kernels on one stream and
+// replayed as a CUDA graph.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <map>
+#include <string>
+#include <vector>
+
+#include "gemm.cuh"
+#include "kernels.cuh"
+
+namespace tb2 {
+
+enum LoraTarget : int { kLoraQ = 0, kLoraK, kLoraV, kLoraO, kLoraGate, kLoraUp, kLoraDown, kLoraCount };
+
+struct LlamaConfig {
+  int vocab = 0, d_model = 0, n_heads = 0, n_kv = 0, d_head = 0, d_ff = 0, n_layers = 0;
+  float rope_base = 1e4f, rms_eps = 1e-5f, freq_scale = 1.0f;
+  int tied = 1, qkv_bias = 0;
+  int T = 0, B = 1;
+  int mode = 0;           // 0 full fine-tune, 1 QLoRA (frozen Q8_0 base + LoRA adapters)
+  int lora_rank = 0;
+  float lora_alpha = 0.f;
+  int lora_targets = 0;   // bitmask over LoraTarget
+  std::vector<float> freq_factors;   // d_head/2 llama3-style factors, or empty
+};
+
+// One named parameter inside the arenas.
+struct Param {
+  std::string name;
+  long long offset = 0;   // element offset in the arenas
+  int rows = 1, cols = 1; // row-major [rows][cols]
+  bool trainable = false;
+  bool q8 = false;        // frozen projection stored as Q8_0 blocks
+  long long q8_offset = 0;
+  long long numel() const { return (long long)rows * cols; }
+};
+
+struct DeviceBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+};
+
+class LlamaEngine {
+ public:
+  LlamaEngine(const LlamaConfig& cfg, int device);
+  ~LlamaEngine();
+  int realize();          // allocate everything; returns 0 or negative
+
+  const LlamaConfig& cfg() const { return cfg_; }
+  int N() const { return cfg_.T * cfg_.B; }
+  cudaStream_t stream() const { return stream_; }
+  const std::vector<Param>& params() const { return params_; }
+  const Param* find(const std::string& name) const;
+  long long n_trainable() const { return n_train_; }
+  long long n_total() const { return n_total_; }
+
+  // Parameter I/O (host f32, row-major). Uploading refreshes the planes.
+  int set_param(const std::string& name, const float* host, long long n);
+  int get_param(const std::string& name, float* host, long long n);
+  int get_grad(const std::string& name, float* host, long long n);
+  int get_moment(const std::string& name, int which, float* host, long long n);
+  int set_param_q8(const std::string& name, const uint8_t* blocks, long long nbytes);
+  int get_param_q8(const std::string& name, uint8_t* blocks, long long nbytes);
+  // Standard deviations stay f64 end to end: the reference draws in f64 and
+  // narrows each value once, so a float std would shift every draw.
+  int init_random(long long seed, double init_scale, double std_all, double lora_a_std, double lora_b_std);
+
+  // Per-step inputs.
+  int set_tokens(const long long* ids, int n);
+  int set_positions(const long long* pos, int n);
+  int set_label_ids(const long long* ids, int n);
+  int set_labels_dense(const double* lab, long long n);
+  int set_hp(const double* hp, int n);
+
+  // One step: forward, CE, backward, (allreduce hook), AdamW. is_first zeroes
+  // the Adam moments first (tnn_graph_reset semantics).
+  int step(bool is_first, bool run_optimizer = true);
+  int forward_only();                    // loss only
+  float last_loss();                     // synchronises
+  int sync();
+
+  // Gradient-arena access for data-parallel reduction.
+  float* grad_arena() { return static_cast<float*>(g_.p); }
+  void set_grad_scale(float s) { grad_scale_ = s; }
+  void set_allreduce_hook(int (*fn)(void*, float*, long long, cudaStream_t), void* ctx) {
+    allreduce_fn_ = fn;
+    allreduce_ctx_ = ctx;
+    graph_valid_ = false;
+  }
+  void set_use_graph(bool on) { use_graph_ = on; graph_valid_ = false; }
+  int launches_per_step() const { return launches_; }
+  // Copy a saved activation of the last step to the host as f32 (planes are
+  // reconstructed as hi + lo). Returns the element count, or negative.
+  long long debug_activation(int which, int layer, float* dst, long long cap);
+
+ private:
+  int alloc(DeviceBuf& b, size_t bytes);
+  int add_param(const std::string& name, int rows, int cols, bool trainable, bool q8);
+  int enqueue_forward();
+  int enqueue_backward();
+  int enqueue_optimizer();
+  int enqueue_step(bool run_optimizer);
+  int gemm(const GemmDesc& d);
+  int lora_forward(int l, int t, Planes X, int d_in, float* Y, long long ldy, int col_off, int d_out);
+  int lora_backward(int l, int t, Planes X, int d_in, Planes dY, long long ld_dy, int col_off, int d_out,
+                    float* dX, const Epilogue* dx_scatter);
+  float* P32(const Param& p) { return static_cast<float*>(p32_.p) + p.offset; }
+  float* G32(const Param& p) { return static_cast<float*>(g_.p) + p.offset; }
+  Planes PP(const Param& p) {
+    return Planes{static_cast<bf16*>(phi_.p) + p.offset, static_cast<bf16*>(plo_.p) + p.offset};
+  }
+  const Param& P(const std::string& n) const;
+  int refresh_planes(const Param& p);
+
+  LlamaConfig cfg_;
+  int device_ = 0;
+  cudaStream_t stream_ = nullptr;
+  bool realized_ = false;
+  std::vector<Param> params_;
+  std::map<std::string, int> pidx_;
+  long long n_train_ = 0, n_total_ = 0, q8_bytes_ = 0;
+  // arenas
+  DeviceBuf p32_, phi_, plo_, g_, m_, v_, q8_;
+  // activations and scratch
+  std::vector<DeviceBuf> bufs_;
+  std::vector<float*> x_, x1_, gu_;
+  std::vector<Planes> h1_, h2_, a_, Qh_, Kh_, Vh_, Pm_, O_;
+  std::vector<std::vector<Planes>> lora_u_;   // [layer][target]
+  float *qkv_ = nullptr, *S_ = nullptr, *logits_ = nullptr, *loss_rows_ = nullptr, *loss_ = nullptr;
+  float *dx_ = nullptr, *dh_ = nullptr, *da_ = nullptr, *dO32_ = nullptr, *dQ_ = nullptr, *dK_ = nullptr,
+        *dV_ = nullptr, *gpart_ = nullptr, *u32_ = nullptr, *du32_ = nullptr;
+  Planes xf_, dlog_, dxp_, dgu_, dO_, dS_, dqkv_, up_tmp_, du_;
+  // inputs
+  int *ids_ = nullptr, *pos_ = nullptr, *labels_ = nullptr, *ord_ = nullptr, *seg_start_ = nullptr,
+      *seg_id_ = nullptr, *nseg_dev_ = nullptr;
+  float *labels_dense_ = nullptr, *hp_ = nullptr, *cs_ = nullptr;
+  int cs_rows_ = 0, nseg_ = 0;
+  bool dense_labels_ = false;
+  // host staging (pinned)
+  void* stage_ = nullptr;
+  size_t stage_bytes_ = 0;
+  int* err_ = nullptr;
+  float grad_scale_ = 1.0f;
+  int (*allreduce_fn_)(void*, float*, long long, cudaStream_t) = nullptr;
+  void* allreduce_ctx_ = nullptr;
+  bool use_graph_ = true;
+  cudaGraphExec_t graph_ = nullptr;
+  bool graph_valid_ = false;
+  bool graph_dense_ = false;
+  int launches_ = 0;
+  int counting_ = 0;
+  int staged(size_t bytes);
+};
+
+}  // namespace tb2

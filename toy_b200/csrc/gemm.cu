@@ -175,7 +175,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const Epilogue& e = args.epi;
     const bool row_ok = ok && m < args.M;
     long long row_off = 0;
-    if (row_ok) row_off = (long long)z * e.bstride + (long long)(m / e.m_div) * e.m_s1 + (long long)(m % e.m_div) * e.m_s0;
+    if (row_ok)
+      row_off = (long long)(z / e.z_div) * e.z_s1 + (long long)(z % e.z_div) * e.bstride +
+                (long long)(m / e.m_div) * e.m_s1 + (long long)(m % e.m_div) * e.m_s0;
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
       float v[32];
@@ -334,7 +336,8 @@ int gemm_launch(const GemmDesc& d, int* dev_err, cudaStream_t stream) {
   // Epilogue vector stores need 16-byte aligned rows.
   const Epilogue& e = d.epi;
   const int al = (e.mode == kEpiStoreSplit || e.mode == kEpiStoreBoth) ? 8 : 4;
-  if ((e.m_s0 % al) || (e.m_s1 % al) || (e.n_s1 % al) || (e.bstride % al) || (e.n_div % 32)) return -3;
+  if ((e.m_s0 % al) || (e.m_s1 % al) || (e.n_s1 % al) || (e.bstride % al) || (e.z_s1 % al) || (e.n_div % 32))
+    return -3;
   if (!d.a.hi || !d.b.hi || (d.split && (!d.a.lo || !d.b.lo))) return -4;
   switch (pick_bn(d.N)) {
     case 64: return d.split ? launch_bn<64, true>(d, dev_err, stream) : launch_bn<64, false>(d, dev_err, stream);

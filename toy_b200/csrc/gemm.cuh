@@ -43,7 +43,8 @@ enum EpiMode : int {
 };
 
 // Output element (z, m, n) lives at
-//   z * bstride + (m / m_div) * m_s1 + (m % m_div) * m_s0 + (n / n_div) * n_s1 + (n % n_div)
+//   (z / z_div) * z_s1 + (z % z_div) * bstride
+//   + (m / m_div) * m_s1 + (m % m_div) * m_s0 + (n / n_div) * n_s1 + (n % n_div)
 // (n_div must be a multiple of 32). Row-major [M][ldc] is m_div = n_div = huge,
 // m_s0 = ldc; a head-major scatter uses n_div = head width.
 struct Epilogue {
@@ -54,6 +55,8 @@ struct Epilogue {
   __nv_bfloat16* out_hi = nullptr;
   __nv_bfloat16* out_lo = nullptr;
   long long bstride = 0;
+  int z_div = 1 << 30;
+  long long z_s1 = 0;
   int m_div = 1 << 30;
   long long m_s1 = 0, m_s0 = 0;
   int n_div = 1 << 30;

@@ -1,11 +1,88 @@
-// Bandwidth-bound kernels of the training step (launch wrappers).
+// Bandwidth-bound kernels of the training step (launch wrappers). All inputs
+// and outputs are device pointers; "planes" means a (hi, lo) pair of bf16
+// arrays carrying an f32 value as hi + lo (see gemm.cuh).
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <cstdint>
 
 namespace tb2 {
 
+using bf16 = __nv_bfloat16;
+
+struct Planes {
+  bf16* hi = nullptr;
+  bf16* lo = nullptr;
+};
+
 // hi = rn_bf16(x), lo = rn_bf16(x - hi)
-int launch_split_f32(const float* x, __nv_bfloat16* hi, __nv_bfloat16* lo, long long n, cudaStream_t st);
+int launch_split_f32(const float* x, bf16* hi, bf16* lo, long long n, cudaStream_t st);
+
+// x0[n, :] = E[ids[n], :]   (ggml get_rows)
+int launch_embed_gather(const float* E, const int* ids, float* x0, int N, int d, cudaStream_t st);
+
+// dE[id, :] += sum of dx rows with that id, in a fixed order: `order` lists the
+// rows grouped by id, seg_start[k]..seg_start[k+1] is the k-th group (ggml get_rows_back).
+// The segment count is read from device memory (*nseg_dev) so a captured graph
+// stays valid for any token batch; max_seg bounds the grid.
+int launch_embed_scatter(const float* dx, const int* order, const int* seg_start, const int* seg_id,
+                         const int* nseg_dev, int max_seg, float* dE, int d, cudaStream_t st);
+
+// h = rmsnorm(x) * gamma written as planes (ggml rms_norm + mul).
+int launch_rmsnorm_fwd(const float* x, const float* gamma, Planes h, int N, int d, float eps, cudaStream_t st);
+
+// dx = dres + rms_norm_back(x, dh * gamma) (f32, may alias dres) and its planes;
+// per-block partial sums of dh * x * rrms into gpart[nblk][d] (for dgamma).
+int launch_rmsnorm_bwd(const float* x, const float* dh, const float* gamma, const float* dres, float* dx,
+                       Planes dxp, float* gpart, int nblk, int N, int d, float eps, cudaStream_t st);
+// gout[c] = (accumulate ? gout[c] : 0) + sum_b gpart[b][c]
+int launch_colsum(const float* gpart, int nblk, int d, float* gout, int accumulate, cudaStream_t st);
+int rmsnorm_bwd_blocks();
+
+// RoPE (NEOX) on the fused q|k|v projection output qkv [N][(H+2KV)*dh] (+ bias),
+// written head-major as planes: Q [B][H][T][dh], K [B][KV][T][dh], V [B][KV][T][dh].
+int launch_rope_qkv_fwd(const float* qkv, const float* bias, const int* pos, const float* cs_tab, int tab_rows,
+                        Planes Q, Planes K, Planes V, int B, int T, int H, int KV, int dh, cudaStream_t st);
+// Inverse: head-major f32 dQ, dK, dV -> token-major planes dqkv [N][(H+2KV)*dh]
+// (rotation by -theta on dQ, dK).
+int launch_rope_qkv_bwd(const float* dQ, const float* dK, const float* dV, const int* pos, const float* cs_tab,
+                        int tab_rows, Planes dqkv, float* dqkv_f32, int B, int T, int H, int KV, int dh,
+                        cudaStream_t st);
+
+// P = softmax(S) over keys k <= q (rows of [Z][T][T]); masked entries 0.
+int launch_softmax_causal_fwd(const float* S, Planes P, long long Z, int T, cudaStream_t st);
+// dS = P * (dP - sum(P * dP)) * scale (ggml soft_max_back), as planes.
+int launch_softmax_causal_bwd(Planes P, const float* dP, Planes dS, long long Z, int T, float scale,
+                              cudaStream_t st);
+
+// a = silu(gate) * up from gu [N][2*ff] (gate | up) -> planes [N][ff].
+int launch_swiglu_fwd(const float* gu, Planes a, int N, int ff, cudaStream_t st);
+// dgate = silu_back(gate, da * up), dup = da * silu(gate) -> planes [N][2*ff].
+int launch_swiglu_bwd(const float* gu, const float* da, Planes dgu, int N, int ff, cudaStream_t st);
+
+// Cross-entropy over rows of logits [N][V]: loss_rows[n] and dlogits planes
+// ((softmax - y) / N). Labels are ids (label_ids, -1 = none) or, when
+// label_dense != nullptr, a dense [N][V] distribution.
+int launch_cross_entropy(const float* logits, const int* label_ids, const float* label_dense, float* loss_rows,
+                         Planes dlogits, int N, int V, cudaStream_t st);
+// loss = sum(loss_rows) / N   (single block, fixed order)
+int launch_loss_reduce(const float* loss_rows, int N, float* loss, cudaStream_t st);
+
+// AdamW over a flat arena (opt_step_adamw semantics, hp = device float[7]):
+// g_eff = g * grad_scale; writes p, m, v and the planes of p.
+int launch_adamw(float* p, const float* g, float* m, float* v, Planes pp, long long n, const float* hp,
+                 float grad_scale, cudaStream_t st);
+
+// Q8_0 blocks [rows][K/32*34] -> planes [rows][K] (value = d * q, exact in f32).
+// When f32 != nullptr the exact f32 values are written there too.
+int launch_q8_0_to_planes(const uint8_t* q, Planes out, float* f32, long long rows, int K, cudaStream_t st);
+// f32 [rows][K] -> Q8_0 blocks (ggml quantize_row_q8_0_ref, bit-exact).
+int launch_q8_0_quantize(const float* x, uint8_t* q, long long rows, int K, cudaStream_t st);
+
+// out[c] = sum over rows of x[N][W] (fixed order), e.g. bias gradients.
+int launch_colsum_rows(const float* x, int N, int W, float* out, cudaStream_t st);
+
+// y[i] += x[i]
+int launch_add_inplace(float* y, const float* x, long long n, cudaStream_t st);
 
 }  // namespace tb2
