@@ -181,6 +181,17 @@ int tb2_step_launches(void *sess);
 int tb2_set_use_graph(void *sess, int on);
 int tb2_forward_only(void *sess);
 int tb2_sync(void *sess);
+/* Run n training steps on the already-uploaded inputs (CUDA-graph replay) and
+ * report their device time in *ms (CUDA events on the step stream). The
+ * device-timed counterpart of the reference's TNN_STEP_PROFILE split
+ * (tinynn/tinynn_ggml.c:2054-2103). */
+int tb2_run_steps(void *sess, int n, float *ms);
+/* One eagerly-enqueued step with an event pair around every kernel: fills
+ * kinds[i] (0 GEMM, 1 rmsnorm fwd, 2 rmsnorm bwd, 3 column sums, 4 rope,
+ * 5 softmax, 6 swiglu, 7 cross-entropy, 8 loss reduce, 9 AdamW, 10 embedding,
+ * 11 split, 12 gradient all-reduce), ms[i] and the GEMM algorithmic flops[i].
+ * Returns the launch count (at most cap entries are written). */
+int tb2_profile_step(void *sess, int is_first, int *kinds, float *ms, double *flops, int cap);
 /* Copy a saved activation of the last step to host f32 (for layer-by-layer
  * parity checks): which = 0 x_in, 1 x_after_attn, 2 attn_norm out, 3 Q (head-major,
  * roped), 4 K, 5 V, 6 softmax probs, 7 attention out, 8 gate|up, 9 swiglu out,

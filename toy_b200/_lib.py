@@ -64,6 +64,8 @@ _SIGS = [
     ("tb2_forward_only", I, [VP]),
     ("tb2_sync", I, [VP]),
     ("tb2_debug_activation", LL, [VP, I, I, C.POINTER(C.c_float), LL]),
+    ("tb2_run_steps", I, [VP, I, C.POINTER(C.c_float)]),
+    ("tb2_profile_step", I, [VP, I, C.POINTER(C.c_int), C.POINTER(C.c_float), C.POINTER(C.c_double), I]),
     ("tnn_graph_reset", I, [VP]),
     ("tnn_graph_reset_grads_only", I, [VP]),
     ("tnn_compute_backward", I, [VP]),

@@ -202,6 +202,16 @@ int tb2_forward_only(void* sess) {
   return S(sess)->eng->forward_only();
 }
 
+int tb2_run_steps(void* sess, int n, float* ms) {
+  if (!sess || !S(sess)->eng) return -2;
+  return S(sess)->eng->run_steps(n, ms);
+}
+
+int tb2_profile_step(void* sess, int is_first, int* kinds, float* ms, double* flops, int cap) {
+  if (!sess || !S(sess)->eng) return -2;
+  return S(sess)->eng->profile_step(is_first != 0, kinds, ms, flops, cap);
+}
+
 int tb2_sync(void* sess) {
   if (!sess || !S(sess)->eng) return -2;
   return S(sess)->eng->sync();

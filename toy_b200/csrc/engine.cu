@@ -568,17 +568,56 @@ int LlamaEngine::set_hp(const double* hp, int n) {
 }
 
 // ------------------------------------------------------------------ step program
+void LlamaEngine::prof_begin(int kind, double flops) {
+  while (evpool_.size() < evnext_ + 2) {
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    evpool_.push_back(e);
+  }
+  cur_kind_ = kind;
+  cur_flops_ = flops;
+  cudaEventRecord(evpool_[evnext_], stream_);
+}
+
+void LlamaEngine::prof_end() {
+  cudaEventRecord(evpool_[evnext_ + 1], stream_);
+  recs_.push_back(Rec{cur_kind_, cur_flops_, evpool_[evnext_], evpool_[evnext_ + 1]});
+  evnext_ += 2;
+}
+
 int LlamaEngine::gemm(const GemmDesc& d) {
   ++counting_;
+  if (profiling_) prof_begin(kKGemm, 2.0 * d.M * d.N * d.K * d.batch);
   const int rc = gemm_launch(d, err_, stream_);
+  if (profiling_) prof_end();
   if (rc) fprintf(stderr, "[toy_b200] gemm launch rejected (%d): M=%d N=%d K=%d batch=%d\n", rc, d.M, d.N, d.K, d.batch);
   return rc;
 }
 
-#define KL(x)              \
-  do {                     \
-    ++counting_;           \
-    CK(x);                 \
+namespace {
+int kind_of(const char* call) {
+  static const struct { const char* prefix; int kind; } table[] = {
+      {"launch_rmsnorm_fwd", LlamaEngine::kKRmsFwd}, {"launch_rmsnorm_bwd", LlamaEngine::kKRmsBwd},
+      {"launch_colsum", LlamaEngine::kKColsum},      {"launch_rope", LlamaEngine::kKRope},
+      {"launch_softmax", LlamaEngine::kKSoftmax},    {"launch_swiglu", LlamaEngine::kKSwiglu},
+      {"launch_cross_entropy", LlamaEngine::kKCe},   {"launch_loss_reduce", LlamaEngine::kKLoss},
+      {"launch_adamw", LlamaEngine::kKAdamw},        {"launch_embed", LlamaEngine::kKEmbed},
+      {"launch_split", LlamaEngine::kKSplit}};
+  for (const auto& t : table)
+    if (strncmp(call, t.prefix, strlen(t.prefix)) == 0) return t.kind;
+  return LlamaEngine::kKCount;
+}
+}  // namespace
+
+// Every non-GEMM launch of the step program goes through KL: it counts the
+// launch and, in a profiled step, brackets it with an event pair.
+#define KL(x)                                      \
+  do {                                             \
+    ++counting_;                                   \
+    if (profiling_) prof_begin(kind_of(#x), 0.0);  \
+    const int rc_k = (x);                          \
+    if (profiling_) prof_end();                    \
+    if (rc_k) return rc_k;                         \
   } while (0)
 
 // Y[:, col_off : col_off + d_out] += s * (X A^T) B^T, saving u = X A^T (planes) for backward.
@@ -884,7 +923,12 @@ int LlamaEngine::enqueue_backward() {
 }
 
 int LlamaEngine::enqueue_optimizer() {
-  if (allreduce_fn_) CK(allreduce_fn_(allreduce_ctx_, grad_arena(), n_train_, stream_));
+  if (allreduce_fn_) {
+    if (profiling_) prof_begin(kKAllreduce, 0.0);
+    const int rc = allreduce_fn_(allreduce_ctx_, grad_arena(), n_train_, stream_);
+    if (profiling_) prof_end();
+    CK(rc);
+  }
   Planes pp{static_cast<bf16*>(phi_.p), static_cast<bf16*>(plo_.p)};
   KL(launch_adamw(static_cast<float*>(p32_.p), static_cast<float*>(g_.p), static_cast<float*>(m_.p),
                   static_cast<float*>(v_.p), pp, n_train_, hp_, grad_scale_, stream_));
@@ -933,6 +977,48 @@ int LlamaEngine::step(bool is_first, bool run_optimizer) {
   graph_valid_ = true;
   graph_dense_ = dense_labels_;
   return 0;
+}
+
+int LlamaEngine::run_steps(int n, float* ms) {
+  if (!realized_ || n <= 0 || !ms) return -1;
+  CU(cudaSetDevice(device_));
+  if (use_graph_ && !(graph_valid_ && graph_dense_ == dense_labels_)) CK(step(false, true));  // capture
+  cudaEvent_t a, b;
+  CU(cudaEventCreate(&a));
+  CU(cudaEventCreate(&b));
+  CU(cudaEventRecord(a, stream_));
+  for (int i = 0; i < n; ++i) CK(step(false, true));
+  CU(cudaEventRecord(b, stream_));
+  CU(cudaEventSynchronize(b));
+  CU(cudaEventElapsedTime(ms, a, b));
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  return 0;
+}
+
+int LlamaEngine::profile_step(bool is_first, int* kinds, float* ms, double* flops, int cap) {
+  if (!realized_) return -2;
+  CU(cudaSetDevice(device_));
+  if (is_first) {
+    CU(cudaMemsetAsync(m_.p, 0, m_.bytes, stream_));
+    CU(cudaMemsetAsync(v_.p, 0, v_.bytes, stream_));
+  }
+  profiling_ = true;
+  recs_.clear();
+  evnext_ = 0;
+  const int rc = enqueue_step(true);
+  profiling_ = false;
+  CK(rc);
+  CU(cudaStreamSynchronize(stream_));
+  const int n = (int)recs_.size();
+  for (int i = 0; i < n && i < cap; ++i) {
+    float t = 0.f;
+    cudaEventElapsedTime(&t, recs_[i].a, recs_[i].b);
+    if (kinds) kinds[i] = recs_[i].kind;
+    if (ms) ms[i] = t;
+    if (flops) flops[i] = recs_[i].flops;
+  }
+  return n;
 }
 
 int LlamaEngine::forward_only() {

@@ -97,6 +97,15 @@ class LlamaEngine {
   // reconstructed as hi + lo). Returns the element count, or negative.
   long long debug_activation(int which, int layer, float* dst, long long cap);
 
+  // Timing. run_steps: n steps (graph replay) between two events on the step
+  // stream; returns total milliseconds in *ms. profile_step: one eager step with
+  // an event pair around every launch; fills per-launch kind, duration and
+  // algorithmic FLOPs (GEMMs), returns the launch count.
+  enum Kind : int { kKGemm = 0, kKRmsFwd, kKRmsBwd, kKColsum, kKRope, kKSoftmax, kKSwiglu, kKCe, kKLoss, kKAdamw,
+                    kKEmbed, kKSplit, kKAllreduce, kKCount };
+  int run_steps(int n, float* ms);
+  int profile_step(bool is_first, int* kinds, float* ms, double* flops, int cap);
+
  private:
   int alloc(DeviceBuf& b, size_t bytes);
   int add_param(const std::string& name, int rows, int cols, bool trainable, bool q8);
@@ -154,6 +163,20 @@ class LlamaEngine {
   int launches_ = 0;
   int counting_ = 0;
   int staged(size_t bytes);
+  // profiling (eager only)
+  struct Rec {
+    int kind;
+    double flops;
+    cudaEvent_t a, b;
+  };
+  bool profiling_ = false;
+  std::vector<Rec> recs_;
+  std::vector<cudaEvent_t> evpool_;
+  size_t evnext_ = 0;
+  int cur_kind_ = 0;
+  double cur_flops_ = 0;
+  void prof_begin(int kind, double flops);
+  void prof_end();
 };
 
 }  // namespace tb2
