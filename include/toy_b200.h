@@ -198,6 +198,18 @@ int tb2_profile_step(void *sess, int is_first, int *kinds, float *ms, double *fl
  * 10 logits, 11 ffn_norm out. Returns the element count (cap too small: nothing copied). */
 long long tb2_debug_activation(void *sess, int which, int layer, float *dst, long long cap);
 
+/* Data parallelism (no counterpart in the reference, which has no multi-GPU
+ * training): one process per GPU, each with a full replica and its own batch.
+ * Rank 0 gets a NCCL unique id (128 bytes) and shares it with the other ranks
+ * through any host channel; every rank then calls tb2_dp_init on its realized
+ * session. From then on each step all-reduces the trainable gradients (sum,
+ * NCCL over NVLink) before AdamW, which scales them by 1/world, so every
+ * replica takes the identical update of the global-batch mean gradient. */
+int tb2_nccl_unique_id(void *out, size_t nbytes);
+int tb2_dp_init(void *sess, const void *unique_id, int rank, int world);
+/* Releases the step graph (which holds NCCL work) and then the communicator. */
+int tb2_dp_free(void *sess);
+
 /* tinynn/tinynn_ggml.h:424 — the next tnn_compute_backward zeroes the Adam moments. */
 int tnn_graph_reset(void *sess);
 /* tinynn/tinynn_ggml.h:419 — gradients are overwritten by every backward; no-op. */

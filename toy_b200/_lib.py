@@ -65,6 +65,9 @@ _SIGS = [
     ("tb2_sync", I, [VP]),
     ("tb2_debug_activation", LL, [VP, I, I, C.POINTER(C.c_float), LL]),
     ("tb2_run_steps", I, [VP, I, C.POINTER(C.c_float)]),
+    ("tb2_nccl_unique_id", I, [VP, SZ]),
+    ("tb2_dp_init", I, [VP, VP, I, I]),
+    ("tb2_dp_free", I, [VP]),
     ("tb2_profile_step", I, [VP, I, C.POINTER(C.c_int), C.POINTER(C.c_float), C.POINTER(C.c_double), I]),
     ("tnn_graph_reset", I, [VP]),
     ("tnn_graph_reset_grads_only", I, [VP]),

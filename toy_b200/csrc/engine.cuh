@@ -92,6 +92,11 @@ class LlamaEngine {
     graph_valid_ = false;
   }
   void set_use_graph(bool on) { use_graph_ = on; graph_valid_ = false; }
+  void drop_graph() {
+    if (graph_) cudaGraphExecDestroy(graph_);
+    graph_ = nullptr;
+    graph_valid_ = false;
+  }
   int launches_per_step() const { return launches_; }
   // Copy a saved activation of the last step to the host as f32 (planes are
   // reconstructed as hi + lo). Returns the element count, or negative.

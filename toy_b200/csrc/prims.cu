@@ -10,6 +10,7 @@ namespace tb2 {
 
 Session::~Session() {
   if (device >= 0) cudaSetDevice(device);
+  dp_free(this);
   for (auto& t : tensors)
     if (t->data && !t->view_of) cudaFree(t->data);
   if (pstream) cudaStreamDestroy(pstream);

@@ -12,6 +12,11 @@
 namespace tb2 {
 
 struct Session;
+struct DpState;
+
+// Data-parallel gradient reduction (dp.cu).
+void dp_free(Session* s);
+int nccl_allreduce_entry(void* ctx, float* buf, long long n, cudaStream_t st);
 
 struct Tensor {
   enum Role : int { kPrim = 0, kIds, kPos, kLabels, kHp, kLoss, kParam };
@@ -42,6 +47,7 @@ struct Session {
   std::vector<std::unique_ptr<Tensor>> tensors;
   Tensor* io[TB2_IO_COUNT] = {nullptr};
   bool first_pending = false;
+  DpState* dp = nullptr;
   // primitive op graph
   std::vector<Tensor*> nodes;
   bool prim_realized = false;

@@ -1,0 +1,83 @@
+"""Data-parallel training across the GPUs of one node (one process per GPU).
+
+The gradient all-reduce itself runs inside the library (NCCL on the step
+stream, include/toy_b200.h tb2_dp_init). This module is the host side: it uses
+torch.distributed (gloo, over the torchrun rendezvous) only to hand rank 0's
+NCCL unique id to every rank, and for host barriers / max-over-ranks timing.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import datetime
+import os
+
+from ._lib import check, lib
+
+UID_BYTES = 128
+
+
+def _pg():
+    import torch.distributed as dist
+    return dist
+
+
+class DataParallel:
+    def __init__(self, rank: int, world: int, local_rank: int, timeout_s: float = 120.0):
+        dist = _pg()
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        if not dist.is_initialized():
+            dist.init_process_group("gloo", rank=rank, world_size=world,
+                                    timeout=datetime.timedelta(seconds=timeout_s))
+        self.rank, self.world, self.local_rank = rank, world, local_rank
+        self.sess = None
+
+    def exchange_uid(self, uid: bytes | None) -> bytes:
+        """Broadcast rank 0's id bytes to every rank (gloo)."""
+        import torch
+        dist = _pg()
+        t = torch.zeros(UID_BYTES, dtype=torch.uint8)
+        if self.rank == 0:
+            t[:len(uid)] = torch.frombuffer(bytearray(uid), dtype=torch.uint8)
+        dist.broadcast(t, src=0)
+        return bytes(t.numpy().tobytes())
+
+    def attach(self, eng) -> None:
+        """Join the engine's session to the NCCL communicator of all ranks."""
+        L = lib()
+        uid = None
+        if self.rank == 0:
+            buf = (C.c_ubyte * UID_BYTES)()
+            n = L.tb2_nccl_unique_id(C.cast(buf, C.c_void_p), UID_BYTES)
+            if n <= 0:
+                raise RuntimeError(f"tb2_nccl_unique_id failed: {n}")
+            uid = bytes(buf)
+        uid = self.exchange_uid(uid)
+        ubuf = (C.c_ubyte * UID_BYTES).from_buffer_copy(uid)
+        check(L.tb2_dp_init(eng.sess, C.cast(ubuf, C.c_void_p), self.rank, self.world), "tb2_dp_init")
+        self.sess = eng.sess
+
+    def barrier(self) -> None:
+        _pg().barrier()
+
+    def max_scalar(self, x: float) -> float:
+        import torch
+        dist = _pg()
+        t = torch.tensor([float(x)], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def mean_scalar(self, x: float) -> float:
+        import torch
+        dist = _pg()
+        t = torch.tensor([float(x)], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item()) / self.world
+
+    def close(self) -> None:
+        if self.sess:
+            lib().tb2_dp_free(self.sess)
+            self.sess = None
+        dist = _pg()
+        if dist.is_initialized():
+            dist.barrier()
+            dist.destroy_process_group()
