@@ -70,10 +70,14 @@ typedef struct tb2_epilogue {
 /* D_z[m,n] = epilogue(sum_k A_z[m,k] B_z[n,k]) on tcgen05 tensor cores.
  * split = 1: 3 MMAs per k-step over (hi, lo) planes (~fp32 accuracy);
  * split = 0: plain bf16 (hi planes only).
+ * ksplits: K ranges reduced deterministically through a per-device workspace
+ * (0 = chosen from the tile count). causal: 0 none, 1 skip output tiles whose
+ * columns all exceed their rows (attention scores), 2 limit K to each row
+ * tile's last row + 1 (products with causal probabilities).
  * Replaces the arithmetic behind tnn_matmul / tnn_out_prod
  * (tinynn/tinynn_ggml.c:815-835) for the training step. */
 int tb2_gemm(int M, int N, int K, int batch, int split, const tb2_operand *a, const tb2_operand *b,
-             const tb2_epilogue *epi, void *stream);
+             const tb2_epilogue *epi, int ksplits, int causal, void *stream);
 
 /* hi = rn_bf16(x), lo = rn_bf16(x - hi) for n f32 values. */
 int tb2_split_f32(const float *x, void *hi, void *lo, size_t n, void *stream);

@@ -42,11 +42,11 @@ def _epi(mode, out=None, ldc=0, res=None, hi=None, lo=None, bstride=0, alpha=1.0
     return e
 
 
-def _gemm(M, N, K, batch, split, a, b, e):
+def _gemm(M, N, K, batch, split, a, b, e, ksplits=0, causal=0):
     import torch
     from toy_b200._lib import lib
     L = lib()
-    rc = L.tb2_gemm(M, N, K, batch, split, C.byref(a), C.byref(b), C.byref(e), None)
+    rc = L.tb2_gemm(M, N, K, batch, split, C.byref(a), C.byref(b), C.byref(e), ksplits, causal, None)
     assert rc == 0, rc
     torch.cuda.synchronize()
     assert L.tb2_device_error() == 0
@@ -134,6 +134,64 @@ def test_gemm_epilogues(cuda):
     _gemm(M, N, K, 1, 1, a, b, e)
     want = ref.view(M // T, T, H, 64).permute(0, 2, 1, 3).reshape(-1)
     assert _relerr(outh, want) < 2e-5
+
+
+@pytest.mark.parametrize("ksplits", [2, 5, 16])
+@pytest.mark.parametrize("mode", [0, 1, 2, 3])
+def test_gemm_split_k_deterministic(cuda, ksplits, mode):
+    """Split-K partials reduced in split order: exact vs fp64 and bit-identical across runs."""
+    import torch
+    M, N, K = 576, 576, 4096
+    A = torch.randn(K, M, device=cuda)     # stored K x M (MN-major), as the dW GEMMs read activations
+    B = torch.randn(K, N, device=cuda)
+    a, ka = _operand(A, 1, K, 1)
+    b, kb = _operand(B, 1, K, 1)
+    ref = A.double().t() @ B.double()
+    outs = []
+    for _ in range(2):
+        base = torch.randn(M, N, device=cuda, generator=torch.Generator(device="cuda").manual_seed(1))
+        out = base.clone()
+        hi = torch.zeros(M, N, device=cuda, dtype=torch.bfloat16)
+        lo = torch.zeros_like(hi)
+        e = _epi(mode, out, N, res=base if mode == 2 else None, hi=hi if mode == 3 else None,
+                 lo=lo if mode == 3 else None)
+        _gemm(M, N, K, 1, 1, a, b, e, ksplits=ksplits)
+        got = (hi.double() + lo.double()) if mode == 3 else out.double() - (base.double() if mode in (1, 2) else 0)
+        outs.append(got)
+        assert _relerr(got, ref) < 2e-5
+    assert torch.equal(outs[0], outs[1])
+
+
+def test_gemm_auto_split_and_causal(cuda):
+    import torch
+    # auto split-K on a tiny tile grid
+    M, N, K = 128, 192, 8192
+    A = torch.randn(M, K, device=cuda)
+    B = torch.randn(N, K, device=cuda)
+    a, ka = _operand(A, 0, M, 1)
+    b, kb = _operand(B, 0, N, 1)
+    out = torch.zeros(M, N, device=cuda)
+    _gemm(M, N, K, 1, 1, a, b, _epi(0, out, N))
+    assert _relerr(out, A.double() @ B.double().t()) < 2e-5
+    # causal 2: K clamped to each row tile's end (columns of A beyond it are zero in a causal P)
+    T, dh, Z = 512, 64, 3
+    P = torch.tril(torch.rand(Z * T, T, device=cuda).view(Z, T, T)).reshape(Z * T, T)
+    V = torch.randn(Z * T, dh, device=cuda)
+    a, ka = _operand(P, 0, T, Z)
+    b, kb = _operand(V, 1, T, Z)
+    out = torch.zeros(Z, T, dh, device=cuda)
+    _gemm(T, dh, T, Z, 1, a, b, _epi(0, out, dh, bstride=T * dh), causal=2)
+    assert _relerr(out, P.double().view(Z, T, T) @ V.double().view(Z, T, dh)) < 2e-5
+    # causal 1: tiles strictly above the diagonal are skipped, the rest exact
+    Q = torch.randn(Z * T, dh, device=cuda)
+    Kt = torch.randn(Z * T, dh, device=cuda)
+    a, ka = _operand(Q, 0, T, Z)
+    b, kb = _operand(Kt, 0, T, Z)
+    out = torch.full((Z, T, T), 7.0, device=cuda)
+    _gemm(T, T, dh, Z, 1, a, b, _epi(0, out, T, bstride=T * T), causal=1)
+    ref = Q.double().view(Z, T, dh) @ Kt.double().view(Z, T, dh).transpose(1, 2)
+    mask = torch.tril(torch.ones(T, T, dtype=torch.bool, device=cuda))
+    assert _relerr(out[:, mask], ref[:, mask]) < 2e-5
 
 
 def test_split_kernel(cuda):

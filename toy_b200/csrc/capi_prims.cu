@@ -26,10 +26,12 @@ tb2::Operand to_op(const tb2_operand* o) {
 extern "C" {
 
 int tb2_gemm(int M, int N, int K, int batch, int split, const tb2_operand* a, const tb2_operand* b,
-             const tb2_epilogue* epi, void* stream) {
-  if (!a || !b || !epi) return -1;
+             const tb2_epilogue* epi, int ksplits, int causal, void* stream) {
+  if (!a || !b || !epi || ksplits < 0) return -1;
   tb2::GemmDesc d;
   d.M = M; d.N = N; d.K = K; d.batch = batch; d.split = split != 0;
+  d.splits = ksplits;
+  d.causal = causal;
   d.a = to_op(a);
   d.b = to_op(b);
   tb2::Epilogue& e = d.epi;
@@ -49,7 +51,7 @@ int tb2_gemm(int M, int N, int K, int batch, int split, const tb2_operand* a, co
   e.n_s1 = epi->n_s1;
   int* err = tb2::device_error_word();
   if (!err) return -3;
-  const int rc = tb2::gemm_launch(d, err, static_cast<cudaStream_t>(stream));
+  const int rc = tb2::gemm_launch(d, tb2::gemm_scratch(), err, static_cast<cudaStream_t>(stream));
   return rc == 0 ? 0 : (rc <= -10 ? -3 : -1);
 }
 

@@ -588,7 +588,7 @@ void LlamaEngine::prof_end() {
 int LlamaEngine::gemm(const GemmDesc& d) {
   ++counting_;
   if (profiling_) prof_begin(kKGemm, 2.0 * d.M * d.N * d.K * d.batch);
-  const int rc = gemm_launch(d, err_, stream_);
+  const int rc = gemm_launch(d, gemm_scratch(), err_, stream_);
   if (profiling_) prof_end();
   if (rc) fprintf(stderr, "[toy_b200] gemm launch rejected (%d): M=%d N=%d K=%d batch=%d\n", rc, d.M, d.N, d.K, d.batch);
   return rc;
@@ -718,6 +718,7 @@ int LlamaEngine::enqueue_forward() {
     gs.M = T; gs.N = T; gs.K = dh; gs.batch = B * H;
     gs.a = bop(Qh_[l], T, dh, dh, B * H, 0);
     gs.b = bop(Kh_[l], T, dh, dh, B * KV, 0, H, KV, G, 1);
+    gs.causal = 1;   // tiles above the diagonal are never read by the causal softmax
     gs.epi.mode = kEpiStoreF32; gs.epi.out = S_; gs.epi.alpha = scale; gs.epi.m_s0 = T;
     gs.epi.bstride = (long long)T * T;
     CK(gemm(gs));
@@ -727,6 +728,7 @@ int LlamaEngine::enqueue_forward() {
     go.M = T; go.N = dh; go.K = T; go.batch = B * H;
     go.a = bop(Pm_[l], T, T, T, B * H, 0);
     go.b = bop(Vh_[l], T, dh, dh, B * KV, 1, H, KV, G, 1);
+    go.causal = 2;   // P is zero for keys past the tile's last query
     go.epi.mode = kEpiStoreSplit; go.epi.out_hi = O_[l].hi; go.epi.out_lo = O_[l].lo;
     go.epi.z_div = H; go.epi.z_s1 = (long long)T * H * dh; go.epi.bstride = dh; go.epi.m_s0 = (long long)H * dh;
     CK(gemm(go));
@@ -869,6 +871,7 @@ int LlamaEngine::enqueue_backward() {
     gp.M = T; gp.N = T; gp.K = dh; gp.batch = B * H;
     gp.a = bop(dO_, T, dh, dh, B * H, 0);
     gp.b = bop(Vh_[l], T, dh, dh, B * KV, 0, H, KV, G, 1);
+    gp.causal = 1;
     gp.epi.mode = kEpiStoreF32; gp.epi.out = S_; gp.epi.m_s0 = T; gp.epi.bstride = (long long)T * T;
     CK(gemm(gp));
     KL(launch_softmax_causal_bwd(Pm_[l], S_, dS_, (long long)B * H, T, scale, stream_));
@@ -876,6 +879,7 @@ int LlamaEngine::enqueue_backward() {
     gq.M = T; gq.N = dh; gq.K = T; gq.batch = B * H;
     gq.a = bop(dS_, T, T, T, B * H, 0);
     gq.b = bop(Kh_[l], T, dh, dh, B * KV, 1, H, KV, G, 1);
+    gq.causal = 2;   // dS is zero past the diagonal
     gq.epi.mode = kEpiStoreF32; gq.epi.out = dQ_; gq.epi.m_s0 = dh; gq.epi.bstride = (long long)T * dh;
     CK(gemm(gq));
     GemmDesc gk;

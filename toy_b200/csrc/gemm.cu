@@ -1,10 +1,24 @@
-// Split-bf16 tensor-core GEMM for sm_100a: TMA-fed shared-memory pipeline,
-// single-thread tcgen05.mma issue into a TMEM accumulator, 4-warp epilogue.
+// Split-bf16 tensor-core GEMM for sm_100a: persistent CTAs, TMA-fed
+// shared-memory pipeline, single-thread tcgen05.mma issue into one of two TMEM
+// accumulators, 4-warp epilogue.
 //
-// CTA = 6 warps:  warp 0 TMA producer, warp 1 TMEM owner + MMA issuer,
+// CTA = 6 warps: warp 0 TMA producer, warp 1 TMEM owner + MMA issuer,
 // warps 2..5 epilogue (warp w reads TMEM lanes 32*(w%4) .. 32*(w%4)+31).
-// One 128 x BN output tile per CTA; K is walked in 64-element blocks through a
-// STAGES-deep ring of shared-memory buffers guarded by full/empty mbarriers.
+// Each CTA walks the work units u = blockIdx.x, blockIdx.x + gridDim.x, ...;
+// a unit is one 128 x BN output tile (of one batch entry) over a range of K.
+// The producer's stage ring runs across units; the MMA issuer alternates
+// between two TMEM accumulators so the epilogue of unit i overlaps the
+// mainloop of unit i+1.
+//
+// Split-K: when the tile grid is too small for the 148 SMs, K is cut into S
+// ranges. Every unit writes its f32 partial tile to a workspace; the CTA that
+// arrives last on the tile's counter sums the S partials in split order (so
+// the result does not depend on arrival order), applies the epilogue, and
+// resets the counter for the next launch.
+//
+// Causal modes for attention: 1 skips tiles whose keys all exceed their
+// queries (n0 > m0 + 127); 2 clamps K (keys) to m0 + 128 because P / dS are
+// zero beyond the diagonal.
 #include "gemm.cuh"
 #include "tc_common.cuh"
 
@@ -20,13 +34,17 @@ constexpr int BM = 128;
 constexpr int BK = 64;          // one 128-byte swizzle atom of bf16 along K
 constexpr int kThreads = 192;
 constexpr int kSmemBudget = 200 * 1024;
+constexpr int kNumSMs = 148;
 
 struct KArgs {
   int M, N, K, batch;
   int a_mn, b_mn;
   int a_bdiv1, a_bmul1, a_bdiv2, a_bmul2;
   int b_bdiv1, b_bmul1, b_bdiv2, b_bmul2;
+  int tiles_m, tiles_n, splits, units, kb_total, causal;
   Epilogue epi;
+  float* ws;
+  int* sem;
   int* err;
 };
 
@@ -38,7 +56,8 @@ template <int BN>
 struct Cfg {
   static constexpr int kTileA = BM * BK * 2;  // bytes per plane
   static constexpr int kTileB = BN * BK * 2;
-  static constexpr int kTmemCols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  static constexpr uint32_t kAccCols = BN <= 64 ? 64 : BN <= 128 ? 128 : 256;  // one accumulator
+  static constexpr uint32_t kTmemCols = 2 * kAccCols;                           // double buffered
 };
 
 template <int BN, bool SPLIT>
@@ -47,6 +66,105 @@ struct Stages {
   static constexpr int kStages = (kSmemBudget / kStageBytes) > 6 ? 6 : (kSmemBudget / kStageBytes);
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align slack*/ + 256 /*barriers*/;
 };
+
+struct Unit {
+  int z, m0, n0, kb0, kb1, tile;
+  bool skip;
+};
+
+template <int BN>
+__device__ __forceinline__ Unit decode(const KArgs& a, int u) {
+  Unit r;
+  const int s = u % a.splits;
+  int t = u / a.splits;
+  r.tile = t;
+  r.n0 = (t % a.tiles_n) * BN;
+  t /= a.tiles_n;
+  r.m0 = (t % a.tiles_m) * BM;
+  r.z = t / a.tiles_m;
+  r.skip = a.causal == 1 && r.n0 > r.m0 + BM - 1;
+  int kbt = a.kb_total;
+  if (a.causal == 2) {
+    const int kmax = min(a.K, r.m0 + BM);
+    kbt = (kmax + BK - 1) / BK;
+  }
+  r.kb0 = (int)((long long)s * kbt / a.splits);
+  r.kb1 = (int)((long long)(s + 1) * kbt / a.splits);
+  return r;
+}
+
+// Apply the epilogue to the 32 consecutive outputs (m, nc .. nc+31) held in v.
+__device__ __forceinline__ void epi_store(const Epilogue& e, int N, int z, int m, int nc, float (&v)[32]) {
+  const long long off = (long long)(z / e.z_div) * e.z_s1 + (long long)(z % e.z_div) * e.bstride +
+                        (long long)(m / e.m_div) * e.m_s1 + (long long)(m % e.m_div) * e.m_s0 +
+                        (long long)(nc / e.n_div) * e.n_s1 + (nc % e.n_div);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] *= e.alpha;
+  const bool full_chunk = nc + 32 <= N;
+  if (e.mode == kEpiStoreF32 || e.mode == kEpiAccumF32 || e.mode == kEpiResidF32 || e.mode == kEpiStoreBoth) {
+    float* dst = e.out + off;
+    if (full_chunk) {
+      float4* d4 = reinterpret_cast<float4*>(dst);
+      if (e.mode == kEpiAccumF32) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float4 o = d4[i];
+          o.x += v[4 * i]; o.y += v[4 * i + 1]; o.z += v[4 * i + 2]; o.w += v[4 * i + 3];
+          d4[i] = o;
+        }
+      } else if (e.mode == kEpiResidF32) {
+        const float4* r4 = reinterpret_cast<const float4*>(e.res + off);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 r = r4[i];
+          d4[i] = make_float4(r.x + v[4 * i], r.y + v[4 * i + 1], r.z + v[4 * i + 2], r.w + v[4 * i + 3]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if (nc + i < N) {
+          if (e.mode == kEpiAccumF32) dst[i] += v[i];
+          else if (e.mode == kEpiResidF32) dst[i] = e.res[off + i] + v[i];
+          else dst[i] = v[i];
+        }
+      }
+    }
+  }
+  if (e.mode == kEpiStoreSplit || e.mode == kEpiStoreBoth) {
+    __nv_bfloat16* dh = e.out_hi + off;
+    __nv_bfloat16* dl = e.out_lo + off;
+    if (full_chunk) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint32_t h[4], l[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float x0 = v[8 * i + 2 * j], x1 = v[8 * i + 2 * j + 1];
+          const __nv_bfloat16 h0 = __float2bfloat16_rn(x0), h1 = __float2bfloat16_rn(x1);
+          const __nv_bfloat16 l0 = __float2bfloat16_rn(x0 - __bfloat162float(h0));
+          const __nv_bfloat16 l1 = __float2bfloat16_rn(x1 - __bfloat162float(h1));
+          h[j] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+          l[j] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
+        }
+        reinterpret_cast<uint4*>(dh)[i] = make_uint4(h[0], h[1], h[2], h[3]);
+        reinterpret_cast<uint4*>(dl)[i] = make_uint4(l[0], l[1], l[2], l[3]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if (nc + i < N) {
+          const __nv_bfloat16 h0 = __float2bfloat16_rn(v[i]);
+          dh[i] = h0;
+          dl[i] = __float2bfloat16_rn(v[i] - __bfloat162float(h0));
+        }
+      }
+    }
+  }
+}
 
 template <int BN, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -57,27 +175,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kTileA = Cfg<BN>::kTileA;
   constexpr int kTileB = Cfg<BN>::kTileB;
   constexpr int kStageBytes = Stages<BN, SPLIT>::kStageBytes;
+  constexpr uint32_t kAccCols = Cfg<BN>::kAccCols;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
   uint64_t* empty = full + STAGES;
-  uint64_t* accum_full = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_full + 1);
+  uint64_t* tfull = empty + STAGES;   // [2] accumulator ready for the epilogue
+  uint64_t* tempty = tfull + 2;       // [2] accumulator drained by the epilogue
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int n0 = blockIdx.x * BN;
-  const int m0 = blockIdx.y * BM;
-  const int z = blockIdx.z;
-  const int num_kb = (args.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -94,37 +213,46 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&map_a_hi);
       tma_prefetch_desc(&map_b_hi);
-      const int za = batch_index(z, args.a_bdiv1, args.a_bmul1, args.a_bdiv2, args.a_bmul2);
-      const int zb = batch_index(z, args.b_bdiv1, args.b_bmul1, args.b_bdiv2, args.b_bmul2);
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1, args.err, kErrWaitEmpty)) break;
-        mbar_arrive_expect_tx(&full[s], kStageBytes);
-        uint8_t* st = smem + s * kStageBytes;
-        uint8_t* a_hi = st;
-        uint8_t* b_hi = st + kTileA;
-        uint8_t* a_lo = st + kTileA + kTileB;
-        uint8_t* b_lo = a_lo + kTileA;
-        const int k0 = kb * BK;
-        if (!args.a_mn) {
-          tma_load_3d(a_hi, &map_a_hi, &full[s], k0, m0, za);
-          if (SPLIT) tma_load_3d(a_lo, &map_a_lo, &full[s], k0, m0, za);
-        } else {
-#pragma unroll
-          for (int j = 0; j < BM / 64; ++j) {
-            tma_load_3d(a_hi + j * 64 * 128, &map_a_hi, &full[s], m0 + 64 * j, k0, za);
-            if (SPLIT) tma_load_3d(a_lo + j * 64 * 128, &map_a_lo, &full[s], m0 + 64 * j, k0, za);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < args.units && ok; u += gridDim.x) {
+        const Unit w = decode<BN>(args, u);
+        if (w.skip) continue;
+        const int za = batch_index(w.z, args.a_bdiv1, args.a_bmul1, args.a_bdiv2, args.a_bmul2);
+        const int zb = batch_index(w.z, args.b_bdiv1, args.b_bmul1, args.b_bdiv2, args.b_bmul2);
+        for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, args.err, kErrWaitEmpty)) {
+            ok = false;
+            break;
           }
-        }
-        if (!args.b_mn) {
-          tma_load_3d(b_hi, &map_b_hi, &full[s], k0, n0, zb);
-          if (SPLIT) tma_load_3d(b_lo, &map_b_lo, &full[s], k0, n0, zb);
-        } else {
+          mbar_arrive_expect_tx(&full[s], kStageBytes);
+          uint8_t* st = smem + s * kStageBytes;
+          uint8_t* a_hi = st;
+          uint8_t* b_hi = st + kTileA;
+          uint8_t* a_lo = st + kTileA + kTileB;
+          uint8_t* b_lo = a_lo + kTileA;
+          const int k0 = kb * BK;
+          if (!args.a_mn) {
+            tma_load_3d(a_hi, &map_a_hi, &full[s], k0, w.m0, za);
+            if (SPLIT) tma_load_3d(a_lo, &map_a_lo, &full[s], k0, w.m0, za);
+          } else {
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j) {
-            tma_load_3d(b_hi + j * 64 * 128, &map_b_hi, &full[s], n0 + 64 * j, k0, zb);
-            if (SPLIT) tma_load_3d(b_lo + j * 64 * 128, &map_b_lo, &full[s], n0 + 64 * j, k0, zb);
+            for (int j = 0; j < BM / 64; ++j) {
+              tma_load_3d(a_hi + j * 64 * 128, &map_a_hi, &full[s], w.m0 + 64 * j, k0, za);
+              if (SPLIT) tma_load_3d(a_lo + j * 64 * 128, &map_a_lo, &full[s], w.m0 + 64 * j, k0, za);
+            }
+          }
+          if (!args.b_mn) {
+            tma_load_3d(b_hi, &map_b_hi, &full[s], k0, w.n0, zb);
+            if (SPLIT) tma_load_3d(b_lo, &map_b_lo, &full[s], k0, w.n0, zb);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) {
+              tma_load_3d(b_hi + j * 64 * 128, &map_b_hi, &full[s], w.n0 + 64 * j, k0, zb);
+              if (SPLIT) tma_load_3d(b_lo + j * 64 * 128, &map_b_lo, &full[s], w.n0 + 64 * j, k0, zb);
+            }
           }
         }
       }
@@ -139,110 +267,84 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t b_kstep = args.b_mn ? 2048u : 32u;
       const uint32_t a_lbo = args.a_mn ? 8192u : 16u;
       const uint32_t b_lbo = args.b_mn ? 8192u : 16u;
+      uint32_t it = 0, local = 0;
       bool ok = true;
-      for (int kb = 0; kb < num_kb && ok; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        ok = mbar_wait(&full[s], ph, args.err, kErrWaitFull);
+      for (int u = blockIdx.x; u < args.units && ok; u += gridDim.x) {
+        const Unit w = decode<BN>(args, u);
+        if (w.skip) continue;
+        const uint32_t b = local & 1, tph = (local >> 1) & 1;
+        ok = mbar_wait(&tempty[b], tph ^ 1, args.err, kErrWaitAccum);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t st = smem_u32(smem + s * kStageBytes);
-        const uint32_t a_hi = st, b_hi = st + kTileA, a_lo = st + kTileA + kTileB, b_lo = a_lo + kTileA;
+        const uint32_t acc_tmem = tmem_base + b * kAccCols;
+        for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          ok = mbar_wait(&full[s], ph, args.err, kErrWaitFull);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t st = smem_u32(smem + s * kStageBytes);
+          const uint32_t a_hi = st, b_hi = st + kTileA, a_lo = st + kTileA + kTileB, b_lo = a_lo + kTileA;
 #pragma unroll
-        for (int ks = 0; ks < BK / 16; ++ks) {
-          const uint64_t dah = make_sdesc_sw128(a_hi + ks * a_kstep, a_lbo, 1024);
-          const uint64_t dbh = make_sdesc_sw128(b_hi + ks * b_kstep, b_lbo, 1024);
-          const uint32_t acc = (kb > 0 || ks > 0) ? 1u : 0u;
-          umma_f16(tmem_base, dah, dbh, idesc, acc);
-          if (SPLIT) {
-            const uint64_t dal = make_sdesc_sw128(a_lo + ks * a_kstep, a_lbo, 1024);
-            const uint64_t dbl = make_sdesc_sw128(b_lo + ks * b_kstep, b_lbo, 1024);
-            umma_f16(tmem_base, dal, dbh, idesc, 1u);
-            umma_f16(tmem_base, dah, dbl, idesc, 1u);
+          for (int ks = 0; ks < BK / 16; ++ks) {
+            const uint64_t dah = make_sdesc_sw128(a_hi + ks * a_kstep, a_lbo, 1024);
+            const uint64_t dbh = make_sdesc_sw128(b_hi + ks * b_kstep, b_lbo, 1024);
+            const uint32_t acc = (kb > w.kb0 || ks > 0) ? 1u : 0u;
+            umma_f16(acc_tmem, dah, dbh, idesc, acc);
+            if (SPLIT) {
+              const uint64_t dal = make_sdesc_sw128(a_lo + ks * a_kstep, a_lbo, 1024);
+              const uint64_t dbl = make_sdesc_sw128(b_lo + ks * b_kstep, b_lbo, 1024);
+              umma_f16(acc_tmem, dal, dbh, idesc, 1u);
+              umma_f16(acc_tmem, dah, dbl, idesc, 1u);
+            }
           }
+          umma_commit(&empty[s]);
         }
-        umma_commit(&empty[s]);
+        umma_commit(&tfull[b]);
+        ++local;
       }
-      umma_commit(accum_full);
     }
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
     const int row = q * 32 + lane;
-    const int m = m0 + row;
-    const bool ok = mbar_wait(accum_full, 0, args.err, kErrWaitAccum);
-    tc_fence_after();
     const Epilogue& e = args.epi;
-    const bool row_ok = ok && m < args.M;
-    long long row_off = 0;
-    if (row_ok)
-      row_off = (long long)(z / e.z_div) * e.z_s1 + (long long)(z % e.z_div) * e.bstride +
-                (long long)(m / e.m_div) * e.m_s1 + (long long)(m % e.m_div) * e.m_s0;
+    uint32_t local = 0;
+    for (int u = blockIdx.x; u < args.units; u += gridDim.x) {
+      const Unit w = decode<BN>(args, u);
+      if (w.skip) continue;
+      const uint32_t b = local & 1, tph = (local >> 1) & 1;
+      ++local;
+      const bool ok = mbar_wait(&tfull[b], tph, args.err, kErrWaitAccum);
+      tc_fence_after();
+      const int m = w.m0 + row;
+      const bool row_ok = ok && m < args.M;
+      const uint32_t acc_tmem = tmem_base + b * kAccCols + ((uint32_t)(q * 32) << 16);
+      // split-K partial of split s: plain row-major [M][N] slab s of the workspace
+      float* part = args.ws + (long long)(u % args.splits) * args.M * args.N + (long long)m * args.N;
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      float v[32];
-      tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
-      const int nc = n0 + c * 32;
-      if (!row_ok || nc >= args.N) continue;
-      const long long off = row_off + (long long)(nc / e.n_div) * e.n_s1 + (nc % e.n_div);
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        tmem_ld32(acc_tmem + (uint32_t)(c * 32), v);
+        if (c == BN / 32 - 1) {   // accumulator fully read: hand it back to the MMA issuer
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[b]);
+        }
+        const int nc = w.n0 + c * 32;
+        if (!row_ok || nc >= args.N) continue;
+        if (args.splits > 1) {
+          if (nc + 32 <= args.N) {
+            float4* p4 = reinterpret_cast<float4*>(part + nc);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] *= e.alpha;
-      const bool full_chunk = nc + 32 <= args.N;
-      if (e.mode == kEpiStoreF32 || e.mode == kEpiAccumF32 || e.mode == kEpiResidF32 || e.mode == kEpiStoreBoth) {
-        float* dst = e.out + off;
-        if (full_chunk) {
-          float4* d4 = reinterpret_cast<float4*>(dst);
-          if (e.mode == kEpiAccumF32) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              float4 o = d4[i];
-              o.x += v[4 * i]; o.y += v[4 * i + 1]; o.z += v[4 * i + 2]; o.w += v[4 * i + 3];
-              d4[i] = o;
-            }
-          } else if (e.mode == kEpiResidF32) {
-            const float4* r4 = reinterpret_cast<const float4*>(e.res + off);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              float4 r = r4[i];
-              d4[i] = make_float4(r.x + v[4 * i], r.y + v[4 * i + 1], r.z + v[4 * i + 2], r.w + v[4 * i + 3]);
-            }
+            for (int i = 0; i < 8; ++i) p4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
           } else {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            for (int i = 0; i < 32; ++i)
+              if (nc + i < args.N) part[nc + i] = v[i];
           }
         } else {
-          for (int i = 0; i < 32 && nc + i < args.N; ++i) {
-            if (e.mode == kEpiAccumF32) dst[i] += v[i];
-            else if (e.mode == kEpiResidF32) dst[i] = e.res[off + i] + v[i];
-            else dst[i] = v[i];
-          }
-        }
-      }
-      if (e.mode == kEpiStoreSplit || e.mode == kEpiStoreBoth) {
-        __nv_bfloat16* dh = e.out_hi + off;
-        __nv_bfloat16* dl = e.out_lo + off;
-        if (full_chunk) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            uint32_t h[4], l[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float x0 = v[8 * i + 2 * j], x1 = v[8 * i + 2 * j + 1];
-              const __nv_bfloat16 h0 = __float2bfloat16_rn(x0), h1 = __float2bfloat16_rn(x1);
-              const __nv_bfloat16 l0 = __float2bfloat16_rn(x0 - __bfloat162float(h0));
-              const __nv_bfloat16 l1 = __float2bfloat16_rn(x1 - __bfloat162float(h1));
-              h[j] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
-              l[j] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
-            }
-            reinterpret_cast<uint4*>(dh)[i] = make_uint4(h[0], h[1], h[2], h[3]);
-            reinterpret_cast<uint4*>(dl)[i] = make_uint4(l[0], l[1], l[2], l[3]);
-          }
-        } else {
-          for (int i = 0; i < 32 && nc + i < args.N; ++i) {
-            const __nv_bfloat16 h0 = __float2bfloat16_rn(v[i]);
-            dh[i] = h0;
-            dl[i] = __float2bfloat16_rn(v[i] - __bfloat162float(h0));
-          }
+          epi_store(e, args.N, w.z, m, nc, v);
         }
       }
     }
@@ -253,6 +355,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg<BN>::kTmemCols);
+  }
+}
+
+// Split-K reduction: out(m, n) = epilogue(sum over s in order of ws[s][m][n]).
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int M, int N, Epilogue e) {
+  const long long n32 = (long long)M * ((N + 31) / 32);
+  const long long slab = (long long)M * N;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n32; i += (long long)gridDim.x * blockDim.x) {
+    const int m = (int)(i / ((N + 31) / 32));
+    const int nc = (int)(i % ((N + 31) / 32)) * 32;
+    float v[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) v[k] = 0.f;
+    const float* p = ws + (long long)m * N + nc;
+    if (nc + 32 <= N && (N % 4) == 0) {
+      for (int s = 0; s < splits; ++s) {
+        const float4* p4 = reinterpret_cast<const float4*>(p + s * slab);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float4 x = __ldcs(p4 + k);
+          v[4 * k] += x.x; v[4 * k + 1] += x.y; v[4 * k + 2] += x.z; v[4 * k + 3] += x.w;
+        }
+      }
+    } else {
+      for (int s = 0; s < splits; ++s)
+        for (int k = 0; k < 32; ++k)
+          if (nc + k < N) v[k] += p[s * slab + k];
+    }
+    epi_store(e, N, 0, m, nc, v);
   }
 }
 
@@ -286,8 +417,31 @@ int make_map(CUtensorMap* map, const __nv_bfloat16* base, const Operand& o, int 
   return r == CUDA_SUCCESS ? 0 : -13;
 }
 
+// Estimated microseconds for S K-splits: the busiest CTA's units times
+// (k-blocks per unit x MMA time per k-block + per-unit fill/epilogue), plus for
+// S > 1 the reduction kernel streaming S partial slabs (and a residual) once.
+int choose_splits(const GemmDesc& d, long long tiles, int kb, long long ws_floats, int bn) {
+  if (d.causal || d.batch != 1 || tiles >= kNumSMs || kb < 8) return 1;
+  const double t_kb = (d.split ? 3.0 : 1.0) * 2.0 * BM * bn * BK / 7740.0 / 1965.0;   // us per k-block
+  const double mn_bytes = 4.0 * d.M * d.N;
+  const bool reads_out = d.epi.mode == kEpiAccumF32 || d.epi.mode == kEpiResidF32;
+  int best = 1;
+  double best_t = 1e30;
+  for (int s = 1; s <= 16 && s <= kb / 2; ++s) {
+    if (s > 1 && (long long)s * d.M * d.N > ws_floats) break;
+    const double per_cta = (double)((tiles * s + kNumSMs - 1) / kNumSMs);
+    double t = per_cta * (((kb + s - 1) / s) * t_kb + 1.5);
+    if (s > 1) t += ((s + 1) * mn_bytes + (reads_out ? mn_bytes : 0.0)) / 5.0e6 + 2.0;
+    if (t < best_t - 1e-9) {
+      best_t = t;
+      best = s;
+    }
+  }
+  return best;
+}
+
 template <int BN, bool SPLIT>
-int launch_bn(const GemmDesc& d, int* dev_err, cudaStream_t stream) {
+int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream_t stream) {
   using S = Stages<BN, SPLIT>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -314,11 +468,33 @@ int launch_bn(const GemmDesc& d, int* dev_err, cudaStream_t stream) {
   k.a_mn = d.a.mn_major; k.b_mn = d.b.mn_major;
   k.a_bdiv1 = d.a.bdiv1; k.a_bmul1 = d.a.bmul1; k.a_bdiv2 = d.a.bdiv2; k.a_bmul2 = d.a.bmul2;
   k.b_bdiv1 = d.b.bdiv1; k.b_bmul1 = d.b.bmul1; k.b_bdiv2 = d.b.bdiv2; k.b_bmul2 = d.b.bmul2;
+  k.tiles_m = (d.M + BM - 1) / BM;
+  k.tiles_n = (d.N + BN - 1) / BN;
+  k.kb_total = (d.K + BK - 1) / BK;
+  k.causal = d.causal;
+  const long long tiles = (long long)d.batch * k.tiles_m * k.tiles_n;
+  int splits = d.splits > 0 ? d.splits : choose_splits(d, tiles, k.kb_total, sc.ws_floats, BN);
+  if (splits > k.kb_total) splits = k.kb_total;
+  if (splits > 1 && (d.causal || d.batch != 1 || !sc.ws || (long long)splits * d.M * d.N > sc.ws_floats))
+    splits = 1;
+  if (tiles * splits > (1LL << 31) - 1) return -5;
+  k.splits = splits;
+  k.units = (int)(tiles * splits);
   k.epi = d.epi;
+  k.ws = sc.ws;
+  k.sem = sc.sem;
   k.err = dev_err;
-  dim3 grid((d.N + BN - 1) / BN, (d.M + BM - 1) / BM, d.batch);
+  const int grid = k.units < kNumSMs ? k.units : kNumSMs;
   gemm_split_bf16_kernel<BN, SPLIT><<<grid, kThreads, S::kSmemBytes, stream>>>(ma_hi, ma_lo, mb_hi, mb_lo, k);
-  return cudaPeekAtLastError() == cudaSuccess ? 0 : -21;
+  if (cudaPeekAtLastError() != cudaSuccess) return -21;
+  if (splits > 1) {
+    const long long work = (long long)d.M * ((d.N + 31) / 32);
+    long long blocks = (work + 127) / 128;
+    if (blocks > 8 * kNumSMs) blocks = 8 * kNumSMs;
+    splitk_reduce_kernel<<<(int)blocks, 128, 0, stream>>>(sc.ws, splits, d.M, d.N, d.epi);
+    if (cudaPeekAtLastError() != cudaSuccess) return -21;
+  }
+  return 0;
 }
 
 int pick_bn(int N) {
@@ -330,9 +506,9 @@ int pick_bn(int N) {
 
 }  // namespace
 
-int gemm_launch(const GemmDesc& d, int* dev_err, cudaStream_t stream) {
+int gemm_launch(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream_t stream) {
   if (d.M <= 0 || d.N <= 0 || d.K <= 0 || d.batch <= 0) return -1;
-  if (d.batch > 65535) return -2;
+  if (d.causal < 0 || d.causal > 2) return -1;
   // Epilogue vector stores need 16-byte aligned rows.
   const Epilogue& e = d.epi;
   const int al = (e.mode == kEpiStoreSplit || e.mode == kEpiStoreBoth) ? 8 : 4;
@@ -340,10 +516,13 @@ int gemm_launch(const GemmDesc& d, int* dev_err, cudaStream_t stream) {
     return -3;
   if (!d.a.hi || !d.b.hi || (d.split && (!d.a.lo || !d.b.lo))) return -4;
   switch (pick_bn(d.N)) {
-    case 64: return d.split ? launch_bn<64, true>(d, dev_err, stream) : launch_bn<64, false>(d, dev_err, stream);
-    case 128: return d.split ? launch_bn<128, true>(d, dev_err, stream) : launch_bn<128, false>(d, dev_err, stream);
-    case 192: return d.split ? launch_bn<192, true>(d, dev_err, stream) : launch_bn<192, false>(d, dev_err, stream);
-    default: return d.split ? launch_bn<256, true>(d, dev_err, stream) : launch_bn<256, false>(d, dev_err, stream);
+    case 64: return d.split ? launch_bn<64, true>(d, sc, dev_err, stream) : launch_bn<64, false>(d, sc, dev_err, stream);
+    case 128:
+      return d.split ? launch_bn<128, true>(d, sc, dev_err, stream) : launch_bn<128, false>(d, sc, dev_err, stream);
+    case 192:
+      return d.split ? launch_bn<192, true>(d, sc, dev_err, stream) : launch_bn<192, false>(d, sc, dev_err, stream);
+    default:
+      return d.split ? launch_bn<256, true>(d, sc, dev_err, stream) : launch_bn<256, false>(d, sc, dev_err, stream);
   }
 }
 

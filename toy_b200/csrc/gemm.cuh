@@ -66,14 +66,25 @@ struct Epilogue {
 struct GemmDesc {
   int M = 0, N = 0, K = 0, batch = 1;
   bool split = true;
+  int splits = 0;   // K ranges reduced through the workspace; 0 = choose from the tile count
+  int causal = 0;   // 1: skip tiles with n0 > m0 + 127; 2: clamp K to m0 + 128 (zero beyond)
   Operand a, b;
   Epilogue epi;
+};
+
+// Split-K workspace: f32 partial tiles and per-tile arrival counters (zero at
+// rest; the reducing CTA resets its counter). One GEMM at a time may use it.
+struct GemmScratch {
+  float* ws = nullptr;
+  long long ws_floats = 0;
+  int* sem = nullptr;
+  long long sem_count = 0;
 };
 
 // Enqueue the GEMM on `stream`. Returns 0 on success, negative on a rejected
 // shape/alignment (nothing launched). `dev_err` is a device int the kernel sets
 // to a DeviceError code if one of its bounded waits gives up.
-int gemm_launch(const GemmDesc& d, int* dev_err, cudaStream_t stream);
+int gemm_launch(const GemmDesc& d, const GemmScratch& scratch, int* dev_err, cudaStream_t stream);
 
 // Row-major helpers used by the step program.
 inline Operand op_rowmajor(const __nv_bfloat16* hi, const __nv_bfloat16* lo, int rows, int cols, long long ld,

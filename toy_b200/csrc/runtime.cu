@@ -9,7 +9,32 @@ namespace tb2 {
 namespace {
 std::mutex g_mu;
 int* g_err[64] = {nullptr};
+GemmScratch g_scratch[64];
+constexpr long long kWsFloats = 16LL << 20;   // 64 MiB
+constexpr long long kSemCount = 64LL << 10;
 }  // namespace
+
+const GemmScratch& gemm_scratch() {
+  static const GemmScratch none;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return none;
+  std::lock_guard<std::mutex> lk(g_mu);
+  GemmScratch& s = g_scratch[dev];
+  if (!s.ws) {
+    float* ws = nullptr;
+    int* sem = nullptr;
+    if (cudaMalloc(&ws, kWsFloats * sizeof(float)) != cudaSuccess) return none;
+    if (cudaMalloc(&sem, kSemCount * sizeof(int)) != cudaSuccess || cudaMemset(sem, 0, kSemCount * sizeof(int)) != cudaSuccess) {
+      cudaFree(ws);
+      return none;
+    }
+    s.ws = ws;
+    s.ws_floats = kWsFloats;
+    s.sem = sem;
+    s.sem_count = kSemCount;
+  }
+  return s;
+}
 
 int* device_error_word() {
   int dev = 0;
