@@ -79,6 +79,20 @@ typedef struct tb2_epilogue {
 int tb2_gemm(int M, int N, int K, int batch, int split, const tb2_operand *a, const tb2_operand *b,
              const tb2_epilogue *epi, int ksplits, int causal, void *stream);
 
+/* tb2_gemm for callers that cannot allocate device memory. No counterpart in
+ * the reference. Some hosts own every device buffer (a framework's memory pool,
+ * a real-time loop where an allocator call would synchronise the device) and
+ * can only hand this library inputs and outputs; tb2_gemm allocates its split-K
+ * workspace on first use, this variant uses an 8 MiB workspace compiled into
+ * the library (held on every GPU that loads it until exit) and never calls an
+ * allocator. Explicit ksplits with ksplits*M*N > 2^21 floats returns -5; with
+ * ksplits = 0 the split count is chosen to fit. Calls share the workspace: calls
+ * that overlap on the GPU race, so serialise them on one stream. The first call
+ * on a device looks up the workspace's device address; make it before any
+ * stream capture. Same arguments and results as tb2_gemm. */
+int tb2_gemm_noalloc(int M, int N, int K, int batch, int split, const tb2_operand *a, const tb2_operand *b,
+                     const tb2_epilogue *epi, int ksplits, int causal, void *stream);
+
 /* hi = rn_bf16(x), lo = rn_bf16(x - hi) for n f32 values. */
 int tb2_split_f32(const float *x, void *hi, void *lo, size_t n, void *stream);
 
