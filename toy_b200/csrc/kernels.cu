@@ -1,6 +1,6 @@
-// Bandwidth-bound kernels of the training step: vectorised loads, warp-shuffle
-// reductions, fixed-order (deterministic) reductions, grids sized in multiples
-// of the SM count.
+// Bandwidth-bound kernels of the training step: vectorised loads, rows held in
+// registers, warp-shuffle reductions, fixed-order (deterministic) reductions,
+// grids sized in multiples of the SM count.
 #include "kernels.cuh"
 
 #include <cuda_fp16.h>
@@ -36,8 +36,22 @@ __device__ __forceinline__ void store_planes4(const Planes& p, long long i, floa
   *reinterpret_cast<uint2*>(p.lo + i) = *reinterpret_cast<const uint2*>(l);
 }
 
-__device__ __forceinline__ float load_planes(const Planes& p, long long i) {
-  return __bfloat162float(p.hi[i]) + __bfloat162float(p.lo[i]);
+// Two consecutive values (i % 2 == 0) as two 4-byte stores.
+__device__ __forceinline__ void store_planes2(const Planes& p, long long i, float a, float b) {
+  __align__(4) bf16 h[2], l[2];
+  split2(a, h[0], l[0]);
+  split2(b, h[1], l[1]);
+  *reinterpret_cast<uint32_t*>(p.hi + i) = *reinterpret_cast<const uint32_t*>(h);
+  *reinterpret_cast<uint32_t*>(p.lo + i) = *reinterpret_cast<const uint32_t*>(l);
+}
+
+__device__ __forceinline__ float4 load_planes4(const Planes& p, long long i) {
+  const uint2 h = *reinterpret_cast<const uint2*>(p.hi + i);
+  const uint2 l = *reinterpret_cast<const uint2*>(p.lo + i);
+  const bf16* hh = reinterpret_cast<const bf16*>(&h);
+  const bf16* ll = reinterpret_cast<const bf16*>(&l);
+  return make_float4(__bfloat162float(hh[0]) + __bfloat162float(ll[0]), __bfloat162float(hh[1]) + __bfloat162float(ll[1]),
+                     __bfloat162float(hh[2]) + __bfloat162float(ll[2]), __bfloat162float(hh[3]) + __bfloat162float(ll[3]));
 }
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -51,6 +65,8 @@ __device__ __forceinline__ float warp_max(float v) {
   for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
 }
+
+__device__ __forceinline__ float4 f4_zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
 
 int grid_for(long long work, int threads, int per_sm = 8) {
   long long b = (work + threads - 1) / threads;
@@ -106,50 +122,68 @@ __global__ void embed_scatter_kernel(const float* __restrict__ dx, const int* __
 }
 
 // ------------------------------------------------------------------ RMSNorm
-__global__ void rmsnorm_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma, Planes h, int N,
-                                   int d, float eps) {
+// One warp per row; lane l holds float4 chunks c = l + 32*i (i < NC) in registers.
+template <int NC>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+                                                          Planes h, int N, int d, float eps) {
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x % 32;
   const int d4 = d / 4;
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
   for (int n = blockIdx.x * warps + threadIdx.x / 32; n < N; n += gridDim.x * warps) {
     const float4* xr = reinterpret_cast<const float4*>(x + (long long)n * d);
+    float4 v[NC];
     float ss = 0.f;
-    for (int c = lane; c < d4; c += 32) {
-      const float4 v = xr[c];
-      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int c = lane + 32 * i;
+      v[i] = c < d4 ? __ldcs(xr + c) : f4_zero();
+      ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
     }
     ss = warp_sum(ss);
     const float r = 1.0f / sqrtf(ss / (float)d + eps);
-    const float4* g4 = reinterpret_cast<const float4*>(gamma);
-    for (int c = lane; c < d4; c += 32) {
-      const float4 v = xr[c], g = g4[c];
-      store_planes4(h, (long long)n * d + c * 4, make_float4(v.x * r * g.x, v.y * r * g.y, v.z * r * g.z, v.w * r * g.w));
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int c = lane + 32 * i;
+      if (c < d4) {
+        const float4 g = g4[c];
+        store_planes4(h, (long long)n * d + c * 4,
+                      make_float4(v[i].x * r * g.x, v[i].y * r * g.y, v[i].z * r * g.z, v[i].w * r * g.w));
+      }
     }
   }
 }
 
-// Block of 8 warps; warp w accumulates dgamma over its rows in shared memory
-// (fixed row order per warp, fixed warp order in the block sum).
-__global__ void rmsnorm_bwd_kernel(const float* __restrict__ x, const float* __restrict__ dh,
-                                   const float* __restrict__ gamma, const float* dres, float* dx, Planes dxp,
-                                   float* __restrict__ gpart, int N, int d, float eps) {
-  extern __shared__ float gacc[];  // [warps][d]
+// dx = dres + (dz - x * sum(x dz) / (sum x^2 + d eps)) * rrms with dz = dh * gamma.
+// Block of 8 warps; warp w accumulates dgamma (dh * x * rrms) over its rows in
+// shared memory (fixed row order per warp, fixed warp order in the block sum).
+template <int NC>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restrict__ x, const float* __restrict__ dh,
+                                                          const float* __restrict__ gamma, const float* dres,
+                                                          float* dx, Planes dxp, float* __restrict__ gpart, int N,
+                                                          int d, float eps) {
+  extern __shared__ float4 gacc4[];  // [warps][d / 4]
   const int warps = blockDim.x / 32;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int d4 = d / 4;
-  float* my = gacc + warp * d;
-  for (int c = lane; c < d; c += 32) my[c] = 0.f;
+  float4* my = gacc4 + warp * d4;
+  for (int c = lane; c < d4; c += 32) my[c] = f4_zero();
   __syncwarp();
   const float4* g4 = reinterpret_cast<const float4*>(gamma);
   for (int n = blockIdx.x * warps + warp; n < N; n += gridDim.x * warps) {
     const long long base = (long long)n * d;
     const float4* xr = reinterpret_cast<const float4*>(x + base);
     const float4* hr = reinterpret_cast<const float4*>(dh + base);
+    float4 xv[NC], hv[NC];
     float sxx = 0.f, sxdz = 0.f;
-    for (int c = lane; c < d4; c += 32) {
-      const float4 v = xr[c], gg = hr[c], g = g4[c];
-      sxx += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-      sxdz += v.x * gg.x * g.x + v.y * gg.y * g.y + v.z * gg.z * g.z + v.w * gg.w * g.w;
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int c = lane + 32 * i;
+      xv[i] = c < d4 ? xr[c] : f4_zero();
+      hv[i] = c < d4 ? __ldcs(hr + c) : f4_zero();
+      const float4 g = c < d4 ? g4[c] : f4_zero();
+      sxx += xv[i].x * xv[i].x + xv[i].y * xv[i].y + xv[i].z * xv[i].z + xv[i].w * xv[i].w;
+      sxdz += xv[i].x * hv[i].x * g.x + xv[i].y * hv[i].y * g.y + xv[i].z * hv[i].z * g.z + xv[i].w * hv[i].w * g.w;
     }
     sxx = warp_sum(sxx);
     sxdz = warp_sum(sxdz);
@@ -157,9 +191,12 @@ __global__ void rmsnorm_bwd_kernel(const float* __restrict__ x, const float* __r
     const float coef = sxdz / (sxx + (float)d * eps);
     const float4* rres = dres ? reinterpret_cast<const float4*>(dres + base) : nullptr;
     float4* out = reinterpret_cast<float4*>(dx + base);
-    for (int c = lane; c < d4; c += 32) {
-      const float4 v = xr[c], gg = hr[c], g = g4[c];
-      const float4 rs = rres ? rres[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int c = lane + 32 * i;
+      if (c >= d4) continue;
+      const float4 v = xv[i], gg = hv[i], g = g4[c];
+      const float4 rs = rres ? rres[c] : f4_zero();
       float4 o;
       o.x = rs.x + (gg.x * g.x - v.x * coef) * rr;
       o.y = rs.y + (gg.y * g.y - v.y * coef) * rr;
@@ -167,174 +204,256 @@ __global__ void rmsnorm_bwd_kernel(const float* __restrict__ x, const float* __r
       o.w = rs.w + (gg.w * g.w - v.w * coef) * rr;
       out[c] = o;
       if (dxp.hi) store_planes4(dxp, base + c * 4, o);
-      my[4 * c + 0] += gg.x * v.x * rr;
-      my[4 * c + 1] += gg.y * v.y * rr;
-      my[4 * c + 2] += gg.z * v.z * rr;
-      my[4 * c + 3] += gg.w * v.w * rr;
+      float4 a = my[c];
+      a.x += gg.x * v.x * rr;
+      a.y += gg.y * v.y * rr;
+      a.z += gg.z * v.z * rr;
+      a.w += gg.w * v.w * rr;
+      my[c] = a;
     }
   }
   __syncthreads();
-  for (int c = threadIdx.x; c < d; c += blockDim.x) {
-    float s = 0.f;
-    for (int w = 0; w < warps; ++w) s += gacc[w * d + c];
-    gpart[(long long)blockIdx.x * d + c] = s;
+  for (int c = threadIdx.x; c < d4; c += blockDim.x) {
+    float4 s = f4_zero();
+    for (int w = 0; w < warps; ++w) {
+      const float4 a = gacc4[w * d4 + c];
+      s.x += a.x; s.y += a.y; s.z += a.z; s.w += a.w;
+    }
+    reinterpret_cast<float4*>(gpart + (long long)blockIdx.x * d)[c] = s;
   }
 }
 
+// gout[c] = (accumulate ? gout[c] : 0) + sum_b gpart[b][c]: 32 columns per block,
+// 8 row groups summed in fixed order, then the groups in fixed order.
 __global__ void colsum_kernel(const float* __restrict__ gpart, int nblk, int d, float* gout, int accumulate) {
-  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < d; c += gridDim.x * blockDim.x) {
-    float s = 0.f;
-    for (int b = 0; b < nblk; ++b) s += gpart[(long long)b * d + c];
-    gout[c] = accumulate ? gout[c] + s : s;
+  __shared__ float sm[8][33];
+  const int cx = threadIdx.x % 32, gy = threadIdx.x / 32;
+  const int c = blockIdx.x * 32 + cx;
+  float s = 0.f;
+  if (c < d)
+    for (int b = gy; b < nblk; b += 8) s += gpart[(long long)b * d + c];
+  sm[gy][cx] = s;
+  __syncthreads();
+  if (gy == 0 && c < d) {
+    float t = 0.f;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) t += sm[g][cx];
+    gout[c] = accumulate ? gout[c] + t : t;
   }
 }
 
 // ------------------------------------------------------------------ RoPE
-__global__ void rope_qkv_fwd_kernel(const float* __restrict__ qkv, const float* __restrict__ bias,
-                                    const int* __restrict__ pos, const float2* __restrict__ cs, int tab_rows, Planes Q,
-                                    Planes K, Planes V, int B, int T, int H, int KV, int dh) {
+// One block per token; thread i of the block handles pair (j, j + dh/2) of slot s
+// for (s, j) = divmod(i, dh/2) over the H + 2*KV head slots of q | k | v.
+__global__ void __launch_bounds__(256) rope_qkv_fwd_kernel(const float* __restrict__ qkv, const float* __restrict__ bias,
+                                                           const int* __restrict__ pos, const float2* __restrict__ cs,
+                                                           int tab_rows, Planes Q, Planes K, Planes V, int N, int T,
+                                                           int H, int KV, int dh) {
   const int half = dh / 2;
   const int slots = H + 2 * KV;
-  const long long total = (long long)B * T * slots * half;
   const int width = slots * dh;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int j = (int)(i % half);
-    const long long r = i / half;
-    const int slot = (int)(r % slots);
-    const int n = (int)(r / slots);
-    const int b = n / T, t = n % T;
-    const long long src = (long long)n * width + slot * dh + j;
-    float x0 = qkv[src], x1 = qkv[src + half];
-    if (bias) {
-      x0 += bias[slot * dh + j];
-      x1 += bias[slot * dh + j + half];
-    }
-    if (slot < H + KV) {
-      int p = pos[n];
-      p = p < 0 ? 0 : (p >= tab_rows ? tab_rows - 1 : p);
-      const float2 c = cs[(long long)p * half + j];
-      const float y0 = x0 * c.x - x1 * c.y;
-      const float y1 = x0 * c.y + x1 * c.x;
-      const bool isq = slot < H;
-      const int hh = isq ? slot : slot - H;
-      const long long dst = (((long long)b * (isq ? H : KV) + hh) * T + t) * dh + j;
-      const Planes& o = isq ? Q : K;
-      store_planes(o, dst, y0);
-      store_planes(o, dst + half, y1);
-    } else {
-      const int hh = slot - H - KV;
-      const long long dst = (((long long)b * KV + hh) * T + t) * dh + j;
-      store_planes(V, dst, x0);
-      store_planes(V, dst + half, x1);
+  for (int n = blockIdx.x; n < N; n += gridDim.x) {
+    const int b = n / T, t = n - b * T;
+    int p = pos[n];
+    p = p < 0 ? 0 : (p >= tab_rows ? tab_rows - 1 : p);
+    const float* row = qkv + (long long)n * width;
+    const float2* crow = cs + (long long)p * half;
+    for (int i = threadIdx.x; i < slots * half; i += blockDim.x) {
+      const int slot = i / half, j = i - slot * half;
+      float x0 = row[slot * dh + j], x1 = row[slot * dh + j + half];
+      if (bias) {
+        x0 += bias[slot * dh + j];
+        x1 += bias[slot * dh + j + half];
+      }
+      if (slot < H + KV) {
+        const float2 c = crow[j];
+        const bool isq = slot < H;
+        const int hh = isq ? slot : slot - H;
+        const long long dst = (((long long)b * (isq ? H : KV) + hh) * T + t) * dh + j;
+        const Planes& o = isq ? Q : K;
+        store_planes(o, dst, x0 * c.x - x1 * c.y);
+        store_planes(o, dst + half, x0 * c.y + x1 * c.x);
+      } else {
+        const int hh = slot - H - KV;
+        const long long dst = (((long long)b * KV + hh) * T + t) * dh + j;
+        store_planes(V, dst, x0);
+        store_planes(V, dst + half, x1);
+      }
     }
   }
 }
 
-__global__ void rope_qkv_bwd_kernel(const float* __restrict__ dQ, const float* __restrict__ dK,
-                                    const float* __restrict__ dV, const int* __restrict__ pos,
-                                    const float2* __restrict__ cs, int tab_rows, Planes out, float* out_f32, int B,
-                                    int T, int H, int KV, int dh) {
+__global__ void __launch_bounds__(256) rope_qkv_bwd_kernel(const float* __restrict__ dQ, const float* __restrict__ dK,
+                                                           const float* __restrict__ dV, const int* __restrict__ pos,
+                                                           const float2* __restrict__ cs, int tab_rows, Planes out,
+                                                           float* out_f32, int N, int T, int H, int KV, int dh) {
   const int half = dh / 2;
   const int slots = H + 2 * KV;
-  const long long total = (long long)B * T * slots * half;
   const int width = slots * dh;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int j = (int)(i % half);
-    const long long r = i / half;
-    const int slot = (int)(r % slots);
-    const int n = (int)(r / slots);
-    const int b = n / T, t = n % T;
-    float y0, y1;
-    if (slot < H + KV) {
-      const bool isq = slot < H;
-      const int hh = isq ? slot : slot - H;
-      const float* srcb = isq ? dQ : dK;
-      const long long src = (((long long)b * (isq ? H : KV) + hh) * T + t) * dh + j;
-      const float g0 = srcb[src], g1 = srcb[src + half];
-      int p = pos[n];
-      p = p < 0 ? 0 : (p >= tab_rows ? tab_rows - 1 : p);
-      const float2 c = cs[(long long)p * half + j];
-      y0 = g0 * c.x + g1 * c.y;
-      y1 = -g0 * c.y + g1 * c.x;
-    } else {
-      const int hh = slot - H - KV;
-      const long long src = (((long long)b * KV + hh) * T + t) * dh + j;
-      y0 = dV[src];
-      y1 = dV[src + half];
-    }
-    const long long dst = (long long)n * width + slot * dh + j;
-    store_planes(out, dst, y0);
-    store_planes(out, dst + half, y1);
-    if (out_f32) {
-      out_f32[dst] = y0;
-      out_f32[dst + half] = y1;
+  for (int n = blockIdx.x; n < N; n += gridDim.x) {
+    const int b = n / T, t = n - b * T;
+    int p = pos[n];
+    p = p < 0 ? 0 : (p >= tab_rows ? tab_rows - 1 : p);
+    const float2* crow = cs + (long long)p * half;
+    for (int i = threadIdx.x; i < slots * half; i += blockDim.x) {
+      const int slot = i / half, j = i - slot * half;
+      float y0, y1;
+      if (slot < H + KV) {
+        const bool isq = slot < H;
+        const int hh = isq ? slot : slot - H;
+        const float* srcb = isq ? dQ : dK;
+        const long long src = (((long long)b * (isq ? H : KV) + hh) * T + t) * dh + j;
+        const float g0 = srcb[src], g1 = srcb[src + half];
+        const float2 c = crow[j];
+        y0 = g0 * c.x + g1 * c.y;
+        y1 = -g0 * c.y + g1 * c.x;
+      } else {
+        const int hh = slot - H - KV;
+        const long long src = (((long long)b * KV + hh) * T + t) * dh + j;
+        y0 = dV[src];
+        y1 = dV[src + half];
+      }
+      const long long dst = (long long)n * width + slot * dh + j;
+      store_planes(out, dst, y0);
+      store_planes(out, dst + half, y1);
+      if (out_f32) {
+        out_f32[dst] = y0;
+        out_f32[dst + half] = y1;
+      }
     }
   }
 }
 
 // ------------------------------------------------------------------ attention softmax
-__global__ void softmax_causal_fwd_kernel(const float* __restrict__ S, Planes P, long long rows, int T) {
+// One warp per score row (z, q); lane l holds float4 chunks l + 32*i (i < NC,
+// 128*NC >= T) in registers. Keys k <= q are live, the rest are written as 0.
+template <int NC>
+__global__ void __launch_bounds__(256) softmax_causal_fwd_kernel(const float* __restrict__ S, Planes P, long long rows,
+                                                                 int T) {
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x % 32;
+  const int T4 = T / 4;
   for (long long row = blockIdx.x * (long long)warps + threadIdx.x / 32; row < rows;
        row += (long long)gridDim.x * warps) {
     const int q = (int)(row % T);
-    const float* s = S + row * T;
+    const float4* s4 = reinterpret_cast<const float4*>(S + row * T);
+    const int live4 = q / 4 + 1;   // chunks that hold at least one live key
+    float4 v[NC];
     float m = -INFINITY;
-    for (int k = lane; k <= q; k += 32) m = fmaxf(m, s[k]);
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int c = lane + 32 * i;
+      v[i] = c < live4 ? __ldcs(s4 + c) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      if (c < live4) {
+        const int k = 4 * c;
+        if (k + 1 > q) v[i].y = -INFINITY;
+        if (k + 2 > q) v[i].z = -INFINITY;
+        if (k + 3 > q) v[i].w = -INFINITY;
+      }
+      m = fmaxf(m, fmaxf(fmaxf(v[i].x, v[i].y), fmaxf(v[i].z, v[i].w)));
+    }
     m = warp_max(m);
     float sum = 0.f;
-    for (int k = lane; k <= q; k += 32) sum += expf(s[k] - m);
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      v[i].x = expf(v[i].x - m);
+      v[i].y = expf(v[i].y - m);
+      v[i].z = expf(v[i].z - m);
+      v[i].w = expf(v[i].w - m);
+      sum += v[i].x + v[i].y + v[i].z + v[i].w;
+    }
     sum = warp_sum(sum);
     const float inv = 1.0f / sum;
-    for (int k = lane; k < T; k += 32) store_planes(P, row * T + k, k <= q ? expf(s[k] - m) * inv : 0.f);
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int c = lane + 32 * i;
+      if (c < T4)
+        store_planes4(P, row * T + 4 * c, make_float4(v[i].x * inv, v[i].y * inv, v[i].z * inv, v[i].w * inv));
+    }
   }
 }
 
-__global__ void softmax_causal_bwd_kernel(Planes P, const float* __restrict__ dP, Planes dS, long long rows, int T,
-                                          float scale) {
+// dS = P * (dP - sum(P * dP)) * scale (ggml soft_max_back), zero past the diagonal.
+template <int NC>
+__global__ void __launch_bounds__(256) softmax_causal_bwd_kernel(Planes P, const float* __restrict__ dP, Planes dS,
+                                                                 long long rows, int T, float scale) {
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x % 32;
+  const int T4 = T / 4;
   for (long long row = blockIdx.x * (long long)warps + threadIdx.x / 32; row < rows;
        row += (long long)gridDim.x * warps) {
     const int q = (int)(row % T);
     const long long base = row * T;
+    const int live4 = q / 4 + 1;
+    float4 pv[NC], gv[NC];
     float dot = 0.f;
-    for (int k = lane; k <= q; k += 32) dot += load_planes(P, base + k) * dP[base + k];
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int c = lane + 32 * i;
+      if (c < live4) {
+        pv[i] = load_planes4(P, base + 4 * c);
+        gv[i] = __ldcs(reinterpret_cast<const float4*>(dP + base) + c);
+        const int k = 4 * c;
+        if (k + 1 > q) pv[i].y = 0.f;
+        if (k + 2 > q) pv[i].z = 0.f;
+        if (k + 3 > q) pv[i].w = 0.f;
+      } else {
+        pv[i] = f4_zero();
+        gv[i] = f4_zero();
+      }
+      dot += pv[i].x * gv[i].x + pv[i].y * gv[i].y + pv[i].z * gv[i].z + pv[i].w * gv[i].w;
+    }
     dot = warp_sum(dot);
-    for (int k = lane; k < T; k += 32) {
-      const float v = k <= q ? load_planes(P, base + k) * (dP[base + k] - dot) * scale : 0.f;
-      store_planes(dS, base + k, v);
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int c = lane + 32 * i;
+      if (c < T4)
+        store_planes4(dS, base + 4 * c,
+                      make_float4(pv[i].x * (gv[i].x - dot) * scale, pv[i].y * (gv[i].y - dot) * scale,
+                                  pv[i].z * (gv[i].z - dot) * scale, pv[i].w * (gv[i].w - dot) * scale));
     }
   }
 }
 
 // ------------------------------------------------------------------ SwiGLU
-__global__ void swiglu_fwd_kernel(const float* __restrict__ gu, Planes a, int N, int ff) {
-  const long long total = (long long)N * ff;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long n = i / ff;
-    const int j = (int)(i % ff);
-    const float g = gu[n * 2 * ff + j], u = gu[n * 2 * ff + ff + j];
-    store_planes(a, i, g / (1.0f + expf(-g)) * u);
+// One block per token row, float4 over the ff columns of gate | up.
+__global__ void __launch_bounds__(128) swiglu_fwd_kernel(const float* __restrict__ gu, Planes a, int N, int ff) {
+  const int ff4 = ff / 4;
+  for (int n = blockIdx.x; n < N; n += gridDim.x) {
+    const float4* g4 = reinterpret_cast<const float4*>(gu + (long long)n * 2 * ff);
+    const float4* u4 = g4 + ff4;
+    for (int c = threadIdx.x; c < ff4; c += blockDim.x) {
+      const float4 g = __ldcs(g4 + c), u = __ldcs(u4 + c);
+      store_planes4(a, (long long)n * ff + 4 * c,
+                    make_float4(g.x / (1.0f + expf(-g.x)) * u.x, g.y / (1.0f + expf(-g.y)) * u.y,
+                                g.z / (1.0f + expf(-g.z)) * u.z, g.w / (1.0f + expf(-g.w)) * u.w));
+    }
   }
 }
 
-__global__ void swiglu_bwd_kernel(const float* __restrict__ gu, const float* __restrict__ da, Planes dgu, int N,
-                                  int ff) {
-  const long long total = (long long)N * ff;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long n = i / ff;
-    const int j = (int)(i % ff);
-    const float g = gu[n * 2 * ff + j], u = gu[n * 2 * ff + ff + j];
-    const float s = 1.0f / (1.0f + expf(-g));
-    const float dy = da[i];
-    store_planes(dgu, n * 2 * ff + j, dy * u * (s * (1.0f + g * (1.0f - s))));
-    store_planes(dgu, n * 2 * ff + ff + j, dy * g * s);
+__device__ __forceinline__ void swiglu_back1(float g, float u, float dy, float& dg, float& du) {
+  const float s = 1.0f / (1.0f + expf(-g));
+  dg = dy * u * (s * (1.0f + g * (1.0f - s)));
+  du = dy * g * s;
+}
+
+__global__ void __launch_bounds__(128) swiglu_bwd_kernel(const float* __restrict__ gu, const float* __restrict__ da,
+                                                         Planes dgu, int N, int ff) {
+  const int ff4 = ff / 4;
+  for (int n = blockIdx.x; n < N; n += gridDim.x) {
+    const float4* g4 = reinterpret_cast<const float4*>(gu + (long long)n * 2 * ff);
+    const float4* u4 = g4 + ff4;
+    const float4* d4 = reinterpret_cast<const float4*>(da + (long long)n * ff);
+    for (int c = threadIdx.x; c < ff4; c += blockDim.x) {
+      const float4 g = g4[c], u = u4[c], dy = __ldcs(d4 + c);
+      float4 dg, du;
+      swiglu_back1(g.x, u.x, dy.x, dg.x, du.x);
+      swiglu_back1(g.y, u.y, dy.y, dg.y, du.y);
+      swiglu_back1(g.z, u.z, dy.z, dg.z, du.z);
+      swiglu_back1(g.w, u.w, dy.w, dg.w, du.w);
+      store_planes4(dgu, (long long)n * 2 * ff + 4 * c, dg);
+      store_planes4(dgu, (long long)n * 2 * ff + ff + 4 * c, du);
+    }
   }
 }
 
@@ -357,16 +476,30 @@ __global__ void __launch_bounds__(kCeThreads) cross_entropy_kernel(const float* 
   __shared__ float bc[2];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const float invN = 1.0f / (float)N;
+  const bool vec = (V % 4) == 0;
   for (int n = blockIdx.x; n < N; n += gridDim.x) {
     const float* z = logits + (long long)n * V;
     float m = -INFINITY, s = 0.f;
-    for (int v = threadIdx.x; v < V; v += blockDim.x) {
-      const float x = z[v];
-      if (x > m) {
-        s = s * expf(m - x) + 1.0f;
-        m = x;
-      } else {
-        s += expf(x - m);
+    if (vec) {
+      const float4* z4 = reinterpret_cast<const float4*>(z);
+      for (int v = threadIdx.x; v < V / 4; v += blockDim.x) {
+        const float4 x = z4[v];
+        const float mx = fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w));
+        if (mx > m) {
+          s *= expf(m - mx);
+          m = mx;
+        }
+        s += expf(x.x - m) + expf(x.y - m) + expf(x.z - m) + expf(x.w - m);
+      }
+    } else {
+      for (int v = threadIdx.x; v < V; v += blockDim.x) {
+        const float x = z[v];
+        if (x > m) {
+          s = s * expf(m - x) + 1.0f;
+          m = x;
+        } else {
+          s += expf(x - m);
+        }
       }
     }
 #pragma unroll
@@ -389,16 +522,30 @@ __global__ void __launch_bounds__(kCeThreads) cross_entropy_kernel(const float* 
     int lab = label_dense ? -1 : label_ids[n];
     if (lab >= V) lab = -1;
     float dense_acc = 0.f;
-    for (int v = threadIdx.x; v < V; v += blockDim.x) {
-      const float x = z[v];
-      float y = 0.f;
-      if (label_dense) {
-        y = label_dense[(long long)n * V + v];
-        dense_acc += y * (x - lse);
-      } else if (v == lab) {
-        y = 1.0f;
+    if (vec && !label_dense) {
+      const float4* z4 = reinterpret_cast<const float4*>(z);
+      for (int v = threadIdx.x; v < V / 4; v += blockDim.x) {
+        const float4 x = __ldcs(z4 + v);
+        float4 g = make_float4(expf(x.x - M) * inv, expf(x.y - M) * inv, expf(x.z - M) * inv, expf(x.w - M) * inv);
+        const int k = lab - 4 * v;
+        if (k == 0) g.x -= 1.0f;
+        if (k == 1) g.y -= 1.0f;
+        if (k == 2) g.z -= 1.0f;
+        if (k == 3) g.w -= 1.0f;
+        store_planes4(dl, (long long)n * V + 4 * v, make_float4(g.x * invN, g.y * invN, g.z * invN, g.w * invN));
       }
-      store_planes(dl, (long long)n * V + v, (expf(x - M) * inv - y) * invN);
+    } else {
+      for (int v = threadIdx.x; v < V; v += blockDim.x) {
+        const float x = z[v];
+        float y = 0.f;
+        if (label_dense) {
+          y = label_dense[(long long)n * V + v];
+          dense_acc += y * (x - lse);
+        } else if (v == lab) {
+          y = 1.0f;
+        }
+        store_planes(dl, (long long)n * V + v, (expf(x - M) * inv - y) * invN);
+      }
     }
     if (label_dense) {
       dense_acc = warp_sum(dense_acc);
@@ -440,7 +587,7 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
        i += (long long)gridDim.x * blockDim.x) {
     float4 P = reinterpret_cast<float4*>(p)[i];
-    const float4 G = reinterpret_cast<const float4*>(g)[i];
+    const float4 G = __ldcs(reinterpret_cast<const float4*>(g) + i);
     float4 M = reinterpret_cast<float4*>(m)[i];
     float4 Vv = reinterpret_cast<float4*>(v)[i];
     float* pe = &P.x;
@@ -522,6 +669,71 @@ __global__ void add_inplace_kernel(float* __restrict__ y, const float* __restric
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Register-chunk count (float4 chunks per lane) for a row of `len` floats.
+int row_chunks(int len) {
+  const int nc = (len / 4 + 31) / 32;
+  static const int choices[] = {1, 2, 4, 5, 8, 12, 16, 24, 28, 32};
+  for (int c : choices)
+    if (nc <= c) return c;
+  return -1;
+}
+
+template <template <int> class F, typename... A>
+int dispatch_nc(int nc, A... a) {
+  switch (nc) {
+    case 1: return F<1>::run(a...);
+    case 2: return F<2>::run(a...);
+    case 4: return F<4>::run(a...);
+    case 5: return F<5>::run(a...);
+    case 8: return F<8>::run(a...);
+    case 12: return F<12>::run(a...);
+    case 16: return F<16>::run(a...);
+    case 24: return F<24>::run(a...);
+    case 28: return F<28>::run(a...);
+    case 32: return F<32>::run(a...);
+    default: return -1;
+  }
+}
+
+template <int NC>
+struct RmsFwd {
+  static int run(const float* x, const float* gamma, Planes h, int N, int d, float eps, cudaStream_t st) {
+    rmsnorm_fwd_kernel<NC><<<grid_for((long long)N * 32, 256), 256, 0, st>>>(x, gamma, h, N, d, eps);
+    return ok();
+  }
+};
+
+template <int NC>
+struct RmsBwd {
+  static int run(const float* x, const float* dh, const float* gamma, const float* dres, float* dx, Planes dxp,
+                 float* gpart, int nblk, int N, int d, float eps, cudaStream_t st) {
+    const size_t smem = (size_t)8 * d * sizeof(float);
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(rmsnorm_bwd_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      attr = true;
+    }
+    rmsnorm_bwd_kernel<NC><<<nblk, 256, smem, st>>>(x, dh, gamma, dres, dx, dxp, gpart, N, d, eps);
+    return ok();
+  }
+};
+
+template <int NC>
+struct SmFwd {
+  static int run(const float* S, Planes P, long long rows, int T, cudaStream_t st) {
+    softmax_causal_fwd_kernel<NC><<<grid_for(rows * 32, 256), 256, 0, st>>>(S, P, rows, T);
+    return ok();
+  }
+};
+
+template <int NC>
+struct SmBwd {
+  static int run(Planes P, const float* dP, Planes dS, long long rows, int T, float scale, cudaStream_t st) {
+    softmax_causal_bwd_kernel<NC><<<grid_for(rows * 32, 256), 256, 0, st>>>(P, dP, dS, rows, T, scale);
+    return ok();
+  }
+};
+
 }  // namespace
 
 int rmsnorm_bwd_blocks() { return kRmsBwdBlocks; }
@@ -549,66 +761,59 @@ int launch_embed_scatter(const float* dx, const int* order, const int* seg_start
 
 int launch_rmsnorm_fwd(const float* x, const float* gamma, Planes h, int N, int d, float eps, cudaStream_t st) {
   if (d % 4) return -1;
-  rmsnorm_fwd_kernel<<<grid_for((long long)N * 32, 256), 256, 0, st>>>(x, gamma, h, N, d, eps);
-  return ok();
+  return dispatch_nc<RmsFwd>(row_chunks(d), x, gamma, h, N, d, eps, st);
 }
 
 int launch_rmsnorm_bwd(const float* x, const float* dh, const float* gamma, const float* dres, float* dx,
                        Planes dxp, float* gpart, int nblk, int N, int d, float eps, cudaStream_t st) {
   if (d % 4 || nblk != kRmsBwdBlocks) return -1;
-  const int threads = 256;
-  const size_t smem = (size_t)(threads / 32) * d * sizeof(float);
-  if (smem > 200 * 1024) return -1;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(rmsnorm_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr = true;
-  }
-  rmsnorm_bwd_kernel<<<nblk, threads, smem, st>>>(x, dh, gamma, dres, dx, dxp, gpart, N, d, eps);
-  return ok();
+  if ((size_t)8 * d * sizeof(float) > 200 * 1024) return -1;
+  return dispatch_nc<RmsBwd>(row_chunks(d), x, dh, gamma, dres, dx, dxp, gpart, nblk, N, d, eps, st);
 }
 
 int launch_colsum(const float* gpart, int nblk, int d, float* gout, int accumulate, cudaStream_t st) {
-  colsum_kernel<<<(d + 255) / 256, 256, 0, st>>>(gpart, nblk, d, gout, accumulate);
+  colsum_kernel<<<(d + 31) / 32, 256, 0, st>>>(gpart, nblk, d, gout, accumulate);
   return ok();
 }
 
 int launch_rope_qkv_fwd(const float* qkv, const float* bias, const int* pos, const float* cs_tab, int tab_rows,
                         Planes Q, Planes K, Planes V, int B, int T, int H, int KV, int dh, cudaStream_t st) {
   if (dh % 2) return -1;
-  const long long total = (long long)B * T * (H + 2 * KV) * (dh / 2);
-  rope_qkv_fwd_kernel<<<grid_for(total, 256), 256, 0, st>>>(qkv, bias, pos, reinterpret_cast<const float2*>(cs_tab),
-                                                            tab_rows, Q, K, V, B, T, H, KV, dh);
+  const int N = B * T;
+  rope_qkv_fwd_kernel<<<N < 8 * kSMs ? N : 8 * kSMs, 256, 0, st>>>(
+      qkv, bias, pos, reinterpret_cast<const float2*>(cs_tab), tab_rows, Q, K, V, N, T, H, KV, dh);
   return ok();
 }
 
 int launch_rope_qkv_bwd(const float* dQ, const float* dK, const float* dV, const int* pos, const float* cs_tab,
                         int tab_rows, Planes dqkv, float* dqkv_f32, int B, int T, int H, int KV, int dh,
                         cudaStream_t st) {
-  const long long total = (long long)B * T * (H + 2 * KV) * (dh / 2);
-  rope_qkv_bwd_kernel<<<grid_for(total, 256), 256, 0, st>>>(dQ, dK, dV, pos, reinterpret_cast<const float2*>(cs_tab),
-                                                            tab_rows, dqkv, dqkv_f32, B, T, H, KV, dh);
+  const int N = B * T;
+  rope_qkv_bwd_kernel<<<N < 8 * kSMs ? N : 8 * kSMs, 256, 0, st>>>(
+      dQ, dK, dV, pos, reinterpret_cast<const float2*>(cs_tab), tab_rows, dqkv, dqkv_f32, N, T, H, KV, dh);
   return ok();
 }
 
 int launch_softmax_causal_fwd(const float* S, Planes P, long long Z, int T, cudaStream_t st) {
-  softmax_causal_fwd_kernel<<<grid_for(Z * T * 32, 256), 256, 0, st>>>(S, P, Z * T, T);
-  return ok();
+  if (T % 4) return -1;
+  return dispatch_nc<SmFwd>(row_chunks(T), S, P, Z * T, T, st);
 }
 
 int launch_softmax_causal_bwd(Planes P, const float* dP, Planes dS, long long Z, int T, float scale,
                               cudaStream_t st) {
-  softmax_causal_bwd_kernel<<<grid_for(Z * T * 32, 256), 256, 0, st>>>(P, dP, dS, Z * T, T, scale);
-  return ok();
+  if (T % 4) return -1;
+  return dispatch_nc<SmBwd>(row_chunks(T), P, dP, dS, Z * T, T, scale, st);
 }
 
 int launch_swiglu_fwd(const float* gu, Planes a, int N, int ff, cudaStream_t st) {
-  swiglu_fwd_kernel<<<grid_for((long long)N * ff, 256), 256, 0, st>>>(gu, a, N, ff);
+  if (ff % 4) return -1;
+  swiglu_fwd_kernel<<<N < 16 * kSMs ? N : 16 * kSMs, 128, 0, st>>>(gu, a, N, ff);
   return ok();
 }
 
 int launch_swiglu_bwd(const float* gu, const float* da, Planes dgu, int N, int ff, cudaStream_t st) {
-  swiglu_bwd_kernel<<<grid_for((long long)N * ff, 256), 256, 0, st>>>(gu, da, dgu, N, ff);
+  if (ff % 4) return -1;
+  swiglu_bwd_kernel<<<N < 16 * kSMs ? N : 16 * kSMs, 128, 0, st>>>(gu, da, dgu, N, ff);
   return ok();
 }
 
