@@ -11,10 +11,9 @@
 // mainloop of unit i+1.
 //
 // Split-K: when the tile grid is too small for the 148 SMs, K is cut into S
-// ranges. Every unit writes its f32 partial tile to a workspace; the CTA that
-// arrives last on the tile's counter sums the S partials in split order (so
-// the result does not depend on arrival order), applies the epilogue, and
-// resets the counter for the next launch.
+// ranges. Every unit writes its f32 partial tile to slab s of a workspace and
+// a second, bandwidth-bound kernel sums the S slabs in split order (so the
+// result does not depend on scheduling) and applies the epilogue.
 //
 // Causal modes for attention: 1 skips tiles whose keys all exceed their
 // queries (n0 > m0 + 127); 2 clamps K (keys) to m0 + 128 because P / dS are
@@ -93,11 +92,25 @@ __device__ __forceinline__ Unit decode(const KArgs& a, int u) {
   return r;
 }
 
+__device__ __forceinline__ long long epi_offset(const Epilogue& e, int z, int m, int nc) {
+  return (long long)(z / e.z_div) * e.z_s1 + (long long)(z % e.z_div) * e.bstride +
+         (long long)(m / e.m_div) * e.m_s1 + (long long)(m % e.m_div) * e.m_s0 + (long long)(nc / e.n_div) * e.n_s1 +
+         (nc % e.n_div);
+}
+
+// The 32 addend values of a residual / accumulate epilogue for chunk (m, nc),
+// loaded ahead of the chunk's accumulator (they do not depend on the MMA).
+__device__ __forceinline__ void epi_prefetch(const Epilogue& e, int N, long long off, int nc, float4 (&r)[8]) {
+  if (nc + 32 > N || (e.mode != kEpiAccumF32 && e.mode != kEpiResidF32)) return;
+  const float4* src = reinterpret_cast<const float4*>((e.mode == kEpiAccumF32 ? e.out : e.res) + off);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) r[i] = src[i];
+}
+
 // Apply the epilogue to the 32 consecutive outputs (m, nc .. nc+31) held in v.
-__device__ __forceinline__ void epi_store(const Epilogue& e, int N, int z, int m, int nc, float (&v)[32]) {
-  const long long off = (long long)(z / e.z_div) * e.z_s1 + (long long)(z % e.z_div) * e.bstride +
-                        (long long)(m / e.m_div) * e.m_s1 + (long long)(m % e.m_div) * e.m_s0 +
-                        (long long)(nc / e.n_div) * e.n_s1 + (nc % e.n_div);
+// `pre` holds the addend loaded by epi_prefetch (used when the chunk is full).
+__device__ __forceinline__ void epi_store(const Epilogue& e, int N, long long off, int nc, float (&v)[32],
+                                          const float4 (&pre)[8]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] *= e.alpha;
   const bool full_chunk = nc + 32 <= N;
@@ -105,18 +118,10 @@ __device__ __forceinline__ void epi_store(const Epilogue& e, int N, int z, int m
     float* dst = e.out + off;
     if (full_chunk) {
       float4* d4 = reinterpret_cast<float4*>(dst);
-      if (e.mode == kEpiAccumF32) {
+      if (e.mode == kEpiAccumF32 || e.mode == kEpiResidF32) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          float4 o = d4[i];
-          o.x += v[4 * i]; o.y += v[4 * i + 1]; o.z += v[4 * i + 2]; o.w += v[4 * i + 3];
-          d4[i] = o;
-        }
-      } else if (e.mode == kEpiResidF32) {
-        const float4* r4 = reinterpret_cast<const float4*>(e.res + off);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 r = r4[i];
+          const float4 r = pre[i];
           d4[i] = make_float4(r.x + v[4 * i], r.y + v[4 * i + 1], r.z + v[4 * i + 2], r.w + v[4 * i + 3]);
         }
       } else {
@@ -315,15 +320,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (w.skip) continue;
       const uint32_t b = local & 1, tph = (local >> 1) & 1;
       ++local;
+      const int m = w.m0 + row;
+      const bool row_in = m < args.M;
+      const bool direct = args.splits == 1;
+      // output offset of this row (without the column part); the residual /
+      // accumulate addend of the first chunk is loaded before the accumulator
+      // is ready, the next chunk's while the current one is stored
+      const long long rowoff = row_in && direct ? epi_offset(e, w.z, m, 0) : 0;
+      float4 pre[2][8];
+      if (row_in && direct && w.n0 < args.N)
+        epi_prefetch(e, args.N, rowoff + (w.n0 / e.n_div) * e.n_s1 + (w.n0 % e.n_div), w.n0, pre[0]);
       const bool ok = mbar_wait(&tfull[b], tph, args.err, kErrWaitAccum);
       tc_fence_after();
-      const int m = w.m0 + row;
-      const bool row_ok = ok && m < args.M;
+      const bool row_ok = ok && row_in;
       const uint32_t acc_tmem = tmem_base + b * kAccCols + ((uint32_t)(q * 32) << 16);
       // split-K partial of split s: plain row-major [M][N] slab s of the workspace
       float* part = args.ws + (long long)(u % args.splits) * args.M * args.N + (long long)m * args.N;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      // one 32-column chunk: drain TMEM, store (or write the partial); the
+      // addend of the following chunk is prefetched into `next`
+      auto chunk = [&](int c, const float4 (&cur)[8], float4 (&next)[8]) {
         float v[32];
         tmem_ld32(acc_tmem + (uint32_t)(c * 32), v);
         if (c == BN / 32 - 1) {   // accumulator fully read: hand it back to the MMA issuer
@@ -332,8 +347,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) mbar_arrive(&tempty[b]);
         }
         const int nc = w.n0 + c * 32;
-        if (!row_ok || nc >= args.N) continue;
-        if (args.splits > 1) {
+        if (!row_ok || nc >= args.N) return;
+        if (!direct) {
           if (nc + 32 <= args.N) {
             float4* p4 = reinterpret_cast<float4*>(part + nc);
 #pragma unroll
@@ -344,8 +359,15 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (nc + i < args.N) part[nc + i] = v[i];
           }
         } else {
-          epi_store(e, args.N, w.z, m, nc, v);
+          if (c + 1 < BN / 32 && nc + 32 < args.N)
+            epi_prefetch(e, args.N, rowoff + ((nc + 32) / e.n_div) * e.n_s1 + ((nc + 32) % e.n_div), nc + 32, next);
+          epi_store(e, args.N, rowoff + (nc / e.n_div) * e.n_s1 + (nc % e.n_div), nc, v, cur);
         }
+      };
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; c += 2) {   // BN / 32 is even for every BN
+        chunk(c, pre[0], pre[1]);
+        chunk(c + 1, pre[1], pre[0]);
       }
     }
   }
@@ -383,7 +405,10 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
         for (int k = 0; k < 32; ++k)
           if (nc + k < N) v[k] += p[s * slab + k];
     }
-    epi_store(e, N, 0, m, nc, v);
+    float4 pre[8];
+    const long long off = epi_offset(e, 0, m, nc);
+    epi_prefetch(e, N, off, nc, pre);
+    epi_store(e, N, off, nc, v, pre);
   }
 }
 
