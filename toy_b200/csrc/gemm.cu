@@ -19,6 +19,7 @@
 // queries (n0 > m0 + 127); 2 clamps K (keys) to m0 + 128 because P / dS are
 // zero beyond the diagonal.
 #include "gemm.cuh"
+#include "pdl.cuh"
 #include "tc_common.cuh"
 
 #include <cudaTypedefs.h>
@@ -212,6 +213,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Barrier set-up and the TMEM allocation above overlap the previous kernel's
+  // tail; nothing in global memory is touched before this point.
+  griddep_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -382,6 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // Split-K reduction: out(m, n) = epilogue(sum over s in order of ws[s][m][n]).
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int M, int N, Epilogue e) {
+  griddep_wait();
   const long long n32 = (long long)M * ((N + 31) / 32);
   const long long slab = (long long)M * N;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n32; i += (long long)gridDim.x * blockDim.x) {
@@ -510,14 +515,15 @@ int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream
   k.sem = sc.sem;
   k.err = dev_err;
   const int grid = k.units < kNumSMs ? k.units : kNumSMs;
-  gemm_split_bf16_kernel<BN, SPLIT><<<grid, kThreads, S::kSmemBytes, stream>>>(ma_hi, ma_lo, mb_hi, mb_lo, k);
-  if (cudaPeekAtLastError() != cudaSuccess) return -21;
+  if (launch_pdl(gemm_split_bf16_kernel<BN, SPLIT>, dim3(grid), dim3(kThreads), S::kSmemBytes, stream, ma_hi, ma_lo,
+                 mb_hi, mb_lo, k) != 0)
+    return -21;
   if (splits > 1) {
     const long long work = (long long)d.M * ((d.N + 31) / 32);
     long long blocks = (work + 127) / 128;
     if (blocks > 8 * kNumSMs) blocks = 8 * kNumSMs;
-    splitk_reduce_kernel<<<(int)blocks, 128, 0, stream>>>(sc.ws, splits, d.M, d.N, d.epi);
-    if (cudaPeekAtLastError() != cudaSuccess) return -21;
+    if (launch_pdl(splitk_reduce_kernel, dim3((int)blocks), dim3(128), 0, stream, sc.ws, splits, d.M, d.N, d.epi) != 0)
+      return -21;
   }
   return 0;
 }

@@ -2,6 +2,7 @@
 // registers, warp-shuffle reductions, fixed-order (deterministic) reductions,
 // grids sized in multiples of the SM count.
 #include "kernels.cuh"
+#include "pdl.cuh"
 
 #include <cuda_fp16.h>
 #include <cstdint>
@@ -81,6 +82,7 @@ int ok() { return cudaPeekAtLastError() == cudaSuccess ? 0 : -3; }
 // ------------------------------------------------------------------ split
 __global__ void split_f32_kernel(const float* __restrict__ x, bf16* __restrict__ hi, bf16* __restrict__ lo,
                                  long long n) {
+  griddep_wait();
   const long long n4 = n / 4;
   const long long stride = (long long)gridDim.x * blockDim.x;
   Planes p{hi, lo};
@@ -93,6 +95,7 @@ __global__ void split_f32_kernel(const float* __restrict__ x, bf16* __restrict__
 // ------------------------------------------------------------------ embedding
 __global__ void embed_gather_kernel(const float* __restrict__ E, const int* __restrict__ ids, float* __restrict__ x0,
                                     int N, int d4) {
+  griddep_wait();
   const long long total = (long long)N * d4;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -104,6 +107,7 @@ __global__ void embed_gather_kernel(const float* __restrict__ E, const int* __re
 __global__ void embed_scatter_kernel(const float* __restrict__ dx, const int* __restrict__ order,
                                      const int* __restrict__ seg_start, const int* __restrict__ seg_id,
                                      const int* __restrict__ nseg_dev, float* __restrict__ dE, int d) {
+  griddep_wait();
   const int nseg = *nseg_dev;
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x % 32;
@@ -126,6 +130,7 @@ __global__ void embed_scatter_kernel(const float* __restrict__ dx, const int* __
 template <int NC>
 __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                                                           Planes h, int N, int d, float eps) {
+  griddep_wait();
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x % 32;
   const int d4 = d / 4;
@@ -162,6 +167,7 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restric
                                                           const float* __restrict__ gamma, const float* dres,
                                                           float* dx, Planes dxp, float* __restrict__ gpart, int N,
                                                           int d, float eps) {
+  griddep_wait();
   extern __shared__ float4 gacc4[];  // [warps][d / 4]
   const int warps = blockDim.x / 32;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -226,6 +232,7 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restric
 // gout[c] = (accumulate ? gout[c] : 0) + sum_b gpart[b][c]: 32 columns per block,
 // 8 row groups summed in fixed order, then the groups in fixed order.
 __global__ void colsum_kernel(const float* __restrict__ gpart, int nblk, int d, float* gout, int accumulate) {
+  griddep_wait();
   __shared__ float sm[8][33];
   const int cx = threadIdx.x % 32, gy = threadIdx.x / 32;
   const int c = blockIdx.x * 32 + cx;
@@ -249,6 +256,7 @@ __global__ void __launch_bounds__(256) rope_qkv_fwd_kernel(const float* __restri
                                                            const int* __restrict__ pos, const float2* __restrict__ cs,
                                                            int tab_rows, Planes Q, Planes K, Planes V, int N, int T,
                                                            int H, int KV, int dh) {
+  griddep_wait();
   const int half = dh / 2;
   const int slots = H + 2 * KV;
   const int width = slots * dh;
@@ -287,6 +295,7 @@ __global__ void __launch_bounds__(256) rope_qkv_bwd_kernel(const float* __restri
                                                            const float* __restrict__ dV, const int* __restrict__ pos,
                                                            const float2* __restrict__ cs, int tab_rows, Planes out,
                                                            float* out_f32, int N, int T, int H, int KV, int dh) {
+  griddep_wait();
   const int half = dh / 2;
   const int slots = H + 2 * KV;
   const int width = slots * dh;
@@ -330,6 +339,7 @@ __global__ void __launch_bounds__(256) rope_qkv_bwd_kernel(const float* __restri
 template <int NC>
 __global__ void __launch_bounds__(256) softmax_causal_fwd_kernel(const float* __restrict__ S, Planes P, long long rows,
                                                                  int T) {
+  griddep_wait();
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x % 32;
   const int T4 = T / 4;
@@ -377,6 +387,7 @@ __global__ void __launch_bounds__(256) softmax_causal_fwd_kernel(const float* __
 template <int NC>
 __global__ void __launch_bounds__(256) softmax_causal_bwd_kernel(Planes P, const float* __restrict__ dP, Planes dS,
                                                                  long long rows, int T, float scale) {
+  griddep_wait();
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x % 32;
   const int T4 = T / 4;
@@ -418,6 +429,7 @@ __global__ void __launch_bounds__(256) softmax_causal_bwd_kernel(Planes P, const
 // ------------------------------------------------------------------ SwiGLU
 // One block per token row, float4 over the ff columns of gate | up.
 __global__ void __launch_bounds__(128) swiglu_fwd_kernel(const float* __restrict__ gu, Planes a, int N, int ff) {
+  griddep_wait();
   const int ff4 = ff / 4;
   for (int n = blockIdx.x; n < N; n += gridDim.x) {
     const float4* g4 = reinterpret_cast<const float4*>(gu + (long long)n * 2 * ff);
@@ -439,6 +451,7 @@ __device__ __forceinline__ void swiglu_back1(float g, float u, float dy, float& 
 
 __global__ void __launch_bounds__(128) swiglu_bwd_kernel(const float* __restrict__ gu, const float* __restrict__ da,
                                                          Planes dgu, int N, int ff) {
+  griddep_wait();
   const int ff4 = ff / 4;
   for (int n = blockIdx.x; n < N; n += gridDim.x) {
     const float4* g4 = reinterpret_cast<const float4*>(gu + (long long)n * 2 * ff);
@@ -472,6 +485,7 @@ __global__ void __launch_bounds__(kCeThreads) cross_entropy_kernel(const float* 
                                                                    const float* __restrict__ label_dense,
                                                                    float* __restrict__ loss_rows, Planes dl, int N,
                                                                    int V) {
+  griddep_wait();
   __shared__ float sm_m[kCeThreads / 32], sm_s[kCeThreads / 32];
   __shared__ float bc[2];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -565,6 +579,7 @@ __global__ void __launch_bounds__(kCeThreads) cross_entropy_kernel(const float* 
 }
 
 __global__ void loss_reduce_kernel(const float* __restrict__ rows, int N, float* __restrict__ loss) {
+  griddep_wait();
   __shared__ float sm[1024 / 32];
   float s = 0.f;
   for (int i = threadIdx.x; i < N; i += blockDim.x) s += rows[i];
@@ -582,6 +597,7 @@ __global__ void loss_reduce_kernel(const float* __restrict__ rows, int N, float*
 __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, Planes pp, long long n4, const float* __restrict__ hp,
                              float grad_scale) {
+  griddep_wait();
   const float alpha = hp[0], b1 = hp[1], b2 = hp[2], eps = hp[3], wd = hp[4], b1h = hp[5], b2h = hp[6];
   const float keep = 1.0f - alpha * wd;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
@@ -611,6 +627,7 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
 // ------------------------------------------------------------------ Q8_0
 __global__ void q8_0_to_planes_kernel(const uint8_t* __restrict__ q, Planes out, float* __restrict__ f32,
                                       long long rows, int K) {
+  griddep_wait();
   const long long total = rows * K;
   const int row_bytes = K / 32 * 34;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -636,6 +653,7 @@ __device__ __forceinline__ int round_half_away(float v) {
 }
 
 __global__ void q8_0_quantize_kernel(const float* __restrict__ x, uint8_t* __restrict__ q, long long nblocks) {
+  griddep_wait();
   for (long long b = blockIdx.x * (long long)blockDim.x + threadIdx.x; b < nblocks;
        b += (long long)gridDim.x * blockDim.x) {
     const float* xb = x + b * 32;
@@ -655,6 +673,7 @@ __global__ void q8_0_quantize_kernel(const float* __restrict__ x, uint8_t* __res
 }
 
 __global__ void colsum_rows_kernel(const float* __restrict__ x, int N, int W, float* __restrict__ out) {
+  griddep_wait();
   for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < W; c += gridDim.x * blockDim.x) {
     float s = 0.f;
     for (int n = 0; n < N; ++n) s += x[(long long)n * W + c];
@@ -663,6 +682,7 @@ __global__ void colsum_rows_kernel(const float* __restrict__ x, int N, int W, fl
 }
 
 __global__ void add_inplace_kernel(float* __restrict__ y, const float* __restrict__ x, long long n) {
+  griddep_wait();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
     y[i] += x[i];
 }
@@ -698,7 +718,7 @@ int dispatch_nc(int nc, A... a) {
 template <int NC>
 struct RmsFwd {
   static int run(const float* x, const float* gamma, Planes h, int N, int d, float eps, cudaStream_t st) {
-    rmsnorm_fwd_kernel<NC><<<grid_for((long long)N * 32, 256), 256, 0, st>>>(x, gamma, h, N, d, eps);
+    launch_pdl(rmsnorm_fwd_kernel<NC>, dim3(grid_for((long long)N * 32, 256)), dim3(256), 0, st, x, gamma, h, N, d, eps);
     return ok();
   }
 };
@@ -713,7 +733,7 @@ struct RmsBwd {
       cudaFuncSetAttribute(rmsnorm_bwd_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
       attr = true;
     }
-    rmsnorm_bwd_kernel<NC><<<nblk, 256, smem, st>>>(x, dh, gamma, dres, dx, dxp, gpart, N, d, eps);
+    launch_pdl(rmsnorm_bwd_kernel<NC>, dim3(nblk), dim3(256), smem, st, x, dh, gamma, dres, dx, dxp, gpart, N, d, eps);
     return ok();
   }
 };
@@ -721,7 +741,7 @@ struct RmsBwd {
 template <int NC>
 struct SmFwd {
   static int run(const float* S, Planes P, long long rows, int T, cudaStream_t st) {
-    softmax_causal_fwd_kernel<NC><<<grid_for(rows * 32, 256), 256, 0, st>>>(S, P, rows, T);
+    launch_pdl(softmax_causal_fwd_kernel<NC>, dim3(grid_for(rows * 32, 256)), dim3(256), 0, st, S, P, rows, T);
     return ok();
   }
 };
@@ -729,7 +749,7 @@ struct SmFwd {
 template <int NC>
 struct SmBwd {
   static int run(Planes P, const float* dP, Planes dS, long long rows, int T, float scale, cudaStream_t st) {
-    softmax_causal_bwd_kernel<NC><<<grid_for(rows * 32, 256), 256, 0, st>>>(P, dP, dS, rows, T, scale);
+    launch_pdl(softmax_causal_bwd_kernel<NC>, dim3(grid_for(rows * 32, 256)), dim3(256), 0, st, P, dP, dS, rows, T, scale);
     return ok();
   }
 };
@@ -741,20 +761,20 @@ int rmsnorm_bwd_blocks() { return kRmsBwdBlocks; }
 int launch_split_f32(const float* x, bf16* hi, bf16* lo, long long n, cudaStream_t st) {
   if (n <= 0) return 0;
   if (!aligned16(x) || (reinterpret_cast<uintptr_t>(hi) & 7u) || (reinterpret_cast<uintptr_t>(lo) & 7u)) return -1;
-  split_f32_kernel<<<grid_for(n / 4 + 1, 256), 256, 0, st>>>(x, hi, lo, n);
+  launch_pdl(split_f32_kernel, dim3(grid_for(n / 4 + 1, 256)), dim3(256), 0, st, x, hi, lo, n);
   return ok();
 }
 
 int launch_embed_gather(const float* E, const int* ids, float* x0, int N, int d, cudaStream_t st) {
   if (d % 4) return -1;
-  embed_gather_kernel<<<grid_for((long long)N * d / 4, 256), 256, 0, st>>>(E, ids, x0, N, d / 4);
+  launch_pdl(embed_gather_kernel, dim3(grid_for((long long)N * d / 4, 256)), dim3(256), 0, st, E, ids, x0, N, d / 4);
   return ok();
 }
 
 int launch_embed_scatter(const float* dx, const int* order, const int* seg_start, const int* seg_id,
                          const int* nseg_dev, int max_seg, float* dE, int d, cudaStream_t st) {
   if (d % 4 || max_seg <= 0) return -1;
-  embed_scatter_kernel<<<grid_for((long long)max_seg * 32, 256), 256, 0, st>>>(dx, order, seg_start, seg_id,
+  launch_pdl(embed_scatter_kernel, dim3(grid_for((long long)max_seg * 32, 256)), dim3(256), 0, st, dx, order, seg_start, seg_id,
                                                                                nseg_dev, dE, d);
   return ok();
 }
@@ -772,7 +792,7 @@ int launch_rmsnorm_bwd(const float* x, const float* dh, const float* gamma, cons
 }
 
 int launch_colsum(const float* gpart, int nblk, int d, float* gout, int accumulate, cudaStream_t st) {
-  colsum_kernel<<<(d + 31) / 32, 256, 0, st>>>(gpart, nblk, d, gout, accumulate);
+  launch_pdl(colsum_kernel, dim3((d + 31) / 32), dim3(256), 0, st, gpart, nblk, d, gout, accumulate);
   return ok();
 }
 
@@ -780,7 +800,7 @@ int launch_rope_qkv_fwd(const float* qkv, const float* bias, const int* pos, con
                         Planes Q, Planes K, Planes V, int B, int T, int H, int KV, int dh, cudaStream_t st) {
   if (dh % 2) return -1;
   const int N = B * T;
-  rope_qkv_fwd_kernel<<<N < 8 * kSMs ? N : 8 * kSMs, 256, 0, st>>>(
+  launch_pdl(rope_qkv_fwd_kernel, dim3(N < 8 * kSMs ? N : 8 * kSMs), dim3(256), 0, st,
       qkv, bias, pos, reinterpret_cast<const float2*>(cs_tab), tab_rows, Q, K, V, N, T, H, KV, dh);
   return ok();
 }
@@ -789,7 +809,7 @@ int launch_rope_qkv_bwd(const float* dQ, const float* dK, const float* dV, const
                         int tab_rows, Planes dqkv, float* dqkv_f32, int B, int T, int H, int KV, int dh,
                         cudaStream_t st) {
   const int N = B * T;
-  rope_qkv_bwd_kernel<<<N < 8 * kSMs ? N : 8 * kSMs, 256, 0, st>>>(
+  launch_pdl(rope_qkv_bwd_kernel, dim3(N < 8 * kSMs ? N : 8 * kSMs), dim3(256), 0, st,
       dQ, dK, dV, pos, reinterpret_cast<const float2*>(cs_tab), tab_rows, dqkv, dqkv_f32, N, T, H, KV, dh);
   return ok();
 }
@@ -807,55 +827,55 @@ int launch_softmax_causal_bwd(Planes P, const float* dP, Planes dS, long long Z,
 
 int launch_swiglu_fwd(const float* gu, Planes a, int N, int ff, cudaStream_t st) {
   if (ff % 4) return -1;
-  swiglu_fwd_kernel<<<N < 16 * kSMs ? N : 16 * kSMs, 128, 0, st>>>(gu, a, N, ff);
+  launch_pdl(swiglu_fwd_kernel, dim3(N < 16 * kSMs ? N : 16 * kSMs), dim3(128), 0, st, gu, a, N, ff);
   return ok();
 }
 
 int launch_swiglu_bwd(const float* gu, const float* da, Planes dgu, int N, int ff, cudaStream_t st) {
   if (ff % 4) return -1;
-  swiglu_bwd_kernel<<<N < 16 * kSMs ? N : 16 * kSMs, 128, 0, st>>>(gu, da, dgu, N, ff);
+  launch_pdl(swiglu_bwd_kernel, dim3(N < 16 * kSMs ? N : 16 * kSMs), dim3(128), 0, st, gu, da, dgu, N, ff);
   return ok();
 }
 
 int launch_cross_entropy(const float* logits, const int* label_ids, const float* label_dense, float* loss_rows,
                          Planes dlogits, int N, int V, cudaStream_t st) {
   int g = N < 4 * kSMs ? N : 4 * kSMs;
-  cross_entropy_kernel<<<g, kCeThreads, 0, st>>>(logits, label_ids, label_dense, loss_rows, dlogits, N, V);
+  launch_pdl(cross_entropy_kernel, dim3(g), dim3(kCeThreads), 0, st, logits, label_ids, label_dense, loss_rows, dlogits, N, V);
   return ok();
 }
 
 int launch_loss_reduce(const float* loss_rows, int N, float* loss, cudaStream_t st) {
-  loss_reduce_kernel<<<1, 1024, 0, st>>>(loss_rows, N, loss);
+  launch_pdl(loss_reduce_kernel, dim3(1), dim3(1024), 0, st, loss_rows, N, loss);
   return ok();
 }
 
 int launch_adamw(float* p, const float* g, float* m, float* v, Planes pp, long long n, const float* hp,
                  float grad_scale, cudaStream_t st) {
   if (n % 4 || !aligned16(p) || !aligned16(g) || !aligned16(m) || !aligned16(v)) return -1;
-  adamw_kernel<<<grid_for(n / 4, 256), 256, 0, st>>>(p, g, m, v, pp, n / 4, hp, grad_scale);
+  launch_pdl(adamw_kernel, dim3(grid_for(n / 4, 256)), dim3(256), 0, st, p, g, m, v, pp, n / 4, hp, grad_scale);
   return ok();
 }
 
 int launch_q8_0_to_planes(const uint8_t* q, Planes out, float* f32, long long rows, int K, cudaStream_t st) {
   if (K % 32) return -1;
-  q8_0_to_planes_kernel<<<grid_for(rows * K, 256), 256, 0, st>>>(q, out, f32, rows, K);
+  launch_pdl(q8_0_to_planes_kernel, dim3(grid_for(rows * K, 256)), dim3(256), 0, st, q, out, f32, rows, K);
   return ok();
 }
 
 int launch_q8_0_quantize(const float* x, uint8_t* q, long long rows, int K, cudaStream_t st) {
   if (K % 32 || (reinterpret_cast<uintptr_t>(q) & 1u) || (reinterpret_cast<uintptr_t>(x) & 3u)) return -1;
   const long long nb = rows * (K / 32);
-  q8_0_quantize_kernel<<<grid_for(nb, 128), 128, 0, st>>>(x, q, nb);
+  launch_pdl(q8_0_quantize_kernel, dim3(grid_for(nb, 128)), dim3(128), 0, st, x, q, nb);
   return ok();
 }
 
 int launch_colsum_rows(const float* x, int N, int W, float* out, cudaStream_t st) {
-  colsum_rows_kernel<<<(W + 127) / 128, 128, 0, st>>>(x, N, W, out);
+  launch_pdl(colsum_rows_kernel, dim3((W + 127) / 128), dim3(128), 0, st, x, N, W, out);
   return ok();
 }
 
 int launch_add_inplace(float* y, const float* x, long long n, cudaStream_t st) {
-  add_inplace_kernel<<<grid_for(n, 256), 256, 0, st>>>(y, x, n);
+  launch_pdl(add_inplace_kernel, dim3(grid_for(n, 256)), dim3(256), 0, st, y, x, n);
   return ok();
 }
 

@@ -1,0 +1,31 @@
+// Programmatic dependent launch: every kernel of the step is launched with
+// programmatic stream serialisation, so the next kernel's launch and its
+// data-independent prologue overlap the tail of the previous one. Each kernel
+// calls griddep_wait() before it touches global memory, which waits for the
+// previous kernel to complete and its writes to be visible; since every kernel
+// waits, completion is ordered transitively down the stream.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <utility>
+
+namespace tb2 {
+
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KParams, typename... Args>
+int launch_pdl(void (*kernel)(KParams...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...) == cudaSuccess ? 0 : -3;
+}
+
+}  // namespace tb2
