@@ -153,6 +153,7 @@ typedef struct tb2_llama_config {
   double lora_alpha;
   int lora_targets;
   const double *rope_freq_factors; /* d_head/2 llama3 factors or NULL */
+  int attn_impl;                   /* 0: fused flash attention (d_head 64), 1: materialised scores */
 } tb2_llama_config;
 
 /* Realize the forward + cross-entropy + backward + AdamW program for a Llama

@@ -84,6 +84,7 @@ int tb2_llama_realize(void* sess, const tb2_llama_config* cfg) {
   c.freq_scale = cfg->freq_scale > 0 ? (float)cfg->freq_scale : 1.0f;
   c.tied = cfg->tied; c.qkv_bias = cfg->qkv_bias; c.T = cfg->t_seq; c.B = cfg->t_batch; c.mode = cfg->mode;
   c.lora_rank = cfg->lora_rank; c.lora_alpha = (float)cfg->lora_alpha; c.lora_targets = cfg->lora_targets;
+  c.attn_impl = cfg->attn_impl;
   if (cfg->rope_freq_factors)
     for (int i = 0; i < cfg->d_head / 2; ++i) c.freq_factors.push_back((float)cfg->rope_freq_factors[i]);
   if (cudaSetDevice(s->device) != cudaSuccess) return -3;

@@ -7,6 +7,7 @@
 #include <cstring>
 #include <thread>
 
+#include "flash_attn.cuh"
 #include "runtime.cuh"
 
 namespace tb2 {
@@ -145,7 +146,10 @@ int LlamaEngine::realize() {
   if (c.vocab <= 0 || c.d_model <= 0 || c.n_heads <= 0 || c.n_kv <= 0 || c.d_head <= 0 || c.d_ff <= 0 ||
       c.n_layers <= 0 || c.T <= 0 || c.B <= 0)
     return -1;
-  if (c.n_heads % c.n_kv || c.d_model % 64 || c.d_ff % 64 || c.d_head % 32 || c.T % 64 || c.vocab % 8) return -1;
+  if (c.n_heads % c.n_kv || c.d_model % 64 || c.d_ff % 64 || c.d_head % 32 || c.vocab % 8) return -1;
+  // the materialised score path tiles T x T matrices in 64-wide blocks; the
+  // fused attention masks ragged tiles and takes any T
+  if (c.T % 64 && !(c.attn_impl == 0 && flash_supported(c.d_head))) return -1;
   if (c.mode == 1 && (c.lora_rank <= 0 || c.lora_rank % 8 || c.lora_targets == 0)) return -1;
   CU(cudaSetDevice(device_));
   CU(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
@@ -235,6 +239,7 @@ int LlamaEngine::realize() {
     return Planes{base, base + np};
   };
   const long long att = (long long)B * H * T * T;
+  flash_ = c.attn_impl == 0 && flash_supported(dh);
   for (int l = 0; l <= c.n_layers; ++l) x_.push_back(f32((long long)N * d));
   lora_u_.resize(c.n_layers);
   for (int l = 0; l < c.n_layers; ++l) {
@@ -246,14 +251,15 @@ int LlamaEngine::realize() {
     Qh_.push_back(pl((long long)N * H * dh));
     Kh_.push_back(pl((long long)N * KV * dh));
     Vh_.push_back(pl((long long)N * KV * dh));
-    Pm_.push_back(pl(att));
+    Pm_.push_back(flash_ ? Planes{} : pl(att));
+    lse2_.push_back(flash_ ? f32((long long)B * H * T) : nullptr);
     O_.push_back(pl((long long)N * H * dh));
     lora_u_[l].resize(kLoraCount);
     for (int t = 0; t < kLoraCount; ++t)
       if (!full && (c.lora_targets & (1 << t))) lora_u_[l][t] = pl((long long)N * r);
   }
   qkv_ = f32((long long)N * W);
-  S_ = f32(att);
+  if (!flash_) S_ = f32(att);
   logits_ = f32((long long)N * V);
   loss_rows_ = f32(N);
   loss_ = f32(64);
@@ -261,16 +267,21 @@ int LlamaEngine::realize() {
   dh_ = f32((long long)N * d);
   da_ = f32((long long)N * ff);
   dO32_ = f32((long long)N * H * dh);
-  dQ_ = f32((long long)N * H * dh);
-  dK_ = f32((long long)N * KV * dh);
-  dV_ = f32((long long)N * KV * dh);
+  if (!flash_) {
+    dQ_ = f32((long long)N * H * dh);
+    dK_ = f32((long long)N * KV * dh);
+    dV_ = f32((long long)N * KV * dh);
+  } else {
+    dvec_ = f32((long long)B * H * T);
+    fws_ = f32(flash_bwd_ws_floats(B, T, H, KV, dh));
+  }
   gpart_ = f32((long long)rmsnorm_bwd_blocks() * d);
   xf_ = pl((long long)N * d);
   dlog_ = pl((long long)N * V);
   dxp_ = pl((long long)N * d);
   dgu_ = pl((long long)N * 2 * ff);
   dO_ = pl((long long)N * H * dh);
-  dS_ = pl(att);
+  if (!flash_) dS_ = pl(att);
   dqkv_ = pl((long long)N * W);
   if (!full) {
     u32_ = f32((long long)N * r);
@@ -602,7 +613,9 @@ int kind_of(const char* call) {
       {"launch_softmax", LlamaEngine::kKSoftmax},    {"launch_swiglu", LlamaEngine::kKSwiglu},
       {"launch_cross_entropy", LlamaEngine::kKCe},   {"launch_loss_reduce", LlamaEngine::kKLoss},
       {"launch_adamw", LlamaEngine::kKAdamw},        {"launch_embed", LlamaEngine::kKEmbed},
-      {"launch_split", LlamaEngine::kKSplit}};
+      {"launch_split", LlamaEngine::kKSplit},        {"launch_flash_fwd", LlamaEngine::kKFlashFwd},
+      {"launch_flash_bwd_prep", LlamaEngine::kKFlashPrep}, {"launch_flash_bwd", LlamaEngine::kKFlashBwd},
+      {"launch_flash_rope", LlamaEngine::kKRope}};
   for (const auto& t : table)
     if (strncmp(call, t.prefix, strlen(t.prefix)) == 0) return t.kind;
   return LlamaEngine::kKCount;
@@ -713,25 +726,30 @@ int LlamaEngine::enqueue_forward() {
     }
     const float* bias = c.qkv_bias ? P32(P(pre + "attn_q.bias")) : nullptr;
     KL(launch_rope_qkv_fwd(qkv_, bias, pos_, cs_, cs_rows_, Qh_[l], Kh_[l], Vh_[l], B, T, H, KV, dh, stream_));
-    // scores S = scale * Q K^T per (sequence, head)
-    GemmDesc gs;
-    gs.M = T; gs.N = T; gs.K = dh; gs.batch = B * H;
-    gs.a = bop(Qh_[l], T, dh, dh, B * H, 0);
-    gs.b = bop(Kh_[l], T, dh, dh, B * KV, 0, H, KV, G, 1);
-    gs.causal = 1;   // tiles above the diagonal are never read by the causal softmax
-    gs.epi.mode = kEpiStoreF32; gs.epi.out = S_; gs.epi.alpha = scale; gs.epi.m_s0 = T;
-    gs.epi.bstride = (long long)T * T;
-    CK(gemm(gs));
-    KL(launch_softmax_causal_fwd(S_, Pm_[l], (long long)B * H, T, stream_));
-    // O = P V, written token-major [N][H*dh]
-    GemmDesc go;
-    go.M = T; go.N = dh; go.K = T; go.batch = B * H;
-    go.a = bop(Pm_[l], T, T, T, B * H, 0);
-    go.b = bop(Vh_[l], T, dh, dh, B * KV, 1, H, KV, G, 1);
-    go.causal = 2;   // P is zero for keys past the tile's last query
-    go.epi.mode = kEpiStoreSplit; go.epi.out_hi = O_[l].hi; go.epi.out_lo = O_[l].lo;
-    go.epi.z_div = H; go.epi.z_s1 = (long long)T * H * dh; go.epi.bstride = dh; go.epi.m_s0 = (long long)H * dh;
-    CK(gemm(go));
+    if (flash_) {
+      // fused: O (token-major planes) and the row normalisers for the backward
+      KL(launch_flash_fwd(Qh_[l], Kh_[l], Vh_[l], O_[l], lse2_[l], B, T, H, KV, dh, scale, err_, stream_));
+    } else {
+      // scores S = scale * Q K^T per (sequence, head)
+      GemmDesc gs;
+      gs.M = T; gs.N = T; gs.K = dh; gs.batch = B * H;
+      gs.a = bop(Qh_[l], T, dh, dh, B * H, 0);
+      gs.b = bop(Kh_[l], T, dh, dh, B * KV, 0, H, KV, G, 1);
+      gs.causal = 1;   // tiles above the diagonal are never read by the causal softmax
+      gs.epi.mode = kEpiStoreF32; gs.epi.out = S_; gs.epi.alpha = scale; gs.epi.m_s0 = T;
+      gs.epi.bstride = (long long)T * T;
+      CK(gemm(gs));
+      KL(launch_softmax_causal_fwd(S_, Pm_[l], (long long)B * H, T, stream_));
+      // O = P V, written token-major [N][H*dh]
+      GemmDesc go;
+      go.M = T; go.N = dh; go.K = T; go.batch = B * H;
+      go.a = bop(Pm_[l], T, T, T, B * H, 0);
+      go.b = bop(Vh_[l], T, dh, dh, B * KV, 1, H, KV, G, 1);
+      go.causal = 2;   // P is zero for keys past the tile's last query
+      go.epi.mode = kEpiStoreSplit; go.epi.out_hi = O_[l].hi; go.epi.out_lo = O_[l].lo;
+      go.epi.z_div = H; go.epi.z_s1 = (long long)T * H * dh; go.epi.bstride = dh; go.epi.m_s0 = (long long)H * dh;
+      CK(gemm(go));
+    }
     // x1 = x + O Wo^T
     GemmDesc gw;
     gw.M = N; gw.N = d; gw.K = H * dh;
@@ -865,37 +883,46 @@ int LlamaEngine::enqueue_backward() {
     }
     if (lora && (c.lora_targets & (1 << kLoraO)))
       CK(lora_backward(l, kLoraO, O_[l], H * dh, dxp_, d, 0, d, dO32_, &hm));
-    KL(launch_split_f32(dO32_, dO_.hi, dO_.lo, (long long)N * H * dh, stream_));
-    // ---- attention core
-    GemmDesc gp;
-    gp.M = T; gp.N = T; gp.K = dh; gp.batch = B * H;
-    gp.a = bop(dO_, T, dh, dh, B * H, 0);
-    gp.b = bop(Vh_[l], T, dh, dh, B * KV, 0, H, KV, G, 1);
-    gp.causal = 1;
-    gp.epi.mode = kEpiStoreF32; gp.epi.out = S_; gp.epi.m_s0 = T; gp.epi.bstride = (long long)T * T;
-    CK(gemm(gp));
-    KL(launch_softmax_causal_bwd(Pm_[l], S_, dS_, (long long)B * H, T, scale, stream_));
-    GemmDesc gq;
-    gq.M = T; gq.N = dh; gq.K = T; gq.batch = B * H;
-    gq.a = bop(dS_, T, T, T, B * H, 0);
-    gq.b = bop(Kh_[l], T, dh, dh, B * KV, 1, H, KV, G, 1);
-    gq.causal = 2;   // dS is zero past the diagonal
-    gq.epi.mode = kEpiStoreF32; gq.epi.out = dQ_; gq.epi.m_s0 = dh; gq.epi.bstride = (long long)T * dh;
-    CK(gemm(gq));
-    GemmDesc gk;
-    gk.M = T; gk.N = dh; gk.K = G * T; gk.batch = B * KV;
-    gk.a = bop(dS_, G * T, T, T, B * KV, 1);
-    gk.b = bop(Qh_[l], G * T, dh, dh, B * KV, 1);
-    gk.epi.mode = kEpiStoreF32; gk.epi.out = dK_; gk.epi.m_s0 = dh; gk.epi.bstride = (long long)T * dh;
-    CK(gemm(gk));
-    GemmDesc gv;
-    gv.M = T; gv.N = dh; gv.K = G * T; gv.batch = B * KV;
-    gv.a = bop(Pm_[l], G * T, T, T, B * KV, 1);
-    gv.b = bop(dO_, G * T, dh, dh, B * KV, 1);
-    gv.epi.mode = kEpiStoreF32; gv.epi.out = dV_; gv.epi.m_s0 = dh; gv.epi.bstride = (long long)T * dh;
-    CK(gemm(gv));
-    KL(launch_rope_qkv_bwd(dQ_, dK_, dV_, pos_, cs_, cs_rows_, dqkv_, c.qkv_bias ? qkv_ : nullptr, B, T, H, KV, dh,
-                           stream_));
+    if (flash_) {
+      // ---- attention core, fused: partial dQ / dK / dV summed by the RoPE backward
+      KL(launch_flash_bwd_prep(dO32_, O_[l], dO_, dvec_, B, T, H, dh, stream_));
+      KL(launch_flash_bwd(Qh_[l], Kh_[l], Vh_[l], dO_, lse2_[l], dvec_, fws_, B, T, H, KV, dh, scale, err_,
+                          stream_));
+      KL(launch_flash_rope_bwd(fws_, pos_, cs_, cs_rows_, dqkv_, c.qkv_bias ? qkv_ : nullptr, B, T, H, KV, dh,
+                               stream_));
+    } else {
+      KL(launch_split_f32(dO32_, dO_.hi, dO_.lo, (long long)N * H * dh, stream_));
+      // ---- attention core
+      GemmDesc gp;
+      gp.M = T; gp.N = T; gp.K = dh; gp.batch = B * H;
+      gp.a = bop(dO_, T, dh, dh, B * H, 0);
+      gp.b = bop(Vh_[l], T, dh, dh, B * KV, 0, H, KV, G, 1);
+      gp.causal = 1;
+      gp.epi.mode = kEpiStoreF32; gp.epi.out = S_; gp.epi.m_s0 = T; gp.epi.bstride = (long long)T * T;
+      CK(gemm(gp));
+      KL(launch_softmax_causal_bwd(Pm_[l], S_, dS_, (long long)B * H, T, scale, stream_));
+      GemmDesc gq;
+      gq.M = T; gq.N = dh; gq.K = T; gq.batch = B * H;
+      gq.a = bop(dS_, T, T, T, B * H, 0);
+      gq.b = bop(Kh_[l], T, dh, dh, B * KV, 1, H, KV, G, 1);
+      gq.causal = 2;   // dS is zero past the diagonal
+      gq.epi.mode = kEpiStoreF32; gq.epi.out = dQ_; gq.epi.m_s0 = dh; gq.epi.bstride = (long long)T * dh;
+      CK(gemm(gq));
+      GemmDesc gk;
+      gk.M = T; gk.N = dh; gk.K = G * T; gk.batch = B * KV;
+      gk.a = bop(dS_, G * T, T, T, B * KV, 1);
+      gk.b = bop(Qh_[l], G * T, dh, dh, B * KV, 1);
+      gk.epi.mode = kEpiStoreF32; gk.epi.out = dK_; gk.epi.m_s0 = dh; gk.epi.bstride = (long long)T * dh;
+      CK(gemm(gk));
+      GemmDesc gv;
+      gv.M = T; gv.N = dh; gv.K = G * T; gv.batch = B * KV;
+      gv.a = bop(Pm_[l], G * T, T, T, B * KV, 1);
+      gv.b = bop(dO_, G * T, dh, dh, B * KV, 1);
+      gv.epi.mode = kEpiStoreF32; gv.epi.out = dV_; gv.epi.m_s0 = dh; gv.epi.bstride = (long long)T * dh;
+      CK(gemm(gv));
+      KL(launch_rope_qkv_bwd(dQ_, dK_, dV_, pos_, cs_, cs_rows_, dqkv_, c.qkv_bias ? qkv_ : nullptr, B, T, H, KV, dh,
+                             stream_));
+    }
     if (c.qkv_bias && full) KL(launch_colsum_rows(qkv_, N, W, G32(P(pre + "attn_q.bias")), stream_));
     // ---- QKV projection
     GemmDesc gx;
@@ -1063,7 +1090,9 @@ long long LlamaEngine::debug_activation(int which, int layer, float* dst, long l
     case 3: p = Qh_[layer]; n = N * H * dh; break;
     case 4: p = Kh_[layer]; n = N * KV * dh; break;
     case 5: p = Vh_[layer]; n = N * KV * dh; break;
-    case 6: p = Pm_[layer]; n = (long long)c.B * H * c.T * c.T; break;
+    case 6:
+      if (flash_) return -2;   // the fused attention keeps no probability matrix
+      p = Pm_[layer]; n = (long long)c.B * H * c.T * c.T; break;
     case 7: p = O_[layer]; n = N * H * dh; break;
     case 8: f = gu_[layer]; n = N * 2 * ff; break;
     case 9: p = a_[layer]; n = N * ff; break;

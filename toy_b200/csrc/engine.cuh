@@ -26,6 +26,7 @@ struct LlamaConfig {
   float lora_alpha = 0.f;
   int lora_targets = 0;   // bitmask over LoraTarget
   std::vector<float> freq_factors;   // d_head/2 llama3-style factors, or empty
+  int attn_impl = 0;      // 0: fused flash attention where supported, 1: materialised scores
 };
 
 // One named parameter inside the arenas.
@@ -107,7 +108,7 @@ class LlamaEngine {
   // an event pair around every launch; fills per-launch kind, duration and
   // algorithmic FLOPs (GEMMs), returns the launch count.
   enum Kind : int { kKGemm = 0, kKRmsFwd, kKRmsBwd, kKColsum, kKRope, kKSoftmax, kKSwiglu, kKCe, kKLoss, kKAdamw,
-                    kKEmbed, kKSplit, kKAllreduce, kKCount };
+                    kKEmbed, kKSplit, kKAllreduce, kKFlashFwd, kKFlashBwd, kKFlashPrep, kKCount };
   int run_steps(int n, float* ms);
   int profile_step(bool is_first, int* kinds, float* ms, double* flops, int cap);
 
@@ -143,6 +144,9 @@ class LlamaEngine {
   std::vector<DeviceBuf> bufs_;
   std::vector<float*> x_, x1_, gu_;
   std::vector<Planes> h1_, h2_, a_, Qh_, Kh_, Vh_, Pm_, O_;
+  bool flash_ = false;             // attention core on the fused flash kernels
+  std::vector<float*> lse2_;       // flash: per-layer softmax normalisers [B][H][T]
+  float *dvec_ = nullptr, *fws_ = nullptr;   // flash backward: D and partial-gradient workspace
   std::vector<std::vector<Planes>> lora_u_;   // [layer][target]
   float *qkv_ = nullptr, *S_ = nullptr, *logits_ = nullptr, *loss_rows_ = nullptr, *loss_ = nullptr;
   float *dx_ = nullptr, *dh_ = nullptr, *da_ = nullptr, *dO32_ = nullptr, *dQ_ = nullptr, *dK_ = nullptr,

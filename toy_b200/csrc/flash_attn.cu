@@ -1,0 +1,794 @@
+// Fused causal attention forward and backward on tcgen05 (sm_100a).
+//
+// Every product runs on split-bf16 operands with three UMMAs per k-step
+// (hi*hi + lo*hi + hi*lo, f32 accumulate in TMEM), like the GEMM in gemm.cu.
+// Tiles are 128 rows x 64 head columns; one [128 x 64] bf16 plane tile is a
+// 16 KB block in the TMA 128-byte swizzle layout (row r at r * 128 bytes, its
+// 16-byte chunk c stored at chunk c ^ (r % 8)). The same tile serves as a
+// K-major operand (rows = M or N, head columns = K) and as an MN-major operand
+// (rows = K, head columns = N), so Q, K, V and dO are loaded once per use.
+//
+// CTA = 10 warps: warp 0 issues TMA loads, warp 1 allocates TMEM and issues
+// the UMMAs, warps 2..9 do the softmax arithmetic. A warp may only touch the
+// 32 TMEM lanes of its quarter (warp % 4), so each quarter -- 32 query rows in
+// the forward, 32 key rows in the backward -- is served by two warps, one per
+// 64-column half of the 128-column score tile. Probability / score-gradient
+// tiles go from registers to shared memory in the swizzled layout and feed the
+// next UMMA directly; nothing of size T x T reaches HBM.
+//
+// Forward (per sequence, head, query tile of 128): two passes over the key
+// tiles 0..qi. Pass 1 computes S = Q K^T and each row's maximum; pass 2
+// recomputes S, writes P = exp(S - max) to shared memory while summing it,
+// and accumulates O += P V in TMEM; the epilogue divides O by the sum. Every
+// P uses the final maximum, so O needs no rescaling. The scores of the next
+// key tile are computed while the softmax warps work on the current one (two
+// TMEM score buffers).
+//
+// Backward (per sequence, query head, key tile j of 128), over the query tiles
+// i = j .. : dP^T = V dO^T and S^T = K Q^T in TMEM; the softmax warps write
+// P^T to shared memory and park dS^T = P^T (dP^T - D) * scale in the S^T
+// columns; dV += P^T dO; then dS^T moves to the same shared buffer, dK += dS^T Q
+// and dQ_i = dS K (the dS^T tile read MN-major).
+// dQ_i leaves through one of two TMEM buffers as this key tile's partial; dK
+// and dV leave at the end as this query head's partial. The RoPE backward
+// kernel sums the partials in a fixed order, so the result is deterministic.
+#include "flash_attn.cuh"
+
+#include "gemm.cuh"
+#include "pdl.cuh"
+#include "tc_common.cuh"
+
+#include <cmath>
+
+namespace tb2 {
+
+namespace {
+
+constexpr int kTile = 128;                 // query / key rows per tile
+constexpr int kDh = 64;                    // head width
+constexpr int kPlane = kTile * kDh * 2;    // one [128 x 64] bf16 plane tile: 16 KB
+constexpr int kSoftWarps = 8;              // two per TMEM lane quarter, one per 64-column half
+constexpr int kThreads = 32 * (2 + kSoftWarps);
+constexpr int kRing = 3;                   // forward key/value stages
+
+// forward: Q, ring, P, then the row max / row sum exchange between column halves
+constexpr int kFwdSmem = (2 + 2 * kRing + 4) * kPlane + 4 * kTile * 4 + 1024 + 256;
+// backward: K, V, Q, dO, P^T / dS^T, then per-warp lse2 / D staging
+constexpr int kBwdSmem = (8 + 4) * kPlane + kSoftWarps * 2 * 64 * 4 + 1024 + 256;
+
+struct FwdArgs {
+  int B, T, H, KV, G, nq;
+  float scale_log2;
+  bf16* o_hi;
+  bf16* o_lo;
+  float* lse2;
+  int* err;
+};
+
+struct BwdArgs {
+  int B, T, H, KV, G, nq;
+  float scale_log2, scale;
+  const float* lse2;
+  const float* Dv;
+  float* dq_part;
+  float* dk_part;
+  float* dv_part;
+  int* err;
+};
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// Byte offset of 16-byte chunk `chunk` (0..7) of row `row` in a swizzled tile.
+__device__ __forceinline__ uint32_t sw_off(int row, int chunk) {
+  return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// (x0, x1) as packed bf16 pairs hi = rn(x), lo = rn(x - hi); x0 in the low half.
+__device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& h, uint32_t& l) {
+  const __nv_bfloat162 hb = __floats2bfloat162_rn(x0, x1);
+  h = reinterpret_cast<const uint32_t&>(hb);
+  const __nv_bfloat162 lb =
+      __floats2bfloat162_rn(x0 - __uint_as_float(h << 16), x1 - __uint_as_float(h & 0xffff0000u));
+  l = reinterpret_cast<const uint32_t&>(lb);
+}
+
+__device__ __forceinline__ void split8(const float (&v)[32], int u, uint4& h, uint4& l) {
+  split_pair(v[8 * u], v[8 * u + 1], h.x, l.x);
+  split_pair(v[8 * u + 2], v[8 * u + 3], h.y, l.y);
+  split_pair(v[8 * u + 4], v[8 * u + 5], h.z, l.z);
+  split_pair(v[8 * u + 6], v[8 * u + 7], h.w, l.w);
+}
+
+// Store 32 values as columns c*32 .. c*32+31 (c = 0, 1) of row `row` of one
+// swizzled [128 x 64] tile per plane (hi tile th, lo tile tl).
+__device__ __forceinline__ void store_row32(uint8_t* th, uint8_t* tl, int row, int c, const float (&v)[32]) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    uint4 h, l;
+    split8(v, u, h, l);
+    const uint32_t off = sw_off(row, c * 4 + u);
+    *reinterpret_cast<uint4*>(th + off) = h;
+    *reinterpret_cast<uint4*>(tl + off) = l;
+  }
+}
+
+// 32 values as planes at 16-byte aligned global addresses.
+__device__ __forceinline__ void store_planes32(bf16* hi, bf16* lo, const float (&v)[32]) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    uint4 h, l;
+    split8(v, u, h, l);
+    reinterpret_cast<uint4*>(hi)[u] = h;
+    reinterpret_cast<uint4*>(lo)[u] = l;
+  }
+}
+
+__device__ __forceinline__ void store_f32x32(float* dst, const float (&v)[32]) {
+  float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+  for (int u = 0; u < 8; ++u) d4[u] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+}
+
+// acc (+)= A * B^T over K = 16 * nsteps with split operands (three UMMAs per
+// k-step). A K-major operand spans K in [128 x 64] tiles kPlane bytes apart; an
+// MN-major operand holds K as rows of 128 bytes, with MN atoms `lbo` bytes apart.
+__device__ __forceinline__ void mma_split(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint32_t a_lbo, bool a_mn,
+                                          uint32_t b_hi, uint32_t b_lo, uint32_t b_lbo, bool b_mn, uint32_t idesc,
+                                          int nsteps, bool accumulate) {
+#pragma unroll 1
+  for (int ks = 0; ks < nsteps; ++ks) {
+    // K-major: 32 B per 16 columns inside a tile, next tile every 4 steps.
+    // MN-major: 16 rows of 128 B per step.
+    const uint32_t ao = a_mn ? (uint32_t)ks * 2048u : (uint32_t)(ks >> 2) * kPlane + (uint32_t)(ks & 3) * 32u;
+    const uint32_t bo = b_mn ? (uint32_t)ks * 2048u : (uint32_t)(ks >> 2) * kPlane + (uint32_t)(ks & 3) * 32u;
+    const uint64_t dah = make_sdesc_sw128(a_hi + ao, a_lbo, 1024), dal = make_sdesc_sw128(a_lo + ao, a_lbo, 1024);
+    const uint64_t dbh = make_sdesc_sw128(b_hi + bo, b_lbo, 1024), dbl = make_sdesc_sw128(b_lo + bo, b_lbo, 1024);
+    umma_f16(d, dah, dbh, idesc, (accumulate || ks > 0) ? 1u : 0u);
+    umma_f16(d, dal, dbh, idesc, 1u);
+    umma_f16(d, dah, dbl, idesc, 1u);
+  }
+}
+
+// Bounded wait by every lane of a warp; the result is warp-uniform.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  const bool ok = mbar_wait(bar, parity, err, code);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// ------------------------------------------------------------------ forward
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_fwd_kernel(const __grid_constant__ CUtensorMap mq_hi, const __grid_constant__ CUtensorMap mq_lo,
+                     const __grid_constant__ CUtensorMap mk_hi, const __grid_constant__ CUtensorMap mk_lo,
+                     const __grid_constant__ CUtensorMap mv_hi, const __grid_constant__ CUtensorMap mv_lo,
+                     const FwdArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sQ = smem;                          // Q hi, Q lo
+  uint8_t* sRing = sQ + 2 * kPlane;            // kRing x (hi, lo) key or value tiles
+  uint8_t* sP = sRing + 2 * kRing * kPlane;    // P hi (2 tiles), P lo (2 tiles)
+  float* xmax = reinterpret_cast<float*>(sP + 4 * kPlane);   // [2][128] per column half
+  float* xsum = xmax + 2 * kTile;                             // [2][128]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(xsum + 2 * kTile);
+  uint64_t* q_full = bar;
+  uint64_t* r_full = bar + 1;
+  uint64_t* r_empty = r_full + kRing;
+  uint64_t* s_full = r_empty + kRing;   // [2]
+  uint64_t* s_empty = s_full + 2;       // [2]
+  uint64_t* p_full = s_empty + 2;
+  uint64_t* p_empty = p_full + 1;
+  uint64_t* o_full = p_empty + 1;
+  uint64_t* mx_done = o_full + 1;    // both halves' row maxima written
+  uint64_t* sum_done = o_full + 2;   // both halves' row sums written
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 3);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int BH = a.B * a.H;
+  const int bh = blockIdx.x % BH;
+  const int qi = a.nq - 1 - blockIdx.x / BH;   // longest query tiles first
+  const int b = bh / a.H, h = bh % a.H;
+  const int bkv = b * a.KV + h / a.G;
+  const int n = qi + 1;                        // key tiles 0 .. qi
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kRing; ++s) {
+      mbar_init(&r_full[s], 1);
+      mbar_init(&r_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], kSoftWarps);
+    }
+    mbar_init(p_full, kSoftWarps);
+    mbar_init(p_empty, 1);
+    mbar_init(o_full, 1);
+    mbar_init(mx_done, kSoftWarps);
+    mbar_init(sum_done, kSoftWarps);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;   // S buffers at columns 0 and 128, O at 256
+  griddep_wait();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    // Ring order: K_0 .. K_{n-1} (pass 1), then K_0 and, for each j,
+    // K_{j+1} (if any) followed by V_j -- the order the MMA issuer consumes.
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, 2 * kPlane);
+      tma_load_3d(sQ, &mq_hi, q_full, 0, qi * kTile, bh);
+      tma_load_3d(sQ + kPlane, &mq_lo, q_full, 0, qi * kTile, bh);
+      uint32_t it = 0;
+      auto push = [&](const CUtensorMap* mh, const CUtensorMap* ml, int j) -> bool {
+        const int s = it % kRing;
+        const uint32_t ph = (it / kRing) & 1;
+        ++it;
+        if (!mbar_wait(&r_empty[s], ph ^ 1, a.err, kErrWaitEmpty)) return false;
+        uint8_t* dst = sRing + s * 2 * kPlane;
+        mbar_arrive_expect_tx(&r_full[s], 2 * kPlane);
+        tma_load_3d(dst, mh, &r_full[s], 0, j * kTile, bkv);
+        tma_load_3d(dst + kPlane, ml, &r_full[s], 0, j * kTile, bkv);
+        return true;
+      };
+      bool ok = true;
+      for (int j = 0; j < n && ok; ++j) ok = push(&mk_hi, &mk_lo, j);
+      if (ok) ok = push(&mk_hi, &mk_lo, 0);
+      for (int j = 0; j < n && ok; ++j) {
+        if (j + 1 < n) ok = push(&mk_hi, &mk_lo, j + 1);
+        if (ok) ok = push(&mv_hi, &mv_lo, j);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t id_s = make_idesc_f16(kTile, kTile, true, false, false);
+      const uint32_t id_o = make_idesc_f16(kTile, kDh, true, false, true);
+      const uint32_t q_hi = smem_u32(sQ), q_lo = q_hi + kPlane;
+      const uint32_t p_hi = smem_u32(sP), p_lo = p_hi + 2 * kPlane;
+      uint32_t it = 0, sc = 0;
+      bool ok = mbar_wait(q_full, 0, a.err, kErrWaitFull);
+      tc_fence_after();
+      // S = Q K^T for the next ring item, into score buffer sc % 2
+      auto issue_s = [&]() -> bool {
+        const int s = it % kRing;
+        const uint32_t ph = (it / kRing) & 1;
+        ++it;
+        const uint32_t sb = sc & 1, sph = (sc >> 1) & 1;
+        ++sc;
+        if (!mbar_wait(&s_empty[sb], sph ^ 1, a.err, kErrWaitAccum)) return false;
+        if (!mbar_wait(&r_full[s], ph, a.err, kErrWaitFull)) return false;
+        tc_fence_after();
+        const uint32_t k_hi = smem_u32(sRing + s * 2 * kPlane), k_lo = k_hi + kPlane;
+        mma_split(tmem + sb * kTile, q_hi, q_lo, 16, false, k_hi, k_lo, 16, false, id_s, kDh / 16, false);
+        umma_commit(&r_empty[s]);
+        umma_commit(&s_full[sb]);
+        return true;
+      };
+      for (int j = 0; j < n && ok; ++j) ok = issue_s();   // pass 1
+      if (ok) ok = issue_s();                             // pass 2, key tile 0
+      for (int j = 0; j < n && ok; ++j) {
+        if (j + 1 < n) ok = issue_s();
+        if (!ok) break;
+        // O += P_j V_j: P K-major over the 128 keys, V MN-major (keys = K rows)
+        const int s = it % kRing;
+        const uint32_t ph = (it / kRing) & 1;
+        ++it;
+        ok = mbar_wait(&r_full[s], ph, a.err, kErrWaitFull) && mbar_wait(p_full, j & 1, a.err, kErrWaitFull);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t v_hi = smem_u32(sRing + s * 2 * kPlane), v_lo = v_hi + kPlane;
+        mma_split(tmem + 2 * kTile, p_hi, p_lo, 16, false, v_hi, v_lo, 2 * kPlane, true, id_o, kTile / 16, j > 0);
+        umma_commit(&r_empty[s]);
+        umma_commit(p_empty);
+      }
+      if (ok) umma_commit(o_full);
+    }
+  } else {
+    // -------------------------------------------------------- softmax warps
+    const int sw = warp - 2;
+    const int qw = warp & 3;     // TMEM lane quarter this warp may access
+    const int half = sw >> 2;    // score columns half * 64 .. half * 64 + 63
+    const int row = qw * 32 + lane;
+    const int qrow = qi * kTile + row;
+    const uint32_t lanes = (uint32_t)(qw * 32) << 16;
+    uint32_t sc = 0;
+    bool ok = true;
+    // pass 1: maximum raw score over the live keys (k <= q, k < T); only the
+    // diagonal tile (and a ragged last tile, which is the diagonal) needs the mask
+    float m = -INFINITY;
+    for (int j = 0; j < n && ok; ++j, ++sc) {
+      const uint32_t sb = sc & 1, sph = (sc >> 1) & 1;
+      ok = warp_wait(&s_full[sb], sph, a.err, kErrWaitAccum);
+      tc_fence_after();
+      if (ok) {
+        const bool mask = j == qi;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          float v[32];
+          tmem_ld32(tmem + lanes + sb * kTile + half * 64 + c * 32, v);
+          const int k0 = j * kTile + half * 64 + c * 32;
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (!mask || (k0 + e <= qrow && k0 + e < a.T)) m = fmaxf(m, v[e]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[sb]);
+    }
+    xmax[half * kTile + row] = m;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(mx_done);
+    ok = ok && warp_wait(mx_done, 0, a.err, kErrWaitAccum);
+    // p = exp2(S * scale_log2 - mb): scale_log2 > 0, so the scaled maximum is mb
+    const float mb = fmaxf(xmax[row], xmax[kTile + row]) * a.scale_log2;
+    // pass 2: unnormalised P = exp2(S * scale_log2 - mb) into shared memory (this
+    // half's 64 keys are one K-major tile), row sums in registers
+    float l = 0.f;
+    uint8_t* th = sP + half * kPlane;
+    uint8_t* tl = sP + (2 + half) * kPlane;
+    for (int j = 0; j < n && ok; ++j, ++sc) {
+      const uint32_t sb = sc & 1, sph = (sc >> 1) & 1;
+      ok = warp_wait(&s_full[sb], sph, a.err, kErrWaitAccum) &&
+           warp_wait(p_empty, (j & 1) ^ 1, a.err, kErrWaitAccum);
+      tc_fence_after();
+      if (ok) {
+        const bool mask = j == qi;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          float v[32];
+          tmem_ld32(tmem + lanes + sb * kTile + half * 64 + c * 32, v);
+          const int k0 = j * kTile + half * 64 + c * 32;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            float p = ex2(fmaf(v[e], a.scale_log2, -mb));
+            if (mask && !(k0 + e <= qrow && k0 + e < a.T)) p = 0.f;
+            v[e] = p;
+            l += p;
+          }
+          store_row32(th, tl, row, c, v);
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&s_empty[sb]);
+        mbar_arrive(p_full);
+      }
+    }
+    xsum[half * kTile + row] = l;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(sum_done);
+    ok = ok && warp_wait(sum_done, 0, a.err, kErrWaitAccum) && warp_wait(o_full, 0, a.err, kErrWaitAccum);
+    tc_fence_after();
+    if (ok) {
+      // this half's 32 of the 64 output columns, divided by the row sum
+      const float lt = xsum[row] + xsum[kTile + row];
+      const float inv = lt > 0.f ? 1.0f / lt : 0.f;
+      float o[32];
+      tmem_ld32(tmem + lanes + 2 * kTile + half * 32, o);
+#pragma unroll
+      for (int e = 0; e < 32; ++e) o[e] *= inv;
+      if (qrow < a.T) {
+        const long long off = ((long long)(b * a.T + qrow) * a.H + h) * kDh + half * 32;
+        store_planes32(a.o_hi + off, a.o_lo + off, o);
+        if (half == 0) a.lse2[(long long)bh * a.T + qrow] = mb + log2f(lt);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------ backward
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_bwd_kernel(const __grid_constant__ CUtensorMap mq_hi, const __grid_constant__ CUtensorMap mq_lo,
+                     const __grid_constant__ CUtensorMap mk_hi, const __grid_constant__ CUtensorMap mk_lo,
+                     const __grid_constant__ CUtensorMap mv_hi, const __grid_constant__ CUtensorMap mv_lo,
+                     const __grid_constant__ CUtensorMap mo_hi, const __grid_constant__ CUtensorMap mo_lo,
+                     const BwdArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sK = smem;                  // K hi, lo
+  uint8_t* sV = sK + 2 * kPlane;       // V hi, lo
+  uint8_t* sQ = sV + 2 * kPlane;       // Q_i hi, lo
+  uint8_t* sO = sQ + 2 * kPlane;       // dO_i hi, lo
+  uint8_t* sP = sO + 2 * kPlane;       // P^T then dS^T: hi (2 tiles), lo (2 tiles)
+  float* s_vec = reinterpret_cast<float*>(sP + 4 * kPlane);   // per softmax warp: lse2[64], D[64]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(s_vec + kSoftWarps * 2 * 64);
+  uint64_t* kv_full = bar;
+  uint64_t* q_full = bar + 1;
+  uint64_t* q_empty = bar + 2;
+  uint64_t* o_full = bar + 3;
+  uint64_t* o_empty = bar + 4;
+  uint64_t* sdp_full = bar + 5;
+  uint64_t* sdp_empty = bar + 6;
+  uint64_t* p_full = bar + 7;
+  uint64_t* p_used = bar + 8;
+  uint64_t* ds_full = bar + 9;
+  uint64_t* ds_used = bar + 10;
+  uint64_t* dq_full = bar + 11;    // [2]
+  uint64_t* dq_empty = bar + 13;   // [2]
+  uint64_t* acc_full = bar + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 16);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int BH = a.B * a.H;
+  const int bh = blockIdx.x % BH;
+  const int j = blockIdx.x / BH;       // key tile; j = 0 has the most query tiles
+  const int b = bh / a.H, h = bh % a.H;
+  const int bkv = b * a.KV + h / a.G;
+  const int n_it = a.nq - j;           // query tiles i = j .. nq - 1
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    mbar_init(o_full, 1);
+    mbar_init(o_empty, 1);
+    mbar_init(sdp_full, 1);
+    mbar_init(sdp_empty, kSoftWarps);
+    mbar_init(p_full, kSoftWarps);
+    mbar_init(p_used, 1);
+    mbar_init(ds_full, kSoftWarps);
+    mbar_init(ds_used, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&dq_full[s], 1);
+      mbar_init(&dq_empty[s], kSoftWarps);
+    }
+    mbar_init(acc_full, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  // TMEM columns: S^T 0, dP^T 128, dV 256, dK 320, dQ buffers 384 and 448
+  const uint32_t tmem = *tmem_slot;
+  griddep_wait();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(kv_full, 4 * kPlane);
+      tma_load_3d(sK, &mk_hi, kv_full, 0, j * kTile, bkv);
+      tma_load_3d(sK + kPlane, &mk_lo, kv_full, 0, j * kTile, bkv);
+      tma_load_3d(sV, &mv_hi, kv_full, 0, j * kTile, bkv);
+      tma_load_3d(sV + kPlane, &mv_lo, kv_full, 0, j * kTile, bkv);
+      for (int it = 0; it < n_it; ++it) {
+        const int i = j + it;
+        const uint32_t ph = (it & 1) ^ 1;
+        if (!mbar_wait(q_empty, ph, a.err, kErrWaitEmpty)) break;
+        mbar_arrive_expect_tx(q_full, 2 * kPlane);
+        tma_load_3d(sQ, &mq_hi, q_full, 0, i * kTile, bh);
+        tma_load_3d(sQ + kPlane, &mq_lo, q_full, 0, i * kTile, bh);
+        if (!mbar_wait(o_empty, ph, a.err, kErrWaitEmpty)) break;
+        mbar_arrive_expect_tx(o_full, 2 * kPlane);
+        tma_load_3d(sO, &mo_hi, o_full, 0, i * kTile, bh);
+        tma_load_3d(sO + kPlane, &mo_lo, o_full, 0, i * kTile, bh);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t id_s = make_idesc_f16(kTile, kTile, true, false, false);
+      const uint32_t id_kv = make_idesc_f16(kTile, kDh, true, false, true);   // dV, dK: B (dO, Q) MN-major
+      const uint32_t id_q = make_idesc_f16(kTile, kDh, true, true, true);     // dQ: A (dS) and B (K) MN-major
+      const uint32_t k_hi = smem_u32(sK), k_lo = k_hi + kPlane;
+      const uint32_t v_hi = smem_u32(sV), v_lo = v_hi + kPlane;
+      const uint32_t q_hi = smem_u32(sQ), q_lo = q_hi + kPlane;
+      const uint32_t o_hi = smem_u32(sO), o_lo = o_hi + kPlane;
+      const uint32_t p_hi = smem_u32(sP), p_lo = p_hi + 2 * kPlane;
+      bool ok = mbar_wait(kv_full, 0, a.err, kErrWaitFull);
+      for (int it = 0; it < n_it && ok; ++it) {
+        const uint32_t ph = it & 1;
+        // dO_i arrives first (its slot frees after dV), so dP^T goes before S^T
+        ok = mbar_wait(o_full, ph, a.err, kErrWaitFull) && mbar_wait(sdp_empty, ph ^ 1, a.err, kErrWaitAccum);
+        if (!ok) break;
+        tc_fence_after();
+        mma_split(tmem + kTile, v_hi, v_lo, 16, false, o_hi, o_lo, 16, false, id_s, kDh / 16, false);   // dP^T
+        ok = mbar_wait(q_full, ph, a.err, kErrWaitFull);
+        if (!ok) break;
+        tc_fence_after();
+        mma_split(tmem, k_hi, k_lo, 16, false, q_hi, q_lo, 16, false, id_s, kDh / 16, false);           // S^T
+        umma_commit(sdp_full);
+        ok = mbar_wait(p_full, ph, a.err, kErrWaitFull);
+        if (!ok) break;
+        tc_fence_after();
+        // dV += P^T dO   (K = the 128 queries)
+        mma_split(tmem + 2 * kTile, p_hi, p_lo, 16, false, o_hi, o_lo, 2 * kPlane, true, id_kv, kTile / 16,
+                  it > 0);
+        umma_commit(p_used);
+        umma_commit(o_empty);
+        ok = mbar_wait(ds_full, ph, a.err, kErrWaitFull) &&
+             mbar_wait(&dq_empty[it & 1], ((it >> 1) & 1) ^ 1, a.err, kErrWaitAccum);
+        if (!ok) break;
+        tc_fence_after();
+        // dK += dS^T Q; the Q slot then takes the next query tile during dQ
+        mma_split(tmem + 2 * kTile + kDh, p_hi, p_lo, 16, false, q_hi, q_lo, 2 * kPlane, true, id_kv, kTile / 16,
+                  it > 0);
+        umma_commit(q_empty);
+        // dQ_i = dS K: dS^T read MN-major (query atoms 64 wide, one tile apart), K MN-major
+        mma_split(tmem + 2 * kTile + 2 * kDh + (it & 1) * kDh, p_hi, p_lo, kPlane, true, k_hi, k_lo, 2 * kPlane,
+                  true, id_q, kTile / 16, false);
+        umma_commit(ds_used);
+        umma_commit(&dq_full[it & 1]);
+      }
+      if (ok) umma_commit(acc_full);
+    }
+  } else {
+    // -------------------------------------------------------- softmax warps
+    const int sw = warp - 2;
+    const int qw = warp & 3;     // TMEM lane quarter
+    const int half = sw >> 2;    // query columns half * 64 .. half * 64 + 63 of the tile
+    const int row = qw * 32 + lane;
+    const int key = j * kTile + row;
+    const uint32_t lanes = (uint32_t)(qw * 32) << 16;
+    float* vec = s_vec + sw * 128;   // this warp's lse2[64] and D[64]
+    uint8_t* th = sP + half * kPlane;
+    uint8_t* tl = sP + (2 + half) * kPlane;
+    bool ok = true;
+    // dQ partial of iteration it: TMEM rows are the queries of tile j + it
+    auto dq_out = [&](int it) {
+      ok = ok && warp_wait(&dq_full[it & 1], (it >> 1) & 1, a.err, kErrWaitAccum);
+      tc_fence_after();
+      if (!ok) return;
+      float v[32];
+      tmem_ld32(tmem + lanes + 2 * kTile + 2 * kDh + (it & 1) * kDh + half * 32, v);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&dq_empty[it & 1]);
+      const int q = (j + it) * kTile + row;
+      if (q < a.T) store_f32x32(a.dq_part + (((long long)j * a.B * a.H + bh) * a.T + q) * kDh + half * 32, v);
+    };
+    for (int it = 0; it < n_it && ok; ++it) {
+      const int i = j + it;
+      const uint32_t ph = it & 1;
+      __syncwarp();
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int c = lane + 32 * u, q = i * kTile + half * 64 + c;
+        vec[c] = q < a.T ? a.lse2[(long long)bh * a.T + q] : INFINITY;
+        vec[64 + c] = q < a.T ? a.Dv[(long long)bh * a.T + q] : 0.f;
+      }
+      __syncwarp();
+      ok = warp_wait(sdp_full, ph, a.err, kErrWaitAccum) && warp_wait(ds_used, ph ^ 1, a.err, kErrWaitAccum);
+      tc_fence_after();
+      if (ok) {
+        // P^T[key, q] = exp2(S^T * scale_log2 - lse2[q]) for live q >= key, and
+        // dS^T = P^T (dP^T - D[q]) * scale parked in the S^T columns
+        const bool mask = i == j || (i + 1) * kTile > a.T;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          float sv[32], dp[32];
+          const uint32_t col = half * 64 + c * 32;
+          tmem_ld32(tmem + lanes + col, sv);
+          tmem_ld32(tmem + lanes + kTile + col, dp);
+          const float4* l4 = reinterpret_cast<const float4*>(vec + c * 32);
+          const float4* d4 = reinterpret_cast<const float4*>(vec + 64 + c * 32);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const float4 L = l4[u], D = d4[u];
+            const float lv[4] = {L.x, L.y, L.z, L.w}, dv[4] = {D.x, D.y, D.z, D.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int e = 4 * u + k;
+              float p = ex2(fmaf(sv[e], a.scale_log2, -lv[k]));
+              if (mask) {
+                const int q = i * kTile + (int)col + e;
+                if (!(q >= key && q < a.T)) p = 0.f;
+              }
+              dp[e] = p * (dp[e] - dv[k]) * a.scale;
+              sv[e] = p;
+            }
+          }
+          store_row32(th, tl, row, c, sv);
+          tmem_st32(tmem + lanes + col, dp);
+        }
+        tmem_wait_st();
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      if (it > 0) dq_out(it - 1);   // overlaps the dV UMMAs
+      ok = ok && warp_wait(p_used, ph, a.err, kErrWaitAccum);
+      tc_fence_after();
+      if (ok) {
+        // the P^T buffer is free: dS^T into it
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          float v[32];
+          tmem_ld32(tmem + lanes + half * 64 + c * 32, v);
+          store_row32(th, tl, row, c, v);
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(sdp_empty);
+        mbar_arrive(ds_full);
+      }
+    }
+    if (ok && n_it > 0) dq_out(n_it - 1);
+    ok = ok && warp_wait(acc_full, 0, a.err, kErrWaitAccum);
+    tc_fence_after();
+    if (ok) {
+      const int g = h % a.G;
+      const long long off = (((long long)g * a.B * a.KV + bkv) * a.T + key) * kDh + half * 32;
+#pragma unroll 1
+      for (int which = 0; which < 2; ++which) {   // 0: dV, 1: dK
+        float v[32];
+        tmem_ld32(tmem + lanes + 2 * kTile + which * kDh + half * 32, v);
+        if (key < a.T) store_f32x32((which ? a.dk_part : a.dv_part) + off, v);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// dO planes (head-major) and D = rowsum(dO * O); one warp per (b, h, t) row.
+__global__ void __launch_bounds__(256) flash_bwd_prep_kernel(const float* __restrict__ dO32, Planes O, Planes dO,
+                                                             float* __restrict__ Dv, int B, int T, int H) {
+  griddep_wait();
+  const int warps = blockDim.x / 32, lane = threadIdx.x % 32;
+  const long long rows = (long long)B * H * T;
+  for (long long r = blockIdx.x * (long long)warps + threadIdx.x / 32; r < rows; r += (long long)gridDim.x * warps) {
+    const int t = (int)(r % T);
+    const long long bh = r / T;
+    const int b = (int)(bh / H), h = (int)(bh % H);
+    const float2 g = reinterpret_cast<const float2*>(dO32 + r * kDh)[lane];
+    const long long oo = ((long long)(b * T + t) * H + h) * kDh + 2 * lane;
+    const float o0 = __bfloat162float(O.hi[oo]) + __bfloat162float(O.lo[oo]);
+    const float o1 = __bfloat162float(O.hi[oo + 1]) + __bfloat162float(O.lo[oo + 1]);
+    float d = g.x * o0 + g.y * o1;
+#pragma unroll
+    for (int s = 16; s; s >>= 1) d += __shfl_xor_sync(0xffffffffu, d, s);
+    const bf16 h0 = __float2bfloat16_rn(g.x), h1 = __float2bfloat16_rn(g.y);
+    __nv_bfloat162 hv, lv;
+    hv.x = h0;
+    hv.y = h1;
+    lv.x = __float2bfloat16_rn(g.x - __bfloat162float(h0));
+    lv.y = __float2bfloat16_rn(g.y - __bfloat162float(h1));
+    reinterpret_cast<__nv_bfloat162*>(dO.hi + r * kDh)[lane] = hv;
+    reinterpret_cast<__nv_bfloat162*>(dO.lo + r * kDh)[lane] = lv;
+    if (lane == 0) Dv[r] = d;
+  }
+}
+
+Operand head_operand(const bf16* hi, const bf16* lo, int T, int nbatch) {
+  Operand o;
+  o.hi = hi; o.lo = lo; o.mn_major = 0; o.ld = kDh; o.rows = T; o.cols = kDh;
+  o.batch_stride = (long long)T * kDh; o.nbatch = nbatch;
+  return o;
+}
+
+int maps_for(CUtensorMap* m, Planes p, int T, int nbatch) {
+  const Operand o = head_operand(p.hi, p.lo, T, nbatch);
+  int rc = make_plane_map(&m[0], p.hi, o, kTile);
+  if (!rc) rc = make_plane_map(&m[1], p.lo, o, kTile);
+  return rc;
+}
+
+bool shape_ok(int B, int T, int H, int KV, int dh) {
+  return B > 0 && T > 0 && H > 0 && KV > 0 && H % KV == 0 && dh == kDh;
+}
+
+}  // namespace
+
+bool flash_supported(int dh) { return dh == kDh; }
+
+int launch_flash_fwd(Planes Q, Planes K, Planes V, Planes O, float* lse2, int B, int T, int H, int KV, int dh,
+                     float scale, int* err, cudaStream_t st) {
+  if (!shape_ok(B, T, H, KV, dh)) return -1;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem) != cudaSuccess)
+      return -20;
+    attr = true;
+  }
+  CUtensorMap mq[2], mk[2], mv[2];
+  int rc;
+  if ((rc = maps_for(mq, Q, T, B * H)) || (rc = maps_for(mk, K, T, B * KV)) || (rc = maps_for(mv, V, T, B * KV)))
+    return rc;
+  FwdArgs a;
+  a.B = B; a.T = T; a.H = H; a.KV = KV; a.G = H / KV; a.nq = (T + kTile - 1) / kTile;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.o_hi = O.hi; a.o_lo = O.lo; a.lse2 = lse2; a.err = err;
+  const long long grid = (long long)a.nq * B * H;
+  if (grid > 0x7fffffffLL) return -5;
+  return launch_pdl(flash_fwd_kernel, dim3((unsigned)grid), dim3(kThreads), kFwdSmem, st, mq[0], mq[1], mk[0], mk[1],
+                    mv[0], mv[1], a) ? -21 : 0;
+}
+
+int launch_flash_bwd_prep(const float* dO32, Planes O, Planes dO, float* Dvec, int B, int T, int H, int dh,
+                          cudaStream_t st) {
+  if (dh != kDh) return -1;
+  const long long rows = (long long)B * H * T;
+  long long blocks = (rows + 7) / 8;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  return launch_pdl(flash_bwd_prep_kernel, dim3((unsigned)blocks), dim3(256), 0, st, dO32, O, dO, Dvec, B, T, H)
+             ? -21 : 0;
+}
+
+long long flash_bwd_ws_floats(int B, int T, int H, int KV, int dh) {
+  const long long nq = (T + kTile - 1) / kTile;
+  const long long G = KV > 0 ? H / KV : 0;
+  return nq * B * H * T * dh + 2 * G * B * KV * T * dh;
+}
+
+int launch_flash_bwd(Planes Q, Planes K, Planes V, Planes dO, const float* lse2, const float* Dvec, float* ws, int B,
+                     int T, int H, int KV, int dh, float scale, int* err, cudaStream_t st) {
+  if (!shape_ok(B, T, H, KV, dh)) return -1;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(flash_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem) != cudaSuccess)
+      return -20;
+    attr = true;
+  }
+  CUtensorMap mq[2], mk[2], mv[2], mo[2];
+  int rc;
+  if ((rc = maps_for(mq, Q, T, B * H)) || (rc = maps_for(mk, K, T, B * KV)) || (rc = maps_for(mv, V, T, B * KV)) ||
+      (rc = maps_for(mo, dO, T, B * H)))
+    return rc;
+  BwdArgs a;
+  a.B = B; a.T = T; a.H = H; a.KV = KV; a.G = H / KV; a.nq = (T + kTile - 1) / kTile;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.scale = scale;
+  a.lse2 = lse2; a.Dv = Dvec;
+  a.dq_part = ws;
+  a.dk_part = ws + (long long)a.nq * B * H * T * kDh;
+  a.dv_part = a.dk_part + (long long)a.G * B * KV * T * kDh;
+  a.err = err;
+  const long long grid = (long long)a.nq * B * H;
+  if (grid > 0x7fffffffLL) return -5;
+  return launch_pdl(flash_bwd_kernel, dim3((unsigned)grid), dim3(kThreads), kBwdSmem, st, mq[0], mq[1], mk[0], mk[1],
+                    mv[0], mv[1], mo[0], mo[1], a) ? -21 : 0;
+}
+
+int launch_flash_rope_bwd(const float* ws, const int* pos, const float* cs_tab, int tab_rows, Planes dqkv,
+                          float* dqkv_f32, int B, int T, int H, int KV, int dh, cudaStream_t st) {
+  if (!shape_ok(B, T, H, KV, dh)) return -1;
+  const long long nq = (T + kTile - 1) / kTile;
+  const long long qs = (long long)B * H * T * kDh, kvs = (long long)B * KV * T * kDh;
+  const int G = H / KV;
+  const float* dk = ws + nq * qs;
+  const float* dv = dk + G * kvs;
+  return launch_rope_qkv_bwd_sum(ws, qs, kTile, dk, dv, kvs, G, pos, cs_tab, tab_rows, dqkv, dqkv_f32, B, T, H, KV, dh,
+                                 st);
+}
+
+}  // namespace tb2

@@ -537,6 +537,10 @@ int pick_bn(int N) {
 
 }  // namespace
 
+int make_plane_map(CUtensorMap* map, const __nv_bfloat16* base, const Operand& o, int box_rows) {
+  return make_map(map, base, o, box_rows);
+}
+
 int gemm_launch(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream_t stream) {
   if (d.M <= 0 || d.N <= 0 || d.K <= 0 || d.batch <= 0) return -1;
   if (d.causal < 0 || d.causal > 2) return -1;

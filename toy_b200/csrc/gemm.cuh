@@ -9,6 +9,7 @@
 // hold gradients within 1e-3 relative L2 of an fp64 evaluation. Without `split`
 // the lo planes are ignored (one UMMA per k-step, plain bf16).
 #pragma once
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
@@ -85,6 +86,11 @@ struct GemmScratch {
 // shape/alignment (nothing launched). `dev_err` is a device int the kernel sets
 // to a DeviceError code if one of its bounded waits gives up.
 int gemm_launch(const GemmDesc& d, const GemmScratch& scratch, int* dev_err, cudaStream_t stream);
+
+// TMA map over one bf16 plane laid out as `o` describes: dims {cols, rows,
+// nbatch}, box {64, box_rows, 1}, 128-byte swizzle. Rows past `rows` inside a
+// batch read as zero. Returns 0 or a negative alignment / driver error.
+int make_plane_map(CUtensorMap* map, const __nv_bfloat16* base, const Operand& o, int box_rows);
 
 // Row-major helpers used by the step program.
 inline Operand op_rowmajor(const __nv_bfloat16* hi, const __nv_bfloat16* lo, int rows, int cols, long long ld,

@@ -291,8 +291,13 @@ __global__ void __launch_bounds__(256) rope_qkv_fwd_kernel(const float* __restri
   }
 }
 
-__global__ void __launch_bounds__(256) rope_qkv_bwd_kernel(const float* __restrict__ dQ, const float* __restrict__ dK,
-                                                           const float* __restrict__ dV, const int* __restrict__ pos,
+// dQ / dK / dV may each be a sum of partial arrays: dQ of token t is the sum of
+// parts p <= t / q_tile (q_tile = 0: one part), p * q_pstride apart; dK and dV
+// are sums of kv_parts parts, kv_pstride apart. Parts are added in index order.
+__global__ void __launch_bounds__(256) rope_qkv_bwd_kernel(const float* __restrict__ dQ, long long q_pstride,
+                                                           int q_tile, const float* __restrict__ dK,
+                                                           const float* __restrict__ dV, long long kv_pstride,
+                                                           int kv_parts, const int* __restrict__ pos,
                                                            const float2* __restrict__ cs, int tab_rows, Planes out,
                                                            float* out_f32, int N, int T, int H, int KV, int dh) {
   griddep_wait();
@@ -304,6 +309,7 @@ __global__ void __launch_bounds__(256) rope_qkv_bwd_kernel(const float* __restri
     int p = pos[n];
     p = p < 0 ? 0 : (p >= tab_rows ? tab_rows - 1 : p);
     const float2* crow = cs + (long long)p * half;
+    const int q_parts = q_tile > 0 ? t / q_tile + 1 : 1;
     for (int i = threadIdx.x; i < slots * half; i += blockDim.x) {
       const int slot = i / half, j = i - slot * half;
       float y0, y1;
@@ -312,15 +318,25 @@ __global__ void __launch_bounds__(256) rope_qkv_bwd_kernel(const float* __restri
         const int hh = isq ? slot : slot - H;
         const float* srcb = isq ? dQ : dK;
         const long long src = (((long long)b * (isq ? H : KV) + hh) * T + t) * dh + j;
-        const float g0 = srcb[src], g1 = srcb[src + half];
+        const int parts = isq ? q_parts : kv_parts;
+        const long long pstride = isq ? q_pstride : kv_pstride;
+        float g0 = 0.f, g1 = 0.f;
+        for (int q = 0; q < parts; ++q) {
+          g0 += srcb[src + q * pstride];
+          g1 += srcb[src + q * pstride + half];
+        }
         const float2 c = crow[j];
         y0 = g0 * c.x + g1 * c.y;
         y1 = -g0 * c.y + g1 * c.x;
       } else {
         const int hh = slot - H - KV;
         const long long src = (((long long)b * KV + hh) * T + t) * dh + j;
-        y0 = dV[src];
-        y1 = dV[src + half];
+        y0 = 0.f;
+        y1 = 0.f;
+        for (int q = 0; q < kv_parts; ++q) {
+          y0 += dV[src + q * kv_pstride];
+          y1 += dV[src + q * kv_pstride + half];
+        }
       }
       const long long dst = (long long)n * width + slot * dh + j;
       store_planes(out, dst, y0);
@@ -808,9 +824,17 @@ int launch_rope_qkv_fwd(const float* qkv, const float* bias, const int* pos, con
 int launch_rope_qkv_bwd(const float* dQ, const float* dK, const float* dV, const int* pos, const float* cs_tab,
                         int tab_rows, Planes dqkv, float* dqkv_f32, int B, int T, int H, int KV, int dh,
                         cudaStream_t st) {
+  return launch_rope_qkv_bwd_sum(dQ, 0, 0, dK, dV, 0, 1, pos, cs_tab, tab_rows, dqkv, dqkv_f32, B, T, H, KV, dh, st);
+}
+
+int launch_rope_qkv_bwd_sum(const float* dQ, long long q_pstride, int q_tile, const float* dK, const float* dV,
+                            long long kv_pstride, int kv_parts, const int* pos, const float* cs_tab, int tab_rows,
+                            Planes dqkv, float* dqkv_f32, int B, int T, int H, int KV, int dh, cudaStream_t st) {
   const int N = B * T;
-  launch_pdl(rope_qkv_bwd_kernel, dim3(N < 8 * kSMs ? N : 8 * kSMs), dim3(256), 0, st,
-      dQ, dK, dV, pos, reinterpret_cast<const float2*>(cs_tab), tab_rows, dqkv, dqkv_f32, N, T, H, KV, dh);
+  if (q_tile < 0 || kv_parts < 1) return -1;
+  launch_pdl(rope_qkv_bwd_kernel, dim3(N < 8 * kSMs ? N : 8 * kSMs), dim3(256), 0, st, dQ, q_pstride, q_tile, dK, dV,
+             kv_pstride, kv_parts, pos, reinterpret_cast<const float2*>(cs_tab), tab_rows, dqkv, dqkv_f32, N, T, H,
+             KV, dh);
   return ok();
 }
 

@@ -48,6 +48,12 @@ int launch_rope_qkv_fwd(const float* qkv, const float* bias, const int* pos, con
 int launch_rope_qkv_bwd(const float* dQ, const float* dK, const float* dV, const int* pos, const float* cs_tab,
                         int tab_rows, Planes dqkv, float* dqkv_f32, int B, int T, int H, int KV, int dh,
                         cudaStream_t st);
+// Same, with dQ / dK / dV given as sums of partial arrays added in index order:
+// dQ of position t sums parts 0 .. t / q_tile (q_tile = 0: one part), q_pstride
+// floats apart; dK and dV sum kv_parts parts, kv_pstride floats apart.
+int launch_rope_qkv_bwd_sum(const float* dQ, long long q_pstride, int q_tile, const float* dK, const float* dV,
+                            long long kv_pstride, int kv_parts, const int* pos, const float* cs_tab, int tab_rows,
+                            Planes dqkv, float* dqkv_f32, int B, int T, int H, int KV, int dh, cudaStream_t st);
 
 // P = softmax(S) over keys k <= q (rows of [Z][T][T]); masked entries 0.
 int launch_softmax_causal_fwd(const float* S, Planes P, long long Z, int T, cudaStream_t st);

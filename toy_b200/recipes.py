@@ -66,6 +66,9 @@ class RecipeOptions:
     qkv_bias: bool = False
     seed: int = 42
     init_scale: float = 1.0
+    # attention core: "flash" (fused kernels, d_head 64; other widths use the
+    # materialised path) or "materialized" (score GEMM + softmax + PV GEMM)
+    attention: str = "flash"
 
 
 @dataclass
@@ -111,6 +114,9 @@ class LlamaSeqEngine:
         c.tied = 0 if (opts.untied or not cfg.tied) else 1
         c.qkv_bias = 1 if (opts.qkv_bias or cfg.qkv_bias) else 0
         c.t_seq, c.t_batch, c.mode = opts.t_seq, opts.t_batch, mode
+        if opts.attention not in ("flash", "materialized"):
+            raise ValueError(f"unknown attention implementation {opts.attention!r}")
+        c.attn_impl = 0 if opts.attention == "flash" else 1
         if lora is not None:
             c.lora_rank, c.lora_alpha = lora.rank, lora.alpha
             c.lora_targets = sum(LORA_BITS[t] for t in lora.targets)
