@@ -223,9 +223,16 @@ long long tb2_debug_activation(void *sess, int which, int layer, float *dst, lon
  * through any host channel; every rank then calls tb2_dp_init on its realized
  * session. From then on each step all-reduces the trainable gradients (sum,
  * NCCL over NVLink) before AdamW, which scales them by 1/world, so every
- * replica takes the identical update of the global-batch mean gradient. */
+ * replica takes the identical update of the global-batch mean gradient.
+ * The reduction runs in buckets on a second stream while the backward goes on:
+ * as soon as the finished gradients (the backward completes them from the last
+ * layer down) reach the bucket size, they are all-reduced; the rest follows
+ * the backward. */
 int tb2_nccl_unique_id(void *out, size_t nbytes);
 int tb2_dp_init(void *sess, const void *unique_id, int rank, int world);
+/* Bucket size in floats (default 2^20); every rank must use the same value.
+ * Takes effect at the next step (the step graph is re-captured). */
+int tb2_dp_set_bucket_floats(void *sess, long long floats);
 /* Releases the step graph (which holds NCCL work) and then the communicator. */
 int tb2_dp_free(void *sess);
 

@@ -1,5 +1,7 @@
 """Data-parallel step on 2 GPUs (NCCL all-reduce inside the library) equals the
-single-GPU step on the joined batch. Needs two B200s; skipped on one."""
+single-GPU step on the joined batch, with the gradients reduced in one bucket
+after the backward and in per-layer buckets overlapped with it. Needs two
+B200s; skipped on one."""
 import os
 import socket
 
@@ -26,7 +28,7 @@ def _cfgs():
     return oc, LlamaConfig(512, 128, 4, 2, 32, 256, 2, 1e4, 1e-5)
 
 
-def _rank(rank, world, port, q):
+def _rank(rank, world, port, q, bucket):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -37,7 +39,7 @@ def _rank(rank, world, port, q):
     dp = DataParallel(rank, world, rank, timeout_s=120)
     rec = FromScratch(device=rank)
     rec.realize(gc, RecipeOptions(t_seq=T, t_batch=1, seed=3))
-    dp.attach(rec.fs_cache)
+    dp.attach(rec.fs_cache, bucket_floats=bucket)
     ids = O.token_ids(5, 2 * T, oc.vocab)
     lab = O.next_token_labels(ids, T, 2, oc.vocab)
     sl = slice(rank * T, (rank + 1) * T)
@@ -48,14 +50,15 @@ def _rank(rank, world, port, q):
     rec.fs_cache.close()
 
 
-def test_dp2_matches_joined_batch(cuda):
+@pytest.mark.parametrize("bucket", [None, 4096])
+def test_dp2_matches_joined_batch(cuda, bucket):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=_rank, args=(r, 2, port, q, bucket)) for r in range(2)]
     for p in ps:
         p.start()
     res = sorted((q.get(timeout=300) for _ in range(2)), key=lambda r: r[0])

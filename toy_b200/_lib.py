@@ -68,6 +68,7 @@ _SIGS = [
     ("tb2_nccl_unique_id", I, [VP, SZ]),
     ("tb2_dp_init", I, [VP, VP, I, I]),
     ("tb2_dp_free", I, [VP]),
+    ("tb2_dp_set_bucket_floats", I, [VP, LL]),
     ("tb2_profile_step", I, [VP, I, C.POINTER(C.c_int), C.POINTER(C.c_float), C.POINTER(C.c_double), I]),
     ("tnn_graph_reset", I, [VP]),
     ("tnn_graph_reset_grads_only", I, [VP]),

@@ -76,6 +76,14 @@ int tb2_dp_init(void* sess, const void* unique_id, int rank, int world) {
   return 0;
 }
 
+int tb2_dp_set_bucket_floats(void* sess, long long floats) {
+  if (!sess || floats < 1) return -1;
+  Session* s = static_cast<Session*>(sess);
+  if (!s->eng) return -2;
+  s->eng->set_bucket_floats(floats);
+  return 0;
+}
+
 int tb2_dp_free(void* sess) {
   if (!sess) return -1;
   tb2::dp_free(static_cast<Session*>(sess));

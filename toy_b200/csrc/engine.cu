@@ -2,6 +2,7 @@
 #include "engine.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -113,7 +114,63 @@ LlamaEngine::~LlamaEngine() {
   for (auto& b : bufs_)
     if (b.p) cudaFree(b.p);
   if (stage_) cudaFreeHost(stage_);
+  for (cudaEvent_t e : bucket_ev_) cudaEventDestroy(e);
+  if (comm_stream_) cudaStreamDestroy(comm_stream_);
   if (stream_) cudaStreamDestroy(stream_);
+}
+
+// ---------------------------------------------------------------- gradient buckets
+int LlamaEngine::bucket_begin() {
+  bucket_next_ = 0;
+  pend_lo_ = pend_hi_ = n_train_;
+  comm_used_ = false;
+  if (!allreduce_fn_ || profiling_) return 0;
+  if (!comm_stream_) CU(cudaStreamCreateWithFlags(&comm_stream_, cudaStreamNonBlocking));
+  return 0;
+}
+
+// Trainable gradients at arena offsets >= lo are final. With flush (or once the
+// pending range reaches bucket_floats_) the pending range is all-reduced: on
+// comm_stream_ after an event on the step stream, or, in a profiled step, on
+// the step stream itself. Every rank runs the same bucket sequence.
+int LlamaEngine::bucket_ready(long long lo, bool flush) {
+  if (!allreduce_fn_) return 0;
+  pend_lo_ = std::min(pend_lo_, lo);
+  if (pend_hi_ <= pend_lo_ || (!flush && pend_hi_ - pend_lo_ < bucket_floats_)) return 0;
+  float* buf = grad_arena() + pend_lo_;
+  const long long n = pend_hi_ - pend_lo_;
+  pend_hi_ = pend_lo_;
+  if (profiling_) {
+    prof_begin(kKAllreduce, 0.0);
+    const int rc = allreduce_fn_(allreduce_ctx_, buf, n, stream_);
+    prof_end();
+    return rc;
+  }
+  if (bucket_next_ == bucket_ev_.size()) {
+    cudaEvent_t e;
+    CU(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    bucket_ev_.push_back(e);
+  }
+  cudaEvent_t e = bucket_ev_[bucket_next_++];
+  CU(cudaEventRecord(e, stream_));
+  CU(cudaStreamWaitEvent(comm_stream_, e, 0));
+  comm_used_ = true;
+  return allreduce_fn_(allreduce_ctx_, buf, n, comm_stream_);
+}
+
+// The step stream waits for every bucket before the optimiser.
+int LlamaEngine::bucket_join() {
+  if (!comm_used_) return 0;
+  if (bucket_next_ == bucket_ev_.size()) {
+    cudaEvent_t e;
+    CU(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    bucket_ev_.push_back(e);
+  }
+  cudaEvent_t e = bucket_ev_[bucket_next_++];
+  CU(cudaEventRecord(e, comm_stream_));
+  CU(cudaStreamWaitEvent(stream_, e, 0));
+  comm_used_ = false;
+  return 0;
 }
 
 int LlamaEngine::alloc(DeviceBuf& b, size_t bytes) {
@@ -210,6 +267,12 @@ int LlamaEngine::realize() {
   }
   n_total_ = off;
   q8_bytes_ = qoff;
+  layer_grad_lo_.assign(c.n_layers, n_train_);
+  for (const auto& p : params_) {
+    if (!p.trainable || p.name.compare(0, 4, "blk.") != 0) continue;
+    const int l = std::atoi(p.name.c_str() + 4);
+    if (l >= 0 && l < c.n_layers) layer_grad_lo_[l] = std::min(layer_grad_lo_[l], p.offset);
+  }
   // fused operands must be contiguous
   for (int l = 0; l < c.n_layers; ++l) {
     const std::string pre = "blk." + std::to_string(l) + ".";
@@ -948,18 +1011,15 @@ int LlamaEngine::enqueue_backward() {
     const Param& g1 = P(pre + "attn_norm.weight");
     KL(launch_rmsnorm_bwd(x_[l], dh_, P32(g1), dx_, dx_, dxp_, gpart_, nblk, N, d, c.rms_eps, stream_));
     if (full) KL(launch_colsum(gpart_, nblk, d, G32(g1), 0, stream_));
+    CK(bucket_ready(layer_grad_lo_[l], false));   // this layer's gradients are final
   }
   if (full) KL(launch_embed_scatter(dx_, ord_, seg_start_, seg_id_, nseg_dev_, N, G32(E), d, stream_));
+  CK(bucket_ready(0, true));
+  CK(bucket_join());
   return 0;
 }
 
 int LlamaEngine::enqueue_optimizer() {
-  if (allreduce_fn_) {
-    if (profiling_) prof_begin(kKAllreduce, 0.0);
-    const int rc = allreduce_fn_(allreduce_ctx_, grad_arena(), n_train_, stream_);
-    if (profiling_) prof_end();
-    CK(rc);
-  }
   Planes pp{static_cast<bf16*>(phi_.p), static_cast<bf16*>(plo_.p)};
   KL(launch_adamw(static_cast<float*>(p32_.p), static_cast<float*>(g_.p), static_cast<float*>(m_.p),
                   static_cast<float*>(v_.p), pp, n_train_, hp_, grad_scale_, stream_));
@@ -968,6 +1028,7 @@ int LlamaEngine::enqueue_optimizer() {
 
 int LlamaEngine::enqueue_step(bool run_optimizer) {
   counting_ = 0;
+  CK(bucket_begin());
   CK(enqueue_forward());
   CK(enqueue_backward());
   if (run_optimizer) CK(enqueue_optimizer());

@@ -93,6 +93,10 @@ class LlamaEngine {
     graph_valid_ = false;
   }
   void set_use_graph(bool on) { use_graph_ = on; graph_valid_ = false; }
+  void set_bucket_floats(long long n) {
+    bucket_floats_ = n;
+    graph_valid_ = false;
+  }
   void drop_graph() {
     if (graph_) cudaGraphExecDestroy(graph_);
     graph_ = nullptr;
@@ -165,6 +169,20 @@ class LlamaEngine {
   float grad_scale_ = 1.0f;
   int (*allreduce_fn_)(void*, float*, long long, cudaStream_t) = nullptr;
   void* allreduce_ctx_ = nullptr;
+  // Gradient buckets: the backward finalises the arena from the top down (layer
+  // L-1 first); every range of at least bucket_floats_ finished floats is reduced
+  // on comm_stream_ while the backward continues, the rest after the backward.
+  // bucket_floats_ is the minimum bucket size.
+  long long bucket_floats_ = 1LL << 20;
+  cudaStream_t comm_stream_ = nullptr;
+  std::vector<cudaEvent_t> bucket_ev_;
+  size_t bucket_next_ = 0;
+  long long pend_lo_ = 0, pend_hi_ = 0;   // finished, not yet reduced: [pend_lo_, pend_hi_)
+  std::vector<long long> layer_grad_lo_;  // lowest arena offset of each layer's trainable gradients
+  bool comm_used_ = false;
+  int bucket_begin();
+  int bucket_ready(long long lo, bool flush);
+  int bucket_join();
   bool use_graph_ = true;
   cudaGraphExec_t graph_ = nullptr;
   bool graph_valid_ = false;

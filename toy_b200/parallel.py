@@ -10,6 +10,7 @@ from __future__ import annotations
 import ctypes as C
 import datetime
 import os
+from typing import Optional
 
 from ._lib import check, lib
 
@@ -41,8 +42,9 @@ class DataParallel:
         dist.broadcast(t, src=0)
         return bytes(t.numpy().tobytes())
 
-    def attach(self, eng) -> None:
-        """Join the engine's session to the NCCL communicator of all ranks."""
+    def attach(self, eng, bucket_floats: Optional[int] = None) -> None:
+        """Join the engine's session to the NCCL communicator of all ranks;
+        gradients are reduced in buckets of at least bucket_floats floats."""
         L = lib()
         uid = None
         if self.rank == 0:
@@ -54,6 +56,8 @@ class DataParallel:
         uid = self.exchange_uid(uid)
         ubuf = (C.c_ubyte * UID_BYTES).from_buffer_copy(uid)
         check(L.tb2_dp_init(eng.sess, C.cast(ubuf, C.c_void_p), self.rank, self.world), "tb2_dp_init")
+        if bucket_floats is not None:
+            check(L.tb2_dp_set_bucket_floats(eng.sess, int(bucket_floats)), "tb2_dp_set_bucket_floats")
         self.sess = eng.sess
 
     def barrier(self) -> None:
