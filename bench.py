@@ -31,7 +31,8 @@ sys.path.insert(0, ROOT)
 
 METRIC = "train tokens/sec (fwd+bwd+AdamW) at 1/2/4/8 B200; % of step roofline"
 KIND_NAMES = ["gemm", "rmsnorm_fwd", "rmsnorm_bwd", "colsum", "rope", "softmax", "swiglu", "cross_entropy",
-              "loss_reduce", "adamw", "embedding", "split", "allreduce", "flash_fwd", "flash_bwd", "flash_prep"]
+              "loss_reduce", "adamw", "embedding", "split", "allreduce", "flash_fwd", "flash_bwd", "flash_prep",
+              "lora"]
 
 WORKLOADS = {
     "smollm2_full_ft_b8_t512": dict(mode=0, B=8, T=512, lora=None, lr=1e-4, wd=0.01),

@@ -45,6 +45,13 @@ typedef struct tb2_operand {
   long long batch_stride;
   int nbatch;
   int bdiv1, bmul1, bdiv2, bmul2;
+  /* Q8_0 B operand of a non-batched split GEMM (NULL otherwise; hi / lo are
+   * then unused): int8 quants of the stored [rows][cols] matrix, row stride ld
+   * bytes, and the fp16 scale bits [rows][cols / 32] -- Q8_0 blocks (ggml
+   * block_q8_0) with the scales split off. Tiles are dequantised in shared
+   * memory, never in HBM. */
+  const void *q8;
+  const void *q8_scale;
 } tb2_operand;
 
 /* Epilogue: mode 0 store f32, 1 accumulate f32, 2 residual (out = res + acc),

@@ -15,7 +15,8 @@ LIB_PATH = os.path.join(_HERE, "libtoyb200.so")
 class Operand(C.Structure):
     _fields_ = [("hi", C.c_void_p), ("lo", C.c_void_p), ("mn_major", C.c_int), ("ld", C.c_longlong),
                 ("rows", C.c_int), ("cols", C.c_int), ("batch_stride", C.c_longlong), ("nbatch", C.c_int),
-                ("bdiv1", C.c_int), ("bmul1", C.c_int), ("bdiv2", C.c_int), ("bmul2", C.c_int)]
+                ("bdiv1", C.c_int), ("bmul1", C.c_int), ("bdiv2", C.c_int), ("bmul2", C.c_int),
+                ("q8", C.c_void_p), ("q8_scale", C.c_void_p)]
 
 
 class Epilogue(C.Structure):

@@ -19,6 +19,8 @@ tb2::Operand to_op(const tb2_operand* o) {
   r.bmul1 = o->bmul1;
   r.bdiv2 = o->bdiv2 > 0 ? o->bdiv2 : 1;
   r.bmul2 = o->bmul2;
+  r.q8 = static_cast<const int8_t*>(o->q8);
+  r.q8_scale = static_cast<const uint16_t*>(o->q8_scale);
   return r;
 }
 }  // namespace

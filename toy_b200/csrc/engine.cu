@@ -9,6 +9,7 @@
 #include <thread>
 
 #include "flash_attn.cuh"
+#include "lora.cuh"
 #include "runtime.cuh"
 
 namespace tb2 {
@@ -109,7 +110,7 @@ LlamaEngine::LlamaEngine(const LlamaConfig& cfg, int device) : cfg_(cfg), device
 LlamaEngine::~LlamaEngine() {
   cudaSetDevice(device_);
   if (graph_) cudaGraphExecDestroy(graph_);
-  for (DeviceBuf* b : {&p32_, &phi_, &plo_, &g_, &m_, &v_, &q8_})
+  for (DeviceBuf* b : {&p32_, &phi_, &plo_, &g_, &m_, &v_, &q8_, &q8v_, &q8s_})
     if (b->p) cudaFree(b->p);
   for (auto& b : bufs_)
     if (b.p) cudaFree(b.p);
@@ -207,7 +208,7 @@ int LlamaEngine::realize() {
   // the materialised score path tiles T x T matrices in 64-wide blocks; the
   // fused attention masks ragged tiles and takes any T
   if (c.T % 64 && !(c.attn_impl == 0 && flash_supported(c.d_head))) return -1;
-  if (c.mode == 1 && (c.lora_rank <= 0 || c.lora_rank % 8 || c.lora_targets == 0)) return -1;
+  if (c.mode == 1 && (c.lora_rank <= 0 || c.lora_rank > kLoraMaxRank || c.lora_targets == 0)) return -1;
   CU(cudaSetDevice(device_));
   CU(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
   err_ = device_error_word();
@@ -254,16 +255,23 @@ int LlamaEngine::realize() {
     if (!c.tied) add_param("output.weight", V, d, false, false);
     add_param("output_norm.weight", 1, d, false, false);
   }
-  long long off = 0, qoff = 0;
+  long long off = 0, qoff = 0, qvoff = 0, qsoff = 0;
   for (auto& p : params_) {
     if (p.trainable && off != n_train_) return -1;
+    if (p.q8) {
+      // frozen Q8_0 projection: only the blocks and their quant / scale split
+      p.offset = -1;
+      p.q8_offset = qoff;
+      qoff += p.numel() / 32 * 34;
+      p.q8v_offset = qvoff;
+      qvoff += p.numel();
+      p.q8s_offset = qsoff;
+      qsoff += p.numel() / 32;
+      continue;
+    }
     p.offset = off;
     off += (p.numel() + 63) / 64 * 64;
     if (p.trainable) n_train_ = off;
-    if (p.q8) {
-      p.q8_offset = qoff;
-      qoff += p.numel() / 32 * 34;
-    }
   }
   n_total_ = off;
   q8_bytes_ = qoff;
@@ -274,11 +282,15 @@ int LlamaEngine::realize() {
     if (l >= 0 && l < c.n_layers) layer_grad_lo_[l] = std::min(layer_grad_lo_[l], p.offset);
   }
   // fused operands must be contiguous
+  auto follows = [](const Param& a, const Param& b) {   // b stored right after a
+    return a.q8 ? (b.q8v_offset == a.q8v_offset + a.numel() && b.q8s_offset == a.q8s_offset + a.numel() / 32)
+                : b.offset == a.offset + a.numel();
+  };
   for (int l = 0; l < c.n_layers; ++l) {
     const std::string pre = "blk." + std::to_string(l) + ".";
-    if (P(pre + "attn_k.weight").offset != P(pre + "attn_q.weight").offset + (long long)H * dh * d) return -1;
-    if (P(pre + "attn_v.weight").offset != P(pre + "attn_k.weight").offset + (long long)KV * dh * d) return -1;
-    if (P(pre + "ffn_up.weight").offset != P(pre + "ffn_gate.weight").offset + (long long)ff * d) return -1;
+    if (!follows(P(pre + "attn_q.weight"), P(pre + "attn_k.weight"))) return -1;
+    if (!follows(P(pre + "attn_k.weight"), P(pre + "attn_v.weight"))) return -1;
+    if (!follows(P(pre + "ffn_gate.weight"), P(pre + "ffn_up.weight"))) return -1;
   }
   CK(alloc(p32_, n_total_ * 4));
   CK(alloc(phi_, n_total_ * 2));
@@ -286,7 +298,11 @@ int LlamaEngine::realize() {
   CK(alloc(g_, std::max<long long>(n_train_, 64) * 4));
   CK(alloc(m_, std::max<long long>(n_train_, 64) * 4));
   CK(alloc(v_, std::max<long long>(n_train_, 64) * 4));
-  if (q8_bytes_) CK(alloc(q8_, q8_bytes_));
+  if (q8_bytes_) {
+    CK(alloc(q8_, q8_bytes_));
+    CK(alloc(q8v_, qvoff));
+    CK(alloc(q8s_, qsoff * 2));
+  }
 
   const int N = this->N(), T = c.T, B = c.B, W = (H + 2 * KV) * dh;
   auto f32 = [&](long long n) -> float* {
@@ -305,6 +321,7 @@ int LlamaEngine::realize() {
   flash_ = c.attn_impl == 0 && flash_supported(dh);
   for (int l = 0; l <= c.n_layers; ++l) x_.push_back(f32((long long)N * d));
   lora_u_.resize(c.n_layers);
+  lora_bt_.resize(c.n_layers);
   for (int l = 0; l < c.n_layers; ++l) {
     x1_.push_back(f32((long long)N * d));
     gu_.push_back(f32((long long)N * 2 * ff));
@@ -317,9 +334,13 @@ int LlamaEngine::realize() {
     Pm_.push_back(flash_ ? Planes{} : pl(att));
     lse2_.push_back(flash_ ? f32((long long)B * H * T) : nullptr);
     O_.push_back(pl((long long)N * H * dh));
-    lora_u_[l].resize(kLoraCount);
+    lora_u_[l].assign(kLoraCount, nullptr);
+    lora_bt_[l].assign(kLoraCount, nullptr);
     for (int t = 0; t < kLoraCount; ++t)
-      if (!full && (c.lora_targets & (1 << t))) lora_u_[l][t] = pl((long long)N * r);
+      if (!full && (c.lora_targets & (1 << t))) {
+        lora_u_[l][t] = f32((long long)N * r);
+        lora_bt_[l][t] = f32((long long)r * std::max(std::max(d, ff), H * dh));
+      }
   }
   qkv_ = f32((long long)N * W);
   if (!flash_) S_ = f32(att);
@@ -347,9 +368,8 @@ int LlamaEngine::realize() {
   if (!flash_) dS_ = pl(att);
   dqkv_ = pl((long long)N * W);
   if (!full) {
-    u32_ = f32((long long)N * r);
     du32_ = f32((long long)N * r);
-    du_ = pl((long long)N * r);
+    lora_part_ = f32(lora_wgrad_partial_floats(N, std::max(std::max(d, ff), H * dh), r));
   }
   hp_ = f32(8);
   bufs_.emplace_back();
@@ -419,16 +439,35 @@ int LlamaEngine::set_param(const std::string& name, const float* host, long long
   // Stream-ordered copy: a plain cudaMemcpy from pageable memory may return
   // before its DMA lands, and stream_ does not order against the legacy stream.
   CU(cudaStreamSynchronize(stream_));
-  CU(cudaMemcpyAsync(P32(*p), host, n * 4, cudaMemcpyHostToDevice, stream_));
   if (p->q8) {
-    CK(launch_q8_0_quantize(P32(*p), static_cast<uint8_t*>(q8_.p) + p->q8_offset, p->rows, p->cols, stream_));
-    CK(launch_q8_0_to_planes(static_cast<uint8_t*>(q8_.p) + p->q8_offset, PP(*p), P32(*p), p->rows, p->cols,
-                             stream_));
-  } else {
-    CK(refresh_planes(*p));
+    // quantise through a temporary f32 copy; only the Q8_0 data is kept
+    float* tmp = nullptr;
+    CU(cudaMalloc(&tmp, n * 4));
+    int rc = cudaMemcpyAsync(tmp, host, n * 4, cudaMemcpyHostToDevice, stream_) == cudaSuccess ? 0 : -3;
+    if (!rc) rc = launch_q8_0_quantize(tmp, static_cast<uint8_t*>(q8_.p) + p->q8_offset, p->rows, p->cols, stream_);
+    if (!rc) rc = split_q8(*p);
+    if (cudaStreamSynchronize(stream_) != cudaSuccess && !rc) rc = -3;
+    cudaFree(tmp);
+    return rc;
   }
+  CU(cudaMemcpyAsync(P32(*p), host, n * 4, cudaMemcpyHostToDevice, stream_));
+  CK(refresh_planes(*p));
   CU(cudaStreamSynchronize(stream_));
   return 0;
+}
+
+int LlamaEngine::split_q8(const Param& p) {
+  return launch_q8_0_split(static_cast<const uint8_t*>(q8_.p) + p.q8_offset,
+                           static_cast<int8_t*>(q8v_.p) + p.q8v_offset,
+                           static_cast<uint16_t*>(q8s_.p) + p.q8s_offset, p.numel() / 32, stream_);
+}
+
+Operand LlamaEngine::wop(const Param& p, int rows, int cols, long long ld, int mn) {
+  if (!p.q8) return op(PP(p), rows, cols, ld, mn);
+  Operand o = op(Planes{}, rows, cols, ld, mn);
+  o.q8 = static_cast<const int8_t*>(q8v_.p) + p.q8v_offset;
+  o.q8_scale = static_cast<const uint16_t*>(q8s_.p) + p.q8s_offset;
+  return o;
 }
 
 int LlamaEngine::set_param_q8(const std::string& name, const uint8_t* blocks, long long nbytes) {
@@ -437,7 +476,7 @@ int LlamaEngine::set_param_q8(const std::string& name, const uint8_t* blocks, lo
   CU(cudaStreamSynchronize(stream_));
   uint8_t* dst = static_cast<uint8_t*>(q8_.p) + p->q8_offset;
   CU(cudaMemcpyAsync(dst, blocks, nbytes, cudaMemcpyHostToDevice, stream_));
-  CK(launch_q8_0_to_planes(dst, PP(*p), P32(*p), p->rows, p->cols, stream_));
+  CK(split_q8(*p));
   CU(cudaStreamSynchronize(stream_));
   return 0;
 }
@@ -454,6 +493,18 @@ int LlamaEngine::get_param(const std::string& name, float* host, long long n) {
   const Param* p = find(name);
   if (!p || !host || n != p->numel()) return -1;
   CU(cudaStreamSynchronize(stream_));
+  if (p->q8) {   // dequantise the blocks on the host: value = fp16 scale * int8 quant
+    std::vector<uint8_t> blk((size_t)(n / 32 * 34));
+    CU(cudaMemcpy(blk.data(), static_cast<uint8_t*>(q8_.p) + p->q8_offset, blk.size(), cudaMemcpyDeviceToHost));
+    for (long long b = 0; b < n / 32; ++b) {
+      const uint8_t* q = blk.data() + b * 34;
+      __half_raw hr;
+      hr.x = (unsigned short)(q[0] | (q[1] << 8));
+      const float dsc = __half2float(__half(hr));
+      for (int j = 0; j < 32; ++j) host[b * 32 + j] = dsc * (float)(int8_t)q[2 + j];
+    }
+    return 0;
+  }
   CU(cudaMemcpy(host, P32(*p), n * 4, cudaMemcpyDeviceToHost));
   return 0;
 }
@@ -678,7 +729,7 @@ int kind_of(const char* call) {
       {"launch_adamw", LlamaEngine::kKAdamw},        {"launch_embed", LlamaEngine::kKEmbed},
       {"launch_split", LlamaEngine::kKSplit},        {"launch_flash_fwd", LlamaEngine::kKFlashFwd},
       {"launch_flash_bwd_prep", LlamaEngine::kKFlashPrep}, {"launch_flash_bwd", LlamaEngine::kKFlashBwd},
-      {"launch_flash_rope", LlamaEngine::kKRope}};
+      {"launch_flash_rope", LlamaEngine::kKRope},   {"launch_lora", LlamaEngine::kKLora}};
   for (const auto& t : table)
     if (strncmp(call, t.prefix, strlen(t.prefix)) == 0) return t.kind;
   return LlamaEngine::kKCount;
@@ -703,19 +754,14 @@ int LlamaEngine::lora_forward(int l, int t, Planes X, int d_in, float* Y, long l
   const std::string pre = "blk." + std::to_string(l) + "." + kProjName[t];
   const Param& A = P(pre + ".lora_a");
   const Param& Bp = P(pre + ".lora_b");
-  Planes u = lora_u_[l][t];
-  GemmDesc g1;
-  g1.M = N; g1.N = r; g1.K = d_in;
-  g1.a = op(X, N, d_in, d_in, 0);
-  g1.b = op(PP(A), r, d_in, d_in, 0);
-  g1.epi.mode = kEpiStoreSplit; g1.epi.out_hi = u.hi; g1.epi.out_lo = u.lo; g1.epi.m_s0 = r;
-  CK(gemm(g1));
-  GemmDesc g2;
-  g2.M = N; g2.N = d_out; g2.K = r;
-  g2.a = op(u, N, r, r, 0);
-  g2.b = op(PP(Bp), d_out, r, r, 0);
-  g2.epi = epi_rowmajor(kEpiAccumF32, Y + col_off, ldy, c.lora_alpha / (float)r);
-  return gemm(g2);
+  float* u = lora_u_[l][t];
+  float* bt = lora_bt_[l][t];
+  // u = X A^T [N][r]; Y[:, col_off ..] += s * u B^T (B^T kept for the backward)
+  KL(launch_lora_transpose(P32(Bp), d_out, r, bt, stream_));
+  KL(launch_lora_down(X, d_in, N, d_in, P32(A), r, 1.0f, u, stream_));
+  KL(launch_lora_up(u, N, r, bt, d_out, c.lora_alpha / (float)r, epi_rowmajor(kEpiAccumF32, Y + col_off, ldy),
+                    stream_));
+  return 0;
 }
 
 // Gradients of the adapter on projection (l, t): dB, dA into the gradient
@@ -728,41 +774,19 @@ int LlamaEngine::lora_backward(int l, int t, Planes X, int d_in, Planes dY, long
   const std::string pre = "blk." + std::to_string(l) + "." + kProjName[t];
   const Param& A = P(pre + ".lora_a");
   const Param& Bp = P(pre + ".lora_b");
-  Planes u = lora_u_[l][t];
+  const float* u = lora_u_[l][t];
+  const float* bt = lora_bt_[l][t];
   Planes dYo = offset(dY, col_off);
   // dB = s * dY^T u   [d_out][r]
-  GemmDesc g3;
-  g3.M = d_out; g3.N = r; g3.K = N;
-  g3.a = op(dYo, N, d_out, ld_dy, 1);
-  g3.b = op(u, N, r, r, 1);
-  g3.epi = epi_rowmajor(kEpiStoreF32, G32(Bp), r, s);
-  CK(gemm(g3));
+  KL(launch_lora_wgrad(dYo, ld_dy, u, N, d_out, r, s, G32(Bp), r, 1, lora_part_, stream_));
   // du = s * dY B   [N][r]
-  GemmDesc g4;
-  g4.M = N; g4.N = r; g4.K = d_out;
-  g4.a = op(dYo, N, d_out, ld_dy, 0);
-  g4.b = op(PP(Bp), d_out, r, r, 1);
-  g4.epi.mode = kEpiStoreSplit; g4.epi.alpha = s; g4.epi.out_hi = du_.hi; g4.epi.out_lo = du_.lo; g4.epi.m_s0 = r;
-  CK(gemm(g4));
+  KL(launch_lora_down(dYo, ld_dy, N, d_out, bt, r, s, du32_, stream_));
   // dA = du^T X   [r][d_in]
-  GemmDesc g5;
-  g5.M = r; g5.N = d_in; g5.K = N;
-  g5.a = op(du_, N, r, r, 1);
-  g5.b = op(X, N, d_in, d_in, 1);
-  g5.epi = epi_rowmajor(kEpiStoreF32, G32(A), d_in);
-  CK(gemm(g5));
+  KL(launch_lora_wgrad(X, d_in, du32_, N, d_in, r, 1.0f, G32(A), 1, d_in, lora_part_, stream_));
   // dX += du A   [N][d_in]
-  GemmDesc g6;
-  g6.M = N; g6.N = d_in; g6.K = r;
-  g6.a = op(du_, N, r, r, 0);
-  g6.b = op(PP(A), r, d_in, d_in, 1);
-  if (dx_scatter) {
-    g6.epi = *dx_scatter;
-    g6.epi.mode = kEpiAccumF32;
-  } else {
-    g6.epi = epi_rowmajor(kEpiAccumF32, dX, d_in);
-  }
-  return gemm(g6);
+  Epilogue e = dx_scatter ? *dx_scatter : epi_rowmajor(kEpiAccumF32, dX, d_in);
+  KL(launch_lora_up(du32_, N, r, P32(A), d_in, 1.0f, e, stream_));
+  return 0;
 }
 
 int LlamaEngine::enqueue_forward() {
@@ -779,7 +803,7 @@ int LlamaEngine::enqueue_forward() {
     GemmDesc g;
     g.M = N; g.N = W; g.K = d;
     g.a = op(h1_[l], N, d, d, 0);
-    g.b = op(PP(P(pre + "attn_q.weight")), W, d, d, 0);
+    g.b = wop(P(pre + "attn_q.weight"), W, d, d, 0);
     g.epi = epi_rowmajor(kEpiStoreF32, qkv_, W);
     CK(gemm(g));
     if (lora) {
@@ -817,7 +841,7 @@ int LlamaEngine::enqueue_forward() {
     GemmDesc gw;
     gw.M = N; gw.N = d; gw.K = H * dh;
     gw.a = op(O_[l], N, H * dh, H * dh, 0);
-    gw.b = op(PP(P(pre + "attn_output.weight")), d, H * dh, H * dh, 0);
+    gw.b = wop(P(pre + "attn_output.weight"), d, H * dh, H * dh, 0);
     gw.epi = epi_rowmajor(kEpiResidF32, x1_[l], d);
     gw.epi.res = x_[l];
     CK(gemm(gw));
@@ -826,7 +850,7 @@ int LlamaEngine::enqueue_forward() {
     GemmDesc gg;
     gg.M = N; gg.N = 2 * ff; gg.K = d;
     gg.a = op(h2_[l], N, d, d, 0);
-    gg.b = op(PP(P(pre + "ffn_gate.weight")), 2 * ff, d, d, 0);
+    gg.b = wop(P(pre + "ffn_gate.weight"), 2 * ff, d, d, 0);
     gg.epi = epi_rowmajor(kEpiStoreF32, gu_[l], 2 * ff);
     CK(gemm(gg));
     if (lora && (c.lora_targets & (1 << kLoraGate))) CK(lora_forward(l, kLoraGate, h2_[l], d, gu_[l], 2 * ff, 0, ff));
@@ -835,7 +859,7 @@ int LlamaEngine::enqueue_forward() {
     GemmDesc gd;
     gd.M = N; gd.N = d; gd.K = ff;
     gd.a = op(a_[l], N, ff, ff, 0);
-    gd.b = op(PP(P(pre + "ffn_down.weight")), d, ff, ff, 0);
+    gd.b = wop(P(pre + "ffn_down.weight"), d, ff, ff, 0);
     gd.epi = epi_rowmajor(kEpiResidF32, x_[l + 1], d);
     gd.epi.res = x1_[l];
     CK(gemm(gd));
@@ -891,7 +915,7 @@ int LlamaEngine::enqueue_backward() {
     GemmDesc gda;
     gda.M = N; gda.N = ff; gda.K = d;
     gda.a = op(dxp_, N, d, d, 0);
-    gda.b = op(PP(Wd), d, ff, ff, 1);
+    gda.b = wop(Wd, d, ff, ff, 1);
     gda.epi = epi_rowmajor(kEpiStoreF32, da_, ff);
     CK(gemm(gda));
     if (full) {
@@ -908,7 +932,7 @@ int LlamaEngine::enqueue_backward() {
     GemmDesc gh;
     gh.M = N; gh.N = d; gh.K = 2 * ff;
     gh.a = op(dgu_, N, 2 * ff, 2 * ff, 0);
-    gh.b = op(PP(Wg), 2 * ff, d, d, 1);
+    gh.b = wop(Wg, 2 * ff, d, d, 1);
     gh.epi = epi_rowmajor(kEpiStoreF32, dh_, d);
     CK(gemm(gh));
     if (full) {
@@ -933,7 +957,7 @@ int LlamaEngine::enqueue_backward() {
     GemmDesc gdo;
     gdo.M = N; gdo.N = H * dh; gdo.K = d;
     gdo.a = op(dxp_, N, d, d, 0);
-    gdo.b = op(PP(Wo), d, H * dh, H * dh, 1);
+    gdo.b = wop(Wo, d, H * dh, H * dh, 1);
     gdo.epi = hm;
     CK(gemm(gdo));
     if (full) {
@@ -991,7 +1015,7 @@ int LlamaEngine::enqueue_backward() {
     GemmDesc gx;
     gx.M = N; gx.N = d; gx.K = W;
     gx.a = op(dqkv_, N, W, W, 0);
-    gx.b = op(PP(Wq), W, d, d, 1);
+    gx.b = wop(Wq, W, d, d, 1);
     gx.epi = epi_rowmajor(kEpiStoreF32, dh_, d);
     CK(gemm(gx));
     if (full) {

@@ -35,8 +35,10 @@ struct Param {
   long long offset = 0;   // element offset in the arenas
   int rows = 1, cols = 1; // row-major [rows][cols]
   bool trainable = false;
-  bool q8 = false;        // frozen projection stored as Q8_0 blocks
-  long long q8_offset = 0;
+  bool q8 = false;        // frozen projection stored as Q8_0 (no f32 / plane copy: offset unused)
+  long long q8_offset = 0;   // bytes into q8_ (the blocks as uploaded)
+  long long q8v_offset = 0;  // bytes into q8v_ (int8 quants, row-major)
+  long long q8s_offset = 0;  // elements into q8s_ (fp16 scale bits, one per 32 quants)
   long long numel() const { return (long long)rows * cols; }
 };
 
@@ -112,7 +114,7 @@ class LlamaEngine {
   // an event pair around every launch; fills per-launch kind, duration and
   // algorithmic FLOPs (GEMMs), returns the launch count.
   enum Kind : int { kKGemm = 0, kKRmsFwd, kKRmsBwd, kKColsum, kKRope, kKSoftmax, kKSwiglu, kKCe, kKLoss, kKAdamw,
-                    kKEmbed, kKSplit, kKAllreduce, kKFlashFwd, kKFlashBwd, kKFlashPrep, kKCount };
+                    kKEmbed, kKSplit, kKAllreduce, kKFlashFwd, kKFlashBwd, kKFlashPrep, kKLora, kKCount };
   int run_steps(int n, float* ms);
   int profile_step(bool is_first, int* kinds, float* ms, double* flops, int cap);
 
@@ -132,8 +134,12 @@ class LlamaEngine {
   Planes PP(const Param& p) {
     return Planes{static_cast<bf16*>(phi_.p) + p.offset, static_cast<bf16*>(plo_.p) + p.offset};
   }
+  // GEMM operand over a weight (and, for fused operands, the weights stored
+  // after it): split planes, or the quants + scales of a Q8_0 projection.
+  Operand wop(const Param& p, int rows, int cols, long long ld, int mn);
   const Param& P(const std::string& n) const;
   int refresh_planes(const Param& p);
+  int split_q8(const Param& p);   // blocks -> quants + scales
 
   LlamaConfig cfg_;
   int device_ = 0;
@@ -143,7 +149,7 @@ class LlamaEngine {
   std::map<std::string, int> pidx_;
   long long n_train_ = 0, n_total_ = 0, q8_bytes_ = 0;
   // arenas
-  DeviceBuf p32_, phi_, plo_, g_, m_, v_, q8_;
+  DeviceBuf p32_, phi_, plo_, g_, m_, v_, q8_, q8v_, q8s_;
   // activations and scratch
   std::vector<DeviceBuf> bufs_;
   std::vector<float*> x_, x1_, gu_;
@@ -151,11 +157,13 @@ class LlamaEngine {
   bool flash_ = false;             // attention core on the fused flash kernels
   std::vector<float*> lse2_;       // flash: per-layer softmax normalisers [B][H][T]
   float *dvec_ = nullptr, *fws_ = nullptr;   // flash backward: D and partial-gradient workspace
-  std::vector<std::vector<Planes>> lora_u_;   // [layer][target]
+  std::vector<std::vector<float*>> lora_u_;    // [layer][target] u = X A^T, f32 [N][r]
+  std::vector<std::vector<float*>> lora_bt_;   // [layer][target] B^T, f32 [r][d_out] (this step's B)
+  float* lora_part_ = nullptr;                 // weight-gradient partial sums
   float *qkv_ = nullptr, *S_ = nullptr, *logits_ = nullptr, *loss_rows_ = nullptr, *loss_ = nullptr;
   float *dx_ = nullptr, *dh_ = nullptr, *da_ = nullptr, *dO32_ = nullptr, *dQ_ = nullptr, *dK_ = nullptr,
-        *dV_ = nullptr, *gpart_ = nullptr, *u32_ = nullptr, *du32_ = nullptr;
-  Planes xf_, dlog_, dxp_, dgu_, dO_, dS_, dqkv_, up_tmp_, du_;
+        *dV_ = nullptr, *gpart_ = nullptr, *du32_ = nullptr;
+  Planes xf_, dlog_, dxp_, dgu_, dO_, dS_, dqkv_, up_tmp_;
   // inputs
   int *ids_ = nullptr, *pos_ = nullptr, *labels_ = nullptr, *ord_ = nullptr, *seg_start_ = nullptr,
       *seg_id_ = nullptr, *nseg_dev_ = nullptr;

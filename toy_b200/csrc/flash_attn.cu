@@ -80,28 +80,10 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-// Byte offset of 16-byte chunk `chunk` (0..7) of row `row` in a swizzled tile.
-__device__ __forceinline__ uint32_t sw_off(int row, int chunk) {
-  return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
-}
-
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// (x0, x1) as packed bf16 pairs hi = rn(x), lo = rn(x - hi); x0 in the low half.
-__device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& h, uint32_t& l) {
-  const __nv_bfloat162 hb = __floats2bfloat162_rn(x0, x1);
-  h = reinterpret_cast<const uint32_t&>(hb);
-  const __nv_bfloat162 lb =
-      __floats2bfloat162_rn(x0 - __uint_as_float(h << 16), x1 - __uint_as_float(h & 0xffff0000u));
-  l = reinterpret_cast<const uint32_t&>(lb);
 }
 
 __device__ __forceinline__ void split8(const float (&v)[32], int u, uint4& h, uint4& l) {
@@ -159,12 +141,6 @@ __device__ __forceinline__ void mma_split(uint32_t d, uint32_t a_hi, uint32_t a_
     umma_f16(d, dal, dbh, idesc, 1u);
     umma_f16(d, dah, dbl, idesc, 1u);
   }
-}
-
-// Bounded wait by every lane of a warp; the result is warp-uniform.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
-  const bool ok = mbar_wait(bar, parity, err, code);
-  return __all_sync(0xffffffffu, ok);
 }
 
 // ------------------------------------------------------------------ forward

@@ -32,9 +32,15 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;          // one 128-byte swizzle atom of bf16 along K
-constexpr int kThreads = 192;
+constexpr int kThreads = 192;   // producer, MMA issuer, 4 epilogue warps
+constexpr int kConvWarps = 8;   // Q8_0 B operand: warps 6.. dequantise into the B tiles
 constexpr int kSmemBudget = 200 * 1024;
 constexpr int kNumSMs = 148;
+
+template <bool Q8>
+constexpr int threads_of() {
+  return Q8 ? kThreads + 32 * kConvWarps : kThreads;
+}
 
 struct KArgs {
   int M, N, K, batch;
@@ -46,6 +52,8 @@ struct KArgs {
   float* ws;
   int* sem;
   int* err;
+  const uint16_t* q8_scale;   // Q8_0 B operand: scales and stored extent
+  int q8_rows, q8_cols;
 };
 
 __device__ __forceinline__ int batch_index(int z, int d1, int m1, int d2, int m2) {
@@ -60,10 +68,16 @@ struct Cfg {
   static constexpr uint32_t kTmemCols = 2 * kAccCols;                           // double buffered
 };
 
-template <int BN, bool SPLIT>
+// A stage holds the A and B plane tiles and, for a Q8_0 B operand, the int8
+// quant tile the converters read (BN rows x 64 bytes, or BN / 64 blocks of
+// 64 x 64 bytes when B is MN-major). TMA fills A and the quants (kTxBytes).
+template <int BN, bool SPLIT, bool Q8 = false>
 struct Stages {
-  static constexpr int kStageBytes = (SPLIT ? 2 : 1) * (Cfg<BN>::kTileA + Cfg<BN>::kTileB);
-  static constexpr int kStages = (kSmemBudget / kStageBytes) > 6 ? 6 : (kSmemBudget / kStageBytes);
+  static constexpr int kQBytes = Q8 ? BN * 64 : 0;
+  static constexpr int kStageBytes = (SPLIT ? 2 : 1) * (Cfg<BN>::kTileA + Cfg<BN>::kTileB) + kQBytes;
+  static constexpr int kTxBytes = Q8 ? 2 * Cfg<BN>::kTileA + kQBytes : kStageBytes;
+  static constexpr int kBudget = Q8 ? 216 * 1024 : kSmemBudget;
+  static constexpr int kStages = (kBudget / kStageBytes) > 6 ? 6 : (kBudget / kStageBytes);
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align slack*/ + 256 /*barriers*/;
 };
 
@@ -172,15 +186,17 @@ __device__ __forceinline__ void epi_store(const Epilogue& e, int N, long long of
   }
 }
 
-template <int BN, bool SPLIT>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BN, bool SPLIT, bool Q8>
+__global__ void __launch_bounds__(threads_of<Q8>(), 1)
     gemm_split_bf16_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_constant__ CUtensorMap map_a_lo,
                            const __grid_constant__ CUtensorMap map_b_hi, const __grid_constant__ CUtensorMap map_b_lo,
                            const KArgs args) {
-  constexpr int STAGES = Stages<BN, SPLIT>::kStages;
+  static_assert(!Q8 || SPLIT, "a Q8_0 operand is always dequantised into split planes");
+  constexpr int STAGES = Stages<BN, SPLIT, Q8>::kStages;
   constexpr int kTileA = Cfg<BN>::kTileA;
   constexpr int kTileB = Cfg<BN>::kTileB;
-  constexpr int kStageBytes = Stages<BN, SPLIT>::kStageBytes;
+  constexpr int kStageBytes = Stages<BN, SPLIT, Q8>::kStageBytes;
+  constexpr int kTxBytes = Stages<BN, SPLIT, Q8>::kTxBytes;
   constexpr uint32_t kAccCols = Cfg<BN>::kAccCols;
 
   extern __shared__ uint8_t smem_raw[];
@@ -189,7 +205,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;   // [2] accumulator ready for the epilogue
   uint64_t* tempty = tfull + 2;       // [2] accumulator drained by the epilogue
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* conv = tempty + 2;        // [STAGES] Q8_0: B tiles dequantised
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(conv + (Q8 ? STAGES : 0));
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -198,6 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      if (Q8) mbar_init(&conv[s], kConvWarps);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
@@ -236,7 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], kStageBytes);
+          mbar_arrive_expect_tx(&full[s], kTxBytes);
           uint8_t* st = smem + s * kStageBytes;
           uint8_t* a_hi = st;
           uint8_t* b_hi = st + kTileA;
@@ -253,7 +271,16 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (SPLIT) tma_load_3d(a_lo + j * 64 * 128, &map_a_lo, &full[s], w.m0 + 64 * j, k0, za);
             }
           }
-          if (!args.b_mn) {
+          if (Q8) {
+            // int8 quants; map_b_hi is the quant map (box {64 bytes, rows})
+            uint8_t* qd = st + 2 * (kTileA + kTileB);
+            if (!args.b_mn) {
+              tma_load_3d(qd, &map_b_hi, &full[s], k0, w.n0, 0);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j) tma_load_3d(qd + j * 64 * 64, &map_b_hi, &full[s], w.n0 + 64 * j, k0, 0);
+            }
+          } else if (!args.b_mn) {
             tma_load_3d(b_hi, &map_b_hi, &full[s], k0, w.n0, zb);
             if (SPLIT) tma_load_3d(b_lo, &map_b_lo, &full[s], k0, w.n0, zb);
           } else {
@@ -290,6 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           ok = mbar_wait(&full[s], ph, args.err, kErrWaitFull);
+          if (Q8) ok = ok && mbar_wait(&conv[s], ph, args.err, kErrWaitFull);
           if (!ok) break;
           tc_fence_after();
           const uint32_t st = smem_u32(smem + s * kStageBytes);
@@ -311,6 +339,81 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         umma_commit(&tfull[b]);
         ++local;
+      }
+    }
+  } else if (warp >= kThreads / 32) {
+    // ------------------------------------------------ Q8_0 dequantisation
+    // Each item is one Q8_0 block (32 quants of a stored row, one scale): value
+    // = scale * q, split into hi / lo bf16 and written to the B plane tiles in
+    // the swizzled layout the UMMA descriptors expect -- the same bits a TMA
+    // load of planes would give.
+    if constexpr (Q8) {
+      const int ct = threadIdx.x - kThreads;
+      const int sblk = args.q8_cols / 32;
+      uint32_t it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < args.units && ok; u += gridDim.x) {
+        const Unit w = decode<BN>(args, u);
+        if (w.skip) continue;
+        for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          ok = warp_wait(&full[s], ph, args.err, kErrWaitFull);
+          if (!ok) break;
+          uint8_t* st = smem + s * kStageBytes;
+          uint8_t* b_hi = st + kTileA;
+          uint8_t* b_lo = st + 2 * kTileA + kTileB;
+          const uint8_t* qs = st + 2 * (kTileA + kTileB);
+          const int k0 = kb * BK;
+#pragma unroll 1
+          for (int i = ct; i < BN * 2; i += 32 * kConvWarps) {
+            // item = one Q8_0 block: 32 quants of stored row `srow`, columns
+            // c32 * 32 .. +31 of this tile's 64
+            int r, srow, sb;
+            const int c32 = i & 1;
+            const uint8_t* src;
+            uint32_t tile;
+            if (!args.b_mn) {   // tile rows = output columns n, 64 k
+              r = i >> 1;
+              src = qs + r * 64 + c32 * 32;
+              srow = w.n0 + r;
+              sb = (k0 >> 5) + c32;
+              tile = 0;
+            } else {            // BN / 64 tiles of 64 k rows x 64 n
+              const int j = i >> 7;
+              r = (i >> 1) & 63;
+              src = qs + j * 4096 + r * 64 + c32 * 32;
+              srow = k0 + r;
+              sb = ((w.n0 + 64 * j) >> 5) + c32;
+              tile = (uint32_t)j * 8192u;
+            }
+            const float sc = (srow < args.q8_rows && sb < sblk)
+                                 ? __half2float(__ushort_as_half(args.q8_scale[(long long)srow * sblk + sb]))
+                                 : 0.f;
+            const uint4 raw0 = reinterpret_cast<const uint4*>(src)[0];
+            const uint4 raw1 = reinterpret_cast<const uint4*>(src)[1];
+            const uint32_t words[8] = {raw0.x, raw0.y, raw0.z, raw0.w, raw1.x, raw1.y, raw1.z, raw1.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {   // 16-byte chunk c32 * 4 + u of each plane
+              uint32_t hv[4], lv[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                // q + 128 as the low mantissa byte of 2^23: exact int8 -> f32
+                const uint32_t wv = words[2 * u + (e >> 1)] ^ 0x80808080u;
+                const int b0 = (e & 1) * 2;
+                const float q0 = __uint_as_float(__byte_perm(wv, 0x4B000000u, 0x7540u | b0)) - 8388736.0f;
+                const float q1 = __uint_as_float(__byte_perm(wv, 0x4B000000u, 0x7540u | (b0 + 1))) - 8388736.0f;
+                split_pair(sc * q0, sc * q1, hv[e], lv[e]);
+              }
+              const uint32_t o = tile + sw_off(r, c32 * 4 + u);
+              *reinterpret_cast<uint4*>(b_hi + o) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+              *reinterpret_cast<uint4*>(b_lo + o) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&conv[s]);
+        }
       }
     }
   } else {
@@ -447,6 +550,23 @@ int make_map(CUtensorMap* map, const __nv_bfloat16* base, const Operand& o, int 
   return r == CUDA_SUCCESS ? 0 : -13;
 }
 
+// Tensor map over the int8 quants of a Q8_0 operand: dims {cols, rows, 1},
+// row stride ld bytes, box {64 bytes, box_rows, 1}, no swizzle (the converters
+// read it row by row). Rows / columns past the matrix read as zero.
+int make_q8_map(CUtensorMap* map, const Operand& o, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return -10;
+  if (reinterpret_cast<uintptr_t>(o.q8) % 16 != 0 || o.ld % 16 != 0) return -11;
+  cuuint64_t dims[3] = {(cuuint64_t)o.cols, (cuuint64_t)o.rows, 1};
+  cuuint64_t strides[2] = {(cuuint64_t)o.ld, (cuuint64_t)o.ld * o.rows};
+  cuuint32_t box[3] = {64u, (cuuint32_t)box_rows, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(o.q8), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -13;
+}
+
 // Estimated microseconds for S K-splits: the busiest CTA's units times
 // (k-blocks per unit x MMA time per k-block + per-unit fill/epilogue), plus for
 // S > 1 the reduction kernel streaming S partial slabs (and a residual) once.
@@ -470,12 +590,12 @@ int choose_splits(const GemmDesc& d, long long tiles, int kb, long long ws_float
   return best;
 }
 
-template <int BN, bool SPLIT>
+template <int BN, bool SPLIT, bool Q8 = false>
 int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream_t stream) {
-  using S = Stages<BN, SPLIT>;
+  using S = Stages<BN, SPLIT, Q8>;
   static bool attr_set = false;
   if (!attr_set) {
-    if (cudaFuncSetAttribute(gemm_split_bf16_kernel<BN, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(gemm_split_bf16_kernel<BN, SPLIT, Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              S::kSmemBytes) != cudaSuccess)
       return -20;
     attr_set = true;
@@ -485,10 +605,15 @@ int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream
   const int b_box = d.b.mn_major ? 64 : BN;
   int rc;
   if ((rc = make_map(&ma_hi, d.a.hi, d.a, a_box))) return rc;
-  if ((rc = make_map(&mb_hi, d.b.hi, d.b, b_box))) return rc;
+  if (Q8) {
+    if ((rc = make_q8_map(&mb_hi, d.b, b_box))) return rc;
+  } else if ((rc = make_map(&mb_hi, d.b.hi, d.b, b_box))) {
+    return rc;
+  }
   if (SPLIT) {
     if ((rc = make_map(&ma_lo, d.a.lo, d.a, a_box))) return rc;
-    if ((rc = make_map(&mb_lo, d.b.lo, d.b, b_box))) return rc;
+    if (Q8) mb_lo = mb_hi;
+    else if ((rc = make_map(&mb_lo, d.b.lo, d.b, b_box))) return rc;
   } else {
     ma_lo = ma_hi;
     mb_lo = mb_hi;
@@ -514,9 +639,12 @@ int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream
   k.ws = sc.ws;
   k.sem = sc.sem;
   k.err = dev_err;
+  k.q8_scale = d.b.q8_scale;
+  k.q8_rows = d.b.rows;
+  k.q8_cols = d.b.cols;
   const int grid = k.units < kNumSMs ? k.units : kNumSMs;
-  if (launch_pdl(gemm_split_bf16_kernel<BN, SPLIT>, dim3(grid), dim3(kThreads), S::kSmemBytes, stream, ma_hi, ma_lo,
-                 mb_hi, mb_lo, k) != 0)
+  if (launch_pdl(gemm_split_bf16_kernel<BN, SPLIT, Q8>, dim3(grid), dim3(threads_of<Q8>()), S::kSmemBytes, stream,
+                 ma_hi, ma_lo, mb_hi, mb_lo, k) != 0)
     return -21;
   if (splits > 1) {
     const long long work = (long long)d.M * ((d.N + 31) / 32);
@@ -549,6 +677,13 @@ int gemm_launch(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStre
   const int al = (e.mode == kEpiStoreSplit || e.mode == kEpiStoreBoth) ? 8 : 4;
   if ((e.m_s0 % al) || (e.m_s1 % al) || (e.n_s1 % al) || (e.bstride % al) || (e.z_s1 % al) || (e.n_div % 32))
     return -3;
+  if (d.b.q8) {
+    // Q8_0 B: dequantised in shared memory into split planes; 64 / 128-wide tiles
+    // keep three stages of A planes + B planes + quants within shared memory
+    if (!d.split || d.batch != 1 || !d.b.q8_scale || d.b.cols % 32 || !d.a.hi || !d.a.lo) return -4;
+    return d.N <= 64 ? launch_bn<64, true, true>(d, sc, dev_err, stream)
+                     : launch_bn<128, true, true>(d, sc, dev_err, stream);
+  }
   if (!d.a.hi || !d.b.hi || (d.split && (!d.a.lo || !d.b.lo))) return -4;
   switch (pick_bn(d.N)) {
     case 64: return d.split ? launch_bn<64, true>(d, sc, dev_err, stream) : launch_bn<64, false>(d, sc, dev_err, stream);

@@ -33,6 +33,13 @@ struct Operand {
   long long batch_stride = 0;  // elements between batches
   int nbatch = 1;
   int bdiv1 = 1, bmul1 = 1, bdiv2 = 1, bmul2 = 0;
+  // Q8_0 operand (B of a non-batched GEMM only): instead of planes, the int8
+  // quants of the stored [rows][cols] matrix (row stride ld bytes) and one fp16
+  // scale per 32 consecutive columns of a row ([rows][cols / 32]), so element
+  // (r, c) = scale[r][c / 32] * q8[r][c] -- Q8_0 blocks with the scales split
+  // off. The GEMM dequantises tiles in shared memory.
+  const int8_t* q8 = nullptr;
+  const uint16_t* q8_scale = nullptr;
 };
 
 enum EpiMode : int {

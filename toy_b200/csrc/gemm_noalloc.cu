@@ -91,6 +91,7 @@ extern "C" int tb2_gemm_noalloc(int M, int N, int K, int batch, int split, const
     r.batch_stride = o->batch_stride; r.nbatch = o->nbatch;
     r.bdiv1 = o->bdiv1 > 0 ? o->bdiv1 : 1; r.bmul1 = o->bmul1;
     r.bdiv2 = o->bdiv2 > 0 ? o->bdiv2 : 1; r.bmul2 = o->bmul2;
+    r.q8 = static_cast<const int8_t*>(o->q8); r.q8_scale = static_cast<const uint16_t*>(o->q8_scale);
     return r;
   };
   d.a = cvt(a);

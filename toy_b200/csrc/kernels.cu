@@ -688,6 +688,23 @@ __global__ void q8_0_quantize_kernel(const float* __restrict__ x, uint8_t* __res
   }
 }
 
+// One thread per block: 17 little-endian 16-bit words (scale, then quant pairs).
+__global__ void q8_0_split_kernel(const uint8_t* __restrict__ blocks, int8_t* __restrict__ qv,
+                                  uint16_t* __restrict__ qs, long long nblocks) {
+  griddep_wait();
+  for (long long b = blockIdx.x * (long long)blockDim.x + threadIdx.x; b < nblocks;
+       b += (long long)gridDim.x * blockDim.x) {
+    const unsigned short* w = reinterpret_cast<const unsigned short*>(blocks + b * 34);
+    qs[b] = w[0];
+    uint32_t out[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) out[j] = (uint32_t)w[1 + 2 * j] | ((uint32_t)w[2 + 2 * j] << 16);
+    uint4* dst = reinterpret_cast<uint4*>(qv + b * 32);
+    dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
+    dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
+  }
+}
+
 __global__ void colsum_rows_kernel(const float* __restrict__ x, int N, int W, float* __restrict__ out) {
   griddep_wait();
   for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < W; c += gridDim.x * blockDim.x) {
@@ -883,6 +900,14 @@ int launch_adamw(float* p, const float* g, float* m, float* v, Planes pp, long l
 int launch_q8_0_to_planes(const uint8_t* q, Planes out, float* f32, long long rows, int K, cudaStream_t st) {
   if (K % 32) return -1;
   launch_pdl(q8_0_to_planes_kernel, dim3(grid_for(rows * K, 256)), dim3(256), 0, st, q, out, f32, rows, K);
+  return ok();
+}
+
+int launch_q8_0_split(const uint8_t* blocks, int8_t* qv, uint16_t* qs, long long nblocks, cudaStream_t st) {
+  if ((reinterpret_cast<uintptr_t>(blocks) & 1u) || (reinterpret_cast<uintptr_t>(qv) & 15u) ||
+      (reinterpret_cast<uintptr_t>(qs) & 1u))
+    return -1;
+  launch_pdl(q8_0_split_kernel, dim3(grid_for(nblocks, 128)), dim3(128), 0, st, blocks, qv, qs, nblocks);
   return ok();
 }
 

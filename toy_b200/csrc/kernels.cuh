@@ -84,6 +84,10 @@ int launch_adamw(float* p, const float* g, float* m, float* v, Planes pp, long l
 int launch_q8_0_to_planes(const uint8_t* q, Planes out, float* f32, long long rows, int K, cudaStream_t st);
 // f32 [rows][K] -> Q8_0 blocks (ggml quantize_row_q8_0_ref, bit-exact).
 int launch_q8_0_quantize(const float* x, uint8_t* q, long long rows, int K, cudaStream_t st);
+// Q8_0 blocks -> the GEMM's quant layout: the 32 int8 quants of block b at
+// qv[32 b ..] and its fp16 scale bits at qs[b] (the same Q8_0 content, scales
+// split off so quant tiles are TMA-loadable).
+int launch_q8_0_split(const uint8_t* blocks, int8_t* qv, uint16_t* qs, long long nblocks, cudaStream_t st);
 
 // out[c] = sum over rows of x[N][W] (fixed order), e.g. bias gradients.
 int launch_colsum_rows(const float* x, int N, int W, float* out, cudaStream_t st);

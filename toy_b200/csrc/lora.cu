@@ -1,0 +1,313 @@
+// Low-rank adapter kernels (see lora.cuh). Every reduction runs in a fixed
+// order, so results do not depend on scheduling.
+#include "lora.cuh"
+
+#include "pdl.cuh"
+
+namespace tb2 {
+
+namespace {
+
+constexpr int kWgradChunks = 32;   // token chunks of the weight-gradient reduction (at least)
+constexpr int kWgradSmem = 16 * 1024;   // a chunk's S rows staged in shared memory
+
+// Chunking of the N tokens: at least kWgradChunks chunks, each small enough
+// for its S rows to fit kWgradSmem.
+void wgrad_chunks(int N, int r, int& nch, int& chunk) {
+  chunk = (N + kWgradChunks - 1) / kWgradChunks;
+  const int cap = kWgradSmem / (4 * r);
+  if (chunk > cap) chunk = cap;
+  if (chunk < 1) chunk = 1;
+  nch = (N + chunk - 1) / chunk;
+}
+
+__device__ __forceinline__ float4 load_planes4(Planes p, long long i) {
+  const uint2 h = *reinterpret_cast<const uint2*>(p.hi + i);
+  const uint2 l = *reinterpret_cast<const uint2*>(p.lo + i);
+  return make_float4(__uint_as_float(h.x << 16) + __uint_as_float(l.x << 16),
+                     __uint_as_float(h.x & 0xffff0000u) + __uint_as_float(l.x & 0xffff0000u),
+                     __uint_as_float(h.y << 16) + __uint_as_float(l.y << 16),
+                     __uint_as_float(h.y & 0xffff0000u) + __uint_as_float(l.y & 0xffff0000u));
+}
+
+__device__ __forceinline__ float2 load_planes2(Planes p, long long i) {
+  const uint32_t h = *reinterpret_cast<const uint32_t*>(p.hi + i);
+  const uint32_t l = *reinterpret_cast<const uint32_t*>(p.lo + i);
+  return make_float2(__uint_as_float(h << 16) + __uint_as_float(l << 16),
+                     __uint_as_float(h & 0xffff0000u) + __uint_as_float(l & 0xffff0000u));
+}
+
+// Output element (0, m, n) of the GEMM epilogue addressing (gemm.cuh).
+__device__ __forceinline__ long long out_offset(const Epilogue& e, int m, int n) {
+  return (long long)(m / e.m_div) * e.m_s1 + (long long)(m % e.m_div) * e.m_s0 + (long long)(n / e.n_div) * e.n_s1 +
+         (n % e.n_div);
+}
+
+// One warp per row: lane l covers columns 4l, 4l + 128, ...; the r partial
+// sums are reduced across the warp by butterfly shuffles. W is staged in
+// shared memory ([r][K], read as float4 along K: conflict-free) when it fits;
+// each warp keeps two rows in flight.
+template <int RT, bool SMEM_W>
+__global__ void __launch_bounds__(256) lora_down_kernel(Planes X, long long ldx, int N, int K,
+                                                        const float* __restrict__ W, int r, float alpha,
+                                                        float* __restrict__ out) {
+  griddep_wait();
+  extern __shared__ float4 wsm4[];
+  const float* w = W;
+  if (SMEM_W) {
+    float* wsm = reinterpret_cast<float*>(wsm4);
+    for (int i = threadIdx.x * 4; i < r * K; i += 256 * 4)
+      *reinterpret_cast<float4*>(wsm + i) = __ldg(reinterpret_cast<const float4*>(W + i));
+    __syncthreads();
+    w = wsm;
+  }
+  const int lane = threadIdx.x % 32;
+  const int warps = gridDim.x * 8;
+  for (int n = (blockIdx.x * 8 + threadIdx.x / 32) * 2; n < N; n += warps * 2) {
+    const bool two = n + 1 < N;
+    float acc0[RT], acc1[RT];
+#pragma unroll
+    for (int j = 0; j < RT; ++j) acc0[j] = acc1[j] = 0.f;
+    for (int k = lane * 4; k < K; k += 128) {
+      const float4 x0 = load_planes4(X, (long long)n * ldx + k);
+      const float4 x1 = two ? load_planes4(X, (long long)(n + 1) * ldx + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < RT; ++j) {
+        if (j < r) {
+          const float4 wv = *reinterpret_cast<const float4*>(w + (long long)j * K + k);
+          acc0[j] += x0.x * wv.x + x0.y * wv.y + x0.z * wv.z + x0.w * wv.w;
+          acc1[j] += x1.x * wv.x + x1.y * wv.y + x1.z * wv.z + x1.w * wv.w;
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < RT; ++j) {
+      float v0 = acc0[j], v1 = acc1[j];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        v0 += __shfl_xor_sync(0xffffffffu, v0, o);
+        v1 += __shfl_xor_sync(0xffffffffu, v1, o);
+      }
+      if (j < r && lane == (j & 31)) {
+        out[(long long)n * r + j] = alpha * v0;
+        if (two) out[(long long)(n + 1) * r + j] = alpha * v1;
+      }
+    }
+  }
+}
+
+// Tile of 32 rows x 128 columns: thread (ty, tx) owns rows 4 ty .. 4 ty + 3 and
+// columns 4 tx .. 4 tx + 3.
+template <int RT>
+__global__ void __launch_bounds__(256) lora_up_kernel(const float* __restrict__ U, int N, int r,
+                                                      const float* __restrict__ W, int C, float alpha, Epilogue e) {
+  griddep_wait();
+  __shared__ float us[32][RT];
+  __shared__ __align__(16) float ws[RT][128];
+  const int tid = threadIdx.x, tx = tid % 32, ty = tid / 32;
+  const int c0 = blockIdx.x * 128, n0 = blockIdx.y * 32;
+  for (int i = tid; i < 32 * r; i += 256) {
+    const int rr = i / r, j = i % r;
+    us[rr][j] = n0 + rr < N ? U[(long long)(n0 + rr) * r + j] : 0.f;
+  }
+  for (int i = tid; i < r * 128; i += 256) {
+    const int j = i / 128, cc = i % 128;
+    ws[j][cc] = c0 + cc < C ? W[(long long)j * C + c0 + cc] : 0.f;
+  }
+  __syncthreads();
+  float4 acc[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < RT; ++j) {
+    if (j < r) {
+      const float4 w = *reinterpret_cast<const float4*>(&ws[j][tx * 4]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float u = us[ty * 4 + q][j];
+        acc[q].x += u * w.x; acc[q].y += u * w.y; acc[q].z += u * w.z; acc[q].w += u * w.w;
+      }
+    }
+  }
+  const int c = c0 + tx * 4;
+  if (c >= C) return;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int n = n0 + ty * 4 + q;
+    if (n >= N) break;
+    float4* y = reinterpret_cast<float4*>(e.out + out_offset(e, n, c));
+    float4 v = *y;
+    v.x += alpha * acc[q].x; v.y += alpha * acc[q].y; v.z += alpha * acc[q].z; v.w += alpha * acc[q].w;
+    *y = v;
+  }
+}
+
+// Block of WARPS warps over 64 columns (lane: columns 2 l, 2 l + 1) and the
+// token chunk by; warp w takes tokens n0 + w, n0 + w + WARPS, ... and the
+// warps' sums are added in warp order: partial[by][c][j] = sum over the chunk
+// of Big[n][c] * S[n][j].
+template <int RT>
+struct WgradCfg {
+  static constexpr int kWarps = RT <= 16 ? 8 : (RT <= 32 ? 4 : 2);
+};
+
+template <int RT>
+__global__ void __launch_bounds__(WgradCfg<RT>::kWarps * 32)
+    lora_wgrad_partial_kernel(Planes Big, long long ldb, const float* __restrict__ S, int N, int C, int r, int chunk,
+                              float* __restrict__ partial) {
+  griddep_wait();
+  constexpr int WARPS = WgradCfg<RT>::kWarps;
+  extern __shared__ float ss[];          // [chunk][r] S rows, then [WARPS][64][RT] warp sums
+  float* red = ss + chunk * r;
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  const int c = blockIdx.x * 64 + lane * 2;
+  const int n0 = blockIdx.y * chunk;
+  const int n1 = min(N, n0 + chunk);
+  for (int i = threadIdx.x; i < (n1 - n0) * r; i += WARPS * 32) ss[i] = S[(long long)n0 * r + i];
+  __syncthreads();
+  float a0[RT], a1[RT];
+#pragma unroll
+  for (int j = 0; j < RT; ++j) a0[j] = a1[j] = 0.f;
+  if (c < C) {
+#pragma unroll 4
+    for (int n = n0 + warp; n < n1; n += WARPS) {
+      const float2 b = load_planes2(Big, (long long)n * ldb + c);
+      const float* sr = ss + (n - n0) * r;
+#pragma unroll
+      for (int j = 0; j < RT; ++j) {
+        if (j < r) {
+          const float sv = sr[j];
+          a0[j] += b.x * sv;
+          a1[j] += b.y * sv;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < RT; ++j) {
+    red[(warp * 64 + lane * 2) * RT + j] = a0[j];
+    red[(warp * 64 + lane * 2 + 1) * RT + j] = a1[j];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 64 * r; i += WARPS * 32) {
+    const int cc = i / r, j = i % r;
+    if (blockIdx.x * 64 + cc >= C) continue;
+    float sum = 0.f;
+#pragma unroll
+    for (int w2 = 0; w2 < WARPS; ++w2) sum += red[(w2 * 64 + cc) * RT + j];
+    partial[((long long)blockIdx.y * C + blockIdx.x * 64 + cc) * r + j] = sum;
+  }
+}
+
+__global__ void lora_wgrad_reduce_kernel(const float* __restrict__ partial, int nch, int C, int r, float alpha,
+                                         float* __restrict__ out, long long o_sc, long long o_sj) {
+  griddep_wait();
+  const long long total = (long long)C * r;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int ch = 0; ch < nch; ++ch) s += partial[(long long)ch * total + i];
+    const int c = (int)(i / r), j = (int)(i % r);
+    out[(long long)c * o_sc + (long long)j * o_sj] = alpha * s;
+  }
+}
+
+__global__ void lora_transpose_kernel(const float* __restrict__ W, int C, int r, float* __restrict__ Wt) {
+  griddep_wait();
+  const long long total = (long long)C * r;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int j = (int)(i / C), c = (int)(i % C);
+    Wt[i] = W[(long long)c * r + j];
+  }
+}
+
+template <template <int> class F, typename... A>
+int by_rank(int r, A... a) {
+  if (r <= 8) return F<8>::run(a...);
+  if (r <= 16) return F<16>::run(a...);
+  if (r <= 32) return F<32>::run(a...);
+  return F<64>::run(a...);
+}
+
+template <int RT>
+struct Down {
+  static int run(Planes X, long long ldx, int N, int K, const float* W, int r, float alpha, float* out,
+                 cudaStream_t st) {
+    long long blocks = (N + 15) / 16;
+    if (blocks > 148 * 2) blocks = 148 * 2;
+    const size_t wbytes = (size_t)r * K * sizeof(float);
+    if (wbytes <= 48 * 1024)
+      return launch_pdl(lora_down_kernel<RT, true>, dim3((unsigned)blocks), dim3(256), wbytes, st, X, ldx, N, K, W, r,
+                        alpha, out);
+    return launch_pdl(lora_down_kernel<RT, false>, dim3((unsigned)blocks), dim3(256), 0, st, X, ldx, N, K, W, r,
+                      alpha, out);
+  }
+};
+
+template <int RT>
+struct Up {
+  static int run(const float* U, int N, int r, const float* W, int C, float alpha, Epilogue e, cudaStream_t st) {
+    return launch_pdl(lora_up_kernel<RT>, dim3((unsigned)((C + 127) / 128), (unsigned)((N + 31) / 32)), dim3(256), 0,
+                      st, U, N, r, W, C, alpha, e);
+  }
+};
+
+template <int RT>
+struct Wgrad {
+  static int run(Planes Big, long long ldb, const float* S, int N, int C, int r, int nch, int chunk, float* partial,
+                 cudaStream_t st) {
+    constexpr int WARPS = WgradCfg<RT>::kWarps;
+    const size_t smem = ((size_t)chunk * r + (size_t)WARPS * 64 * RT) * sizeof(float);
+    if (smem > 48 * 1024) return -1;
+    return launch_pdl(lora_wgrad_partial_kernel<RT>, dim3((unsigned)((C + 63) / 64), (unsigned)nch),
+                      dim3(WARPS * 32), smem, st, Big, ldb, S, N, C, r, chunk, partial);
+  }
+};
+
+bool rank_ok(int r) { return r >= 1 && r <= kLoraMaxRank; }
+
+}  // namespace
+
+int launch_lora_down(Planes X, long long ldx, int N, int K, const float* W, int r, float alpha, float* out,
+                     cudaStream_t st) {
+  if (!rank_ok(r) || N <= 0 || K <= 0 || K % 4 || ldx % 4) return -1;
+  return by_rank<Down>(r, X, ldx, N, K, W, r, alpha, out, st) ? -3 : 0;
+}
+
+int launch_lora_up(const float* U, int N, int r, const float* W, int C, float alpha, const Epilogue& e,
+                   cudaStream_t st) {
+  if (!rank_ok(r) || N <= 0 || C <= 0 || C % 4 || e.n_div % 4 || e.m_s0 % 4 || e.m_s1 % 4 || e.n_s1 % 4) return -1;
+  return by_rank<Up>(r, U, N, r, W, C, alpha, e, st) ? -3 : 0;
+}
+
+long long lora_wgrad_partial_floats(int N, int C, int r) {
+  if (!rank_ok(r) || N <= 0) return 0;
+  int nch, chunk;
+  wgrad_chunks(N, r, nch, chunk);
+  return (long long)nch * C * r;
+}
+
+int launch_lora_wgrad(Planes Big, long long ldb, const float* S, int N, int C, int r, float alpha, float* out,
+                      long long o_sc, long long o_sj, float* partial, cudaStream_t st) {
+  if (!rank_ok(r) || N <= 0 || C <= 0 || C % 2 || ldb % 2) return -1;
+  int nch, chunk;
+  wgrad_chunks(N, r, nch, chunk);
+  int rc = by_rank<Wgrad>(r, Big, ldb, S, N, C, r, nch, chunk, partial, st);
+  if (rc) return rc < 0 ? rc : -3;
+  const long long total = (long long)C * r;
+  long long blocks = (total + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  return launch_pdl(lora_wgrad_reduce_kernel, dim3((unsigned)blocks), dim3(256), 0, st, partial, nch, C, r, alpha,
+                    out, o_sc, o_sj)
+             ? -3 : 0;
+}
+
+int launch_lora_transpose(const float* W, int C, int r, float* Wt, cudaStream_t st) {
+  if (!rank_ok(r) || C <= 0) return -1;
+  long long blocks = ((long long)C * r + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  return launch_pdl(lora_transpose_kernel, dim3((unsigned)blocks), dim3(256), 0, st, W, C, r, Wt) ? -3 : 0;
+}
+
+}  // namespace tb2

@@ -1,0 +1,39 @@
+// Low-rank adapter products of the LoRA / QLoRA step on CUDA cores (f32).
+//
+// With rank r <= 64 every product is skinny (one side is r wide), so these are
+// bandwidth-bound kernels rather than tensor-core tiles: reading the activation
+// or gradient once dominates, and a tcgen05 GEMM would spend its time filling
+// and draining a 128-row pipeline for 8 output columns.
+//
+// Layouts: activations / gradients are split planes [N][ld] (hi + lo carry the
+// f32 value); u, du are f32 [N][r]; adapter matrices are f32 in the layouts the
+// kernels name ([r][K] means r rows of K contiguous values).
+#pragma once
+#include "gemm.cuh"
+#include "kernels.cuh"
+
+namespace tb2 {
+
+constexpr int kLoraMaxRank = 64;
+
+// out[n][j] = alpha * sum_k X[n][k] * W[j][k]     (X planes [N][ldx], W [r][K])
+int launch_lora_down(Planes X, long long ldx, int N, int K, const float* W, int r, float alpha, float* out,
+                     cudaStream_t st);
+
+// Y(n, c) += alpha * sum_j U[n][j] * W[j][c]     (U [N][r], W [r][C]); Y(n, c)
+// is e.out[epi offset of (z = 0, m = n, n = c)] (gemm.cuh Epilogue addressing;
+// e.n_div must be a multiple of 4, rows 16-byte aligned).
+int launch_lora_up(const float* U, int N, int r, const float* W, int C, float alpha, const Epilogue& e,
+                   cudaStream_t st);
+
+// G(c, j) = alpha * sum_n Big[n][c] * S[n][j]    (Big planes [N][ldb], S [N][r])
+// written to out[c * o_sc + j * o_sj]; token chunks are summed in a fixed
+// order through `partial` (lora_wgrad_partial_floats floats).
+long long lora_wgrad_partial_floats(int N, int C, int r);
+int launch_lora_wgrad(Planes Big, long long ldb, const float* S, int N, int C, int r, float alpha, float* out,
+                      long long o_sc, long long o_sj, float* partial, cudaStream_t st);
+
+// Wt[j][c] = W[c][j]   (W [C][r] -> Wt [r][C])
+int launch_lora_transpose(const float* W, int C, int r, float* Wt, cudaStream_t st);
+
+}  // namespace tb2

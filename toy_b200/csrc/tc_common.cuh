@@ -75,6 +75,34 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   return true;
 }
 
+// Bounded wait by every lane of a warp; the result is warp-uniform.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  const bool ok = mbar_wait(bar, parity, err, code);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// Make this thread's generic-proxy shared-memory writes visible to the async
+// proxy (TMA, tensor core) before signalling their consumer.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Byte offset of 16-byte chunk `chunk` (0..7) of row `row` in a [rows x 64]
+// bf16 tile in the 128-byte swizzle layout TMA writes (chunk c of row r is
+// stored at chunk c ^ (r % 8)).
+__device__ __forceinline__ uint32_t sw_off(int row, int chunk) {
+  return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+// (x0, x1) as packed bf16 pairs hi = rn(x), lo = rn(x - hi); x0 in the low half.
+__device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& h, uint32_t& l) {
+  const __nv_bfloat162 hb = __floats2bfloat162_rn(x0, x1);
+  h = reinterpret_cast<const uint32_t&>(hb);
+  const __nv_bfloat162 lb =
+      __floats2bfloat162_rn(x0 - __uint_as_float(h << 16), x1 - __uint_as_float(h & 0xffff0000u));
+  l = reinterpret_cast<const uint32_t&>(lb);
+}
+
 // ------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
