@@ -181,6 +181,8 @@ def main():
     ap.add_argument("--workload", default="smollm2_full_ft_b8_t512", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=0, help="override sequences per GPU (small profiling cases)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="override the decoder depth (small profiling cases; recorded in config)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     wl = WORKLOADS[args.workload]
@@ -195,6 +197,8 @@ def main():
     from toy_b200._lib import lib
     L = lib()
     cfg = LlamaConfig.smollm2_135m()
+    if args.layers:
+        cfg.n_layers = args.layers
     B, T = (args.batch or wl["B"]), wl["T"]
     N = B * T
     dp = None
@@ -292,7 +296,8 @@ def main():
         "data": "synthetic (uniform ids, seeded init)",
         "config": {"workload": args.workload, "model": "SmolLM2-135M shape", "global_batch": B * world,
                    "seq_len": T, "parallelism": f"dp{world}", "tokens_per_step": tokens,
-                   "l2": "working set (activations ~6 GB, weights+moments 2 GB) far exceeds the 126 MB L2"},
+                   "l2": "working set (activations ~6 GB, weights+moments 2 GB) far exceeds the 126 MB L2",
+                   **({"layers_override": cfg.n_layers} if args.layers else {})},
         "step_roofline": {"tflops_algorithmic": step_tflops, "peak_tflops": sustained,
                           "frac": step_tflops / sustained, "peak_source": f"bf16 sustained, {src}",
                           "flops_per_token": f_tok},

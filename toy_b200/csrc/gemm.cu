@@ -390,20 +390,25 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
             const float sc = (srow < args.q8_rows && sb < sblk)
                                  ? __half2float(__ushort_as_half(args.q8_scale[(long long)srow * sblk + sb]))
                                  : 0.f;
-            const uint4 raw0 = reinterpret_cast<const uint4*>(src)[0];
-            const uint4 raw1 = reinterpret_cast<const uint4*>(src)[1];
+            // the two 16-byte halves in a lane-dependent order: each 8-lane
+            // phase of a shared load then touches 8 distinct bank groups
+            const int sw = (lane >> 2) & 1;
+            const uint4 ra = reinterpret_cast<const uint4*>(src)[sw];
+            const uint4 rb = reinterpret_cast<const uint4*>(src)[sw ^ 1];
+            const uint4 raw0 = sw ? rb : ra, raw1 = sw ? ra : rb;
             const uint32_t words[8] = {raw0.x, raw0.y, raw0.z, raw0.w, raw1.x, raw1.y, raw1.z, raw1.w};
+            const uint64_t scp = pack_f2(sc, sc);
 #pragma unroll
             for (int u = 0; u < 4; ++u) {   // 16-byte chunk c32 * 4 + u of each plane
               uint32_t hv[4], lv[4];
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                // q + 128 as the low mantissa byte of 2^23: exact int8 -> f32
+                // q + 128 as the low mantissa byte of 2^23: exact int8 -> f32 (a pair at a time)
                 const uint32_t wv = words[2 * u + (e >> 1)] ^ 0x80808080u;
                 const int b0 = (e & 1) * 2;
-                const float q0 = __uint_as_float(__byte_perm(wv, 0x4B000000u, 0x7540u | b0)) - 8388736.0f;
-                const float q1 = __uint_as_float(__byte_perm(wv, 0x4B000000u, 0x7540u | (b0 + 1))) - 8388736.0f;
-                split_pair(sc * q0, sc * q1, hv[e], lv[e]);
+                const uint64_t m = ((uint64_t)__byte_perm(wv, 0x4B000000u, 0x7540u | (b0 + 1)) << 32) |
+                                   __byte_perm(wv, 0x4B000000u, 0x7540u | b0);
+                split_pair2(f2_mul(f2_add(m, kMagicPair), scp), hv[e], lv[e]);
               }
               const uint32_t o = tile + sw_off(r, c32 * 4 + u);
               *reinterpret_cast<uint4*>(b_hi + o) = make_uint4(hv[0], hv[1], hv[2], hv[3]);

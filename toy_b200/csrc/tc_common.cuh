@@ -103,6 +103,40 @@ __device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& h, uint
   l = reinterpret_cast<const uint32_t&>(lb);
 }
 
+// Packed pairs of f32 in one 64-bit register (element 0 in the low half) and
+// the sm_100 two-wide f32 arithmetic on them.
+__device__ __forceinline__ uint64_t pack_f2(float x0, float x1) {
+  return ((uint64_t)__float_as_uint(x1) << 32) | __float_as_uint(x0);
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// -(2^23 + 128) in both halves: subtracts the int8 -> f32 magic offset.
+constexpr uint64_t kMagicPair = 0xCB000080CB000080ull;
+
+// split_pair on a packed pair: hi = rn_bf16(x), lo = rn_bf16(x - hi), element 0
+// in the low half of each result.
+__device__ __forceinline__ void split_pair2(uint64_t x, uint32_t& h, uint32_t& l) {
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(__uint_as_float((uint32_t)(x >> 32))),
+      "f"(__uint_as_float((uint32_t)x)));
+  const uint64_t hf = ((uint64_t)(h & 0xffff0000u) << 32) | (uint64_t)(h << 16);
+  const uint64_t r = f2_sub(x, hf);
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(l) : "f"(__uint_as_float((uint32_t)(r >> 32))),
+      "f"(__uint_as_float((uint32_t)r)));
+}
+
 // ------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
