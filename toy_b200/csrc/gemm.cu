@@ -23,6 +23,8 @@
 #include "tc_common.cuh"
 
 #include <cudaTypedefs.h>
+#include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <mutex>
 
@@ -572,31 +574,73 @@ int make_q8_map(CUtensorMap* map, const Operand& o, int box_rows) {
   return r == CUDA_SUCCESS ? 0 : -13;
 }
 
-// Estimated microseconds for S K-splits: the busiest CTA's units times
-// (k-blocks per unit x MMA time per k-block + per-unit fill/epilogue), plus for
-// S > 1 the reduction kernel streaming S partial slabs (and a residual) once.
-int choose_splits(const GemmDesc& d, long long tiles, int kb, long long ws_floats, int bn) {
-  if (d.causal || d.batch != 1 || tiles >= kNumSMs || kb < 8) return 1;
-  const double t_kb = (d.split ? 3.0 : 1.0) * 2.0 * BM * bn * BK / 7740.0 / 1965.0;   // us per k-block
-  const double mn_bytes = 4.0 * d.M * d.N;
+// Launch plan: tile width BN and number of K splits, chosen by a cost model
+// (a pure function of the shape, so the choice -- and with it the summation
+// order -- is the same on every run and every rank). Calibrated on this
+// kernel's measured behaviour on B200: the main loop sustains ~1310 TFLOP/s
+// of executed MMA work over 148 SMs; a CTA switching tiles costs ~0.5 us;
+// filling the pipeline ~1.2 us; the last tile's epilogue drains its output at
+// the CTA's share of HBM bandwidth; K splits add a reduction kernel that
+// streams the partial slabs once. A k-block also cannot finish faster than
+// its operand tiles arrive: ~82 GB/s per SM from L2 (~12 TB/s over the chip),
+// which is what makes narrow tiles slow.
+constexpr double kSmFlopsPerUs = 1310.0e6 / kNumSMs;
+constexpr double kSmOperandBytesPerUs = 82.0e3;
+
+double estimate_us(const GemmDesc& d, int bn, int s) {
+  const int tm = (d.M + BM - 1) / BM, tn = (d.N + bn - 1) / bn;
+  double tiles = (double)d.batch * tm * tn;
+  int kb = (d.K + BK - 1) / BK;
+  if (d.causal == 1) tiles *= (double)(tm + 1) / (2.0 * tm);   // tiles above the diagonal are skipped
+  if (d.causal == 2) kb = kb / 2 + 1;                          // K clamped at the diagonal, on average
+  const double units = tiles * s;
+  const double per_cta = std::ceil(units / kNumSMs);
+  const double t_mma = (d.split ? 3.0 : 1.0) * 2.0 * BM * bn * BK / kSmFlopsPerUs;
+  const double t_feed = (d.split ? 2.0 : 1.0) * (BM + bn) * BK * 2.0 / kSmOperandBytesPerUs;
+  const double t_kb = std::max(t_mma, t_feed);
   const bool reads_out = d.epi.mode == kEpiAccumF32 || d.epi.mode == kEpiResidF32;
-  int best = 1;
+  const double active = units < kNumSMs ? units : (double)kNumSMs;
+  const double drain_bw = std::min(100.0e3, 6.5e6 / active);   // bytes per us per CTA
+  const double tile_bytes = (double)BM * bn * 4.0 * (s == 1 && reads_out ? 2.0 : 1.0);
+  double t = 1.2 + per_cta * (std::ceil((double)kb / s) * t_kb + 0.5) + tile_bytes / drain_bw;
+  if (s > 1) t += ((s + 1.0) * d.M * d.N * 4.0 + (reads_out ? d.M * d.N * 4.0 : 0.0)) / 5.0e6 + 2.5;
+  return t;
+}
+
+struct Plan {
+  int bn = 128, splits = 1;
+};
+
+Plan choose_plan(const GemmDesc& d, long long ws_floats, bool q8) {
+  static const int kBn[] = {64, 128, 192, 256};
+  const int kb = (d.K + BK - 1) / BK;
+  const bool can_split = !d.causal && d.batch == 1 && ws_floats > 0;
+  Plan best;
   double best_t = 1e30;
-  for (int s = 1; s <= 16 && s <= kb / 2; ++s) {
-    if (s > 1 && (long long)s * d.M * d.N > ws_floats) break;
-    const double per_cta = (double)((tiles * s + kNumSMs - 1) / kNumSMs);
-    double t = per_cta * (((kb + s - 1) / s) * t_kb + 1.5);
-    if (s > 1) t += ((s + 1) * mn_bytes + (reads_out ? mn_bytes : 0.0)) / 5.0e6 + 2.0;
-    if (t < best_t - 1e-9) {
-      best_t = t;
-      best = s;
+  for (int bn : kBn) {
+    if (q8 && bn > 128) break;
+    if (bn > 64 && bn - 64 >= d.N) break;   // a narrower tile already covers N
+    int s_lo = 1, s_hi = 1;
+    if (d.splits > 0) {
+      s_lo = s_hi = d.splits;
+    } else if (can_split && kb >= 8) {
+      s_hi = std::min(16, kb / 2);
+    }
+    for (int s = s_lo; s <= s_hi; ++s) {
+      if (s > 1 && (long long)s * d.M * d.N > ws_floats) break;
+      const double t = estimate_us(d, bn, s);
+      if (t < best_t - 1e-9) {
+        best_t = t;
+        best.bn = bn;
+        best.splits = s;
+      }
     }
   }
   return best;
 }
 
 template <int BN, bool SPLIT, bool Q8 = false>
-int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream_t stream) {
+int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream_t stream, int splits) {
   using S = Stages<BN, SPLIT, Q8>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -633,7 +677,7 @@ int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream
   k.kb_total = (d.K + BK - 1) / BK;
   k.causal = d.causal;
   const long long tiles = (long long)d.batch * k.tiles_m * k.tiles_n;
-  int splits = d.splits > 0 ? d.splits : choose_splits(d, tiles, k.kb_total, sc.ws_floats, BN);
+  if (splits < 1) splits = 1;
   if (splits > k.kb_total) splits = k.kb_total;
   if (splits > 1 && (d.causal || d.batch != 1 || !sc.ws || (long long)splits * d.M * d.N > sc.ws_floats))
     splits = 1;
@@ -661,13 +705,6 @@ int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream
   return 0;
 }
 
-int pick_bn(int N) {
-  if (N <= 64) return 64;
-  if (N <= 128) return 128;
-  const int t256 = (N + 255) / 256 * 256, t192 = (N + 191) / 192 * 192;
-  return t192 < t256 ? 192 : 256;
-}
-
 }  // namespace
 
 int make_plane_map(CUtensorMap* map, const __nv_bfloat16* base, const Operand& o, int box_rows) {
@@ -682,22 +719,28 @@ int gemm_launch(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStre
   const int al = (e.mode == kEpiStoreSplit || e.mode == kEpiStoreBoth) ? 8 : 4;
   if ((e.m_s0 % al) || (e.m_s1 % al) || (e.n_s1 % al) || (e.bstride % al) || (e.z_s1 % al) || (e.n_div % 32))
     return -3;
+  const Plan pl = choose_plan(d, sc.ws ? sc.ws_floats : 0, d.b.q8 != nullptr);
   if (d.b.q8) {
     // Q8_0 B: dequantised in shared memory into split planes; 64 / 128-wide tiles
     // keep three stages of A planes + B planes + quants within shared memory
     if (!d.split || d.batch != 1 || !d.b.q8_scale || d.b.cols % 32 || !d.a.hi || !d.a.lo) return -4;
-    return d.N <= 64 ? launch_bn<64, true, true>(d, sc, dev_err, stream)
-                     : launch_bn<128, true, true>(d, sc, dev_err, stream);
+    return pl.bn <= 64 ? launch_bn<64, true, true>(d, sc, dev_err, stream, pl.splits)
+                       : launch_bn<128, true, true>(d, sc, dev_err, stream, pl.splits);
   }
   if (!d.a.hi || !d.b.hi || (d.split && (!d.a.lo || !d.b.lo))) return -4;
-  switch (pick_bn(d.N)) {
-    case 64: return d.split ? launch_bn<64, true>(d, sc, dev_err, stream) : launch_bn<64, false>(d, sc, dev_err, stream);
+  const int sp = pl.splits;
+  switch (pl.bn) {
+    case 64:
+      return d.split ? launch_bn<64, true>(d, sc, dev_err, stream, sp) : launch_bn<64, false>(d, sc, dev_err, stream, sp);
     case 128:
-      return d.split ? launch_bn<128, true>(d, sc, dev_err, stream) : launch_bn<128, false>(d, sc, dev_err, stream);
+      return d.split ? launch_bn<128, true>(d, sc, dev_err, stream, sp)
+                     : launch_bn<128, false>(d, sc, dev_err, stream, sp);
     case 192:
-      return d.split ? launch_bn<192, true>(d, sc, dev_err, stream) : launch_bn<192, false>(d, sc, dev_err, stream);
+      return d.split ? launch_bn<192, true>(d, sc, dev_err, stream, sp)
+                     : launch_bn<192, false>(d, sc, dev_err, stream, sp);
     default:
-      return d.split ? launch_bn<256, true>(d, sc, dev_err, stream) : launch_bn<256, false>(d, sc, dev_err, stream);
+      return d.split ? launch_bn<256, true>(d, sc, dev_err, stream, sp)
+                     : launch_bn<256, false>(d, sc, dev_err, stream, sp);
   }
 }
 
