@@ -747,20 +747,35 @@ int kind_of(const char* call) {
     if (rc_k) return rc_k;                         \
   } while (0)
 
-// Y[:, col_off : col_off + d_out] += s * (X A^T) B^T, saving u = X A^T (planes) for backward.
-int LlamaEngine::lora_forward(int l, int t, Planes X, int d_in, float* Y, long long ldy, int col_off, int d_out) {
+// u = X A^T [N][r] (saved for the backward) and B^T [r][d_out] of adapter
+// (l, t), ahead of the base GEMM that splices s u B^T into its output.
+int LlamaEngine::lora_prep(int l, int t, Planes X, int d_in, int d_out) {
   const LlamaConfig& c = cfg_;
   const int N = this->N(), r = c.lora_rank;
   const std::string pre = "blk." + std::to_string(l) + "." + kProjName[t];
-  const Param& A = P(pre + ".lora_a");
-  const Param& Bp = P(pre + ".lora_b");
-  float* u = lora_u_[l][t];
-  float* bt = lora_bt_[l][t];
-  // u = X A^T [N][r]; Y[:, col_off ..] += s * u B^T (B^T kept for the backward)
-  KL(launch_lora_transpose(P32(Bp), d_out, r, bt, stream_));
-  KL(launch_lora_down(X, d_in, N, d_in, P32(A), r, 1.0f, u, stream_));
-  KL(launch_lora_up(u, N, r, bt, d_out, c.lora_alpha / (float)r, epi_rowmajor(kEpiAccumF32, Y + col_off, ldy),
-                    stream_));
+  KL(launch_lora_transpose(P32(P(pre + ".lora_b")), d_out, r, lora_bt_[l][t], stream_));
+  KL(launch_lora_down(X, d_in, N, d_in, P32(P(pre + ".lora_a")), r, 1.0f, lora_u_[l][t], stream_));
+  return 0;
+}
+
+// The splice of adapter (l, t) as a GEMM epilogue addend on output columns [c0, c0 + d_out).
+LoraAddend LlamaEngine::lora_addend(int l, int t, int c0, int d_out) const {
+  LoraAddend a;
+  a.u = lora_u_[l][t];
+  a.bt = lora_bt_[l][t];
+  a.c0 = c0;
+  a.width = d_out;
+  a.r = cfg_.lora_rank;
+  a.scale = cfg_.lora_alpha / (float)cfg_.lora_rank;
+  return a;
+}
+
+// Y[:, col_off : col_off + d_out] += s * (X A^T) B^T as a separate kernel (for
+// base GEMMs without a fused epilogue), saving u = X A^T for the backward.
+int LlamaEngine::lora_forward(int l, int t, Planes X, int d_in, float* Y, long long ldy, int col_off, int d_out) {
+  CK(lora_prep(l, t, X, d_in, d_out));
+  const LoraAddend a = lora_addend(l, t, col_off, d_out);
+  KL(launch_lora_up(a.u, N(), a.r, a.bt, d_out, a.scale, epi_rowmajor(kEpiAccumF32, Y + col_off, ldy), stream_));
   return 0;
 }
 
@@ -804,15 +819,30 @@ int LlamaEngine::enqueue_forward() {
     g.M = N; g.N = W; g.K = d;
     g.a = op(h1_[l], N, d, d, 0);
     g.b = wop(P(pre + "attn_q.weight"), W, d, d, 0);
-    g.epi = epi_rowmajor(kEpiStoreF32, qkv_, W);
-    CK(gemm(g));
-    if (lora) {
-      if (c.lora_targets & (1 << kLoraQ)) CK(lora_forward(l, kLoraQ, h1_[l], d, qkv_, W, 0, H * dh));
-      if (c.lora_targets & (1 << kLoraK)) CK(lora_forward(l, kLoraK, h1_[l], d, qkv_, W, H * dh, KV * dh));
-      if (c.lora_targets & (1 << kLoraV)) CK(lora_forward(l, kLoraV, h1_[l], d, qkv_, W, (H + KV) * dh, KV * dh));
-    }
     const float* bias = c.qkv_bias ? P32(P(pre + "attn_q.bias")) : nullptr;
-    KL(launch_rope_qkv_fwd(qkv_, bias, pos_, cs_, cs_rows_, Qh_[l], Kh_[l], Vh_[l], B, T, H, KV, dh, stream_));
+    const int qkv_t[3] = {kLoraQ, kLoraK, kLoraV};
+    const int qkv_c0[3] = {0, H * dh, (H + KV) * dh}, qkv_w[3] = {H * dh, KV * dh, KV * dh};
+    if (dh == 64) {
+      // one launch: q|k|v projection, adapters, bias, RoPE, head-major Q / K / V planes
+      g.epi.mode = kEpiRopeQKV;
+      RopeOut& ro = g.epi.rope;
+      ro.pos = pos_; ro.cs = cs_; ro.tab_rows = cs_rows_; ro.bias = bias;
+      ro.q_hi = Qh_[l].hi; ro.q_lo = Qh_[l].lo; ro.k_hi = Kh_[l].hi; ro.k_lo = Kh_[l].lo;
+      ro.v_hi = Vh_[l].hi; ro.v_lo = Vh_[l].lo;
+      ro.T = T; ro.H = H; ro.KV = KV; ro.dh = dh;
+      for (int i = 0; i < 3 && lora; ++i)
+        if (c.lora_targets & (1 << qkv_t[i])) {
+          CK(lora_prep(l, qkv_t[i], h1_[l], d, qkv_w[i]));
+          g.epi.lora[g.epi.n_lora++] = lora_addend(l, qkv_t[i], qkv_c0[i], qkv_w[i]);
+        }
+      CK(gemm(g));
+    } else {
+      g.epi = epi_rowmajor(kEpiStoreF32, qkv_, W);
+      CK(gemm(g));
+      for (int i = 0; i < 3 && lora; ++i)
+        if (c.lora_targets & (1 << qkv_t[i])) CK(lora_forward(l, qkv_t[i], h1_[l], d, qkv_, W, qkv_c0[i], qkv_w[i]));
+      KL(launch_rope_qkv_fwd(qkv_, bias, pos_, cs_, cs_rows_, Qh_[l], Kh_[l], Vh_[l], B, T, H, KV, dh, stream_));
+    }
     if (flash_) {
       // fused: O (token-major planes) and the row normalisers for the backward
       KL(launch_flash_fwd(Qh_[l], Kh_[l], Vh_[l], O_[l], lse2_[l], B, T, H, KV, dh, scale, err_, stream_));
@@ -844,26 +874,52 @@ int LlamaEngine::enqueue_forward() {
     gw.b = wop(P(pre + "attn_output.weight"), d, H * dh, H * dh, 0);
     gw.epi = epi_rowmajor(kEpiResidF32, x1_[l], d);
     gw.epi.res = x_[l];
+    if (lora && (c.lora_targets & (1 << kLoraO))) {
+      CK(lora_prep(l, kLoraO, O_[l], H * dh, d));
+      gw.epi.lora[gw.epi.n_lora++] = lora_addend(l, kLoraO, 0, d);
+    }
     CK(gemm(gw));
-    if (lora && (c.lora_targets & (1 << kLoraO))) CK(lora_forward(l, kLoraO, O_[l], H * dh, x1_[l], d, 0, d));
     KL(launch_rmsnorm_fwd(x1_[l], P32(P(pre + "ffn_norm.weight")), h2_[l], N, d, c.rms_eps, stream_));
     GemmDesc gg;
     gg.M = N; gg.N = 2 * ff; gg.K = d;
     gg.a = op(h2_[l], N, d, d, 0);
-    gg.b = wop(P(pre + "ffn_gate.weight"), 2 * ff, d, d, 0);
-    gg.epi = epi_rowmajor(kEpiStoreF32, gu_[l], 2 * ff);
-    CK(gemm(gg));
-    if (lora && (c.lora_targets & (1 << kLoraGate))) CK(lora_forward(l, kLoraGate, h2_[l], d, gu_[l], 2 * ff, 0, ff));
-    if (lora && (c.lora_targets & (1 << kLoraUp))) CK(lora_forward(l, kLoraUp, h2_[l], d, gu_[l], 2 * ff, ff, ff));
-    KL(launch_swiglu_fwd(gu_[l], a_[l], N, ff, stream_));
+    const Param& Wgu = P(pre + "ffn_gate.weight");
+    gg.b = wop(Wgu, 2 * ff, d, d, 0);
+    if (Wgu.q8) {
+      // Q8_0 base: one launch -- gate|up projection (gate and up rows paired per
+      // tile), adapters, a = silu(gate) * up as planes; gate|up kept in f32 for
+      // the backward. (The dequantising GEMM has operand-feed headroom for the
+      // extra epilogue stores; the plane GEMM does not, so full fine-tunes keep
+      // SwiGLU as its own kernel.)
+      gg.epi = epi_rowmajor(kEpiSwiGLU, gu_[l], 2 * ff);
+      gg.epi.out_hi = a_[l].hi; gg.epi.out_lo = a_[l].lo; gg.epi.pair_off = ff;
+      if (lora && (c.lora_targets & (1 << kLoraGate))) {
+        CK(lora_prep(l, kLoraGate, h2_[l], d, ff));
+        gg.epi.lora[gg.epi.n_lora++] = lora_addend(l, kLoraGate, 0, ff);
+      }
+      if (lora && (c.lora_targets & (1 << kLoraUp))) {
+        CK(lora_prep(l, kLoraUp, h2_[l], d, ff));
+        gg.epi.lora[gg.epi.n_lora++] = lora_addend(l, kLoraUp, ff, ff);
+      }
+      CK(gemm(gg));
+    } else {
+      gg.epi = epi_rowmajor(kEpiStoreF32, gu_[l], 2 * ff);
+      CK(gemm(gg));
+      if (lora && (c.lora_targets & (1 << kLoraGate))) CK(lora_forward(l, kLoraGate, h2_[l], d, gu_[l], 2 * ff, 0, ff));
+      if (lora && (c.lora_targets & (1 << kLoraUp))) CK(lora_forward(l, kLoraUp, h2_[l], d, gu_[l], 2 * ff, ff, ff));
+      KL(launch_swiglu_fwd(gu_[l], a_[l], N, ff, stream_));
+    }
     GemmDesc gd;
     gd.M = N; gd.N = d; gd.K = ff;
     gd.a = op(a_[l], N, ff, ff, 0);
     gd.b = wop(P(pre + "ffn_down.weight"), d, ff, ff, 0);
     gd.epi = epi_rowmajor(kEpiResidF32, x_[l + 1], d);
     gd.epi.res = x1_[l];
+    if (lora && (c.lora_targets & (1 << kLoraDown))) {
+      CK(lora_prep(l, kLoraDown, a_[l], ff, d));
+      gd.epi.lora[gd.epi.n_lora++] = lora_addend(l, kLoraDown, 0, d);
+    }
     CK(gemm(gd));
-    if (lora && (c.lora_targets & (1 << kLoraDown))) CK(lora_forward(l, kLoraDown, a_[l], ff, x_[l + 1], d, 0, d));
   }
   KL(launch_rmsnorm_fwd(x_[c.n_layers], P32(P("output_norm.weight")), xf_, N, d, c.rms_eps, stream_));
   const Param& Wout = c.tied ? E : P("output.weight");

@@ -127,6 +127,8 @@ class LlamaEngine {
   int enqueue_step(bool run_optimizer);
   int gemm(const GemmDesc& d);
   int lora_forward(int l, int t, Planes X, int d_in, float* Y, long long ldy, int col_off, int d_out);
+  int lora_prep(int l, int t, Planes X, int d_in, int d_out);
+  LoraAddend lora_addend(int l, int t, int c0, int d_out) const;
   int lora_backward(int l, int t, Planes X, int d_in, Planes dY, long long ld_dy, int col_off, int d_out,
                     float* dX, const Epilogue* dx_scatter);
   float* P32(const Param& p) { return static_cast<float*>(p32_.p) + p.offset; }

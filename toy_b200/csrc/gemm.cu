@@ -188,7 +188,147 @@ __device__ __forceinline__ void epi_store(const Epilogue& e, int N, long long of
   }
 }
 
-template <int BN, bool SPLIT, bool Q8>
+// v(m, nc + i) += scale * sum_j u[m][j] * bt[j][nc + i - c0] for every LoRA
+// addend whose column range holds the chunk (ranges are multiples of 32). All
+// lanes of a warp read the same bt chunk (broadcast); u is the lane's own row.
+__device__ __forceinline__ void lora_add(const Epilogue& e, int m, int nc, float (&v)[32]) {
+#pragma unroll 1
+  for (int a = 0; a < e.n_lora; ++a) {
+    const LoraAddend& L = e.lora[a];
+    if (nc < L.c0 || nc >= L.c0 + L.width) continue;
+    const float* ur = L.u + (long long)m * L.r;
+    const float* bt = L.bt + (nc - L.c0);
+#pragma unroll 1
+    for (int j = 0; j < L.r; ++j) {
+      const float su = L.scale * ur[j];
+      const float4* b4 = reinterpret_cast<const float4*>(bt + (long long)j * L.width);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 w4 = __ldg(b4 + q);
+        v[4 * q] = fmaf(su, w4.x, v[4 * q]);
+        v[4 * q + 1] = fmaf(su, w4.y, v[4 * q + 1]);
+        v[4 * q + 2] = fmaf(su, w4.z, v[4 * q + 2]);
+        v[4 * q + 3] = fmaf(su, w4.w, v[4 * q + 3]);
+      }
+    }
+  }
+}
+
+// 32 values as hi / lo bf16 planes at 16-byte aligned addresses.
+__device__ __forceinline__ void store_split32(__nv_bfloat16* hi, __nv_bfloat16* lo, const float (&v)[32]) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) split_pair(v[8 * u + 2 * j], v[8 * u + 2 * j + 1], h[j], l[j]);
+    reinterpret_cast<uint4*>(hi)[u] = make_uint4(h[0], h[1], h[2], h[3]);
+    reinterpret_cast<uint4*>(lo)[u] = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
+
+__device__ __forceinline__ void release_acc(uint64_t* tempty, int lane) {
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(tempty);
+}
+
+// kEpiRopeQKV for one tile row: one head (NCH chunks of 32 columns) at a time --
+// LoRA addends, bias, RoPE rotation of q / k heads by pos[m], head-major planes.
+template <int BN, int NCH>
+__device__ __forceinline__ void epi_rope(const Epilogue& e, int m, int n0, bool row_ok, int N, uint32_t acc,
+                                         uint64_t* tempty, int lane) {
+  constexpr int DH = NCH * 32, HALF = DH / 2;
+  const RopeOut& R = e.rope;
+  int bq = 0, t = 0, p = 0;
+  if (row_ok) {
+    bq = m / R.T;
+    t = m - bq * R.T;
+    p = R.pos[m];
+    p = p < 0 ? 0 : (p >= R.tab_rows ? R.tab_rows - 1 : p);
+  }
+  const float2* crow = reinterpret_cast<const float2*>(R.cs) + (long long)p * HALF;
+#pragma unroll 1
+  for (int hb = 0; hb < BN; hb += DH) {
+    float v[NCH][32];
+#pragma unroll
+    for (int k = 0; k < NCH; ++k) tmem_ld32(acc + (uint32_t)(hb + 32 * k), v[k]);
+    if (hb + DH >= BN) release_acc(tempty, lane);
+    const int c0 = n0 + hb;
+    if (!row_ok || c0 >= N) continue;
+#pragma unroll
+    for (int k = 0; k < NCH; ++k) {
+      if (e.n_lora) lora_add(e, m, c0 + 32 * k, v[k]);
+      if (R.bias) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[k][i] += R.bias[c0 + 32 * k + i];
+      }
+    }
+    const int slot = c0 / DH;
+    __nv_bfloat16 *oh, *ol;
+    long long dst;
+    bool rot = true;
+    if (slot < R.H) {
+      dst = (((long long)bq * R.H + slot) * R.T + t) * DH;
+      oh = R.q_hi; ol = R.q_lo;
+    } else if (slot < R.H + R.KV) {
+      dst = (((long long)bq * R.KV + (slot - R.H)) * R.T + t) * DH;
+      oh = R.k_hi; ol = R.k_lo;
+    } else {
+      dst = (((long long)bq * R.KV + (slot - R.H - R.KV)) * R.T + t) * DH;
+      oh = R.v_hi; ol = R.v_lo;
+      rot = false;
+    }
+    if (rot) {
+      // pairs (j, j + dh/2): y0 = x0 cos - x1 sin, y1 = x0 sin + x1 cos
+#pragma unroll
+      for (int j = 0; j < HALF; ++j) {
+        const float2 c = crow[j];
+        const float x0 = v[j / 32][j % 32], x1 = v[(j + HALF) / 32][j % 32];
+        v[j / 32][j % 32] = x0 * c.x - x1 * c.y;
+        v[(j + HALF) / 32][j % 32] = x0 * c.y + x1 * c.x;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < NCH; ++k) store_split32(oh + dst + 32 * k, ol + dst + 32 * k, v[k]);
+  }
+}
+
+// kEpiSwiGLU for one tile row of a 128-wide tile with paired B rows: columns
+// [0, 64) are gate features n0/2 .., [64, 128) the same up features.
+template <int BN>
+__device__ __forceinline__ void epi_swiglu(const Epilogue& e, int m, int n0, bool row_ok, uint32_t acc,
+                                           uint64_t* tempty, int lane) {
+  const int ff = e.pair_off, f0 = n0 / 2;
+#pragma unroll 1
+  for (int k = 0; k < BN / 64; ++k) {
+    float g[32], u[32];
+    tmem_ld32(acc + (uint32_t)(32 * k), g);
+    tmem_ld32(acc + (uint32_t)(BN / 2 + 32 * k), u);
+    if (k == BN / 64 - 1) release_acc(tempty, lane);
+    const int fc = f0 + 32 * k;
+    if (!row_ok || fc >= ff) continue;
+    if (e.n_lora) {
+      lora_add(e, m, fc, g);        // gate columns [0, ff)
+      lora_add(e, m, ff + fc, u);   // up columns [ff, 2 ff)
+    }
+    float* orow = e.out + (long long)m * e.m_s0;
+    float4* og = reinterpret_cast<float4*>(orow + fc);
+    float4* ou = reinterpret_cast<float4*>(orow + ff + fc);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      og[i] = make_float4(g[4 * i], g[4 * i + 1], g[4 * i + 2], g[4 * i + 3]);
+      ou[i] = make_float4(u[4 * i], u[4 * i + 1], u[4 * i + 2], u[4 * i + 3]);
+    }
+    // silu with the hardware exp2 / reciprocal approximations (~1e-7 relative)
+#pragma unroll
+    for (int i = 0; i < 32; ++i) g[i] = __fdividef(g[i], 1.0f + __expf(-g[i])) * u[i];
+    store_split32(e.out_hi + (long long)m * ff + fc, e.out_lo + (long long)m * ff + fc, g);
+  }
+}
+
+// FUSED instantiations carry the fused epilogues (LoRA addends, RoPE / SwiGLU
+// modes); the others leave that code out so they keep their register budget.
+template <int BN, bool SPLIT, bool Q8, bool FUSED>
 __global__ void __launch_bounds__(threads_of<Q8>(), 1)
     gemm_split_bf16_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_constant__ CUtensorMap map_a_lo,
                            const __grid_constant__ CUtensorMap map_b_hi, const __grid_constant__ CUtensorMap map_b_lo,
@@ -276,11 +416,22 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
           if (Q8) {
             // int8 quants; map_b_hi is the quant map (box {64 bytes, rows})
             uint8_t* qd = st + 2 * (kTileA + kTileB);
-            if (!args.b_mn) {
+            if (args.epi.pair_off) {   // gate rows, then the matching up rows
+              tma_load_3d(qd, &map_b_hi, &full[s], k0, w.n0 / 2, 0);
+              tma_load_3d(qd + (BN / 2) * 64, &map_b_hi, &full[s], k0, args.epi.pair_off + w.n0 / 2, 0);
+            } else if (!args.b_mn) {
               tma_load_3d(qd, &map_b_hi, &full[s], k0, w.n0, 0);
             } else {
 #pragma unroll
               for (int j = 0; j < BN / 64; ++j) tma_load_3d(qd + j * 64 * 64, &map_b_hi, &full[s], w.n0 + 64 * j, k0, 0);
+            }
+          } else if (args.epi.pair_off) {   // gate rows, then the matching up rows
+            const int r0 = w.n0 / 2, r1 = args.epi.pair_off + w.n0 / 2;
+            tma_load_3d(b_hi, &map_b_hi, &full[s], k0, r0, zb);
+            tma_load_3d(b_hi + (BN / 2) * 128, &map_b_hi, &full[s], k0, r1, zb);
+            if (SPLIT) {
+              tma_load_3d(b_lo, &map_b_lo, &full[s], k0, r0, zb);
+              tma_load_3d(b_lo + (BN / 2) * 128, &map_b_lo, &full[s], k0, r1, zb);
             }
           } else if (!args.b_mn) {
             tma_load_3d(b_hi, &map_b_hi, &full[s], k0, w.n0, zb);
@@ -378,7 +529,8 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
             if (!args.b_mn) {   // tile rows = output columns n, 64 k
               r = i >> 1;
               src = qs + r * 64 + c32 * 32;
-              srow = w.n0 + r;
+              srow = !args.epi.pair_off ? w.n0 + r
+                                        : (r < BN / 2 ? w.n0 / 2 + r : args.epi.pair_off + w.n0 / 2 + r - BN / 2);
               sb = (k0 >> 5) + c32;
               tile = 0;
             } else {            // BN / 64 tiles of 64 k rows x 64 n
@@ -448,6 +600,16 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
       tc_fence_after();
       const bool row_ok = ok && row_in;
       const uint32_t acc_tmem = tmem_base + b * kAccCols + ((uint32_t)(q * 32) << 16);
+      if constexpr (FUSED) {
+        if (e.mode == kEpiRopeQKV) {
+          epi_rope<BN, 2>(e, m, w.n0, row_ok, args.N, acc_tmem, &tempty[b], lane);
+          continue;
+        }
+        if (e.mode == kEpiSwiGLU) {
+          if constexpr (BN == 128 || BN == 256) epi_swiglu<BN>(e, m, w.n0, row_ok, acc_tmem, &tempty[b], lane);
+          continue;
+        }
+      }
       // split-K partial of split s: plain row-major [M][N] slab s of the workspace
       float* part = args.ws + (long long)(u % args.splits) * args.M * args.N + (long long)m * args.N;
       // one 32-column chunk: drain TMEM, store (or write the partial); the
@@ -475,6 +637,9 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
         } else {
           if (c + 1 < BN / 32 && nc + 32 < args.N)
             epi_prefetch(e, args.N, rowoff + ((nc + 32) / e.n_div) * e.n_s1 + ((nc + 32) % e.n_div), nc + 32, next);
+          if constexpr (FUSED) {
+            if (e.n_lora) lora_add(e, m, nc, v);
+          }
           epi_store(e, args.N, rowoff + (nc / e.n_div) * e.n_s1 + (nc % e.n_div), nc, v, cur);
         }
       };
@@ -595,14 +760,21 @@ double estimate_us(const GemmDesc& d, int bn, int s) {
   if (d.causal == 2) kb = kb / 2 + 1;                          // K clamped at the diagonal, on average
   const double units = tiles * s;
   const double per_cta = std::ceil(units / kNumSMs);
-  const double t_mma = (d.split ? 3.0 : 1.0) * 2.0 * BM * bn * BK / kSmFlopsPerUs;
-  const double t_feed = (d.split ? 2.0 : 1.0) * (BM + bn) * BK * 2.0 / kSmOperandBytesPerUs;
-  const double t_kb = std::max(t_mma, t_feed);
   const bool reads_out = d.epi.mode == kEpiAccumF32 || d.epi.mode == kEpiResidF32;
+  // bytes the epilogue moves per output element: they share the SM's path to
+  // L2 with the operand tiles of the next unit's main loop
+  double out_b = (s == 1 && reads_out) ? 8.0 : 4.0;
+  if (d.epi.mode == kEpiStoreBoth) out_b = 8.0;
+  if (d.epi.mode == kEpiSwiGLU) out_b = 6.0;   // gate|up f32 + half of a feature's planes
+  const double tile_bytes = (double)BM * bn * out_b;
+  const double kb_unit = std::ceil((double)kb / s);
+  const double t_mma = (d.split ? 3.0 : 1.0) * 2.0 * BM * bn * BK / kSmFlopsPerUs;
+  const double t_feed =
+      ((d.split ? 2.0 : 1.0) * (BM + bn) * BK * 2.0 + tile_bytes / kb_unit) / kSmOperandBytesPerUs;
+  const double t_kb = std::max(t_mma, t_feed);
   const double active = units < kNumSMs ? units : (double)kNumSMs;
   const double drain_bw = std::min(100.0e3, 6.5e6 / active);   // bytes per us per CTA
-  const double tile_bytes = (double)BM * bn * 4.0 * (s == 1 && reads_out ? 2.0 : 1.0);
-  double t = 1.2 + per_cta * (std::ceil((double)kb / s) * t_kb + 0.5) + tile_bytes / drain_bw;
+  double t = 1.2 + per_cta * (kb_unit * t_kb + 0.5) + tile_bytes / drain_bw;
   if (s > 1) t += ((s + 1.0) * d.M * d.N * 4.0 + (reads_out ? d.M * d.N * 4.0 : 0.0)) / 5.0e6 + 2.5;
   return t;
 }
@@ -614,14 +786,19 @@ struct Plan {
 Plan choose_plan(const GemmDesc& d, long long ws_floats, bool q8) {
   static const int kBn[] = {64, 128, 192, 256};
   const int kb = (d.K + BK - 1) / BK;
-  const bool can_split = !d.causal && d.batch == 1 && ws_floats > 0;
+  // fused epilogues act on whole output rows of a tile: no K splits
+  const bool fused = d.epi.mode == kEpiRopeQKV || d.epi.mode == kEpiSwiGLU || d.epi.n_lora > 0;
+  const bool can_split = !d.causal && d.batch == 1 && ws_floats > 0 && !fused;
   Plan best;
   double best_t = 1e30;
   for (int bn : kBn) {
     if (q8 && bn > 128) break;
     if (bn > 64 && bn - 64 >= d.N) break;   // a narrower tile already covers N
+    if (d.epi.mode == kEpiSwiGLU && bn != 128 && bn != 256) continue;   // BN/2 gate + BN/2 up columns
+    if (d.epi.mode == kEpiSwiGLU && q8 && bn != 128) continue;
+    if (d.epi.mode == kEpiRopeQKV && bn % d.epi.rope.dh) continue;       // whole heads per tile
     int s_lo = 1, s_hi = 1;
-    if (d.splits > 0) {
+    if (d.splits > 0 && !fused) {
       s_lo = s_hi = d.splits;
     } else if (can_split && kb >= 8) {
       s_hi = std::min(16, kb / 2);
@@ -639,19 +816,19 @@ Plan choose_plan(const GemmDesc& d, long long ws_floats, bool q8) {
   return best;
 }
 
-template <int BN, bool SPLIT, bool Q8 = false>
+template <int BN, bool SPLIT, bool Q8 = false, bool FUSED = false>
 int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream_t stream, int splits) {
   using S = Stages<BN, SPLIT, Q8>;
   static bool attr_set = false;
   if (!attr_set) {
-    if (cudaFuncSetAttribute(gemm_split_bf16_kernel<BN, SPLIT, Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(gemm_split_bf16_kernel<BN, SPLIT, Q8, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              S::kSmemBytes) != cudaSuccess)
       return -20;
     attr_set = true;
   }
   CUtensorMap ma_hi, ma_lo, mb_hi, mb_lo;
   const int a_box = d.a.mn_major ? 64 : BM;
-  const int b_box = d.b.mn_major ? 64 : BN;
+  const int b_box = d.epi.pair_off ? BN / 2 : (d.b.mn_major ? 64 : BN);
   int rc;
   if ((rc = make_map(&ma_hi, d.a.hi, d.a, a_box))) return rc;
   if (Q8) {
@@ -692,7 +869,7 @@ int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream
   k.q8_rows = d.b.rows;
   k.q8_cols = d.b.cols;
   const int grid = k.units < kNumSMs ? k.units : kNumSMs;
-  if (launch_pdl(gemm_split_bf16_kernel<BN, SPLIT, Q8>, dim3(grid), dim3(threads_of<Q8>()), S::kSmemBytes, stream,
+  if (launch_pdl(gemm_split_bf16_kernel<BN, SPLIT, Q8, FUSED>, dim3(grid), dim3(threads_of<Q8>()), S::kSmemBytes, stream,
                  ma_hi, ma_lo, mb_hi, mb_lo, k) != 0)
     return -21;
   if (splits > 1) {
@@ -719,16 +896,50 @@ int gemm_launch(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStre
   const int al = (e.mode == kEpiStoreSplit || e.mode == kEpiStoreBoth) ? 8 : 4;
   if ((e.m_s0 % al) || (e.m_s1 % al) || (e.n_s1 % al) || (e.bstride % al) || (e.z_s1 % al) || (e.n_div % 32))
     return -3;
+  if (e.n_lora < 0 || e.n_lora > kMaxLoraAddends || (e.n_lora && e.alpha != 1.0f)) return -3;
+  for (int i = 0; i < e.n_lora; ++i) {
+    const LoraAddend& L = e.lora[i];
+    if (!L.u || !L.bt || L.r < 1 || L.c0 % 32 || L.width % 32 || L.c0 + L.width > d.N ||
+        (reinterpret_cast<uintptr_t>(L.bt) & 15))
+      return -3;
+  }
+  if (e.mode == kEpiRopeQKV) {
+    const RopeOut& R = e.rope;
+    if ((R.dh != 64 && R.dh != 128) || d.N != (R.H + 2 * R.KV) * R.dh || d.M % R.T || !R.pos || !R.cs ||
+        !R.q_hi || !R.q_lo || !R.k_hi || !R.k_lo || !R.v_hi || !R.v_lo || d.batch != 1)
+      return -3;
+  }
+  if (e.mode == kEpiSwiGLU) {
+    if (e.pair_off <= 0 || d.N != 2 * e.pair_off || e.pair_off % 64 || d.b.mn_major || d.batch != 1 || !e.out ||
+        !e.out_hi || !e.out_lo || e.m_s0 != 2LL * e.pair_off)
+      return -3;
+  } else if (e.pair_off) {
+    return -3;
+  }
+  if (e.mode == kEpiRopeQKV && e.rope.dh != 64) return -3;
+  const bool fused = e.mode == kEpiRopeQKV || e.mode == kEpiSwiGLU || e.n_lora > 0;
+  if (fused && !d.split) return -3;
   const Plan pl = choose_plan(d, sc.ws ? sc.ws_floats : 0, d.b.q8 != nullptr);
   if (d.b.q8) {
     // Q8_0 B: dequantised in shared memory into split planes; 64 / 128-wide tiles
     // keep three stages of A planes + B planes + quants within shared memory
     if (!d.split || d.batch != 1 || !d.b.q8_scale || d.b.cols % 32 || !d.a.hi || !d.a.lo) return -4;
+    if (fused)
+      return pl.bn <= 64 ? launch_bn<64, true, true, true>(d, sc, dev_err, stream, pl.splits)
+                         : launch_bn<128, true, true, true>(d, sc, dev_err, stream, pl.splits);
     return pl.bn <= 64 ? launch_bn<64, true, true>(d, sc, dev_err, stream, pl.splits)
                        : launch_bn<128, true, true>(d, sc, dev_err, stream, pl.splits);
   }
   if (!d.a.hi || !d.b.hi || (d.split && (!d.a.lo || !d.b.lo))) return -4;
   const int sp = pl.splits;
+  if (fused) {
+    switch (pl.bn) {
+      case 64: return launch_bn<64, true, false, true>(d, sc, dev_err, stream, sp);
+      case 128: return launch_bn<128, true, false, true>(d, sc, dev_err, stream, sp);
+      case 192: return launch_bn<192, true, false, true>(d, sc, dev_err, stream, sp);
+      default: return launch_bn<256, true, false, true>(d, sc, dev_err, stream, sp);
+    }
+  }
   switch (pl.bn) {
     case 64:
       return d.split ? launch_bn<64, true>(d, sc, dev_err, stream, sp) : launch_bn<64, false>(d, sc, dev_err, stream, sp);

@@ -48,6 +48,33 @@ enum EpiMode : int {
   kEpiResidF32 = 2,   // out = res + alpha * acc
   kEpiStoreSplit = 3, // (out_hi, out_lo) = split(alpha * acc)
   kEpiStoreBoth = 4,  // out = alpha * acc and (out_hi, out_lo) = split(alpha * acc)
+  kEpiRopeQKV = 5,    // fused q|k|v projection: + bias, RoPE (NEOX) on q and k, head-major planes (Epilogue::rope)
+  kEpiSwiGLU = 6,     // fused gate|up projection with paired B rows: out = gate|up f32, (out_hi, out_lo) = silu(g) u
+};
+
+// Low-rank adapter added to the accumulator before the epilogue mode (the
+// LoRA splice y += s B (A x) of the base projection): for the output columns
+// [c0, c0 + width) (multiples of 32), v(m, c) += scale * sum_j u[m][j] * bt[j][c - c0],
+// with u = A x saved as f32 [M][r] and bt = B^T as f32 [r][width].
+struct LoraAddend {
+  const float* u = nullptr;
+  const float* bt = nullptr;
+  int c0 = 0, width = 0, r = 0;
+  float scale = 0.f;
+};
+constexpr int kMaxLoraAddends = 3;
+
+// kEpiRopeQKV: the output columns are the (H + 2 KV) heads of width dh of one
+// token (row m = b * T + t); after bias the q and k heads are rotated by the
+// RoPE angle of pos[m] (cos / sin table cs [tab_rows][dh / 2] of float2) and
+// every head is written as planes to Q [B][H][T][dh], K and V [B][KV][T][dh].
+struct RopeOut {
+  const int* pos = nullptr;
+  const float* cs = nullptr;
+  int tab_rows = 0;
+  const float* bias = nullptr;
+  __nv_bfloat16 *q_hi = nullptr, *q_lo = nullptr, *k_hi = nullptr, *k_lo = nullptr, *v_hi = nullptr, *v_lo = nullptr;
+  int T = 1, H = 0, KV = 0, dh = 64;
 };
 
 // Output element (z, m, n) lives at
@@ -69,6 +96,15 @@ struct Epilogue {
   long long m_s1 = 0, m_s0 = 0;
   int n_div = 1 << 30;
   long long n_s1 = 0;
+  // fused extras (kEpiStoreF32 / AccumF32 / ResidF32 / RopeQKV / SwiGLU, no K splits)
+  int n_lora = 0;
+  LoraAddend lora[kMaxLoraAddends];
+  RopeOut rope;
+  // kEpiSwiGLU: B rows are paired -- tile columns [0, BN/2) are gate rows
+  // n0/2 .., [BN/2, BN) the matching up rows pair_off + n0/2 .. (pair_off = ff);
+  // out (f32 [M][2 ff], m_s0 = 2 ff) keeps gate | up for the backward and
+  // (out_hi, out_lo) ([M][ff]) get silu(gate) * up.
+  int pair_off = 0;
 };
 
 struct GemmDesc {
