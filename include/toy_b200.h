@@ -243,12 +243,103 @@ int tb2_dp_set_bucket_floats(void *sess, long long floats);
 /* Releases the step graph (which holds NCCL work) and then the communicator. */
 int tb2_dp_free(void *sess);
 
-/* tinynn/tinynn_ggml.h:424 — the next tnn_compute_backward zeroes the Adam moments. */
+/* tinynn/tinynn_ggml.h:424 — the next tnn_compute_backward zeroes the Adam moments
+ * (of the step program, or of every tnn_opt_step_adamw node of a primitive graph). */
 int tnn_graph_reset(void *sess);
 /* tinynn/tinynn_ggml.h:419 — gradients are overwritten by every backward; no-op. */
 int tnn_graph_reset_grads_only(void *sess);
-/* tinynn/tinynn_ggml.h:425 — forward, CE, backward and AdamW in one call. */
+/* tinynn/tinynn_ggml.h:425 — forward, CE, backward and AdamW in one call: the
+ * fused step program after tb2_llama_realize, or the primitive graph built
+ * with the calls below. */
 int tnn_compute_backward(void *sess);
+
+/* ===================================================================== */
+/* Primitive op graph (tinynn/tinynn_ggml.h:97-469): the same calls toy's */
+/* graph builders make. Tensors use ggml's shape convention (ne0 fastest; */
+/* a "rows x cols" input has ne0 = cols). Ops return NULL on a shape or   */
+/* type mismatch; nodes run at tnn_compute / tnn_compute_backward.        */
+/* Supported: f32, i32 and Q8_0 (type 8) tensors; RoPE in NEOX mode       */
+/* without YaRN (ext_factor 0); soft_max_ext without ALiBi (max_bias 0). */
+/* A session uses either this graph or the fused step program.           */
+/* ===================================================================== */
+/* tinynn_ggml.h:97-141,303-308,394,455 */
+void *tnn_input_1d_f32(void *sess, int n);
+void *tnn_input_2d_f32(void *sess, int rows, int cols);
+void *tnn_input_2d_f32_persistent(void *sess, int rows, int cols);
+void *tnn_input_1d_f32_persistent(void *sess, int n);
+void *tnn_input_3d_f32_persistent(void *sess, int ne0, int ne1, int ne2);
+void *tnn_input_4d_f32_persistent(void *sess, int ne0, int ne1, int ne2, int ne3);
+void *tnn_input_2d_persistent_typed(void *sess, int rows, int cols, int ggml_type);
+void *tnn_input_1d_i32(void *sess, int n);
+void *tnn_input_1d_i32_ctx(void *sess, int n);
+void *tnn_rope_freq_factors_alloc(void *sess, int n_dims);
+long tnn_row_size(int ggml_type, int ne0);
+int tnn_finalize_weights(void *sess);
+int tnn_session_set_graph_capacity(void *sess, int capacity);
+int tnn_zero_tensor(void *sess, void *tensor);
+/* Q8_0 blocks copied verbatim into a type-8 tensor (the bytes tinynn_gguf.c:634-682
+ * copies from a GGUF file). No reference counterpart as a single call. */
+int tnn_upload_q8_0_blocks(void *sess, void *tensor, const void *blocks, size_t nbytes);
+
+/* tinynn_ggml.h:157-400 — forward and backward ops */
+void *tnn_matmul(void *sess, void *a, void *b);          /* ggml_mul_mat: a [K,M,..] (f32 or Q8_0), b [K,N,..] -> [M,N,..] */
+void *tnn_out_prod(void *sess, void *a, void *b);        /* ggml_out_prod: r[n][m] = sum_k a[k][m] b[k][n] */
+void *tnn_add(void *sess, void *a, void *b);             /* b broadcast over a */
+void *tnn_sub(void *sess, void *a, void *b);
+void *tnn_mul(void *sess, void *a, void *b);
+void *tnn_scale(void *sess, void *a, double s);
+void *tnn_silu(void *sess, void *a);
+void *tnn_silu_back(void *sess, void *x, void *dy);
+void *tnn_swiglu_split(void *sess, void *gate, void *up);
+void *tnn_rms_norm(void *sess, void *x, void *gamma_row, double eps);
+void *tnn_rms_norm_back(void *sess, void *x, void *dy, double eps);
+void *tnn_rope_ext(void *sess, void *a, void *pos, int n_dims, double freq_base, double freq_scale,
+                   double ext_factor, double attn_factor, double beta_fast, double beta_slow, void *freq_factors);
+void *tnn_rope_ext_back(void *sess, void *dy, void *pos, int n_dims, double freq_base, double freq_scale,
+                        double ext_factor, double attn_factor, double beta_fast, double beta_slow,
+                        void *freq_factors);
+void *tnn_softmax(void *sess, void *a);
+void *tnn_soft_max_ext(void *sess, void *a, void *mask, double scale, double max_bias);
+void *tnn_softmax_back(void *sess, void *a, void *dy);
+void *tnn_diag_mask_inf(void *sess, void *a, int n_past);
+void *tnn_transpose(void *sess, void *a);
+void *tnn_permute(void *sess, void *a, int axis0, int axis1, int axis2, int axis3);
+void *tnn_cont(void *sess, void *a);
+void *tnn_cont_2d(void *sess, void *a, int ne0, int ne1);
+void *tnn_reshape_2d(void *sess, void *a, int ne0, int ne1);
+void *tnn_reshape_3d(void *sess, void *a, int ne0, int ne1, int ne2);
+void *tnn_view_1d(void *sess, void *a, int ne0, long offset);
+void *tnn_view_2d(void *sess, void *a, int ne0, int ne1, long nb1, long offset);
+void *tnn_view_3d(void *sess, void *a, int ne0, int ne1, int ne2, long nb1, long nb2, long offset);
+void *tnn_concat(void *sess, void *a, void *b, int dim);
+void *tnn_get_rows(void *sess, void *table, void *idx);
+void *tnn_get_rows_back(void *sess, void *d_out, void *idx, void *table_shape);
+void *tnn_cross_entropy_loss(void *sess, void *a, void *b);
+void *tnn_sum(void *sess, void *a);
+void *tnn_sum_rows(void *sess, void *a);
+void *tnn_opt_step_adamw(void *sess, void *a, void *grad, void *m, void *v, void *params);
+
+/* tinynn_ggml.h:376-469 — programs and autograd */
+void tnn_set_param(void *tensor);
+void tnn_set_loss(void *tensor);
+void tnn_set_output(void *tensor);
+int tnn_add_to_graph(void *sess, void *tensor);
+int tnn_realize(void *sess, void *result);
+int tnn_build_forward_only(void *sess, void *result);
+int tnn_build_backward(void *sess);
+int tnn_extend_backward_graph(void *sess, void *node);
+int tnn_realize_backward(void *sess);
+void *tnn_tensor_grad(void *sess, void *tensor);
+int tnn_compute(void *sess);
+int tnn_reset_for_rebuild(void *sess);
+
+/* tinynn_ggml.h:527-532 — graph introspection */
+int tnn_tensor_op(void *t);
+const char *tnn_tensor_op_name(void *t);
+void *tnn_tensor_src(void *t, int i);
+int tnn_tensor_flags(void *t);
+int tnn_graph_n_nodes(void *sess);
+void *tnn_graph_node(void *sess, int i);
 
 /* ===================================================================== */
 /* Tensor I/O (tinynn/tinynn_ggml.h:486-537)                             */

@@ -96,6 +96,73 @@ _SIGS = [
     ("tb2_q8_0_dequantize", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_longlong, C.c_int,
                                       C.c_void_p]),
     ("tb2_version", C.c_char_p, []),
+    # primitive op graph
+    ("tnn_input_1d_f32", VP, [VP, I]),
+    ("tnn_input_2d_f32", VP, [VP, I, I]),
+    ("tnn_input_2d_f32_persistent", VP, [VP, I, I]),
+    ("tnn_input_1d_f32_persistent", VP, [VP, I]),
+    ("tnn_input_3d_f32_persistent", VP, [VP, I, I, I]),
+    ("tnn_input_4d_f32_persistent", VP, [VP, I, I, I, I]),
+    ("tnn_input_2d_persistent_typed", VP, [VP, I, I, I]),
+    ("tnn_input_1d_i32", VP, [VP, I]),
+    ("tnn_input_1d_i32_ctx", VP, [VP, I]),
+    ("tnn_rope_freq_factors_alloc", VP, [VP, I]),
+    ("tnn_row_size", C.c_long, [I, I]),
+    ("tnn_finalize_weights", I, [VP]),
+    ("tnn_session_set_graph_capacity", I, [VP, I]),
+    ("tnn_zero_tensor", I, [VP, VP]),
+    ("tnn_upload_q8_0_blocks", I, [VP, VP, VP, SZ]),
+    ("tnn_matmul", VP, [VP, VP, VP]),
+    ("tnn_out_prod", VP, [VP, VP, VP]),
+    ("tnn_add", VP, [VP, VP, VP]),
+    ("tnn_sub", VP, [VP, VP, VP]),
+    ("tnn_mul", VP, [VP, VP, VP]),
+    ("tnn_scale", VP, [VP, VP, D]),
+    ("tnn_silu", VP, [VP, VP]),
+    ("tnn_silu_back", VP, [VP, VP, VP]),
+    ("tnn_swiglu_split", VP, [VP, VP, VP]),
+    ("tnn_rms_norm", VP, [VP, VP, VP, D]),
+    ("tnn_rms_norm_back", VP, [VP, VP, VP, D]),
+    ("tnn_rope_ext", VP, [VP, VP, VP, I, D, D, D, D, D, D, VP]),
+    ("tnn_rope_ext_back", VP, [VP, VP, VP, I, D, D, D, D, D, D, VP]),
+    ("tnn_softmax", VP, [VP, VP]),
+    ("tnn_soft_max_ext", VP, [VP, VP, VP, D, D]),
+    ("tnn_softmax_back", VP, [VP, VP, VP]),
+    ("tnn_diag_mask_inf", VP, [VP, VP, I]),
+    ("tnn_transpose", VP, [VP, VP]),
+    ("tnn_permute", VP, [VP, VP, I, I, I, I]),
+    ("tnn_cont", VP, [VP, VP]),
+    ("tnn_cont_2d", VP, [VP, VP, I, I]),
+    ("tnn_reshape_2d", VP, [VP, VP, I, I]),
+    ("tnn_reshape_3d", VP, [VP, VP, I, I, I]),
+    ("tnn_view_1d", VP, [VP, VP, I, C.c_long]),
+    ("tnn_view_2d", VP, [VP, VP, I, I, C.c_long, C.c_long]),
+    ("tnn_view_3d", VP, [VP, VP, I, I, I, C.c_long, C.c_long, C.c_long]),
+    ("tnn_concat", VP, [VP, VP, VP, I]),
+    ("tnn_get_rows", VP, [VP, VP, VP]),
+    ("tnn_get_rows_back", VP, [VP, VP, VP, VP]),
+    ("tnn_cross_entropy_loss", VP, [VP, VP, VP]),
+    ("tnn_sum", VP, [VP, VP]),
+    ("tnn_sum_rows", VP, [VP, VP]),
+    ("tnn_opt_step_adamw", VP, [VP, VP, VP, VP, VP, VP]),
+    ("tnn_set_param", None, [VP]),
+    ("tnn_set_loss", None, [VP]),
+    ("tnn_set_output", None, [VP]),
+    ("tnn_add_to_graph", I, [VP, VP]),
+    ("tnn_realize", I, [VP, VP]),
+    ("tnn_build_forward_only", I, [VP, VP]),
+    ("tnn_build_backward", I, [VP]),
+    ("tnn_extend_backward_graph", I, [VP, VP]),
+    ("tnn_realize_backward", I, [VP]),
+    ("tnn_tensor_grad", VP, [VP, VP]),
+    ("tnn_compute", I, [VP]),
+    ("tnn_reset_for_rebuild", I, [VP]),
+    ("tnn_tensor_op", I, [VP]),
+    ("tnn_tensor_op_name", C.c_char_p, [VP]),
+    ("tnn_tensor_src", VP, [VP, I]),
+    ("tnn_tensor_flags", I, [VP]),
+    ("tnn_graph_n_nodes", I, [VP]),
+    ("tnn_graph_node", VP, [VP, I]),
 ]
 
 

@@ -221,21 +221,23 @@ int tb2_sync(void* sess) {
 // ------------------------------------------------------------------ step (tnn_* drop-ins)
 int tnn_graph_reset(void* sess) {
   if (!sess) return -1;
-  if (!S(sess)->eng) return -2;
+  if (!S(sess)->eng) {   // primitive graph: zero the optimizer moments at the next backward
+    S(sess)->reset_pending = true;
+    return 0;
+  }
   S(sess)->first_pending = true;
   return 0;
 }
 
 int tnn_graph_reset_grads_only(void* sess) {
   if (!sess) return -1;
-  if (!S(sess)->eng) return -2;
-  return 0;  // every gradient element is overwritten by the next backward
+  return 0;  // every gradient element is overwritten by the next backward (both programs)
 }
 
 int tnn_compute_backward(void* sess) {
   if (!sess) return -1;
   Session* s = S(sess);
-  if (!s->eng) return -2;
+  if (!s->eng) return s->bwd_built ? tb2::prim_compute_backward(s) : -2;
   const bool first = s->first_pending;
   s->first_pending = false;
   return s->eng->step(first, true);

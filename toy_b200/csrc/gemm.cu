@@ -625,7 +625,7 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
         const int nc = w.n0 + c * 32;
         if (!row_ok || nc >= args.N) return;
         if (!direct) {
-          if (nc + 32 <= args.N) {
+          if (nc + 32 <= args.N && (args.N & 3) == 0) {   // float4 stores need 16-byte aligned rows
             float4* p4 = reinterpret_cast<float4*>(part + nc);
 #pragma unroll
             for (int i = 0; i < 8; ++i) p4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);

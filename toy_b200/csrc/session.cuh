@@ -30,14 +30,23 @@ struct Tensor {
   void* data = nullptr;     // device buffer (owned unless view_of is set)
   size_t bytes = 0;
   int op = 0;               // 0 = leaf
-  Tensor* src[4] = {nullptr, nullptr, nullptr, nullptr};
+  Tensor* src[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
   double fp[12] = {0};
   int ip[4] = {0};
   bool persistent = false;
   bool is_param = false;
   bool is_output = false;
   Tensor* view_of = nullptr;
+  // primitive graph extras
+  size_t view_off = 0;       // aliasing view: byte offset into view_of's buffer
+  Tensor* grad = nullptr;    // autograd: the node holding d loss / d this
+  bool is_loss = false;
+  void* q8v = nullptr;       // Q8_0 tensor: int8 quants [rows][ne0]
+  void* q8s = nullptr;       //              fp16 scale bits [rows][ne0 / 32]
+  void* planes = nullptr;    // split-bf16 copy of a GEMM operand (hi then lo)
+  void* outpad = nullptr;    // GEMM result with its rows padded to 4 floats (when ne0 % 4)
   long long nel() const { return (long long)ne[0] * ne[1] * ne[2] * ne[3]; }
+  long long rows() const { return (long long)ne[1] * ne[2] * ne[3]; }
 };
 
 struct Session {
@@ -49,8 +58,15 @@ struct Session {
   bool first_pending = false;
   DpState* dp = nullptr;
   // primitive op graph
-  std::vector<Tensor*> nodes;
+  std::vector<Tensor*> nodes;     // forward program (topological order)
+  std::vector<Tensor*> bwd;       // backward program (creation order)
+  std::vector<Tensor*> ext;       // appended nodes (optimizer steps)
+  std::vector<Tensor*> roots;     // extra forward roots (tnn_add_to_graph / outputs)
+  Tensor* loss = nullptr;
+  Tensor* ones = nullptr;         // d loss / d loss
   bool prim_realized = false;
+  bool bwd_built = false;
+  bool reset_pending = false;     // zero optimizer moments at the next backward
   cudaStream_t pstream = nullptr;
   ~Session();
 };
