@@ -100,6 +100,17 @@ int tb2_gemm(int M, int N, int K, int batch, int split, const tb2_operand *a, co
 int tb2_gemm_noalloc(int M, int N, int K, int batch, int split, const tb2_operand *a, const tb2_operand *b,
                      const tb2_epilogue *epi, int ksplits, int causal, void *stream);
 
+/* Tile scheduling of every GEMM this library launches: mode 1 runs each GEMM
+ * whose shape allows it (split planes, no causal mode) on CTA pairs -- two
+ * CTAs on neighbouring SMs sharing one 256-row tensor-core tile
+ * (tcgen05 cta_group::2), each holding half of the B tile; 0 never (single
+ * CTAs); -1 (the default) only the shapes where pairs measured faster (both
+ * operands K-major and N >= 2048: the LM head and the gate|up projections).
+ * Results are the same sums in the same order either way. No counterpart in
+ * the reference.
+ * Returns 0, or -1 for an unknown mode. */
+int tb2_gemm_set_pair_mode(int mode);
+
 /* hi = rn_bf16(x), lo = rn_bf16(x - hi) for n f32 values. */
 int tb2_split_f32(const float *x, void *hi, void *lo, size_t n, void *stream);
 

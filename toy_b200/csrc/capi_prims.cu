@@ -57,6 +57,8 @@ int tb2_gemm(int M, int N, int K, int batch, int split, const tb2_operand* a, co
   return rc == 0 ? 0 : (rc <= -10 ? -3 : -1);
 }
 
+int tb2_gemm_set_pair_mode(int mode) { return tb2::gemm_set_pair_mode(mode); }
+
 int tb2_split_f32(const float* x, void* hi, void* lo, size_t n, void* stream) {
   if (!x || !hi || !lo) return -1;
   return tb2::launch_split_f32(x, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo), (long long)n,

@@ -369,7 +369,8 @@ int LlamaEngine::realize() {
   dqkv_ = pl((long long)N * W);
   if (!full) {
     du32_ = f32((long long)N * r);
-    lora_part_ = f32(lora_wgrad_partial_floats(N, std::max(std::max(d, ff), H * dh), r));
+    lora_part_ = f32(std::max(lora_wgrad_partial_floats(N, std::max(std::max(d, ff), H * dh), r),
+                              lora_bwd_partial_floats(N, std::max(ff, H * dh), d, r)));
   }
   hp_ = f32(8);
   bufs_.emplace_back();
@@ -753,8 +754,9 @@ int LlamaEngine::lora_prep(int l, int t, Planes X, int d_in, int d_out) {
   const LlamaConfig& c = cfg_;
   const int N = this->N(), r = c.lora_rank;
   const std::string pre = "blk." + std::to_string(l) + "." + kProjName[t];
-  KL(launch_lora_transpose(P32(P(pre + ".lora_b")), d_out, r, lora_bt_[l][t], stream_));
-  KL(launch_lora_down(X, d_in, N, d_in, P32(P(pre + ".lora_a")), r, 1.0f, lora_u_[l][t], stream_));
+  // u = X A^T, and B^T for the splice in the same launch
+  KL(launch_lora_down(X, d_in, N, d_in, P32(P(pre + ".lora_a")), r, 1.0f, lora_u_[l][t], stream_,
+                      P32(P(pre + ".lora_b")), d_out, lora_bt_[l][t]));
   return 0;
 }
 
@@ -792,6 +794,12 @@ int LlamaEngine::lora_backward(int l, int t, Planes X, int d_in, Planes dY, long
   const float* u = lora_u_[l][t];
   const float* bt = lora_bt_[l][t];
   Planes dYo = offset(dY, col_off);
+  Epilogue e = dx_scatter ? *dx_scatter : epi_rowmajor(kEpiAccumF32, dX, d_in);
+  if (r <= kLoraBwdMaxRank) {   // one fused pass over dY and X, then the fixed-order chunk reduction
+    KL(launch_lora_backward(dYo, ld_dy, d_out, X, d_in, d_in, u, bt, P32(A), r, s, N, e, du32_, lora_part_, G32(Bp),
+                            G32(A), stream_));
+    return 0;
+  }
   // dB = s * dY^T u   [d_out][r]
   KL(launch_lora_wgrad(dYo, ld_dy, u, N, d_out, r, s, G32(Bp), r, 1, lora_part_, stream_));
   // du = s * dY B   [N][r]
@@ -799,7 +807,6 @@ int LlamaEngine::lora_backward(int l, int t, Planes X, int d_in, Planes dY, long
   // dA = du^T X   [r][d_in]
   KL(launch_lora_wgrad(X, d_in, du32_, N, d_in, r, 1.0f, G32(A), 1, d_in, lora_part_, stream_));
   // dX += du A   [N][d_in]
-  Epilogue e = dx_scatter ? *dx_scatter : epi_rowmajor(kEpiAccumF32, dX, d_in);
   KL(launch_lora_up(du32_, N, r, P32(A), d_in, 1.0f, e, stream_));
   return 0;
 }

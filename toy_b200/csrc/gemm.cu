@@ -62,22 +62,26 @@ __device__ __forceinline__ int batch_index(int z, int d1, int m1, int d2, int m2
   return (z / d1) * m1 + ((z % d1) / d2) * m2;
 }
 
-template <int BN>
+template <int BN, bool PAIR = false>
 struct Cfg {
+  static constexpr int kRowsB = PAIR ? BN / 2 : BN;   // B rows in this CTA's shared memory
   static constexpr int kTileA = BM * BK * 2;  // bytes per plane
-  static constexpr int kTileB = BN * BK * 2;
+  static constexpr int kTileB = kRowsB * BK * 2;
   static constexpr uint32_t kAccCols = BN <= 64 ? 64 : BN <= 128 ? 128 : 256;  // one accumulator
   static constexpr uint32_t kTmemCols = 2 * kAccCols;                           // double buffered
 };
 
 // A stage holds the A and B plane tiles and, for a Q8_0 B operand, the int8
-// quant tile the converters read (BN rows x 64 bytes, or BN / 64 blocks of
-// 64 x 64 bytes when B is MN-major). TMA fills A and the quants (kTxBytes).
-template <int BN, bool SPLIT, bool Q8 = false>
+// quant tile the converters read (B rows x 64 bytes, or B rows / 64 blocks of
+// 64 x 64 bytes when B is MN-major). kTxBytes is what the `full` barrier
+// counts: the planes TMA writes (of both CTAs of a pair). Quants count on a
+// per-CTA `qfull` barrier, so the converters start as soon as they land.
+template <int BN, bool SPLIT, bool Q8 = false, bool PAIR = false>
 struct Stages {
-  static constexpr int kQBytes = Q8 ? BN * 64 : 0;
-  static constexpr int kStageBytes = (SPLIT ? 2 : 1) * (Cfg<BN>::kTileA + Cfg<BN>::kTileB) + kQBytes;
-  static constexpr int kTxBytes = Q8 ? 2 * Cfg<BN>::kTileA + kQBytes : kStageBytes;
+  using C = Cfg<BN, PAIR>;
+  static constexpr int kQBytes = Q8 ? C::kRowsB * 64 : 0;
+  static constexpr int kStageBytes = (SPLIT ? 2 : 1) * (C::kTileA + C::kTileB) + kQBytes;
+  static constexpr int kTxBytes = (PAIR ? 2 : 1) * (Q8 ? 2 * C::kTileA : kStageBytes);
   static constexpr int kBudget = Q8 ? 216 * 1024 : kSmemBudget;
   static constexpr int kStages = (kBudget / kStageBytes) > 6 ? 6 : (kBudget / kStageBytes);
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align slack*/ + 256 /*barriers*/;
@@ -88,7 +92,9 @@ struct Unit {
   bool skip;
 };
 
-template <int BN>
+// unit u -> (batch, first output row, first output column, K range); a unit
+// covers BMT rows (BM, or 2 BM for a CTA pair)
+template <int BN, int BMT = BM>
 __device__ __forceinline__ Unit decode(const KArgs& a, int u) {
   Unit r;
   const int s = u % a.splits;
@@ -96,7 +102,7 @@ __device__ __forceinline__ Unit decode(const KArgs& a, int u) {
   r.tile = t;
   r.n0 = (t % a.tiles_n) * BN;
   t /= a.tiles_n;
-  r.m0 = (t % a.tiles_m) * BM;
+  r.m0 = (t % a.tiles_m) * BMT;
   r.z = t / a.tiles_m;
   r.skip = a.causal == 1 && r.n0 > r.m0 + BM - 1;
   int kbt = a.kb_total;
@@ -226,15 +232,21 @@ __device__ __forceinline__ void store_split32(__nv_bfloat16* hi, __nv_bfloat16* 
   }
 }
 
+// The warp has read its accumulator lanes: hand the accumulator back to the
+// MMA issuer (rank 0's barrier for a CTA pair).
+template <bool PAIR>
 __device__ __forceinline__ void release_acc(uint64_t* tempty, int lane) {
   tc_fence_before();
   __syncwarp();
-  if (lane == 0) mbar_arrive(tempty);
+  if (lane == 0) {
+    if constexpr (PAIR) mbar_arrive_cluster(cluster_addr(tempty, 0));
+    else mbar_arrive(tempty);
+  }
 }
 
 // kEpiRopeQKV for one tile row: one head (NCH chunks of 32 columns) at a time --
 // LoRA addends, bias, RoPE rotation of q / k heads by pos[m], head-major planes.
-template <int BN, int NCH>
+template <int BN, int NCH, bool PAIR>
 __device__ __forceinline__ void epi_rope(const Epilogue& e, int m, int n0, bool row_ok, int N, uint32_t acc,
                                          uint64_t* tempty, int lane) {
   constexpr int DH = NCH * 32, HALF = DH / 2;
@@ -252,7 +264,7 @@ __device__ __forceinline__ void epi_rope(const Epilogue& e, int m, int n0, bool 
     float v[NCH][32];
 #pragma unroll
     for (int k = 0; k < NCH; ++k) tmem_ld32(acc + (uint32_t)(hb + 32 * k), v[k]);
-    if (hb + DH >= BN) release_acc(tempty, lane);
+    if (hb + DH >= BN) release_acc<PAIR>(tempty, lane);
     const int c0 = n0 + hb;
     if (!row_ok || c0 >= N) continue;
 #pragma unroll
@@ -295,7 +307,7 @@ __device__ __forceinline__ void epi_rope(const Epilogue& e, int m, int n0, bool 
 
 // kEpiSwiGLU for one tile row of a 128-wide tile with paired B rows: columns
 // [0, 64) are gate features n0/2 .., [64, 128) the same up features.
-template <int BN>
+template <int BN, bool PAIR>
 __device__ __forceinline__ void epi_swiglu(const Epilogue& e, int m, int n0, bool row_ok, uint32_t acc,
                                            uint64_t* tempty, int lane) {
   const int ff = e.pair_off, f0 = n0 / 2;
@@ -304,7 +316,7 @@ __device__ __forceinline__ void epi_swiglu(const Epilogue& e, int m, int n0, boo
     float g[32], u[32];
     tmem_ld32(acc + (uint32_t)(32 * k), g);
     tmem_ld32(acc + (uint32_t)(BN / 2 + 32 * k), u);
-    if (k == BN / 64 - 1) release_acc(tempty, lane);
+    if (k == BN / 64 - 1) release_acc<PAIR>(tempty, lane);
     const int fc = f0 + 32 * k;
     if (!row_ok || fc >= ff) continue;
     if (e.n_lora) {
@@ -328,17 +340,21 @@ __device__ __forceinline__ void epi_swiglu(const Epilogue& e, int m, int n0, boo
 
 // FUSED instantiations carry the fused epilogues (LoRA addends, RoPE / SwiGLU
 // modes); the others leave that code out so they keep their register budget.
-template <int BN, bool SPLIT, bool Q8, bool FUSED>
+template <int BN, bool SPLIT, bool Q8, bool FUSED, bool PAIR>
 __global__ void __launch_bounds__(threads_of<Q8>(), 1)
     gemm_split_bf16_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_constant__ CUtensorMap map_a_lo,
                            const __grid_constant__ CUtensorMap map_b_hi, const __grid_constant__ CUtensorMap map_b_lo,
                            const KArgs args) {
   static_assert(!Q8 || SPLIT, "a Q8_0 operand is always dequantised into split planes");
-  constexpr int STAGES = Stages<BN, SPLIT, Q8>::kStages;
-  constexpr int kTileA = Cfg<BN>::kTileA;
-  constexpr int kTileB = Cfg<BN>::kTileB;
-  constexpr int kStageBytes = Stages<BN, SPLIT, Q8>::kStageBytes;
-  constexpr int kTxBytes = Stages<BN, SPLIT, Q8>::kTxBytes;
+  static_assert(!PAIR || (SPLIT && (BN == 128 || BN == 256)), "CTA pairs run split planes, 128 / 256-wide tiles");
+  using St = Stages<BN, SPLIT, Q8, PAIR>;
+  constexpr int STAGES = St::kStages;
+  constexpr int kTileA = Cfg<BN, PAIR>::kTileA;
+  constexpr int kTileB = Cfg<BN, PAIR>::kTileB;
+  constexpr int RB = Cfg<BN, PAIR>::kRowsB;   // B rows (output columns) held by this CTA
+  constexpr int BMT = PAIR ? 2 * BM : BM;     // output rows of a unit
+  constexpr int kStageBytes = St::kStageBytes;
+  constexpr int kTxBytes = St::kTxBytes;
   constexpr uint32_t kAccCols = Cfg<BN>::kAccCols;
 
   extern __shared__ uint8_t smem_raw[];
@@ -348,29 +364,43 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
   uint64_t* tfull = empty + STAGES;   // [2] accumulator ready for the epilogue
   uint64_t* tempty = tfull + 2;       // [2] accumulator drained by the epilogue
   uint64_t* conv = tempty + 2;        // [STAGES] Q8_0: B tiles dequantised
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(conv + (Q8 ? STAGES : 0));
+  uint64_t* qfull = conv + (Q8 ? STAGES : 0);   // [STAGES] Q8_0: this CTA's quant tile landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(qfull + (Q8 ? STAGES : 0));
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
+  // CTA pair: both CTAs walk the same units; rank 0 issues the MMAs and owns
+  // the full / conv / tempty barriers the pair shares (the peer reaches them
+  // through cluster addresses)
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
+  const int walker = PAIR ? (int)(blockIdx.x / 2) : (int)blockIdx.x;
+  const int walkers = PAIR ? (int)(gridDim.x / 2) : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      if (Q8) mbar_init(&conv[s], kConvWarps);
+      if (Q8) mbar_init(&conv[s], (PAIR ? 2 : 1) * kConvWarps);
+      if (Q8) mbar_init(&qfull[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
+      mbar_init(&tempty[b], PAIR ? 8 : 4);
     }
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, Cfg<BN>::kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, Cfg<BN>::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, Cfg<BN>::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();   // the peer's barriers are initialised before any remote use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // Barrier set-up and the TMEM allocation above overlap the previous kernel's
@@ -384,11 +414,15 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
       tma_prefetch_desc(&map_b_hi);
       uint32_t it = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < args.units && ok; u += gridDim.x) {
-        const Unit w = decode<BN>(args, u);
+      for (int u = walker; u < args.units && ok; u += walkers) {
+        const Unit w = decode<BN, BMT>(args, u);
         if (w.skip) continue;
         const int za = batch_index(w.z, args.a_bdiv1, args.a_bmul1, args.a_bdiv2, args.a_bmul2);
         const int zb = batch_index(w.z, args.b_bdiv1, args.b_bmul1, args.b_bdiv2, args.b_bmul2);
+        const int m0 = w.m0 + (int)rank * BM;   // this CTA's A rows
+        const int nb = w.n0 + (int)rank * RB;   // this CTA's B rows (unpaired)
+        // paired gate / up rows: one CTA of a pair loads the gate rows, the other the up rows
+        const int pr = (int)rank == 0 ? w.n0 / 2 : args.epi.pair_off + w.n0 / 2;
         for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -396,7 +430,14 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], kTxBytes);
+          // A (and B) plane tiles of both CTAs count on rank 0's full barrier
+          const uint32_t fc = PAIR ? cluster_addr(&full[s], 0) : 0u;
+          auto ld = [&](void* dst, const CUtensorMap* map, int c0, int c1, int c2) {
+            if constexpr (PAIR) tma_load_3d_pair(dst, map, fc, c0, c1, c2);
+            else tma_load_3d(dst, map, &full[s], c0, c1, c2);
+          };
+          if (!PAIR || rank == 0) mbar_arrive_expect_tx(&full[s], kTxBytes);
+          if (Q8) mbar_arrive_expect_tx(&qfull[s], St::kQBytes);
           uint8_t* st = smem + s * kStageBytes;
           uint8_t* a_hi = st;
           uint8_t* b_hi = st + kTileA;
@@ -404,52 +445,71 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
           uint8_t* b_lo = a_lo + kTileA;
           const int k0 = kb * BK;
           if (!args.a_mn) {
-            tma_load_3d(a_hi, &map_a_hi, &full[s], k0, w.m0, za);
-            if (SPLIT) tma_load_3d(a_lo, &map_a_lo, &full[s], k0, w.m0, za);
+            ld(a_hi, &map_a_hi, k0, m0, za);
+            if (SPLIT) ld(a_lo, &map_a_lo, k0, m0, za);
           } else {
 #pragma unroll
             for (int j = 0; j < BM / 64; ++j) {
-              tma_load_3d(a_hi + j * 64 * 128, &map_a_hi, &full[s], w.m0 + 64 * j, k0, za);
-              if (SPLIT) tma_load_3d(a_lo + j * 64 * 128, &map_a_lo, &full[s], w.m0 + 64 * j, k0, za);
+              ld(a_hi + j * 64 * 128, &map_a_hi, m0 + 64 * j, k0, za);
+              if (SPLIT) ld(a_lo + j * 64 * 128, &map_a_lo, m0 + 64 * j, k0, za);
             }
           }
           if (Q8) {
-            // int8 quants; map_b_hi is the quant map (box {64 bytes, rows})
+            // int8 quants; map_b_hi is the quant map (box {64 bytes, rows}),
+            // counted on this CTA's qfull: its own converters read them
             uint8_t* qd = st + 2 * (kTileA + kTileB);
-            if (args.epi.pair_off) {   // gate rows, then the matching up rows
-              tma_load_3d(qd, &map_b_hi, &full[s], k0, w.n0 / 2, 0);
-              tma_load_3d(qd + (BN / 2) * 64, &map_b_hi, &full[s], k0, args.epi.pair_off + w.n0 / 2, 0);
+            uint64_t* qb = &qfull[s];
+            if (args.epi.pair_off) {
+              if (PAIR) {
+                tma_load_3d(qd, &map_b_hi, qb, k0, pr, 0);
+              } else {   // gate rows, then the matching up rows
+                tma_load_3d(qd, &map_b_hi, qb, k0, w.n0 / 2, 0);
+                tma_load_3d(qd + (BN / 2) * 64, &map_b_hi, qb, k0, args.epi.pair_off + w.n0 / 2, 0);
+              }
             } else if (!args.b_mn) {
-              tma_load_3d(qd, &map_b_hi, &full[s], k0, w.n0, 0);
+              tma_load_3d(qd, &map_b_hi, qb, k0, nb, 0);
             } else {
 #pragma unroll
-              for (int j = 0; j < BN / 64; ++j) tma_load_3d(qd + j * 64 * 64, &map_b_hi, &full[s], w.n0 + 64 * j, k0, 0);
+              for (int j = 0; j < RB / 64; ++j) tma_load_3d(qd + j * 64 * 64, &map_b_hi, qb, nb + 64 * j, k0, 0);
             }
-          } else if (args.epi.pair_off) {   // gate rows, then the matching up rows
-            const int r0 = w.n0 / 2, r1 = args.epi.pair_off + w.n0 / 2;
-            tma_load_3d(b_hi, &map_b_hi, &full[s], k0, r0, zb);
-            tma_load_3d(b_hi + (BN / 2) * 128, &map_b_hi, &full[s], k0, r1, zb);
-            if (SPLIT) {
-              tma_load_3d(b_lo, &map_b_lo, &full[s], k0, r0, zb);
-              tma_load_3d(b_lo + (BN / 2) * 128, &map_b_lo, &full[s], k0, r1, zb);
+          } else if (args.epi.pair_off) {
+            if (PAIR) {
+              ld(b_hi, &map_b_hi, k0, pr, zb);
+              ld(b_lo, &map_b_lo, k0, pr, zb);
+            } else {   // gate rows, then the matching up rows
+              const int r0 = w.n0 / 2, r1 = args.epi.pair_off + w.n0 / 2;
+              ld(b_hi, &map_b_hi, k0, r0, zb);
+              ld(b_hi + (BN / 2) * 128, &map_b_hi, k0, r1, zb);
+              if (SPLIT) {
+                ld(b_lo, &map_b_lo, k0, r0, zb);
+                ld(b_lo + (BN / 2) * 128, &map_b_lo, k0, r1, zb);
+              }
             }
           } else if (!args.b_mn) {
-            tma_load_3d(b_hi, &map_b_hi, &full[s], k0, w.n0, zb);
-            if (SPLIT) tma_load_3d(b_lo, &map_b_lo, &full[s], k0, w.n0, zb);
+            ld(b_hi, &map_b_hi, k0, nb, zb);
+            if (SPLIT) ld(b_lo, &map_b_lo, k0, nb, zb);
           } else {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) {
-              tma_load_3d(b_hi + j * 64 * 128, &map_b_hi, &full[s], w.n0 + 64 * j, k0, zb);
-              if (SPLIT) tma_load_3d(b_lo + j * 64 * 128, &map_b_lo, &full[s], w.n0 + 64 * j, k0, zb);
+            for (int j = 0; j < RB / 64; ++j) {
+              ld(b_hi + j * 64 * 128, &map_b_hi, nb + 64 * j, k0, zb);
+              if (SPLIT) ld(b_lo + j * 64 * 128, &map_b_lo, nb + 64 * j, k0, zb);
             }
           }
+        }
+      }
+      // A pair member exits only after the MMAs have released every stage it
+      // filled (their commits arrive on this CTA's empty barriers).
+      if (PAIR && ok) {
+        for (int j = 0; j < STAGES; ++j, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, args.err, kErrWaitEmpty)) break;
         }
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = make_idesc_f16(BM, BN, true, args.a_mn != 0, args.b_mn != 0);
+    if (lane == 0 && (!PAIR || rank == 0)) {
+      const uint32_t idesc = make_idesc_f16(BMT, BN, true, args.a_mn != 0, args.b_mn != 0);
       // K-major: advance 32 B per 16-element k-step inside the swizzle atom.
       // MN-major: advance 16 rows of 128 B; MN atoms are 64 rows (8 KB) apart.
       const uint32_t a_kstep = args.a_mn ? 2048u : 32u;
@@ -458,11 +518,12 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
       const uint32_t b_lbo = args.b_mn ? 8192u : 16u;
       uint32_t it = 0, local = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < args.units && ok; u += gridDim.x) {
-        const Unit w = decode<BN>(args, u);
+      for (int u = walker; u < args.units && ok; u += walkers) {
+        const Unit w = decode<BN, BMT>(args, u);
         if (w.skip) continue;
         const uint32_t b = local & 1, tph = (local >> 1) & 1;
-        ok = mbar_wait(&tempty[b], tph ^ 1, args.err, kErrWaitAccum);
+        ok = PAIR ? mbar_wait_cluster(&tempty[b], tph ^ 1, args.err, kErrWaitAccum)
+                  : mbar_wait(&tempty[b], tph ^ 1, args.err, kErrWaitAccum);
         if (!ok) break;
         tc_fence_after();
         const uint32_t acc_tmem = tmem_base + b * kAccCols;
@@ -470,7 +531,10 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           ok = mbar_wait(&full[s], ph, args.err, kErrWaitFull);
-          if (Q8) ok = ok && mbar_wait(&conv[s], ph, args.err, kErrWaitFull);
+          if (Q8) {
+            ok = ok && (PAIR ? mbar_wait_cluster(&conv[s], ph, args.err, kErrWaitFull)
+                             : mbar_wait(&conv[s], ph, args.err, kErrWaitFull));
+          }
           if (!ok) break;
           tc_fence_after();
           const uint32_t st = smem_u32(smem + s * kStageBytes);
@@ -480,17 +544,35 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
             const uint64_t dah = make_sdesc_sw128(a_hi + ks * a_kstep, a_lbo, 1024);
             const uint64_t dbh = make_sdesc_sw128(b_hi + ks * b_kstep, b_lbo, 1024);
             const uint32_t acc = (kb > w.kb0 || ks > 0) ? 1u : 0u;
-            umma_f16(acc_tmem, dah, dbh, idesc, acc);
-            if (SPLIT) {
+            if constexpr (PAIR) {
               const uint64_t dal = make_sdesc_sw128(a_lo + ks * a_kstep, a_lbo, 1024);
               const uint64_t dbl = make_sdesc_sw128(b_lo + ks * b_kstep, b_lbo, 1024);
-              umma_f16(acc_tmem, dal, dbh, idesc, 1u);
-              umma_f16(acc_tmem, dah, dbl, idesc, 1u);
+              umma_f16_pair(acc_tmem, dah, dbh, idesc, acc);
+              umma_f16_pair(acc_tmem, dal, dbh, idesc, 1u);
+              umma_f16_pair(acc_tmem, dah, dbl, idesc, 1u);
+            } else {
+              umma_f16(acc_tmem, dah, dbh, idesc, acc);
+              if (SPLIT) {
+                const uint64_t dal = make_sdesc_sw128(a_lo + ks * a_kstep, a_lbo, 1024);
+                const uint64_t dbl = make_sdesc_sw128(b_lo + ks * b_kstep, b_lbo, 1024);
+                umma_f16(acc_tmem, dal, dbh, idesc, 1u);
+                umma_f16(acc_tmem, dah, dbl, idesc, 1u);
+              }
             }
           }
-          umma_commit(&empty[s]);
+          if constexpr (PAIR) {   // free the stage in both CTAs
+            umma_commit_pair(cluster_addr(&empty[s], 0));
+            umma_commit_pair(cluster_addr(&empty[s], 1));
+          } else {
+            umma_commit(&empty[s]);
+          }
         }
-        umma_commit(&tfull[b]);
+        if constexpr (PAIR) {
+          umma_commit_pair(cluster_addr(&tfull[b], 0));
+          umma_commit_pair(cluster_addr(&tfull[b], 1));
+        } else {
+          umma_commit(&tfull[b]);
+        }
         ++local;
       }
     }
@@ -505,13 +587,14 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
       const int sblk = args.q8_cols / 32;
       uint32_t it = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < args.units && ok; u += gridDim.x) {
-        const Unit w = decode<BN>(args, u);
+      for (int u = walker; u < args.units && ok; u += walkers) {
+        const Unit w = decode<BN, BMT>(args, u);
         if (w.skip) continue;
+        const int nb = w.n0 + (int)rank * RB;
         for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
-          ok = warp_wait(&full[s], ph, args.err, kErrWaitFull);
+          ok = warp_wait(&qfull[s], ph, args.err, kErrWaitFull);
           if (!ok) break;
           uint8_t* st = smem + s * kStageBytes;
           uint8_t* b_hi = st + kTileA;
@@ -519,7 +602,7 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
           const uint8_t* qs = st + 2 * (kTileA + kTileB);
           const int k0 = kb * BK;
 #pragma unroll 1
-          for (int i = ct; i < BN * 2; i += 32 * kConvWarps) {
+          for (int i = ct; i < RB * 2; i += 32 * kConvWarps) {
             // item = one Q8_0 block: 32 quants of stored row `srow`, columns
             // c32 * 32 .. +31 of this tile's 64
             int r, srow, sb;
@@ -529,8 +612,9 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
             if (!args.b_mn) {   // tile rows = output columns n, 64 k
               r = i >> 1;
               src = qs + r * 64 + c32 * 32;
-              srow = !args.epi.pair_off ? w.n0 + r
-                                        : (r < BN / 2 ? w.n0 / 2 + r : args.epi.pair_off + w.n0 / 2 + r - BN / 2);
+              if (!args.epi.pair_off) srow = nb + r;
+              else if (PAIR) srow = ((int)rank == 0 ? w.n0 / 2 : args.epi.pair_off + w.n0 / 2) + r;
+              else srow = r < BN / 2 ? w.n0 / 2 + r : args.epi.pair_off + w.n0 / 2 + r - BN / 2;
               sb = (k0 >> 5) + c32;
               tile = 0;
             } else {            // BN / 64 tiles of 64 k rows x 64 n
@@ -538,7 +622,7 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
               r = (i >> 1) & 63;
               src = qs + j * 4096 + r * 64 + c32 * 32;
               srow = k0 + r;
-              sb = ((w.n0 + 64 * j) >> 5) + c32;
+              sb = ((nb + 64 * j) >> 5) + c32;
               tile = (uint32_t)j * 8192u;
             }
             const float sc = (srow < args.q8_rows && sb < sblk)
@@ -571,7 +655,10 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
           }
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&conv[s]);
+          if (lane == 0) {
+            if constexpr (PAIR) mbar_arrive_cluster(cluster_addr(&conv[s], 0));
+            else mbar_arrive(&conv[s]);
+          }
         }
       }
     }
@@ -581,12 +668,12 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
     const int row = q * 32 + lane;
     const Epilogue& e = args.epi;
     uint32_t local = 0;
-    for (int u = blockIdx.x; u < args.units; u += gridDim.x) {
-      const Unit w = decode<BN>(args, u);
+    for (int u = walker; u < args.units; u += walkers) {
+      const Unit w = decode<BN, BMT>(args, u);
       if (w.skip) continue;
       const uint32_t b = local & 1, tph = (local >> 1) & 1;
       ++local;
-      const int m = w.m0 + row;
+      const int m = w.m0 + (int)rank * BM + row;
       const bool row_in = m < args.M;
       const bool direct = args.splits == 1;
       // output offset of this row (without the column part); the residual /
@@ -602,11 +689,11 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
       const uint32_t acc_tmem = tmem_base + b * kAccCols + ((uint32_t)(q * 32) << 16);
       if constexpr (FUSED) {
         if (e.mode == kEpiRopeQKV) {
-          epi_rope<BN, 2>(e, m, w.n0, row_ok, args.N, acc_tmem, &tempty[b], lane);
+          epi_rope<BN, 2, PAIR>(e, m, w.n0, row_ok, args.N, acc_tmem, &tempty[b], lane);
           continue;
         }
         if (e.mode == kEpiSwiGLU) {
-          if constexpr (BN == 128 || BN == 256) epi_swiglu<BN>(e, m, w.n0, row_ok, acc_tmem, &tempty[b], lane);
+          if constexpr (BN == 128 || BN == 256) epi_swiglu<BN, PAIR>(e, m, w.n0, row_ok, acc_tmem, &tempty[b], lane);
           continue;
         }
       }
@@ -617,11 +704,7 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
       auto chunk = [&](int c, const float4 (&cur)[8], float4 (&next)[8]) {
         float v[32];
         tmem_ld32(acc_tmem + (uint32_t)(c * 32), v);
-        if (c == BN / 32 - 1) {   // accumulator fully read: hand it back to the MMA issuer
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[b]);
-        }
+        if (c == BN / 32 - 1) release_acc<PAIR>(&tempty[b], lane);   // accumulator read: back to the MMA issuer
         const int nc = w.n0 + c * 32;
         if (!row_ok || nc >= args.N) return;
         if (!direct) {
@@ -653,9 +736,13 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
 
   tc_fence_before();
   __syncthreads();
+  // a pair frees its TMEM together, after both CTAs are done with each
+  // other's barriers and accumulators
+  if constexpr (PAIR) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg<BN>::kTmemCols);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, Cfg<BN>::kTmemCols);
+    else tmem_dealloc(tmem_base, Cfg<BN>::kTmemCols);
   }
 }
 
@@ -752,14 +839,20 @@ int make_q8_map(CUtensorMap* map, const Operand& o, int box_rows) {
 constexpr double kSmFlopsPerUs = 1310.0e6 / kNumSMs;
 constexpr double kSmOperandBytesPerUs = 82.0e3;
 
-double estimate_us(const GemmDesc& d, int bn, int s) {
-  const int tm = (d.M + BM - 1) / BM, tn = (d.N + bn - 1) / bn;
+// Q8_0 B operand: elements the 8 converter warps dequantise and split per us
+constexpr double kConvElemsPerUs = 6000.0;
+
+double estimate_us(const GemmDesc& d, int bn, int s, bool pair, bool q8) {
+  const int bmt = pair ? 2 * BM : BM;            // output rows of a unit
+  const double slots = pair ? kNumSMs / 2 : kNumSMs;   // units in flight
+  const int rb = pair ? bn / 2 : bn;              // B rows per CTA
+  const int tm = (d.M + bmt - 1) / bmt, tn = (d.N + bn - 1) / bn;
   double tiles = (double)d.batch * tm * tn;
   int kb = (d.K + BK - 1) / BK;
   if (d.causal == 1) tiles *= (double)(tm + 1) / (2.0 * tm);   // tiles above the diagonal are skipped
   if (d.causal == 2) kb = kb / 2 + 1;                          // K clamped at the diagonal, on average
   const double units = tiles * s;
-  const double per_cta = std::ceil(units / kNumSMs);
+  const double per_cta = std::ceil(units / slots);
   const bool reads_out = d.epi.mode == kEpiAccumF32 || d.epi.mode == kEpiResidF32;
   // bytes the epilogue moves per output element: they share the SM's path to
   // L2 with the operand tiles of the next unit's main loop
@@ -768,11 +861,13 @@ double estimate_us(const GemmDesc& d, int bn, int s) {
   if (d.epi.mode == kEpiSwiGLU) out_b = 6.0;   // gate|up f32 + half of a feature's planes
   const double tile_bytes = (double)BM * bn * out_b;
   const double kb_unit = std::ceil((double)kb / s);
+  const double planes = d.split ? 2.0 : 1.0;
   const double t_mma = (d.split ? 3.0 : 1.0) * 2.0 * BM * bn * BK / kSmFlopsPerUs;
-  const double t_feed =
-      ((d.split ? 2.0 : 1.0) * (BM + bn) * BK * 2.0 + tile_bytes / kb_unit) / kSmOperandBytesPerUs;
-  const double t_kb = std::max(t_mma, t_feed);
-  const double active = units < kNumSMs ? units : (double)kNumSMs;
+  const double b_bytes = q8 ? (double)rb * BK : planes * rb * BK * 2.0;
+  const double t_feed = (planes * BM * BK * 2.0 + b_bytes + tile_bytes / kb_unit) / kSmOperandBytesPerUs;
+  const double t_conv = q8 ? (double)rb * BK / kConvElemsPerUs : 0.0;
+  const double t_kb = std::max(t_mma, std::max(t_feed, t_conv));
+  const double active = (units < slots ? units : slots) * (pair ? 2 : 1);
   const double drain_bw = std::min(100.0e3, 6.5e6 / active);   // bytes per us per CTA
   double t = 1.2 + per_cta * (kb_unit * t_kb + 0.5) + tile_bytes / drain_bw;
   if (s > 1) t += ((s + 1.0) * d.M * d.N * 4.0 + (reads_out ? d.M * d.N * 4.0 : 0.0)) / 5.0e6 + 2.5;
@@ -781,7 +876,22 @@ double estimate_us(const GemmDesc& d, int bn, int s) {
 
 struct Plan {
   int bn = 128, splits = 1;
+  bool pair = false;
 };
+
+// CTA pairs: -1 by shape (below), 0 never, 1 wherever the shape allows
+int g_pair_mode = -1;
+
+// Measured on B200 (SmolLM2 step shapes, M = 4096 tokens): a pair beats two
+// single CTAs when both operands are K-major and N is wide -- the LM head
+// (N = 49152: 746 -> 625 us), gate|up (N = 3072; Q8_0 with a plain store:
+// 100 -> 75 us, the converter work per MMA halves). With N = 576 .. 960 the
+// 256-row units leave half the pairs idle, with an MN-major B (dX products)
+// the pair's cross-CTA stage hand-off costs more than it saves, and the Q8_0
+// gate|up with its SwiGLU epilogue measured slower in the step (91 -> 103 us).
+bool pair_wins(const GemmDesc& d) {
+  return !d.a.mn_major && !d.b.mn_major && d.N >= 2048 && d.M >= 1024 && d.epi.mode != kEpiSwiGLU;
+}
 
 Plan choose_plan(const GemmDesc& d, long long ws_floats, bool q8) {
   static const int kBn[] = {64, 128, 192, 256};
@@ -789,46 +899,71 @@ Plan choose_plan(const GemmDesc& d, long long ws_floats, bool q8) {
   // fused epilogues act on whole output rows of a tile: no K splits
   const bool fused = d.epi.mode == kEpiRopeQKV || d.epi.mode == kEpiSwiGLU || d.epi.n_lora > 0;
   const bool can_split = !d.causal && d.batch == 1 && ws_floats > 0 && !fused;
+  const bool pair_ok = g_pair_mode != 0 && d.split && !d.causal && (g_pair_mode == 1 || pair_wins(d));
   Plan best;
   double best_t = 1e30;
-  for (int bn : kBn) {
-    if (q8 && bn > 128) break;
-    if (bn > 64 && bn - 64 >= d.N) break;   // a narrower tile already covers N
-    if (d.epi.mode == kEpiSwiGLU && bn != 128 && bn != 256) continue;   // BN/2 gate + BN/2 up columns
-    if (d.epi.mode == kEpiSwiGLU && q8 && bn != 128) continue;
-    if (d.epi.mode == kEpiRopeQKV && bn % d.epi.rope.dh) continue;       // whole heads per tile
-    int s_lo = 1, s_hi = 1;
-    if (d.splits > 0 && !fused) {
-      s_lo = s_hi = d.splits;
-    } else if (can_split && kb >= 8) {
-      s_hi = std::min(16, kb / 2);
-    }
-    for (int s = s_lo; s <= s_hi; ++s) {
-      if (s > 1 && (long long)s * d.M * d.N > ws_floats) break;
-      const double t = estimate_us(d, bn, s);
-      if (t < best_t - 1e-9) {
-        best_t = t;
-        best.bn = bn;
-        best.splits = s;
+  for (int pr = 0; pr < 2; ++pr) {
+    const bool pair = pr == 1;
+    if (pair && !pair_ok) continue;
+    if (!pair && pair_ok) continue;   // a shape that qualifies runs on pairs
+    for (int bn : kBn) {
+      if (pair && bn != 128 && bn != 256) continue;
+      if (q8 && !pair && bn > 128) break;
+      if (bn > 64 && bn - 64 >= d.N && !(pair && bn == 128)) break;   // a narrower tile already covers N
+      if (d.epi.mode == kEpiSwiGLU && bn != 128 && bn != 256) continue;   // BN/2 gate + BN/2 up columns
+      if (d.epi.mode == kEpiSwiGLU && q8 && !pair && bn != 128) continue;
+      if (d.epi.mode == kEpiRopeQKV && bn % d.epi.rope.dh) continue;       // whole heads per tile
+      int s_lo = 1, s_hi = 1;
+      if (d.splits > 0 && !fused) {
+        s_lo = s_hi = d.splits;
+      } else if (can_split && kb >= 8) {
+        s_hi = std::min(16, kb / 2);
+      }
+      for (int s = s_lo; s <= s_hi; ++s) {
+        if (s > 1 && (long long)s * d.M * d.N > ws_floats) break;
+        const double t = estimate_us(d, bn, s, pair, q8);
+        if (t < best_t - 1e-9) {
+          best_t = t;
+          best.bn = bn;
+          best.splits = s;
+          best.pair = pair;
+        }
       }
     }
   }
   return best;
 }
 
-template <int BN, bool SPLIT, bool Q8 = false, bool FUSED = false>
+template <int BN, bool SPLIT, bool Q8 = false, bool FUSED = false, bool PAIR = false>
 int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream_t stream, int splits) {
-  using S = Stages<BN, SPLIT, Q8>;
+  using S = Stages<BN, SPLIT, Q8, PAIR>;
+  auto* kern = gemm_split_bf16_kernel<BN, SPLIT, Q8, FUSED, PAIR>;
   static bool attr_set = false;
+  static int max_pairs = 0;   // co-resident CTA pairs (clusters of 2) on this GPU
   if (!attr_set) {
-    if (cudaFuncSetAttribute(gemm_split_bf16_kernel<BN, SPLIT, Q8, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             S::kSmemBytes) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes) != cudaSuccess)
       return -20;
+    if (PAIR) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * kNumSMs);
+      cfg.blockDim = dim3(threads_of<Q8>());
+      cfg.dynamicSmemBytes = S::kSmemBytes;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = 2;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&max_pairs, kern, &cfg) != cudaSuccess || max_pairs < 1) return -22;
+    }
     attr_set = true;
   }
   CUtensorMap ma_hi, ma_lo, mb_hi, mb_lo;
   const int a_box = d.a.mn_major ? 64 : BM;
-  const int b_box = d.epi.pair_off ? BN / 2 : (d.b.mn_major ? 64 : BN);
+  // B box rows: a pair holds half of B's rows per CTA, paired gate|up rows are
+  // fetched as two half-width boxes
+  const int b_box = d.epi.pair_off ? BN / 2 : (d.b.mn_major ? 64 : Cfg<BN, PAIR>::kRowsB);
   int rc;
   if ((rc = make_map(&ma_hi, d.a.hi, d.a, a_box))) return rc;
   if (Q8) {
@@ -849,7 +984,7 @@ int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream
   k.a_mn = d.a.mn_major; k.b_mn = d.b.mn_major;
   k.a_bdiv1 = d.a.bdiv1; k.a_bmul1 = d.a.bmul1; k.a_bdiv2 = d.a.bdiv2; k.a_bmul2 = d.a.bmul2;
   k.b_bdiv1 = d.b.bdiv1; k.b_bmul1 = d.b.bmul1; k.b_bdiv2 = d.b.bdiv2; k.b_bmul2 = d.b.bmul2;
-  k.tiles_m = (d.M + BM - 1) / BM;
+  k.tiles_m = (d.M + (PAIR ? 2 : 1) * BM - 1) / ((PAIR ? 2 : 1) * BM);
   k.tiles_n = (d.N + BN - 1) / BN;
   k.kb_total = (d.K + BK - 1) / BK;
   k.causal = d.causal;
@@ -868,10 +1003,16 @@ int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream
   k.q8_scale = d.b.q8_scale;
   k.q8_rows = d.b.rows;
   k.q8_cols = d.b.cols;
-  const int grid = k.units < kNumSMs ? k.units : kNumSMs;
-  if (launch_pdl(gemm_split_bf16_kernel<BN, SPLIT, Q8, FUSED>, dim3(grid), dim3(threads_of<Q8>()), S::kSmemBytes, stream,
-                 ma_hi, ma_lo, mb_hi, mb_lo, k) != 0)
-    return -21;
+  if constexpr (PAIR) {
+    const int pairs = k.units < max_pairs ? k.units : max_pairs;
+    if (launch_pdl_cluster(kern, dim3(2 * pairs), dim3(threads_of<Q8>()), S::kSmemBytes, stream, 2, ma_hi, ma_lo, mb_hi,
+                           mb_lo, k) != 0)
+      return -21;
+  } else {
+    const int grid = k.units < kNumSMs ? k.units : kNumSMs;
+    if (launch_pdl(kern, dim3(grid), dim3(threads_of<Q8>()), S::kSmemBytes, stream, ma_hi, ma_lo, mb_hi, mb_lo, k) != 0)
+      return -21;
+  }
   if (splits > 1) {
     const long long work = (long long)d.M * ((d.N + 31) / 32);
     long long blocks = (work + 127) / 128;
@@ -883,6 +1024,12 @@ int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream
 }
 
 }  // namespace
+
+int gemm_set_pair_mode(int mode) {
+  if (mode < -1 || mode > 1) return -1;
+  g_pair_mode = mode;
+  return 0;
+}
 
 int make_plane_map(CUtensorMap* map, const __nv_bfloat16* base, const Operand& o, int box_rows) {
   return make_map(map, base, o, box_rows);
@@ -920,17 +1067,31 @@ int gemm_launch(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStre
   const bool fused = e.mode == kEpiRopeQKV || e.mode == kEpiSwiGLU || e.n_lora > 0;
   if (fused && !d.split) return -3;
   const Plan pl = choose_plan(d, sc.ws ? sc.ws_floats : 0, d.b.q8 != nullptr);
+  if (d.b.q8 && (!d.split || d.batch != 1 || !d.b.q8_scale || d.b.cols % 32 || !d.a.hi || !d.a.lo)) return -4;
+  if (!d.b.q8 && (!d.a.hi || !d.b.hi || (d.split && (!d.a.lo || !d.b.lo)))) return -4;
+  if (pl.pair) {   // CTA pairs: 256-row units, 128 / 256-wide tiles, split planes
+    const int sp = pl.splits;
+    const bool w = pl.bn == 256;
+    if (d.b.q8) {
+      if (fused) return w ? launch_bn<256, true, true, true, true>(d, sc, dev_err, stream, sp)
+                          : launch_bn<128, true, true, true, true>(d, sc, dev_err, stream, sp);
+      return w ? launch_bn<256, true, true, false, true>(d, sc, dev_err, stream, sp)
+               : launch_bn<128, true, true, false, true>(d, sc, dev_err, stream, sp);
+    }
+    if (fused) return w ? launch_bn<256, true, false, true, true>(d, sc, dev_err, stream, sp)
+                        : launch_bn<128, true, false, true, true>(d, sc, dev_err, stream, sp);
+    return w ? launch_bn<256, true, false, false, true>(d, sc, dev_err, stream, sp)
+             : launch_bn<128, true, false, false, true>(d, sc, dev_err, stream, sp);
+  }
   if (d.b.q8) {
     // Q8_0 B: dequantised in shared memory into split planes; 64 / 128-wide tiles
     // keep three stages of A planes + B planes + quants within shared memory
-    if (!d.split || d.batch != 1 || !d.b.q8_scale || d.b.cols % 32 || !d.a.hi || !d.a.lo) return -4;
     if (fused)
       return pl.bn <= 64 ? launch_bn<64, true, true, true>(d, sc, dev_err, stream, pl.splits)
                          : launch_bn<128, true, true, true>(d, sc, dev_err, stream, pl.splits);
     return pl.bn <= 64 ? launch_bn<64, true, true>(d, sc, dev_err, stream, pl.splits)
                        : launch_bn<128, true, true>(d, sc, dev_err, stream, pl.splits);
   }
-  if (!d.a.hi || !d.b.hi || (d.split && (!d.a.lo || !d.b.lo))) return -4;
   const int sp = pl.splits;
   if (fused) {
     switch (pl.bn) {

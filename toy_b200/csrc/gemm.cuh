@@ -130,6 +130,12 @@ struct GemmScratch {
 // to a DeviceError code if one of its bounded waits gives up.
 int gemm_launch(const GemmDesc& d, const GemmScratch& scratch, int* dev_err, cudaStream_t stream);
 
+// GEMMs on CTA pairs (cta_group::2: 256-row units, each CTA holding half of
+// the B tile): -1 (the default) for the shapes where pairs measured faster
+// (both operands K-major, N >= 2048), 0 never, 1 wherever the shape allows.
+// Process-wide; returns 0 or -1 for a bad mode.
+int gemm_set_pair_mode(int mode);
+
 // TMA map over one bf16 plane laid out as `o` describes: dims {cols, rows,
 // nbatch}, box {64, box_rows, 1}, 128-byte swizzle. Rows past `rows` inside a
 // batch read as zero. Returns 0 or a negative alignment / driver error.

@@ -50,8 +50,16 @@ __device__ __forceinline__ long long out_offset(const Epilogue& e, int m, int n)
 template <int RT, bool SMEM_W>
 __global__ void __launch_bounds__(256) lora_down_kernel(Planes X, long long ldx, int N, int K,
                                                         const float* __restrict__ W, int r, float alpha,
-                                                        float* __restrict__ out) {
+                                                        float* __restrict__ out, const float* __restrict__ bsrc,
+                                                        int bc, float* __restrict__ bt) {
   griddep_wait();
+  // side job: bt[j][c] = bsrc[c][j] (the adapter's B transposed for the splice)
+  if (bt) {
+    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < (long long)bc * r; i += (long long)gridDim.x * 256) {
+      const int c = (int)(i / r), j = (int)(i % r);
+      bt[(long long)j * bc + c] = bsrc[i];
+    }
+  }
   extern __shared__ float4 wsm4[];
   const float* w = W;
   if (SMEM_W) {
@@ -222,6 +230,185 @@ __global__ void lora_transpose_kernel(const float* __restrict__ W, int C, int r,
   }
 }
 
+// Adapter backward, row pass: one warp per token row (two rows in flight)
+//   du[n][j] = s sum_c dY[n][c] bt[j][c]     (saved for the weight gradients)
+//   dX(n, k) += sum_j du[n][j] A[j][k]        (epilogue addressing, as lora_up)
+// bt = B^T [r][d_out] is staged in shared memory when it fits.
+template <int RT, bool SMEM_B>
+__global__ void __launch_bounds__(256) lora_bwd_rows_kernel(Planes dY, long long ldy, int d_out, int d_in,
+                                                            const float* __restrict__ bt,
+                                                            const float* __restrict__ A, int r, float s, int N,
+                                                            float* __restrict__ du, Epilogue edx) {
+  griddep_wait();
+  extern __shared__ float4 bsm4[];
+  const float* b = bt;
+  if (SMEM_B) {
+    float* bsm = reinterpret_cast<float*>(bsm4);
+    for (int i = threadIdx.x * 4; i < r * d_out; i += 256 * 4)
+      *reinterpret_cast<float4*>(bsm + i) = __ldg(reinterpret_cast<const float4*>(bt + i));
+    __syncthreads();
+    b = bsm;
+  }
+  const int lane = threadIdx.x % 32;
+  const int warps = gridDim.x * 8;
+  for (int n = (blockIdx.x * 8 + threadIdx.x / 32) * 2; n < N; n += warps * 2) {
+    const bool two = n + 1 < N;
+    float acc0[RT], acc1[RT];
+#pragma unroll
+    for (int j = 0; j < RT; ++j) acc0[j] = acc1[j] = 0.f;
+    for (int c = lane * 4; c < d_out; c += 128) {
+      const float4 y0 = load_planes4(dY, (long long)n * ldy + c);
+      const float4 y1 = two ? load_planes4(dY, (long long)(n + 1) * ldy + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < RT; ++j) {
+        if (j < r) {
+          const float4 w = *reinterpret_cast<const float4*>(b + (long long)j * d_out + c);
+          acc0[j] += y0.x * w.x + y0.y * w.y + y0.z * w.z + y0.w * w.w;
+          acc1[j] += y1.x * w.x + y1.y * w.y + y1.z * w.z + y1.w * w.w;
+        }
+      }
+    }
+    // full sums in every lane (butterfly), scaled
+#pragma unroll
+    for (int j = 0; j < RT; ++j) {
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        acc0[j] += __shfl_xor_sync(0xffffffffu, acc0[j], o);
+        acc1[j] += __shfl_xor_sync(0xffffffffu, acc1[j], o);
+      }
+      acc0[j] *= s;
+      acc1[j] *= s;
+      if (j < r && lane == (j & 31)) {
+        du[(long long)n * r + j] = acc0[j];
+        if (two) du[(long long)(n + 1) * r + j] = acc1[j];
+      }
+    }
+    for (int k = lane * 4; k < d_in; k += 128) {
+      float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
+#pragma unroll
+      for (int j = 0; j < RT; ++j) {
+        if (j < r) {
+          const float4 a4 = __ldg(reinterpret_cast<const float4*>(A + (long long)j * d_in + k));
+          x0.x += acc0[j] * a4.x; x0.y += acc0[j] * a4.y; x0.z += acc0[j] * a4.z; x0.w += acc0[j] * a4.w;
+          x1.x += acc1[j] * a4.x; x1.y += acc1[j] * a4.y; x1.z += acc1[j] * a4.z; x1.w += acc1[j] * a4.w;
+        }
+      }
+      float4* y = reinterpret_cast<float4*>(edx.out + out_offset(edx, n, k));
+      float4 v = *y;
+      v.x += x0.x; v.y += x0.y; v.z += x0.z; v.w += x0.w;
+      *y = v;
+      if (two) {
+        y = reinterpret_cast<float4*>(edx.out + out_offset(edx, n + 1, k));
+        v = *y;
+        v.x += x1.x; v.y += x1.y; v.z += x1.z; v.w += x1.w;
+        *y = v;
+      }
+    }
+  }
+}
+
+// Adapter backward, weight-gradient partials of both factors in one launch:
+// blocks x < gy take 64 columns of dY with S = u (dB, scaled by s), the rest 64
+// columns of X with S = du (dA); block y is a token chunk. Within a block the
+// warps' sums are added in warp order: part[y][col][j], col over d_out then d_in.
+template <int RT>
+__global__ void __launch_bounds__(WgradCfg<RT>::kWarps * 32)
+    lora_bwd_wgrad_kernel(Planes dY, long long ldy, int d_out, const float* __restrict__ U, Planes X, long long ldx,
+                          int d_in, const float* __restrict__ du, int gy, int N, int r, float s, int chunk,
+                          float* __restrict__ part) {
+  griddep_wait();
+  constexpr int WARPS = WgradCfg<RT>::kWarps;
+  extern __shared__ float ss[];          // [chunk][r] S rows, then [WARPS][64][RT] warp sums
+  float* red = ss + chunk * r;
+  const bool on_y = (int)blockIdx.x < gy;
+  const Planes big = on_y ? dY : X;
+  const long long ldb = on_y ? ldy : ldx;
+  const int C = on_y ? d_out : d_in;
+  const float* S = on_y ? U : du;
+  const float alpha = on_y ? s : 1.0f;
+  const int cb = on_y ? (int)blockIdx.x * 64 : ((int)blockIdx.x - gy) * 64;
+  const long long col0 = on_y ? 0 : d_out;
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  const int c = cb + lane * 2;
+  const int n0 = blockIdx.y * chunk;
+  const int n1 = min(N, n0 + chunk);
+  for (int i = threadIdx.x; i < (n1 - n0) * r; i += WARPS * 32) ss[i] = S[(long long)n0 * r + i];
+  __syncthreads();
+  float a0[RT], a1[RT];
+#pragma unroll
+  for (int j = 0; j < RT; ++j) a0[j] = a1[j] = 0.f;
+  if (c < C) {
+#pragma unroll 4
+    for (int n = n0 + warp; n < n1; n += WARPS) {
+      const float2 bv = load_planes2(big, (long long)n * ldb + c);
+      const float* sr = ss + (n - n0) * r;
+#pragma unroll
+      for (int j = 0; j < RT; ++j) {
+        if (j < r) {
+          const float sv = sr[j];
+          a0[j] += bv.x * sv;
+          a1[j] += bv.y * sv;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < RT; ++j) {
+    red[(warp * 64 + lane * 2) * RT + j] = a0[j];
+    red[(warp * 64 + lane * 2 + 1) * RT + j] = a1[j];
+  }
+  __syncthreads();
+  const long long ct = (long long)d_out + d_in;
+  for (int i = threadIdx.x; i < 64 * r; i += WARPS * 32) {
+    const int cc = i / r, j = i % r;
+    if (cb + cc >= C) continue;
+    float sum = 0.f;
+#pragma unroll
+    for (int w2 = 0; w2 < WARPS; ++w2) sum += red[(w2 * 64 + cc) * RT + j];
+    part[((long long)blockIdx.y * ct + col0 + cb + cc) * r + j] = alpha * sum;
+  }
+}
+
+// dB[c][j] = sum_chunk part[chunk][c][j] (c < d_out); dA[j][k] = sum_chunk part[chunk][d_out + k][j]
+__global__ void lora_bwd_reduce_kernel(const float* __restrict__ part, int nch, int d_out, int d_in, int r,
+                                       float* __restrict__ dB, float* __restrict__ dA) {
+  griddep_wait();
+  const long long total = ((long long)d_out + d_in) * r;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int b = 0; b < nch; ++b) s += part[(long long)b * total + i];
+    const int c = (int)(i / r), j = (int)(i % r);
+    if (c < d_out) dB[(long long)c * r + j] = s;
+    else dA[(long long)j * d_in + (c - d_out)] = s;
+  }
+}
+
+template <int RT>
+struct Bwd {
+  static int run(Planes dY, long long ldy, int d_out, Planes X, long long ldx, int d_in, const float* U,
+                 const float* bt, const float* A, int r, float s, int N, const Epilogue& e, float* du, float* part,
+                 cudaStream_t st) {
+    long long blocks = (N + 15) / 16;
+    if (blocks > 148 * 2) blocks = 148 * 2;
+    const size_t bbytes = (size_t)r * d_out * sizeof(float);
+    int rc = bbytes <= 48 * 1024
+                 ? launch_pdl(lora_bwd_rows_kernel<RT, true>, dim3((unsigned)blocks), dim3(256), bbytes, st, dY, ldy,
+                              d_out, d_in, bt, A, r, s, N, du, e)
+                 : launch_pdl(lora_bwd_rows_kernel<RT, false>, dim3((unsigned)blocks), dim3(256), 0, st, dY, ldy,
+                              d_out, d_in, bt, A, r, s, N, du, e);
+    if (rc) return rc;
+    int nch, chunk;
+    wgrad_chunks(N, r, nch, chunk);
+    constexpr int WARPS = WgradCfg<RT>::kWarps;
+    const size_t smem = ((size_t)chunk * r + (size_t)WARPS * 64 * RT) * sizeof(float);
+    if (smem > 48 * 1024) return -1;
+    const int gy = (d_out + 63) / 64, gx = (d_in + 63) / 64;
+    return launch_pdl(lora_bwd_wgrad_kernel<RT>, dim3((unsigned)(gy + gx), (unsigned)nch), dim3(WARPS * 32), smem, st,
+                      dY, ldy, d_out, U, X, ldx, d_in, (const float*)du, gy, N, r, s, chunk, part);
+  }
+};
+
 template <template <int> class F, typename... A>
 int by_rank(int r, A... a) {
   if (r <= 8) return F<8>::run(a...);
@@ -233,15 +420,15 @@ int by_rank(int r, A... a) {
 template <int RT>
 struct Down {
   static int run(Planes X, long long ldx, int N, int K, const float* W, int r, float alpha, float* out,
-                 cudaStream_t st) {
+                 const float* bsrc, int bc, float* bt, cudaStream_t st) {
     long long blocks = (N + 15) / 16;
     if (blocks > 148 * 2) blocks = 148 * 2;
     const size_t wbytes = (size_t)r * K * sizeof(float);
     if (wbytes <= 48 * 1024)
       return launch_pdl(lora_down_kernel<RT, true>, dim3((unsigned)blocks), dim3(256), wbytes, st, X, ldx, N, K, W, r,
-                        alpha, out);
+                        alpha, out, bsrc, bc, bt);
     return launch_pdl(lora_down_kernel<RT, false>, dim3((unsigned)blocks), dim3(256), 0, st, X, ldx, N, K, W, r,
-                      alpha, out);
+                      alpha, out, bsrc, bc, bt);
   }
 };
 
@@ -270,9 +457,9 @@ bool rank_ok(int r) { return r >= 1 && r <= kLoraMaxRank; }
 }  // namespace
 
 int launch_lora_down(Planes X, long long ldx, int N, int K, const float* W, int r, float alpha, float* out,
-                     cudaStream_t st) {
-  if (!rank_ok(r) || N <= 0 || K <= 0 || K % 4 || ldx % 4) return -1;
-  return by_rank<Down>(r, X, ldx, N, K, W, r, alpha, out, st) ? -3 : 0;
+                     cudaStream_t st, const float* b_src, int b_rows, float* bt_out) {
+  if (!rank_ok(r) || N <= 0 || K <= 0 || K % 4 || ldx % 4 || (bt_out && (!b_src || b_rows <= 0))) return -1;
+  return by_rank<Down>(r, X, ldx, N, K, W, r, alpha, out, b_src, b_rows, bt_out, st) ? -3 : 0;
 }
 
 int launch_lora_up(const float* U, int N, int r, const float* W, int C, float alpha, const Epilogue& e,
@@ -300,6 +487,32 @@ int launch_lora_wgrad(Planes Big, long long ldb, const float* S, int N, int C, i
   if (blocks > 148 * 8) blocks = 148 * 8;
   return launch_pdl(lora_wgrad_reduce_kernel, dim3((unsigned)blocks), dim3(256), 0, st, partial, nch, C, r, alpha,
                     out, o_sc, o_sj)
+             ? -3 : 0;
+}
+
+long long lora_bwd_partial_floats(int N, int d_out, int d_in, int r) {
+  if (!rank_ok(r) || N <= 0) return 0;
+  int nch, chunk;
+  wgrad_chunks(N, r, nch, chunk);
+  return (long long)nch * ((long long)d_out + d_in) * r;
+}
+
+int launch_lora_backward(Planes dY, long long ldy, int d_out, Planes X, long long ldx, int d_in, const float* U,
+                         const float* bt, const float* A, int r, float s, int N, const Epilogue& edx, float* du,
+                         float* part, float* dB, float* dA, cudaStream_t st) {
+  if (r < 1 || r > kLoraBwdMaxRank || N <= 0 || d_out % 4 || d_in % 4 || ldy % 4 || ldx % 4 || edx.n_div % 4 ||
+      edx.m_s0 % 4 || edx.m_s1 % 4 || edx.n_s1 % 4)
+    return -1;
+  const int rc = r <= 8 ? Bwd<8>::run(dY, ldy, d_out, X, ldx, d_in, U, bt, A, r, s, N, edx, du, part, st)
+                        : Bwd<16>::run(dY, ldy, d_out, X, ldx, d_in, U, bt, A, r, s, N, edx, du, part, st);
+  if (rc) return rc < 0 ? rc : -3;
+  int nch, chunk;
+  wgrad_chunks(N, r, nch, chunk);
+  const long long total = ((long long)d_out + d_in) * r;
+  long long blocks = (total + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  return launch_pdl(lora_bwd_reduce_kernel, dim3((unsigned)blocks), dim3(256), 0, st, (const float*)part, nch, d_out,
+                    d_in, r, dB, dA)
              ? -3 : 0;
 }
 

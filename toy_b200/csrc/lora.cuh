@@ -16,9 +16,23 @@ namespace tb2 {
 
 constexpr int kLoraMaxRank = 64;
 
-// out[n][j] = alpha * sum_k X[n][k] * W[j][k]     (X planes [N][ldx], W [r][K])
+// out[n][j] = alpha * sum_k X[n][k] * W[j][k]     (X planes [N][ldx], W [r][K]).
+// With bt_out set, the same launch also writes bt_out[j][c] = b_src[c][j]
+// (b_src [b_rows][r]): an adapter's B transposed for the splice.
 int launch_lora_down(Planes X, long long ldx, int N, int K, const float* W, int r, float alpha, float* out,
-                     cudaStream_t st);
+                     cudaStream_t st, const float* b_src = nullptr, int b_rows = 0, float* bt_out = nullptr);
+
+// The whole adapter backward of one projection in three launches (r <= 16):
+// a row pass du = s dY B (into du [N][r]) and dX(n, k) += sum_j du[n][j] A[j][k]
+// (epilogue addressing, as lora_up); one launch of token-chunk partials of
+// dB = s dY^T u ([d_out][r]) and dA = du^T X ([r][d_in]); their fixed-order
+// sum. dY planes [N][ldy] (d_out columns), X planes [N][ldx], U = u [N][r],
+// bt = B^T [r][d_out], A [r][d_in]; `part` holds lora_bwd_partial_floats.
+constexpr int kLoraBwdMaxRank = 16;
+long long lora_bwd_partial_floats(int N, int d_out, int d_in, int r);
+int launch_lora_backward(Planes dY, long long ldy, int d_out, Planes X, long long ldx, int d_in, const float* U,
+                         const float* bt, const float* A, int r, float s, int N, const Epilogue& edx, float* du,
+                         float* part, float* dB, float* dA, cudaStream_t st);
 
 // Y(n, c) += alpha * sum_j U[n][j] * W[j][c]     (U [N][r], W [r][C]); Y(n, c)
 // is e.out[epi offset of (z = 0, m = n, n = c)] (gemm.cuh Epilogue addressing;

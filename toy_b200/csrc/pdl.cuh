@@ -28,4 +28,25 @@ int launch_pdl(void (*kernel)(KParams...), dim3 grid, dim3 block, size_t smem, c
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...) == cudaSuccess ? 0 : -3;
 }
 
+// The same launch with thread-block clusters of `cluster_x` CTAs along x.
+template <typename... KParams, typename... Args>
+int launch_pdl_cluster(void (*kernel)(KParams...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, int cluster_x,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = cluster_x;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...) == cudaSuccess ? 0 : -3;
+}
+
 }  // namespace tb2
