@@ -368,9 +368,16 @@ int LlamaEngine::realize() {
   if (!flash_) dS_ = pl(att);
   dqkv_ = pl((long long)N * W);
   if (!full) {
-    du32_ = f32((long long)N * r);
-    lora_part_ = f32(std::max(lora_wgrad_partial_floats(N, std::max(std::max(d, ff), H * dh), r),
-                              lora_bwd_partial_floats(N, std::max(ff, H * dh), d, r)));
+    du32_ = f32((long long)kLoraMaxSegs * N * r);   // du of each adapter of a group
+    long long part = std::max(lora_wgrad_partial_floats(N, std::max(std::max(d, ff), H * dh), r),
+                              lora_bwd_partial_floats(N, std::max(ff, H * dh), d, r));
+    if (r <= 16) {
+      part = std::max(part, lora_group_partial_floats(N, r, d, W, 3));             // q|k|v
+      part = std::max(part, lora_group_partial_floats(N, r, d, 2 * ff, 2));        // gate|up
+      part = std::max(part, lora_group_partial_floats(N, r, H * dh, d, 1));        // o
+      part = std::max(part, lora_group_partial_floats(N, r, ff, d, 1));            // down
+    }
+    lora_part_ = f32(part);
   }
   hp_ = f32(8);
   bufs_.emplace_back();
@@ -772,10 +779,9 @@ LoraAddend LlamaEngine::lora_addend(int l, int t, int c0, int d_out) const {
   return a;
 }
 
-// Y[:, col_off : col_off + d_out] += s * (X A^T) B^T as a separate kernel (for
-// base GEMMs without a fused epilogue), saving u = X A^T for the backward.
-int LlamaEngine::lora_forward(int l, int t, Planes X, int d_in, float* Y, long long ldy, int col_off, int d_out) {
-  CK(lora_prep(l, t, X, d_in, d_out));
+// Y[:, col_off : col_off + d_out] += s * u B^T as a separate kernel (for base
+// GEMMs without a fused epilogue); u and B^T come from lora_group_prep.
+int LlamaEngine::lora_forward(int l, int t, float* Y, long long ldy, int col_off, int d_out) {
   const LoraAddend a = lora_addend(l, t, col_off, d_out);
   KL(launch_lora_up(a.u, N(), a.r, a.bt, d_out, a.scale, epi_rowmajor(kEpiAccumF32, Y + col_off, ldy), stream_));
   return 0;
@@ -811,6 +817,93 @@ int LlamaEngine::lora_backward(int l, int t, Planes X, int d_in, Planes dY, long
   return 0;
 }
 
+LlamaEngine::LoraGroup LlamaEngine::lora_group(int g) const {
+  const LlamaConfig& c = cfg_;
+  const int d = c.d_model, H = c.n_heads, KV = c.n_kv, dh = c.d_head, ff = c.d_ff;
+  LoraGroup G;
+  auto add = [&](int t, int c0, int w) {
+    if (c.mode == 1 && (c.lora_targets & (1 << t))) {
+      G.t[G.n] = t; G.c0[G.n] = c0; G.w[G.n] = w;
+      ++G.n;
+    }
+  };
+  if (g == kGroupQKV) {
+    add(kLoraQ, 0, H * dh);
+    add(kLoraK, H * dh, KV * dh);
+    add(kLoraV, (H + KV) * dh, KV * dh);
+  } else if (g == kGroupO) {
+    add(kLoraO, 0, d);
+  } else if (g == kGroupGU) {
+    add(kLoraGate, 0, ff);
+    add(kLoraUp, ff, ff);
+  } else {
+    add(kLoraDown, 0, d);
+  }
+  return G;
+}
+
+int LlamaEngine::lora_group_prep(int l, const LoraGroup& G, Planes X, int d_in) {
+  const int N = this->N(), r = cfg_.lora_rank;
+  if (r > 16) {
+    for (int i = 0; i < G.n; ++i) CK(lora_prep(l, G.t[i], X, d_in, G.w[i]));
+    return 0;
+  }
+  LoraSegs segs;
+  for (int i = 0; i < G.n; ++i) {
+    const std::string pre = "blk." + std::to_string(l) + "." + kProjName[G.t[i]];
+    LoraSeg& sg = segs.s[segs.n++];
+    sg.col_off = 0; sg.width = d_in;
+    sg.w = P32(P(pre + ".lora_a"));
+    sg.alpha = 1.0f;
+    sg.out = lora_u_[l][G.t[i]];
+    sg.b_src = P32(P(pre + ".lora_b")); sg.b_rows = G.w[i]; sg.bt = lora_bt_[l][G.t[i]];
+  }
+  KL(launch_lora_down_group(X, d_in, N, r, segs, stream_));
+  return 0;
+}
+
+int LlamaEngine::lora_group_du(int l, const LoraGroup& G, Planes dY, long long ld_dy, int d_in, Epilogue& dx_epi) {
+  const int N = this->N(), r = cfg_.lora_rank;
+  const float s = cfg_.lora_alpha / (float)r;
+  LoraSegs segs;
+  for (int i = 0; i < G.n; ++i) {
+    LoraSeg& sg = segs.s[segs.n++];
+    sg.col_off = G.c0[i]; sg.width = G.w[i];
+    sg.w = lora_bt_[l][G.t[i]];
+    sg.alpha = s;
+    sg.out = du32_ + (long long)i * N * r;
+  }
+  KL(launch_lora_down_group(dY, ld_dy, N, r, segs, stream_));
+  for (int i = 0; i < G.n; ++i) {
+    const std::string pre = "blk." + std::to_string(l) + "." + kProjName[G.t[i]];
+    LoraAddend& a = dx_epi.lora[dx_epi.n_lora++];
+    a.u = du32_ + (long long)i * N * r;
+    a.bt = P32(P(pre + ".lora_a"));   // A [r][d_in]: dX += du A
+    a.c0 = 0;
+    a.width = d_in;
+    a.r = r;
+    a.scale = 1.0f;
+  }
+  return 0;
+}
+
+int LlamaEngine::lora_group_wgrad(int l, const LoraGroup& G, Planes X, int d_in, Planes dY, long long ld_dy) {
+  const int N = this->N(), r = cfg_.lora_rank;
+  const float s = cfg_.lora_alpha / (float)r;
+  LoraWgGroup g;
+  for (int i = 0; i < G.n; ++i) {
+    const std::string pre = "blk." + std::to_string(l) + "." + kProjName[G.t[i]];
+    LoraWgSeg& sg = g.s[g.n++];
+    sg.col_off = G.c0[i]; sg.width = G.w[i];
+    sg.u = lora_u_[l][G.t[i]];
+    sg.du = du32_ + (long long)i * N * r;
+    sg.dB = G32(P(pre + ".lora_b"));
+    sg.dA = G32(P(pre + ".lora_a"));
+  }
+  KL(launch_lora_wgrad_group(dY, ld_dy, X, d_in, d_in, N, r, s, g, lora_part_, stream_));
+  return 0;
+}
+
 int LlamaEngine::enqueue_forward() {
   const LlamaConfig& c = cfg_;
   const int N = this->N(), d = c.d_model, H = c.n_heads, KV = c.n_kv, dh = c.d_head, ff = c.d_ff, T = c.T, B = c.B;
@@ -837,17 +930,18 @@ int LlamaEngine::enqueue_forward() {
       ro.q_hi = Qh_[l].hi; ro.q_lo = Qh_[l].lo; ro.k_hi = Kh_[l].hi; ro.k_lo = Kh_[l].lo;
       ro.v_hi = Vh_[l].hi; ro.v_lo = Vh_[l].lo;
       ro.T = T; ro.H = H; ro.KV = KV; ro.dh = dh;
-      for (int i = 0; i < 3 && lora; ++i)
-        if (c.lora_targets & (1 << qkv_t[i])) {
-          CK(lora_prep(l, qkv_t[i], h1_[l], d, qkv_w[i]));
-          g.epi.lora[g.epi.n_lora++] = lora_addend(l, qkv_t[i], qkv_c0[i], qkv_w[i]);
-        }
+      const LoraGroup Gq = lora_group(kGroupQKV);
+      if (Gq.n) {
+        CK(lora_group_prep(l, Gq, h1_[l], d));
+        for (int i = 0; i < Gq.n; ++i) g.epi.lora[g.epi.n_lora++] = lora_addend(l, Gq.t[i], Gq.c0[i], Gq.w[i]);
+      }
       CK(gemm(g));
     } else {
       g.epi = epi_rowmajor(kEpiStoreF32, qkv_, W);
       CK(gemm(g));
-      for (int i = 0; i < 3 && lora; ++i)
-        if (c.lora_targets & (1 << qkv_t[i])) CK(lora_forward(l, qkv_t[i], h1_[l], d, qkv_, W, qkv_c0[i], qkv_w[i]));
+      const LoraGroup Gq = lora_group(kGroupQKV);
+      if (Gq.n) CK(lora_group_prep(l, Gq, h1_[l], d));
+      for (int i = 0; i < Gq.n; ++i) CK(lora_forward(l, Gq.t[i], qkv_, W, Gq.c0[i], Gq.w[i]));
       KL(launch_rope_qkv_fwd(qkv_, bias, pos_, cs_, cs_rows_, Qh_[l], Kh_[l], Vh_[l], B, T, H, KV, dh, stream_));
     }
     if (flash_) {
@@ -881,8 +975,9 @@ int LlamaEngine::enqueue_forward() {
     gw.b = wop(P(pre + "attn_output.weight"), d, H * dh, H * dh, 0);
     gw.epi = epi_rowmajor(kEpiResidF32, x1_[l], d);
     gw.epi.res = x_[l];
-    if (lora && (c.lora_targets & (1 << kLoraO))) {
-      CK(lora_prep(l, kLoraO, O_[l], H * dh, d));
+    const LoraGroup Go = lora_group(kGroupO);
+    if (Go.n) {
+      CK(lora_group_prep(l, Go, O_[l], H * dh));
       gw.epi.lora[gw.epi.n_lora++] = lora_addend(l, kLoraO, 0, d);
     }
     CK(gemm(gw));
@@ -900,20 +995,18 @@ int LlamaEngine::enqueue_forward() {
       // SwiGLU as its own kernel.)
       gg.epi = epi_rowmajor(kEpiSwiGLU, gu_[l], 2 * ff);
       gg.epi.out_hi = a_[l].hi; gg.epi.out_lo = a_[l].lo; gg.epi.pair_off = ff;
-      if (lora && (c.lora_targets & (1 << kLoraGate))) {
-        CK(lora_prep(l, kLoraGate, h2_[l], d, ff));
-        gg.epi.lora[gg.epi.n_lora++] = lora_addend(l, kLoraGate, 0, ff);
-      }
-      if (lora && (c.lora_targets & (1 << kLoraUp))) {
-        CK(lora_prep(l, kLoraUp, h2_[l], d, ff));
-        gg.epi.lora[gg.epi.n_lora++] = lora_addend(l, kLoraUp, ff, ff);
+      const LoraGroup Gg = lora_group(kGroupGU);
+      if (Gg.n) {
+        CK(lora_group_prep(l, Gg, h2_[l], d));
+        for (int i = 0; i < Gg.n; ++i) gg.epi.lora[gg.epi.n_lora++] = lora_addend(l, Gg.t[i], Gg.c0[i], Gg.w[i]);
       }
       CK(gemm(gg));
     } else {
       gg.epi = epi_rowmajor(kEpiStoreF32, gu_[l], 2 * ff);
       CK(gemm(gg));
-      if (lora && (c.lora_targets & (1 << kLoraGate))) CK(lora_forward(l, kLoraGate, h2_[l], d, gu_[l], 2 * ff, 0, ff));
-      if (lora && (c.lora_targets & (1 << kLoraUp))) CK(lora_forward(l, kLoraUp, h2_[l], d, gu_[l], 2 * ff, ff, ff));
+      const LoraGroup Gg = lora_group(kGroupGU);
+      if (Gg.n) CK(lora_group_prep(l, Gg, h2_[l], d));
+      for (int i = 0; i < Gg.n; ++i) CK(lora_forward(l, Gg.t[i], gu_[l], 2 * ff, Gg.c0[i], Gg.w[i]));
       KL(launch_swiglu_fwd(gu_[l], a_[l], N, ff, stream_));
     }
     GemmDesc gd;
@@ -922,8 +1015,9 @@ int LlamaEngine::enqueue_forward() {
     gd.b = wop(P(pre + "ffn_down.weight"), d, ff, ff, 0);
     gd.epi = epi_rowmajor(kEpiResidF32, x_[l + 1], d);
     gd.epi.res = x1_[l];
-    if (lora && (c.lora_targets & (1 << kLoraDown))) {
-      CK(lora_prep(l, kLoraDown, a_[l], ff, d));
+    const LoraGroup Gd = lora_group(kGroupDown);
+    if (Gd.n) {
+      CK(lora_group_prep(l, Gd, a_[l], ff));
       gd.epi.lora[gd.epi.n_lora++] = lora_addend(l, kLoraDown, 0, d);
     }
     CK(gemm(gd));
@@ -980,7 +1074,11 @@ int LlamaEngine::enqueue_backward() {
     gda.a = op(dxp_, N, d, d, 0);
     gda.b = wop(Wd, d, ff, ff, 1);
     gda.epi = epi_rowmajor(kEpiStoreF32, da_, ff);
+    const LoraGroup Gd = lora_group(kGroupDown);
+    const bool gd_grp = Gd.n && lora_grouped(ff);
+    if (gd_grp) CK(lora_group_du(l, Gd, dxp_, d, ff, gda.epi));
     CK(gemm(gda));
+    if (gd_grp) CK(lora_group_wgrad(l, Gd, a_[l], ff, dxp_, d));
     if (full) {
       GemmDesc gw;
       gw.M = d; gw.N = ff; gw.K = N;
@@ -989,15 +1087,18 @@ int LlamaEngine::enqueue_backward() {
       gw.epi = epi_rowmajor(kEpiStoreF32, G32(Wd), ff);
       CK(gemm(gw));
     }
-    if (lora && (c.lora_targets & (1 << kLoraDown)))
-      CK(lora_backward(l, kLoraDown, a_[l], ff, dxp_, d, 0, d, da_, nullptr));
+    if (Gd.n && !gd_grp) CK(lora_backward(l, kLoraDown, a_[l], ff, dxp_, d, 0, d, da_, nullptr));
     KL(launch_swiglu_bwd(gu_[l], da_, dgu_, N, ff, stream_));
     GemmDesc gh;
     gh.M = N; gh.N = d; gh.K = 2 * ff;
     gh.a = op(dgu_, N, 2 * ff, 2 * ff, 0);
     gh.b = wop(Wg, 2 * ff, d, d, 1);
     gh.epi = epi_rowmajor(kEpiStoreF32, dh_, d);
+    const LoraGroup Gg = lora_group(kGroupGU);
+    const bool gg_grp = Gg.n && lora_grouped(d);
+    if (gg_grp) CK(lora_group_du(l, Gg, dgu_, 2 * ff, d, gh.epi));
     CK(gemm(gh));
+    if (gg_grp) CK(lora_group_wgrad(l, Gg, h2_[l], d, dgu_, 2 * ff));
     if (full) {
       GemmDesc gw;
       gw.M = 2 * ff; gw.N = d; gw.K = N;
@@ -1006,10 +1107,8 @@ int LlamaEngine::enqueue_backward() {
       gw.epi = epi_rowmajor(kEpiStoreF32, G32(Wg), d);
       CK(gemm(gw));
     }
-    if (lora && (c.lora_targets & (1 << kLoraGate)))
-      CK(lora_backward(l, kLoraGate, h2_[l], d, dgu_, 2 * ff, 0, ff, dh_, nullptr));
-    if (lora && (c.lora_targets & (1 << kLoraUp)))
-      CK(lora_backward(l, kLoraUp, h2_[l], d, dgu_, 2 * ff, ff, ff, dh_, nullptr));
+    for (int i = 0; i < Gg.n && !gg_grp; ++i)
+      CK(lora_backward(l, Gg.t[i], h2_[l], d, dgu_, 2 * ff, Gg.c0[i], Gg.w[i], dh_, nullptr));
     const Param& g2 = P(pre + "ffn_norm.weight");
     KL(launch_rmsnorm_bwd(x1_[l], dh_, P32(g2), dx_, dx_, dxp_, gpart_, nblk, N, d, c.rms_eps, stream_));
     if (full) KL(launch_colsum(gpart_, nblk, d, G32(g2), 0, stream_));
@@ -1022,7 +1121,11 @@ int LlamaEngine::enqueue_backward() {
     gdo.a = op(dxp_, N, d, d, 0);
     gdo.b = wop(Wo, d, H * dh, H * dh, 1);
     gdo.epi = hm;
+    const LoraGroup Go = lora_group(kGroupO);
+    const bool go_grp = Go.n && lora_grouped(H * dh);
+    if (go_grp) CK(lora_group_du(l, Go, dxp_, d, H * dh, gdo.epi));
     CK(gemm(gdo));
+    if (go_grp) CK(lora_group_wgrad(l, Go, O_[l], H * dh, dxp_, d));
     if (full) {
       GemmDesc gw;
       gw.M = d; gw.N = H * dh; gw.K = N;
@@ -1031,8 +1134,7 @@ int LlamaEngine::enqueue_backward() {
       gw.epi = epi_rowmajor(kEpiStoreF32, G32(Wo), H * dh);
       CK(gemm(gw));
     }
-    if (lora && (c.lora_targets & (1 << kLoraO)))
-      CK(lora_backward(l, kLoraO, O_[l], H * dh, dxp_, d, 0, d, dO32_, &hm));
+    if (Go.n && !go_grp) CK(lora_backward(l, kLoraO, O_[l], H * dh, dxp_, d, 0, d, dO32_, &hm));
     if (flash_) {
       // ---- attention core, fused: partial dQ / dK / dV summed by the RoPE backward
       KL(launch_flash_bwd_prep(dO32_, O_[l], dO_, dvec_, B, T, H, dh, stream_));
@@ -1080,7 +1182,11 @@ int LlamaEngine::enqueue_backward() {
     gx.a = op(dqkv_, N, W, W, 0);
     gx.b = wop(Wq, W, d, d, 1);
     gx.epi = epi_rowmajor(kEpiStoreF32, dh_, d);
+    const LoraGroup Gq = lora_group(kGroupQKV);
+    const bool gq_grp = Gq.n && lora_grouped(d);
+    if (gq_grp) CK(lora_group_du(l, Gq, dqkv_, W, d, gx.epi));
     CK(gemm(gx));
+    if (gq_grp) CK(lora_group_wgrad(l, Gq, h1_[l], d, dqkv_, W));
     if (full) {
       GemmDesc gw;
       gw.M = W; gw.N = d; gw.K = N;
@@ -1089,12 +1195,8 @@ int LlamaEngine::enqueue_backward() {
       gw.epi = epi_rowmajor(kEpiStoreF32, G32(Wq), d);
       CK(gemm(gw));
     }
-    if (lora && (c.lora_targets & (1 << kLoraQ)))
-      CK(lora_backward(l, kLoraQ, h1_[l], d, dqkv_, W, 0, H * dh, dh_, nullptr));
-    if (lora && (c.lora_targets & (1 << kLoraK)))
-      CK(lora_backward(l, kLoraK, h1_[l], d, dqkv_, W, H * dh, KV * dh, dh_, nullptr));
-    if (lora && (c.lora_targets & (1 << kLoraV)))
-      CK(lora_backward(l, kLoraV, h1_[l], d, dqkv_, W, (H + KV) * dh, KV * dh, dh_, nullptr));
+    for (int i = 0; i < Gq.n && !gq_grp; ++i)
+      CK(lora_backward(l, Gq.t[i], h1_[l], d, dqkv_, W, Gq.c0[i], Gq.w[i], dh_, nullptr));
     const Param& g1 = P(pre + "attn_norm.weight");
     KL(launch_rmsnorm_bwd(x_[l], dh_, P32(g1), dx_, dx_, dxp_, gpart_, nblk, N, d, c.rms_eps, stream_));
     if (full) KL(launch_colsum(gpart_, nblk, d, G32(g1), 0, stream_));

@@ -126,11 +126,28 @@ class LlamaEngine {
   int enqueue_optimizer();
   int enqueue_step(bool run_optimizer);
   int gemm(const GemmDesc& d);
-  int lora_forward(int l, int t, Planes X, int d_in, float* Y, long long ldy, int col_off, int d_out);
+  int lora_forward(int l, int t, float* Y, long long ldy, int col_off, int d_out);
   int lora_prep(int l, int t, Planes X, int d_in, int d_out);
   LoraAddend lora_addend(int l, int t, int c0, int d_out) const;
   int lora_backward(int l, int t, Planes X, int d_in, Planes dY, long long ld_dy, int col_off, int d_out,
                     float* dX, const Epilogue* dx_scatter);
+  // Adapter groups: the enabled adapters whose base projections form one GEMM
+  // (kGroupQKV: q|k|v, kGroupO, kGroupGU: gate|up, kGroupDown), with their
+  // first column and width in the GEMM's output.
+  enum { kGroupQKV = 0, kGroupO, kGroupGU, kGroupDown };
+  struct LoraGroup {
+    int n = 0;
+    int t[3] = {0, 0, 0}, c0[3] = {0, 0, 0}, w[3] = {0, 0, 0};
+  };
+  LoraGroup lora_group(int g) const;
+  // forward: u = X A^T and B^T of every adapter of the group, one launch
+  int lora_group_prep(int l, const LoraGroup& G, Planes X, int d_in);
+  // backward, before the group's dX GEMM: du = s dY B of every adapter (one
+  // launch) and the splices dX += du A as addends of that GEMM's epilogue
+  int lora_group_du(int l, const LoraGroup& G, Planes dY, long long ld_dy, int d_in, Epilogue& dx_epi);
+  // backward, after it: dB and dA of every adapter (partials + fixed-order sum)
+  int lora_group_wgrad(int l, const LoraGroup& G, Planes X, int d_in, Planes dY, long long ld_dy);
+  bool lora_grouped(int d_in) const { return cfg_.lora_rank <= 16 && d_in % 32 == 0; }
   float* P32(const Param& p) { return static_cast<float*>(p32_.p) + p.offset; }
   float* G32(const Param& p) { return static_cast<float*>(g_.p) + p.offset; }
   Planes PP(const Param& p) {

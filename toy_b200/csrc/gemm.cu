@@ -585,49 +585,53 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
     if constexpr (Q8) {
       const int ct = threadIdx.x - kThreads;
       const int sblk = args.q8_cols / 32;
+      // one Q8_0 block (item) per converter thread and k-block: tile row r,
+      // half c32 of the 64 columns and, MN-major, 64-column tile tj
+      static_assert(RB * 2 <= 32 * kConvWarps, "one item per converter thread");
+      const bool has_item = ct < RB * 2;
+      const int c32 = ct & 1;
+      const int r = args.b_mn ? (ct >> 1) & 63 : ct >> 1;
+      const int tj = args.b_mn ? ct >> 7 : 0;
       uint32_t it = 0;
       bool ok = true;
       for (int u = walker; u < args.units && ok; u += walkers) {
         const Unit w = decode<BN, BMT>(args, u);
         if (w.skip) continue;
         const int nb = w.n0 + (int)rank * RB;
+        // this item's scale for k-block kb (a global load, issued ahead of
+        // the stage wait so its latency overlaps the wait and the conversion)
+        auto scale_of = [&](int kb) -> float {
+          const int k0 = kb * BK;
+          int srow, sb;
+          if (!args.b_mn) {
+            if (!args.epi.pair_off) srow = nb + r;
+            else if (PAIR) srow = ((int)rank == 0 ? w.n0 / 2 : args.epi.pair_off + w.n0 / 2) + r;
+            else srow = r < BN / 2 ? w.n0 / 2 + r : args.epi.pair_off + w.n0 / 2 + r - BN / 2;
+            sb = (k0 >> 5) + c32;
+          } else {
+            srow = k0 + r;
+            sb = ((nb + 64 * tj) >> 5) + c32;
+          }
+          return (has_item && srow < args.q8_rows && sb < sblk)
+                     ? __half2float(__ushort_as_half(args.q8_scale[(long long)srow * sblk + sb]))
+                     : 0.f;
+        };
+        float sc_next = scale_of(w.kb0);
         for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
+          const float sc = sc_next;
+          if (kb + 1 < w.kb1) sc_next = scale_of(kb + 1);
           ok = warp_wait(&qfull[s], ph, args.err, kErrWaitFull);
           if (!ok) break;
           uint8_t* st = smem + s * kStageBytes;
           uint8_t* b_hi = st + kTileA;
           uint8_t* b_lo = st + 2 * kTileA + kTileB;
           const uint8_t* qs = st + 2 * (kTileA + kTileB);
-          const int k0 = kb * BK;
-#pragma unroll 1
-          for (int i = ct; i < RB * 2; i += 32 * kConvWarps) {
-            // item = one Q8_0 block: 32 quants of stored row `srow`, columns
-            // c32 * 32 .. +31 of this tile's 64
-            int r, srow, sb;
-            const int c32 = i & 1;
-            const uint8_t* src;
-            uint32_t tile;
-            if (!args.b_mn) {   // tile rows = output columns n, 64 k
-              r = i >> 1;
-              src = qs + r * 64 + c32 * 32;
-              if (!args.epi.pair_off) srow = nb + r;
-              else if (PAIR) srow = ((int)rank == 0 ? w.n0 / 2 : args.epi.pair_off + w.n0 / 2) + r;
-              else srow = r < BN / 2 ? w.n0 / 2 + r : args.epi.pair_off + w.n0 / 2 + r - BN / 2;
-              sb = (k0 >> 5) + c32;
-              tile = 0;
-            } else {            // BN / 64 tiles of 64 k rows x 64 n
-              const int j = i >> 7;
-              r = (i >> 1) & 63;
-              src = qs + j * 4096 + r * 64 + c32 * 32;
-              srow = k0 + r;
-              sb = ((nb + 64 * j) >> 5) + c32;
-              tile = (uint32_t)j * 8192u;
-            }
-            const float sc = (srow < args.q8_rows && sb < sblk)
-                                 ? __half2float(__ushort_as_half(args.q8_scale[(long long)srow * sblk + sb]))
-                                 : 0.f;
+          if (has_item) {
+            // item = one Q8_0 block: 32 quants of tile row r, columns c32 * 32 .. +31 of this tile's 64
+            const uint8_t* src = !args.b_mn ? qs + r * 64 + c32 * 32 : qs + tj * 4096 + r * 64 + c32 * 32;
+            const uint32_t tile = !args.b_mn ? 0u : (uint32_t)tj * 8192u;
             // the two 16-byte halves in a lane-dependent order: each 8-lane
             // phase of a shared load then touches 8 distinct bank groups
             const int sw = (lane >> 2) & 1;

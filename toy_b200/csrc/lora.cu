@@ -2,6 +2,8 @@
 // order, so results do not depend on scheduling.
 #include "lora.cuh"
 
+#include <algorithm>
+
 #include "pdl.cuh"
 
 namespace tb2 {
@@ -409,6 +411,212 @@ struct Bwd {
   }
 };
 
+// Group down pass: one warp per token row (two rows in flight). Every
+// adapter's w is staged in shared memory ([r][width] each, read as float4
+// along k: conflict-free). When all adapters read the same columns of X (the
+// forward: one normalised input, several adapters) each X chunk is loaded
+// once for all of them. Also writes the B^T copies.
+template <int RT, int NS, bool SHARED>
+__global__ void __launch_bounds__(256) lora_down_group_kernel(Planes X, long long ldx, int N, int r, LoraSegs g) {
+  griddep_wait();
+  extern __shared__ float4 wsm4[];
+  float* wsm = reinterpret_cast<float*>(wsm4);
+  int wofs[kLoraMaxSegs];
+  {
+    int o = 0;
+#pragma unroll
+    for (int a = 0; a < NS; ++a) {
+      wofs[a] = o;
+      o += r * g.s[a].width;
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < NS; ++a) {
+    const LoraSeg& sg = g.s[a];
+    for (int i = threadIdx.x * 4; i < r * sg.width; i += 256 * 4)
+      *reinterpret_cast<float4*>(wsm + wofs[a] + i) = __ldg(reinterpret_cast<const float4*>(sg.w + i));
+    if (sg.bt) {
+      for (long long i = blockIdx.x * 256LL + threadIdx.x; i < (long long)sg.b_rows * r;
+           i += (long long)gridDim.x * 256) {
+        const int c = (int)(i / r), j = (int)(i % r);
+        sg.bt[(long long)j * sg.b_rows + c] = sg.b_src[i];
+      }
+    }
+  }
+  __syncthreads();
+  const int lane = threadIdx.x % 32;
+  const int warps = gridDim.x * 8;
+  for (int n = (blockIdx.x * 8 + threadIdx.x / 32) * 2; n < N; n += warps * 2) {
+    const bool two = n + 1 < N;
+    float acc0[NS][RT], acc1[NS][RT];
+#pragma unroll
+    for (int a = 0; a < NS; ++a)
+#pragma unroll
+      for (int j = 0; j < RT; ++j) acc0[a][j] = acc1[a][j] = 0.f;
+    auto dot = [&](int a, int k, const float4& x0, const float4& x1) {
+      const int w = g.s[a].width;
+#pragma unroll
+      for (int j = 0; j < RT; ++j) {
+        if (j < r) {
+          const float4 wv = *reinterpret_cast<const float4*>(wsm + wofs[a] + j * w + k);
+          acc0[a][j] += x0.x * wv.x + x0.y * wv.y + x0.z * wv.z + x0.w * wv.w;
+          acc1[a][j] += x1.x * wv.x + x1.y * wv.y + x1.z * wv.z + x1.w * wv.w;
+        }
+      }
+    };
+    if constexpr (SHARED) {
+      const long long r0 = (long long)n * ldx + g.s[0].col_off;
+      for (int k = lane * 4; k < g.s[0].width; k += 128) {
+        const float4 x0 = load_planes4(X, r0 + k);
+        const float4 x1 = two ? load_planes4(X, r0 + ldx + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int a = 0; a < NS; ++a) dot(a, k, x0, x1);
+      }
+    } else {
+#pragma unroll
+      for (int a = 0; a < NS; ++a) {
+        const long long r0 = (long long)n * ldx + g.s[a].col_off;
+        for (int k = lane * 4; k < g.s[a].width; k += 128) {
+          const float4 x0 = load_planes4(X, r0 + k);
+          const float4 x1 = two ? load_planes4(X, r0 + ldx + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+          dot(a, k, x0, x1);
+        }
+      }
+    }
+#pragma unroll
+    for (int a = 0; a < NS; ++a) {
+#pragma unroll
+      for (int j = 0; j < RT; ++j) {
+        float v0 = acc0[a][j], v1 = acc1[a][j];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+          v0 += __shfl_xor_sync(0xffffffffu, v0, o);
+          v1 += __shfl_xor_sync(0xffffffffu, v1, o);
+        }
+        if (j < r && lane == (j & 31)) {
+          g.s[a].out[(long long)n * r + j] = g.s[a].alpha * v0;
+          if (two) g.s[a].out[(long long)(n + 1) * r + j] = g.s[a].alpha * v1;
+        }
+      }
+    }
+  }
+}
+
+template <int RT, int NS>
+int down_group(Planes X, long long ldx, int N, int r, const LoraSegs& segs, bool shared, size_t smem,
+               cudaStream_t st) {
+  static bool attr[2] = {false, false};
+  auto* k0 = lora_down_group_kernel<RT, NS, false>;
+  auto* k1 = lora_down_group_kernel<RT, NS, true>;
+  if (!attr[shared]) {
+    if (cudaFuncSetAttribute(shared ? k1 : k0, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
+        cudaSuccess)
+      return -3;
+    attr[shared] = true;
+  }
+  const unsigned blocks = (unsigned)std::min<long long>(148, (N + 15) / 16);
+  return shared ? launch_pdl(k1, dim3(blocks), dim3(256), smem, st, X, ldx, N, r, segs)
+                : launch_pdl(k0, dim3(blocks), dim3(256), smem, st, X, ldx, N, r, segs);
+}
+
+template <int RT>
+int down_group_ns(Planes X, long long ldx, int N, int r, const LoraSegs& segs, bool shared, size_t smem,
+                  cudaStream_t st) {
+  if (segs.n == 1) return down_group<RT, 1>(X, ldx, N, r, segs, shared, smem, st);
+  if (segs.n == 2) return down_group<RT, 2>(X, ldx, N, r, segs, shared, smem, st);
+  return down_group<RT, 3>(X, ldx, N, r, segs, shared, smem, st);
+}
+
+// Group weight-gradient partials. Factor f = 2 i (dB of adapter i: dY columns
+// col_off_i .., S = u_i, scaled by s) or 2 i + 1 (dA: X columns, S = du_i);
+// blockIdx.x walks the 64-column groups of all factors (gbase[f] = first
+// group of factor f), blockIdx.y the token chunks. Partials are [chunk][col][r]
+// over the concatenated columns (cbase[f] = first column of factor f).
+struct WgLayout {
+  int nf;
+  int gbase[2 * kLoraMaxSegs + 1];
+  int cbase[2 * kLoraMaxSegs + 1];
+};
+
+template <int RT>
+__global__ void __launch_bounds__(WgradCfg<RT>::kWarps * 32)
+    lora_wgrad_group_kernel(Planes dY, long long ldy, Planes X, long long ldx, int d_in, int N, int r, float s,
+                            int chunk, LoraWgGroup g, WgLayout lay, float* __restrict__ part) {
+  griddep_wait();
+  constexpr int WARPS = WgradCfg<RT>::kWarps;
+  extern __shared__ float ss[];   // [chunk][r] S rows, then [WARPS][64][RT] warp sums
+  float* red = ss + chunk * r;
+  int f = 0;
+  while (f + 1 < lay.nf && (int)blockIdx.x >= lay.gbase[f + 1]) ++f;
+  const LoraWgSeg& sg = g.s[f / 2];
+  const bool dB = (f & 1) == 0;
+  const Planes big = dB ? dY : X;
+  const long long ldb = dB ? ldy : ldx;
+  const int off = dB ? sg.col_off : 0;
+  const int C = dB ? sg.width : d_in;
+  const float* S = dB ? sg.u : sg.du;
+  const float alpha = dB ? s : 1.0f;
+  const int cb = ((int)blockIdx.x - lay.gbase[f]) * 64;
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  const int c = cb + lane * 2;
+  const int n0 = blockIdx.y * chunk;
+  const int n1 = min(N, n0 + chunk);
+  for (int i = threadIdx.x; i < (n1 - n0) * r; i += WARPS * 32) ss[i] = S[(long long)n0 * r + i];
+  __syncthreads();
+  float a0[RT], a1[RT];
+#pragma unroll
+  for (int j = 0; j < RT; ++j) a0[j] = a1[j] = 0.f;
+  if (c < C) {
+#pragma unroll 4
+    for (int n = n0 + warp; n < n1; n += WARPS) {
+      const float2 bv = load_planes2(big, (long long)n * ldb + off + c);
+      const float* sr = ss + (n - n0) * r;
+#pragma unroll
+      for (int j = 0; j < RT; ++j) {
+        if (j < r) {
+          const float sv = sr[j];
+          a0[j] += bv.x * sv;
+          a1[j] += bv.y * sv;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < RT; ++j) {
+    red[(warp * 64 + lane * 2) * RT + j] = a0[j];
+    red[(warp * 64 + lane * 2 + 1) * RT + j] = a1[j];
+  }
+  __syncthreads();
+  const long long ct = lay.cbase[lay.nf];
+  for (int i = threadIdx.x; i < 64 * r; i += WARPS * 32) {
+    const int cc = i / r, j = i % r;
+    if (cb + cc >= C) continue;
+    float sum = 0.f;
+#pragma unroll
+    for (int w2 = 0; w2 < WARPS; ++w2) sum += red[(w2 * 64 + cc) * RT + j];
+    part[((long long)blockIdx.y * ct + lay.cbase[f] + cb + cc) * r + j] = alpha * sum;
+  }
+}
+
+__global__ void lora_group_reduce_kernel(const float* __restrict__ part, int nch, int r, int d_in, LoraWgGroup g,
+                                         WgLayout lay) {
+  griddep_wait();
+  const long long ct = lay.cbase[lay.nf];
+  const long long total = ct * r;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int b = 0; b < nch; ++b) s += part[(long long)b * total + i];
+    const int col = (int)(i / r), j = (int)(i % r);
+    int f = 0;
+    while (f + 1 < lay.nf && col >= lay.cbase[f + 1]) ++f;
+    const LoraWgSeg& sg = g.s[f / 2];
+    const int c = col - lay.cbase[f];
+    if ((f & 1) == 0) sg.dB[(long long)c * r + j] = s;
+    else sg.dA[(long long)j * d_in + c] = s;
+  }
+}
+
 template <template <int> class F, typename... A>
 int by_rank(int r, A... a) {
   if (r <= 8) return F<8>::run(a...);
@@ -513,6 +721,74 @@ int launch_lora_backward(Planes dY, long long ldy, int d_out, Planes X, long lon
   if (blocks > 148 * 8) blocks = 148 * 8;
   return launch_pdl(lora_bwd_reduce_kernel, dim3((unsigned)blocks), dim3(256), 0, st, (const float*)part, nch, d_out,
                     d_in, r, dB, dA)
+             ? -3 : 0;
+}
+
+int launch_lora_down_group(Planes X, long long ldx, int N, int r, const LoraSegs& segs, cudaStream_t st) {
+  if (r < 1 || r > 16 || N <= 0 || segs.n < 1 || segs.n > kLoraMaxSegs || ldx % 4) return -1;
+  size_t wfloats = 0;
+  bool shared = true;
+  for (int a = 0; a < segs.n; ++a) {
+    const LoraSeg& sg = segs.s[a];
+    if (!sg.w || !sg.out || sg.width <= 0 || sg.width % 4 || sg.col_off % 4 || (sg.bt && (!sg.b_src || sg.b_rows <= 0)))
+      return -1;
+    wfloats += (size_t)r * sg.width;
+    shared = shared && sg.col_off == segs.s[0].col_off && sg.width == segs.s[0].width;
+  }
+  const size_t smem = wfloats * sizeof(float);
+  if (smem > 200 * 1024) return -1;
+  const int rc = r <= 8 ? down_group_ns<8>(X, ldx, N, r, segs, shared, smem, st)
+                        : down_group_ns<16>(X, ldx, N, r, segs, shared, smem, st);
+  return rc ? -3 : 0;
+}
+
+namespace {
+WgLayout wg_layout(const LoraWgGroup& g, int d_in) {
+  WgLayout l;
+  l.nf = 2 * g.n;
+  l.gbase[0] = l.cbase[0] = 0;
+  for (int f = 0; f < l.nf; ++f) {
+    const int C = (f & 1) ? d_in : g.s[f / 2].width;
+    l.gbase[f + 1] = l.gbase[f] + (C + 63) / 64;
+    l.cbase[f + 1] = l.cbase[f] + C;
+  }
+  return l;
+}
+}  // namespace
+
+long long lora_group_partial_floats(int N, int r, int d_in, int total_width, int n_adapters) {
+  if (r < 1 || r > 16 || N <= 0) return 0;
+  int nch, chunk;
+  wgrad_chunks(N, r, nch, chunk);
+  return (long long)nch * ((long long)total_width + (long long)n_adapters * d_in) * r;
+}
+
+int launch_lora_wgrad_group(Planes dY, long long ldy, Planes X, long long ldx, int d_in, int N, int r, float s,
+                            const LoraWgGroup& g, float* part, cudaStream_t st) {
+  if (r < 1 || r > 16 || N <= 0 || g.n < 1 || g.n > kLoraMaxSegs || d_in % 2 || ldy % 2 || ldx % 2) return -1;
+  for (int a = 0; a < g.n; ++a) {
+    const LoraWgSeg& sg = g.s[a];
+    if (!sg.u || !sg.du || !sg.dB || !sg.dA || sg.width <= 0 || sg.width % 2 || sg.col_off % 2) return -1;
+  }
+  const WgLayout lay = wg_layout(g, d_in);
+  int nch, chunk;
+  wgrad_chunks(N, r, nch, chunk);
+  int rc;
+  if (r <= 8) {
+    const size_t smem = ((size_t)chunk * r + (size_t)WgradCfg<8>::kWarps * 64 * 8) * sizeof(float);
+    rc = launch_pdl(lora_wgrad_group_kernel<8>, dim3((unsigned)lay.gbase[lay.nf], (unsigned)nch),
+                    dim3(WgradCfg<8>::kWarps * 32), smem, st, dY, ldy, X, ldx, d_in, N, r, s, chunk, g, lay, part);
+  } else {
+    const size_t smem = ((size_t)chunk * r + (size_t)WgradCfg<16>::kWarps * 64 * 16) * sizeof(float);
+    rc = launch_pdl(lora_wgrad_group_kernel<16>, dim3((unsigned)lay.gbase[lay.nf], (unsigned)nch),
+                    dim3(WgradCfg<16>::kWarps * 32), smem, st, dY, ldy, X, ldx, d_in, N, r, s, chunk, g, lay, part);
+  }
+  if (rc) return -3;
+  const long long total = (long long)lay.cbase[lay.nf] * r;
+  long long blocks = (total + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  return launch_pdl(lora_group_reduce_kernel, dim3((unsigned)blocks), dim3(256), 0, st, (const float*)part, nch, r, d_in,
+                    g, lay)
              ? -3 : 0;
 }
 

@@ -34,6 +34,48 @@ int launch_lora_backward(Planes dY, long long ldy, int d_out, Planes X, long lon
                          const float* bt, const float* A, int r, float s, int N, const Epilogue& edx, float* du,
                          float* part, float* dB, float* dA, cudaStream_t st);
 
+// ---- adapter groups: the adapters whose base projections form one GEMM
+// (q|k|v, gate|up, or a single projection) share one launch per pass.
+constexpr int kLoraMaxSegs = 3;
+
+// One adapter of a group for the down pass out[n][j] = alpha * sum_k
+// X[n][col_off + k] * w[j][k] (k < width); with bt set the launch also writes
+// bt[j][c] = b_src[c][j] for c < b_rows.
+struct LoraSeg {
+  int col_off = 0, width = 0;
+  const float* w = nullptr;
+  float alpha = 1.0f;
+  float* out = nullptr;
+  const float* b_src = nullptr;
+  int b_rows = 0;
+  float* bt = nullptr;
+};
+struct LoraSegs {
+  LoraSeg s[kLoraMaxSegs];
+  int n = 0;
+};
+// Every adapter of the group in one launch (r <= 16; X planes [N][ldx]).
+int launch_lora_down_group(Planes X, long long ldx, int N, int r, const LoraSegs& segs, cudaStream_t st);
+
+// Weight gradients of a group: for adapter i, dB_i[c][j] = s sum_n
+// dY[n][col_off_i + c] u_i[n][j] (c < width_i) and dA_i[j][k] = sum_n du_i[n][j]
+// X[n][k] (k < d_in), as token-chunk partials in one launch and their
+// fixed-order sum in a second (r <= 16).
+struct LoraWgSeg {
+  int col_off = 0, width = 0;
+  const float* u = nullptr;
+  const float* du = nullptr;
+  float* dB = nullptr;   // [width][r]
+  float* dA = nullptr;   // [r][d_in]
+};
+struct LoraWgGroup {
+  LoraWgSeg s[kLoraMaxSegs];
+  int n = 0;
+};
+long long lora_group_partial_floats(int N, int r, int d_in, int total_width, int n_adapters);
+int launch_lora_wgrad_group(Planes dY, long long ldy, Planes X, long long ldx, int d_in, int N, int r, float s,
+                            const LoraWgGroup& g, float* part, cudaStream_t st);
+
 // Y(n, c) += alpha * sum_j U[n][j] * W[j][c]     (U [N][r], W [r][C]); Y(n, c)
 // is e.out[epi offset of (z = 0, m = n, n = c)] (gemm.cuh Epilogue addressing;
 // e.n_div must be a multiple of 4, rows 16-byte aligned).
