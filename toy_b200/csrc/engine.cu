@@ -362,6 +362,8 @@ int LlamaEngine::realize() {
   gpart_ = f32((long long)rmsnorm_bwd_blocks() * d);
   xf_ = pl((long long)N * d);
   dlog_ = pl((long long)N * V);
+  lse_part_ = reinterpret_cast<float2*>(f32(2LL * ((V + 63) / 64) * N));
+  lse_ms_ = reinterpret_cast<float2*>(f32(2LL * N));
   dxp_ = pl((long long)N * d);
   dgu_ = pl((long long)N * 2 * ff);
   dO_ = pl((long long)N * H * dh);
@@ -1029,8 +1031,17 @@ int LlamaEngine::enqueue_forward() {
   gl.a = op(xf_, N, d, d, 0);
   gl.b = op(PP(Wout), V, d, d, 0);
   gl.epi = epi_rowmajor(kEpiStoreF32, logits_, V);
-  CK(gemm(gl));
-  KL(launch_cross_entropy(logits_, labels_, dense_labels_ ? labels_dense_ : nullptr, loss_rows_, dlog_, N, V, stream_));
+  if (!dense_labels_) {
+    // the LM head writes each row's vocab-chunk (max, sum exp) pairs with the
+    // logits; the cross-entropy then needs a single pass over them
+    gl.epi.mode = kEpiStoreLse;
+    gl.epi.lse_part = lse_part_;
+    CK(gemm(gl));
+    KL(launch_cross_entropy_lse(logits_, lse_part_, lse_ms_, labels_, loss_rows_, dlog_, N, V, stream_));
+  } else {
+    CK(gemm(gl));
+    KL(launch_cross_entropy(logits_, labels_, labels_dense_, loss_rows_, dlog_, N, V, stream_));
+  }
   KL(launch_loss_reduce(loss_rows_, N, loss_, stream_));
   return 0;
 }

@@ -179,6 +179,8 @@ class LlamaEngine {
   std::vector<std::vector<float*>> lora_u_;    // [layer][target] u = X A^T, f32 [N][r]
   std::vector<std::vector<float*>> lora_bt_;   // [layer][target] B^T, f32 [r][d_out] (this step's B)
   float* lora_part_ = nullptr;                 // weight-gradient partial sums
+  float2* lse_part_ = nullptr;                 // LM head: (max, sum exp) per 64-column vocab chunk [V/64][N]
+  float2* lse_ms_ = nullptr;                   // per row (max, sum exp) [N]
   float *qkv_ = nullptr, *S_ = nullptr, *logits_ = nullptr, *loss_rows_ = nullptr, *loss_ = nullptr;
   float *dx_ = nullptr, *dh_ = nullptr, *da_ = nullptr, *dO32_ = nullptr, *dQ_ = nullptr, *dK_ = nullptr,
         *dV_ = nullptr, *gpart_ = nullptr, *du32_ = nullptr;

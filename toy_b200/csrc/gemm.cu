@@ -137,7 +137,8 @@ __device__ __forceinline__ void epi_store(const Epilogue& e, int N, long long of
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] *= e.alpha;
   const bool full_chunk = nc + 32 <= N;
-  if (e.mode == kEpiStoreF32 || e.mode == kEpiAccumF32 || e.mode == kEpiResidF32 || e.mode == kEpiStoreBoth) {
+  if (e.mode == kEpiStoreF32 || e.mode == kEpiAccumF32 || e.mode == kEpiResidF32 || e.mode == kEpiStoreBoth ||
+      e.mode == kEpiStoreLse) {
     float* dst = e.out + off;
     if (full_chunk) {
       float4* d4 = reinterpret_cast<float4*>(dst);
@@ -703,6 +704,7 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
       }
       // split-K partial of split s: plain row-major [M][N] slab s of the workspace
       float* part = args.ws + (long long)(u % args.splits) * args.M * args.N + (long long)m * args.N;
+      float lse_m = -INFINITY, lse_s = 0.f;   // kEpiStoreLse: running pair of the current 64-column group
       // one 32-column chunk: drain TMEM, store (or write the partial); the
       // addend of the following chunk is prefetched into `next`
       auto chunk = [&](int c, const float4 (&cur)[8], float4 (&next)[8]) {
@@ -711,6 +713,33 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
         if (c == BN / 32 - 1) release_acc<PAIR>(&tempty[b], lane);   // accumulator read: back to the MMA issuer
         const int nc = w.n0 + c * 32;
         if (!row_ok || nc >= args.N) return;
+        if constexpr (!Q8) {   // (the LM head's operands are planes; Q8_0 kernels keep their registers)
+          if (e.mode == kEpiStoreLse) {
+            // (max, sum exp) of this row's valid columns in the chunk, merged
+            // with the other chunk of its 64-column group; written once per group
+            float cm = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (nc + i < args.N) cm = fmaxf(cm, v[i]);
+            // hardware exp2-based exponential (~2 ulp): these sums only set the
+            // normaliser, far inside the loss tolerance, and the four epilogue
+            // warps must keep pace with the main loop
+            float cs = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (nc + i < args.N) cs += __expf(v[i] - cm);
+            if ((c & 1) == 0) {
+              lse_m = cm;
+              lse_s = cs;
+            } else {
+              const float mm = fmaxf(lse_m, cm);
+              lse_s = lse_s * __expf(lse_m - mm) + cs * __expf(cm - mm);
+              lse_m = mm;
+            }
+            if ((c & 1) == 1 || nc + 32 >= args.N)
+              e.lse_part[(long long)(nc >> 6) * args.M + m] = make_float2(lse_m, lse_s);
+          }
+        }
         if (!direct) {
           if (nc + 32 <= args.N && (args.N & 3) == 0) {   // float4 stores need 16-byte aligned rows
             float4* p4 = reinterpret_cast<float4*>(part + nc);
@@ -902,7 +931,8 @@ Plan choose_plan(const GemmDesc& d, long long ws_floats, bool q8) {
   const int kb = (d.K + BK - 1) / BK;
   // fused epilogues act on whole output rows of a tile: no K splits
   const bool fused = d.epi.mode == kEpiRopeQKV || d.epi.mode == kEpiSwiGLU || d.epi.n_lora > 0;
-  const bool can_split = !d.causal && d.batch == 1 && ws_floats > 0 && !fused;
+  // the logsumexp epilogue reduces whole tile rows: no K splits either
+  const bool can_split = !d.causal && d.batch == 1 && ws_floats > 0 && !fused && d.epi.mode != kEpiStoreLse;
   const bool pair_ok = g_pair_mode != 0 && d.split && !d.causal && (g_pair_mode == 1 || pair_wins(d));
   Plan best;
   double best_t = 1e30;
@@ -918,7 +948,7 @@ Plan choose_plan(const GemmDesc& d, long long ws_floats, bool q8) {
       if (d.epi.mode == kEpiSwiGLU && q8 && !pair && bn != 128) continue;
       if (d.epi.mode == kEpiRopeQKV && bn % d.epi.rope.dh) continue;       // whole heads per tile
       int s_lo = 1, s_hi = 1;
-      if (d.splits > 0 && !fused) {
+      if (d.splits > 0 && !fused && d.epi.mode != kEpiStoreLse) {
         s_lo = s_hi = d.splits;
       } else if (can_split && kb >= 8) {
         s_hi = std::min(16, kb / 2);
@@ -993,7 +1023,7 @@ int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream
   k.kb_total = (d.K + BK - 1) / BK;
   k.causal = d.causal;
   const long long tiles = (long long)d.batch * k.tiles_m * k.tiles_n;
-  if (splits < 1) splits = 1;
+  if (splits < 1 || d.epi.mode == kEpiStoreLse) splits = 1;
   if (splits > k.kb_total) splits = k.kb_total;
   if (splits > 1 && (d.causal || d.batch != 1 || !sc.ws || (long long)splits * d.M * d.N > sc.ws_floats))
     splits = 1;
@@ -1068,6 +1098,9 @@ int gemm_launch(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStre
     return -3;
   }
   if (e.mode == kEpiRopeQKV && e.rope.dh != 64) return -3;
+  if (e.mode == kEpiStoreLse && (!e.lse_part || e.alpha != 1.0f || d.batch != 1 || e.m_div != (1 << 30) ||
+                                 e.n_div != (1 << 30) || d.b.q8))
+    return -3;
   const bool fused = e.mode == kEpiRopeQKV || e.mode == kEpiSwiGLU || e.n_lora > 0;
   if (fused && !d.split) return -3;
   const Plan pl = choose_plan(d, sc.ws ? sc.ws_floats : 0, d.b.q8 != nullptr);

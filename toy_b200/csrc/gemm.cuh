@@ -50,6 +50,8 @@ enum EpiMode : int {
   kEpiStoreBoth = 4,  // out = alpha * acc and (out_hi, out_lo) = split(alpha * acc)
   kEpiRopeQKV = 5,    // fused q|k|v projection: + bias, RoPE (NEOX) on q and k, head-major planes (Epilogue::rope)
   kEpiSwiGLU = 6,     // fused gate|up projection with paired B rows: out = gate|up f32, (out_hi, out_lo) = silu(g) u
+  kEpiStoreLse = 7,   // out = acc (logits), and per row and 64-column group the pair (max, sum exp(x - max))
+                      // written to lse_part[(n / 64) * M + m] (the vocab-chunked logsumexp of a cross-entropy)
 };
 
 // Low-rank adapter added to the accumulator before the epilogue mode (the
@@ -105,6 +107,8 @@ struct Epilogue {
   // out (f32 [M][2 ff], m_s0 = 2 ff) keeps gate | up for the backward and
   // (out_hi, out_lo) ([M][ff]) get silu(gate) * up.
   int pair_off = 0;
+  // kEpiStoreLse: [ceil(N / 64)][M] (max, sum exp) pairs
+  float2* lse_part = nullptr;
 };
 
 struct GemmDesc {

@@ -594,6 +594,64 @@ __global__ void __launch_bounds__(kCeThreads) cross_entropy_kernel(const float* 
   }
 }
 
+// Row statistics from the LM-head GEMM's vocab-chunk pairs: (max, sum exp(z -
+// max)) over the G = ceil(V / 64) chunks of row n, combined in chunk-slice
+// order (block: 32 rows x 8 slices; slice y takes chunks y, y + 8, ...).
+__global__ void __launch_bounds__(256) lse_combine_kernel(const float2* __restrict__ part, int G, int N,
+                                                          float2* __restrict__ ms) {
+  griddep_wait();
+  __shared__ float2 sm[8][32];
+  const int n = blockIdx.x * 32 + threadIdx.x % 32, y = threadIdx.x / 32;
+  float m = -INFINITY, s = 0.f;
+  if (n < N)
+    for (int g = y; g < G; g += 8) {
+      const float2 p = part[(long long)g * N + n];
+      ms_combine(m, s, p.x, p.y);
+    }
+  sm[y][threadIdx.x % 32] = make_float2(m, s);
+  __syncthreads();
+  if (y == 0 && n < N) {
+    for (int k = 1; k < 8; ++k) ms_combine(m, s, sm[k][threadIdx.x].x, sm[k][threadIdx.x].y);
+    ms[n] = make_float2(m, s);
+  }
+}
+
+// The cross-entropy gradient in one pass over the logits, given each row's
+// (max, sum exp): dz = (softmax(z) - onehot(label)) / N as planes; loss row =
+// lse - z[label] (0 for label -1).
+__global__ void __launch_bounds__(kCeThreads) cross_entropy_grad_kernel(const float* __restrict__ logits,
+                                                                        const float2* __restrict__ ms,
+                                                                        const int* __restrict__ label_ids,
+                                                                        float* __restrict__ loss_rows, Planes dl,
+                                                                        int N, int V) {
+  griddep_wait();
+  const float invN = 1.0f / (float)N;
+  for (int n = blockIdx.x; n < N; n += gridDim.x) {
+    const float2 st = ms[n];
+    const float M = st.x, inv = 1.0f / st.y;
+    const float* z = logits + (long long)n * V;
+    int lab = label_ids[n];
+    if (lab >= V) lab = -1;
+    if ((V % 4) == 0) {
+      const float4* z4 = reinterpret_cast<const float4*>(z);
+      for (int v = threadIdx.x; v < V / 4; v += blockDim.x) {
+        const float4 x = __ldcs(z4 + v);
+        float4 g = make_float4(expf(x.x - M) * inv, expf(x.y - M) * inv, expf(x.z - M) * inv, expf(x.w - M) * inv);
+        const int k = lab - 4 * v;
+        if (k == 0) g.x -= 1.0f;
+        if (k == 1) g.y -= 1.0f;
+        if (k == 2) g.z -= 1.0f;
+        if (k == 3) g.w -= 1.0f;
+        store_planes4(dl, (long long)n * V + 4 * v, make_float4(g.x * invN, g.y * invN, g.z * invN, g.w * invN));
+      }
+    } else {
+      for (int v = threadIdx.x; v < V; v += blockDim.x)
+        store_planes(dl, (long long)n * V + v, (expf(z[v] - M) * inv - (v == lab ? 1.0f : 0.0f)) * invN);
+    }
+    if (threadIdx.x == 0) loss_rows[n] = lab >= 0 ? M + logf(st.y) - z[lab] : 0.f;
+  }
+}
+
 __global__ void loss_reduce_kernel(const float* __restrict__ rows, int N, float* __restrict__ loss) {
   griddep_wait();
   __shared__ float sm[1024 / 32];
@@ -882,6 +940,16 @@ int launch_cross_entropy(const float* logits, const int* label_ids, const float*
                          Planes dlogits, int N, int V, cudaStream_t st) {
   int g = N < 4 * kSMs ? N : 4 * kSMs;
   launch_pdl(cross_entropy_kernel, dim3(g), dim3(kCeThreads), 0, st, logits, label_ids, label_dense, loss_rows, dlogits, N, V);
+  return ok();
+}
+
+int launch_cross_entropy_lse(const float* logits, const float2* lse_part, float2* ms, const int* label_ids,
+                             float* loss_rows, Planes dlogits, int N, int V, cudaStream_t st) {
+  launch_pdl(lse_combine_kernel, dim3((N + 31) / 32), dim3(256), 0, st, lse_part, (V + 63) / 64, N, ms);
+  if (ok()) return -3;
+  const int g = N < 4 * kSMs ? N : 4 * kSMs;
+  launch_pdl(cross_entropy_grad_kernel, dim3(g), dim3(kCeThreads), 0, st, logits, (const float2*)ms, label_ids,
+             loss_rows, dlogits, N, V);
   return ok();
 }
 

@@ -71,6 +71,12 @@ int launch_swiglu_bwd(const float* gu, const float* da, Planes dgu, int N, int f
 // label_dense != nullptr, a dense [N][V] distribution.
 int launch_cross_entropy(const float* logits, const int* label_ids, const float* label_dense, float* loss_rows,
                          Planes dlogits, int N, int V, cudaStream_t st);
+// The same for id labels, from the (max, sum exp) pairs of 64-column vocab
+// chunks the LM-head GEMM wrote (kEpiStoreLse, lse_part [ceil(V / 64)][N]):
+// one launch combines them per row into ms [N], one pass over the logits
+// writes the gradient planes and loss rows.
+int launch_cross_entropy_lse(const float* logits, const float2* lse_part, float2* ms, const int* label_ids,
+                             float* loss_rows, Planes dlogits, int N, int V, cudaStream_t st);
 // loss = sum(loss_rows) / N   (single block, fixed order)
 int launch_loss_reduce(const float* loss_rows, int N, float* loss, cudaStream_t st);
 
