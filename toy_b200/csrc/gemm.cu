@@ -198,7 +198,8 @@ __device__ __forceinline__ void epi_store(const Epilogue& e, int N, long long of
 // v(m, nc + i) += scale * sum_j u[m][j] * bt[j][nc + i - c0] for every LoRA
 // addend whose column range holds the chunk (ranges are multiples of 32). All
 // lanes of a warp read the same bt chunk (broadcast); u is the lane's own row.
-__device__ __forceinline__ void lora_add(const Epilogue& e, int m, int nc, float (&v)[32]) {
+template <int W>
+__device__ __forceinline__ void lora_add(const Epilogue& e, int m, int nc, float (&v)[W]) {
 #pragma unroll 1
   for (int a = 0; a < e.n_lora; ++a) {
     const LoraAddend& L = e.lora[a];
@@ -210,7 +211,7 @@ __device__ __forceinline__ void lora_add(const Epilogue& e, int m, int nc, float
       const float su = L.scale * ur[j];
       const float4* b4 = reinterpret_cast<const float4*>(bt + (long long)j * L.width);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
+      for (int q = 0; q < W / 4; ++q) {
         const float4 w4 = __ldg(b4 + q);
         v[4 * q] = fmaf(su, w4.x, v[4 * q]);
         v[4 * q + 1] = fmaf(su, w4.y, v[4 * q + 1]);
@@ -233,6 +234,18 @@ __device__ __forceinline__ void store_split32(__nv_bfloat16* hi, __nv_bfloat16* 
   }
 }
 
+// 16 values as hi / lo bf16 planes at 16-byte aligned addresses.
+__device__ __forceinline__ void store_split16(__nv_bfloat16* hi, __nv_bfloat16* lo, const float (&v)[16]) {
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) split_pair(v[8 * u + 2 * j], v[8 * u + 2 * j + 1], h[j], l[j]);
+    reinterpret_cast<uint4*>(hi)[u] = make_uint4(h[0], h[1], h[2], h[3]);
+    reinterpret_cast<uint4*>(lo)[u] = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
+
 // The warp has read its accumulator lanes: hand the accumulator back to the
 // MMA issuer (rank 0's barrier for a CTA pair).
 template <bool PAIR>
@@ -245,8 +258,9 @@ __device__ __forceinline__ void release_acc(uint64_t* tempty, int lane) {
   }
 }
 
-// kEpiRopeQKV for one tile row: one head (NCH chunks of 32 columns) at a time --
-// LoRA addends, bias, RoPE rotation of q / k heads by pos[m], head-major planes.
+// kEpiRopeQKV for one tile row: one head (NCH chunks of 32 columns) at a time,
+// sixteen rotation pairs per step -- LoRA addends, bias, RoPE rotation of q / k
+// heads by pos[m], head-major planes.
 template <int BN, int NCH, bool PAIR>
 __device__ __forceinline__ void epi_rope(const Epilogue& e, int m, int n0, bool row_ok, int N, uint32_t acc,
                                          uint64_t* tempty, int lane) {
@@ -262,20 +276,8 @@ __device__ __forceinline__ void epi_rope(const Epilogue& e, int m, int n0, bool 
   const float2* crow = reinterpret_cast<const float2*>(R.cs) + (long long)p * HALF;
 #pragma unroll 1
   for (int hb = 0; hb < BN; hb += DH) {
-    float v[NCH][32];
-#pragma unroll
-    for (int k = 0; k < NCH; ++k) tmem_ld32(acc + (uint32_t)(hb + 32 * k), v[k]);
-    if (hb + DH >= BN) release_acc<PAIR>(tempty, lane);
     const int c0 = n0 + hb;
-    if (!row_ok || c0 >= N) continue;
-#pragma unroll
-    for (int k = 0; k < NCH; ++k) {
-      if (e.n_lora) lora_add(e, m, c0 + 32 * k, v[k]);
-      if (R.bias) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[k][i] += R.bias[c0 + 32 * k + i];
-      }
-    }
+    const bool live = row_ok && c0 < N;
     const int slot = c0 / DH;
     __nv_bfloat16 *oh, *ol;
     long long dst;
@@ -291,34 +293,54 @@ __device__ __forceinline__ void epi_rope(const Epilogue& e, int m, int n0, bool 
       oh = R.v_hi; ol = R.v_lo;
       rot = false;
     }
-    if (rot) {
-      // pairs (j, j + dh/2): y0 = x0 cos - x1 sin, y1 = x0 sin + x1 cos
-#pragma unroll
-      for (int j = 0; j < HALF; ++j) {
-        const float2 c = crow[j];
-        const float x0 = v[j / 32][j % 32], x1 = v[(j + HALF) / 32][j % 32];
-        v[j / 32][j % 32] = x0 * c.x - x1 * c.y;
-        v[(j + HALF) / 32][j % 32] = x0 * c.y + x1 * c.x;
+    // rotation pairs (j, j + dh/2) sixteen at a time: x0 = columns j.., x1 = j + dh/2 ..
+#pragma unroll 1
+    for (int q = 0; q < HALF / 16; ++q) {
+      float x0[16], x1[16];
+      tmem_ld16(acc + (uint32_t)(hb + 16 * q), x0);
+      tmem_ld16(acc + (uint32_t)(hb + HALF + 16 * q), x1);
+      if (hb + DH >= BN && q == HALF / 16 - 1) release_acc<PAIR>(tempty, lane);
+      if (!live) continue;
+      const int ca = c0 + 16 * q, cb = c0 + HALF + 16 * q;
+      if (e.n_lora) {
+        lora_add(e, m, ca, x0);
+        lora_add(e, m, cb, x1);
       }
-    }
+      if (R.bias) {
 #pragma unroll
-    for (int k = 0; k < NCH; ++k) store_split32(oh + dst + 32 * k, ol + dst + 32 * k, v[k]);
+        for (int i = 0; i < 16; ++i) {
+          x0[i] += R.bias[ca + i];
+          x1[i] += R.bias[cb + i];
+        }
+      }
+      if (rot) {   // y0 = x0 cos - x1 sin, y1 = x0 sin + x1 cos
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 c = crow[16 * q + i];
+          const float a0 = x0[i], a1 = x1[i];
+          x0[i] = a0 * c.x - a1 * c.y;
+          x1[i] = a0 * c.y + a1 * c.x;
+        }
+      }
+      store_split16(oh + dst + 16 * q, ol + dst + 16 * q, x0);
+      store_split16(oh + dst + HALF + 16 * q, ol + dst + HALF + 16 * q, x1);
+    }
   }
 }
 
-// kEpiSwiGLU for one tile row of a 128-wide tile with paired B rows: columns
-// [0, 64) are gate features n0/2 .., [64, 128) the same up features.
+// kEpiSwiGLU for one tile row of a tile with paired B rows: columns [0, BN/2)
+// are gate features n0/2 .., [BN/2, BN) the same up features; 16 of each at a time.
 template <int BN, bool PAIR>
 __device__ __forceinline__ void epi_swiglu(const Epilogue& e, int m, int n0, bool row_ok, uint32_t acc,
                                            uint64_t* tempty, int lane) {
   const int ff = e.pair_off, f0 = n0 / 2;
 #pragma unroll 1
-  for (int k = 0; k < BN / 64; ++k) {
-    float g[32], u[32];
-    tmem_ld32(acc + (uint32_t)(32 * k), g);
-    tmem_ld32(acc + (uint32_t)(BN / 2 + 32 * k), u);
-    if (k == BN / 64 - 1) release_acc<PAIR>(tempty, lane);
-    const int fc = f0 + 32 * k;
+  for (int k = 0; k < BN / 32; ++k) {
+    float g[16], u[16];
+    tmem_ld16(acc + (uint32_t)(16 * k), g);
+    tmem_ld16(acc + (uint32_t)(BN / 2 + 16 * k), u);
+    if (k == BN / 32 - 1) release_acc<PAIR>(tempty, lane);
+    const int fc = f0 + 16 * k;
     if (!row_ok || fc >= ff) continue;
     if (e.n_lora) {
       lora_add(e, m, fc, g);        // gate columns [0, ff)
@@ -328,14 +350,14 @@ __device__ __forceinline__ void epi_swiglu(const Epilogue& e, int m, int n0, boo
     float4* og = reinterpret_cast<float4*>(orow + fc);
     float4* ou = reinterpret_cast<float4*>(orow + ff + fc);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < 4; ++i) {
       og[i] = make_float4(g[4 * i], g[4 * i + 1], g[4 * i + 2], g[4 * i + 3]);
       ou[i] = make_float4(u[4 * i], u[4 * i + 1], u[4 * i + 2], u[4 * i + 3]);
     }
     // silu with the hardware exp2 / reciprocal approximations (~1e-7 relative)
 #pragma unroll
-    for (int i = 0; i < 32; ++i) g[i] = __fdividef(g[i], 1.0f + __expf(-g[i])) * u[i];
-    store_split32(e.out_hi + (long long)m * ff + fc, e.out_lo + (long long)m * ff + fc, g);
+    for (int i = 0; i < 16; ++i) g[i] = __fdividef(g[i], 1.0f + __expf(-g[i])) * u[i];
+    store_split16(e.out_hi + (long long)m * ff + fc, e.out_lo + (long long)m * ff + fc, g);
   }
 }
 
