@@ -291,6 +291,17 @@ int tnn_zero_tensor(void *sess, void *tensor);
 /* Q8_0 blocks copied verbatim into a type-8 tensor (the bytes tinynn_gguf.c:634-682
  * copies from a GGUF file). No reference counterpart as a single call. */
 int tnn_upload_q8_0_blocks(void *sess, void *tensor, const void *blocks, size_t nbytes);
+/* tinynn_ggml.c:1715, tinynn_ggml.h:117 */
+void *tnn_input_1d_i32_persistent(void *sess, int n);
+void *tnn_input_3d_persistent_typed(void *sess, int ne0, int ne1, int ne2, int ggml_type);
+/* tinynn_ggml.h:120-131 -- weights whose bytes (F32 or Q8_0 blocks) sit at
+ * buf_offset inside a host region the caller attached (e.g. an mmap'd GGUF).
+ * The region stays the caller's; the bytes are copied to the device when the
+ * tensor is created, so the region may be unmapped afterwards. */
+int tnn_session_attach_weight_mmap(void *sess, void *base, size_t size);
+void *tnn_input_2d_persistent_mmap(void *sess, int rows, int cols, int ggml_type, size_t buf_offset);
+void *tnn_input_3d_persistent_mmap(void *sess, int ne0, int ne1, int ne2, int ggml_type, size_t buf_offset);
+void *tnn_input_1d_persistent_mmap(void *sess, int n, int ggml_type, size_t buf_offset);
 
 /* tinynn_ggml.h:157-400 — forward and backward ops */
 void *tnn_matmul(void *sess, void *a, void *b);          /* ggml_mul_mat: a [K,M,..] (f32 or Q8_0), b [K,N,..] -> [M,N,..] */
@@ -329,6 +340,17 @@ void *tnn_cross_entropy_loss(void *sess, void *a, void *b);
 void *tnn_sum(void *sess, void *a);
 void *tnn_sum_rows(void *sess, void *a);
 void *tnn_opt_step_adamw(void *sess, void *a, void *grad, void *m, void *v, void *params);
+/* tinynn_ggml.c:2044 -- p = p (1 - alpha wd) - alpha grad, params = [alpha, wd] */
+void *tnn_opt_step_sgd(void *sess, void *a, void *grad, void *params);
+/* tinynn_ggml.c:1335 (ggml_cast) -- to F32 (dtype 0) only: a copy of an F32
+ * tensor, or the dequantised values of a Q8_0 one; NULL for other dtypes. */
+void *tnn_cast(void *sess, void *a, int dtype);
+/* tinynn_ggml.h:251 (inference, as in the reference): q [dh, Tq, H, B], k, v
+ * [dh, Tk, KV, B], mask [Tk, >= Tq] or NULL -> [dh, H, Tq, B]; computed as
+ * softmax(scale k^T q + mask) v on the tensor-core GEMM. NULL for
+ * logit_softcap != 0 or max_bias != 0 (ALiBi). */
+void *tnn_flash_attn_ext(void *sess, void *q, void *k, void *v, void *mask, double scale, double max_bias,
+                         double logit_softcap);
 
 /* tinynn_ggml.h:376-469 — programs and autograd */
 void tnn_set_param(void *tensor);
@@ -343,6 +365,8 @@ int tnn_realize_backward(void *sess);
 void *tnn_tensor_grad(void *sess, void *tensor);
 int tnn_compute(void *sess);
 int tnn_reset_for_rebuild(void *sess);
+/* tinynn_ggml.h:376 -- every node here keeps its own buffer: a no-op (0) */
+int tnn_pin_all_graph_b_nodes(void *sess);
 
 /* tinynn_ggml.h:527-532 — graph introspection */
 int tnn_tensor_op(void *t);
@@ -358,6 +382,22 @@ void *tnn_graph_node(void *sess, int i);
 int tnn_upload_from_float_array(void *sess, void *tensor, const double *data, size_t n);
 int tnn_upload_from_int_array(void *sess, void *tensor, const long *data, size_t n);
 int tnn_download_to_f64_array(void *sess, void *tensor, double *dst, size_t n);
+/* tinynn_ggml.h:471-484,563-567 -- a 16 MiB f32 host staging area per session:
+ * element-wise set / get (f32, or i32 bits), bulk tnn_upload / tnn_download
+ * of a whole tensor through it, and statistics over its first n floats. */
+void tnn_scratch_set(void *sess, int idx, double v);
+double tnn_scratch_get(void *sess, int idx);
+void tnn_scratch_set_i32(void *sess, int idx, int value);
+int tnn_scratch_get_i32(void *sess, int idx);
+int tnn_upload(void *sess, void *tensor);
+int tnn_download(void *sess, void *tensor);
+double tnn_scratch_min_f32(void *sess, int n);
+double tnn_scratch_max_f32(void *sess, int n);
+double tnn_scratch_sum_abs_f32(void *sess, int n);
+int tnn_scratch_nan_count_f32(void *sess, int n);
+/* tinynn_ggml.h:493-497 -- the row-major (br x bc) matrix, transposed: its
+ * column j becomes elements j*br .. j*br + br - 1 of the tensor. */
+int tnn_upload_transposed_f64(void *sess, void *tensor, const double *src, int br, int bc);
 int tnn_tensor_ne0(void *t);
 int tnn_tensor_ne1(void *t);
 int tnn_tensor_ne2(void *t);

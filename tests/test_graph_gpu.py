@@ -428,3 +428,86 @@ def test_opt_step_adamw_graph(cuda):
         r = rel(g.get(t).reshape(ref[k].shape), ref[k])
         assert r < 1e-3, (k, r)
     g.close()
+
+
+def test_cast_sgd_and_flash_attn_ext(cuda):
+    from oracle import oracle as O
+    rng = np.random.default_rng(6)
+    g = Graph()
+    L, s = g.L, g.s
+    W = 0.05 * rng.standard_normal((6, 64))
+    wq = L.tnn_input_2d_persistent_typed(s, 6, 64, 8)
+    blocks = O.q8_0_quantize(W.astype(np.float32))
+    assert L.tnn_upload_q8_0_blocks(s, wq, blocks.ctypes.data, blocks.nbytes) == 0
+    deq = L.tnn_cast(s, wq, 0)                     # Q8_0 -> F32 (ggml_cast = CPY)
+    X = rng.standard_normal((3, 8))
+    cp = L.tnn_cast(s, g.f32(X), 0)
+    assert not L.tnn_cast(s, wq, 30)               # bf16 target: not supported
+    P0, G0 = rng.standard_normal(20), rng.standard_normal(20)
+    p, gr = g.f32(P0), g.f32(G0)
+    sgd = L.tnn_opt_step_sgd(s, p, gr, g.f32(np.array([0.1, 0.01])))
+    # attention: B = 2, H = 4 query heads over KV = 2, dh = 16, causal mask
+    B, Tq, Tk, H, KV, dh = 2, 5, 5, 4, 2, 16
+    Q = rng.standard_normal((B, H, Tq, dh)); K = rng.standard_normal((B, KV, Tk, dh)); V = rng.standard_normal((B, KV, Tk, dh))
+    mask = np.where(np.arange(Tk)[None, :] > np.arange(Tq)[:, None], -1e30, 0.0)
+    fa = L.tnn_flash_attn_ext(s, g.f32(Q), g.f32(K), g.f32(V), g.f32(mask), 0.25, 0.0, 0.0)
+    assert not L.tnn_flash_attn_ext(s, g.f32(Q), g.f32(K), g.f32(V), None, 0.25, 0.0, 30.0)   # softcap
+    r_deq, r_cp, r_sgd, r_fa = g.run([deq, cp, sgd, fa])
+    assert np.array_equal(r_deq.reshape(6, 64), O.q8_0_dequantize(blocks, 64).astype(np.float64))
+    assert rel(r_cp, np.float32(X)) == 0
+    ref = np.float32(P0) * (1 - 0.1 * 0.01) - 0.1 * np.float32(G0)
+    assert rel(r_sgd.reshape(-1), ref) < 1e-6
+    ref_o = np.zeros((B, Tq, H, dh))
+    for b in range(B):
+        for h in range(H):
+            sc = 0.25 * Q[b, h] @ K[b, h // 2].T + mask
+            ref_o[b, :, h] = softmax(sc) @ V[b, h // 2]
+    assert rel(r_fa.reshape(B, Tq, H, dh), ref_o) < 2e-5
+    g.close()
+
+
+def test_scratch_mmap_and_transposed_upload(cuda):
+    from oracle import oracle as O
+    rng = np.random.default_rng(7)
+    g = Graph()
+    L, s = g.L, g.s
+    # weights from an attached host region: F32 at offset 64, Q8_0 blocks at offset 64 + 4 * 24
+    F = rng.standard_normal((4, 6)).astype(np.float32)
+    Wq = (0.05 * rng.standard_normal((3, 32))).astype(np.float32)
+    qb = O.q8_0_quantize(Wq)
+    region = np.zeros(64 + F.nbytes + qb.nbytes + 16, np.uint8)
+    region[64:64 + F.nbytes] = F.view(np.uint8).reshape(-1)
+    region[64 + F.nbytes:64 + F.nbytes + qb.nbytes] = qb.reshape(-1)
+    assert L.tnn_session_attach_weight_mmap(s, region.ctypes.data, region.nbytes) == 0
+    tf = L.tnn_input_2d_persistent_mmap(s, 4, 6, 0, 64)
+    tq = L.tnn_input_2d_persistent_mmap(s, 3, 32, 8, 64 + F.nbytes)
+    assert tf and tq
+    assert not L.tnn_input_1d_persistent_mmap(s, 64, 0, region.nbytes - 8)    # past the region
+    assert np.array_equal(g.get(tf), F.astype(np.float64))
+    assert np.array_equal(g.get(tq), O.q8_0_dequantize(qb, 32).astype(np.float64))
+    # scratch staging: element-wise set, bulk upload, an op, bulk download, statistics
+    t = L.tnn_input_2d_f32_persistent(s, 2, 3)
+    vals = [1.5, -2.0, 0.25, 4.0, -0.5, 3.0]
+    for i, v in enumerate(vals):
+        L.tnn_scratch_set(s, i, v)
+    assert L.tnn_upload(s, t) == 0
+    y = L.tnn_scale(s, t, 2.0)
+    L.tnn_set_output(y)
+    assert L.tnn_realize(s, y) == 0 and L.tnn_compute(s) == 0
+    assert L.tnn_download(s, y) == 0
+    assert [L.tnn_scratch_get(s, i) for i in range(6)] == [2 * v for v in vals]
+    assert L.tnn_scratch_min_f32(s, 6) == -4.0 and L.tnn_scratch_max_f32(s, 6) == 8.0
+    assert L.tnn_scratch_sum_abs_f32(s, 6) == sum(2 * abs(v) for v in vals)
+    assert L.tnn_scratch_nan_count_f32(s, 6) == 0
+    ti = L.tnn_input_1d_i32_persistent(s, 4)
+    for i, v in enumerate([7, -1, 3, 100000]):
+        L.tnn_scratch_set_i32(s, i, v)
+    assert L.tnn_upload(s, ti) == 0 and L.tnn_download(s, ti) == 0
+    assert [L.tnn_scratch_get_i32(s, i) for i in range(4)] == [7, -1, 3, 100000]
+    # transposed upload: column j of a row-major (br x bc) matrix -> elements j*br ..
+    M = rng.standard_normal((3, 5))
+    tt = L.tnn_input_2d_f32_persistent(s, 5, 3)
+    assert L.tnn_upload_transposed_f64(s, tt, np.ascontiguousarray(M).ctypes.data_as(C.POINTER(C.c_double)), 3, 5) == 0
+    assert rel(g.get(tt), np.float32(M).T) == 0
+    assert L.tnn_pin_all_graph_b_nodes(s) == 0
+    g.close()

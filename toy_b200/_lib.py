@@ -164,6 +164,27 @@ _SIGS = [
     ("tnn_tensor_flags", I, [VP]),
     ("tnn_graph_n_nodes", I, [VP]),
     ("tnn_graph_node", VP, [VP, I]),
+    ("tnn_input_1d_i32_persistent", VP, [VP, I]),
+    ("tnn_input_3d_persistent_typed", VP, [VP, I, I, I, I]),
+    ("tnn_session_attach_weight_mmap", I, [VP, VP, SZ]),
+    ("tnn_input_2d_persistent_mmap", VP, [VP, I, I, I, SZ]),
+    ("tnn_input_3d_persistent_mmap", VP, [VP, I, I, I, I, SZ]),
+    ("tnn_input_1d_persistent_mmap", VP, [VP, I, I, SZ]),
+    ("tnn_opt_step_sgd", VP, [VP, VP, VP, VP]),
+    ("tnn_cast", VP, [VP, VP, I]),
+    ("tnn_flash_attn_ext", VP, [VP, VP, VP, VP, VP, D, D, D]),
+    ("tnn_pin_all_graph_b_nodes", I, [VP]),
+    ("tnn_scratch_set", None, [VP, I, D]),
+    ("tnn_scratch_get", D, [VP, I]),
+    ("tnn_scratch_set_i32", None, [VP, I, I]),
+    ("tnn_scratch_get_i32", I, [VP, I]),
+    ("tnn_upload", I, [VP, VP]),
+    ("tnn_download", I, [VP, VP]),
+    ("tnn_scratch_min_f32", D, [VP, I]),
+    ("tnn_scratch_max_f32", D, [VP, I]),
+    ("tnn_scratch_sum_abs_f32", D, [VP, I]),
+    ("tnn_scratch_nan_count_f32", I, [VP, I]),
+    ("tnn_upload_transposed_f64", I, [VP, VP, DP, I, I]),
 ]
 
 

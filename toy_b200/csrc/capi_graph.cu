@@ -2,6 +2,11 @@
 // creation, op nodes, realize / compute, autograd and introspection. Names,
 // arguments and NULL / negative-code error behaviour follow the reference
 // header; see graph.cu for the execution model.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
 #include "prims.cuh"
 #include "toy_b200.h"
 
@@ -290,6 +295,177 @@ int tnn_reset_for_rebuild(void* sess) {
   s->prim_realized = false;
   return 0;
 }
+void* tnn_input_1d_i32_persistent(void* sess, int n) { return input(sess, 26, n, 1, 1, 1, true); }
+void* tnn_input_3d_persistent_typed(void* sess, int ne0, int ne1, int ne2, int ggml_type) {
+  if (ggml_type != 0 && ggml_type != 8) return nullptr;
+  if (ggml_type == 8 && ne0 % 32) return nullptr;
+  return input(sess, ggml_type, ne0, ne1, ne2, 1, true);
+}
+void* tnn_cast(void* sess, void* a, int dtype) {
+  Session* s = graph_session(sess);
+  return s && mine(s, a) ? tb2::prim_cast(s, T(a), dtype) : nullptr;
+}
+void* tnn_flash_attn_ext(void* sess, void* q, void* k, void* v, void* mask, double scale, double max_bias,
+                         double logit_softcap) {
+  Session* s = graph_session(sess);
+  if (!s || !mine(s, q) || !mine(s, k) || !mine(s, v) || (mask && !mine(s, mask)) || logit_softcap != 0.0)
+    return nullptr;
+  return tb2::prim_flash_attn_ext(s, T(q), T(k), T(v), mask ? T(mask) : nullptr, scale, max_bias);
+}
+void* tnn_opt_step_sgd(void* sess, void* a, void* grad, void* params) {
+  Session* s = graph_session(sess);
+  if (!s || !mine(s, a) || !mine(s, grad) || !mine(s, params)) return nullptr;
+  return tb2::prim_opt_sgd(s, T(a), T(grad), T(params));
+}
+int tnn_pin_all_graph_b_nodes(void* sess) { return graph_session(sess) ? 0 : -1; }   // every node keeps its buffer
+
+// ---------------------------------------------------------------- weights from a host region (tinynn_ggml.h:120-131)
+int tnn_session_attach_weight_mmap(void* sess, void* base, size_t size) {
+  Session* s = graph_session(sess);
+  if (!s || !base || !size) return -1;
+  s->mmap_base = static_cast<const uint8_t*>(base);
+  s->mmap_size = size;
+  return 0;
+}
+
+namespace {
+// a persistent tensor whose bytes are copied from the attached region at buf_offset
+void* mmap_input(void* sess, int type, int ne0, int ne1, int ne2, size_t off) {
+  Session* s = graph_session(sess);
+  if (!s || !s->mmap_base || (type != 0 && type != 8) || (type == 8 && ne0 % 32)) return nullptr;
+  Tensor* t = tb2::prim_new(s, type, ne0, ne1, ne2, 1, tb2::kOpNone, true);
+  if (!t) return nullptr;
+  const size_t nbytes = type == 8 ? (size_t)t->nel() / 32 * 34 : (size_t)t->nel() * 4;
+  if (off > s->mmap_size || nbytes > s->mmap_size - off) return nullptr;
+  const uint8_t* src = s->mmap_base + off;
+  int rc;
+  if (type == 8) {
+    rc = tb2::prim_upload_q8_0(s, t, src, nbytes);
+  } else {
+    std::vector<float> h((size_t)t->nel());
+    std::memcpy(h.data(), src, nbytes);   // the region may be unaligned
+    rc = tb2::prim_upload_f32_raw(s, t, h.data(), h.size());
+  }
+  return rc ? nullptr : t;
+}
+}  // namespace
+
+void* tnn_input_2d_persistent_mmap(void* sess, int rows, int cols, int ggml_type, size_t buf_offset) {
+  return mmap_input(sess, ggml_type, cols, rows, 1, buf_offset);
+}
+void* tnn_input_3d_persistent_mmap(void* sess, int ne0, int ne1, int ne2, int ggml_type, size_t buf_offset) {
+  return mmap_input(sess, ggml_type, ne0, ne1, ne2, buf_offset);
+}
+void* tnn_input_1d_persistent_mmap(void* sess, int n, int ggml_type, size_t buf_offset) {
+  return mmap_input(sess, ggml_type, n, 1, 1, buf_offset);
+}
+
+// ---------------------------------------------------------------- scratch staging (tinynn_ggml.h:471-484,563-567)
+namespace {
+constexpr size_t kScratchFloats = (16u << 20) / 4;   // 16 MiB
+std::vector<float>* scratch_of(void* sess) {
+  if (!sess) return nullptr;
+  Session* s = S(sess);
+  if (s->scratch.empty()) s->scratch.assign(kScratchFloats, 0.0f);
+  return &s->scratch;
+}
+}  // namespace
+
+void tnn_scratch_set(void* sess, int idx, double v) {
+  auto* sc = scratch_of(sess);
+  if (sc && idx >= 0 && (size_t)idx < sc->size()) (*sc)[idx] = (float)v;
+}
+double tnn_scratch_get(void* sess, int idx) {
+  auto* sc = scratch_of(sess);
+  return sc && idx >= 0 && (size_t)idx < sc->size() ? (double)(*sc)[idx] : 0.0;
+}
+void tnn_scratch_set_i32(void* sess, int idx, int value) {
+  auto* sc = scratch_of(sess);
+  if (sc && idx >= 0 && (size_t)idx < sc->size()) std::memcpy(&(*sc)[idx], &value, 4);
+}
+int tnn_scratch_get_i32(void* sess, int idx) {
+  auto* sc = scratch_of(sess);
+  int v = 0;
+  if (sc && idx >= 0 && (size_t)idx < sc->size()) std::memcpy(&v, &(*sc)[idx], 4);
+  return v;
+}
+int tnn_upload(void* sess, void* tensor) {
+  auto* sc = scratch_of(sess);
+  if (!sc || !tensor || T(tensor)->sess != S(sess)) return -1;
+  Tensor* t = T(tensor);
+  const size_t n = (size_t)t->nel();
+  if (n > sc->size()) return -2;
+  const bool ints = t->type == 26 || t->role == Tensor::kIds || t->role == Tensor::kPos;
+  if (ints) {
+    std::vector<long> v(n);
+    for (size_t i = 0; i < n; ++i) {
+      int x;
+      std::memcpy(&x, &(*sc)[i], 4);
+      v[i] = x;
+    }
+    return tnn_upload_from_int_array(sess, tensor, v.data(), n);
+  }
+  if (t->role == Tensor::kPrim && t->type == 0) return tb2::prim_upload_f32_raw(S(sess), t, sc->data(), n);
+  std::vector<double> v(sc->begin(), sc->begin() + n);
+  return tnn_upload_from_float_array(sess, tensor, v.data(), n);
+}
+int tnn_download(void* sess, void* tensor) {
+  auto* sc = scratch_of(sess);
+  if (!sc || !tensor || T(tensor)->sess != S(sess)) return -1;
+  Tensor* t = T(tensor);
+  const size_t n = t->role == Tensor::kLoss ? 1 : (size_t)t->nel();
+  if (n > sc->size()) return -2;
+  if (t->role == Tensor::kPrim) {
+    if (t->type == 26) {
+      std::vector<float> f(n);
+      const int rc = tb2::prim_download_f32_raw(S(sess), t, f.data(), n);
+      for (size_t i = 0; i < n && !rc; ++i) tnn_scratch_set_i32(sess, (int)i, (int)f[i]);
+      return rc;
+    }
+    return tb2::prim_download_f32_raw(S(sess), t, sc->data(), n);
+  }
+  std::vector<double> v(n);
+  const int rc = tnn_download_to_f64_array(sess, tensor, v.data(), n);
+  for (size_t i = 0; i < n && !rc; ++i) (*sc)[i] = (float)v[i];
+  return rc;
+}
+int tnn_upload_transposed_f64(void* sess, void* tensor, const double* src, int br, int bc) {
+  if (!sess || !tensor || !src || br <= 0 || bc <= 0) return -1;
+  Tensor* t = T(tensor);
+  if ((long long)br * bc > t->nel()) return -2;
+  // column j of the row-major (br x bc) matrix becomes the contiguous run t[j * br ..]
+  std::vector<double> v((size_t)br * bc);
+  for (int j = 0; j < bc; ++j)
+    for (int i = 0; i < br; ++i) v[(size_t)j * br + i] = src[(size_t)i * bc + j];
+  return tnn_upload_from_float_array(sess, tensor, v.data(), v.size());
+}
+double tnn_scratch_min_f32(void* sess, int n) {
+  auto* sc = scratch_of(sess);
+  if (!sc || n <= 0) return 0.0;
+  float m = (*sc)[0];
+  for (int i = 1; i < n && (size_t)i < sc->size(); ++i) m = std::min(m, (*sc)[i]);
+  return m;
+}
+double tnn_scratch_max_f32(void* sess, int n) {
+  auto* sc = scratch_of(sess);
+  if (!sc || n <= 0) return 0.0;
+  float m = (*sc)[0];
+  for (int i = 1; i < n && (size_t)i < sc->size(); ++i) m = std::max(m, (*sc)[i]);
+  return m;
+}
+double tnn_scratch_sum_abs_f32(void* sess, int n) {
+  auto* sc = scratch_of(sess);
+  double a = 0.0;
+  for (int i = 0; sc && i < n && (size_t)i < sc->size(); ++i) a += std::fabs((double)(*sc)[i]);
+  return a;
+}
+int tnn_scratch_nan_count_f32(void* sess, int n) {
+  auto* sc = scratch_of(sess);
+  int c = 0;
+  for (int i = 0; sc && i < n && (size_t)i < sc->size(); ++i) c += std::isnan((*sc)[i]) ? 1 : 0;
+  return c;
+}
+
 int tnn_upload_q8_0_blocks(void* sess, void* tensor, const void* blocks, size_t nbytes) {
   Session* s = graph_session(sess);
   if (!s || !mine(s, tensor) || !blocks) return -1;

@@ -53,7 +53,7 @@ const char* prim_op_name(int op) {
       "RMS_NORM", "RMS_NORM_BACK", "ROPE", "ROPE_BACK", "SOFT_MAX", "SOFT_MAX_BACK", "DIAG_MASK_INF",
       "DIAG_MASK_ZERO", "TRANSPOSE", "CONT", "RESHAPE", "VIEW", "CONCAT", "SLICE", "GET_ROWS", "GET_ROWS_BACK",
       "CROSS_ENTROPY_LOSS", "CROSS_ENTROPY_LOSS_BACK", "SUM", "SUM_ROWS", "REPEAT", "REPEAT_BACK", "OPT_STEP_ADAMW",
-      "ACC_VIEW"};
+      "ACC_VIEW", "CPY", "OPT_STEP_SGD"};
   return op >= 0 && op < kOpCount ? names[op] : "?";
 }
 
@@ -517,6 +517,20 @@ __global__ void k_unpad(const float* __restrict__ src, float* __restrict__ o, in
   GRID_LOOP(i, n) o[i] = src[(i / cols) * ldp + i % cols];
 }
 
+// Q8_0 -> f32: value = fp16 scale * int8 quant (from the split quant / scale arrays)
+__global__ void k_dequant(const int8_t* __restrict__ q, const uint16_t* __restrict__ sc, float* __restrict__ o,
+                          long long n) {
+  griddep_wait();
+  GRID_LOOP(i, n) o[i] = __half2float(__ushort_as_half(sc[i / 32])) * (float)q[i];
+}
+
+// ggml opt_step_sgd: p = p (1 - alpha wd) - alpha g; hp = [alpha, wd]
+__global__ void k_sgd(float* __restrict__ p, const float* __restrict__ g, const float* __restrict__ hp, long long n) {
+  griddep_wait();
+  const float alpha = hp[0], keep = 1.0f - hp[0] * hp[1];
+  GRID_LOOP(i, n) p[i] = p[i] * keep - alpha * g[i];
+}
+
 #undef GRID_LOOP
 
 // ------------------------------------------------------------------ graph helpers
@@ -904,6 +918,61 @@ Tensor* prim_opt_adamw(Session* s, Tensor* a, Tensor* g, Tensor* m, Tensor* v, T
   return t;
 }
 
+Tensor* prim_opt_sgd(Session* s, Tensor* a, Tensor* g, Tensor* hp) {
+  if (!is_f32(a) || !is_f32(g) || !is_f32(hp) || a->nel() != g->nel() || hp->nel() < 2) return nullptr;
+  Tensor* t = prim_new(s, 0, a->ne[0], a->ne[1], a->ne[2], a->ne[3], kOpOptSgd, false);
+  if (t) {
+    t->src[0] = a; t->src[1] = g; t->src[2] = hp;
+    t->view_of = a;   // updated in place
+  }
+  return t;
+}
+
+Tensor* prim_cast(Session* s, Tensor* a, int type) {
+  if (!a || type != 0) return nullptr;
+  if (a->type == 0) return prim_cont(s, a, a->ne[0], a->ne[1], a->ne[2], a->ne[3]);
+  if (a->type != 8) return nullptr;
+  Tensor* t = prim_new(s, 0, a->ne[0], a->ne[1], a->ne[2], a->ne[3], kOpDequant, false);
+  if (t) t->src[0] = a;
+  return t;
+}
+
+Tensor* prim_flash_attn_ext(Session* s, Tensor* q, Tensor* k, Tensor* v, Tensor* mask, double scale,
+                            double max_bias) {
+  if (!is_f32(q) || !is_f32(k) || !is_f32(v) || q->ne[0] != k->ne[0] || !same_shape(k, v) || q->ne[3] != k->ne[3])
+    return nullptr;
+  Tensor* kq = prim_mul_mat(s, k, q);                                    // [Tk, Tq, H, B]
+  Tensor* p = kq ? prim_softmax(s, kq, mask, scale, max_bias) : nullptr;
+  Tensor* vt = p ? prim_permute(s, v, 1, 0, 2, 3) : nullptr;            // [Tk, dh, KV, B]
+  Tensor* o = vt ? prim_mul_mat(s, vt, p) : nullptr;                     // [dh, Tq, H, B]
+  return o ? prim_permute(s, o, 0, 2, 1, 3) : nullptr;                   // [dh, H, Tq, B]
+}
+
+int prim_upload_f32_raw(Session* s, Tensor* t, const float* src, size_t n) {
+  if (t->type != 0 || (long long)n > t->nel()) return -2;
+  if (prim_alloc(s, t)) return -3;
+  return cudaMemcpy(t->data, src, n * 4, cudaMemcpyHostToDevice) == cudaSuccess ? 0 : -3;
+}
+
+int prim_download_f32_raw(Session* s, Tensor* t, float* dst, size_t n) {
+  (void)s;
+  if (!t->data || (long long)n > t->nel()) return -2;
+  if (t->type == 8) {
+    std::vector<double> d(n);
+    const int rc = prim_download_f64(s, t, d.data(), n);
+    for (size_t i = 0; i < n && !rc; ++i) dst[i] = (float)d[i];
+    return rc;
+  }
+  if (cudaDeviceSynchronize() != cudaSuccess) return -3;
+  if (t->type == 26) {
+    std::vector<int> h(n);
+    if (cudaMemcpy(h.data(), t->data, n * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return -3;
+    for (size_t i = 0; i < n; ++i) dst[i] = (float)h[i];
+    return 0;
+  }
+  return cudaMemcpy(dst, t->data, n * 4, cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -3;
+}
+
 // ------------------------------------------------------------------ execution
 namespace {
 
@@ -1073,6 +1142,12 @@ int exec(Session* s, Tensor* t) {
     case kOpSumRows:
       return launch_pdl(k_sum_rows, dim3(grid_for(t->nel() * 32, threads)), dim3(threads), 0, st, F(a), F(t),
                         a->rows(), a->ne[0]);
+    case kOpDequant:
+      return launch_pdl(k_dequant, dim3(grid_for(n, threads)), dim3(threads), 0, st, (const int8_t*)a->q8v,
+                        (const uint16_t*)a->q8s, F(t), n);
+    case kOpOptSgd:
+      return launch_pdl(k_sgd, dim3(grid_for(n, threads)), dim3(threads), 0, st, F(a), (const float*)F(b),
+                        (const float*)F(t->src[2]), n);
     case kOpOptAdamw:
       return launch_pdl(k_adamw, dim3(grid_for(n, threads)), dim3(threads), 0, st, F(a), (const float*)F(b),
                         F(t->src[2]), F(t->src[3]), (const float*)F(t->src[4]), n);

@@ -9,7 +9,7 @@ enum PrimOp : int {
   kOpNone = 0, kOpAdd, kOpSub, kOpMul, kOpScale, kOpSilu, kOpSiluBack, kOpSwiglu, kOpMulMat, kOpOutProd, kOpMulMatAT,
   kOpRmsNorm, kOpRmsNormBack, kOpRope, kOpRopeBack, kOpSoftMax, kOpSoftMaxBack, kOpDiagMaskInf, kOpDiagMaskZero,
   kOpTranspose, kOpCont, kOpReshape, kOpView, kOpConcat, kOpSlice, kOpGetRows, kOpGetRowsBack, kOpCrossEntropy,
-  kOpCrossEntropyBack, kOpSum, kOpSumRows, kOpRepeat, kOpRepeatBack, kOpOptAdamw, kOpAccView, kOpCount
+  kOpCrossEntropyBack, kOpSum, kOpSumRows, kOpRepeat, kOpRepeatBack, kOpOptAdamw, kOpAccView, kOpDequant, kOpOptSgd, kOpCount
 };
 const char* prim_op_name(int op);
 
@@ -45,6 +45,13 @@ Tensor* prim_get_rows_back(Session* s, Tensor* g, Tensor* idx, Tensor* like);
 Tensor* prim_cross_entropy(Session* s, Tensor* a, Tensor* b);
 Tensor* prim_sum(Session* s, int op, Tensor* a);                        // kOpSum / kOpSumRows
 Tensor* prim_opt_adamw(Session* s, Tensor* a, Tensor* g, Tensor* m, Tensor* v, Tensor* hp);
+Tensor* prim_opt_sgd(Session* s, Tensor* a, Tensor* g, Tensor* hp);     // hp = [alpha, wd]
+Tensor* prim_cast(Session* s, Tensor* a, int type);                    // to F32: copy, or Q8_0 dequantised
+// ggml_flash_attn_ext semantics (inference): q [dh, Tq, H, B], k / v [dh, Tk, KV, B],
+// mask [Tk, >= Tq] or null -> [dh, H, Tq, B]; composed of score product, softmax, value product
+Tensor* prim_flash_attn_ext(Session* s, Tensor* q, Tensor* k, Tensor* v, Tensor* mask, double scale, double max_bias);
+int prim_upload_f32_raw(Session* s, Tensor* t, const float* src, size_t n);
+int prim_download_f32_raw(Session* s, Tensor* t, float* dst, size_t n);
 
 // programs
 int prim_build_forward(Session* s, Tensor* result);

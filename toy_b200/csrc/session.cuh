@@ -68,6 +68,10 @@ struct Session {
   bool bwd_built = false;
   bool reset_pending = false;     // zero optimizer moments at the next backward
   cudaStream_t pstream = nullptr;
+  // tnn_scratch_* host staging (16 MiB of f32) and the attached weight region
+  std::vector<float> scratch;
+  const uint8_t* mmap_base = nullptr;
+  size_t mmap_size = 0;
   ~Session();
 };
 
