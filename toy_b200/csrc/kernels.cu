@@ -596,22 +596,24 @@ __global__ void __launch_bounds__(kCeThreads) cross_entropy_kernel(const float* 
 
 // Row statistics from the LM-head GEMM's vocab-chunk pairs: (max, sum exp(z -
 // max)) over the G = ceil(V / 64) chunks of row n, combined in chunk-slice
-// order (block: 32 rows x 8 slices; slice y takes chunks y, y + 8, ...).
-__global__ void __launch_bounds__(256) lse_combine_kernel(const float2* __restrict__ part, int G, int N,
-                                                          float2* __restrict__ ms) {
+// order (block: 32 rows x 32 slices; slice y takes chunks y, y + 32, ...;
+// then the slices in order).
+__global__ void __launch_bounds__(1024) lse_combine_kernel(const float2* __restrict__ part, int G, int N,
+                                                           float2* __restrict__ ms) {
   griddep_wait();
-  __shared__ float2 sm[8][32];
-  const int n = blockIdx.x * 32 + threadIdx.x % 32, y = threadIdx.x / 32;
+  __shared__ float2 sm[32][33];
+  const int x = threadIdx.x % 32, y = threadIdx.x / 32;
+  const int n = blockIdx.x * 32 + x;
   float m = -INFINITY, s = 0.f;
   if (n < N)
-    for (int g = y; g < G; g += 8) {
+    for (int g = y; g < G; g += 32) {
       const float2 p = part[(long long)g * N + n];
       ms_combine(m, s, p.x, p.y);
     }
-  sm[y][threadIdx.x % 32] = make_float2(m, s);
+  sm[y][x] = make_float2(m, s);
   __syncthreads();
   if (y == 0 && n < N) {
-    for (int k = 1; k < 8; ++k) ms_combine(m, s, sm[k][threadIdx.x].x, sm[k][threadIdx.x].y);
+    for (int k = 1; k < 32; ++k) ms_combine(m, s, sm[k][x].x, sm[k][x].y);
     ms[n] = make_float2(m, s);
   }
 }
@@ -945,7 +947,7 @@ int launch_cross_entropy(const float* logits, const int* label_ids, const float*
 
 int launch_cross_entropy_lse(const float* logits, const float2* lse_part, float2* ms, const int* label_ids,
                              float* loss_rows, Planes dlogits, int N, int V, cudaStream_t st) {
-  launch_pdl(lse_combine_kernel, dim3((N + 31) / 32), dim3(256), 0, st, lse_part, (V + 63) / 64, N, ms);
+  launch_pdl(lse_combine_kernel, dim3((N + 31) / 32), dim3(1024), 0, st, lse_part, (V + 63) / 64, N, ms);
   if (ok()) return -3;
   const int g = N < 4 * kSMs ? N : 4 * kSMs;
   launch_pdl(cross_entropy_grad_kernel, dim3(g), dim3(kCeThreads), 0, st, logits, (const float2*)ms, label_ids,
