@@ -844,6 +844,40 @@ LlamaEngine::LoraGroup LlamaEngine::lora_group(int g) const {
   return G;
 }
 
+// RMSNorm of x into h, and -- for the group of adapters that read h -- their
+// down-projections u = h A^T and B^T copies in the same pass when possible.
+int LlamaEngine::rmsnorm_lora(int l, const float* x, const float* gamma, Planes h, const LoraGroup& G) {
+  const LlamaConfig& c = cfg_;
+  const int N = this->N(), d = c.d_model;
+  if (G.n && c.lora_rank <= 16) {
+    LoraSegs segs = lora_group_segs(l, G, d);
+    if (profiling_) prof_begin(kKRmsFwd, 0.0);
+    const int rc = launch_rmsnorm_fwd_lora(x, gamma, h, N, d, c.rms_eps, c.lora_rank, segs, stream_);
+    if (profiling_) prof_end();
+    if (rc != -2) {   // -2: no variant for this width, run the two passes below
+      ++counting_;
+      return rc;
+    }
+  }
+  KL(launch_rmsnorm_fwd(x, gamma, h, N, d, c.rms_eps, stream_));
+  if (G.n) CK(lora_group_prep(l, G, h, d));
+  return 0;
+}
+
+LoraSegs LlamaEngine::lora_group_segs(int l, const LoraGroup& G, int d_in) {
+  LoraSegs segs;
+  for (int i = 0; i < G.n; ++i) {
+    const std::string pre = "blk." + std::to_string(l) + "." + kProjName[G.t[i]];
+    LoraSeg& sg = segs.s[segs.n++];
+    sg.col_off = 0; sg.width = d_in;
+    sg.w = P32(P(pre + ".lora_a"));
+    sg.alpha = 1.0f;
+    sg.out = lora_u_[l][G.t[i]];
+    sg.b_src = P32(P(pre + ".lora_b")); sg.b_rows = G.w[i]; sg.bt = lora_bt_[l][G.t[i]];
+  }
+  return segs;
+}
+
 int LlamaEngine::lora_group_prep(int l, const LoraGroup& G, Planes X, int d_in) {
   const int N = this->N(), r = cfg_.lora_rank;
   if (r > 16) {
@@ -916,7 +950,8 @@ int LlamaEngine::enqueue_forward() {
   KL(launch_embed_gather(P32(E), ids_, x_[0], N, d, stream_));
   for (int l = 0; l < c.n_layers; ++l) {
     const std::string pre = "blk." + std::to_string(l) + ".";
-    KL(launch_rmsnorm_fwd(x_[l], P32(P(pre + "attn_norm.weight")), h1_[l], N, d, c.rms_eps, stream_));
+    const LoraGroup Gq = lora_group(kGroupQKV);
+    CK(rmsnorm_lora(l, x_[l], P32(P(pre + "attn_norm.weight")), h1_[l], Gq));   // + the q|k|v adapters' u
     GemmDesc g;
     g.M = N; g.N = W; g.K = d;
     g.a = op(h1_[l], N, d, d, 0);
@@ -932,17 +967,11 @@ int LlamaEngine::enqueue_forward() {
       ro.q_hi = Qh_[l].hi; ro.q_lo = Qh_[l].lo; ro.k_hi = Kh_[l].hi; ro.k_lo = Kh_[l].lo;
       ro.v_hi = Vh_[l].hi; ro.v_lo = Vh_[l].lo;
       ro.T = T; ro.H = H; ro.KV = KV; ro.dh = dh;
-      const LoraGroup Gq = lora_group(kGroupQKV);
-      if (Gq.n) {
-        CK(lora_group_prep(l, Gq, h1_[l], d));
-        for (int i = 0; i < Gq.n; ++i) g.epi.lora[g.epi.n_lora++] = lora_addend(l, Gq.t[i], Gq.c0[i], Gq.w[i]);
-      }
+      for (int i = 0; i < Gq.n; ++i) g.epi.lora[g.epi.n_lora++] = lora_addend(l, Gq.t[i], Gq.c0[i], Gq.w[i]);
       CK(gemm(g));
     } else {
       g.epi = epi_rowmajor(kEpiStoreF32, qkv_, W);
       CK(gemm(g));
-      const LoraGroup Gq = lora_group(kGroupQKV);
-      if (Gq.n) CK(lora_group_prep(l, Gq, h1_[l], d));
       for (int i = 0; i < Gq.n; ++i) CK(lora_forward(l, Gq.t[i], qkv_, W, Gq.c0[i], Gq.w[i]));
       KL(launch_rope_qkv_fwd(qkv_, bias, pos_, cs_, cs_rows_, Qh_[l], Kh_[l], Vh_[l], B, T, H, KV, dh, stream_));
     }
@@ -983,7 +1012,8 @@ int LlamaEngine::enqueue_forward() {
       gw.epi.lora[gw.epi.n_lora++] = lora_addend(l, kLoraO, 0, d);
     }
     CK(gemm(gw));
-    KL(launch_rmsnorm_fwd(x1_[l], P32(P(pre + "ffn_norm.weight")), h2_[l], N, d, c.rms_eps, stream_));
+    const LoraGroup Gg = lora_group(kGroupGU);
+    CK(rmsnorm_lora(l, x1_[l], P32(P(pre + "ffn_norm.weight")), h2_[l], Gg));   // + the gate|up adapters' u
     GemmDesc gg;
     gg.M = N; gg.N = 2 * ff; gg.K = d;
     gg.a = op(h2_[l], N, d, d, 0);
@@ -997,17 +1027,11 @@ int LlamaEngine::enqueue_forward() {
       // SwiGLU as its own kernel.)
       gg.epi = epi_rowmajor(kEpiSwiGLU, gu_[l], 2 * ff);
       gg.epi.out_hi = a_[l].hi; gg.epi.out_lo = a_[l].lo; gg.epi.pair_off = ff;
-      const LoraGroup Gg = lora_group(kGroupGU);
-      if (Gg.n) {
-        CK(lora_group_prep(l, Gg, h2_[l], d));
-        for (int i = 0; i < Gg.n; ++i) gg.epi.lora[gg.epi.n_lora++] = lora_addend(l, Gg.t[i], Gg.c0[i], Gg.w[i]);
-      }
+      for (int i = 0; i < Gg.n; ++i) gg.epi.lora[gg.epi.n_lora++] = lora_addend(l, Gg.t[i], Gg.c0[i], Gg.w[i]);
       CK(gemm(gg));
     } else {
       gg.epi = epi_rowmajor(kEpiStoreF32, gu_[l], 2 * ff);
       CK(gemm(gg));
-      const LoraGroup Gg = lora_group(kGroupGU);
-      if (Gg.n) CK(lora_group_prep(l, Gg, h2_[l], d));
       for (int i = 0; i < Gg.n; ++i) CK(lora_forward(l, Gg.t[i], gu_[l], 2 * ff, Gg.c0[i], Gg.w[i]));
       KL(launch_swiglu_fwd(gu_[l], a_[l], N, ff, stream_));
     }

@@ -142,6 +142,8 @@ class LlamaEngine {
   LoraGroup lora_group(int g) const;
   // forward: u = X A^T and B^T of every adapter of the group, one launch
   int lora_group_prep(int l, const LoraGroup& G, Planes X, int d_in);
+  LoraSegs lora_group_segs(int l, const LoraGroup& G, int d_in);
+  int rmsnorm_lora(int l, const float* x, const float* gamma, Planes h, const LoraGroup& G);
   // backward, before the group's dX GEMM: du = s dY B of every adapter (one
   // launch) and the splices dX += du A as addends of that GEMM's epilogue
   int lora_group_du(int l, const LoraGroup& G, Planes dY, long long ld_dy, int d_in, Epilogue& dx_epi);

@@ -2,6 +2,7 @@
 // registers, warp-shuffle reductions, fixed-order (deterministic) reductions,
 // grids sized in multiples of the SM count.
 #include "kernels.cuh"
+#include "lora.cuh"
 #include "pdl.cuh"
 
 #include <cuda_fp16.h>
@@ -808,6 +809,108 @@ int dispatch_nc(int nc, A... a) {
   }
 }
 
+// rmsnorm_fwd fused with the low-rank down-projections of the adapters that
+// read its output row: u_a[n][j] = sum_k h[n][k] A_a[j][k] for each adapter a
+// (A_a [r][d] staged in shared memory), plus the B^T copies the splice reads.
+template <int NC, int RT, int NS>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_lora_kernel(const float* __restrict__ x,
+                                                               const float* __restrict__ gamma, Planes h, int N,
+                                                               int d, float eps, int r, LoraSegs g) {
+  griddep_wait();
+  extern __shared__ float4 asm4[];
+  float* as = reinterpret_cast<float*>(asm4);   // NS x [r][d]
+#pragma unroll
+  for (int a = 0; a < NS; ++a) {
+    const LoraSeg& sg = g.s[a];
+    for (int i = threadIdx.x * 4; i < r * d; i += 256 * 4)
+      *reinterpret_cast<float4*>(as + a * r * d + i) = __ldg(reinterpret_cast<const float4*>(sg.w + i));
+    if (sg.bt) {
+      for (long long i = blockIdx.x * 256LL + threadIdx.x; i < (long long)sg.b_rows * r;
+           i += (long long)gridDim.x * 256) {
+        const int c = (int)(i / r), j = (int)(i % r);
+        sg.bt[(long long)j * sg.b_rows + c] = sg.b_src[i];
+      }
+    }
+  }
+  __syncthreads();
+  const int warps = blockDim.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int d4 = d / 4;
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  for (int n = blockIdx.x * warps + threadIdx.x / 32; n < N; n += gridDim.x * warps) {
+    const float4* xr = reinterpret_cast<const float4*>(x + (long long)n * d);
+    float4 v[NC];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int c = lane + 32 * i;
+      v[i] = c < d4 ? __ldcs(xr + c) : f4_zero();
+      ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+    }
+    ss = warp_sum(ss);
+    const float rr = 1.0f / sqrtf(ss / (float)d + eps);
+    float acc[NS][RT];
+#pragma unroll
+    for (int a = 0; a < NS; ++a)
+#pragma unroll
+      for (int j = 0; j < RT; ++j) acc[a][j] = 0.f;
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int c = lane + 32 * i;
+      if (c < d4) {
+        const float4 gg = g4[c];
+        const float4 y = make_float4(v[i].x * rr * gg.x, v[i].y * rr * gg.y, v[i].z * rr * gg.z, v[i].w * rr * gg.w);
+        store_planes4(h, (long long)n * d + c * 4, y);
+#pragma unroll
+        for (int a = 0; a < NS; ++a)
+#pragma unroll
+          for (int j = 0; j < RT; ++j) {
+            if (j < r) {
+              const float4 w = *reinterpret_cast<const float4*>(as + (a * r + j) * d + c * 4);
+              acc[a][j] += y.x * w.x + y.y * w.y + y.z * w.z + y.w * w.w;
+            }
+          }
+      }
+    }
+#pragma unroll
+    for (int a = 0; a < NS; ++a)
+#pragma unroll
+      for (int j = 0; j < RT; ++j) {
+        const float t = warp_sum(acc[a][j]);
+        if (j < r && lane == (j & 31)) g.s[a].out[(long long)n * r + j] = g.s[a].alpha * t;
+      }
+  }
+}
+
+template <int NC>
+struct RmsFwdLora {
+  template <int RT, int NS>
+  static int go(const float* x, const float* gamma, Planes h, int N, int d, float eps, int r, const LoraSegs& g,
+                cudaStream_t st) {
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(rmsnorm_fwd_lora_kernel<NC, RT, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           200 * 1024);
+      attr = true;
+    }
+    const size_t smem = (size_t)NS * r * d * sizeof(float);
+    launch_pdl(rmsnorm_fwd_lora_kernel<NC, RT, NS>, dim3(grid_for((long long)N * 32, 256)), dim3(256), smem, st, x,
+               gamma, h, N, d, eps, r, g);
+    return ok();
+  }
+  static int run(const float* x, const float* gamma, Planes h, int N, int d, float eps, int r, LoraSegs g,
+                 cudaStream_t st) {
+    if (r <= 8) {
+      if (g.n == 1) return go<8, 1>(x, gamma, h, N, d, eps, r, g, st);
+      if (g.n == 2) return go<8, 2>(x, gamma, h, N, d, eps, r, g, st);
+      return go<8, 3>(x, gamma, h, N, d, eps, r, g, st);
+    }
+    if (g.n == 1) return go<16, 1>(x, gamma, h, N, d, eps, r, g, st);
+    if (g.n == 2) return go<16, 2>(x, gamma, h, N, d, eps, r, g, st);
+    return go<16, 3>(x, gamma, h, N, d, eps, r, g, st);
+  }
+};
+
 template <int NC>
 struct RmsFwd {
   static int run(const float* x, const float* gamma, Planes h, int N, int d, float eps, cudaStream_t st) {
@@ -875,6 +978,25 @@ int launch_embed_scatter(const float* dx, const int* order, const int* seg_start
 int launch_rmsnorm_fwd(const float* x, const float* gamma, Planes h, int N, int d, float eps, cudaStream_t st) {
   if (d % 4) return -1;
   return dispatch_nc<RmsFwd>(row_chunks(d), x, gamma, h, N, d, eps, st);
+}
+
+int launch_rmsnorm_fwd_lora(const float* x, const float* gamma, Planes h, int N, int d, float eps, int r,
+                            const LoraSegs& g, cudaStream_t st) {
+  if (d % 4 || r < 1 || r > 16 || g.n < 1 || g.n > kLoraMaxSegs) return -1;
+  if ((size_t)g.n * r * d * 4 > 200 * 1024) return -2;   // the adapters' A do not fit in shared memory
+  for (int a = 0; a < g.n; ++a)
+    if (!g.s[a].w || !g.s[a].out || g.s[a].col_off != 0 || g.s[a].width != d ||
+        (g.s[a].bt && (!g.s[a].b_src || g.s[a].b_rows <= 0)))
+      return -1;
+  switch (row_chunks(d)) {   // the chunk counts whose register arrays stay small next to the adapter sums
+    case 1: return RmsFwdLora<1>::run(x, gamma, h, N, d, eps, r, g, st);
+    case 2: return RmsFwdLora<2>::run(x, gamma, h, N, d, eps, r, g, st);
+    case 4: return RmsFwdLora<4>::run(x, gamma, h, N, d, eps, r, g, st);
+    case 5: return RmsFwdLora<5>::run(x, gamma, h, N, d, eps, r, g, st);
+    case 8: return RmsFwdLora<8>::run(x, gamma, h, N, d, eps, r, g, st);
+    case 16: return RmsFwdLora<16>::run(x, gamma, h, N, d, eps, r, g, st);
+    default: return -2;   // caller falls back to rmsnorm_fwd + the group down-projection
+  }
 }
 
 int launch_rmsnorm_bwd(const float* x, const float* dh, const float* gamma, const float* dres, float* dx,

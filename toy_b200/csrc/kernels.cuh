@@ -33,6 +33,13 @@ int launch_rmsnorm_fwd(const float* x, const float* gamma, Planes h, int N, int 
 
 // dx = dres + rms_norm_back(x, dh * gamma) (f32, may alias dres) and its planes;
 // per-block partial sums of dh * x * rrms into gpart[nblk][d] (for dgamma).
+struct LoraSegs;
+// launch_rmsnorm_fwd plus, in the same pass over each row, u_a = h A_a^T for
+// the adapters in g (all reading the whole row: col_off 0, width d; A_a [r][d];
+// rank <= 16) and their B^T copies. Returns -2 for a width it has no variant
+// for (the caller then runs the two passes).
+int launch_rmsnorm_fwd_lora(const float* x, const float* gamma, Planes h, int N, int d, float eps, int r,
+                            const LoraSegs& g, cudaStream_t st);
 int launch_rmsnorm_bwd(const float* x, const float* dh, const float* gamma, const float* dres, float* dx,
                        Planes dxp, float* gpart, int nblk, int N, int d, float eps, cudaStream_t st);
 // gout[c] = (accumulate ? gout[c] : 0) + sum_b gpart[b][c]
