@@ -111,6 +111,18 @@ int tb2_gemm_noalloc(int M, int N, int K, int batch, int split, const tb2_operan
  * Returns 0, or -1 for an unknown mode. */
 int tb2_gemm_set_pair_mode(int mode);
 
+/* How a QLoRA step feeds its frozen Q8_0 projections to the tensor cores,
+ * fixed for each session when its engine is realised: 1 (the default)
+ * dequantises each transformer block's projections once per use (once in the
+ * forward, once in the backward) into a two-slot ring of bf16 hi / lo planes
+ * that the plain GEMMs read; 0 hands the quants and fp16 scales to the GEMM,
+ * which dequantises B in shared memory for every 128-row M tile. The values
+ * the tensor cores see are bit-identical either way; the resident copy of the
+ * base is the Q8_0 data in both. No counterpart in the reference (its
+ * ggml_mul_mat dequantises inside the matmul).
+ * Returns the previous mode, or -1 for an unknown mode. */
+int tb2_set_q8_base_mode(int mode);
+
 /* hi = rn_bf16(x), lo = rn_bf16(x - hi) for n f32 values. */
 int tb2_split_f32(const float *x, void *hi, void *lo, size_t n, void *stream);
 

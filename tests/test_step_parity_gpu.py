@@ -109,6 +109,34 @@ def test_qlora_step(cuda, targets):
         compare_step(eng, mdl, loss_g, loss_r, grads)
 
 
+@pytest.mark.parametrize("q8_mode", [1, 0])
+def test_qlora_q8_base_modes(cuda, q8_mode):
+    """Both ways of feeding the Q8_0 base to the GEMMs, over three blocks (the
+    backward re-dequantises block 0 after block 2 took its ring slot)."""
+    from toy_b200 import LlamaConfig, LoRA, LoraOptions, RecipeOptions
+    from toy_b200._lib import lib
+    oc = O.LlamaCfg(vocab=512, d_model=128, n_heads=4, n_kv=2, d_head=32, d_ff=256, n_layers=3, rope_base=1e4)
+    gc = LlamaConfig(512, 128, 4, 2, 32, 256, 3, 1e4, 1e-5)
+    T, B = 64, 2
+    targets = ("q", "k", "v", "o", "gate", "up", "down")
+    prev = lib().tb2_set_q8_base_mode(q8_mode)
+    try:
+        rec = LoRA()
+        lo = LoraOptions(rank=8, alpha=16.0, targets=targets, a_std=0.125, b_std=0.01, base_std=0.02)
+        rec.realize(gc, 8, RecipeOptions(t_seq=T, t_batch=B, seed=13), lo)
+    finally:
+        lib().tb2_set_q8_base_mode(prev)
+    mdl = O.qlora_model(oc, O.LoraCfg(rank=8, alpha=16.0, targets=targets, a_std=0.125, b_std=0.01), seed=13,
+                        base_std=0.02)
+    eng = rec.lora_cache
+    ids, pos, lab = inputs(oc, T, B, seed=6)
+    for step in (1, 2, 3):
+        hp = O.hp_lora(1e-4, step, wd=0.01)
+        loss_g = rec.step(ids, pos, lab, hp, step == 1)
+        loss_r, grads = O.train_step(mdl, ids, pos, lab, T, B, hp, step == 1)
+        compare_step(eng, mdl, loss_g, loss_r, grads)
+
+
 def test_dense_labels_match_index_labels(cuda):
     from toy_b200 import FromScratch, RecipeOptions
     oc, gc = tiny_cfgs()

@@ -1,5 +1,6 @@
 // C ABI for the device-pointer primitives (tb2_gemm, tb2_split_f32, ...).
 #include "toy_b200.h"
+#include "engine.cuh"
 #include "gemm.cuh"
 #include "kernels.cuh"
 #include "runtime.cuh"
@@ -58,6 +59,8 @@ int tb2_gemm(int M, int N, int K, int batch, int split, const tb2_operand* a, co
 }
 
 int tb2_gemm_set_pair_mode(int mode) { return tb2::gemm_set_pair_mode(mode); }
+
+int tb2_set_q8_base_mode(int mode) { return tb2::engine_set_q8_base_mode(mode); }
 
 int tb2_split_f32(const float* x, void* hi, void* lo, size_t n, void* stream) {
   if (!x || !hi || !lo) return -1;

@@ -24,6 +24,15 @@ namespace tb2 {
     if ((x) != cudaSuccess) return -3;        \
   } while (0)
 
+int g_q8_base_mode = 1;
+
+int engine_set_q8_base_mode(int mode) {
+  if (mode < 0 || mode > 1) return -1;
+  const int prev = g_q8_base_mode;
+  g_q8_base_mode = mode;
+  return prev;
+}
+
 namespace {
 
 Operand op(Planes p, int rows, int cols, long long ld, int mn) {
@@ -110,7 +119,7 @@ LlamaEngine::LlamaEngine(const LlamaConfig& cfg, int device) : cfg_(cfg), device
 LlamaEngine::~LlamaEngine() {
   cudaSetDevice(device_);
   if (graph_) cudaGraphExecDestroy(graph_);
-  for (DeviceBuf* b : {&p32_, &phi_, &plo_, &g_, &m_, &v_, &q8_, &q8v_, &q8s_})
+  for (DeviceBuf* b : {&p32_, &phi_, &plo_, &g_, &m_, &v_, &q8_, &q8v_, &q8s_, &q8pl_, &ring_desc_})
     if (b->p) cudaFree(b->p);
   for (auto& b : bufs_)
     if (b.p) cudaFree(b.p);
@@ -275,6 +284,36 @@ int LlamaEngine::realize() {
   }
   n_total_ = off;
   q8_bytes_ = qoff;
+  // Q8_0 base as ring planes: the four group operands of a block, each with
+  // 64 extra reduction columns / rows when its adapters are folded in
+  q8_planes_ = q8_bytes_ && g_q8_base_mode == 1;
+  for (auto& p : params_) {
+    if (!p.q8) continue;
+    p.layer = std::atoi(p.name.c_str() + 4);
+    if (p.name.compare(0, 4, "blk.") != 0 || p.layer < 0 || p.layer >= c.n_layers) return -1;
+    static const char* kFirst[4] = {"attn_q.weight", "attn_output.weight", "ffn_gate.weight", "ffn_down.weight"};
+    const size_t dot = p.name.find('.', 4);
+    for (int g = 0; g < 4; ++g)
+      if (dot != std::string::npos && p.name.compare(dot + 1, std::string::npos, kFirst[g]) == 0) p.ring_group = g;
+  }
+  if (q8_planes_) {
+    const int dims[4][2] = {{(H + 2 * KV) * dh, d}, {d, H * dh}, {2 * ff, d}, {d, ff}};
+    long long slot = 0;
+    for (int g = 0; g < 4; ++g) {
+      RingGroup& rg = ring_[g];
+      rg.d_out = dims[g][0];
+      rg.d_in = dims[g][1];
+      if (rg.d_in % 16) return -1;
+      const LoraGroup G = lora_group(g);
+      const bool fold = (g == kGroupQKV || g == kGroupGU) && G.n && lora_grouped(rg.d_in);
+      rg.ext = fold ? 64 : 0;
+      ext_[g] = rg.ext;
+      rg.off = slot;
+      slot += ((long long)(rg.d_out + rg.ext) * (rg.d_in + rg.ext) + 127) / 128 * 128;
+      ring_chunks_ += (long long)(rg.d_out + rg.ext) * (rg.d_in + rg.ext) / 16;
+    }
+    q8_slot_elems_ = slot;
+  }
   layer_grad_lo_.assign(c.n_layers, n_train_);
   for (const auto& p : params_) {
     if (!p.trainable || p.name.compare(0, 4, "blk.") != 0) continue;
@@ -302,6 +341,10 @@ int LlamaEngine::realize() {
     CK(alloc(q8_, q8_bytes_));
     CK(alloc(q8v_, qvoff));
     CK(alloc(q8s_, qsoff * 2));
+    if (q8_planes_) {
+      CK(alloc(q8pl_, q8_slot_elems_ * 2 * 2 * 2));   // 2 slots x (hi, lo) x bf16
+      CK(build_ring(qvoff));
+    }
   }
 
   const int N = this->N(), T = c.T, B = c.B, W = (H + 2 * KV) * dh;
@@ -325,8 +368,8 @@ int LlamaEngine::realize() {
   for (int l = 0; l < c.n_layers; ++l) {
     x1_.push_back(f32((long long)N * d));
     gu_.push_back(f32((long long)N * 2 * ff));
-    h1_.push_back(pl((long long)N * d));
-    h2_.push_back(pl((long long)N * d));
+    h1_.push_back(pl((long long)N * (d + ext_[kGroupQKV])));   // + the q|k|v adapters' u columns
+    h2_.push_back(pl((long long)N * (d + ext_[kGroupGU])));    // + the gate|up adapters' u columns
     a_.push_back(pl((long long)N * ff));
     Qh_.push_back(pl((long long)N * H * dh));
     Kh_.push_back(pl((long long)N * KV * dh));
@@ -365,10 +408,10 @@ int LlamaEngine::realize() {
   lse_part_ = reinterpret_cast<float2*>(f32(2LL * ((V + 63) / 64) * N));
   lse_ms_ = reinterpret_cast<float2*>(f32(2LL * N));
   dxp_ = pl((long long)N * d);
-  dgu_ = pl((long long)N * 2 * ff);
+  dgu_ = pl((long long)N * (2 * ff + ext_[kGroupGU]));
   dO_ = pl((long long)N * H * dh);
   if (!flash_) dS_ = pl(att);
-  dqkv_ = pl((long long)N * W);
+  dqkv_ = pl((long long)N * (W + ext_[kGroupQKV]));
   if (!full) {
     du32_ = f32((long long)kLoraMaxSegs * N * r);   // du of each adapter of a group
     long long part = std::max(lora_wgrad_partial_floats(N, std::max(std::max(d, ff), H * dh), r),
@@ -474,6 +517,19 @@ int LlamaEngine::split_q8(const Param& p) {
 
 Operand LlamaEngine::wop(const Param& p, int rows, int cols, long long ld, int mn) {
   if (!p.q8) return op(PP(p), rows, cols, ld, mn);
+  if (q8_planes_) {
+    // the ring slot dequant_layer filled for this block (a null operand, which
+    // the GEMM rejects, if the step program did not fill it first); the
+    // group's extra reduction width extends K: columns of the rows (forward)
+    // or rows of the MN-major read (dX)
+    const int slot = p.layer & 1;
+    if (p.ring_group < 0 || ring_layer_[slot] != p.layer) return op(Planes{}, rows, cols, ld, mn);
+    const RingGroup& rg = ring_[p.ring_group];
+    bf16* base = static_cast<bf16*>(q8pl_.p) + (long long)slot * 2 * q8_slot_elems_ + rg.off;
+    const Planes pl{base, base + q8_slot_elems_};
+    const int e = rg.ext;
+    return mn ? op(pl, rows + e, cols, rg.d_in + e, 1) : op(pl, rows, cols + e, rg.d_in + e, 0);
+  }
   Operand o = op(Planes{}, rows, cols, ld, mn);
   o.q8 = static_cast<const int8_t*>(q8v_.p) + p.q8v_offset;
   o.q8_scale = static_cast<const uint16_t*>(q8s_.p) + p.q8s_offset;
@@ -737,7 +793,7 @@ int kind_of(const char* call) {
       {"launch_softmax", LlamaEngine::kKSoftmax},    {"launch_swiglu", LlamaEngine::kKSwiglu},
       {"launch_cross_entropy", LlamaEngine::kKCe},   {"launch_loss_reduce", LlamaEngine::kKLoss},
       {"launch_adamw", LlamaEngine::kKAdamw},        {"launch_embed", LlamaEngine::kKEmbed},
-      {"launch_split", LlamaEngine::kKSplit},        {"launch_flash_fwd", LlamaEngine::kKFlashFwd},
+      {"launch_split", LlamaEngine::kKSplit},        {"launch_q8_0_ring", LlamaEngine::kKSplit},        {"launch_flash_fwd", LlamaEngine::kKFlashFwd},
       {"launch_flash_bwd_prep", LlamaEngine::kKFlashPrep}, {"launch_flash_bwd", LlamaEngine::kKFlashBwd},
       {"launch_flash_rope", LlamaEngine::kKRope},   {"launch_lora", LlamaEngine::kKLora}};
   for (const auto& t : table)
@@ -779,6 +835,59 @@ LoraAddend LlamaEngine::lora_addend(int l, int t, int c0, int d_out) const {
   a.r = cfg_.lora_rank;
   a.scale = cfg_.lora_alpha / (float)cfg_.lora_rank;
   return a;
+}
+
+int LlamaEngine::dequant_layer(int l) {
+  if (!q8_planes_) return 0;
+  const int slot = l & 1;
+  if (ring_layer_[slot] == l) return 0;
+  KL(launch_q8_0_ring(static_cast<const RingLayer*>(ring_desc_.p) + l, ring_chunks_, stream_));
+  ring_layer_[slot] = l;
+  return 0;
+}
+
+// Fill descriptors of every block's ring operands (pointers into the Q8_0
+// arena, the adapters' f32 parameters and the ring slot), built once.
+int LlamaEngine::build_ring(long long qvoff) {
+  const LlamaConfig& c = cfg_;
+  const float s = c.lora_rank > 0 ? c.lora_alpha / (float)c.lora_rank : 0.f;
+  static const char* kFirst[4] = {"attn_q.weight", "attn_output.weight", "ffn_gate.weight", "ffn_down.weight"};
+  std::vector<RingLayer> host(c.n_layers);
+  for (int l = 0; l < c.n_layers; ++l) {
+    RingLayer& L = host[l];
+    bf16* base = static_cast<bf16*>(q8pl_.p) + (long long)(l & 1) * 2 * q8_slot_elems_;
+    long long chunk = 0;
+    for (int g = 0; g < 4; ++g) {
+      const RingGroup& rg = ring_[g];
+      const Param& W = P("blk." + std::to_string(l) + "." + kFirst[g]);
+      if (W.q8v_offset + (long long)rg.d_out * rg.d_in > qvoff || W.q8s_offset * 32 != W.q8v_offset) return -1;
+      RingMat& M = L.m[L.n++];
+      M.qv = static_cast<const int8_t*>(q8v_.p) + W.q8v_offset;
+      M.qs = static_cast<const uint16_t*>(q8s_.p) + W.q8s_offset;
+      M.hi = base + rg.off;
+      M.lo = base + q8_slot_elems_ + rg.off;
+      M.d_out = rg.d_out; M.d_in = rg.d_in; M.ext = rg.ext; M.r = c.lora_rank; M.s = s;
+      M.chunk0 = chunk;
+      chunk += (long long)(rg.d_out + rg.ext) * (rg.d_in + rg.ext) / 16;
+      if (rg.ext) {
+        const LoraGroup G = lora_group(g);
+        if (G.n > 3 || c.lora_rank > 16) return -1;
+        for (int i = 0; i < G.n; ++i) {
+          const std::string pre = "blk." + std::to_string(l) + "." + kProjName[G.t[i]];
+          RingAdapter& a = M.ad[M.n_ad++];
+          a.A = P32(P(pre + ".lora_a"));
+          a.B = P32(P(pre + ".lora_b"));
+          a.c0 = G.c0[i];
+          a.width = G.w[i];
+        }
+      }
+    }
+    L.chunks = chunk;
+    if (chunk != ring_chunks_) return -1;
+  }
+  CK(alloc(ring_desc_, host.size() * sizeof(RingLayer)));
+  CU(cudaMemcpy(ring_desc_.p, host.data(), host.size() * sizeof(RingLayer), cudaMemcpyHostToDevice));
+  return 0;
 }
 
 // Y[:, col_off : col_off + d_out] += s * u B^T as a separate kernel (for base
@@ -846,25 +955,27 @@ LlamaEngine::LoraGroup LlamaEngine::lora_group(int g) const {
 
 // RMSNorm of x into h, and -- for the group of adapters that read h -- their
 // down-projections u = h A^T and B^T copies in the same pass when possible.
-int LlamaEngine::rmsnorm_lora(int l, const float* x, const float* gamma, Planes h, const LoraGroup& G) {
+int LlamaEngine::rmsnorm_lora(int l, const float* x, const float* gamma, Planes h, const LoraGroup& G,
+                              long long ldh) {
   const LlamaConfig& c = cfg_;
   const int N = this->N(), d = c.d_model;
+  const int ext_base = ldh > d ? d : -1;   // the adapters' u also as h's extra columns
   if (G.n && c.lora_rank <= 16) {
-    LoraSegs segs = lora_group_segs(l, G, d);
+    LoraSegs segs = lora_group_segs(l, G, d, ext_base);
     if (profiling_) prof_begin(kKRmsFwd, 0.0);
-    const int rc = launch_rmsnorm_fwd_lora(x, gamma, h, N, d, c.rms_eps, c.lora_rank, segs, stream_);
+    const int rc = launch_rmsnorm_fwd_lora(x, gamma, h, N, d, c.rms_eps, c.lora_rank, segs, stream_, ldh);
     if (profiling_) prof_end();
     if (rc != -2) {   // -2: no variant for this width, run the two passes below
       ++counting_;
       return rc;
     }
   }
-  KL(launch_rmsnorm_fwd(x, gamma, h, N, d, c.rms_eps, stream_));
-  if (G.n) CK(lora_group_prep(l, G, h, d));
+  KL(launch_rmsnorm_fwd(x, gamma, h, N, d, c.rms_eps, stream_, ldh));
+  if (G.n) CK(lora_group_prep(l, G, h, d, ldh));
   return 0;
 }
 
-LoraSegs LlamaEngine::lora_group_segs(int l, const LoraGroup& G, int d_in) {
+LoraSegs LlamaEngine::lora_group_segs(int l, const LoraGroup& G, int d_in, int ext_base) {
   LoraSegs segs;
   for (int i = 0; i < G.n; ++i) {
     const std::string pre = "blk." + std::to_string(l) + "." + kProjName[G.t[i]];
@@ -874,31 +985,24 @@ LoraSegs LlamaEngine::lora_group_segs(int l, const LoraGroup& G, int d_in) {
     sg.alpha = 1.0f;
     sg.out = lora_u_[l][G.t[i]];
     sg.b_src = P32(P(pre + ".lora_b")); sg.b_rows = G.w[i]; sg.bt = lora_bt_[l][G.t[i]];
+    sg.ext_col = ext_base >= 0 ? ext_base + 16 * i : -1;
   }
   return segs;
 }
 
-int LlamaEngine::lora_group_prep(int l, const LoraGroup& G, Planes X, int d_in) {
+int LlamaEngine::lora_group_prep(int l, const LoraGroup& G, Planes X, int d_in, long long ldx) {
   const int N = this->N(), r = cfg_.lora_rank;
   if (r > 16) {
     for (int i = 0; i < G.n; ++i) CK(lora_prep(l, G.t[i], X, d_in, G.w[i]));
     return 0;
   }
-  LoraSegs segs;
-  for (int i = 0; i < G.n; ++i) {
-    const std::string pre = "blk." + std::to_string(l) + "." + kProjName[G.t[i]];
-    LoraSeg& sg = segs.s[segs.n++];
-    sg.col_off = 0; sg.width = d_in;
-    sg.w = P32(P(pre + ".lora_a"));
-    sg.alpha = 1.0f;
-    sg.out = lora_u_[l][G.t[i]];
-    sg.b_src = P32(P(pre + ".lora_b")); sg.b_rows = G.w[i]; sg.bt = lora_bt_[l][G.t[i]];
-  }
-  KL(launch_lora_down_group(X, d_in, N, r, segs, stream_));
+  const LoraSegs segs = lora_group_segs(l, G, d_in, ldx > d_in ? d_in : -1);
+  KL(launch_lora_down_group(X, ldx, N, r, segs, stream_));
   return 0;
 }
 
-int LlamaEngine::lora_group_du(int l, const LoraGroup& G, Planes dY, long long ld_dy, int d_in, Epilogue& dx_epi) {
+int LlamaEngine::lora_group_du(int l, const LoraGroup& G, Planes dY, long long ld_dy, int d_in, Epilogue& dx_epi,
+                                int ext_base) {
   const int N = this->N(), r = cfg_.lora_rank;
   const float s = cfg_.lora_alpha / (float)r;
   LoraSegs segs;
@@ -908,8 +1012,10 @@ int LlamaEngine::lora_group_du(int l, const LoraGroup& G, Planes dY, long long l
     sg.w = lora_bt_[l][G.t[i]];
     sg.alpha = s;
     sg.out = du32_ + (long long)i * N * r;
+    sg.ext_col = ext_base >= 0 ? ext_base + 16 * i : -1;
   }
   KL(launch_lora_down_group(dY, ld_dy, N, r, segs, stream_));
+  if (ext_base >= 0) return 0;   // the dX GEMM reads du from dY's extra columns
   for (int i = 0; i < G.n; ++i) {
     const std::string pre = "blk." + std::to_string(l) + "." + kProjName[G.t[i]];
     LoraAddend& a = dx_epi.lora[dx_epi.n_lora++];
@@ -923,7 +1029,8 @@ int LlamaEngine::lora_group_du(int l, const LoraGroup& G, Planes dY, long long l
   return 0;
 }
 
-int LlamaEngine::lora_group_wgrad(int l, const LoraGroup& G, Planes X, int d_in, Planes dY, long long ld_dy) {
+int LlamaEngine::lora_group_wgrad(int l, const LoraGroup& G, Planes X, long long ldx, int d_in, Planes dY,
+                                   long long ld_dy) {
   const int N = this->N(), r = cfg_.lora_rank;
   const float s = cfg_.lora_alpha / (float)r;
   LoraWgGroup g;
@@ -936,7 +1043,7 @@ int LlamaEngine::lora_group_wgrad(int l, const LoraGroup& G, Planes X, int d_in,
     sg.dB = G32(P(pre + ".lora_b"));
     sg.dA = G32(P(pre + ".lora_a"));
   }
-  KL(launch_lora_wgrad_group(dY, ld_dy, X, d_in, d_in, N, r, s, g, lora_part_, stream_));
+  KL(launch_lora_wgrad_group(dY, ld_dy, X, ldx, d_in, N, r, s, g, lora_part_, stream_));
   return 0;
 }
 
@@ -948,13 +1055,16 @@ int LlamaEngine::enqueue_forward() {
   const bool lora = c.mode == 1;
   const Param& E = P("token_embd.weight");
   KL(launch_embed_gather(P32(E), ids_, x_[0], N, d, stream_));
+  ring_layer_[0] = ring_layer_[1] = -1;
   for (int l = 0; l < c.n_layers; ++l) {
     const std::string pre = "blk." + std::to_string(l) + ".";
+    CK(dequant_layer(l));
     const LoraGroup Gq = lora_group(kGroupQKV);
-    CK(rmsnorm_lora(l, x_[l], P32(P(pre + "attn_norm.weight")), h1_[l], Gq));   // + the q|k|v adapters' u
+    const int eq = ext_[kGroupQKV];   // q|k|v adapters folded into the GEMM as extra reduction columns
+    CK(rmsnorm_lora(l, x_[l], P32(P(pre + "attn_norm.weight")), h1_[l], Gq, d + eq));   // + the adapters' u
     GemmDesc g;
-    g.M = N; g.N = W; g.K = d;
-    g.a = op(h1_[l], N, d, d, 0);
+    g.M = N; g.N = W; g.K = d + eq;
+    g.a = op(h1_[l], N, d + eq, d + eq, 0);
     g.b = wop(P(pre + "attn_q.weight"), W, d, d, 0);
     const float* bias = c.qkv_bias ? P32(P(pre + "attn_q.bias")) : nullptr;
     const int qkv_t[3] = {kLoraQ, kLoraK, kLoraV};
@@ -967,12 +1077,12 @@ int LlamaEngine::enqueue_forward() {
       ro.q_hi = Qh_[l].hi; ro.q_lo = Qh_[l].lo; ro.k_hi = Kh_[l].hi; ro.k_lo = Kh_[l].lo;
       ro.v_hi = Vh_[l].hi; ro.v_lo = Vh_[l].lo;
       ro.T = T; ro.H = H; ro.KV = KV; ro.dh = dh;
-      for (int i = 0; i < Gq.n; ++i) g.epi.lora[g.epi.n_lora++] = lora_addend(l, Gq.t[i], Gq.c0[i], Gq.w[i]);
+      for (int i = 0; i < Gq.n && !eq; ++i) g.epi.lora[g.epi.n_lora++] = lora_addend(l, Gq.t[i], Gq.c0[i], Gq.w[i]);
       CK(gemm(g));
     } else {
       g.epi = epi_rowmajor(kEpiStoreF32, qkv_, W);
       CK(gemm(g));
-      for (int i = 0; i < Gq.n; ++i) CK(lora_forward(l, Gq.t[i], qkv_, W, Gq.c0[i], Gq.w[i]));
+      for (int i = 0; i < Gq.n && !eq; ++i) CK(lora_forward(l, Gq.t[i], qkv_, W, Gq.c0[i], Gq.w[i]));
       KL(launch_rope_qkv_fwd(qkv_, bias, pos_, cs_, cs_rows_, Qh_[l], Kh_[l], Vh_[l], B, T, H, KV, dh, stream_));
     }
     if (flash_) {
@@ -1008,18 +1118,19 @@ int LlamaEngine::enqueue_forward() {
     gw.epi.res = x_[l];
     const LoraGroup Go = lora_group(kGroupO);
     if (Go.n) {
-      CK(lora_group_prep(l, Go, O_[l], H * dh));
+      CK(lora_group_prep(l, Go, O_[l], H * dh, H * dh));
       gw.epi.lora[gw.epi.n_lora++] = lora_addend(l, kLoraO, 0, d);
     }
     CK(gemm(gw));
     const LoraGroup Gg = lora_group(kGroupGU);
-    CK(rmsnorm_lora(l, x1_[l], P32(P(pre + "ffn_norm.weight")), h2_[l], Gg));   // + the gate|up adapters' u
+    const int eg = ext_[kGroupGU];
+    CK(rmsnorm_lora(l, x1_[l], P32(P(pre + "ffn_norm.weight")), h2_[l], Gg, d + eg));   // + the adapters' u
     GemmDesc gg;
-    gg.M = N; gg.N = 2 * ff; gg.K = d;
-    gg.a = op(h2_[l], N, d, d, 0);
+    gg.M = N; gg.N = 2 * ff; gg.K = d + eg;
+    gg.a = op(h2_[l], N, d + eg, d + eg, 0);
     const Param& Wgu = P(pre + "ffn_gate.weight");
     gg.b = wop(Wgu, 2 * ff, d, d, 0);
-    if (Wgu.q8) {
+    if (Wgu.q8 && !q8_planes_) {
       // Q8_0 base: one launch -- gate|up projection (gate and up rows paired per
       // tile), adapters, a = silu(gate) * up as planes; gate|up kept in f32 for
       // the backward. (The dequantising GEMM has operand-feed headroom for the
@@ -1032,7 +1143,7 @@ int LlamaEngine::enqueue_forward() {
     } else {
       gg.epi = epi_rowmajor(kEpiStoreF32, gu_[l], 2 * ff);
       CK(gemm(gg));
-      for (int i = 0; i < Gg.n; ++i) CK(lora_forward(l, Gg.t[i], gu_[l], 2 * ff, Gg.c0[i], Gg.w[i]));
+      for (int i = 0; i < Gg.n && !eg; ++i) CK(lora_forward(l, Gg.t[i], gu_[l], 2 * ff, Gg.c0[i], Gg.w[i]));
       KL(launch_swiglu_fwd(gu_[l], a_[l], N, ff, stream_));
     }
     GemmDesc gd;
@@ -1043,7 +1154,7 @@ int LlamaEngine::enqueue_forward() {
     gd.epi.res = x1_[l];
     const LoraGroup Gd = lora_group(kGroupDown);
     if (Gd.n) {
-      CK(lora_group_prep(l, Gd, a_[l], ff));
+      CK(lora_group_prep(l, Gd, a_[l], ff, ff));
       gd.epi.lora[gd.epi.n_lora++] = lora_addend(l, kLoraDown, 0, d);
     }
     CK(gemm(gd));
@@ -1099,6 +1210,7 @@ int LlamaEngine::enqueue_backward() {
   if (full) KL(launch_colsum(gpart_, nblk, d, G32(gf), 0, stream_));
   for (int l = c.n_layers - 1; l >= 0; --l) {
     const std::string pre = "blk." + std::to_string(l) + ".";
+    CK(dequant_layer(l));   // the forward's last two blocks are still in the ring
     const Param& Wd = P(pre + "ffn_down.weight");
     const Param& Wg = P(pre + "ffn_gate.weight");
     const Param& Wo = P(pre + "attn_output.weight");
@@ -1111,9 +1223,9 @@ int LlamaEngine::enqueue_backward() {
     gda.epi = epi_rowmajor(kEpiStoreF32, da_, ff);
     const LoraGroup Gd = lora_group(kGroupDown);
     const bool gd_grp = Gd.n && lora_grouped(ff);
-    if (gd_grp) CK(lora_group_du(l, Gd, dxp_, d, ff, gda.epi));
+    if (gd_grp) CK(lora_group_du(l, Gd, dxp_, d, ff, gda.epi, -1));
     CK(gemm(gda));
-    if (gd_grp) CK(lora_group_wgrad(l, Gd, a_[l], ff, dxp_, d));
+    if (gd_grp) CK(lora_group_wgrad(l, Gd, a_[l], ff, ff, dxp_, d));
     if (full) {
       GemmDesc gw;
       gw.M = d; gw.N = ff; gw.K = N;
@@ -1123,17 +1235,18 @@ int LlamaEngine::enqueue_backward() {
       CK(gemm(gw));
     }
     if (Gd.n && !gd_grp) CK(lora_backward(l, kLoraDown, a_[l], ff, dxp_, d, 0, d, da_, nullptr));
-    KL(launch_swiglu_bwd(gu_[l], da_, dgu_, N, ff, stream_));
+    const int eg = ext_[kGroupGU];   // dgu carries du of the gate|up adapters in its extra columns
+    KL(launch_swiglu_bwd(gu_[l], da_, dgu_, N, ff, stream_, 2 * ff + eg));
     GemmDesc gh;
-    gh.M = N; gh.N = d; gh.K = 2 * ff;
-    gh.a = op(dgu_, N, 2 * ff, 2 * ff, 0);
+    gh.M = N; gh.N = d; gh.K = 2 * ff + eg;
+    gh.a = op(dgu_, N, 2 * ff + eg, 2 * ff + eg, 0);
     gh.b = wop(Wg, 2 * ff, d, d, 1);
     gh.epi = epi_rowmajor(kEpiStoreF32, dh_, d);
     const LoraGroup Gg = lora_group(kGroupGU);
     const bool gg_grp = Gg.n && lora_grouped(d);
-    if (gg_grp) CK(lora_group_du(l, Gg, dgu_, 2 * ff, d, gh.epi));
+    if (gg_grp) CK(lora_group_du(l, Gg, dgu_, 2 * ff + eg, d, gh.epi, eg ? 2 * ff : -1));
     CK(gemm(gh));
-    if (gg_grp) CK(lora_group_wgrad(l, Gg, h2_[l], d, dgu_, 2 * ff));
+    if (gg_grp) CK(lora_group_wgrad(l, Gg, h2_[l], d + eg, d, dgu_, 2 * ff + eg));
     if (full) {
       GemmDesc gw;
       gw.M = 2 * ff; gw.N = d; gw.K = N;
@@ -1158,9 +1271,9 @@ int LlamaEngine::enqueue_backward() {
     gdo.epi = hm;
     const LoraGroup Go = lora_group(kGroupO);
     const bool go_grp = Go.n && lora_grouped(H * dh);
-    if (go_grp) CK(lora_group_du(l, Go, dxp_, d, H * dh, gdo.epi));
+    if (go_grp) CK(lora_group_du(l, Go, dxp_, d, H * dh, gdo.epi, -1));
     CK(gemm(gdo));
-    if (go_grp) CK(lora_group_wgrad(l, Go, O_[l], H * dh, dxp_, d));
+    if (go_grp) CK(lora_group_wgrad(l, Go, O_[l], H * dh, H * dh, dxp_, d));
     if (full) {
       GemmDesc gw;
       gw.M = d; gw.N = H * dh; gw.K = N;
@@ -1176,7 +1289,7 @@ int LlamaEngine::enqueue_backward() {
       KL(launch_flash_bwd(Qh_[l], Kh_[l], Vh_[l], dO_, lse2_[l], dvec_, fws_, B, T, H, KV, dh, scale, err_,
                           stream_));
       KL(launch_flash_rope_bwd(fws_, pos_, cs_, cs_rows_, dqkv_, c.qkv_bias ? qkv_ : nullptr, B, T, H, KV, dh,
-                               stream_));
+                               stream_, W + ext_[kGroupQKV]));
     } else {
       KL(launch_split_f32(dO32_, dO_.hi, dO_.lo, (long long)N * H * dh, stream_));
       // ---- attention core
@@ -1208,20 +1321,21 @@ int LlamaEngine::enqueue_backward() {
       gv.epi.mode = kEpiStoreF32; gv.epi.out = dV_; gv.epi.m_s0 = dh; gv.epi.bstride = (long long)T * dh;
       CK(gemm(gv));
       KL(launch_rope_qkv_bwd(dQ_, dK_, dV_, pos_, cs_, cs_rows_, dqkv_, c.qkv_bias ? qkv_ : nullptr, B, T, H, KV, dh,
-                             stream_));
+                             stream_, W + ext_[kGroupQKV]));
     }
     if (c.qkv_bias && full) KL(launch_colsum_rows(qkv_, N, W, G32(P(pre + "attn_q.bias")), stream_));
     // ---- QKV projection
+    const int eq = ext_[kGroupQKV];   // dqkv carries du of the q|k|v adapters in its extra columns
     GemmDesc gx;
-    gx.M = N; gx.N = d; gx.K = W;
-    gx.a = op(dqkv_, N, W, W, 0);
+    gx.M = N; gx.N = d; gx.K = W + eq;
+    gx.a = op(dqkv_, N, W + eq, W + eq, 0);
     gx.b = wop(Wq, W, d, d, 1);
     gx.epi = epi_rowmajor(kEpiStoreF32, dh_, d);
     const LoraGroup Gq = lora_group(kGroupQKV);
     const bool gq_grp = Gq.n && lora_grouped(d);
-    if (gq_grp) CK(lora_group_du(l, Gq, dqkv_, W, d, gx.epi));
+    if (gq_grp) CK(lora_group_du(l, Gq, dqkv_, W + eq, d, gx.epi, eq ? W : -1));
     CK(gemm(gx));
-    if (gq_grp) CK(lora_group_wgrad(l, Gq, h1_[l], d, dqkv_, W));
+    if (gq_grp) CK(lora_group_wgrad(l, Gq, h1_[l], d + eq, d, dqkv_, W + eq));
     if (full) {
       GemmDesc gw;
       gw.M = W; gw.N = d; gw.K = N;
@@ -1367,11 +1481,11 @@ long long LlamaEngine::debug_activation(int which, int layer, float* dst, long l
   if (layer < 0 || layer > c.n_layers || (layer == c.n_layers && which != 0)) return -1;
   const float* f = nullptr;
   Planes p{};
-  long long n = 0;
+  long long n = 0, ld = 0;   // ld: row pitch of planes with extra columns (rows of d values)
   switch (which) {
     case 0: f = x_[layer]; n = N * d; break;
     case 1: f = x1_[layer]; n = N * d; break;
-    case 2: p = h1_[layer]; n = N * d; break;
+    case 2: p = h1_[layer]; n = N * d; ld = d + ext_[kGroupQKV]; break;
     case 3: p = Qh_[layer]; n = N * H * dh; break;
     case 4: p = Kh_[layer]; n = N * KV * dh; break;
     case 5: p = Vh_[layer]; n = N * KV * dh; break;
@@ -1382,7 +1496,7 @@ long long LlamaEngine::debug_activation(int which, int layer, float* dst, long l
     case 8: f = gu_[layer]; n = N * 2 * ff; break;
     case 9: p = a_[layer]; n = N * ff; break;
     case 10: f = logits_; n = N * c.vocab; break;
-    case 11: p = h2_[layer]; n = N * d; break;
+    case 11: p = h2_[layer]; n = N * d; ld = d + ext_[kGroupGU]; break;
     case 12: f = qkv_; n = N * W; break;
     default: return -1;
   }
@@ -1393,8 +1507,13 @@ long long LlamaEngine::debug_activation(int which, int layer, float* dst, long l
     return n;
   }
   std::vector<bf16> hi(n), lo(n);
-  CU(cudaMemcpy(hi.data(), p.hi, n * 2, cudaMemcpyDeviceToHost));
-  CU(cudaMemcpy(lo.data(), p.lo, n * 2, cudaMemcpyDeviceToHost));
+  if (ld > d) {
+    CU(cudaMemcpy2D(hi.data(), d * 2, p.hi, ld * 2, d * 2, N, cudaMemcpyDeviceToHost));
+    CU(cudaMemcpy2D(lo.data(), d * 2, p.lo, ld * 2, d * 2, N, cudaMemcpyDeviceToHost));
+  } else {
+    CU(cudaMemcpy(hi.data(), p.hi, n * 2, cudaMemcpyDeviceToHost));
+    CU(cudaMemcpy(lo.data(), p.lo, n * 2, cudaMemcpyDeviceToHost));
+  }
   for (long long i = 0; i < n; ++i) dst[i] = __bfloat162float(hi[i]) + __bfloat162float(lo[i]);
   return n;
 }

@@ -39,8 +39,20 @@ struct Param {
   long long q8_offset = 0;   // bytes into q8_ (the blocks as uploaded)
   long long q8v_offset = 0;  // bytes into q8v_ (int8 quants, row-major)
   long long q8s_offset = 0;  // elements into q8s_ (fp16 scale bits, one per 32 quants)
+  int layer = -1;            // block index of a Q8_0 projection
+  int ring_group = -1;       // first projection of a ring operand: its adapter group (kGroupQKV ..)
   long long numel() const { return (long long)rows * cols; }
 };
+
+// How the step feeds a frozen Q8_0 projection to its GEMMs (read when an engine
+// is realised): 1 (default) dequantises each block's projections once per use
+// into a two-slot ring of split planes that the plain GEMMs read, with the
+// adapters of a group (rank <= 16) appended as extra reduction columns / rows
+// (q|k|v and gate|up); 0 hands the quants and scales to the GEMM, which
+// dequantises every k-block of B in shared memory for every M tile, and adds
+// the adapters in GEMM epilogues. Same values either way. Returns the previous
+// mode, or -1 for a mode out of range.
+int engine_set_q8_base_mode(int mode);
 
 struct DeviceBuf {
   void* p = nullptr;
@@ -141,14 +153,18 @@ class LlamaEngine {
   };
   LoraGroup lora_group(int g) const;
   // forward: u = X A^T and B^T of every adapter of the group, one launch
-  int lora_group_prep(int l, const LoraGroup& G, Planes X, int d_in);
-  LoraSegs lora_group_segs(int l, const LoraGroup& G, int d_in);
-  int rmsnorm_lora(int l, const float* x, const float* gamma, Planes h, const LoraGroup& G);
+  int lora_group_prep(int l, const LoraGroup& G, Planes X, int d_in, long long ldx);
+  // ext_base >= 0: u of adapter i also goes to X's columns ext_base + 16 i + j
+  LoraSegs lora_group_segs(int l, const LoraGroup& G, int d_in, int ext_base);
+  int rmsnorm_lora(int l, const float* x, const float* gamma, Planes h, const LoraGroup& G, long long ldh);
   // backward, before the group's dX GEMM: du = s dY B of every adapter (one
   // launch) and the splices dX += du A as addends of that GEMM's epilogue
-  int lora_group_du(int l, const LoraGroup& G, Planes dY, long long ld_dy, int d_in, Epilogue& dx_epi);
+  // With ext_base >= 0 du goes to dY's columns ext_base + 16 i + j (the dX
+  // GEMM's extra reduction columns) instead of the epilogue.
+  int lora_group_du(int l, const LoraGroup& G, Planes dY, long long ld_dy, int d_in, Epilogue& dx_epi,
+                    int ext_base);
   // backward, after it: dB and dA of every adapter (partials + fixed-order sum)
-  int lora_group_wgrad(int l, const LoraGroup& G, Planes X, int d_in, Planes dY, long long ld_dy);
+  int lora_group_wgrad(int l, const LoraGroup& G, Planes X, long long ldx, int d_in, Planes dY, long long ld_dy);
   bool lora_grouped(int d_in) const { return cfg_.lora_rank <= 16 && d_in % 32 == 0; }
   float* P32(const Param& p) { return static_cast<float*>(p32_.p) + p.offset; }
   float* G32(const Param& p) { return static_cast<float*>(g_.p) + p.offset; }
@@ -161,6 +177,10 @@ class LlamaEngine {
   const Param& P(const std::string& n) const;
   int refresh_planes(const Param& p);
   int split_q8(const Param& p);   // blocks -> quants + scales
+  // Ring slot l % 2 := block l's ring operands (Q8_0 projections as planes,
+  // with the adapters of the groups that fold them in); no launch when the
+  // slot already holds them in this step program.
+  int dequant_layer(int l);
 
   LlamaConfig cfg_;
   int device_ = 0;
@@ -171,6 +191,26 @@ class LlamaEngine {
   long long n_train_ = 0, n_total_ = 0, q8_bytes_ = 0;
   // arenas
   DeviceBuf p32_, phi_, plo_, g_, m_, v_, q8_, q8v_, q8s_;
+  // Q8_0 base as planes: per block the first quant / scale index and the count
+  // of its projections' elements; two slots of slot_elems hi then lo values
+  bool q8_planes_ = false;
+  DeviceBuf q8pl_;
+  long long q8_slot_elems_ = 0;
+  int ring_layer_[2] = {-1, -1};
+  // ring operand of each adapter group: [d_out + ext][d_in + ext] planes at
+  // element offset off of a slot's hi (and lo) half; the blocks' fill
+  // descriptors live in ring_desc_
+  struct RingGroup {
+    int d_out = 0, d_in = 0, ext = 0;
+    long long off = 0;
+  };
+  RingGroup ring_[4];
+  DeviceBuf ring_desc_;
+  long long ring_chunks_ = 0;
+  // extra reduction width of each group's base GEMMs (0, or 64 with the
+  // group's adapters folded into the ring operand)
+  int ext_[4] = {0, 0, 0, 0};
+  int build_ring(long long qvoff);
   // activations and scratch
   std::vector<DeviceBuf> bufs_;
   std::vector<float*> x_, x1_, gu_;

@@ -756,7 +756,8 @@ int launch_flash_bwd(Planes Q, Planes K, Planes V, Planes dO, const float* lse2,
 }
 
 int launch_flash_rope_bwd(const float* ws, const int* pos, const float* cs_tab, int tab_rows, Planes dqkv,
-                          float* dqkv_f32, int B, int T, int H, int KV, int dh, cudaStream_t st) {
+                          float* dqkv_f32, int B, int T, int H, int KV, int dh, cudaStream_t st,
+                          long long ld_dqkv) {
   if (!shape_ok(B, T, H, KV, dh)) return -1;
   const long long nq = (T + kTile - 1) / kTile;
   const long long qs = (long long)B * H * T * kDh, kvs = (long long)B * KV * T * kDh;
@@ -764,7 +765,7 @@ int launch_flash_rope_bwd(const float* ws, const int* pos, const float* cs_tab, 
   const float* dk = ws + nq * qs;
   const float* dv = dk + G * kvs;
   return launch_rope_qkv_bwd_sum(ws, qs, kTile, dk, dv, kvs, G, pos, cs_tab, tab_rows, dqkv, dqkv_f32, B, T, H, KV, dh,
-                                 st);
+                                 st, ld_dqkv);
 }
 
 }  // namespace tb2

@@ -37,8 +37,10 @@ int launch_flash_bwd(Planes Q, Planes K, Planes V, Planes dO, const float* lse2,
 
 // RoPE backward over the flash backward's partials: dQ = sum over key tiles
 // j <= t / 128, dK and dV = sum over the group's query heads; writes the
-// token-major dqkv planes (and f32 copy when dqkv_f32 is set).
+// token-major dqkv planes, rows ld_dqkv apart (0: (H + 2 KV) dh), and the f32
+// copy when dqkv_f32 is set.
 int launch_flash_rope_bwd(const float* ws, const int* pos, const float* cs_tab, int tab_rows, Planes dqkv,
-                          float* dqkv_f32, int B, int T, int H, int KV, int dh, cudaStream_t st);
+                          float* dqkv_f32, int B, int T, int H, int KV, int dh, cudaStream_t st,
+                          long long ld_dqkv = 0);
 
 }  // namespace tb2

@@ -4,6 +4,7 @@
 #include "kernels.cuh"
 #include "lora.cuh"
 #include "pdl.cuh"
+#include "warp_reduce.cuh"
 
 #include <cuda_fp16.h>
 #include <cstdint>
@@ -130,7 +131,7 @@ __global__ void embed_scatter_kernel(const float* __restrict__ dx, const int* __
 // One warp per row; lane l holds float4 chunks c = l + 32*i (i < NC) in registers.
 template <int NC>
 __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
-                                                          Planes h, int N, int d, float eps) {
+                                                          Planes h, long long ldh, int N, int d, float eps) {
   griddep_wait();
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x % 32;
@@ -153,7 +154,7 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const float* __restric
       const int c = lane + 32 * i;
       if (c < d4) {
         const float4 g = g4[c];
-        store_planes4(h, (long long)n * d + c * 4,
+        store_planes4(h, (long long)n * ldh + c * 4,
                       make_float4(v[i].x * r * g.x, v[i].y * r * g.y, v[i].z * r * g.z, v[i].w * r * g.w));
       }
     }
@@ -300,7 +301,8 @@ __global__ void __launch_bounds__(256) rope_qkv_bwd_kernel(const float* __restri
                                                            const float* __restrict__ dV, long long kv_pstride,
                                                            int kv_parts, const int* __restrict__ pos,
                                                            const float2* __restrict__ cs, int tab_rows, Planes out,
-                                                           float* out_f32, int N, int T, int H, int KV, int dh) {
+                                                           long long ldo, float* out_f32, int N, int T, int H, int KV,
+                                                           int dh) {
   griddep_wait();
   const int half = dh / 2;
   const int slots = H + 2 * KV;
@@ -340,8 +342,9 @@ __global__ void __launch_bounds__(256) rope_qkv_bwd_kernel(const float* __restri
         }
       }
       const long long dst = (long long)n * width + slot * dh + j;
-      store_planes(out, dst, y0);
-      store_planes(out, dst + half, y1);
+      const long long dp = (long long)n * ldo + slot * dh + j;
+      store_planes(out, dp, y0);
+      store_planes(out, dp + half, y1);
       if (out_f32) {
         out_f32[dst] = y0;
         out_f32[dst + half] = y1;
@@ -467,7 +470,7 @@ __device__ __forceinline__ void swiglu_back1(float g, float u, float dy, float& 
 }
 
 __global__ void __launch_bounds__(128) swiglu_bwd_kernel(const float* __restrict__ gu, const float* __restrict__ da,
-                                                         Planes dgu, int N, int ff) {
+                                                         Planes dgu, long long ldo, int N, int ff) {
   griddep_wait();
   const int ff4 = ff / 4;
   for (int n = blockIdx.x; n < N; n += gridDim.x) {
@@ -481,8 +484,8 @@ __global__ void __launch_bounds__(128) swiglu_bwd_kernel(const float* __restrict
       swiglu_back1(g.y, u.y, dy.y, dg.y, du.y);
       swiglu_back1(g.z, u.z, dy.z, dg.z, du.z);
       swiglu_back1(g.w, u.w, dy.w, dg.w, du.w);
-      store_planes4(dgu, (long long)n * 2 * ff + 4 * c, dg);
-      store_planes4(dgu, (long long)n * 2 * ff + ff + 4 * c, du);
+      store_planes4(dgu, (long long)n * ldo + 4 * c, dg);
+      store_planes4(dgu, (long long)n * ldo + ff + 4 * c, du);
     }
   }
 }
@@ -719,6 +722,62 @@ __global__ void q8_0_to_planes_kernel(const uint8_t* __restrict__ q, Planes out,
   }
 }
 
+// One 16-value chunk of a ring matrix per thread iteration (layout in kernels.cuh).
+__global__ void __launch_bounds__(256) q8_0_ring_kernel(const RingLayer* __restrict__ L) {
+  griddep_wait();
+  const int nm = L->n;
+  const long long total = L->chunks;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += stride) {
+    int k = 0;
+    while (k + 1 < nm && i >= L->m[k + 1].chunk0) ++k;
+    const RingMat& M = L->m[k];
+    const int d_in = M.d_in, d_out = M.d_out, ld = d_in + M.ext;
+    const long long c = i - M.chunk0;
+    const int cpr = ld / 16;
+    const int row = (int)(c / cpr), col = (int)(c % cpr) * 16;
+    float v[16];
+    if (row < d_out && col < d_in) {
+      const long long e = (long long)row * d_in + col;
+      const int4 q = __ldg(reinterpret_cast<const int4*>(M.qv + e));
+      const float sc = __half2float(__ushort_as_half(__ldg(M.qs + e / 32)));
+      const int8_t* b = reinterpret_cast<const int8_t*>(&q);
+#pragma unroll
+      for (int t = 0; t < 16; ++t) v[t] = sc * (float)b[t];
+    } else if (row < d_out) {
+      const int a = (col - d_in) / 16;
+      const bool on = a < M.n_ad && row >= M.ad[a].c0 && row < M.ad[a].c0 + M.ad[a].width;
+      const float* br = on ? M.ad[a].B + (long long)(row - M.ad[a].c0) * M.r : nullptr;
+#pragma unroll
+      for (int t = 0; t < 16; ++t) v[t] = (on && t < M.r) ? M.s * br[t] : 0.f;
+    } else {
+      const int rr = row - d_out, a = rr / 16, j = rr % 16;
+      const bool on = col < d_in && a < M.n_ad && j < M.r;
+      if (on) {
+        const float4* src = reinterpret_cast<const float4*>(M.ad[a].A + (long long)j * d_in + col);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float4 t4 = __ldg(src + u);
+          v[4 * u] = t4.x; v[4 * u + 1] = t4.y; v[4 * u + 2] = t4.z; v[4 * u + 3] = t4.w;
+        }
+      } else {
+#pragma unroll
+        for (int t = 0; t < 16; ++t) v[t] = 0.f;
+      }
+    }
+    __align__(16) bf16 h[16], l[16];
+#pragma unroll
+    for (int t = 0; t < 16; ++t) split2(v[t], h[t], l[t]);
+    const long long o = (long long)row * ld + col;
+    uint4* ph = reinterpret_cast<uint4*>(M.hi + o);
+    uint4* pl = reinterpret_cast<uint4*>(M.lo + o);
+    ph[0] = reinterpret_cast<const uint4*>(h)[0];
+    ph[1] = reinterpret_cast<const uint4*>(h)[1];
+    pl[0] = reinterpret_cast<const uint4*>(l)[0];
+    pl[1] = reinterpret_cast<const uint4*>(l)[1];
+  }
+}
+
 // Round half away from zero (C roundf / numpy-gguf np_roundf semantics) spelled
 // out so a half-way product always rounds outward: t = trunc(v); v - t is exact
 // for |v| < 2^23, so the comparison with 0.5 decides ties exactly.
@@ -811,19 +870,33 @@ int dispatch_nc(int nc, A... a) {
 
 // rmsnorm_fwd fused with the low-rank down-projections of the adapters that
 // read its output row: u_a[n][j] = sum_k h[n][k] A_a[j][k] for each adapter a
-// (A_a [r][d] staged in shared memory), plus the B^T copies the splice reads.
-template <int NC, int RT, int NS>
+// (A_a [r][d] staged in shared memory once per block), plus the B^T copies the
+// splice reads. A warp normalises RW rows at a time, so each A value read from
+// shared memory serves RW rows; the r sums of an adapter are reduced across the
+// warp with warp_sum_multi. With ext_col >= 0, u_a is also written as planes
+// into h's columns ext_col + j.
+template <int NC, int RT, int NS, int RW>
 __global__ void __launch_bounds__(256) rmsnorm_fwd_lora_kernel(const float* __restrict__ x,
-                                                               const float* __restrict__ gamma, Planes h, int N,
-                                                               int d, float eps, int r, LoraSegs g) {
+                                                               const float* __restrict__ gamma, Planes h, long long ldh,
+                                                               int N, int d, float eps, int r, LoraSegs g) {
   griddep_wait();
   extern __shared__ float4 asm4[];
   float* as = reinterpret_cast<float*>(asm4);   // NS x [r][d]
+  const int n4 = r * d / 4;
 #pragma unroll
   for (int a = 0; a < NS; ++a) {
     const LoraSeg& sg = g.s[a];
-    for (int i = threadIdx.x * 4; i < r * d; i += 256 * 4)
-      *reinterpret_cast<float4*>(as + a * r * d + i) = __ldg(reinterpret_cast<const float4*>(sg.w + i));
+    const float4* src = reinterpret_cast<const float4*>(sg.w);
+    float4* dst = asm4 + a * n4;
+    for (int i0 = threadIdx.x; i0 < n4; i0 += 4 * 256) {   // four loads in flight per thread
+      float4 t[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (i0 + u * 256 < n4) t[u] = __ldg(src + i0 + u * 256);
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (i0 + u * 256 < n4) dst[i0 + u * 256] = t[u];
+    }
     if (sg.bt) {
       for (long long i = blockIdx.x * 256LL + threadIdx.x; i < (long long)sg.b_rows * r;
            i += (long long)gridDim.x * 256) {
@@ -837,84 +910,116 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_lora_kernel(const float* __re
   const int lane = threadIdx.x % 32;
   const int d4 = d / 4;
   const float4* g4 = reinterpret_cast<const float4*>(gamma);
-  for (int n = blockIdx.x * warps + threadIdx.x / 32; n < N; n += gridDim.x * warps) {
-    const float4* xr = reinterpret_cast<const float4*>(x + (long long)n * d);
-    float4 v[NC];
-    float ss = 0.f;
+  for (int n0 = (blockIdx.x * warps + threadIdx.x / 32) * RW; n0 < N; n0 += gridDim.x * warps * RW) {
+    float4 y[RW][NC];
 #pragma unroll
-    for (int i = 0; i < NC; ++i) {
-      const int c = lane + 32 * i;
-      v[i] = c < d4 ? __ldcs(xr + c) : f4_zero();
-      ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+    for (int q = 0; q < RW; ++q) {
+      const int n = n0 + q;
+      const float4* xr = reinterpret_cast<const float4*>(x + (long long)n * d);
+#pragma unroll
+      for (int i = 0; i < NC; ++i) {
+        const int c = lane + 32 * i;
+        y[q][i] = (n < N && c < d4) ? __ldcs(xr + c) : f4_zero();
+      }
     }
-    ss = warp_sum(ss);
-    const float rr = 1.0f / sqrtf(ss / (float)d + eps);
-    float acc[NS][RT];
 #pragma unroll
-    for (int a = 0; a < NS; ++a)
+    for (int q = 0; q < RW; ++q) {
+      float ss = 0.f;
 #pragma unroll
-      for (int j = 0; j < RT; ++j) acc[a][j] = 0.f;
+      for (int i = 0; i < NC; ++i)
+        ss += y[q][i].x * y[q][i].x + y[q][i].y * y[q][i].y + y[q][i].z * y[q][i].z + y[q][i].w * y[q][i].w;
+      ss = warp_sum(ss);
+      const float rr = 1.0f / sqrtf(ss / (float)d + eps);
+      const int n = n0 + q;
 #pragma unroll
-    for (int i = 0; i < NC; ++i) {
-      const int c = lane + 32 * i;
-      if (c < d4) {
-        const float4 gg = g4[c];
-        const float4 y = make_float4(v[i].x * rr * gg.x, v[i].y * rr * gg.y, v[i].z * rr * gg.z, v[i].w * rr * gg.w);
-        store_planes4(h, (long long)n * d + c * 4, y);
+      for (int i = 0; i < NC; ++i) {
+        const int c = lane + 32 * i;
+        if (c < d4) {
+          const float4 gg = g4[c];
+          y[q][i] = make_float4(y[q][i].x * rr * gg.x, y[q][i].y * rr * gg.y, y[q][i].z * rr * gg.z,
+                                y[q][i].w * rr * gg.w);
+          if (n < N) store_planes4(h, (long long)n * ldh + c * 4, y[q][i]);
+        }
+      }
+    }
 #pragma unroll
-        for (int a = 0; a < NS; ++a)
+    for (int a = 0; a < NS; ++a) {
+      float acc[RW][RT];
+#pragma unroll
+      for (int q = 0; q < RW; ++q)
+#pragma unroll
+        for (int j = 0; j < RT; ++j) acc[q][j] = 0.f;
+#pragma unroll
+      for (int i = 0; i < NC; ++i) {
+        const int c = lane + 32 * i;
+        if (c < d4) {
 #pragma unroll
           for (int j = 0; j < RT; ++j) {
             if (j < r) {
               const float4 w = *reinterpret_cast<const float4*>(as + (a * r + j) * d + c * 4);
-              acc[a][j] += y.x * w.x + y.y * w.y + y.z * w.z + y.w * w.w;
+#pragma unroll
+              for (int q = 0; q < RW; ++q)
+                acc[q][j] += y[q][i].x * w.x + y[q][i].y * w.y + y[q][i].z * w.z + y[q][i].w * w.w;
             }
           }
+        }
+      }
+      const LoraSeg& sg = g.s[a];
+      const int j = warp_sum_multi_index<RT>(lane);
+#pragma unroll
+      for (int q = 0; q < RW; ++q) {
+        const float t = sg.alpha * warp_sum_multi<RT>(acc[q], lane);
+        const int n = n0 + q;
+        if (n < N && j < r && warp_sum_multi_leader<RT>(lane)) {
+          sg.out[(long long)n * r + j] = t;
+          if (sg.ext_col >= 0) {
+            bf16 hh, ll;
+            split2(t, hh, ll);
+            h.hi[(long long)n * ldh + sg.ext_col + j] = hh;
+            h.lo[(long long)n * ldh + sg.ext_col + j] = ll;
+          }
+        }
       }
     }
-#pragma unroll
-    for (int a = 0; a < NS; ++a)
-#pragma unroll
-      for (int j = 0; j < RT; ++j) {
-        const float t = warp_sum(acc[a][j]);
-        if (j < r && lane == (j & 31)) g.s[a].out[(long long)n * r + j] = g.s[a].alpha * t;
-      }
   }
 }
 
 template <int NC>
 struct RmsFwdLora {
   template <int RT, int NS>
-  static int go(const float* x, const float* gamma, Planes h, int N, int d, float eps, int r, const LoraSegs& g,
-                cudaStream_t st) {
+  static int go(const float* x, const float* gamma, Planes h, long long ldh, int N, int d, float eps, int r,
+                const LoraSegs& g, cudaStream_t st) {
+    constexpr int RW = NS * RT <= 32 ? 2 : 1;
+    auto* kern = rmsnorm_fwd_lora_kernel<NC, RT, NS, RW>;
     static bool attr = false;
     if (!attr) {
-      cudaFuncSetAttribute(rmsnorm_fwd_lora_kernel<NC, RT, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           200 * 1024);
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
       attr = true;
     }
     const size_t smem = (size_t)NS * r * d * sizeof(float);
-    launch_pdl(rmsnorm_fwd_lora_kernel<NC, RT, NS>, dim3(grid_for((long long)N * 32, 256)), dim3(256), smem, st, x,
-               gamma, h, N, d, eps, r, g);
+    launch_pdl(kern, dim3(grid_for(((long long)N + RW - 1) / RW * 32, 256)), dim3(256), smem, st, x, gamma, h, ldh, N,
+               d, eps, r, g);
     return ok();
   }
-  static int run(const float* x, const float* gamma, Planes h, int N, int d, float eps, int r, LoraSegs g,
-                 cudaStream_t st) {
+  static int run(const float* x, const float* gamma, Planes h, long long ldh, int N, int d, float eps, int r,
+                 LoraSegs g, cudaStream_t st) {
     if (r <= 8) {
-      if (g.n == 1) return go<8, 1>(x, gamma, h, N, d, eps, r, g, st);
-      if (g.n == 2) return go<8, 2>(x, gamma, h, N, d, eps, r, g, st);
-      return go<8, 3>(x, gamma, h, N, d, eps, r, g, st);
+      if (g.n == 1) return go<8, 1>(x, gamma, h, ldh, N, d, eps, r, g, st);
+      if (g.n == 2) return go<8, 2>(x, gamma, h, ldh, N, d, eps, r, g, st);
+      return go<8, 3>(x, gamma, h, ldh, N, d, eps, r, g, st);
     }
-    if (g.n == 1) return go<16, 1>(x, gamma, h, N, d, eps, r, g, st);
-    if (g.n == 2) return go<16, 2>(x, gamma, h, N, d, eps, r, g, st);
-    return go<16, 3>(x, gamma, h, N, d, eps, r, g, st);
+    if (g.n == 1) return go<16, 1>(x, gamma, h, ldh, N, d, eps, r, g, st);
+    if (g.n == 2) return go<16, 2>(x, gamma, h, ldh, N, d, eps, r, g, st);
+    return go<16, 3>(x, gamma, h, ldh, N, d, eps, r, g, st);
   }
 };
 
 template <int NC>
 struct RmsFwd {
-  static int run(const float* x, const float* gamma, Planes h, int N, int d, float eps, cudaStream_t st) {
-    launch_pdl(rmsnorm_fwd_kernel<NC>, dim3(grid_for((long long)N * 32, 256)), dim3(256), 0, st, x, gamma, h, N, d, eps);
+  static int run(const float* x, const float* gamma, Planes h, long long ldh, int N, int d, float eps,
+                 cudaStream_t st) {
+    launch_pdl(rmsnorm_fwd_kernel<NC>, dim3(grid_for((long long)N * 32, 256)), dim3(256), 0, st, x, gamma, h, ldh, N, d,
+               eps);
     return ok();
   }
 };
@@ -975,26 +1080,31 @@ int launch_embed_scatter(const float* dx, const int* order, const int* seg_start
   return ok();
 }
 
-int launch_rmsnorm_fwd(const float* x, const float* gamma, Planes h, int N, int d, float eps, cudaStream_t st) {
-  if (d % 4) return -1;
-  return dispatch_nc<RmsFwd>(row_chunks(d), x, gamma, h, N, d, eps, st);
+int launch_rmsnorm_fwd(const float* x, const float* gamma, Planes h, int N, int d, float eps, cudaStream_t st,
+                       long long ldh) {
+  if (ldh == 0) ldh = d;
+  if (d % 4 || ldh % 4 || ldh < d) return -1;
+  return dispatch_nc<RmsFwd>(row_chunks(d), x, gamma, h, ldh, N, d, eps, st);
 }
 
 int launch_rmsnorm_fwd_lora(const float* x, const float* gamma, Planes h, int N, int d, float eps, int r,
-                            const LoraSegs& g, cudaStream_t st) {
-  if (d % 4 || r < 1 || r > 16 || g.n < 1 || g.n > kLoraMaxSegs) return -1;
+                            const LoraSegs& g, cudaStream_t st, long long ldh) {
+  if (ldh == 0) ldh = d;
+  if (d % 4 || ldh % 4 || ldh < d || r < 1 || r > 16 || g.n < 1 || g.n > kLoraMaxSegs) return -1;
+  for (int a = 0; a < g.n; ++a)
+    if (g.s[a].ext_col >= 0 && (g.s[a].ext_col < d || g.s[a].ext_col + r > ldh)) return -1;
   if ((size_t)g.n * r * d * 4 > 200 * 1024) return -2;   // the adapters' A do not fit in shared memory
   for (int a = 0; a < g.n; ++a)
     if (!g.s[a].w || !g.s[a].out || g.s[a].col_off != 0 || g.s[a].width != d ||
         (g.s[a].bt && (!g.s[a].b_src || g.s[a].b_rows <= 0)))
       return -1;
   switch (row_chunks(d)) {   // the chunk counts whose register arrays stay small next to the adapter sums
-    case 1: return RmsFwdLora<1>::run(x, gamma, h, N, d, eps, r, g, st);
-    case 2: return RmsFwdLora<2>::run(x, gamma, h, N, d, eps, r, g, st);
-    case 4: return RmsFwdLora<4>::run(x, gamma, h, N, d, eps, r, g, st);
-    case 5: return RmsFwdLora<5>::run(x, gamma, h, N, d, eps, r, g, st);
-    case 8: return RmsFwdLora<8>::run(x, gamma, h, N, d, eps, r, g, st);
-    case 16: return RmsFwdLora<16>::run(x, gamma, h, N, d, eps, r, g, st);
+    case 1: return RmsFwdLora<1>::run(x, gamma, h, ldh, N, d, eps, r, g, st);
+    case 2: return RmsFwdLora<2>::run(x, gamma, h, ldh, N, d, eps, r, g, st);
+    case 4: return RmsFwdLora<4>::run(x, gamma, h, ldh, N, d, eps, r, g, st);
+    case 5: return RmsFwdLora<5>::run(x, gamma, h, ldh, N, d, eps, r, g, st);
+    case 8: return RmsFwdLora<8>::run(x, gamma, h, ldh, N, d, eps, r, g, st);
+    case 16: return RmsFwdLora<16>::run(x, gamma, h, ldh, N, d, eps, r, g, st);
     default: return -2;   // caller falls back to rmsnorm_fwd + the group down-projection
   }
 }
@@ -1022,18 +1132,22 @@ int launch_rope_qkv_fwd(const float* qkv, const float* bias, const int* pos, con
 
 int launch_rope_qkv_bwd(const float* dQ, const float* dK, const float* dV, const int* pos, const float* cs_tab,
                         int tab_rows, Planes dqkv, float* dqkv_f32, int B, int T, int H, int KV, int dh,
-                        cudaStream_t st) {
-  return launch_rope_qkv_bwd_sum(dQ, 0, 0, dK, dV, 0, 1, pos, cs_tab, tab_rows, dqkv, dqkv_f32, B, T, H, KV, dh, st);
+                        cudaStream_t st, long long ld_dqkv) {
+  return launch_rope_qkv_bwd_sum(dQ, 0, 0, dK, dV, 0, 1, pos, cs_tab, tab_rows, dqkv, dqkv_f32, B, T, H, KV, dh, st,
+                                 ld_dqkv);
 }
 
 int launch_rope_qkv_bwd_sum(const float* dQ, long long q_pstride, int q_tile, const float* dK, const float* dV,
                             long long kv_pstride, int kv_parts, const int* pos, const float* cs_tab, int tab_rows,
-                            Planes dqkv, float* dqkv_f32, int B, int T, int H, int KV, int dh, cudaStream_t st) {
+                            Planes dqkv, float* dqkv_f32, int B, int T, int H, int KV, int dh, cudaStream_t st,
+                            long long ld_dqkv) {
   const int N = B * T;
-  if (q_tile < 0 || kv_parts < 1) return -1;
+  const long long width = (long long)(H + 2 * KV) * dh;
+  if (ld_dqkv == 0) ld_dqkv = width;
+  if (q_tile < 0 || kv_parts < 1 || ld_dqkv < width) return -1;
   launch_pdl(rope_qkv_bwd_kernel, dim3(N < 8 * kSMs ? N : 8 * kSMs), dim3(256), 0, st, dQ, q_pstride, q_tile, dK, dV,
-             kv_pstride, kv_parts, pos, reinterpret_cast<const float2*>(cs_tab), tab_rows, dqkv, dqkv_f32, N, T, H,
-             KV, dh);
+             kv_pstride, kv_parts, pos, reinterpret_cast<const float2*>(cs_tab), tab_rows, dqkv, ld_dqkv, dqkv_f32, N,
+             T, H, KV, dh);
   return ok();
 }
 
@@ -1054,9 +1168,10 @@ int launch_swiglu_fwd(const float* gu, Planes a, int N, int ff, cudaStream_t st)
   return ok();
 }
 
-int launch_swiglu_bwd(const float* gu, const float* da, Planes dgu, int N, int ff, cudaStream_t st) {
-  if (ff % 4) return -1;
-  launch_pdl(swiglu_bwd_kernel, dim3(N < 16 * kSMs ? N : 16 * kSMs), dim3(128), 0, st, gu, da, dgu, N, ff);
+int launch_swiglu_bwd(const float* gu, const float* da, Planes dgu, int N, int ff, cudaStream_t st, long long ld_dgu) {
+  if (ld_dgu == 0) ld_dgu = 2LL * ff;
+  if (ff % 4 || ld_dgu % 4 || ld_dgu < 2LL * ff) return -1;
+  launch_pdl(swiglu_bwd_kernel, dim3(N < 16 * kSMs ? N : 16 * kSMs), dim3(128), 0, st, gu, da, dgu, ld_dgu, N, ff);
   return ok();
 }
 
@@ -1092,6 +1207,12 @@ int launch_adamw(float* p, const float* g, float* m, float* v, Planes pp, long l
 int launch_q8_0_to_planes(const uint8_t* q, Planes out, float* f32, long long rows, int K, cudaStream_t st) {
   if (K % 32) return -1;
   launch_pdl(q8_0_to_planes_kernel, dim3(grid_for(rows * K, 256)), dim3(256), 0, st, q, out, f32, rows, K);
+  return ok();
+}
+
+int launch_q8_0_ring(const RingLayer* desc, long long chunks, cudaStream_t st) {
+  if (!desc || chunks <= 0) return -1;
+  launch_pdl(q8_0_ring_kernel, dim3(grid_for(chunks, 256)), dim3(256), 0, st, desc);
   return ok();
 }
 

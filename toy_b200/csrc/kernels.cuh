@@ -29,17 +29,20 @@ int launch_embed_scatter(const float* dx, const int* order, const int* seg_start
                          const int* nseg_dev, int max_seg, float* dE, int d, cudaStream_t st);
 
 // h = rmsnorm(x) * gamma written as planes (ggml rms_norm + mul).
-int launch_rmsnorm_fwd(const float* x, const float* gamma, Planes h, int N, int d, float eps, cudaStream_t st);
+int launch_rmsnorm_fwd(const float* x, const float* gamma, Planes h, int N, int d, float eps, cudaStream_t st,
+                       long long ldh = 0);   // h rows ldh apart (0: d)
 
 // dx = dres + rms_norm_back(x, dh * gamma) (f32, may alias dres) and its planes;
 // per-block partial sums of dh * x * rrms into gpart[nblk][d] (for dgamma).
 struct LoraSegs;
 // launch_rmsnorm_fwd plus, in the same pass over each row, u_a = h A_a^T for
 // the adapters in g (all reading the whole row: col_off 0, width d; A_a [r][d];
-// rank <= 16) and their B^T copies. Returns -2 for a width it has no variant
-// for (the caller then runs the two passes).
+// rank <= 16) and their B^T copies; h rows are ldh apart (0: d), and an
+// adapter with ext_col >= 0 also gets u_a as planes in h's columns ext_col + j.
+// Returns -2 for a width it has no variant for (the caller then runs the two
+// passes).
 int launch_rmsnorm_fwd_lora(const float* x, const float* gamma, Planes h, int N, int d, float eps, int r,
-                            const LoraSegs& g, cudaStream_t st);
+                            const LoraSegs& g, cudaStream_t st, long long ldh = 0);
 int launch_rmsnorm_bwd(const float* x, const float* dh, const float* gamma, const float* dres, float* dx,
                        Planes dxp, float* gpart, int nblk, int N, int d, float eps, cudaStream_t st);
 // gout[c] = (accumulate ? gout[c] : 0) + sum_b gpart[b][c]
@@ -54,13 +57,14 @@ int launch_rope_qkv_fwd(const float* qkv, const float* bias, const int* pos, con
 // (rotation by -theta on dQ, dK).
 int launch_rope_qkv_bwd(const float* dQ, const float* dK, const float* dV, const int* pos, const float* cs_tab,
                         int tab_rows, Planes dqkv, float* dqkv_f32, int B, int T, int H, int KV, int dh,
-                        cudaStream_t st);
+                        cudaStream_t st, long long ld_dqkv = 0);
 // Same, with dQ / dK / dV given as sums of partial arrays added in index order:
 // dQ of position t sums parts 0 .. t / q_tile (q_tile = 0: one part), q_pstride
 // floats apart; dK and dV sum kv_parts parts, kv_pstride floats apart.
 int launch_rope_qkv_bwd_sum(const float* dQ, long long q_pstride, int q_tile, const float* dK, const float* dV,
                             long long kv_pstride, int kv_parts, const int* pos, const float* cs_tab, int tab_rows,
-                            Planes dqkv, float* dqkv_f32, int B, int T, int H, int KV, int dh, cudaStream_t st);
+                            Planes dqkv, float* dqkv_f32, int B, int T, int H, int KV, int dh, cudaStream_t st,
+                            long long ld_dqkv = 0);
 
 // P = softmax(S) over keys k <= q (rows of [Z][T][T]); masked entries 0.
 int launch_softmax_causal_fwd(const float* S, Planes P, long long Z, int T, cudaStream_t st);
@@ -71,7 +75,9 @@ int launch_softmax_causal_bwd(Planes P, const float* dP, Planes dS, long long Z,
 // a = silu(gate) * up from gu [N][2*ff] (gate | up) -> planes [N][ff].
 int launch_swiglu_fwd(const float* gu, Planes a, int N, int ff, cudaStream_t st);
 // dgate = silu_back(gate, da * up), dup = da * silu(gate) -> planes [N][2*ff].
-int launch_swiglu_bwd(const float* gu, const float* da, Planes dgu, int N, int ff, cudaStream_t st);
+// dgu planes rows are ld_dgu apart (0: 2 ff).
+int launch_swiglu_bwd(const float* gu, const float* da, Planes dgu, int N, int ff, cudaStream_t st,
+                      long long ld_dgu = 0);
 
 // Cross-entropy over rows of logits [N][V]: loss_rows[n] and dlogits planes
 // ((softmax - y) / N). Labels are ids (label_ids, -1 = none) or, when
@@ -97,6 +103,39 @@ int launch_adamw(float* p, const float* g, float* m, float* v, Planes pp, long l
 int launch_q8_0_to_planes(const uint8_t* q, Planes out, float* f32, long long rows, int K, cudaStream_t st);
 // f32 [rows][K] -> Q8_0 blocks (ggml quantize_row_q8_0_ref, bit-exact).
 int launch_q8_0_quantize(const float* x, uint8_t* q, long long rows, int K, cudaStream_t st);
+// The ring copy of one GEMM operand over a transformer block's frozen Q8_0
+// projections (the q|k|v rows, o, the gate|up rows or down): planes
+// [d_out + ext][d_in + ext], row pitch d_in + ext. Rows < d_out hold the
+// dequantised W (columns < d_in; bit-identical to what the Q8_0 GEMM builds in
+// shared memory: hi = rn(v), lo = rn(v - hi), v = scale * quant) and, in
+// extension column d_in + 16 a + j, s * B_a[row - c0_a][j] for the rows adapter
+// a covers; extension row d_out + 16 a + j holds A_a[j][:]; all else is 0. So
+// [X | u] times the rows (K-major) is X W^T + s u B^T, and [dY | du] times the
+// matrix read MN-major is dY W + du A (du = s dY B).
+struct RingAdapter {
+  const float* A = nullptr;   // [r][d_in]
+  const float* B = nullptr;   // [width][r]
+  int c0 = 0, width = 0;
+};
+struct RingMat {
+  const int8_t* qv = nullptr;     // quants [d_out][d_in]
+  const uint16_t* qs = nullptr;   // fp16 scale bits [d_out * d_in / 32]
+  bf16* hi = nullptr;
+  bf16* lo = nullptr;
+  int d_out = 0, d_in = 0, ext = 0, n_ad = 0, r = 0;
+  float s = 0.f;
+  long long chunk0 = 0;           // first 16-value chunk of this matrix in the launch
+  RingAdapter ad[3];
+};
+constexpr int kRingMats = 4;
+struct RingLayer {
+  RingMat m[kRingMats];
+  int n = 0;
+  long long chunks = 0;           // 16-value chunks of all n matrices
+};
+// Fills the matrices of one block; desc is a RingLayer in device memory whose
+// chunk count is `chunks`.
+int launch_q8_0_ring(const RingLayer* desc, long long chunks, cudaStream_t st);
 // Q8_0 blocks -> the GEMM's quant layout: the 32 int8 quants of block b at
 // qv[32 b ..] and its fp16 scale bits at qs[b] (the same Q8_0 content, scales
 // split off so quant tiles are TMA-loadable).

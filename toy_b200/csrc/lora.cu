@@ -5,6 +5,7 @@
 #include <algorithm>
 
 #include "pdl.cuh"
+#include "warp_reduce.cuh"
 
 namespace tb2 {
 
@@ -411,11 +412,14 @@ struct Bwd {
   }
 };
 
-// Group down pass: one warp per token row (two rows in flight). Every
-// adapter's w is staged in shared memory ([r][width] each, read as float4
-// along k: conflict-free). When all adapters read the same columns of X (the
-// forward: one normalised input, several adapters) each X chunk is loaded
-// once for all of them. Also writes the B^T copies.
+// Group down pass: one warp per two token rows. Every adapter's w is staged
+// in shared memory ([r][width] each, read as float4 along k: conflict-free).
+// When all adapters read the same columns of X (the forward: one normalised
+// input, several adapters) each X chunk is loaded once for all of them. Four
+// 128-column chunks of both rows are loaded before they are used; the r sums
+// of an adapter are reduced with warp_sum_multi. Also writes the B^T copies,
+// and, for adapters with ext_col >= 0, the results as planes into X's columns
+// ext_col + j.
 template <int RT, int NS, bool SHARED>
 __global__ void __launch_bounds__(256) lora_down_group_kernel(Planes X, long long ldx, int N, int r, LoraSegs g) {
   griddep_wait();
@@ -433,8 +437,18 @@ __global__ void __launch_bounds__(256) lora_down_group_kernel(Planes X, long lon
 #pragma unroll
   for (int a = 0; a < NS; ++a) {
     const LoraSeg& sg = g.s[a];
-    for (int i = threadIdx.x * 4; i < r * sg.width; i += 256 * 4)
-      *reinterpret_cast<float4*>(wsm + wofs[a] + i) = __ldg(reinterpret_cast<const float4*>(sg.w + i));
+    const int n4 = r * sg.width / 4;
+    const float4* src = reinterpret_cast<const float4*>(sg.w);
+    float4* dst = wsm4 + wofs[a] / 4;
+    for (int i0 = threadIdx.x; i0 < n4; i0 += 4 * 256) {   // four loads in flight per thread
+      float4 t[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (i0 + u * 256 < n4) t[u] = __ldg(src + i0 + u * 256);
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (i0 + u * 256 < n4) dst[i0 + u * 256] = t[u];
+    }
     if (sg.bt) {
       for (long long i = blockIdx.x * 256LL + threadIdx.x; i < (long long)sg.b_rows * r;
            i += (long long)gridDim.x * 256) {
@@ -464,38 +478,55 @@ __global__ void __launch_bounds__(256) lora_down_group_kernel(Planes X, long lon
         }
       }
     };
+    // columns [col_off, col_off + width) of rows n, n + 1, four chunks at a time
+    auto pass = [&](int col_off, int width, auto&& use) {
+      const long long r0 = (long long)n * ldx + col_off;
+      for (int k0 = lane * 4; k0 < width; k0 += 4 * 128) {
+        float4 x0[4], x1[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int k = k0 + u * 128;
+          x0[u] = k < width ? load_planes4(X, r0 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+          x1[u] = (k < width && two) ? load_planes4(X, r0 + ldx + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (k0 + u * 128 < width) use(k0 + u * 128, x0[u], x1[u]);
+      }
+    };
     if constexpr (SHARED) {
-      const long long r0 = (long long)n * ldx + g.s[0].col_off;
-      for (int k = lane * 4; k < g.s[0].width; k += 128) {
-        const float4 x0 = load_planes4(X, r0 + k);
-        const float4 x1 = two ? load_planes4(X, r0 + ldx + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+      pass(g.s[0].col_off, g.s[0].width, [&](int k, const float4& x0, const float4& x1) {
 #pragma unroll
         for (int a = 0; a < NS; ++a) dot(a, k, x0, x1);
-      }
+      });
     } else {
 #pragma unroll
-      for (int a = 0; a < NS; ++a) {
-        const long long r0 = (long long)n * ldx + g.s[a].col_off;
-        for (int k = lane * 4; k < g.s[a].width; k += 128) {
-          const float4 x0 = load_planes4(X, r0 + k);
-          const float4 x1 = two ? load_planes4(X, r0 + ldx + k) : make_float4(0.f, 0.f, 0.f, 0.f);
-          dot(a, k, x0, x1);
-        }
-      }
+      for (int a = 0; a < NS; ++a)
+        pass(g.s[a].col_off, g.s[a].width, [&](int k, const float4& x0, const float4& x1) { dot(a, k, x0, x1); });
     }
+    const int j = warp_sum_multi_index<RT>(lane);
+    const bool lead = warp_sum_multi_leader<RT>(lane) && j < r;
 #pragma unroll
     for (int a = 0; a < NS; ++a) {
-#pragma unroll
-      for (int j = 0; j < RT; ++j) {
-        float v0 = acc0[a][j], v1 = acc1[a][j];
-#pragma unroll
-        for (int o = 16; o; o >>= 1) {
-          v0 += __shfl_xor_sync(0xffffffffu, v0, o);
-          v1 += __shfl_xor_sync(0xffffffffu, v1, o);
-        }
-        if (j < r && lane == (j & 31)) {
-          g.s[a].out[(long long)n * r + j] = g.s[a].alpha * v0;
-          if (two) g.s[a].out[(long long)(n + 1) * r + j] = g.s[a].alpha * v1;
+      const LoraSeg& sg = g.s[a];
+      const float v0 = sg.alpha * warp_sum_multi<RT>(acc0[a], lane);
+      const float v1 = sg.alpha * warp_sum_multi<RT>(acc1[a], lane);
+      if (lead) {
+        sg.out[(long long)n * r + j] = v0;
+        if (two) sg.out[(long long)(n + 1) * r + j] = v1;
+        if (sg.ext_col >= 0) {
+          const long long e0 = (long long)n * ldx + sg.ext_col + j;
+          __nv_bfloat16 h, l;
+          h = __float2bfloat16_rn(v0);
+          l = __float2bfloat16_rn(v0 - __bfloat162float(h));
+          X.hi[e0] = h;
+          X.lo[e0] = l;
+          if (two) {
+            h = __float2bfloat16_rn(v1);
+            l = __float2bfloat16_rn(v1 - __bfloat162float(h));
+            X.hi[e0 + ldx] = h;
+            X.lo[e0 + ldx] = l;
+          }
         }
       }
     }
@@ -732,6 +763,7 @@ int launch_lora_down_group(Planes X, long long ldx, int N, int r, const LoraSegs
     const LoraSeg& sg = segs.s[a];
     if (!sg.w || !sg.out || sg.width <= 0 || sg.width % 4 || sg.col_off % 4 || (sg.bt && (!sg.b_src || sg.b_rows <= 0)))
       return -1;
+    if (sg.ext_col >= 0 && sg.ext_col + r > ldx) return -1;
     wfloats += (size_t)r * sg.width;
     shared = shared && sg.col_off == segs.s[0].col_off && sg.width == segs.s[0].width;
   }

@@ -41,6 +41,11 @@ constexpr int kLoraMaxSegs = 3;
 // One adapter of a group for the down pass out[n][j] = alpha * sum_k
 // X[n][col_off + k] * w[j][k] (k < width); with bt set the launch also writes
 // bt[j][c] = b_src[c][j] for c < b_rows.
+//
+// With ext_col >= 0 the results are also written as planes into the row's own
+// buffer (X for the down pass, h for the fused RMSNorm) at columns ext_col + j:
+// the extra reduction columns through which the base GEMM adds the adapter
+// (y = [X | u] [W | s B]^T, dX = [dY | du] [W ; A]).
 struct LoraSeg {
   int col_off = 0, width = 0;
   const float* w = nullptr;
@@ -49,6 +54,7 @@ struct LoraSeg {
   const float* b_src = nullptr;
   int b_rows = 0;
   float* bt = nullptr;
+  int ext_col = -1;
 };
 struct LoraSegs {
   LoraSeg s[kLoraMaxSegs];
