@@ -304,51 +304,70 @@ __global__ void __launch_bounds__(256) rope_qkv_bwd_kernel(const float* __restri
                                                            long long ldo, float* out_f32, int N, int T, int H, int KV,
                                                            int dh) {
   griddep_wait();
-  const int half = dh / 2;
+  // one item = four consecutive rotation pairs (j .. j + 3, j + half ..) of one
+  // head slot of one token; the partial sums are added in part order
+  const int half = dh / 2, h4 = half / 4;
   const int slots = H + 2 * KV;
   const int width = slots * dh;
-  for (int n = blockIdx.x; n < N; n += gridDim.x) {
+  const long long items = (long long)N * slots * h4;
+  for (long long it = blockIdx.x * (long long)blockDim.x + threadIdx.x; it < items;
+       it += (long long)gridDim.x * blockDim.x) {
+    const int n = (int)(it / (slots * h4));
+    const int rem = (int)(it - (long long)n * slots * h4);
+    const int slot = rem / h4, j = (rem - slot * h4) * 4;
     const int b = n / T, t = n - b * T;
-    int p = pos[n];
-    p = p < 0 ? 0 : (p >= tab_rows ? tab_rows - 1 : p);
-    const float2* crow = cs + (long long)p * half;
-    const int q_parts = q_tile > 0 ? t / q_tile + 1 : 1;
-    for (int i = threadIdx.x; i < slots * half; i += blockDim.x) {
-      const int slot = i / half, j = i - slot * half;
-      float y0, y1;
-      if (slot < H + KV) {
-        const bool isq = slot < H;
-        const int hh = isq ? slot : slot - H;
-        const float* srcb = isq ? dQ : dK;
-        const long long src = (((long long)b * (isq ? H : KV) + hh) * T + t) * dh + j;
-        const int parts = isq ? q_parts : kv_parts;
-        const long long pstride = isq ? q_pstride : kv_pstride;
-        float g0 = 0.f, g1 = 0.f;
-        for (int q = 0; q < parts; ++q) {
-          g0 += srcb[src + q * pstride];
-          g1 += srcb[src + q * pstride + half];
-        }
-        const float2 c = crow[j];
-        y0 = g0 * c.x + g1 * c.y;
-        y1 = -g0 * c.y + g1 * c.x;
-      } else {
-        const int hh = slot - H - KV;
-        const long long src = (((long long)b * KV + hh) * T + t) * dh + j;
-        y0 = 0.f;
-        y1 = 0.f;
-        for (int q = 0; q < kv_parts; ++q) {
-          y0 += dV[src + q * kv_pstride];
-          y1 += dV[src + q * kv_pstride + half];
-        }
+    float4 g0 = make_float4(0.f, 0.f, 0.f, 0.f), g1 = g0;
+    const float* srcb;
+    long long src, pstride;
+    int parts;
+    if (slot < H) {
+      srcb = dQ; src = (((long long)b * H + slot) * T + t) * dh + j;
+      pstride = q_pstride; parts = q_tile > 0 ? t / q_tile + 1 : 1;
+    } else if (slot < H + KV) {
+      srcb = dK; src = (((long long)b * KV + slot - H) * T + t) * dh + j;
+      pstride = kv_pstride; parts = kv_parts;
+    } else {
+      srcb = dV; src = (((long long)b * KV + slot - H - KV) * T + t) * dh + j;
+      pstride = kv_pstride; parts = kv_parts;
+    }
+    int q = 0;
+    for (; q + 4 <= parts; q += 4) {   // four parts' loads in flight
+      float4 u0[4], u1[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        u0[k] = *reinterpret_cast<const float4*>(srcb + src + (q + k) * pstride);
+        u1[k] = *reinterpret_cast<const float4*>(srcb + src + (q + k) * pstride + half);
       }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        g0.x += u0[k].x; g0.y += u0[k].y; g0.z += u0[k].z; g0.w += u0[k].w;
+        g1.x += u1[k].x; g1.y += u1[k].y; g1.z += u1[k].z; g1.w += u1[k].w;
+      }
+    }
+    for (; q < parts; ++q) {
+      const float4 u0 = *reinterpret_cast<const float4*>(srcb + src + q * pstride);
+      const float4 u1 = *reinterpret_cast<const float4*>(srcb + src + q * pstride + half);
+      g0.x += u0.x; g0.y += u0.y; g0.z += u0.z; g0.w += u0.w;
+      g1.x += u1.x; g1.y += u1.y; g1.z += u1.z; g1.w += u1.w;
+    }
+    float4 y0 = g0, y1 = g1;
+    if (slot < H + KV) {   // rotation by -theta on dQ, dK
+      int p = pos[n];
+      p = p < 0 ? 0 : (p >= tab_rows ? tab_rows - 1 : p);
+      const float2* c = cs + (long long)p * half + j;
+      const float2 c0 = c[0], c1 = c[1], c2 = c[2], c3 = c[3];
+      y0 = make_float4(g0.x * c0.x + g1.x * c0.y, g0.y * c1.x + g1.y * c1.y, g0.z * c2.x + g1.z * c2.y,
+                       g0.w * c3.x + g1.w * c3.y);
+      y1 = make_float4(-g0.x * c0.y + g1.x * c0.x, -g0.y * c1.y + g1.y * c1.x, -g0.z * c2.y + g1.z * c2.x,
+                       -g0.w * c3.y + g1.w * c3.x);
+    }
+    const long long dp = (long long)n * ldo + slot * dh + j;
+    store_planes4(out, dp, y0);
+    store_planes4(out, dp + half, y1);
+    if (out_f32) {
       const long long dst = (long long)n * width + slot * dh + j;
-      const long long dp = (long long)n * ldo + slot * dh + j;
-      store_planes(out, dp, y0);
-      store_planes(out, dp + half, y1);
-      if (out_f32) {
-        out_f32[dst] = y0;
-        out_f32[dst + half] = y1;
-      }
+      *reinterpret_cast<float4*>(out_f32 + dst) = y0;
+      *reinterpret_cast<float4*>(out_f32 + dst + half) = y1;
     }
   }
 }
@@ -1144,8 +1163,10 @@ int launch_rope_qkv_bwd_sum(const float* dQ, long long q_pstride, int q_tile, co
   const int N = B * T;
   const long long width = (long long)(H + 2 * KV) * dh;
   if (ld_dqkv == 0) ld_dqkv = width;
-  if (q_tile < 0 || kv_parts < 1 || ld_dqkv < width) return -1;
-  launch_pdl(rope_qkv_bwd_kernel, dim3(N < 8 * kSMs ? N : 8 * kSMs), dim3(256), 0, st, dQ, q_pstride, q_tile, dK, dV,
+  if (q_tile < 0 || kv_parts < 1 || ld_dqkv < width || dh % 8 || ld_dqkv % 4 || q_pstride % 4 || kv_pstride % 4)
+    return -1;
+  const long long items = (long long)N * (H + 2 * KV) * (dh / 8);
+  launch_pdl(rope_qkv_bwd_kernel, dim3(grid_for(items, 256)), dim3(256), 0, st, dQ, q_pstride, q_tile, dK, dV,
              kv_pstride, kv_parts, pos, reinterpret_cast<const float2*>(cs_tab), tab_rows, dqkv, ld_dqkv, dqkv_f32, N,
              T, H, KV, dh);
   return ok();

@@ -5,6 +5,8 @@
 #include <algorithm>
 
 #include "pdl.cuh"
+#include "runtime.cuh"
+#include "tc_common.cuh"
 #include "warp_reduce.cuh"
 
 namespace tb2 {
@@ -533,6 +535,147 @@ __global__ void __launch_bounds__(256) lora_down_group_kernel(Planes X, long lon
   }
 }
 
+// Bulk-staged group down pass: a block of 8 warps takes kDownRows consecutive
+// rows. Warp 0 issues bulk copies of every adapter's w and of the columns each
+// adapter reads from those rows (both planes) into shared memory, all
+// completing on one mbarrier, so every block's loads are in flight at once;
+// warp w then reduces rows w and w + 8 from shared memory. Shared memory:
+// the barrier, w of each adapter ([r][width] f32), then per row and staged
+// segment the hi and the lo columns. Results, B^T copies and extra-column
+// planes as lora_down_group_kernel.
+constexpr int kDownRows = 16;
+
+template <int RT, int NS, bool SHARED>
+__global__ void __launch_bounds__(256) lora_down_bulk_kernel(Planes X, long long ldx, int N, int r, LoraSegs g,
+                                                            int* err) {
+  extern __shared__ __align__(128) uint8_t dsm[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(dsm);
+  float* wsm = reinterpret_cast<float*>(dsm + 16);
+  constexpr int NSEG = SHARED ? 1 : NS;   // column segments staged per row
+  int wofs[NS], sofs[NSEG], wtot = 0, rowb = 0;
+#pragma unroll
+  for (int a = 0; a < NS; ++a) {
+    wofs[a] = wtot;
+    wtot += r * g.s[a].width;
+  }
+#pragma unroll
+  for (int q = 0; q < NSEG; ++q) {
+    sofs[q] = rowb;
+    rowb += g.s[q].width;
+  }
+  bf16* rsm = reinterpret_cast<bf16*>(wsm + wtot);   // [kDownRows][2 rowb]
+  const int n0 = blockIdx.x * kDownRows;
+  const int rows = min(kDownRows, N - n0);
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  griddep_wait();
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(wtot * 4 + rows * rowb * 4));
+    __syncwarp();
+    const int ncopy = NS + rows * NSEG * 2;
+    for (int c = lane; c < ncopy; c += 32) {
+      if (c < NS) {
+        bulk_load(wsm + wofs[c], g.s[c].w, (uint32_t)(r * g.s[c].width * 4), bar);
+      } else {
+        const int k = c - NS, t = k / (NSEG * 2), q = (k / 2) % NSEG, pl = k % 2;
+        const int w = g.s[q].width;
+        bf16* dst = rsm + (long long)t * 2 * rowb + 2 * sofs[q] + pl * w;
+        const bf16* src = (pl ? X.lo : X.hi) + (long long)(n0 + t) * ldx + g.s[q].col_off;
+        bulk_load(dst, src, (uint32_t)(w * 2), bar);
+      }
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < NS; ++a) {   // B^T copies for the splice, while the copies land
+    const LoraSeg& sg = g.s[a];
+    if (sg.bt) {
+      for (long long i = blockIdx.x * 256LL + threadIdx.x; i < (long long)sg.b_rows * r;
+           i += (long long)gridDim.x * 256) {
+        const int c = (int)(i / r), j = (int)(i % r);
+        sg.bt[(long long)j * sg.b_rows + c] = sg.b_src[i];
+      }
+    }
+  }
+  if (!mbar_wait(bar, 0, err, kErrWaitBulk)) return;
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  const int t0 = warp, t1 = warp + 8;
+  const bool two = t1 < rows;
+  if (t0 >= rows) return;
+  const int j = warp_sum_multi_index<RT>(lane);
+  const bool lead = warp_sum_multi_leader<RT>(lane) && j < r;
+#pragma unroll
+  for (int a = 0; a < NS; ++a) {
+    const LoraSeg& sg = g.s[a];
+    const int q = SHARED ? 0 : a;
+    const int w = sg.width;
+    const bf16* h0 = rsm + (long long)t0 * 2 * rowb + 2 * sofs[q];
+    const bf16* h1 = rsm + (long long)t1 * 2 * rowb + 2 * sofs[q];
+    float acc0[RT], acc1[RT];
+#pragma unroll
+    for (int jj = 0; jj < RT; ++jj) acc0[jj] = acc1[jj] = 0.f;
+    for (int k = lane * 4; k < w; k += 128) {
+      const float4 x0 = load_planes4(Planes{const_cast<bf16*>(h0), const_cast<bf16*>(h0 + w)}, k);
+      const float4 x1 = two ? load_planes4(Planes{const_cast<bf16*>(h1), const_cast<bf16*>(h1 + w)}, k)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int jj = 0; jj < RT; ++jj) {
+        if (jj < r) {
+          const float4 wv = *reinterpret_cast<const float4*>(wsm + wofs[a] + jj * w + k);
+          acc0[jj] += x0.x * wv.x + x0.y * wv.y + x0.z * wv.z + x0.w * wv.w;
+          acc1[jj] += x1.x * wv.x + x1.y * wv.y + x1.z * wv.z + x1.w * wv.w;
+        }
+      }
+    }
+    const float v0 = sg.alpha * warp_sum_multi<RT>(acc0, lane);
+    const float v1 = sg.alpha * warp_sum_multi<RT>(acc1, lane);
+    if (lead) {
+      const long long n = n0 + t0;
+      sg.out[n * r + j] = v0;
+      if (two) sg.out[(n + 8) * r + j] = v1;
+      if (sg.ext_col >= 0) {
+        const long long e0 = n * ldx + sg.ext_col + j;
+        bf16 h = __float2bfloat16_rn(v0);
+        X.hi[e0] = h;
+        X.lo[e0] = __float2bfloat16_rn(v0 - __bfloat162float(h));
+        if (two) {
+          h = __float2bfloat16_rn(v1);
+          X.hi[e0 + 8 * ldx] = h;
+          X.lo[e0 + 8 * ldx] = __float2bfloat16_rn(v1 - __bfloat162float(h));
+        }
+      }
+    }
+  }
+}
+
+template <int RT, int NS>
+int down_bulk(Planes X, long long ldx, int N, int r, const LoraSegs& segs, bool shared, size_t smem, cudaStream_t st) {
+  static bool attr[2] = {false, false};
+  auto* k0 = lora_down_bulk_kernel<RT, NS, false>;
+  auto* k1 = lora_down_bulk_kernel<RT, NS, true>;
+  if (!attr[shared]) {
+    if (cudaFuncSetAttribute(shared ? k1 : k0, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
+        cudaSuccess)
+      return -3;
+    attr[shared] = true;
+  }
+  int* err = device_error_word();
+  const unsigned blocks = (unsigned)((N + kDownRows - 1) / kDownRows);
+  return shared ? launch_pdl(k1, dim3(blocks), dim3(256), smem, st, X, ldx, N, r, segs, err)
+                : launch_pdl(k0, dim3(blocks), dim3(256), smem, st, X, ldx, N, r, segs, err);
+}
+
+template <int RT>
+int down_bulk_ns(Planes X, long long ldx, int N, int r, const LoraSegs& segs, bool shared, size_t smem,
+                 cudaStream_t st) {
+  if (segs.n == 1) return down_bulk<RT, 1>(X, ldx, N, r, segs, shared, smem, st);
+  if (segs.n == 2) return down_bulk<RT, 2>(X, ldx, N, r, segs, shared, smem, st);
+  return down_bulk<RT, 3>(X, ldx, N, r, segs, shared, smem, st);
+}
+
 template <int RT, int NS>
 int down_group(Planes X, long long ldx, int N, int r, const LoraSegs& segs, bool shared, size_t smem,
                cudaStream_t st) {
@@ -545,7 +688,9 @@ int down_group(Planes X, long long ldx, int N, int r, const LoraSegs& segs, bool
       return -3;
     attr[shared] = true;
   }
-  const unsigned blocks = (unsigned)std::min<long long>(148, (N + 15) / 16);
+  // one row pair per warp: the pass is latency-bound, so every row's loads are
+  // in flight at once (each block restages w, a few KB of L2 reads)
+  const unsigned blocks = (unsigned)std::min<long long>(148 * 4, (N + 15) / 16);
   return shared ? launch_pdl(k1, dim3(blocks), dim3(256), smem, st, X, ldx, N, r, segs)
                 : launch_pdl(k0, dim3(blocks), dim3(256), smem, st, X, ldx, N, r, segs);
 }
@@ -558,93 +703,140 @@ int down_group_ns(Planes X, long long ldx, int N, int r, const LoraSegs& segs, b
   return down_group<RT, 3>(X, ldx, N, r, segs, shared, smem, st);
 }
 
-// Group weight-gradient partials. Factor f = 2 i (dB of adapter i: dY columns
-// col_off_i .., S = u_i, scaled by s) or 2 i + 1 (dA: X columns, S = du_i);
-// blockIdx.x walks the 64-column groups of all factors (gbase[f] = first
-// group of factor f), blockIdx.y the token chunks. Partials are [chunk][col][r]
-// over the concatenated columns (cbase[f] = first column of factor f).
-struct WgLayout {
-  int nf;
-  int gbase[2 * kLoraMaxSegs + 1];
-  int cbase[2 * kLoraMaxSegs + 1];
+// Group weight gradients as factors: dB_i = s dY_i^T u_i (columns of dY,
+// S = u_i) for each adapter, and dA = du^T X over X's columns with the S row
+// [du_0 | du_1 | ..] of all adapters at once (or one dA factor per adapter
+// when their ranks add up past kWgMaxS). A block takes 64 columns of one
+// factor and one token chunk: lane l owns columns 2l, 2l + 1; warp w the
+// tokens n0 + w + 8 k, loaded eight at a time; the S rows of the chunk are
+// staged in shared memory. Warp sums are added in warp order, so
+// partial[chunk][col][q] (q < the factor's S width) is a fixed-order sum.
+constexpr int kWgChunks = 32;   // token chunks of a group's weight gradients
+constexpr int kWgMaxS = 16;
+constexpr int kWgMaxFactors = 2 * kLoraMaxSegs;
+
+struct WgFactor {
+  int big = 0;                 // 0: dY columns (dB), 1: X columns (dA)
+  int col_off = 0, C = 0;      // columns [col_off, col_off + C) of the big matrix
+  int n_src = 0;               // S = [src_0 | src_1 | ..], each [N][r]
+  const float* src[kLoraMaxSegs] = {nullptr, nullptr, nullptr};
+  float* dst[kLoraMaxSegs] = {nullptr, nullptr, nullptr};   // dB [C][r] or dA_a [r][C]
+  float alpha = 1.f;
+  int gbase = 0, cbase = 0;    // first 64-column group (blockIdx.x) / output column
+};
+struct WgPlan {
+  WgFactor f[kWgMaxFactors];
+  int nf = 0, groups = 0, ct = 0, r = 0;
 };
 
-template <int RT>
-__global__ void __launch_bounds__(WgradCfg<RT>::kWarps * 32)
-    lora_wgrad_group_kernel(Planes dY, long long ldy, Planes X, long long ldx, int d_in, int N, int r, float s,
-                            int chunk, LoraWgGroup g, WgLayout lay, float* __restrict__ part) {
+template <int RS>
+__global__ void __launch_bounds__(256) lora_wgrad2_kernel(Planes dY, long long ldy, Planes X, long long ldx, int N,
+                                                         int chunk, WgPlan p, float* __restrict__ part) {
   griddep_wait();
-  constexpr int WARPS = WgradCfg<RT>::kWarps;
-  extern __shared__ float ss[];   // [chunk][r] S rows, then [WARPS][64][RT] warp sums
-  float* red = ss + chunk * r;
-  int f = 0;
-  while (f + 1 < lay.nf && (int)blockIdx.x >= lay.gbase[f + 1]) ++f;
-  const LoraWgSeg& sg = g.s[f / 2];
-  const bool dB = (f & 1) == 0;
-  const Planes big = dB ? dY : X;
-  const long long ldb = dB ? ldy : ldx;
-  const int off = dB ? sg.col_off : 0;
-  const int C = dB ? sg.width : d_in;
-  const float* S = dB ? sg.u : sg.du;
-  const float alpha = dB ? s : 1.0f;
-  const int cb = ((int)blockIdx.x - lay.gbase[f]) * 64;
+  extern __shared__ float4 wss4[];
+  float* ss = reinterpret_cast<float*>(wss4);   // [chunk][RS] S rows
+  float* red = ss + chunk * RS;                 // [8 warps][RS][64] warp sums
+  int fi = 0;
+  while (fi + 1 < p.nf && (int)blockIdx.x >= p.f[fi + 1].gbase) ++fi;
+  const WgFactor& F = p.f[fi];
+  const int r = p.r, rs = F.n_src * r;
+  const Planes big = F.big ? X : dY;
+  const long long ldb = F.big ? ldx : ldy;
+  const int cb = ((int)blockIdx.x - F.gbase) * 64;
   const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
-  const int c = cb + lane * 2;
   const int n0 = blockIdx.y * chunk;
   const int n1 = min(N, n0 + chunk);
-  for (int i = threadIdx.x; i < (n1 - n0) * r; i += WARPS * 32) ss[i] = S[(long long)n0 * r + i];
+  const int stot = (n1 - n0) * RS;
+  for (int i0 = threadIdx.x; i0 < stot; i0 += 8 * 256) {   // eight loads in flight per thread
+    float t[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * 256, n = i / RS, q = i % RS;
+      t[u] = (i < stot && q < rs) ? F.src[q / r][(long long)(n0 + n) * r + q % r] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (i0 + u * 256 < stot) ss[i0 + u * 256] = t[u];
+  }
   __syncthreads();
-  float a0[RT], a1[RT];
+  const int c = cb + lane * 2;
+  float a0[RS], a1[RS];
 #pragma unroll
-  for (int j = 0; j < RT; ++j) a0[j] = a1[j] = 0.f;
-  if (c < C) {
-#pragma unroll 4
-    for (int n = n0 + warp; n < n1; n += WARPS) {
-      const float2 bv = load_planes2(big, (long long)n * ldb + off + c);
-      const float* sr = ss + (n - n0) * r;
+  for (int q = 0; q < RS; ++q) a0[q] = a1[q] = 0.f;
+  if (c < F.C) {
+    const long long col = F.col_off + c;
+    for (int nb = n0 + warp; nb < n1; nb += 64) {
+      float2 bv[8];
 #pragma unroll
-      for (int j = 0; j < RT; ++j) {
-        if (j < r) {
-          const float sv = sr[j];
-          a0[j] += bv.x * sv;
-          a1[j] += bv.y * sv;
+      for (int u = 0; u < 8; ++u) {
+        const int n = nb + 8 * u;
+        bv[u] = n < n1 ? load_planes2(big, (long long)n * ldb + col) : make_float2(0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int n = nb + 8 * u;
+        if (n < n1) {
+          const float4* sr = reinterpret_cast<const float4*>(ss + (n - n0) * RS);
+#pragma unroll
+          for (int q4 = 0; q4 < RS / 4; ++q4) {
+            const float4 sv = sr[q4];
+            a0[4 * q4] += bv[u].x * sv.x; a1[4 * q4] += bv[u].y * sv.x;
+            a0[4 * q4 + 1] += bv[u].x * sv.y; a1[4 * q4 + 1] += bv[u].y * sv.y;
+            a0[4 * q4 + 2] += bv[u].x * sv.z; a1[4 * q4 + 2] += bv[u].y * sv.z;
+            a0[4 * q4 + 3] += bv[u].x * sv.w; a1[4 * q4 + 3] += bv[u].y * sv.w;
+          }
         }
       }
     }
   }
 #pragma unroll
-  for (int j = 0; j < RT; ++j) {
-    red[(warp * 64 + lane * 2) * RT + j] = a0[j];
-    red[(warp * 64 + lane * 2 + 1) * RT + j] = a1[j];
-  }
+  for (int q = 0; q < RS; ++q)
+    *reinterpret_cast<float2*>(red + (warp * RS + q) * 64 + lane * 2) = make_float2(a0[q], a1[q]);
   __syncthreads();
-  const long long ct = lay.cbase[lay.nf];
-  for (int i = threadIdx.x; i < 64 * r; i += WARPS * 32) {
-    const int cc = i / r, j = i % r;
-    if (cb + cc >= C) continue;
+  for (int i = threadIdx.x; i < 64 * RS; i += 256) {
+    const int cc = i % 64, q = i / 64;
+    if (cb + cc >= F.C || q >= rs) continue;
     float sum = 0.f;
 #pragma unroll
-    for (int w2 = 0; w2 < WARPS; ++w2) sum += red[(w2 * 64 + cc) * RT + j];
-    part[((long long)blockIdx.y * ct + lay.cbase[f] + cb + cc) * r + j] = alpha * sum;
+    for (int w2 = 0; w2 < 8; ++w2) sum += red[(w2 * RS + q) * 64 + cc];
+    part[((long long)blockIdx.y * p.ct + F.cbase + cb + cc) * RS + q] = F.alpha * sum;
   }
 }
 
-__global__ void lora_group_reduce_kernel(const float* __restrict__ part, int nch, int r, int d_in, LoraWgGroup g,
-                                         WgLayout lay) {
+// Fixed-order sum of the chunk partials, scattered into dB / dA: four
+// consecutive lanes share an output, lane k summing chunks k, k + 4, .. in
+// order, and the four sums are added as (s0 + s1) + (s2 + s3).
+template <int RS>
+__global__ void lora_wgrad2_reduce_kernel(const float* __restrict__ part, int nch, WgPlan p) {
   griddep_wait();
-  const long long ct = lay.cbase[lay.nf];
-  const long long total = ct * r;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
+  const long long total = (long long)p.ct * RS;
+  const int sub = threadIdx.x & 3;
+  const long long span = (total + 7) / 8 * 8;   // whole warps stay in the shuffles
+  for (long long i0 = (blockIdx.x * (long long)blockDim.x + threadIdx.x) / 4; i0 < span;
+       i0 += (long long)gridDim.x * blockDim.x / 4) {
+    const long long i = i0 < total ? i0 : total - 1;
     float s = 0.f;
-    for (int b = 0; b < nch; ++b) s += part[(long long)b * total + i];
-    const int col = (int)(i / r), j = (int)(i % r);
-    int f = 0;
-    while (f + 1 < lay.nf && col >= lay.cbase[f + 1]) ++f;
-    const LoraWgSeg& sg = g.s[f / 2];
-    const int c = col - lay.cbase[f];
-    if ((f & 1) == 0) sg.dB[(long long)c * r + j] = s;
-    else sg.dA[(long long)j * d_in + c] = s;
+    int b = sub;
+    for (; b + 12 < nch; b += 16) {
+      float v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = part[(long long)(b + 4 * u) * total + i];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) s += v[u];
+    }
+    for (; b < nch; b += 4) s += part[(long long)b * total + i];
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    if (sub || i0 >= total) continue;
+    const int col = (int)(i / RS), q = (int)(i % RS);
+    int fi = 0;
+    while (fi + 1 < p.nf && col >= p.f[fi + 1].cbase) ++fi;
+    const WgFactor& F = p.f[fi];
+    const int r = p.r;
+    if (q >= F.n_src * r) continue;
+    const int cc = col - F.cbase;
+    if (!F.big) F.dst[0][(long long)cc * r + q] = s;
+    else F.dst[q / r][(long long)(q % r) * F.C + cc] = s;
   }
 }
 
@@ -769,30 +961,101 @@ int launch_lora_down_group(Planes X, long long ldx, int N, int r, const LoraSegs
   }
   const size_t smem = wfloats * sizeof(float);
   if (smem > 200 * 1024) return -1;
-  const int rc = r <= 8 ? down_group_ns<8>(X, ldx, N, r, segs, shared, smem, st)
-                        : down_group_ns<16>(X, ldx, N, r, segs, shared, smem, st);
+  // bulk-staged variant: 16-byte aligned rows, segments and w; its shared
+  // memory holds w plus kDownRows rows of the staged segments
+  bool bulk = ldx % 8 == 0 && (reinterpret_cast<uintptr_t>(X.hi) & 15) == 0 &&
+              (reinterpret_cast<uintptr_t>(X.lo) & 15) == 0;
+  size_t seg_elems = 0;
+  for (int a = 0; a < segs.n; ++a) {
+    const LoraSeg& sg = segs.s[a];
+    bulk = bulk && sg.col_off % 8 == 0 && sg.width % 8 == 0 && (reinterpret_cast<uintptr_t>(sg.w) & 15) == 0;
+    if (a == 0 || !shared) seg_elems += sg.width;
+  }
+  const size_t bsmem = 16 + smem + (size_t)kDownRows * seg_elems * 4;
+  int rc;
+  if (bulk && bsmem <= 200 * 1024)
+    rc = r <= 8 ? down_bulk_ns<8>(X, ldx, N, r, segs, shared, bsmem, st)
+                : down_bulk_ns<16>(X, ldx, N, r, segs, shared, bsmem, st);
+  else
+    rc = r <= 8 ? down_group_ns<8>(X, ldx, N, r, segs, shared, smem, st)
+                : down_group_ns<16>(X, ldx, N, r, segs, shared, smem, st);
   return rc ? -3 : 0;
 }
 
 namespace {
-WgLayout wg_layout(const LoraWgGroup& g, int d_in) {
-  WgLayout l;
-  l.nf = 2 * g.n;
-  l.gbase[0] = l.cbase[0] = 0;
-  for (int f = 0; f < l.nf; ++f) {
-    const int C = (f & 1) ? d_in : g.s[f / 2].width;
-    l.gbase[f + 1] = l.gbase[f] + (C + 63) / 64;
-    l.cbase[f + 1] = l.cbase[f] + C;
+// Token chunks of the group weight gradients: kWgChunks of them, each small
+// enough for its S rows (kWgMaxS wide) to stay within 64 KB.
+void wg_chunks(int N, int& nch, int& chunk) {
+  chunk = (N + kWgChunks - 1) / kWgChunks;
+  chunk = std::min(chunk, 64 * 1024 / (4 * kWgMaxS));
+  chunk = std::max(chunk, 1);
+  nch = (N + chunk - 1) / chunk;
+}
+
+WgPlan wg_plan(const LoraWgGroup& g, int d_in, int r, float s) {
+  WgPlan p;
+  p.r = r;
+  auto add = [&](const WgFactor& f0) {
+    WgFactor f = f0;
+    f.gbase = p.groups;
+    f.cbase = p.ct;
+    p.groups += (f.C + 63) / 64;
+    p.ct += f.C;
+    p.f[p.nf++] = f;
+  };
+  for (int a = 0; a < g.n; ++a) {
+    WgFactor f;
+    f.big = 0; f.col_off = g.s[a].col_off; f.C = g.s[a].width;
+    f.n_src = 1; f.src[0] = g.s[a].u; f.dst[0] = g.s[a].dB; f.alpha = s;
+    add(f);
   }
-  return l;
+  if (g.n * r <= kWgMaxS) {   // one pass over X for every adapter's dA
+    WgFactor f;
+    f.big = 1; f.col_off = 0; f.C = d_in; f.n_src = g.n; f.alpha = 1.f;
+    for (int a = 0; a < g.n; ++a) {
+      f.src[a] = g.s[a].du;
+      f.dst[a] = g.s[a].dA;
+    }
+    add(f);
+  } else {
+    for (int a = 0; a < g.n; ++a) {
+      WgFactor f;
+      f.big = 1; f.col_off = 0; f.C = d_in; f.n_src = 1; f.alpha = 1.f;
+      f.src[0] = g.s[a].du; f.dst[0] = g.s[a].dA;
+      add(f);
+    }
+  }
+  return p;
+}
+
+template <int RS>
+int wgrad2(Planes dY, long long ldy, Planes X, long long ldx, int N, const WgPlan& p, float* part, cudaStream_t st) {
+  int nch, chunk;
+  wg_chunks(N, nch, chunk);
+  auto* kern = lora_wgrad2_kernel<RS>;
+  const size_t smem = ((size_t)chunk * RS + (size_t)8 * RS * 64) * sizeof(float);
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024) != cudaSuccess) return -3;
+    attr = true;
+  }
+  if (launch_pdl(kern, dim3((unsigned)p.groups, (unsigned)nch), dim3(256), smem, st, dY, ldy, X, ldx, N, chunk, p,
+                 part))
+    return -3;
+  const long long total = (long long)p.ct * RS;
+  long long blocks = (4 * ((total + 7) / 8 * 8) + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  return launch_pdl(lora_wgrad2_reduce_kernel<RS>, dim3((unsigned)blocks), dim3(256), 0, st, (const float*)part, nch, p)
+             ? -3 : 0;
 }
 }  // namespace
 
 long long lora_group_partial_floats(int N, int r, int d_in, int total_width, int n_adapters) {
   if (r < 1 || r > 16 || N <= 0) return 0;
   int nch, chunk;
-  wgrad_chunks(N, r, nch, chunk);
-  return (long long)nch * ((long long)total_width + (long long)n_adapters * d_in) * r;
+  wg_chunks(N, nch, chunk);
+  const long long dcols = (long long)n_adapters * r <= kWgMaxS ? d_in : (long long)n_adapters * d_in;
+  return (long long)nch * ((long long)total_width + dcols) * kWgMaxS;
 }
 
 int launch_lora_wgrad_group(Planes dY, long long ldy, Planes X, long long ldx, int d_in, int N, int r, float s,
@@ -802,26 +1065,10 @@ int launch_lora_wgrad_group(Planes dY, long long ldy, Planes X, long long ldx, i
     const LoraWgSeg& sg = g.s[a];
     if (!sg.u || !sg.du || !sg.dB || !sg.dA || sg.width <= 0 || sg.width % 2 || sg.col_off % 2) return -1;
   }
-  const WgLayout lay = wg_layout(g, d_in);
-  int nch, chunk;
-  wgrad_chunks(N, r, nch, chunk);
-  int rc;
-  if (r <= 8) {
-    const size_t smem = ((size_t)chunk * r + (size_t)WgradCfg<8>::kWarps * 64 * 8) * sizeof(float);
-    rc = launch_pdl(lora_wgrad_group_kernel<8>, dim3((unsigned)lay.gbase[lay.nf], (unsigned)nch),
-                    dim3(WgradCfg<8>::kWarps * 32), smem, st, dY, ldy, X, ldx, d_in, N, r, s, chunk, g, lay, part);
-  } else {
-    const size_t smem = ((size_t)chunk * r + (size_t)WgradCfg<16>::kWarps * 64 * 16) * sizeof(float);
-    rc = launch_pdl(lora_wgrad_group_kernel<16>, dim3((unsigned)lay.gbase[lay.nf], (unsigned)nch),
-                    dim3(WgradCfg<16>::kWarps * 32), smem, st, dY, ldy, X, ldx, d_in, N, r, s, chunk, g, lay, part);
-  }
-  if (rc) return -3;
-  const long long total = (long long)lay.cbase[lay.nf] * r;
-  long long blocks = (total + 255) / 256;
-  if (blocks > 148 * 8) blocks = 148 * 8;
-  return launch_pdl(lora_group_reduce_kernel, dim3((unsigned)blocks), dim3(256), 0, st, (const float*)part, nch, r, d_in,
-                    g, lay)
-             ? -3 : 0;
+  const WgPlan p = wg_plan(g, d_in, r, s);
+  int rs_max = r;
+  for (int f = 0; f < p.nf; ++f) rs_max = std::max(rs_max, p.f[f].n_src * r);
+  return rs_max <= 8 ? wgrad2<8>(dY, ldy, X, ldx, N, p, part, st) : wgrad2<16>(dY, ldy, X, ldx, N, p, part, st);
 }
 
 int launch_lora_transpose(const float* W, int C, int r, float* Wt, cudaStream_t st) {

@@ -22,6 +22,7 @@ enum DeviceError : int {
   kErrWaitEmpty = 2,    // producer timed out waiting for the MMA to free a stage
   kErrWaitAccum = 3,    // epilogue timed out waiting for the accumulator
   kErrShape = 4,        // a launch was given an unsupported shape
+  kErrWaitBulk = 5,     // a bandwidth kernel timed out waiting for its bulk copies
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -79,6 +80,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   const bool ok = mbar_wait(bar, parity, err, code);
   return __all_sync(0xffffffffu, ok);
+}
+
+// Untiled bulk copy (no multicast) of `bytes` from global memory into this
+// CTA's shared memory, completing on bar's transaction count. Both addresses
+// 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
 }
 
 // Make this thread's generic-proxy shared-memory writes visible to the async
