@@ -119,7 +119,7 @@ LlamaEngine::LlamaEngine(const LlamaConfig& cfg, int device) : cfg_(cfg), device
 LlamaEngine::~LlamaEngine() {
   cudaSetDevice(device_);
   if (graph_) cudaGraphExecDestroy(graph_);
-  for (DeviceBuf* b : {&p32_, &phi_, &plo_, &g_, &m_, &v_, &q8_, &q8v_, &q8s_, &q8pl_, &ring_desc_})
+  for (DeviceBuf* b : {&p32_, &phi_, &plo_, &g_, &m_, &v_, &q8_, &q8v_, &q8s_, &q8pl_})
     if (b->p) cudaFree(b->p);
   for (auto& b : bufs_)
     if (b.p) cudaFree(b.p);
@@ -841,7 +841,7 @@ int LlamaEngine::dequant_layer(int l) {
   if (!q8_planes_) return 0;
   const int slot = l & 1;
   if (ring_layer_[slot] == l) return 0;
-  KL(launch_q8_0_ring(static_cast<const RingLayer*>(ring_desc_.p) + l, ring_chunks_, stream_));
+  KL(launch_q8_0_ring(ring_desc_[l], stream_));
   ring_layer_[slot] = l;
   return 0;
 }
@@ -885,8 +885,7 @@ int LlamaEngine::build_ring(long long qvoff) {
     L.chunks = chunk;
     if (chunk != ring_chunks_) return -1;
   }
-  CK(alloc(ring_desc_, host.size() * sizeof(RingLayer)));
-  CU(cudaMemcpy(ring_desc_.p, host.data(), host.size() * sizeof(RingLayer), cudaMemcpyHostToDevice));
+  ring_desc_ = std::move(host);
   return 0;
 }
 
@@ -1206,7 +1205,7 @@ int LlamaEngine::enqueue_backward() {
     CK(gemm(ge));
   }
   const Param& gf = P("output_norm.weight");
-  KL(launch_rmsnorm_bwd(x_[c.n_layers], dh_, P32(gf), nullptr, dx_, dxp_, gpart_, nblk, N, d, c.rms_eps, stream_));
+  KL(launch_rmsnorm_bwd(x_[c.n_layers], dh_, P32(gf), nullptr, dx_, dxp_, full ? gpart_ : nullptr, nblk, N, d, c.rms_eps, stream_));
   if (full) KL(launch_colsum(gpart_, nblk, d, G32(gf), 0, stream_));
   for (int l = c.n_layers - 1; l >= 0; --l) {
     const std::string pre = "blk." + std::to_string(l) + ".";
@@ -1258,7 +1257,7 @@ int LlamaEngine::enqueue_backward() {
     for (int i = 0; i < Gg.n && !gg_grp; ++i)
       CK(lora_backward(l, Gg.t[i], h2_[l], d, dgu_, 2 * ff, Gg.c0[i], Gg.w[i], dh_, nullptr));
     const Param& g2 = P(pre + "ffn_norm.weight");
-    KL(launch_rmsnorm_bwd(x1_[l], dh_, P32(g2), dx_, dx_, dxp_, gpart_, nblk, N, d, c.rms_eps, stream_));
+    KL(launch_rmsnorm_bwd(x1_[l], dh_, P32(g2), dx_, dx_, dxp_, full ? gpart_ : nullptr, nblk, N, d, c.rms_eps, stream_));
     if (full) KL(launch_colsum(gpart_, nblk, d, G32(g2), 0, stream_));
     // ---- attention output projection: dO (head-major f32), dWo
     Epilogue hm;
@@ -1347,7 +1346,7 @@ int LlamaEngine::enqueue_backward() {
     for (int i = 0; i < Gq.n && !gq_grp; ++i)
       CK(lora_backward(l, Gq.t[i], h1_[l], d, dqkv_, W, Gq.c0[i], Gq.w[i], dh_, nullptr));
     const Param& g1 = P(pre + "attn_norm.weight");
-    KL(launch_rmsnorm_bwd(x_[l], dh_, P32(g1), dx_, dx_, dxp_, gpart_, nblk, N, d, c.rms_eps, stream_));
+    KL(launch_rmsnorm_bwd(x_[l], dh_, P32(g1), dx_, dx_, dxp_, full ? gpart_ : nullptr, nblk, N, d, c.rms_eps, stream_));
     if (full) KL(launch_colsum(gpart_, nblk, d, G32(g1), 0, stream_));
     CK(bucket_ready(layer_grad_lo_[l], false));   // this layer's gradients are final
   }

@@ -199,13 +199,13 @@ class LlamaEngine {
   int ring_layer_[2] = {-1, -1};
   // ring operand of each adapter group: [d_out + ext][d_in + ext] planes at
   // element offset off of a slot's hi (and lo) half; the blocks' fill
-  // descriptors live in ring_desc_
+  // descriptors (passed with each fill launch) live in ring_desc_
   struct RingGroup {
     int d_out = 0, d_in = 0, ext = 0;
     long long off = 0;
   };
   RingGroup ring_[4];
-  DeviceBuf ring_desc_;
+  std::vector<RingLayer> ring_desc_;
   long long ring_chunks_ = 0;
   // extra reduction width of each group's base GEMMs (0, or 64 with the
   // group's adapters folded into the ring operand)

@@ -637,31 +637,39 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // dO planes (head-major) and D = rowsum(dO * O); one warp per (b, h, t) row.
+// Half a warp per (b, h, t) row of kDh = 64 values, four per lane: the dO
+// planes and D = rowsum(dO * O) (the four-lane sums are reduced in a fixed
+// butterfly order).
 __global__ void __launch_bounds__(256) flash_bwd_prep_kernel(const float* __restrict__ dO32, Planes O, Planes dO,
                                                              float* __restrict__ Dv, int B, int T, int H) {
   griddep_wait();
-  const int warps = blockDim.x / 32, lane = threadIdx.x % 32;
+  const int lane = threadIdx.x % 32, hl = lane % 16;
   const long long rows = (long long)B * H * T;
-  for (long long r = blockIdx.x * (long long)warps + threadIdx.x / 32; r < rows; r += (long long)gridDim.x * warps) {
+  const long long span = (rows + 1) / 2 * 2;   // both half-warps stay in the shuffles
+  for (long long r0 = (blockIdx.x * (long long)blockDim.x + threadIdx.x) / 16; r0 < span;
+       r0 += (long long)gridDim.x * blockDim.x / 16) {
+    const long long r = r0 < rows ? r0 : rows - 1;
     const int t = (int)(r % T);
     const long long bh = r / T;
     const int b = (int)(bh / H), h = (int)(bh % H);
-    const float2 g = reinterpret_cast<const float2*>(dO32 + r * kDh)[lane];
-    const long long oo = ((long long)(b * T + t) * H + h) * kDh + 2 * lane;
-    const float o0 = __bfloat162float(O.hi[oo]) + __bfloat162float(O.lo[oo]);
-    const float o1 = __bfloat162float(O.hi[oo + 1]) + __bfloat162float(O.lo[oo + 1]);
-    float d = g.x * o0 + g.y * o1;
+    const float4 g = reinterpret_cast<const float4*>(dO32 + r * kDh)[hl];
+    const long long oo = ((long long)(b * T + t) * H + h) * kDh + 4 * hl;
+    const uint2 oh = *reinterpret_cast<const uint2*>(O.hi + oo);
+    const uint2 ol = *reinterpret_cast<const uint2*>(O.lo + oo);
+    const float o0 = __uint_as_float(oh.x << 16) + __uint_as_float(ol.x << 16);
+    const float o1 = __uint_as_float(oh.x & 0xffff0000u) + __uint_as_float(ol.x & 0xffff0000u);
+    const float o2 = __uint_as_float(oh.y << 16) + __uint_as_float(ol.y << 16);
+    const float o3 = __uint_as_float(oh.y & 0xffff0000u) + __uint_as_float(ol.y & 0xffff0000u);
+    float d = g.x * o0 + g.y * o1 + g.z * o2 + g.w * o3;
 #pragma unroll
-    for (int s = 16; s; s >>= 1) d += __shfl_xor_sync(0xffffffffu, d, s);
-    const bf16 h0 = __float2bfloat16_rn(g.x), h1 = __float2bfloat16_rn(g.y);
-    __nv_bfloat162 hv, lv;
-    hv.x = h0;
-    hv.y = h1;
-    lv.x = __float2bfloat16_rn(g.x - __bfloat162float(h0));
-    lv.y = __float2bfloat16_rn(g.y - __bfloat162float(h1));
-    reinterpret_cast<__nv_bfloat162*>(dO.hi + r * kDh)[lane] = hv;
-    reinterpret_cast<__nv_bfloat162*>(dO.lo + r * kDh)[lane] = lv;
-    if (lane == 0) Dv[r] = d;
+    for (int s = 8; s; s >>= 1) d += __shfl_xor_sync(0xffffffffu, d, s);
+    if (r0 >= rows) continue;
+    uint32_t hv[2], lv[2];
+    split_pair(g.x, g.y, hv[0], lv[0]);
+    split_pair(g.z, g.w, hv[1], lv[1]);
+    *reinterpret_cast<uint2*>(dO.hi + r * kDh + 4 * hl) = make_uint2(hv[0], hv[1]);
+    *reinterpret_cast<uint2*>(dO.lo + r * kDh + 4 * hl) = make_uint2(lv[0], lv[1]);
+    if (hl == 0) Dv[r] = d;
   }
 }
 
@@ -714,7 +722,7 @@ int launch_flash_bwd_prep(const float* dO32, Planes O, Planes dO, float* Dvec, i
                           cudaStream_t st) {
   if (dh != kDh) return -1;
   const long long rows = (long long)B * H * T;
-  long long blocks = (rows + 7) / 8;
+  long long blocks = (rows + 15) / 16;
   if (blocks > 148 * 16) blocks = 148 * 16;
   return launch_pdl(flash_bwd_prep_kernel, dim3((unsigned)blocks), dim3(256), 0, st, dO32, O, dO, Dvec, B, T, H)
              ? -21 : 0;

@@ -175,20 +175,23 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restric
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int d4 = d / 4;
   float4* my = gacc4 + warp * d4;
-  for (int c = lane; c < d4; c += 32) my[c] = f4_zero();
+  if (gpart)
+    for (int c = lane; c < d4; c += 32) my[c] = f4_zero();
   __syncwarp();
   const float4* g4 = reinterpret_cast<const float4*>(gamma);
   for (int n = blockIdx.x * warps + warp; n < N; n += gridDim.x * warps) {
     const long long base = (long long)n * d;
     const float4* xr = reinterpret_cast<const float4*>(x + base);
     const float4* hr = reinterpret_cast<const float4*>(dh + base);
-    float4 xv[NC], hv[NC];
+    const float4* rres = dres ? reinterpret_cast<const float4*>(dres + base) : nullptr;
+    float4 xv[NC], hv[NC], rv[NC];
     float sxx = 0.f, sxdz = 0.f;
 #pragma unroll
-    for (int i = 0; i < NC; ++i) {
+    for (int i = 0; i < NC; ++i) {   // x, dh and the residual gradient in one round of loads
       const int c = lane + 32 * i;
       xv[i] = c < d4 ? xr[c] : f4_zero();
       hv[i] = c < d4 ? __ldcs(hr + c) : f4_zero();
+      rv[i] = (rres && c < d4) ? rres[c] : f4_zero();
       const float4 g = c < d4 ? g4[c] : f4_zero();
       sxx += xv[i].x * xv[i].x + xv[i].y * xv[i].y + xv[i].z * xv[i].z + xv[i].w * xv[i].w;
       sxdz += xv[i].x * hv[i].x * g.x + xv[i].y * hv[i].y * g.y + xv[i].z * hv[i].z * g.z + xv[i].w * hv[i].w * g.w;
@@ -197,14 +200,13 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restric
     sxdz = warp_sum(sxdz);
     const float rr = 1.0f / sqrtf(sxx / (float)d + eps);
     const float coef = sxdz / (sxx + (float)d * eps);
-    const float4* rres = dres ? reinterpret_cast<const float4*>(dres + base) : nullptr;
     float4* out = reinterpret_cast<float4*>(dx + base);
 #pragma unroll
     for (int i = 0; i < NC; ++i) {
       const int c = lane + 32 * i;
       if (c >= d4) continue;
       const float4 v = xv[i], gg = hv[i], g = g4[c];
-      const float4 rs = rres ? rres[c] : f4_zero();
+      const float4 rs = rv[i];
       float4 o;
       o.x = rs.x + (gg.x * g.x - v.x * coef) * rr;
       o.y = rs.y + (gg.y * g.y - v.y * coef) * rr;
@@ -212,14 +214,17 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restric
       o.w = rs.w + (gg.w * g.w - v.w * coef) * rr;
       out[c] = o;
       if (dxp.hi) store_planes4(dxp, base + c * 4, o);
-      float4 a = my[c];
-      a.x += gg.x * v.x * rr;
-      a.y += gg.y * v.y * rr;
-      a.z += gg.z * v.z * rr;
-      a.w += gg.w * v.w * rr;
-      my[c] = a;
+      if (gpart) {
+        float4 a = my[c];
+        a.x += gg.x * v.x * rr;
+        a.y += gg.y * v.y * rr;
+        a.z += gg.z * v.z * rr;
+        a.w += gg.w * v.w * rr;
+        my[c] = a;
+      }
     }
   }
+  if (!gpart) return;   // frozen gamma: no dgamma partials
   __syncthreads();
   for (int c = threadIdx.x; c < d4; c += blockDim.x) {
     float4 s = f4_zero();
@@ -741,59 +746,86 @@ __global__ void q8_0_to_planes_kernel(const uint8_t* __restrict__ q, Planes out,
   }
 }
 
-// One 16-value chunk of a ring matrix per thread iteration (layout in kernels.cuh).
-__global__ void __launch_bounds__(256) q8_0_ring_kernel(const RingLayer* __restrict__ L) {
+// Ring fill (layout in kernels.cuh): the block's descriptors come by value
+// (constant bank); each thread takes kRingPer 16-value chunks spaced a grid
+// apart, issuing every chunk's loads before converting and storing any.
+constexpr int kRingPer = 1;
+
+__device__ __forceinline__ void ring_chunk_loc(const RingLayer& L, long long i, int& k, int& row, int& col) {
+  k = 0;
+  while (k + 1 < L.n && i >= L.m[k + 1].chunk0) ++k;
+  const RingMat& M = L.m[k];
+  const int cpr = (M.d_in + M.ext) / 16;
+  const long long c = i - M.chunk0;
+  row = (int)(c / cpr);
+  col = (int)(c % cpr) * 16;
+}
+
+__global__ void __launch_bounds__(256) q8_0_ring_kernel(const __grid_constant__ RingLayer L) {
   griddep_wait();
-  const int nm = L->n;
-  const long long total = L->chunks;
+  const long long total = L.chunks;
   const long long stride = (long long)gridDim.x * blockDim.x;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += stride) {
-    int k = 0;
-    while (k + 1 < nm && i >= L->m[k + 1].chunk0) ++k;
-    const RingMat& M = L->m[k];
-    const int d_in = M.d_in, d_out = M.d_out, ld = d_in + M.ext;
-    const long long c = i - M.chunk0;
-    const int cpr = ld / 16;
-    const int row = (int)(c / cpr), col = (int)(c % cpr) * 16;
-    float v[16];
-    if (row < d_out && col < d_in) {
-      const long long e = (long long)row * d_in + col;
-      const int4 q = __ldg(reinterpret_cast<const int4*>(M.qv + e));
-      const float sc = __half2float(__ushort_as_half(__ldg(M.qs + e / 32)));
-      const int8_t* b = reinterpret_cast<const int8_t*>(&q);
+  for (long long i0 = blockIdx.x * (long long)blockDim.x + threadIdx.x; i0 < total; i0 += stride * kRingPer) {
+    int4 q[kRingPer];
+    float sc[kRingPer];
+    float4 av[kRingPer][4];
+    int kk[kRingPer], rr[kRingPer], cc[kRingPer];
 #pragma unroll
-      for (int t = 0; t < 16; ++t) v[t] = sc * (float)b[t];
-    } else if (row < d_out) {
-      const int a = (col - d_in) / 16;
-      const bool on = a < M.n_ad && row >= M.ad[a].c0 && row < M.ad[a].c0 + M.ad[a].width;
-      const float* br = on ? M.ad[a].B + (long long)(row - M.ad[a].c0) * M.r : nullptr;
+    for (int u = 0; u < kRingPer; ++u) {   // loads of every chunk first
+      const long long i = i0 + u * stride;
+      kk[u] = -1;
+      if (i >= total) continue;
+      ring_chunk_loc(L, i, kk[u], rr[u], cc[u]);
+      const RingMat& M = L.m[kk[u]];
+      if (rr[u] < M.d_out && cc[u] < M.d_in) {
+        const long long e = (long long)rr[u] * M.d_in + cc[u];
+        q[u] = __ldg(reinterpret_cast<const int4*>(M.qv + e));
+        sc[u] = __half2float(__ushort_as_half(__ldg(M.qs + e / 32)));
+      } else if (rr[u] >= M.d_out) {
+        const int t = rr[u] - M.d_out, a = t / 16, j = t % 16;
+        if (cc[u] < M.d_in && a < M.n_ad && j < M.r) {
+          const float4* src = reinterpret_cast<const float4*>(M.ad[a].A + (long long)j * M.d_in + cc[u]);
 #pragma unroll
-      for (int t = 0; t < 16; ++t) v[t] = (on && t < M.r) ? M.s * br[t] : 0.f;
-    } else {
-      const int rr = row - d_out, a = rr / 16, j = rr % 16;
-      const bool on = col < d_in && a < M.n_ad && j < M.r;
-      if (on) {
-        const float4* src = reinterpret_cast<const float4*>(M.ad[a].A + (long long)j * d_in + col);
+          for (int v = 0; v < 4; ++v) av[u][v] = __ldg(src + v);
+        } else {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float4 t4 = __ldg(src + u);
-          v[4 * u] = t4.x; v[4 * u + 1] = t4.y; v[4 * u + 2] = t4.z; v[4 * u + 3] = t4.w;
+          for (int v = 0; v < 4; ++v) av[u][v] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
-      } else {
-#pragma unroll
-        for (int t = 0; t < 16; ++t) v[t] = 0.f;
       }
     }
-    __align__(16) bf16 h[16], l[16];
 #pragma unroll
-    for (int t = 0; t < 16; ++t) split2(v[t], h[t], l[t]);
-    const long long o = (long long)row * ld + col;
-    uint4* ph = reinterpret_cast<uint4*>(M.hi + o);
-    uint4* pl = reinterpret_cast<uint4*>(M.lo + o);
-    ph[0] = reinterpret_cast<const uint4*>(h)[0];
-    ph[1] = reinterpret_cast<const uint4*>(h)[1];
-    pl[0] = reinterpret_cast<const uint4*>(l)[0];
-    pl[1] = reinterpret_cast<const uint4*>(l)[1];
+    for (int u = 0; u < kRingPer; ++u) {
+      if (kk[u] < 0) continue;
+      const RingMat& M = L.m[kk[u]];
+      const int row = rr[u], col = cc[u];
+      float v[16];
+      if (row < M.d_out && col < M.d_in) {
+        const int8_t* b = reinterpret_cast<const int8_t*>(&q[u]);
+#pragma unroll
+        for (int t = 0; t < 16; ++t) v[t] = sc[u] * (float)b[t];
+      } else if (row < M.d_out) {
+        const int a = (col - M.d_in) / 16;
+        const bool on = a < M.n_ad && row >= M.ad[a].c0 && row < M.ad[a].c0 + M.ad[a].width;
+        const float* br = on ? M.ad[a].B + (long long)(row - M.ad[a].c0) * M.r : nullptr;
+#pragma unroll
+        for (int t = 0; t < 16; ++t) v[t] = (on && t < M.r) ? M.s * br[t] : 0.f;
+      } else {
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          v[4 * w] = av[u][w].x; v[4 * w + 1] = av[u][w].y; v[4 * w + 2] = av[u][w].z; v[4 * w + 3] = av[u][w].w;
+        }
+      }
+      __align__(16) bf16 h[16], l[16];
+#pragma unroll
+      for (int t = 0; t < 16; ++t) split2(v[t], h[t], l[t]);
+      const long long o = (long long)row * (M.d_in + M.ext) + col;
+      uint4* ph = reinterpret_cast<uint4*>(M.hi + o);
+      uint4* pl = reinterpret_cast<uint4*>(M.lo + o);
+      ph[0] = reinterpret_cast<const uint4*>(h)[0];
+      ph[1] = reinterpret_cast<const uint4*>(h)[1];
+      pl[0] = reinterpret_cast<const uint4*>(l)[0];
+      pl[1] = reinterpret_cast<const uint4*>(l)[1];
+    }
   }
 }
 
@@ -1231,9 +1263,9 @@ int launch_q8_0_to_planes(const uint8_t* q, Planes out, float* f32, long long ro
   return ok();
 }
 
-int launch_q8_0_ring(const RingLayer* desc, long long chunks, cudaStream_t st) {
-  if (!desc || chunks <= 0) return -1;
-  launch_pdl(q8_0_ring_kernel, dim3(grid_for(chunks, 256)), dim3(256), 0, st, desc);
+int launch_q8_0_ring(const RingLayer& desc, cudaStream_t st) {
+  if (desc.chunks <= 0 || desc.n < 1 || desc.n > kRingMats) return -1;
+  launch_pdl(q8_0_ring_kernel, dim3(grid_for((desc.chunks + kRingPer - 1) / kRingPer, 256)), dim3(256), 0, st, desc);
   return ok();
 }
 

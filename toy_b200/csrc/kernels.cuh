@@ -33,7 +33,8 @@ int launch_rmsnorm_fwd(const float* x, const float* gamma, Planes h, int N, int 
                        long long ldh = 0);   // h rows ldh apart (0: d)
 
 // dx = dres + rms_norm_back(x, dh * gamma) (f32, may alias dres) and its planes;
-// per-block partial sums of dh * x * rrms into gpart[nblk][d] (for dgamma).
+// per-block partial sums of dh * x * rrms into gpart[nblk][d] (for dgamma;
+// none when gpart is null).
 struct LoraSegs;
 // launch_rmsnorm_fwd plus, in the same pass over each row, u_a = h A_a^T for
 // the adapters in g (all reading the whole row: col_off 0, width d; A_a [r][d];
@@ -133,9 +134,9 @@ struct RingLayer {
   int n = 0;
   long long chunks = 0;           // 16-value chunks of all n matrices
 };
-// Fills the matrices of one block; desc is a RingLayer in device memory whose
-// chunk count is `chunks`.
-int launch_q8_0_ring(const RingLayer* desc, long long chunks, cudaStream_t st);
+// Fills the matrices of one transformer block (the descriptors travel with
+// the launch).
+int launch_q8_0_ring(const RingLayer& desc, cudaStream_t st);
 // Q8_0 blocks -> the GEMM's quant layout: the 32 int8 quants of block b at
 // qv[32 b ..] and its fp16 scale bits at qs[b] (the same Q8_0 content, scales
 // split off so quant tiles are TMA-loadable).
