@@ -119,13 +119,15 @@ LlamaEngine::LlamaEngine(const LlamaConfig& cfg, int device) : cfg_(cfg), device
 LlamaEngine::~LlamaEngine() {
   cudaSetDevice(device_);
   if (graph_) cudaGraphExecDestroy(graph_);
-  for (DeviceBuf* b : {&p32_, &phi_, &plo_, &g_, &m_, &v_, &q8_, &q8v_, &q8s_, &q8pl_})
+  for (DeviceBuf* b : {&p32_, &phi_, &plo_, &g_, &m_, &v_, &q8_, &q8v_, &q8s_, &q8pl_, &wsc_ws_})
     if (b->p) cudaFree(b->p);
   for (auto& b : bufs_)
     if (b.p) cudaFree(b.p);
   if (stage_) cudaFreeHost(stage_);
   for (cudaEvent_t e : bucket_ev_) cudaEventDestroy(e);
   if (comm_stream_) cudaStreamDestroy(comm_stream_);
+  for (cudaEvent_t e : sev_) cudaEventDestroy(e);
+  if (wst_) cudaStreamDestroy(wst_);
   if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -162,7 +164,10 @@ int LlamaEngine::bucket_ready(long long lo, bool flush) {
     bucket_ev_.push_back(e);
   }
   cudaEvent_t e = bucket_ev_[bucket_next_++];
-  CU(cudaEventRecord(e, stream_));
+  // the range is final once both streams are past it: the side stream waits
+  // for the step stream, then marks the point
+  CK(fork_side());
+  CU(cudaEventRecord(e, side_ ? wst_ : stream_));
   CU(cudaStreamWaitEvent(comm_stream_, e, 0));
   comm_used_ = true;
   return allreduce_fn_(allreduce_ctx_, buf, n, comm_stream_);
@@ -220,6 +225,7 @@ int LlamaEngine::realize() {
   if (c.mode == 1 && (c.lora_rank <= 0 || c.lora_rank > kLoraMaxRank || c.lora_targets == 0)) return -1;
   CU(cudaSetDevice(device_));
   CU(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+  CU(cudaStreamCreateWithFlags(&wst_, cudaStreamNonBlocking));
   err_ = device_error_word();
   if (!err_) return -3;
   const bool full = c.mode == 0;
@@ -348,6 +354,11 @@ int LlamaEngine::realize() {
   }
 
   const int N = this->N(), T = c.T, B = c.B, W = (H + 2 * KV) * dh;
+  if (full) {   // split-K workspace of the weight-gradient GEMMs on wst_
+    wsc_.ws_floats = gemm_scratch().ws_floats;
+    CK(alloc(wsc_ws_, (size_t)wsc_.ws_floats * sizeof(float)));
+    wsc_.ws = static_cast<float*>(wsc_ws_.p);
+  }
   auto f32 = [&](long long n) -> float* {
     bufs_.emplace_back();
     if (alloc(bufs_.back(), n * 4)) return nullptr;
@@ -407,13 +418,19 @@ int LlamaEngine::realize() {
   dlog_ = pl((long long)N * V);
   lse_part_ = reinterpret_cast<float2*>(f32(2LL * ((V + 63) / 64) * N));
   lse_ms_ = reinterpret_cast<float2*>(f32(2LL * N));
-  dxp_ = pl((long long)N * d);
-  dgu_ = pl((long long)N * (2 * ff + ext_[kGroupGU]));
+  for (int k = 0; k < 2; ++k) {   // two copies of each transient the weight-gradient stream reads
+    dxp2_[k] = pl((long long)N * d);
+    dgu2_[k] = pl((long long)N * (2 * ff + ext_[kGroupGU]));
+    dqkv2_[k] = pl((long long)N * (W + ext_[kGroupQKV]));
+  }
+  dxp_ = dxp2_[0];
+  dgu_ = dgu2_[0];
+  dqkv_ = dqkv2_[0];
   dO_ = pl((long long)N * H * dh);
   if (!flash_) dS_ = pl(att);
-  dqkv_ = pl((long long)N * (W + ext_[kGroupQKV]));
   if (!full) {
-    du32_ = f32((long long)kLoraMaxSegs * N * r);   // du of each adapter of a group
+    for (int k = 0; k < 2; ++k) du2_[k] = f32((long long)kLoraMaxSegs * N * r);   // du of each adapter of a group
+    du32_ = du2_[0];
     long long part = std::max(lora_wgrad_partial_floats(N, std::max(std::max(d, ff), H * dh), r),
                               lora_bwd_partial_floats(N, std::max(ff, H * dh), d, r));
     if (r <= 16) {
@@ -423,6 +440,7 @@ int LlamaEngine::realize() {
       part = std::max(part, lora_group_partial_floats(N, r, ff, d, 1));            // down
     }
     lora_part_ = f32(part);
+    lora_part2_ = f32(part);
   }
   hp_ = f32(8);
   bufs_.emplace_back();
@@ -785,6 +803,62 @@ int LlamaEngine::gemm(const GemmDesc& d) {
   return rc;
 }
 
+int LlamaEngine::gemm_side(const GemmDesc& d) {
+  if (!side_ || !wsc_.ws) return gemm(d);
+  ++counting_;
+  const int rc = gemm_launch(d, wsc_.ws ? wsc_ : gemm_scratch(), err_, wst_);
+  if (rc) fprintf(stderr, "[toy_b200] gemm launch rejected (%d): M=%d N=%d K=%d batch=%d\n", rc, d.M, d.N, d.K, d.batch);
+  return rc;
+}
+
+cudaEvent_t LlamaEngine::next_event() {
+  if (sev_next_ == sev_.size()) {
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return nullptr;
+    sev_.push_back(e);
+  }
+  return sev_[sev_next_++];
+}
+
+int LlamaEngine::fork_side() {
+  if (!side_) return 0;
+  cudaEvent_t e = next_event();
+  if (!e) return -3;
+  CU(cudaEventRecord(e, stream_));
+  CU(cudaStreamWaitEvent(wst_, e, 0));
+  return 0;
+}
+
+int LlamaEngine::side_read2(Transient& a, Transient& b) {
+  if (!side_) return 0;
+  cudaEvent_t e = next_event();
+  if (!e) return -3;
+  CU(cudaEventRecord(e, wst_));
+  a.busy[a.cur] = e;
+  b.busy[b.cur] = e;
+  return 0;
+}
+
+int LlamaEngine::side_read(Transient& t) { return side_read2(t, t); }
+
+int LlamaEngine::flip(Transient& t) {
+  t.cur ^= 1;
+  if (t.busy[t.cur]) {
+    CU(cudaStreamWaitEvent(stream_, t.busy[t.cur], 0));
+    t.busy[t.cur] = nullptr;
+  }
+  return 0;
+}
+
+int LlamaEngine::join_side() {
+  if (!side_) return 0;
+  cudaEvent_t e = next_event();
+  if (!e) return -3;
+  CU(cudaEventRecord(e, wst_));
+  CU(cudaStreamWaitEvent(stream_, e, 0));
+  return 0;
+}
+
 namespace {
 int kind_of(const char* call) {
   static const struct { const char* prefix; int kind; } table[] = {
@@ -1004,6 +1078,8 @@ int LlamaEngine::lora_group_du(int l, const LoraGroup& G, Planes dY, long long l
                                 int ext_base) {
   const int N = this->N(), r = cfg_.lora_rank;
   const float s = cfg_.lora_alpha / (float)r;
+  CK(flip(t_du_));
+  du32_ = du2_[t_du_.cur];
   LoraSegs segs;
   for (int i = 0; i < G.n; ++i) {
     LoraSeg& sg = segs.s[segs.n++];
@@ -1042,7 +1118,7 @@ int LlamaEngine::lora_group_wgrad(int l, const LoraGroup& G, Planes X, long long
     sg.dB = G32(P(pre + ".lora_b"));
     sg.dA = G32(P(pre + ".lora_a"));
   }
-  KL(launch_lora_wgrad_group(dY, ld_dy, X, ldx, d_in, N, r, s, g, lora_part_, stream_));
+  KL(launch_lora_wgrad_group(dY, ld_dy, X, ldx, d_in, N, r, s, g, side_ ? lora_part2_ : lora_part_, sst()));
   return 0;
 }
 
@@ -1189,6 +1265,10 @@ int LlamaEngine::enqueue_backward() {
   const int nblk = rmsnorm_bwd_blocks();
   const Param& E = P("token_embd.weight");
   const Param& Wout = c.tied ? E : P("output.weight");
+  side_ = wst_ && !profiling_;
+  sev_next_ = 0;
+  t_dxp_ = t_dgu_ = t_dqkv_ = t_du_ = Transient{};
+  dxp_ = dxp2_[0]; dgu_ = dgu2_[0]; dqkv_ = dqkv2_[0]; du32_ = du2_[0];
   // dxf = dlogits W_out   ([N][V] x [V][d])
   GemmDesc g;
   g.M = N; g.N = d; g.K = V;
@@ -1202,9 +1282,12 @@ int LlamaEngine::enqueue_backward() {
     ge.a = op(dlog_, N, V, V, 1);
     ge.b = op(xf_, N, d, d, 1);
     ge.epi = epi_rowmajor(kEpiStoreF32, G32(Wout), d);
-    CK(gemm(ge));
+    CK(fork_side());
+    CK(gemm_side(ge));
   }
   const Param& gf = P("output_norm.weight");
+  CK(flip(t_dxp_));
+  dxp_ = dxp2_[t_dxp_.cur];
   KL(launch_rmsnorm_bwd(x_[c.n_layers], dh_, P32(gf), nullptr, dx_, dxp_, full ? gpart_ : nullptr, nblk, N, d, c.rms_eps, stream_));
   if (full) KL(launch_colsum(gpart_, nblk, d, G32(gf), 0, stream_));
   for (int l = c.n_layers - 1; l >= 0; --l) {
@@ -1224,17 +1307,23 @@ int LlamaEngine::enqueue_backward() {
     const bool gd_grp = Gd.n && lora_grouped(ff);
     if (gd_grp) CK(lora_group_du(l, Gd, dxp_, d, ff, gda.epi, -1));
     CK(gemm(gda));
-    if (gd_grp) CK(lora_group_wgrad(l, Gd, a_[l], ff, ff, dxp_, d));
-    if (full) {
-      GemmDesc gw;
-      gw.M = d; gw.N = ff; gw.K = N;
-      gw.a = op(dxp_, N, d, d, 1);
-      gw.b = op(a_[l], N, ff, ff, 1);
-      gw.epi = epi_rowmajor(kEpiStoreF32, G32(Wd), ff);
-      CK(gemm(gw));
+    if (gd_grp || full) {   // weight gradients of the down projection, on the side stream
+      CK(fork_side());
+      if (gd_grp) CK(lora_group_wgrad(l, Gd, a_[l], ff, ff, dxp_, d));
+      if (full) {
+        GemmDesc gw;
+        gw.M = d; gw.N = ff; gw.K = N;
+        gw.a = op(dxp_, N, d, d, 1);
+        gw.b = op(a_[l], N, ff, ff, 1);
+        gw.epi = epi_rowmajor(kEpiStoreF32, G32(Wd), ff);
+        CK(gemm_side(gw));
+      }
+      CK(side_read2(t_dxp_, t_du_));
     }
     if (Gd.n && !gd_grp) CK(lora_backward(l, kLoraDown, a_[l], ff, dxp_, d, 0, d, da_, nullptr));
     const int eg = ext_[kGroupGU];   // dgu carries du of the gate|up adapters in its extra columns
+    CK(flip(t_dgu_));
+    dgu_ = dgu2_[t_dgu_.cur];
     KL(launch_swiglu_bwd(gu_[l], da_, dgu_, N, ff, stream_, 2 * ff + eg));
     GemmDesc gh;
     gh.M = N; gh.N = d; gh.K = 2 * ff + eg;
@@ -1245,18 +1334,24 @@ int LlamaEngine::enqueue_backward() {
     const bool gg_grp = Gg.n && lora_grouped(d);
     if (gg_grp) CK(lora_group_du(l, Gg, dgu_, 2 * ff + eg, d, gh.epi, eg ? 2 * ff : -1));
     CK(gemm(gh));
-    if (gg_grp) CK(lora_group_wgrad(l, Gg, h2_[l], d + eg, d, dgu_, 2 * ff + eg));
-    if (full) {
-      GemmDesc gw;
-      gw.M = 2 * ff; gw.N = d; gw.K = N;
-      gw.a = op(dgu_, N, 2 * ff, 2 * ff, 1);
-      gw.b = op(h2_[l], N, d, d, 1);
-      gw.epi = epi_rowmajor(kEpiStoreF32, G32(Wg), d);
-      CK(gemm(gw));
+    if (gg_grp || full) {
+      CK(fork_side());
+      if (gg_grp) CK(lora_group_wgrad(l, Gg, h2_[l], d + eg, d, dgu_, 2 * ff + eg));
+      if (full) {
+        GemmDesc gw;
+        gw.M = 2 * ff; gw.N = d; gw.K = N;
+        gw.a = op(dgu_, N, 2 * ff, 2 * ff + eg, 1);
+        gw.b = op(h2_[l], N, d, d, 1);
+        gw.epi = epi_rowmajor(kEpiStoreF32, G32(Wg), d);
+        CK(gemm_side(gw));
+      }
+      CK(side_read2(t_dgu_, t_du_));
     }
     for (int i = 0; i < Gg.n && !gg_grp; ++i)
       CK(lora_backward(l, Gg.t[i], h2_[l], d, dgu_, 2 * ff, Gg.c0[i], Gg.w[i], dh_, nullptr));
     const Param& g2 = P(pre + "ffn_norm.weight");
+    CK(flip(t_dxp_));
+    dxp_ = dxp2_[t_dxp_.cur];
     KL(launch_rmsnorm_bwd(x1_[l], dh_, P32(g2), dx_, dx_, dxp_, full ? gpart_ : nullptr, nblk, N, d, c.rms_eps, stream_));
     if (full) KL(launch_colsum(gpart_, nblk, d, G32(g2), 0, stream_));
     // ---- attention output projection: dO (head-major f32), dWo
@@ -1272,16 +1367,22 @@ int LlamaEngine::enqueue_backward() {
     const bool go_grp = Go.n && lora_grouped(H * dh);
     if (go_grp) CK(lora_group_du(l, Go, dxp_, d, H * dh, gdo.epi, -1));
     CK(gemm(gdo));
-    if (go_grp) CK(lora_group_wgrad(l, Go, O_[l], H * dh, H * dh, dxp_, d));
-    if (full) {
-      GemmDesc gw;
-      gw.M = d; gw.N = H * dh; gw.K = N;
-      gw.a = op(dxp_, N, d, d, 1);
-      gw.b = op(O_[l], N, H * dh, H * dh, 1);
-      gw.epi = epi_rowmajor(kEpiStoreF32, G32(Wo), H * dh);
-      CK(gemm(gw));
+    if (go_grp || full) {
+      CK(fork_side());
+      if (go_grp) CK(lora_group_wgrad(l, Go, O_[l], H * dh, H * dh, dxp_, d));
+      if (full) {
+        GemmDesc gw;
+        gw.M = d; gw.N = H * dh; gw.K = N;
+        gw.a = op(dxp_, N, d, d, 1);
+        gw.b = op(O_[l], N, H * dh, H * dh, 1);
+        gw.epi = epi_rowmajor(kEpiStoreF32, G32(Wo), H * dh);
+        CK(gemm_side(gw));
+      }
+      CK(side_read2(t_dxp_, t_du_));
     }
     if (Go.n && !go_grp) CK(lora_backward(l, kLoraO, O_[l], H * dh, dxp_, d, 0, d, dO32_, &hm));
+    CK(flip(t_dqkv_));   // written by the RoPE backward below
+    dqkv_ = dqkv2_[t_dqkv_.cur];
     if (flash_) {
       // ---- attention core, fused: partial dQ / dK / dV summed by the RoPE backward
       KL(launch_flash_bwd_prep(dO32_, O_[l], dO_, dvec_, B, T, H, dh, stream_));
@@ -1334,25 +1435,33 @@ int LlamaEngine::enqueue_backward() {
     const bool gq_grp = Gq.n && lora_grouped(d);
     if (gq_grp) CK(lora_group_du(l, Gq, dqkv_, W + eq, d, gx.epi, eq ? W : -1));
     CK(gemm(gx));
-    if (gq_grp) CK(lora_group_wgrad(l, Gq, h1_[l], d + eq, d, dqkv_, W + eq));
-    if (full) {
-      GemmDesc gw;
-      gw.M = W; gw.N = d; gw.K = N;
-      gw.a = op(dqkv_, N, W, W, 1);
-      gw.b = op(h1_[l], N, d, d, 1);
-      gw.epi = epi_rowmajor(kEpiStoreF32, G32(Wq), d);
-      CK(gemm(gw));
+    if (gq_grp || full) {
+      CK(fork_side());
+      if (gq_grp) CK(lora_group_wgrad(l, Gq, h1_[l], d + eq, d, dqkv_, W + eq));
+      if (full) {
+        GemmDesc gw;
+        gw.M = W; gw.N = d; gw.K = N;
+        gw.a = op(dqkv_, N, W, W + eq, 1);
+        gw.b = op(h1_[l], N, d, d, 1);
+        gw.epi = epi_rowmajor(kEpiStoreF32, G32(Wq), d);
+        CK(gemm_side(gw));
+      }
+      CK(side_read2(t_dqkv_, t_du_));
     }
     for (int i = 0; i < Gq.n && !gq_grp; ++i)
       CK(lora_backward(l, Gq.t[i], h1_[l], d, dqkv_, W, Gq.c0[i], Gq.w[i], dh_, nullptr));
     const Param& g1 = P(pre + "attn_norm.weight");
+    CK(flip(t_dxp_));
+    dxp_ = dxp2_[t_dxp_.cur];
     KL(launch_rmsnorm_bwd(x_[l], dh_, P32(g1), dx_, dx_, dxp_, full ? gpart_ : nullptr, nblk, N, d, c.rms_eps, stream_));
     if (full) KL(launch_colsum(gpart_, nblk, d, G32(g1), 0, stream_));
     CK(bucket_ready(layer_grad_lo_[l], false));   // this layer's gradients are final
   }
+  CK(join_side());   // the embedding scatter adds to the LM head's (tied) gradient
   if (full) KL(launch_embed_scatter(dx_, ord_, seg_start_, seg_id_, nseg_dev_, N, G32(E), d, stream_));
   CK(bucket_ready(0, true));
   CK(bucket_join());
+  side_ = false;
   return 0;
 }
 

@@ -138,6 +138,25 @@ class LlamaEngine {
   int enqueue_optimizer();
   int enqueue_step(bool run_optimizer);
   int gemm(const GemmDesc& d);
+  // Weight gradients (dW GEMMs, adapter dA / dB) feed only the optimiser, so
+  // the backward runs them on a second stream, side by side with the chain of
+  // activation gradients: wst_ forks from the step stream after their inputs
+  // are written and joins it before the optimiser. The transients they read
+  // (dY planes, du) alternate between two copies; before the step stream
+  // writes a copy again it waits for that copy's last side reader. A profiled
+  // step keeps everything on the step stream.
+  struct Transient {
+    int cur = 0;
+    cudaEvent_t busy[2] = {nullptr, nullptr};
+  };
+  int gemm_side(const GemmDesc& d);
+  cudaStream_t sst() const { return side_ ? wst_ : stream_; }
+  cudaEvent_t next_event();
+  int fork_side();                        // wst_ waits for the step stream so far
+  int side_read(Transient& t);            // the copy in use is read by the side work enqueued so far
+  int side_read2(Transient& a, Transient& b);
+  int flip(Transient& t);                 // switch copies, waiting for the new one's side readers
+  int join_side();                        // the step stream waits for wst_
   int lora_forward(int l, int t, float* Y, long long ldy, int col_off, int d_out);
   int lora_prep(int l, int t, Planes X, int d_in, int d_out);
   LoraAddend lora_addend(int l, int t, int c0, int d_out) const;
@@ -211,6 +230,17 @@ class LlamaEngine {
   // group's adapters folded into the ring operand)
   int ext_[4] = {0, 0, 0, 0};
   int build_ring(long long qvoff);
+  // the weight-gradient stream and its state (see Transient)
+  cudaStream_t wst_ = nullptr;
+  GemmScratch wsc_;
+  DeviceBuf wsc_ws_;
+  bool side_ = false;
+  std::vector<cudaEvent_t> sev_;
+  size_t sev_next_ = 0;
+  Transient t_dxp_, t_dgu_, t_dqkv_, t_du_;
+  Planes dxp2_[2], dgu2_[2], dqkv2_[2];
+  float* du2_[2] = {nullptr, nullptr};
+  float* lora_part2_ = nullptr;   // the side stream's weight-gradient partials
   // activations and scratch
   std::vector<DeviceBuf> bufs_;
   std::vector<float*> x_, x1_, gu_;
