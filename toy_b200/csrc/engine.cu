@@ -413,7 +413,8 @@ int LlamaEngine::realize() {
     dvec_ = f32((long long)B * H * T);
     fws_ = f32(flash_bwd_ws_floats(B, T, H, KV, dh));
   }
-  gpart_ = f32((long long)rmsnorm_bwd_blocks() * d);
+  for (int k = 0; k < 2; ++k) gpart2_[k] = f32((long long)rmsnorm_bwd_blocks() * d);
+  gpart_ = gpart2_[0];
   xf_ = pl((long long)N * d);
   dlog_ = pl((long long)N * V);
   lse_part_ = reinterpret_cast<float2*>(f32(2LL * ((V + 63) / 64) * N));
@@ -826,6 +827,7 @@ int LlamaEngine::fork_side() {
   if (!e) return -3;
   CU(cudaEventRecord(e, stream_));
   CU(cudaStreamWaitEvent(wst_, e, 0));
+  side_forked_ = true;
   return 0;
 }
 
@@ -851,7 +853,8 @@ int LlamaEngine::flip(Transient& t) {
 }
 
 int LlamaEngine::join_side() {
-  if (!side_) return 0;
+  if (!side_ || !side_forked_) return 0;
+  side_forked_ = false;
   cudaEvent_t e = next_event();
   if (!e) return -3;
   CU(cudaEventRecord(e, wst_));
@@ -914,9 +917,48 @@ LoraAddend LlamaEngine::lora_addend(int l, int t, int c0, int d_out) const {
 int LlamaEngine::dequant_layer(int l) {
   if (!q8_planes_) return 0;
   const int slot = l & 1;
+  if (ring_layer_[slot] != l) {
+    KL(launch_q8_0_ring(ring_desc_[l], stream_));
+    ring_layer_[slot] = l;
+  }
+  if (ring_ev_[slot]) {   // filled ahead on wst_
+    CU(cudaStreamWaitEvent(stream_, ring_ev_[slot], 0));
+    ring_ev_[slot] = nullptr;
+  }
+  return 0;
+}
+
+int LlamaEngine::fill_ahead(int l) {
+  if (!q8_planes_ || !side_ || l < 0 || l >= cfg_.n_layers) return 0;
+  const int slot = l & 1;
   if (ring_layer_[slot] == l) return 0;
-  KL(launch_q8_0_ring(ring_desc_[l], stream_));
+  CK(fork_side());   // the slot's previous block has been enqueued on the step stream
+  KL(launch_q8_0_ring(ring_desc_[l], wst_));
+  cudaEvent_t e = next_event();
+  if (!e) return -3;
+  CU(cudaEventRecord(e, wst_));
+  ring_ev_[slot] = e;
   ring_layer_[slot] = l;
+  return 0;
+}
+
+int LlamaEngine::norm_bwd(const float* x, const float* gamma, const float* dres, const Param& gp) {
+  const LlamaConfig& c = cfg_;
+  const bool trainable = gp.trainable;
+  CK(flip(t_dxp_));
+  dxp_ = dxp2_[t_dxp_.cur];
+  if (trainable) {
+    CK(flip(t_gpart_));
+    gpart_ = gpart2_[t_gpart_.cur];
+  }
+  const int nblk = rmsnorm_bwd_blocks();
+  KL(launch_rmsnorm_bwd(x, dh_, gamma, dres, dx_, dxp_, trainable ? gpart_ : nullptr, nblk, N(), c.d_model, c.rms_eps,
+                        stream_));
+  if (trainable) {   // dgamma: a weight gradient, on the side stream
+    CK(fork_side());
+    KL(launch_colsum(gpart_, nblk, c.d_model, G32(gp), 0, sst()));
+    CK(side_read(t_gpart_));
+  }
   return 0;
 }
 
@@ -1129,11 +1171,16 @@ int LlamaEngine::enqueue_forward() {
   const float scale = 1.0f / std::sqrt((float)dh);
   const bool lora = c.mode == 1;
   const Param& E = P("token_embd.weight");
-  KL(launch_embed_gather(P32(E), ids_, x_[0], N, d, stream_));
+  side_ = wst_ && !profiling_;   // the forward's side work: ring fills one block ahead
+  side_forked_ = false;
+  sev_next_ = 0;
   ring_layer_[0] = ring_layer_[1] = -1;
+  ring_ev_[0] = ring_ev_[1] = nullptr;
+  KL(launch_embed_gather(P32(E), ids_, x_[0], N, d, stream_));
   for (int l = 0; l < c.n_layers; ++l) {
     const std::string pre = "blk." + std::to_string(l) + ".";
     CK(dequant_layer(l));
+    CK(fill_ahead(l + 1));
     const LoraGroup Gq = lora_group(kGroupQKV);
     const int eq = ext_[kGroupQKV];   // q|k|v adapters folded into the GEMM as extra reduction columns
     CK(rmsnorm_lora(l, x_[l], P32(P(pre + "attn_norm.weight")), h1_[l], Gq, d + eq));   // + the adapters' u
@@ -1234,6 +1281,8 @@ int LlamaEngine::enqueue_forward() {
     }
     CK(gemm(gd));
   }
+  CK(join_side());
+  side_ = false;
   KL(launch_rmsnorm_fwd(x_[c.n_layers], P32(P("output_norm.weight")), xf_, N, d, c.rms_eps, stream_));
   const Param& Wout = c.tied ? E : P("output.weight");
   GemmDesc gl;
@@ -1262,12 +1311,11 @@ int LlamaEngine::enqueue_backward() {
   const int W = (H + 2 * KV) * dh, G = H / KV, V = c.vocab;
   const float scale = 1.0f / std::sqrt((float)dh);
   const bool full = c.mode == 0, lora = c.mode == 1;
-  const int nblk = rmsnorm_bwd_blocks();
   const Param& E = P("token_embd.weight");
   const Param& Wout = c.tied ? E : P("output.weight");
   side_ = wst_ && !profiling_;
-  sev_next_ = 0;
-  t_dxp_ = t_dgu_ = t_dqkv_ = t_du_ = Transient{};
+  side_forked_ = false;
+  t_dxp_ = t_dgu_ = t_dqkv_ = t_du_ = t_gpart_ = Transient{};
   dxp_ = dxp2_[0]; dgu_ = dgu2_[0]; dqkv_ = dqkv2_[0]; du32_ = du2_[0];
   // dxf = dlogits W_out   ([N][V] x [V][d])
   GemmDesc g;
@@ -1286,13 +1334,11 @@ int LlamaEngine::enqueue_backward() {
     CK(gemm_side(ge));
   }
   const Param& gf = P("output_norm.weight");
-  CK(flip(t_dxp_));
-  dxp_ = dxp2_[t_dxp_.cur];
-  KL(launch_rmsnorm_bwd(x_[c.n_layers], dh_, P32(gf), nullptr, dx_, dxp_, full ? gpart_ : nullptr, nblk, N, d, c.rms_eps, stream_));
-  if (full) KL(launch_colsum(gpart_, nblk, d, G32(gf), 0, stream_));
+  CK(norm_bwd(x_[c.n_layers], P32(gf), nullptr, gf));
   for (int l = c.n_layers - 1; l >= 0; --l) {
     const std::string pre = "blk." + std::to_string(l) + ".";
     CK(dequant_layer(l));   // the forward's last two blocks are still in the ring
+    CK(fill_ahead(l - 1));
     const Param& Wd = P(pre + "ffn_down.weight");
     const Param& Wg = P(pre + "ffn_gate.weight");
     const Param& Wo = P(pre + "attn_output.weight");
@@ -1350,10 +1396,7 @@ int LlamaEngine::enqueue_backward() {
     for (int i = 0; i < Gg.n && !gg_grp; ++i)
       CK(lora_backward(l, Gg.t[i], h2_[l], d, dgu_, 2 * ff, Gg.c0[i], Gg.w[i], dh_, nullptr));
     const Param& g2 = P(pre + "ffn_norm.weight");
-    CK(flip(t_dxp_));
-    dxp_ = dxp2_[t_dxp_.cur];
-    KL(launch_rmsnorm_bwd(x1_[l], dh_, P32(g2), dx_, dx_, dxp_, full ? gpart_ : nullptr, nblk, N, d, c.rms_eps, stream_));
-    if (full) KL(launch_colsum(gpart_, nblk, d, G32(g2), 0, stream_));
+    CK(norm_bwd(x1_[l], P32(g2), dx_, g2));
     // ---- attention output projection: dO (head-major f32), dWo
     Epilogue hm;
     hm.mode = kEpiStoreF32; hm.out = dO32_;
@@ -1451,10 +1494,7 @@ int LlamaEngine::enqueue_backward() {
     for (int i = 0; i < Gq.n && !gq_grp; ++i)
       CK(lora_backward(l, Gq.t[i], h1_[l], d, dqkv_, W, Gq.c0[i], Gq.w[i], dh_, nullptr));
     const Param& g1 = P(pre + "attn_norm.weight");
-    CK(flip(t_dxp_));
-    dxp_ = dxp2_[t_dxp_.cur];
-    KL(launch_rmsnorm_bwd(x_[l], dh_, P32(g1), dx_, dx_, dxp_, full ? gpart_ : nullptr, nblk, N, d, c.rms_eps, stream_));
-    if (full) KL(launch_colsum(gpart_, nblk, d, G32(g1), 0, stream_));
+    CK(norm_bwd(x_[l], P32(g1), dx_, g1));
     CK(bucket_ready(layer_grad_lo_[l], false));   // this layer's gradients are final
   }
   CK(join_side());   // the embedding scatter adds to the LM head's (tied) gradient

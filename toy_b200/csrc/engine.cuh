@@ -235,10 +235,18 @@ class LlamaEngine {
   GemmScratch wsc_;
   DeviceBuf wsc_ws_;
   bool side_ = false;
+  bool side_forked_ = false;   // wst_ has work of this program still to join
   std::vector<cudaEvent_t> sev_;
   size_t sev_next_ = 0;
-  Transient t_dxp_, t_dgu_, t_dqkv_, t_du_;
+  Transient t_dxp_, t_dgu_, t_dqkv_, t_du_, t_gpart_;
   Planes dxp2_[2], dgu2_[2], dqkv2_[2];
+  float* gpart2_[2] = {nullptr, nullptr};
+  cudaEvent_t ring_ev_[2] = {nullptr, nullptr};   // a fill of the slot still running on wst_
+  // ring slot (l % 2) := block l on wst_, one block ahead of its use (the
+  // slot's previous block is done on the step stream); dequant_layer waits
+  int fill_ahead(int l);
+  // RMSNorm backward into dx / dxp; for a trainable gamma its column sum on wst_
+  int norm_bwd(const float* x, const float* gamma, const float* dres, const Param& gp);
   float* du2_[2] = {nullptr, nullptr};
   float* lora_part2_ = nullptr;   // the side stream's weight-gradient partials
   // activations and scratch

@@ -4,6 +4,8 @@
 #include "kernels.cuh"
 #include "lora.cuh"
 #include "pdl.cuh"
+#include "runtime.cuh"
+#include "tc_common.cuh"
 #include "warp_reduce.cuh"
 
 #include <cuda_fp16.h>
@@ -921,33 +923,34 @@ int dispatch_nc(int nc, A... a) {
 
 // rmsnorm_fwd fused with the low-rank down-projections of the adapters that
 // read its output row: u_a[n][j] = sum_k h[n][k] A_a[j][k] for each adapter a
-// (A_a [r][d] staged in shared memory once per block), plus the B^T copies the
-// splice reads. A warp normalises RW rows at a time, so each A value read from
+// (A_a [r][d] brought into shared memory once per block by bulk copies that
+// land while the warps load and normalise their first rows), plus the B^T
+// copies the splice reads. A warp normalises RW rows at a time, so each A value read from
 // shared memory serves RW rows; the r sums of an adapter are reduced across the
 // warp with warp_sum_multi. With ext_col >= 0, u_a is also written as planes
 // into h's columns ext_col + j.
 template <int NC, int RT, int NS, int RW>
 __global__ void __launch_bounds__(256) rmsnorm_fwd_lora_kernel(const float* __restrict__ x,
                                                                const float* __restrict__ gamma, Planes h, long long ldh,
-                                                               int N, int d, float eps, int r, LoraSegs g) {
+                                                               int N, int d, float eps, int r, LoraSegs g, int* err) {
+  extern __shared__ __align__(128) float4 asm4[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(asm4);   // bytes 0..15
+  float* as = reinterpret_cast<float*>(asm4 + 1);      // NS x [r][d]
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
   griddep_wait();
-  extern __shared__ float4 asm4[];
-  float* as = reinterpret_cast<float*>(asm4);   // NS x [r][d]
-  const int n4 = r * d / 4;
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(bar, (uint32_t)(NS * r * d * 4));
+#pragma unroll
+    for (int a = 0; a < NS; ++a) bulk_load(as + a * r * d, g.s[a].w, (uint32_t)(r * d * 4), bar);
+  }
+  bool a_ready = false;
 #pragma unroll
   for (int a = 0; a < NS; ++a) {
     const LoraSeg& sg = g.s[a];
-    const float4* src = reinterpret_cast<const float4*>(sg.w);
-    float4* dst = asm4 + a * n4;
-    for (int i0 = threadIdx.x; i0 < n4; i0 += 4 * 256) {   // four loads in flight per thread
-      float4 t[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        if (i0 + u * 256 < n4) t[u] = __ldg(src + i0 + u * 256);
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        if (i0 + u * 256 < n4) dst[i0 + u * 256] = t[u];
-    }
     if (sg.bt) {
       for (long long i = blockIdx.x * 256LL + threadIdx.x; i < (long long)sg.b_rows * r;
            i += (long long)gridDim.x * 256) {
@@ -992,6 +995,10 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_lora_kernel(const float* __re
           if (n < N) store_planes4(h, (long long)n * ldh + c * 4, y[q][i]);
         }
       }
+    }
+    if (!a_ready) {   // the adapters' A have landed
+      if (!mbar_wait(bar, 0, err, kErrWaitBulk)) return;
+      a_ready = true;
     }
 #pragma unroll
     for (int a = 0; a < NS; ++a) {
@@ -1047,9 +1054,9 @@ struct RmsFwdLora {
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
       attr = true;
     }
-    const size_t smem = (size_t)NS * r * d * sizeof(float);
+    const size_t smem = 16 + (size_t)NS * r * d * sizeof(float);
     launch_pdl(kern, dim3(grid_for(((long long)N + RW - 1) / RW * 32, 256)), dim3(256), smem, st, x, gamma, h, ldh, N,
-               d, eps, r, g);
+               d, eps, r, g, device_error_word());
     return ok();
   }
   static int run(const float* x, const float* gamma, Planes h, long long ldh, int N, int d, float eps, int r,
@@ -1144,9 +1151,10 @@ int launch_rmsnorm_fwd_lora(const float* x, const float* gamma, Planes h, int N,
   if (d % 4 || ldh % 4 || ldh < d || r < 1 || r > 16 || g.n < 1 || g.n > kLoraMaxSegs) return -1;
   for (int a = 0; a < g.n; ++a)
     if (g.s[a].ext_col >= 0 && (g.s[a].ext_col < d || g.s[a].ext_col + r > ldh)) return -1;
-  if ((size_t)g.n * r * d * 4 > 200 * 1024) return -2;   // the adapters' A do not fit in shared memory
+  if ((size_t)g.n * r * d * 4 + 16 > 200 * 1024) return -2;   // the adapters' A do not fit in shared memory
   for (int a = 0; a < g.n; ++a)
-    if (!g.s[a].w || !g.s[a].out || g.s[a].col_off != 0 || g.s[a].width != d ||
+    if (!g.s[a].w || (reinterpret_cast<uintptr_t>(g.s[a].w) & 15) || !g.s[a].out || g.s[a].col_off != 0 ||
+        g.s[a].width != d ||
         (g.s[a].bt && (!g.s[a].b_src || g.s[a].b_rows <= 0)))
       return -1;
   switch (row_chunks(d)) {   // the chunk counts whose register arrays stay small next to the adapter sums
