@@ -16,13 +16,15 @@
 // tiles go from registers to shared memory in the swizzled layout and feed the
 // next UMMA directly; nothing of size T x T reaches HBM.
 //
-// Forward (per sequence, head, query tile of 128): two passes over the key
-// tiles 0..qi. Pass 1 computes S = Q K^T and each row's maximum; pass 2
-// recomputes S, writes P = exp(S - max) to shared memory while summing it,
-// and accumulates O += P V in TMEM; the epilogue divides O by the sum. Every
-// P uses the final maximum, so O needs no rescaling. The scores of the next
-// key tile are computed while the softmax warps work on the current one (two
-// TMEM score buffers).
+// Forward (per sequence, head, query tile of 128): one pass over the key tiles
+// 0..qi with a running row maximum m. For each tile the softmax warps take the
+// tile's row maxima (the two warps of a row quarter exchange theirs), and once
+// the previous O += P V has completed they scale their O columns in TMEM by
+// exp(m_old - m_new) when the maximum grew, write P = exp(S - m) to shared
+// memory and add it to the running row sums (scaled alike); the MMA issuer
+// then accumulates O += P V. The epilogue divides O by the sum. The scores of
+// the next key tile are computed while the softmax warps work on the current
+// one (two TMEM score buffers).
 //
 // Backward (per sequence, query head, key tile j of 128), over the query tiles
 // i = j .. : dP^T = V dO^T and S^T = K Q^T in TMEM; the softmax warps write
@@ -52,7 +54,7 @@ constexpr int kThreads = 32 * (2 + kSoftWarps);
 constexpr int kRing = 3;                   // forward key/value stages
 
 // forward: Q, ring, P, then the row max / row sum exchange between column halves
-constexpr int kFwdSmem = (2 + 2 * kRing + 4) * kPlane + 4 * kTile * 4 + 1024 + 256;
+constexpr int kFwdSmem = (2 + 2 * kRing + 4) * kPlane + 6 * kTile * 4 + 1024 + 256;
 // backward: K, V, Q, dO, P^T / dS^T, then per-warp lse2 / D staging
 constexpr int kBwdSmem = (8 + 4) * kPlane + kSoftWarps * 2 * 64 * 4 + 1024 + 256;
 
@@ -154,8 +156,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sQ = smem;                          // Q hi, Q lo
   uint8_t* sRing = sQ + 2 * kPlane;            // kRing x (hi, lo) key or value tiles
   uint8_t* sP = sRing + 2 * kRing * kPlane;    // P hi (2 tiles), P lo (2 tiles)
-  float* xmax = reinterpret_cast<float*>(sP + 4 * kPlane);   // [2][128] per column half
-  float* xsum = xmax + 2 * kTile;                             // [2][128]
+  float* xmax = reinterpret_cast<float*>(sP + 4 * kPlane);   // [tile parity][column half][128] tile maxima
+  float* xsum = xmax + 4 * kTile;                             // [2][128]
   uint64_t* bar = reinterpret_cast<uint64_t*>(xsum + 2 * kTile);
   uint64_t* q_full = bar;
   uint64_t* r_full = bar + 1;
@@ -165,9 +167,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* p_full = s_empty + 2;
   uint64_t* p_empty = p_full + 1;
   uint64_t* o_full = p_empty + 1;
-  uint64_t* mx_done = o_full + 1;    // both halves' row maxima written
-  uint64_t* sum_done = o_full + 2;   // both halves' row sums written
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 3);
+  uint64_t* sum_done = o_full + 1;   // both halves' row sums written
+  uint64_t* mx_q = o_full + 2;       // [4] per row quarter: both halves' tile maxima written
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 6);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int BH = a.B * a.H;
@@ -190,8 +192,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(p_full, kSoftWarps);
     mbar_init(p_empty, 1);
     mbar_init(o_full, 1);
-    mbar_init(mx_done, kSoftWarps);
     mbar_init(sum_done, kSoftWarps);
+    for (int q = 0; q < 4; ++q) mbar_init(&mx_q[q], 2);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -206,8 +208,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    // Ring order: K_0 .. K_{n-1} (pass 1), then K_0 and, for each j,
-    // K_{j+1} (if any) followed by V_j -- the order the MMA issuer consumes.
+    // Ring order: K_0 and, for each j, K_{j+1} (if any) followed by V_j --
+    // the order the MMA issuer consumes.
     if (lane == 0) {
       mbar_arrive_expect_tx(q_full, 2 * kPlane);
       tma_load_3d(sQ, &mq_hi, q_full, 0, qi * kTile, bh);
@@ -224,9 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_3d(dst + kPlane, ml, &r_full[s], 0, j * kTile, bkv);
         return true;
       };
-      bool ok = true;
-      for (int j = 0; j < n && ok; ++j) ok = push(&mk_hi, &mk_lo, j);
-      if (ok) ok = push(&mk_hi, &mk_lo, 0);
+      bool ok = push(&mk_hi, &mk_lo, 0);
       for (int j = 0; j < n && ok; ++j) {
         if (j + 1 < n) ok = push(&mk_hi, &mk_lo, j + 1);
         if (ok) ok = push(&mv_hi, &mv_lo, j);
@@ -258,8 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(&s_full[sb]);
         return true;
       };
-      for (int j = 0; j < n && ok; ++j) ok = issue_s();   // pass 1
-      if (ok) ok = issue_s();                             // pass 2, key tile 0
+      if (ok) ok = issue_s();   // key tile 0
       for (int j = 0; j < n && ok; ++j) {
         if (j + 1 < n) ok = issue_s();
         if (!ok) break;
@@ -287,70 +286,78 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lanes = (uint32_t)(qw * 32) << 16;
     uint32_t sc = 0;
     bool ok = true;
-    // pass 1: maximum raw score over the live keys (k <= q, k < T); only the
-    // diagonal tile (and a ragged last tile, which is the diagonal) needs the mask
-    float m = -INFINITY;
-    for (int j = 0; j < n && ok; ++j, ++sc) {
+    float m = -INFINITY;   // the raw-score maximum every P of this row is relative to
+    float l = 0.f;         // this half's sum of P
+    uint8_t* th = sP + half * kPlane;
+    uint8_t* tl = sP + (2 + half) * kPlane;
+    // Every tile is walked even after a failed wait, so both warps of a quarter
+    // arrive on its exchange barrier the same number of times.
+    for (int j = 0; j < n; ++j, ++sc) {
       const uint32_t sb = sc & 1, sph = (sc >> 1) & 1;
-      ok = warp_wait(&s_full[sb], sph, a.err, kErrWaitAccum);
+      ok = ok && warp_wait(&s_full[sb], sph, a.err, kErrWaitAccum);
       tc_fence_after();
-      if (ok) {
-        const bool mask = j == qi;
+      // this half's 64 raw scores and their maximum over the live keys (k <= q,
+      // k < T); only the diagonal tile (also a ragged last tile) needs the mask
+      const bool mask = j == qi;
+      float v[2][32];
+      float mt = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          float v[32];
-          tmem_ld32(tmem + lanes + sb * kTile + half * 64 + c * 32, v);
-          const int k0 = j * kTile + half * 64 + c * 32;
+      for (int c = 0; c < 2; ++c) {
+        if (ok) tmem_ld32(tmem + lanes + sb * kTile + half * 64 + c * 32, v[c]);
+        const int k0 = j * kTile + half * 64 + c * 32;
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (!mask || (k0 + e <= qrow && k0 + e < a.T)) m = fmaxf(m, v[e]);
+        for (int e = 0; e < 32; ++e) {
+          const bool live = !mask || (k0 + e <= qrow && k0 + e < a.T);
+          if (!ok) v[c][e] = 0.f;
+          if (live) mt = fmaxf(mt, v[c][e]);
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[sb]);
-    }
-    xmax[half * kTile + row] = m;
-    __syncwarp();
-    if (lane == 0) mbar_arrive(mx_done);
-    ok = ok && warp_wait(mx_done, 0, a.err, kErrWaitAccum);
-    // p = exp2(S * scale_log2 - mb): scale_log2 > 0, so the scaled maximum is mb
-    const float mb = fmaxf(xmax[row], xmax[kTile + row]) * a.scale_log2;
-    // pass 2: unnormalised P = exp2(S * scale_log2 - mb) into shared memory (this
-    // half's 64 keys are one K-major tile), row sums in registers
-    float l = 0.f;
-    uint8_t* th = sP + half * kPlane;
-    uint8_t* tl = sP + (2 + half) * kPlane;
-    for (int j = 0; j < n && ok; ++j, ++sc) {
-      const uint32_t sb = sc & 1, sph = (sc >> 1) & 1;
-      ok = warp_wait(&s_full[sb], sph, a.err, kErrWaitAccum) &&
-           warp_wait(p_empty, (j & 1) ^ 1, a.err, kErrWaitAccum);
+      if (lane == 0 && ok) mbar_arrive(&s_empty[sb]);   // the scores are in registers
+      // the row's tile maximum over both halves
+      float* xm = xmax + (j & 1) * 2 * kTile;
+      xm[half * kTile + row] = mt;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&mx_q[qw]);
+      ok = ok && warp_wait(&mx_q[qw], j & 1, a.err, kErrWaitAccum);
+      const float m_new = fmaxf(m, fmaxf(mt, xm[(half ^ 1) * kTile + row]));
+      const bool grow = j > 0 && m_new > m;
+      const float alpha = grow ? ex2((m - m_new) * a.scale_log2) : 1.f;
+      m = m_new;
+      const float mb = m * a.scale_log2;   // p = exp2(S * scale_log2 - mb); scale_log2 > 0
+      // the P buffer is free and O final for tiles < j once O += P_{j-1} V_{j-1} completed
+      ok = ok && warp_wait(p_empty, (j & 1) ^ 1, a.err, kErrWaitAccum);
       tc_fence_after();
+      if (ok && __any_sync(0xffffffffu, grow)) {   // O *= alpha on this warp's 32 rows x 32 columns
+        float o[32];
+        tmem_ld32(tmem + lanes + 2 * kTile + half * 32, o);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] *= alpha;
+        tmem_st32(tmem + lanes + 2 * kTile + half * 32, o);
+        tmem_wait_st();
+      }
+      l *= alpha;
       if (ok) {
-        const bool mask = j == qi;
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
-          float v[32];
-          tmem_ld32(tmem + lanes + sb * kTile + half * 64 + c * 32, v);
           const int k0 = j * kTile + half * 64 + c * 32;
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
-            float p = ex2(fmaf(v[e], a.scale_log2, -mb));
+            float p = ex2(fmaf(v[c][e], a.scale_log2, -mb));
             if (mask && !(k0 + e <= qrow && k0 + e < a.T)) p = 0.f;
-            v[e] = p;
+            v[c][e] = p;
             l += p;
           }
-          store_row32(th, tl, row, c, v);
+          store_row32(th, tl, row, c, v[c]);
         }
       }
       tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&s_empty[sb]);
-        mbar_arrive(p_full);
-      }
+      if (lane == 0 && ok) mbar_arrive(p_full);
     }
+    const float mb = m * a.scale_log2;
     xsum[half * kTile + row] = l;
     __syncwarp();
     if (lane == 0) mbar_arrive(sum_done);
