@@ -311,7 +311,7 @@ int LlamaEngine::realize() {
       rg.d_in = dims[g][1];
       if (rg.d_in % 16) return -1;
       const LoraGroup G = lora_group(g);
-      const bool fold = (g == kGroupQKV || g == kGroupGU) && G.n && lora_grouped(rg.d_in);
+      const bool fold = G.n && lora_grouped(rg.d_in);
       rg.ext = fold ? 64 : 0;
       ext_[g] = rg.ext;
       rg.off = slot;
@@ -320,6 +320,9 @@ int LlamaEngine::realize() {
     }
     q8_slot_elems_ = slot;
   }
+  o_ld_ = (long long)H * dh + ext_[kGroupO];
+  a_ld_ = (long long)ff + ext_[kGroupDown];
+  dxp_ld_ = (long long)d + std::max(ext_[kGroupO], ext_[kGroupDown]);
   layer_grad_lo_.assign(c.n_layers, n_train_);
   for (const auto& p : params_) {
     if (!p.trainable || p.name.compare(0, 4, "blk.") != 0) continue;
@@ -381,13 +384,13 @@ int LlamaEngine::realize() {
     gu_.push_back(f32((long long)N * 2 * ff));
     h1_.push_back(pl((long long)N * (d + ext_[kGroupQKV])));   // + the q|k|v adapters' u columns
     h2_.push_back(pl((long long)N * (d + ext_[kGroupGU])));    // + the gate|up adapters' u columns
-    a_.push_back(pl((long long)N * ff));
+    a_.push_back(pl((long long)N * a_ld_));   // + the down adapters' u columns
     Qh_.push_back(pl((long long)N * H * dh));
     Kh_.push_back(pl((long long)N * KV * dh));
     Vh_.push_back(pl((long long)N * KV * dh));
     Pm_.push_back(flash_ ? Planes{} : pl(att));
     lse2_.push_back(flash_ ? f32((long long)B * H * T) : nullptr);
-    O_.push_back(pl((long long)N * H * dh));
+    O_.push_back(pl((long long)N * o_ld_));   // + the o adapters' u columns
     lora_u_[l].assign(kLoraCount, nullptr);
     lora_bt_[l].assign(kLoraCount, nullptr);
     for (int t = 0; t < kLoraCount; ++t)
@@ -420,7 +423,7 @@ int LlamaEngine::realize() {
   lse_part_ = reinterpret_cast<float2*>(f32(2LL * ((V + 63) / 64) * N));
   lse_ms_ = reinterpret_cast<float2*>(f32(2LL * N));
   for (int k = 0; k < 2; ++k) {   // two copies of each transient the weight-gradient stream reads
-    dxp2_[k] = pl((long long)N * d);
+    dxp2_[k] = pl((long long)N * dxp_ld_);   // + du of the o / down adapters
     dgu2_[k] = pl((long long)N * (2 * ff + ext_[kGroupGU]));
     dqkv2_[k] = pl((long long)N * (W + ext_[kGroupQKV]));
   }
@@ -953,7 +956,7 @@ int LlamaEngine::norm_bwd(const float* x, const float* gamma, const float* dres,
   }
   const int nblk = rmsnorm_bwd_blocks();
   KL(launch_rmsnorm_bwd(x, dh_, gamma, dres, dx_, dxp_, trainable ? gpart_ : nullptr, nblk, N(), c.d_model, c.rms_eps,
-                        stream_));
+                        stream_, dxp_ld_));
   if (trainable) {   // dgamma: a weight gradient, on the side stream
     CK(fork_side());
     KL(launch_colsum(gpart_, nblk, c.d_model, G32(gp), 0, sst()));
@@ -1209,7 +1212,7 @@ int LlamaEngine::enqueue_forward() {
     }
     if (flash_) {
       // fused: O (token-major planes) and the row normalisers for the backward
-      KL(launch_flash_fwd(Qh_[l], Kh_[l], Vh_[l], O_[l], lse2_[l], B, T, H, KV, dh, scale, err_, stream_));
+      KL(launch_flash_fwd(Qh_[l], Kh_[l], Vh_[l], O_[l], lse2_[l], B, T, H, KV, dh, scale, err_, stream_, o_ld_));
     } else {
       // scores S = scale * Q K^T per (sequence, head)
       GemmDesc gs;
@@ -1228,20 +1231,21 @@ int LlamaEngine::enqueue_forward() {
       go.b = bop(Vh_[l], T, dh, dh, B * KV, 1, H, KV, G, 1);
       go.causal = 2;   // P is zero for keys past the tile's last query
       go.epi.mode = kEpiStoreSplit; go.epi.out_hi = O_[l].hi; go.epi.out_lo = O_[l].lo;
-      go.epi.z_div = H; go.epi.z_s1 = (long long)T * H * dh; go.epi.bstride = dh; go.epi.m_s0 = (long long)H * dh;
+      go.epi.z_div = H; go.epi.z_s1 = (long long)T * o_ld_; go.epi.bstride = dh; go.epi.m_s0 = o_ld_;
       CK(gemm(go));
     }
     // x1 = x + O Wo^T
+    const int eo = ext_[kGroupO];   // o adapter folded in as extra reduction columns
     GemmDesc gw;
-    gw.M = N; gw.N = d; gw.K = H * dh;
-    gw.a = op(O_[l], N, H * dh, H * dh, 0);
+    gw.M = N; gw.N = d; gw.K = H * dh + eo;
+    gw.a = op(O_[l], N, H * dh + eo, o_ld_, 0);
     gw.b = wop(P(pre + "attn_output.weight"), d, H * dh, H * dh, 0);
     gw.epi = epi_rowmajor(kEpiResidF32, x1_[l], d);
     gw.epi.res = x_[l];
     const LoraGroup Go = lora_group(kGroupO);
     if (Go.n) {
-      CK(lora_group_prep(l, Go, O_[l], H * dh, H * dh));
-      gw.epi.lora[gw.epi.n_lora++] = lora_addend(l, kLoraO, 0, d);
+      CK(lora_group_prep(l, Go, O_[l], H * dh, o_ld_));
+      if (!eo) gw.epi.lora[gw.epi.n_lora++] = lora_addend(l, kLoraO, 0, d);
     }
     CK(gemm(gw));
     const LoraGroup Gg = lora_group(kGroupGU);
@@ -1266,18 +1270,19 @@ int LlamaEngine::enqueue_forward() {
       gg.epi = epi_rowmajor(kEpiStoreF32, gu_[l], 2 * ff);
       CK(gemm(gg));
       for (int i = 0; i < Gg.n && !eg; ++i) CK(lora_forward(l, Gg.t[i], gu_[l], 2 * ff, Gg.c0[i], Gg.w[i]));
-      KL(launch_swiglu_fwd(gu_[l], a_[l], N, ff, stream_));
+      KL(launch_swiglu_fwd(gu_[l], a_[l], N, ff, stream_, a_ld_));
     }
+    const int ed = ext_[kGroupDown];   // down adapter folded in as extra reduction columns
     GemmDesc gd;
-    gd.M = N; gd.N = d; gd.K = ff;
-    gd.a = op(a_[l], N, ff, ff, 0);
+    gd.M = N; gd.N = d; gd.K = ff + ed;
+    gd.a = op(a_[l], N, ff + ed, a_ld_, 0);
     gd.b = wop(P(pre + "ffn_down.weight"), d, ff, ff, 0);
     gd.epi = epi_rowmajor(kEpiResidF32, x_[l + 1], d);
     gd.epi.res = x1_[l];
     const LoraGroup Gd = lora_group(kGroupDown);
     if (Gd.n) {
-      CK(lora_group_prep(l, Gd, a_[l], ff, ff));
-      gd.epi.lora[gd.epi.n_lora++] = lora_addend(l, kLoraDown, 0, d);
+      CK(lora_group_prep(l, Gd, a_[l], ff, a_ld_));
+      if (!ed) gd.epi.lora[gd.epi.n_lora++] = lora_addend(l, kLoraDown, 0, d);
     }
     CK(gemm(gd));
   }
@@ -1344,29 +1349,30 @@ int LlamaEngine::enqueue_backward() {
     const Param& Wo = P(pre + "attn_output.weight");
     const Param& Wq = P(pre + "attn_q.weight");
     // ---- FFN
+    const int ed = ext_[kGroupDown];   // dY carries du of the down adapter in its extra columns
     GemmDesc gda;
-    gda.M = N; gda.N = ff; gda.K = d;
-    gda.a = op(dxp_, N, d, d, 0);
+    gda.M = N; gda.N = ff; gda.K = d + ed;
+    gda.a = op(dxp_, N, d + ed, dxp_ld_, 0);
     gda.b = wop(Wd, d, ff, ff, 1);
     gda.epi = epi_rowmajor(kEpiStoreF32, da_, ff);
     const LoraGroup Gd = lora_group(kGroupDown);
     const bool gd_grp = Gd.n && lora_grouped(ff);
-    if (gd_grp) CK(lora_group_du(l, Gd, dxp_, d, ff, gda.epi, -1));
+    if (gd_grp) CK(lora_group_du(l, Gd, dxp_, dxp_ld_, ff, gda.epi, ed ? d : -1));
     CK(gemm(gda));
     if (gd_grp || full) {   // weight gradients of the down projection, on the side stream
       CK(fork_side());
-      if (gd_grp) CK(lora_group_wgrad(l, Gd, a_[l], ff, ff, dxp_, d));
+      if (gd_grp) CK(lora_group_wgrad(l, Gd, a_[l], a_ld_, ff, dxp_, dxp_ld_));
       if (full) {
         GemmDesc gw;
         gw.M = d; gw.N = ff; gw.K = N;
-        gw.a = op(dxp_, N, d, d, 1);
-        gw.b = op(a_[l], N, ff, ff, 1);
+        gw.a = op(dxp_, N, d, dxp_ld_, 1);
+        gw.b = op(a_[l], N, ff, a_ld_, 1);
         gw.epi = epi_rowmajor(kEpiStoreF32, G32(Wd), ff);
         CK(gemm_side(gw));
       }
       CK(side_read2(t_dxp_, t_du_));
     }
-    if (Gd.n && !gd_grp) CK(lora_backward(l, kLoraDown, a_[l], ff, dxp_, d, 0, d, da_, nullptr));
+    if (Gd.n && !gd_grp) CK(lora_backward(l, kLoraDown, a_[l], ff, dxp_, dxp_ld_, 0, d, da_, nullptr));
     const int eg = ext_[kGroupGU];   // dgu carries du of the gate|up adapters in its extra columns
     CK(flip(t_dgu_));
     dgu_ = dgu2_[t_dgu_.cur];
@@ -1401,34 +1407,35 @@ int LlamaEngine::enqueue_backward() {
     Epilogue hm;
     hm.mode = kEpiStoreF32; hm.out = dO32_;
     hm.m_div = T; hm.m_s1 = (long long)H * T * dh; hm.m_s0 = dh; hm.n_div = dh; hm.n_s1 = (long long)T * dh;
+    const int eo = ext_[kGroupO];   // dY carries du of the o adapter in its extra columns
     GemmDesc gdo;
-    gdo.M = N; gdo.N = H * dh; gdo.K = d;
-    gdo.a = op(dxp_, N, d, d, 0);
+    gdo.M = N; gdo.N = H * dh; gdo.K = d + eo;
+    gdo.a = op(dxp_, N, d + eo, dxp_ld_, 0);
     gdo.b = wop(Wo, d, H * dh, H * dh, 1);
     gdo.epi = hm;
     const LoraGroup Go = lora_group(kGroupO);
     const bool go_grp = Go.n && lora_grouped(H * dh);
-    if (go_grp) CK(lora_group_du(l, Go, dxp_, d, H * dh, gdo.epi, -1));
+    if (go_grp) CK(lora_group_du(l, Go, dxp_, dxp_ld_, H * dh, gdo.epi, eo ? d : -1));
     CK(gemm(gdo));
     if (go_grp || full) {
       CK(fork_side());
-      if (go_grp) CK(lora_group_wgrad(l, Go, O_[l], H * dh, H * dh, dxp_, d));
+      if (go_grp) CK(lora_group_wgrad(l, Go, O_[l], o_ld_, H * dh, dxp_, dxp_ld_));
       if (full) {
         GemmDesc gw;
         gw.M = d; gw.N = H * dh; gw.K = N;
-        gw.a = op(dxp_, N, d, d, 1);
-        gw.b = op(O_[l], N, H * dh, H * dh, 1);
+        gw.a = op(dxp_, N, d, dxp_ld_, 1);
+        gw.b = op(O_[l], N, H * dh, o_ld_, 1);
         gw.epi = epi_rowmajor(kEpiStoreF32, G32(Wo), H * dh);
         CK(gemm_side(gw));
       }
       CK(side_read2(t_dxp_, t_du_));
     }
-    if (Go.n && !go_grp) CK(lora_backward(l, kLoraO, O_[l], H * dh, dxp_, d, 0, d, dO32_, &hm));
+    if (Go.n && !go_grp) CK(lora_backward(l, kLoraO, O_[l], H * dh, dxp_, dxp_ld_, 0, d, dO32_, &hm));
     CK(flip(t_dqkv_));   // written by the RoPE backward below
     dqkv_ = dqkv2_[t_dqkv_.cur];
     if (flash_) {
       // ---- attention core, fused: partial dQ / dK / dV summed by the RoPE backward
-      KL(launch_flash_bwd_prep(dO32_, O_[l], dO_, dvec_, B, T, H, dh, stream_));
+      KL(launch_flash_bwd_prep(dO32_, O_[l], dO_, dvec_, B, T, H, dh, stream_, o_ld_));
       KL(launch_flash_bwd(Qh_[l], Kh_[l], Vh_[l], dO_, lse2_[l], dvec_, fws_, B, T, H, KV, dh, scale, err_,
                           stream_));
       KL(launch_flash_rope_bwd(fws_, pos_, cs_, cs_rows_, dqkv_, c.qkv_bias ? qkv_ : nullptr, B, T, H, KV, dh,
@@ -1629,7 +1636,7 @@ long long LlamaEngine::debug_activation(int which, int layer, float* dst, long l
   if (layer < 0 || layer > c.n_layers || (layer == c.n_layers && which != 0)) return -1;
   const float* f = nullptr;
   Planes p{};
-  long long n = 0, ld = 0;   // ld: row pitch of planes with extra columns (rows of d values)
+  long long n = 0, ld = 0, rw = d;   // ld: row pitch of planes with extra columns (rows of rw values)
   switch (which) {
     case 0: f = x_[layer]; n = N * d; break;
     case 1: f = x1_[layer]; n = N * d; break;
@@ -1640,9 +1647,9 @@ long long LlamaEngine::debug_activation(int which, int layer, float* dst, long l
     case 6:
       if (flash_) return -2;   // the fused attention keeps no probability matrix
       p = Pm_[layer]; n = (long long)c.B * H * c.T * c.T; break;
-    case 7: p = O_[layer]; n = N * H * dh; break;
+    case 7: p = O_[layer]; n = N * H * dh; rw = H * dh; ld = o_ld_; break;
     case 8: f = gu_[layer]; n = N * 2 * ff; break;
-    case 9: p = a_[layer]; n = N * ff; break;
+    case 9: p = a_[layer]; n = N * ff; rw = ff; ld = a_ld_; break;
     case 10: f = logits_; n = N * c.vocab; break;
     case 11: p = h2_[layer]; n = N * d; ld = d + ext_[kGroupGU]; break;
     case 12: f = qkv_; n = N * W; break;
@@ -1655,9 +1662,9 @@ long long LlamaEngine::debug_activation(int which, int layer, float* dst, long l
     return n;
   }
   std::vector<bf16> hi(n), lo(n);
-  if (ld > d) {
-    CU(cudaMemcpy2D(hi.data(), d * 2, p.hi, ld * 2, d * 2, N, cudaMemcpyDeviceToHost));
-    CU(cudaMemcpy2D(lo.data(), d * 2, p.lo, ld * 2, d * 2, N, cudaMemcpyDeviceToHost));
+  if (ld > rw) {
+    CU(cudaMemcpy2D(hi.data(), rw * 2, p.hi, ld * 2, rw * 2, N, cudaMemcpyDeviceToHost));
+    CU(cudaMemcpy2D(lo.data(), rw * 2, p.lo, ld * 2, rw * 2, N, cudaMemcpyDeviceToHost));
   } else {
     CU(cudaMemcpy(hi.data(), p.hi, n * 2, cudaMemcpyDeviceToHost));
     CU(cudaMemcpy(lo.data(), p.lo, n * 2, cudaMemcpyDeviceToHost));

@@ -229,6 +229,10 @@ class LlamaEngine {
   // extra reduction width of each group's base GEMMs (0, or 64 with the
   // group's adapters folded into the ring operand)
   int ext_[4] = {0, 0, 0, 0};
+  // row pitches of the activations that carry extension columns: the attention
+  // output (o group), the SwiGLU output (down group) and the RMSNorm-backward
+  // planes (dY of both)
+  long long o_ld_ = 0, a_ld_ = 0, dxp_ld_ = 0;
   int build_ring(long long qvoff);
   // the weight-gradient stream and its state (see Transient)
   cudaStream_t wst_ = nullptr;

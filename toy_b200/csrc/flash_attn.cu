@@ -63,6 +63,7 @@ struct FwdArgs {
   float scale_log2;
   bf16* o_hi;
   bf16* o_lo;
+  long long o_ld;   // token-major O row pitch
   float* lse2;
   int* err;
 };
@@ -372,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int e = 0; e < 32; ++e) o[e] *= inv;
       if (qrow < a.T) {
-        const long long off = ((long long)(b * a.T + qrow) * a.H + h) * kDh + half * 32;
+        const long long off = (long long)(b * a.T + qrow) * a.o_ld + h * kDh + half * 32;
         store_planes32(a.o_hi + off, a.o_lo + off, o);
         if (half == 0) a.lse2[(long long)bh * a.T + qrow] = mb + log2f(lt);
       }
@@ -648,7 +649,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // planes and D = rowsum(dO * O) (the four-lane sums are reduced in a fixed
 // butterfly order).
 __global__ void __launch_bounds__(256) flash_bwd_prep_kernel(const float* __restrict__ dO32, Planes O, Planes dO,
-                                                             float* __restrict__ Dv, int B, int T, int H) {
+                                                             float* __restrict__ Dv, int B, int T, int H,
+                                                             long long o_ld) {
   griddep_wait();
   const int lane = threadIdx.x % 32, hl = lane % 16;
   const long long rows = (long long)B * H * T;
@@ -660,7 +662,7 @@ __global__ void __launch_bounds__(256) flash_bwd_prep_kernel(const float* __rest
     const long long bh = r / T;
     const int b = (int)(bh / H), h = (int)(bh % H);
     const float4 g = reinterpret_cast<const float4*>(dO32 + r * kDh)[hl];
-    const long long oo = ((long long)(b * T + t) * H + h) * kDh + 4 * hl;
+    const long long oo = (long long)(b * T + t) * o_ld + h * kDh + 4 * hl;
     const uint2 oh = *reinterpret_cast<const uint2*>(O.hi + oo);
     const uint2 ol = *reinterpret_cast<const uint2*>(O.lo + oo);
     const float o0 = __uint_as_float(oh.x << 16) + __uint_as_float(ol.x << 16);
@@ -703,8 +705,9 @@ bool shape_ok(int B, int T, int H, int KV, int dh) {
 bool flash_supported(int dh) { return dh == kDh; }
 
 int launch_flash_fwd(Planes Q, Planes K, Planes V, Planes O, float* lse2, int B, int T, int H, int KV, int dh,
-                     float scale, int* err, cudaStream_t st) {
-  if (!shape_ok(B, T, H, KV, dh)) return -1;
+                     float scale, int* err, cudaStream_t st, long long o_ld) {
+  if (o_ld == 0) o_ld = (long long)H * dh;
+  if (!shape_ok(B, T, H, KV, dh) || o_ld < (long long)H * dh || o_ld % 8) return -1;
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem) != cudaSuccess)
@@ -718,7 +721,7 @@ int launch_flash_fwd(Planes Q, Planes K, Planes V, Planes O, float* lse2, int B,
   FwdArgs a;
   a.B = B; a.T = T; a.H = H; a.KV = KV; a.G = H / KV; a.nq = (T + kTile - 1) / kTile;
   a.scale_log2 = scale * 1.4426950408889634f;
-  a.o_hi = O.hi; a.o_lo = O.lo; a.lse2 = lse2; a.err = err;
+  a.o_hi = O.hi; a.o_lo = O.lo; a.o_ld = o_ld; a.lse2 = lse2; a.err = err;
   const long long grid = (long long)a.nq * B * H;
   if (grid > 0x7fffffffLL) return -5;
   return launch_pdl(flash_fwd_kernel, dim3((unsigned)grid), dim3(kThreads), kFwdSmem, st, mq[0], mq[1], mk[0], mk[1],
@@ -726,12 +729,13 @@ int launch_flash_fwd(Planes Q, Planes K, Planes V, Planes O, float* lse2, int B,
 }
 
 int launch_flash_bwd_prep(const float* dO32, Planes O, Planes dO, float* Dvec, int B, int T, int H, int dh,
-                          cudaStream_t st) {
-  if (dh != kDh) return -1;
+                          cudaStream_t st, long long o_ld) {
+  if (o_ld == 0) o_ld = (long long)H * dh;
+  if (dh != kDh || o_ld < (long long)H * dh || o_ld % 4) return -1;
   const long long rows = (long long)B * H * T;
   long long blocks = (rows + 15) / 16;
   if (blocks > 148 * 16) blocks = 148 * 16;
-  return launch_pdl(flash_bwd_prep_kernel, dim3((unsigned)blocks), dim3(256), 0, st, dO32, O, dO, Dvec, B, T, H)
+  return launch_pdl(flash_bwd_prep_kernel, dim3((unsigned)blocks), dim3(256), 0, st, dO32, O, dO, Dvec, B, T, H, o_ld)
              ? -21 : 0;
 }
 

@@ -15,14 +15,15 @@ namespace tb2 {
 
 bool flash_supported(int dh);
 
-// O = softmax(scale * Q K^T + causal mask) V, and lse2.
+// O = softmax(scale * Q K^T + causal mask) V, and lse2. O is token-major,
+// rows o_ld apart (0: H dh).
 int launch_flash_fwd(Planes Q, Planes K, Planes V, Planes O, float* lse2, int B, int T, int H, int KV, int dh,
-                     float scale, int* err, cudaStream_t st);
+                     float scale, int* err, cudaStream_t st, long long o_ld = 0);
 
 // Backward preparation: dO (f32, head-major [B][H][T][dh]) as planes, and
 // D[b, h, t] = sum_c dO[b, h, t, c] * O[b, t, h, c].
 int launch_flash_bwd_prep(const float* dO32, Planes O, Planes dO, float* Dvec, int B, int T, int H, int dh,
-                          cudaStream_t st);
+                          cudaStream_t st, long long o_ld = 0);   // O rows o_ld apart (0: H dh)
 
 // Floats of the partial-gradient workspace launch_flash_bwd writes.
 long long flash_bwd_ws_floats(int B, int T, int H, int KV, int dh);

@@ -169,8 +169,8 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const float* __restric
 template <int NC>
 __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restrict__ x, const float* __restrict__ dh,
                                                           const float* __restrict__ gamma, const float* dres,
-                                                          float* dx, Planes dxp, float* __restrict__ gpart, int N,
-                                                          int d, float eps) {
+                                                          float* dx, Planes dxp, long long ldp,
+                                                          float* __restrict__ gpart, int N, int d, float eps) {
   griddep_wait();
   extern __shared__ float4 gacc4[];  // [warps][d / 4]
   const int warps = blockDim.x / 32;
@@ -215,7 +215,7 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restric
       o.z = rs.z + (gg.z * g.z - v.z * coef) * rr;
       o.w = rs.w + (gg.w * g.w - v.w * coef) * rr;
       out[c] = o;
-      if (dxp.hi) store_planes4(dxp, base + c * 4, o);
+      if (dxp.hi) store_planes4(dxp, (long long)n * ldp + c * 4, o);
       if (gpart) {
         float4 a = my[c];
         a.x += gg.x * v.x * rr;
@@ -474,7 +474,8 @@ __global__ void __launch_bounds__(256) softmax_causal_bwd_kernel(Planes P, const
 
 // ------------------------------------------------------------------ SwiGLU
 // One block per token row, float4 over the ff columns of gate | up.
-__global__ void __launch_bounds__(128) swiglu_fwd_kernel(const float* __restrict__ gu, Planes a, int N, int ff) {
+__global__ void __launch_bounds__(128) swiglu_fwd_kernel(const float* __restrict__ gu, Planes a, long long lda, int N,
+                                                         int ff) {
   griddep_wait();
   const int ff4 = ff / 4;
   for (int n = blockIdx.x; n < N; n += gridDim.x) {
@@ -482,7 +483,7 @@ __global__ void __launch_bounds__(128) swiglu_fwd_kernel(const float* __restrict
     const float4* u4 = g4 + ff4;
     for (int c = threadIdx.x; c < ff4; c += blockDim.x) {
       const float4 g = __ldcs(g4 + c), u = __ldcs(u4 + c);
-      store_planes4(a, (long long)n * ff + 4 * c,
+      store_planes4(a, (long long)n * lda + 4 * c,
                     make_float4(g.x / (1.0f + expf(-g.x)) * u.x, g.y / (1.0f + expf(-g.y)) * u.y,
                                 g.z / (1.0f + expf(-g.z)) * u.z, g.w / (1.0f + expf(-g.w)) * u.w));
     }
@@ -1085,14 +1086,15 @@ struct RmsFwd {
 template <int NC>
 struct RmsBwd {
   static int run(const float* x, const float* dh, const float* gamma, const float* dres, float* dx, Planes dxp,
-                 float* gpart, int nblk, int N, int d, float eps, cudaStream_t st) {
+                 long long ldp, float* gpart, int nblk, int N, int d, float eps, cudaStream_t st) {
     const size_t smem = (size_t)8 * d * sizeof(float);
     static bool attr = false;
     if (!attr) {
       cudaFuncSetAttribute(rmsnorm_bwd_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
       attr = true;
     }
-    launch_pdl(rmsnorm_bwd_kernel<NC>, dim3(nblk), dim3(256), smem, st, x, dh, gamma, dres, dx, dxp, gpart, N, d, eps);
+    launch_pdl(rmsnorm_bwd_kernel<NC>, dim3(nblk), dim3(256), smem, st, x, dh, gamma, dres, dx, dxp, ldp, gpart, N, d,
+               eps);
     return ok();
   }
 };
@@ -1169,10 +1171,11 @@ int launch_rmsnorm_fwd_lora(const float* x, const float* gamma, Planes h, int N,
 }
 
 int launch_rmsnorm_bwd(const float* x, const float* dh, const float* gamma, const float* dres, float* dx,
-                       Planes dxp, float* gpart, int nblk, int N, int d, float eps, cudaStream_t st) {
-  if (d % 4 || nblk != kRmsBwdBlocks) return -1;
+                       Planes dxp, float* gpart, int nblk, int N, int d, float eps, cudaStream_t st, long long ldp) {
+  if (ldp == 0) ldp = d;
+  if (d % 4 || ldp % 4 || ldp < d || nblk != kRmsBwdBlocks) return -1;
   if ((size_t)8 * d * sizeof(float) > 200 * 1024) return -1;
-  return dispatch_nc<RmsBwd>(row_chunks(d), x, dh, gamma, dres, dx, dxp, gpart, nblk, N, d, eps, st);
+  return dispatch_nc<RmsBwd>(row_chunks(d), x, dh, gamma, dres, dx, dxp, ldp, gpart, nblk, N, d, eps, st);
 }
 
 int launch_colsum(const float* gpart, int nblk, int d, float* gout, int accumulate, cudaStream_t st) {
@@ -1223,9 +1226,10 @@ int launch_softmax_causal_bwd(Planes P, const float* dP, Planes dS, long long Z,
   return dispatch_nc<SmBwd>(row_chunks(T), P, dP, dS, Z * T, T, scale, st);
 }
 
-int launch_swiglu_fwd(const float* gu, Planes a, int N, int ff, cudaStream_t st) {
-  if (ff % 4) return -1;
-  launch_pdl(swiglu_fwd_kernel, dim3(N < 16 * kSMs ? N : 16 * kSMs), dim3(128), 0, st, gu, a, N, ff);
+int launch_swiglu_fwd(const float* gu, Planes a, int N, int ff, cudaStream_t st, long long lda) {
+  if (lda == 0) lda = ff;
+  if (ff % 4 || lda % 4 || lda < ff) return -1;
+  launch_pdl(swiglu_fwd_kernel, dim3(N < 16 * kSMs ? N : 16 * kSMs), dim3(128), 0, st, gu, a, lda, N, ff);
   return ok();
 }
 

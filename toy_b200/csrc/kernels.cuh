@@ -45,7 +45,8 @@ struct LoraSegs;
 int launch_rmsnorm_fwd_lora(const float* x, const float* gamma, Planes h, int N, int d, float eps, int r,
                             const LoraSegs& g, cudaStream_t st, long long ldh = 0);
 int launch_rmsnorm_bwd(const float* x, const float* dh, const float* gamma, const float* dres, float* dx,
-                       Planes dxp, float* gpart, int nblk, int N, int d, float eps, cudaStream_t st);
+                       Planes dxp, float* gpart, int nblk, int N, int d, float eps, cudaStream_t st,
+                       long long ldp = 0);   // dxp rows ldp apart (0: d)
 // gout[c] = (accumulate ? gout[c] : 0) + sum_b gpart[b][c]
 int launch_colsum(const float* gpart, int nblk, int d, float* gout, int accumulate, cudaStream_t st);
 int rmsnorm_bwd_blocks();
@@ -74,7 +75,8 @@ int launch_softmax_causal_bwd(Planes P, const float* dP, Planes dS, long long Z,
                               cudaStream_t st);
 
 // a = silu(gate) * up from gu [N][2*ff] (gate | up) -> planes [N][ff].
-int launch_swiglu_fwd(const float* gu, Planes a, int N, int ff, cudaStream_t st);
+int launch_swiglu_fwd(const float* gu, Planes a, int N, int ff, cudaStream_t st,
+                      long long lda = 0);   // a rows lda apart (0: ff)
 // dgate = silu_back(gate, da * up), dup = da * silu(gate) -> planes [N][2*ff].
 // dgu planes rows are ld_dgu apart (0: 2 ff).
 int launch_swiglu_bwd(const float* gu, const float* da, Planes dgu, int N, int ff, cudaStream_t st,
