@@ -137,7 +137,11 @@ int LlamaEngine::bucket_begin() {
   pend_lo_ = pend_hi_ = n_train_;
   comm_used_ = false;
   if (!allreduce_fn_ || profiling_) return 0;
-  if (!comm_stream_) CU(cudaStreamCreateWithFlags(&comm_stream_, cudaStreamNonBlocking));
+  if (!comm_stream_) {   // gradient buckets: high priority, so a reduction is not held behind weight gradients
+    int prio_lo = 0, prio_hi = 0;
+    CU(cudaDeviceGetStreamPriorityRange(&prio_lo, &prio_hi));
+    CU(cudaStreamCreateWithPriority(&comm_stream_, cudaStreamNonBlocking, prio_hi));
+  }
   return 0;
 }
 
@@ -224,8 +228,19 @@ int LlamaEngine::realize() {
   if (c.T % 64 && !(c.attn_impl == 0 && flash_supported(c.d_head))) return -1;
   if (c.mode == 1 && (c.lora_rank <= 0 || c.lora_rank > kLoraMaxRank || c.lora_targets == 0)) return -1;
   CU(cudaSetDevice(device_));
-  CU(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
-  CU(cudaStreamCreateWithFlags(&wst_, cudaStreamNonBlocking));
+  // Adapter steps: the activation / activation-gradient chain is the critical
+  // path and the second stream carries light work (adapter weight gradients,
+  // ring fills), so the chain's stream gets the highest priority and SMs freed
+  // by a finishing kernel go to its next kernel first (kernel nodes captured
+  // into the step graph keep these). Measured on one B200, SmolLM2 B=8 T=512:
+  // QLoRA q,v 267.9k -> 271.1k tokens/s. Full fine-tunes keep equal
+  // priorities: their second stream holds the weight-gradient GEMMs, and
+  // favouring either stream lengthened the step (222.6k -> 218.6k with the
+  // chain first, 221.3k -> 218.5k with the weight gradients first).
+  int prio_lo = 0, prio_hi = 0;
+  CU(cudaDeviceGetStreamPriorityRange(&prio_lo, &prio_hi));
+  CU(cudaStreamCreateWithPriority(&stream_, cudaStreamNonBlocking, c.mode == 1 ? prio_hi : prio_lo));
+  CU(cudaStreamCreateWithPriority(&wst_, cudaStreamNonBlocking, prio_lo));
   err_ = device_error_word();
   if (!err_) return -3;
   const bool full = c.mode == 0;
@@ -1556,7 +1571,7 @@ int LlamaEngine::step(bool is_first, bool run_optimizer) {
   }
   if (graph_) cudaGraphExecDestroy(graph_);
   graph_ = nullptr;
-  ce = cudaGraphInstantiate(&graph_, g, 0);
+  ce = cudaGraphInstantiate(&graph_, g, cudaGraphInstantiateFlagUseNodePriority);
   cudaGraphDestroy(g);
   CU(ce);
   graph_valid_ = true;
