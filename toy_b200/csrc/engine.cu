@@ -1271,7 +1271,7 @@ int LlamaEngine::enqueue_forward() {
     gg.a = op(h2_[l], N, d + eg, d + eg, 0);
     const Param& Wgu = P(pre + "ffn_gate.weight");
     gg.b = wop(Wgu, 2 * ff, d, d, 0);
-    if (Wgu.q8 && !q8_planes_) {
+    if (Wgu.q8 && !q8_planes_ && a_ld_ == ff) {   // (the epilogue writes a with a row pitch of d_ff)
       // Q8_0 base: one launch -- gate|up projection (gate and up rows paired per
       // tile), adapters, a = silu(gate) * up as planes; gate|up kept in f32 for
       // the backward. (The dequantising GEMM has operand-feed headroom for the
