@@ -2,10 +2,16 @@
 """Benchmark: train tokens/s of toy's training step (forward + cross-entropy +
 backward + AdamW) on B200s, with the step's roofline fraction.
 
-Default workload (one GPU): SmolLM2-135M shape, full f32 fine-tune, B=8
-sequences of T=512 tokens per GPU, data-parallel over N GPUs (weak scaling).
-Synthetic data: token ids uniform in [0, vocab), labels = ids shifted by one
-inside each sequence, weights from the reference's seeded init stream.
+Default workload (one GPU): SmolLM2-135M shape, full f32 fine-tune with every
+weight N(0, 0.02), B=8 sequences of T=512 tokens per GPU, data-parallel over N
+GPUs (weak scaling). The same line carries the QLoRA workload (q, v adapters
+over a frozen Q8_0 base, B=8 T=512) as `north_star_qlora`. Synthetic data:
+token ids uniform in [0, vocab), labels = ids shifted by one inside each
+sequence, weights from the reference's seeded init stream.
+
+The CPU baseline (rank 0, one GPU) and the reference arm (`--impl reference`)
+run the oracle's numpy restatement of toy's CPU step in float32 on the host
+cores, on the workload's own B and T (one full step, ~0.5-1 min).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                   [--workload smollm2_full_ft_b8_t512|smollm2_qlora_b8_t512]
@@ -29,15 +35,24 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+from toy_b200.adamw import AdamW  # noqa: E402
+from toy_b200.batch import next_token_labels, positions, synthetic_token_ids  # noqa: E402
+
 METRIC = "train tokens/sec (fwd+bwd+AdamW) at 1/2/4/8 B200; % of step roofline"
 KIND_NAMES = ["gemm", "rmsnorm_fwd", "rmsnorm_bwd", "colsum", "rope", "softmax", "swiglu", "cross_entropy",
               "loss_reduce", "adamw", "embedding", "split", "allreduce", "flash_fwd", "flash_bwd", "flash_prep",
               "lora"]
 
 WORKLOADS = {
-    "smollm2_full_ft_b8_t512": dict(mode=0, B=8, T=512, lora=None, lr=1e-4, wd=0.01),
-    "smollm2_qlora_b8_t512": dict(mode=1, B=8, T=512, lora=("q", "v"), lr=1e-4, wd=0.01),
+    "smollm2_full_ft_b8_t512": dict(mode=0, B=8, T=512, lora=None, lr=1e-4, wd=0.01, init_std=0.02),
+    "smollm2_qlora_b8_t512": dict(mode=1, B=8, T=512, lora=("q", "v"), lr=1e-4, wd=0.01, init_std=0.0),
 }
+
+# DRAM traffic of the step's GEMM launches, from one ncu capture of the full
+# workload (dram__bytes_read.sum + dram__bytes_write.sum over every GEMM launch
+# of one step, one pass per launch); the summary and its command are in
+# profiles/. Filled per workload once captured.
+GEMM_TRAFFIC = {}
 
 
 def peaks():
@@ -125,21 +140,28 @@ def dist_env():
     return rank, world, local
 
 
-def cpu_baseline_port(cfg_o, mode, lora, B, T, steps, warmup, lr, wd):
-    """The oracle (numpy f64 restatement of toy's CPU step) on the host cores."""
+def cpu_port_step_rate(wl, steps):
+    """The oracle (numpy restatement of toy's CPU step, float32 like ggml-cpu) on
+    the host cores, on the workload's own B and T: `steps` full steps (forward,
+    CE, backward, AdamW), each timed alone. Returns (tokens/s, steps timed)."""
     from oracle import oracle as O
-    if mode == 0:
-        mdl = O.full_ft_model(cfg_o, seed=42, init_scale=0.02 * (cfg_o.d_model ** 0.5))
+    cfg_o = O.smollm2_135m()
+    B, T = wl["B"], wl["T"]
+    if wl["mode"] == 0:
+        mdl = O.full_ft_model(cfg_o, seed=42, std_all=wl["init_std"])
     else:
-        mdl = O.qlora_model(cfg_o, O.LoraCfg(rank=8, alpha=16.0, targets=lora), seed=42)
+        mdl = O.qlora_model(cfg_o, O.LoraCfg(rank=8, alpha=16.0, targets=wl["lora"]), seed=42)
+    mdl.dtype = np.float32
+    mdl.zero_moments()
     times = []
-    for s in range(warmup + steps):
-        ids = O.token_ids(100 + s, T * B, cfg_o.vocab)
+    opt = AdamW.for_lora()
+    opt.lr, opt.weight_decay = wl["lr"], wl["wd"]
+    for s in range(steps):
+        ids = synthetic_token_ids(100 + s, T * B, cfg_o.vocab)
+        lab = next_token_labels(ids, T, B, cfg_o.vocab)
         t0 = time.perf_counter()
-        O.train_step(mdl, ids, O.positions(T, B), O.next_token_labels(ids, T, B, cfg_o.vocab), T, B,
-                     O.hp_lora(lr, s + 1, wd=wd), s == 0)
-        if s >= warmup:
-            times.append(time.perf_counter() - t0)
+        O.train_step(mdl, ids, positions(T, B), lab, T, B, opt.hp(s + 1), s == 0)
+        times.append(time.perf_counter() - t0)
     return T * B * len(times) / sum(times), len(times)
 
 
@@ -154,80 +176,67 @@ def cores():
     return os.cpu_count() or 1
 
 
-def run_reference(args, wl, cfg_o):
+def cpu_sample_text(wl, n):
+    return (f"{n} full step(s) (fwd+CE+bwd+AdamW) of the oracle port (numpy float32, BLAS threads = host cores) "
+            f"on the workload's own shape, B={wl['B']} T={wl['T']}, same model and init")
+
+
+def run_reference(args, wl):
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    B, T = 1, 64
-    warm = 1 if args.warmup > 1 else args.warmup
-    steps = max(1, min(args.steps, 3))
-    value, n = cpu_baseline_port(cfg_o, wl["mode"], wl["lora"], B, T, steps, warm, wl["lr"], wl["wd"])
-    sample = f"{n} timed steps of the oracle port on B=1, T={T} (full step incl. AdamW) of the same model"
+    # one full step of the workload takes ~0.5-1 min on the host: time one, a second when the first was quick
+    value, n = cpu_port_step_rate(wl, 1)
+    if wl["B"] * wl["T"] / value < 45.0 and args.steps > 1:
+        value, n = cpu_port_step_rate(wl, 2)
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": n, "warmup": warm, "ms_per_step": 1000.0 * B * T / value, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": args.workload, "global_batch": B, "seq_len": T, "parallelism": "none (host CPU)"},
-            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores(), "kind": "port", "sample": sample},
+            "steps": n, "warmup": 0, "ms_per_step": 1000.0 * wl["B"] * wl["T"] / value, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (uniform ids, seeded init)",
+            "config": {"workload": args.workload, "model": "SmolLM2-135M shape", "global_batch": wl["B"],
+                       "seq_len": wl["T"], "parallelism": "none (host CPU, rank 0)"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores(), "kind": "port",
+                             "sample": cpu_sample_text(wl, n)},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="smollm2_full_ft_b8_t512", choices=sorted(WORKLOADS))
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--batch", type=int, default=0, help="override sequences per GPU (small profiling cases)")
-    ap.add_argument("--layers", type=int, default=0,
-                    help="override the decoder depth (small profiling cases; recorded in config)")
-    args = ap.parse_args()
-    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
-    wl = WORKLOADS[args.workload]
-    from oracle import oracle as O
-    cfg_o = O.smollm2_135m()
-    if args.impl == "reference":
-        run_reference(args, wl, cfg_o)
-        return
+def realize(wl, cfg, device):
+    from toy_b200 import FromScratch, LoRA, LoraOptions, RecipeOptions
+    B, T = wl["B"], wl["T"]
+    if wl["mode"] == 0:
+        rec = FromScratch(device=device)
+        rec.realize(cfg, RecipeOptions(t_seq=T, t_batch=B, seed=42, init_std=wl["init_std"]))
+        return rec, rec.fs_cache
+    rec = LoRA(device=device)
+    rec.realize(cfg, 8, RecipeOptions(t_seq=T, t_batch=B, seed=42), LoraOptions(rank=8, alpha=16.0,
+                                                                                 targets=wl["lora"]))
+    return rec, rec.lora_cache
 
-    rank, world, local = dist_env()
-    from toy_b200 import FromScratch, LlamaConfig, LoRA, LoraOptions, RecipeOptions
+
+def measure(wl, cfg, args, dp, rank, world, local, profile=True):
+    """One workload on this rank: warm-up through the public API, e2e (host
+    buffers, public step API, wall clock), then K graph replays timed by CUDA
+    events on the step stream (inputs resident), max over ranks."""
     from toy_b200._lib import lib
     L = lib()
-    cfg = LlamaConfig.smollm2_135m()
-    if args.layers:
-        cfg.n_layers = args.layers
-    B, T = (args.batch or wl["B"]), wl["T"]
+    B, T = wl["B"], wl["T"]
     N = B * T
-    dp = None
-    if world > 1:
-        from toy_b200.parallel import DataParallel
-        dp = DataParallel(rank, world, local)
-    opts = RecipeOptions(t_seq=T, t_batch=B, seed=42, init_scale=0.02 * (cfg.d_model ** 0.5))
-    if wl["mode"] == 0:
-        rec = FromScratch(device=local)
-        rec.realize(cfg, opts)
-        eng = rec.fs_cache
-    else:
-        rec = LoRA(device=local)
-        rec.realize(cfg, 8, opts, LoraOptions(rank=8, alpha=16.0, targets=wl["lora"]))
-        eng = rec.lora_cache
+    rec, eng = realize(wl, cfg, local)
     if dp:
         dp.attach(eng)
     sess = eng.sess
+    opt = AdamW.for_lora()
+    opt.lr, opt.weight_decay = wl["lr"], wl["wd"]
 
     def batch(step):
-        ids = O.token_ids(1000 * step + rank, N, cfg.vocab)
-        return ids, O.positions(T, B), O.next_token_labels(ids, T, B, cfg.vocab)
+        ids = synthetic_token_ids(1000 * step + rank, N, cfg.vocab)
+        return ids, positions(T, B), next_token_labels(ids, T, B, cfg.vocab)
 
     batches = [batch(s) for s in range(4)]
-    hp = lambda s: O.hp_lora(wl["lr"], s + 1, wd=wl["wd"])
     # warm-up through the public API (the first step also captures the CUDA graph)
     for s in range(args.warmup):
         ids, pos, lab = batches[s % len(batches)]
-        rec.step(ids, pos, lab, hp(s), s == 0)
+        rec.step(ids, pos, lab, opt.hp(s + 1), s == 0)
     L.tb2_sync(sess)
     # e2e: the public step API with host buffers (uploads + step + loss read-back), wall clock
     if dp:
@@ -235,7 +244,7 @@ def main():
     t0 = time.perf_counter()
     for s in range(args.steps):
         ids, pos, lab = batches[s % len(batches)]
-        rec.step(ids, pos, lab, hp(args.warmup + s), False)
+        rec.step(ids, pos, lab, opt.hp(args.warmup + s + 1), False)
     L.tb2_sync(sess)
     e2e_s = time.perf_counter() - t0
     if dp:
@@ -256,39 +265,86 @@ def main():
         if dp:
             step_ms = dp.max_scalar(step_ms)
             dp.barrier()
-    clocks = clk.summary()
-    # live per-kernel breakdown from one profiled (eager) step
-    cap = 8192
-    kinds = (C.c_int * cap)()
-    kms = (C.c_float * cap)()
-    kfl = (C.c_double * cap)()
-    n = L.tb2_profile_step(sess, 0, kinds, kms, kfl, cap)
-    per_kind = {}
-    gemm_flops = gemm_ms = 0.0
-    for i in range(min(n, cap)):
-        k = KIND_NAMES[kinds[i]] if kinds[i] < len(KIND_NAMES) else "other"
-        per_kind[k] = per_kind.get(k, 0.0) + kms[i]
-        if kinds[i] == 0:
-            gemm_flops += kfl[i]
-            gemm_ms += kms[i]
-    tot = sum(per_kind.values())
+    out = {"step_ms": step_ms, "e2e_s": e2e_s, "h2d": h2d, "clocks": clk.summary(),
+           "launches": L.tb2_step_launches(sess)}
+    if profile:
+        # live per-kernel breakdown from one profiled (eager) step
+        cap = 8192
+        kinds = (C.c_int * cap)()
+        kms = (C.c_float * cap)()
+        kfl = (C.c_double * cap)()
+        n = L.tb2_profile_step(sess, 0, kinds, kms, kfl, cap)
+        per_kind, gemm_flops, gemm_ms, gemm_n = {}, 0.0, 0.0, 0
+        for i in range(min(n, cap)):
+            k = KIND_NAMES[kinds[i]] if kinds[i] < len(KIND_NAMES) else "other"
+            per_kind[k] = per_kind.get(k, 0.0) + kms[i]
+            if kinds[i] == 0:
+                gemm_flops += kfl[i]
+                gemm_ms += kms[i]
+                gemm_n += 1
+        out.update(per_kind=per_kind, gemm_flops=gemm_flops, gemm_ms=gemm_ms, gemm_n=gemm_n)
+    if dp:
+        dp.detach()
+    eng.close()
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="smollm2_full_ft_b8_t512", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-qlora", action="store_true", help="skip the QLoRA sub-measurement")
+    ap.add_argument("--batch", type=int, default=0, help="override sequences per GPU (small profiling cases)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="override the decoder depth (small profiling cases; recorded in config)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+    wl = dict(WORKLOADS[args.workload])
+    if args.impl == "reference":
+        run_reference(args, wl)
+        return
+
+    rank, world, local = dist_env()
+    from toy_b200 import LlamaConfig
+    cfg = LlamaConfig.smollm2_135m()
+    if args.layers:
+        cfg.n_layers = args.layers
+    if args.batch:
+        wl["B"] = args.batch
+    B, T = wl["B"], wl["T"]
+    N = B * T
+    dp = None
+    if world > 1:
+        from toy_b200.parallel import DataParallel
+        dp = DataParallel(rank, world, local)
+    r = measure(wl, cfg, args, dp, rank, world, local)
+    qlora = None
+    if not args.no_qlora and wl["mode"] == 0:
+        qwl = dict(WORKLOADS["smollm2_qlora_b8_t512"])
+        if args.batch:
+            qwl["B"] = args.batch
+        qlora = measure(qwl, cfg, args, dp, rank, world, local, profile=False)
     burst, sustained, hbm, src = peaks()
-    gemm_tflops = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else 0.0
+    step_ms = r["step_ms"]
+    gemm_tflops = r["gemm_flops"] / (r["gemm_ms"] * 1e-3) / 1e12 if r["gemm_ms"] > 0 else 0.0
     f_tok = step_flops_per_token(cfg, T, wl["mode"], wl["lora"] or (), 8)
     tokens = N * world
     value = tokens / (step_ms * 1e-3)
     step_tflops = f_tok * N / (step_ms * 1e-3) / 1e12
-    launches = L.tb2_step_launches(sess)
     if rank != 0:
         if dp:
             dp.close()
         return
     cpu = None
-    if world == 1 and not args.no_cpu_baseline:
-        Bc, Tc = 1, 128
-        v, nsteps = cpu_baseline_port(cfg_o, wl["mode"], wl["lora"], Bc, Tc, 1, 0, wl["lr"], wl["wd"])
-        cpu = {"value": v, "unit": "tokens/s", "cores": cores(), "kind": "port",
-               "sample": f"{nsteps} full step (fwd+CE+bwd+AdamW) of the oracle port, same model, B=1 T={Tc}"}
+    if world == 1 and not args.no_cpu_baseline and not args.layers and not args.batch:
+        v, nsteps = cpu_port_step_rate(wl, 1)
+        cpu = {"value": v, "unit": "tokens/s", "cores": cores(), "kind": "port", "sample": cpu_sample_text(wl, nsteps)}
+    tot = sum(r["per_kind"].values())
+    traffic = GEMM_TRAFFIC.get(args.workload) if not (args.layers or args.batch) else None
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
@@ -296,23 +352,45 @@ def main():
         "data": "synthetic (uniform ids, seeded init)",
         "config": {"workload": args.workload, "model": "SmolLM2-135M shape", "global_batch": B * world,
                    "seq_len": T, "parallelism": f"dp{world}", "tokens_per_step": tokens,
-                   "l2": "working set (activations ~6 GB, weights+moments 2 GB) far exceeds the 126 MB L2",
+                   "init": "every weight N(0, 0.02) f32" if wl["mode"] == 0 else "Q8_0 base from N(0, 0.02)",
+                   "l2": "inputs larger than L2: working set (activations ~6 GB, weights+moments 2 GB) far "
+                         "exceeds the 126 MB L2",
                    **({"layers_override": cfg.n_layers} if args.layers else {})},
         "step_roofline": {"tflops_algorithmic": step_tflops, "peak_tflops": sustained,
                           "frac": step_tflops / sustained, "peak_source": f"bf16 sustained, {src}",
                           "flops_per_token": f_tok},
         "roofline": {"bound": "tensor", "kernel": "gemm_split_bf16 (all GEMM launches of one step)",
                      "achieved": gemm_tflops, "peak": sustained, "unit": "TFLOP/s",
-                     "frac": gemm_tflops / sustained, "traffic": None, "mma_passes": 3,
+                     "frac": gemm_tflops / sustained,
+                     "traffic": traffic["bytes_per_step"] / r["gemm_n"] if traffic else None,
+                     "traffic_note": (f"mean DRAM bytes per GEMM launch (ncu dram__bytes_read+write over "
+                                      f"{traffic['launches']} GEMM launches of one step, {traffic['source']}); "
+                                      f"algorithmic operand+output bytes per launch "
+                                      f"{traffic['algorithmic_bytes_per_step'] / r['gemm_n']:.3e}")
+                     if traffic else None,
+                     "gemm_launches_per_step": r["gemm_n"], "mma_passes": 3,
                      "peak_source": f"bf16 sustained, {src}"},
-        "kernel_ms": {k: round(v, 4) for k, v in sorted(per_kind.items(), key=lambda kv: -kv[1])},
-        "kernel_share": {k: round(v / tot, 4) for k, v in per_kind.items()} if tot > 0 else {},
-        "e2e": {"value": tokens / (e2e_s / args.steps), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+        "kernel_ms": {k: round(v, 4) for k, v in sorted(r["per_kind"].items(), key=lambda kv: -kv[1])},
+        "kernel_share": {k: round(v / tot, 4) for k, v in r["per_kind"].items()} if tot > 0 else {},
+        "e2e": {"value": tokens / (r["e2e_s"] / args.steps), "unit": "tokens/s", "h2d_bytes_per_step": r["h2d"],
                 "d2h_bytes_per_step": 8},
-        "gpu_launches": launches * args.steps,
-        "clocks": clocks,
+        "gpu_launches": r["launches"] * args.steps,
+        "clocks": r["clocks"],
         "cpu_baseline": cpu,
     }
+    if qlora:
+        qwl = WORKLOADS["smollm2_qlora_b8_t512"]
+        qf = step_flops_per_token(cfg, T, 1, qwl["lora"], 8)
+        qv = qwl["B"] * qwl["T"] * world / (qlora["step_ms"] * 1e-3) if not args.batch else \
+            N * world / (qlora["step_ms"] * 1e-3)
+        line["north_star_qlora"] = {
+            "workload": "smollm2_qlora_b8_t512", "lora": "q,v rank 8 alpha 16 over a frozen Q8_0 base",
+            "value": qv, "unit": "tokens/s", "ms_per_step": qlora["step_ms"], "steps": args.steps,
+            "step_roofline": {"tflops_algorithmic": qf * qv / world / 1e12, "peak_tflops": sustained,
+                              "frac": qf * qv / world / 1e12 / sustained, "flops_per_token": qf},
+            "e2e": {"value": qv * qlora["step_ms"] * 1e-3 / (qlora["e2e_s"] / args.steps), "unit": "tokens/s",
+                    "h2d_bytes_per_step": qlora["h2d"], "d2h_bytes_per_step": 8},
+            "gpu_launches": qlora["launches"] * args.steps, "clocks": qlora["clocks"]}
     print(json.dumps(line), flush=True)
     if dp:
         dp.close()

@@ -395,10 +395,13 @@ class Model:
     q8: Dict[str, np.ndarray] = field(default_factory=dict)   # raw Q8_0 blocks of frozen projections
     m: Dict[str, np.ndarray] = field(default_factory=dict)
     v: Dict[str, np.ndarray] = field(default_factory=dict)
+    # arithmetic type of the step: float64 for parity checks; float32 times the
+    # restatement at the precision toy's CPU path (ggml-cpu) computes in
+    dtype: type = np.float64
 
     def zero_moments(self):
-        self.m = {k: np.zeros(self.params[k].shape, np.float64) for k in self.trainable}
-        self.v = {k: np.zeros(self.params[k].shape, np.float64) for k in self.trainable}
+        self.m = {k: np.zeros(self.params[k].shape, self.dtype) for k in self.trainable}
+        self.v = {k: np.zeros(self.params[k].shape, self.dtype) for k in self.trainable}
 
 
 def full_ft_model(cfg: LlamaCfg, seed: int = 42, init_scale: float = 1.0, std_all: Optional[float] = None) -> Model:
@@ -434,13 +437,13 @@ def _lora_delta(mdl: Model, l: int, p: str, h1):
     ka, kb = f"blk.{l}.{PNAME[p]}.lora_a", f"blk.{l}.{PNAME[p]}.lora_b"
     if lc is None or ka not in mdl.params:
         return None, None
-    A = mdl.params[ka].astype(np.float64)
-    B = mdl.params[kb].astype(np.float64)
+    A = mdl.params[ka].astype(mdl.dtype)
+    B = mdl.params[kb].astype(mdl.dtype)
     if lc.per_head_q:
         cfg = mdl.cfg
         r, dh = lc.rank, cfg.d_head
         u = h1 @ A.T                                   # [N, H*r]
-        out = np.empty((h1.shape[0], cfg.n_heads * dh))
+        out = np.empty((h1.shape[0], cfg.n_heads * dh), mdl.dtype)
         for h in range(cfg.n_heads):
             out[:, h * dh:(h + 1) * dh] = u[:, h * r:(h + 1) * r] @ B[h * dh:(h + 1) * dh].T
         return out, u
@@ -451,8 +454,8 @@ def _lora_delta(mdl: Model, l: int, p: str, h1):
 def _lora_back(mdl: Model, l: int, p: str, h1, u, dy, grads):
     lc = mdl.lora
     ka, kb = f"blk.{l}.{PNAME[p]}.lora_a", f"blk.{l}.{PNAME[p]}.lora_b"
-    A = mdl.params[ka].astype(np.float64)
-    B = mdl.params[kb].astype(np.float64)
+    A = mdl.params[ka].astype(mdl.dtype)
+    B = mdl.params[kb].astype(mdl.dtype)
     if lc.per_head_q:
         cfg = mdl.cfg
         r, dh = lc.rank, cfg.d_head
@@ -480,11 +483,14 @@ def forward_backward(mdl: Model, ids: np.ndarray, pos: np.ndarray, labels: np.nd
     N, d, H, KV, dh, G = T * B, cfg.d_model, cfg.n_heads, cfg.n_kv, cfg.d_head, cfg.group
     eps = cfg.rms_eps
     scale = 1.0 / math.sqrt(dh)
-    f64 = lambda k: P[k].astype(np.float64)
+    dt = mdl.dtype
+    f64 = lambda k: P[k].astype(dt)
     cos, sin = rope_cache(pos, dh, cfg.rope_base, 1.0, cfg.rope_freq_factors)
+    cos, sin = cos.astype(dt), sin.astype(dt)
+    scale = dt(scale)
     E = f64("token_embd.weight")
     x = E[ids]
-    causal = np.triu(np.full((T, T), -np.inf), 1)
+    causal = np.triu(np.full((T, T), -np.inf, dt), 1)
     caches = []
     for l in range(cfg.n_layers):
         c = {"x": x}
@@ -503,8 +509,8 @@ def forward_backward(mdl: Model, ids: np.ndarray, pos: np.ndarray, labels: np.nd
         q = rope(qkv["q"].reshape(N, H, dh), cos, sin)
         k = rope(qkv["k"].reshape(N, KV, dh), cos, sin)
         v = qkv["v"].reshape(N, KV, dh)
-        o = np.empty((N, H, dh))
-        probs = np.empty((B, H, T, T))
+        o = np.empty((N, H, dh), dt)
+        probs = np.empty((B, H, T, T), dt)
         for b in range(B):
             sl = slice(b * T, (b + 1) * T)
             for h in range(H):
@@ -625,7 +631,7 @@ def forward_backward(mdl: Model, ids: np.ndarray, pos: np.ndarray, labels: np.nd
             grads[pre + "attn_norm.weight"] = np.sum(dh1 * x0 * r1, axis=0)
         dx = dx1 + rms_norm_back(x0, dh1 * f64(pre + "attn_norm.weight"), eps)
     if "token_embd.weight" in tr:
-        gE = grads.get("token_embd.weight", np.zeros(E.shape))
+        gE = grads.get("token_embd.weight", np.zeros(E.shape, dt))
         np.add.at(gE, ids, dx)     # get_rows_back: scatter-add (tinynn_ggml.c:1683-1700)
         grads["token_embd.weight"] = gE
     return loss, grads, logits
@@ -638,7 +644,7 @@ def train_step(mdl: Model, ids, pos, labels, T, B, hp, is_first: bool):
         mdl.zero_moments()
     loss, grads, _ = forward_backward(mdl, ids, pos, labels, T, B)
     for k in mdl.trainable:
-        p2, m2, v2 = adamw(mdl.params[k].astype(np.float64), grads[k], mdl.m[k], mdl.v[k], hp)
+        p2, m2, v2 = adamw(mdl.params[k].astype(mdl.dtype), grads[k], mdl.m[k], mdl.v[k], hp)
         mdl.params[k] = p2.astype(np.float32)
         mdl.m[k], mdl.v[k] = m2, v2
     return loss, grads

@@ -1,7 +1,7 @@
 """Data-parallel training across the GPUs of one node (one process per GPU).
 
-The gradient all-reduce itself runs inside the library (NCCL on the step
-stream, include/toy_b200.h tb2_dp_init). This module is the host side: it uses
+The gradient all-reduce itself runs inside the library (NCCL in per-layer
+buckets on a side stream of the step, include/toy_b200.h tb2_dp_init). This module is the host side: it uses
 torch.distributed (gloo, over the torchrun rendezvous) only to hand rank 0's
 NCCL unique id to every rank, and for host barriers / max-over-ranks timing.
 """
@@ -59,6 +59,13 @@ class DataParallel:
         if bucket_floats is not None:
             check(L.tb2_dp_set_bucket_floats(eng.sess, int(bucket_floats)), "tb2_dp_set_bucket_floats")
         self.sess = eng.sess
+
+    def detach(self) -> None:
+        """Free the attached session's communicator; the process group stays up
+        for another attach."""
+        if self.sess:
+            check(lib().tb2_dp_free(self.sess), "tb2_dp_free")
+            self.sess = None
 
     def barrier(self) -> None:
         _pg().barrier()

@@ -66,6 +66,9 @@ class RecipeOptions:
     qkv_bias: bool = False
     seed: int = 42
     init_scale: float = 1.0
+    # > 0: every weight N(0, init_std) instead of the reference's fan-in scaled
+    # init (the benchmark configurations' "all weights N(0, 0.02)")
+    init_std: float = 0.0
     # attention core: "flash" (fused kernels, d_head 64; other widths use the
     # materialised path) or "materialized" (score GEMM + softmax + PV GEMM)
     attention: str = "flash"
@@ -126,7 +129,7 @@ class LlamaSeqEngine:
             c.rope_freq_factors = self._ff.ctypes.data_as(C.POINTER(C.c_double))
         check(lib().tb2_llama_realize(self.sess, C.byref(c)), "tb2_llama_realize")
         if lora is None:
-            check(lib().tb2_llama_init_random(self.sess, opts.seed, opts.init_scale, 0.0, 0.0, 0.0),
+            check(lib().tb2_llama_init_random(self.sess, opts.seed, opts.init_scale, opts.init_std, 0.0, 0.0),
                   "tb2_llama_init_random")
         else:
             check(lib().tb2_llama_init_random(self.sess, opts.seed, 1.0, lora.base_std, lora.a_std, lora.b_std),
