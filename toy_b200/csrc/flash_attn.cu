@@ -38,6 +38,7 @@
 
 #include "gemm.cuh"
 #include "pdl.cuh"
+#include "runtime.cuh"
 #include "tc_common.cuh"
 
 #include <cmath>
@@ -708,12 +709,12 @@ int launch_flash_fwd(Planes Q, Planes K, Planes V, Planes O, float* lse2, int B,
                      float scale, int* err, cudaStream_t st, long long o_ld) {
   if (o_ld == 0) o_ld = (long long)H * dh;
   if (!shape_ok(B, T, H, KV, dh) || o_ld < (long long)H * dh || o_ld % 8) return -1;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem) != cudaSuccess)
-      return -20;
-    attr = true;
-  }
+  static DeviceOnce setup;
+  if (int rc0 = setup.ensure([](int) {
+        return cudaFuncSetAttribute(flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem) == cudaSuccess ? 0
+                                                                                                              : -20;
+      }))
+    return rc0;
   CUtensorMap mq[2], mk[2], mv[2];
   int rc;
   if ((rc = maps_for(mq, Q, T, B * H)) || (rc = maps_for(mk, K, T, B * KV)) || (rc = maps_for(mv, V, T, B * KV)))
@@ -748,12 +749,12 @@ long long flash_bwd_ws_floats(int B, int T, int H, int KV, int dh) {
 int launch_flash_bwd(Planes Q, Planes K, Planes V, Planes dO, const float* lse2, const float* Dvec, float* ws, int B,
                      int T, int H, int KV, int dh, float scale, int* err, cudaStream_t st) {
   if (!shape_ok(B, T, H, KV, dh)) return -1;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(flash_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem) != cudaSuccess)
-      return -20;
-    attr = true;
-  }
+  static DeviceOnce setup;
+  if (int rc0 = setup.ensure([](int) {
+        return cudaFuncSetAttribute(flash_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem) == cudaSuccess ? 0
+                                                                                                              : -20;
+      }))
+    return rc0;
   CUtensorMap mq[2], mk[2], mv[2], mo[2];
   int rc;
   if ((rc = maps_for(mq, Q, T, B * H)) || (rc = maps_for(mk, K, T, B * KV)) || (rc = maps_for(mv, V, T, B * KV)) ||

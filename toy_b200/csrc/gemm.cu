@@ -20,6 +20,7 @@
 // zero beyond the diagonal.
 #include "gemm.cuh"
 #include "pdl.cuh"
+#include "runtime.cuh"
 #include "tc_common.cuh"
 
 #include <cudaTypedefs.h>
@@ -994,9 +995,9 @@ template <int BN, bool SPLIT, bool Q8 = false, bool FUSED = false, bool PAIR = f
 int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream_t stream, int splits) {
   using S = Stages<BN, SPLIT, Q8, PAIR>;
   auto* kern = gemm_split_bf16_kernel<BN, SPLIT, Q8, FUSED, PAIR>;
-  static bool attr_set = false;
-  static int max_pairs = 0;   // co-resident CTA pairs (clusters of 2) on this GPU
-  if (!attr_set) {
+  static DeviceOnce setup;
+  static int max_pairs_of[64] = {};   // co-resident CTA pairs (clusters of 2) per GPU
+  int dev_rc = setup.ensure([&](int dev) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes) != cudaSuccess)
       return -20;
     if (PAIR) {
@@ -1011,10 +1012,16 @@ int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream
       at[0].val.clusterDim.z = 1;
       cfg.attrs = at;
       cfg.numAttrs = 1;
-      if (cudaOccupancyMaxActiveClusters(&max_pairs, kern, &cfg) != cudaSuccess || max_pairs < 1) return -22;
+      int mp = 0;
+      if (cudaOccupancyMaxActiveClusters(&mp, kern, &cfg) != cudaSuccess || mp < 1) return -22;
+      max_pairs_of[dev] = mp;
     }
-    attr_set = true;
-  }
+    return 0;
+  });
+  if (dev_rc) return dev_rc;
+  int cur_dev = 0;
+  cudaGetDevice(&cur_dev);
+  const int max_pairs = max_pairs_of[cur_dev];
   CUtensorMap ma_hi, ma_lo, mb_hi, mb_lo;
   const int a_box = d.a.mn_major ? 64 : BM;
   // B box rows: a pair holds half of B's rows per CTA, paired gate|up rows are
@@ -1089,6 +1096,14 @@ int gemm_set_pair_mode(int mode) {
 
 int make_plane_map(CUtensorMap* map, const __nv_bfloat16* base, const Operand& o, int box_rows) {
   return make_map(map, base, o, box_rows);
+}
+
+int gemm_effective_splits(const GemmDesc& d, int ksplits) {
+  const Epilogue& e = d.epi;
+  const bool fused = e.mode == kEpiRopeQKV || e.mode == kEpiSwiGLU || e.n_lora > 0;
+  if (ksplits <= 1 || d.causal || d.batch != 1 || fused || e.mode == kEpiStoreLse) return 1;
+  const int kb = (d.K + BK - 1) / BK;
+  return ksplits < kb ? ksplits : kb;
 }
 
 int gemm_launch(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream_t stream) {

@@ -133,6 +133,11 @@ struct GemmScratch {
 // shape/alignment (nothing launched). `dev_err` is a device int the kernel sets
 // to a DeviceError code if one of its bounded waits gives up.
 int gemm_launch(const GemmDesc& d, const GemmScratch& scratch, int* dev_err, cudaStream_t stream);
+// The number of K splits gemm_launch runs for an explicit request of
+// `ksplits` (d.splits is ignored): 1 when the shape allows no split (causal,
+// batched, fused or logsumexp epilogues), else ksplits capped at the k-block
+// count. The workspace then has to hold that many M x N partial tiles.
+int gemm_effective_splits(const GemmDesc& d, int ksplits);
 
 // GEMMs on CTA pairs (cta_group::2: 256-row units, each CTA holding half of
 // the B tile): -1 (the default) for the shapes where pairs measured faster

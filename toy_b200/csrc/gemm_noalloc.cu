@@ -12,13 +12,16 @@
 //
 // Limits and sharing:
 //   * the split-K workspace holds kNoAllocWsFloats floats (8 MiB); a call whose
-//     explicit ksplits * M * N exceeds it is rejected with -5 and a message;
-//     with ksplits = 0 the split count is chosen to fit;
+//     explicit ksplits, as the GEMM would run them (capped at the k-block count,
+//     1 where the shape allows no split), times M * N exceeds it is rejected
+//     with -5 and a message; with ksplits = 0 the split count is chosen to fit;
 //   * every GPU that loads the library holds these arrays until process exit;
 //   * all calls on a device share them and the arrays keep the last call's
 //     contents, so calls that overlap on the GPU (different streams, or
 //     different host threads) race; serialise them on one stream;
-//   * the error word is cleared (stream-ordered) at the start of every call.
+//   * the error word (non-zero when a kernel's bounded wait gave up, so the
+//     output is not valid) is cleared, stream-ordered, at the start of every
+//     call; tb2_gemm_noalloc_error() reads and clears it.
 // The first call on each device resolves the arrays' device addresses
 // (cudaGetSymbolAddress with that device current); make that first call before
 // any stream capture.
@@ -68,17 +71,6 @@ int resolve(DevicePtrs* out) {
 extern "C" int tb2_gemm_noalloc(int M, int N, int K, int batch, int split, const tb2_operand* a, const tb2_operand* b,
                                 const tb2_epilogue* epi, int ksplits, int causal, void* stream) {
   if (!a || !b || !epi || ksplits < 0) return -1;
-  if (ksplits > 1 && (long long)ksplits * M * N > kNoAllocWsFloats) {
-    fprintf(stderr,
-            "[toy_b200] tb2_gemm_noalloc: ksplits * M * N = %lld floats exceeds the fixed %lld-float "
-            "split-K workspace\n",
-            (long long)ksplits * M * N, kNoAllocWsFloats);
-    return -5;
-  }
-  DevicePtrs p;
-  if (resolve(&p)) return -3;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(p.err, 0, sizeof(int), st) != cudaSuccess) return -3;
   tb2::GemmDesc d;
   d.M = M; d.N = N; d.K = K; d.batch = batch; d.split = split != 0;
   d.splits = ksplits;
@@ -107,9 +99,34 @@ extern "C" int tb2_gemm_noalloc(int M, int N, int K, int batch, int split, const
   e.m_s1 = epi->m_s1; e.m_s0 = epi->m_s0;
   e.n_div = epi->n_div > 0 ? epi->n_div : (1 << 30);
   e.n_s1 = epi->n_s1;
+  const int eff = tb2::gemm_effective_splits(d, ksplits);
+  if (eff > 1 && (long long)eff * M * N > kNoAllocWsFloats) {
+    fprintf(stderr,
+            "[toy_b200] tb2_gemm_noalloc: %d K splits x M x N = %lld floats exceeds the fixed %lld-float "
+            "split-K workspace\n",
+            eff, (long long)eff * M * N, kNoAllocWsFloats);
+    return -5;
+  }
+  DevicePtrs p;
+  if (resolve(&p)) return -3;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(p.err, 0, sizeof(int), st) != cudaSuccess) return -3;
   tb2::GemmScratch sc;
   sc.ws = p.ws;
   sc.ws_floats = kNoAllocWsFloats;
   const int rc = tb2::gemm_launch(d, sc, p.err, st);
   return rc == 0 ? 0 : (rc <= -10 ? -3 : -1);
+}
+
+extern "C" int tb2_gemm_noalloc_error(void) {
+  DevicePtrs p;
+  if (resolve(&p)) return -3;
+  if (cudaDeviceSynchronize() != cudaSuccess) return -3;
+  int h = 0;
+  if (cudaMemcpyFromSymbol(&h, g_noalloc_err, sizeof(int)) != cudaSuccess) return -3;
+  if (h) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_noalloc_err, &zero, sizeof(int)) != cudaSuccess) return -3;
+  }
+  return h;
 }

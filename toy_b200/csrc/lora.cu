@@ -653,15 +653,16 @@ __global__ void __launch_bounds__(256) lora_down_bulk_kernel(Planes X, long long
 
 template <int RT, int NS>
 int down_bulk(Planes X, long long ldx, int N, int r, const LoraSegs& segs, bool shared, size_t smem, cudaStream_t st) {
-  static bool attr[2] = {false, false};
+  static DeviceOnce setup[2];
   auto* k0 = lora_down_bulk_kernel<RT, NS, false>;
   auto* k1 = lora_down_bulk_kernel<RT, NS, true>;
-  if (!attr[shared]) {
-    if (cudaFuncSetAttribute(shared ? k1 : k0, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
-        cudaSuccess)
-      return -3;
-    attr[shared] = true;
-  }
+  if (setup[shared].ensure([&](int) {
+        return cudaFuncSetAttribute(shared ? k1 : k0, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) ==
+                       cudaSuccess
+                   ? 0
+                   : -3;
+      }))
+    return -3;
   int* err = device_error_word();
   const unsigned blocks = (unsigned)((N + kDownRows - 1) / kDownRows);
   return shared ? launch_pdl(k1, dim3(blocks), dim3(256), smem, st, X, ldx, N, r, segs, err)
@@ -679,15 +680,16 @@ int down_bulk_ns(Planes X, long long ldx, int N, int r, const LoraSegs& segs, bo
 template <int RT, int NS>
 int down_group(Planes X, long long ldx, int N, int r, const LoraSegs& segs, bool shared, size_t smem,
                cudaStream_t st) {
-  static bool attr[2] = {false, false};
+  static DeviceOnce setup[2];
   auto* k0 = lora_down_group_kernel<RT, NS, false>;
   auto* k1 = lora_down_group_kernel<RT, NS, true>;
-  if (!attr[shared]) {
-    if (cudaFuncSetAttribute(shared ? k1 : k0, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
-        cudaSuccess)
-      return -3;
-    attr[shared] = true;
-  }
+  if (setup[shared].ensure([&](int) {
+        return cudaFuncSetAttribute(shared ? k1 : k0, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) ==
+                       cudaSuccess
+                   ? 0
+                   : -3;
+      }))
+    return -3;
   // one row pair per warp: the pass is latency-bound, so every row's loads are
   // in flight at once (each block restages w, a few KB of L2 reads)
   const unsigned blocks = (unsigned)std::min<long long>(148 * 4, (N + 15) / 16);
@@ -1034,11 +1036,13 @@ int wgrad2(Planes dY, long long ldy, Planes X, long long ldx, int N, const WgPla
   wg_chunks(N, nch, chunk);
   auto* kern = lora_wgrad2_kernel<RS>;
   const size_t smem = ((size_t)chunk * RS + (size_t)8 * RS * 64) * sizeof(float);
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024) != cudaSuccess) return -3;
-    attr = true;
-  }
+  static DeviceOnce setup;
+  if (setup.ensure([&](int) {
+        return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024) == cudaSuccess
+                   ? 0
+                   : -3;
+      }))
+    return -3;
   if (launch_pdl(kern, dim3((unsigned)p.groups, (unsigned)nch), dim3(256), smem, st, dY, ldy, X, ldx, N, chunk, p,
                  part))
     return -3;

@@ -1,9 +1,35 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "gemm.cuh"
 
 namespace tb2 {
+// Set-up that must happen once on every device a launch site runs on (a
+// kernel's dynamic shared-memory limit, an occupancy query): ensure(f) calls
+// f(device) the first time the current device reaches it and remembers a
+// success, so a process that drives several GPUs sets each one up. Host
+// threads may call it concurrently.
+class DeviceOnce {
+ public:
+  template <class F>
+  int ensure(F&& f) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return -3;
+    std::lock_guard<std::mutex> lk(mu_);
+    if (done_[dev]) return 0;
+    const int rc = f(dev);
+    if (rc == 0) done_[dev] = true;
+    return rc;
+  }
+
+ private:
+  static constexpr int kMaxDev = 64;
+  std::mutex mu_;
+  bool done_[kMaxDev] = {};
+};
+
 // Device int the kernels of the current device report wait timeouts into.
 int* device_error_word();
 // Synchronise, read the word, clear it. Returns the code (0 = none) or -3.
