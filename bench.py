@@ -46,6 +46,9 @@ KIND_NAMES = ["gemm", "rmsnorm_fwd", "rmsnorm_bwd", "colsum", "rope", "softmax",
 WORKLOADS = {
     "smollm2_full_ft_b8_t512": dict(mode=0, B=8, T=512, lora=None, lr=1e-4, wd=0.01, init_std=0.02),
     "smollm2_qlora_b8_t512": dict(mode=1, B=8, T=512, lora=("q", "v"), lr=1e-4, wd=0.01, init_std=0.0),
+    # toy's own LoRA recipe: per-head LoRA-Q (one rank-8 pair per query head, scale 1) over the Q8_0 base
+    "smollm2_lora_q_b8_t512": dict(mode=1, B=8, T=512, lora=("q",), per_head=True, lr=1e-4, wd=0.01,
+                                   init_std=0.0),
 }
 
 # DRAM traffic of the step's GEMM launches, from one ncu capture of the full
@@ -65,9 +68,10 @@ def peaks():
     return 1590.0, 1400.0, 6650.0, "fallback"
 
 
-def step_flops_per_token(cfg, T, mode, lora_targets, rank):
+def step_flops_per_token(cfg, T, mode, lora_targets, rank, per_head=False):
     """Algorithmic FLOPs per token: full FT 6*P_mm + 3*A; QLoRA 4*P_mm + 3*A + 6*P_lora,
-    P_mm = projection + LM-head parameters touched per token, A = 4*L*H*dh*(T+1)/2."""
+    P_mm = projection + LM-head parameters touched per token, A = 4*L*H*dh*(T+1)/2
+    (per-head LoRA-Q: P_lora = L*H*r*(d + dh))."""
     d, H, KV, dh, ff, L, V = cfg.d_model, cfg.n_heads, cfg.n_kv, cfg.d_head, cfg.d_ff, cfg.n_layers, cfg.vocab
     per_layer = d * (H + 2 * KV) * dh + H * dh * d + 2 * ff * d + ff * d
     p_mm = L * per_layer + V * d
@@ -77,6 +81,8 @@ def step_flops_per_token(cfg, T, mode, lora_targets, rank):
     shapes = {"q": (H * dh, d), "k": (KV * dh, d), "v": (KV * dh, d), "o": (d, H * dh), "gate": (ff, d),
               "up": (ff, d), "down": (d, ff)}
     p_lora = L * sum(rank * (shapes[t][0] + shapes[t][1]) for t in lora_targets)
+    if per_head:
+        p_lora = L * H * rank * (d + dh)
     return 4 * p_mm + 3 * A + 6 * p_lora
 
 
@@ -149,6 +155,8 @@ def cpu_port_step_rate(wl, steps):
     B, T = wl["B"], wl["T"]
     if wl["mode"] == 0:
         mdl = O.full_ft_model(cfg_o, seed=42, std_all=wl["init_std"])
+    elif wl.get("per_head"):
+        mdl = O.qlora_model(cfg_o, O.LoraCfg(rank=8, per_head_q=True, targets=("q",), a_std=1.0), seed=42)
     else:
         mdl = O.qlora_model(cfg_o, O.LoraCfg(rank=8, alpha=16.0, targets=wl["lora"]), seed=42)
     mdl.dtype = np.float32
@@ -208,8 +216,8 @@ def realize(wl, cfg, device):
         rec.realize(cfg, RecipeOptions(t_seq=T, t_batch=B, seed=42, init_std=wl["init_std"]))
         return rec, rec.fs_cache
     rec = LoRA(device=device)
-    rec.realize(cfg, 8, RecipeOptions(t_seq=T, t_batch=B, seed=42), LoraOptions(rank=8, alpha=16.0,
-                                                                                 targets=wl["lora"]))
+    lo = None if wl.get("per_head") else LoraOptions(rank=8, alpha=16.0, targets=wl["lora"])
+    rec.realize(cfg, 8, RecipeOptions(t_seq=T, t_batch=B, seed=42), lo)   # None: the recipe's per-head LoRA-Q
     return rec, rec.lora_cache
 
 
@@ -289,6 +297,50 @@ def measure(wl, cfg, args, dp, rank, world, local, profile=True):
     return out
 
 
+def run_decode(args):
+    """Decode throughput of the KV-cache path (not the training metric): SmolLM2-135M
+    shape over the Q8_0 base, n_seq sequences in lockstep at a context of ctx
+    positions, f32 and Q8_0 caches; tokens/s from CUDA events around graph replays
+    of one decode step (each replay attends over the ctx cached positions)."""
+    from toy_b200 import LlamaConfig, LoRA, LoraOptions, RecipeOptions
+    from toy_b200._lib import lib
+    from toy_b200.decode import KVDecoder
+    L = lib()
+    cfg = LlamaConfig.smollm2_135m()
+    rec = LoRA()
+    rec.realize(cfg, 8, RecipeOptions(t_seq=64, t_batch=1, seed=42), LoraOptions(rank=8, targets=("q", "v")))
+    rows = []
+    ctx = 512
+    for kv_q8 in (False, True):
+        for nseq in (1, 8, 16):
+            dec = KVDecoder(rec.lora_cache, max_T=ctx + 1, n_seq=nseq, kv_q8=kv_q8)
+            prompt = synthetic_token_ids(7, nseq * 4, cfg.vocab).reshape(nseq, 4)
+            dec.decode_batch(prompt)
+            dec.decode_step(prompt[:, 0], np.full(nseq, ctx))   # the timed step attends over ctx + 1 positions
+            ms = C.c_float(0.0)
+            check_rc = L.tb2_kv_run(rec.lora_cache.sess, args.warmup, C.byref(ms))
+            check_rc |= L.tb2_kv_run(rec.lora_cache.sess, args.steps, C.byref(ms))
+            if check_rc:
+                raise RuntimeError("tb2_kv_run failed")
+            step_ms = ms.value / args.steps
+            rows.append({"n_seq": nseq, "kv_cache": "q8_0" if kv_q8 else "f32", "ctx": ctx + 1,
+                         "ms_per_step": step_ms, "tokens_per_s": nseq / (step_ms * 1e-3),
+                         "launches_per_step": L.tb2_kv_launches(rec.lora_cache.sess)})
+            dec.close()
+    burst, sustained, hbm, src = peaks()
+    d, V, ff = cfg.d_model, cfg.vocab, cfg.d_ff
+    per_layer = d * (cfg.n_heads + 2 * cfg.n_kv) * cfg.d_head + cfg.n_heads * cfg.d_head * d + 3 * ff * d
+    weight_bytes = cfg.n_layers * per_layer * 34 / 32 + V * d * 4   # Q8_0 projections + f32 tied head
+    for r in rows:
+        kv = cfg.n_layers * cfg.n_kv * cfg.d_head * 2 * r["ctx"] * r["n_seq"] * (34 / 32 if r["kv_cache"] == "q8_0" else 4)
+        r["hbm_gbs"] = (weight_bytes + kv) / (r["ms_per_step"] * 1e-3) / 1e9
+        r["hbm_frac"] = r["hbm_gbs"] / hbm
+    print(json.dumps({"metric": "decode tokens/s (KV cache, Q8_0 base)", "model": "SmolLM2-135M shape",
+                      "data": "synthetic", "steps": args.steps, "warmup": args.warmup,
+                      "algorithmic_bytes_per_step": "Q8_0 weights + f32 tied head once per step, plus the cache read",
+                      "peak_hbm_gbs": hbm, "rows": rows}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -298,12 +350,16 @@ def main():
     ap.add_argument("--workload", default="smollm2_full_ft_b8_t512", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-qlora", action="store_true", help="skip the QLoRA sub-measurement")
+    ap.add_argument("--decode", action="store_true", help="measure KV-cache decode instead of training")
     ap.add_argument("--batch", type=int, default=0, help="override sequences per GPU (small profiling cases)")
     ap.add_argument("--layers", type=int, default=0,
                     help="override the decoder depth (small profiling cases; recorded in config)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     wl = dict(WORKLOADS[args.workload])
+    if args.decode:
+        run_decode(args)
+        return
     if args.impl == "reference":
         run_reference(args, wl)
         return
@@ -331,7 +387,7 @@ def main():
     burst, sustained, hbm, src = peaks()
     step_ms = r["step_ms"]
     gemm_tflops = r["gemm_flops"] / (r["gemm_ms"] * 1e-3) / 1e12 if r["gemm_ms"] > 0 else 0.0
-    f_tok = step_flops_per_token(cfg, T, wl["mode"], wl["lora"] or (), 8)
+    f_tok = step_flops_per_token(cfg, T, wl["mode"], wl["lora"] or (), 8, wl.get("per_head", False))
     tokens = N * world
     value = tokens / (step_ms * 1e-3)
     step_tflops = f_tok * N / (step_ms * 1e-3) / 1e12

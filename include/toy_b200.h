@@ -92,13 +92,22 @@ int tb2_gemm(int M, int N, int K, int batch, int split, const tb2_operand *a, co
  * can only hand this library inputs and outputs; tb2_gemm allocates its split-K
  * workspace on first use, this variant uses an 8 MiB workspace compiled into
  * the library (held on every GPU that loads it until exit) and never calls an
- * allocator. Explicit ksplits with ksplits*M*N > 2^21 floats returns -5; with
- * ksplits = 0 the split count is chosen to fit. Calls share the workspace: calls
- * that overlap on the GPU race, so serialise them on one stream. The first call
- * on a device looks up the workspace's device address; make it before any
- * stream capture. Same arguments and results as tb2_gemm. */
+ * allocator. An explicit ksplits whose effective count (capped at ceil(K/64),
+ * 1 for causal or batched products) times M*N exceeds 2^21 floats returns -5;
+ * with ksplits = 0 the split count is chosen to fit. Calls share the workspace:
+ * calls that overlap on the GPU race, so serialise them on one stream. The
+ * first call on a device looks up the workspace's device address; make it
+ * before any stream capture. Same arguments and results as tb2_gemm; a kernel
+ * whose bounded wait gave up is reported by tb2_gemm_noalloc_error(), not by
+ * tb2_device_error(). */
 int tb2_gemm_noalloc(int M, int N, int K, int batch, int split, const tb2_operand *a, const tb2_operand *b,
                      const tb2_epilogue *epi, int ksplits, int causal, void *stream);
+/* The error word of tb2_gemm_noalloc on the current device: synchronises the
+ * device, returns 0 when the last call's kernels completed their waits, the
+ * non-zero code a kernel recorded otherwise (its output is then not valid),
+ * or -3 when the word cannot be read; clears it. Allocates nothing. No
+ * counterpart in the reference. */
+int tb2_gemm_noalloc_error(void);
 
 /* Tile scheduling of every GEMM this library launches: mode 1 runs each GEMM
  * whose shape allows it (split planes, no causal mode) on CTA pairs -- two
@@ -184,6 +193,10 @@ typedef struct tb2_llama_config {
   int lora_targets;
   const double *rope_freq_factors; /* d_head/2 llama3 factors or NULL */
   int attn_impl;                   /* 0: fused flash attention (d_head 64), 1: materialised scores */
+  int lora_per_head_q;             /* 1: toy's LoRA-Q recipe -- one (A_h, B_h) pair per query head, scale 1
+                                      (transformer_block.rb:522-579,861-871); lora_targets must be q only;
+                                      attn_q.lora_a is the A_h stacked [H r][d], attn_q.lora_b the B_h
+                                      stacked [H d_head][r]; needs tb2_set_q8_base_mode(1) */
 } tb2_llama_config;
 
 /* Realize the forward + cross-entropy + backward + AdamW program for a Llama
@@ -195,7 +208,10 @@ int tb2_llama_realize(void *sess, const tb2_llama_config *cfg);
 /* Seeded weights in the reference's draw order (upload_random_init!,
  * llama_seq_engine.rb:1161-1340). std_all > 0 draws every tensor from N(0, std_all)
  * (the frozen base of a QLoRA config, quantised to Q8_0 on upload); LoRA A/B
- * follow from the same stream with the given standard deviations. */
+ * follow from the same stream with the given standard deviations. With
+ * lora_per_head_q the adapters follow upload_lora_q_init!(seed, init_scale)
+ * (llama_seq_engine.rb:2545-2575) instead: lora_a_std is init_scale, every
+ * B_h is 0. */
 int tb2_llama_init_random(void *sess, long long seed, double init_scale, double std_all, double lora_a_std,
                           double lora_b_std);
 
@@ -235,6 +251,16 @@ int tb2_sync(void *sess);
  * device-timed counterpart of the reference's TNN_STEP_PROFILE split
  * (tinynn/tinynn_ggml.c:2054-2103). */
 int tb2_run_steps(void *sess, int n, float *ms);
+/* True gradient accumulation over n_micro micro-batches (1 = off, the
+ * default). Each tnn_compute_backward adds its gradients into an accumulation
+ * arena; every n_micro-th call also runs AdamW on the accumulated sum times
+ * 1/n_micro (times 1/world with data parallelism) and clears the arena. With
+ * equal token counts per micro-batch that is exactly the step on the joined
+ * batch, where the reference approximates accumulation by running AdamW every
+ * micro-batch at lr/N (examples/legacy/06_train_from_scratch.rb:64-78). A
+ * tnn_graph_reset (first step) starts a new window. Returns 0, -1 for
+ * n_micro < 1, -2 before tb2_llama_realize. No counterpart in the reference. */
+int tb2_llama_set_grad_accumulation(void *sess, int n_micro);
 /* One eagerly-enqueued step with an event pair around every kernel: fills
  * kinds[i] (0 GEMM, 1 rmsnorm fwd, 2 rmsnorm bwd, 3 column sums, 4 rope,
  * 5 softmax, 6 swiglu, 7 cross-entropy, 8 loss reduce, 9 AdamW, 10 embedding,
@@ -263,8 +289,45 @@ int tb2_dp_init(void *sess, const void *unique_id, int rank, int world);
 /* Bucket size in floats (default 2^20); every rank must use the same value.
  * Takes effect at the next step (the step graph is re-captured). */
 int tb2_dp_set_bucket_floats(void *sess, long long floats);
-/* Releases the step graph (which holds NCCL work) and then the communicator. */
+/* Releases the step graph (which holds NCCL work) and then the communicator.
+ * Releasing a healthy communicator (NCCL finalize + destroy) is collective
+ * across the node's ranks: all ranks free together. A rank that leaves on its
+ * own calls tb2_dp_abort first, after which this frees local state only. */
 int tb2_dp_free(void *sess);
+
+/* Failure handling (host-side; no GPU is made to fault or hang). The
+ * communicator is created non-blocking (ncclCommInitRankConfig, blocking = 0);
+ * every host wait that depends on a peer polls ncclCommGetAsyncError beside
+ * what it waits for, with a time limit: communicator creation (tb2_dp_init),
+ * the enqueue of a collective, and the end of each step -- tnn_compute_backward
+ * of a data-parallel session returns only once its step (collectives
+ * included) is done, and tb2_run_steps waits for its last step the same way.
+ * An NCCL error or the limit aborts the communicator (ncclCommAbort ends the
+ * collectives still running on this GPU) and returns -3 (NCCL error) or -4
+ * (time limit); from then on the session refuses steps (-2) until
+ * tb2_dp_free. Process-wide limit in milliseconds (default 120000). */
+int tb2_dp_set_timeout_ms(long long ms);
+/* Wait, as above, for the session's step stream to be idle: 0, -3 or -4. */
+int tb2_dp_wait(void *sess);
+/* 0 while the communicator is healthy, else the code that ended it (-3 NCCL
+ * error, -4 time limit, -6 tb2_dp_abort). */
+int tb2_dp_status(void *sess);
+/* Abort the communicator from the host (e.g. when the caller has learnt that
+ * a peer rank is gone): collectives in flight on this GPU end, later steps
+ * are refused. Returns 0, or -2 without data parallelism. */
+int tb2_dp_abort(void *sess);
+/* The gradient buckets the backward all-reduces, in issue order, as
+ * [lo, hi) float ranges of the trainable-gradient arena: layer_lo[l] is the
+ * lowest arena offset of layer l's trainable gradients (non-decreasing in l),
+ * n_train the arena size. The backward finalises layers from the last down
+ * and reduces the pending range once it holds bucket_floats (the final range,
+ * with the embedding and final norm, after the backward). Writes 2 values per
+ * bucket while they fit in cap; returns the bucket count, or -1. Pure host
+ * logic, the same rule the step program runs; no GPU needed. */
+long long tb2_dp_bucket_plan(const long long *layer_lo, int n_layers, long long n_train, long long bucket_floats,
+                             long long *out, long long cap);
+/* The same plan for a realized session's own layout and bucket size. */
+long long tb2_dp_session_bucket_plan(void *sess, long long *out, long long cap);
 
 /* tinynn/tinynn_ggml.h:424 — the next tnn_compute_backward zeroes the Adam moments
  * (of the step program, or of every tnn_opt_step_adamw node of a primitive graph). */
@@ -419,6 +482,116 @@ int tnn_tensor_nelements(void *t);
 const char *tnn_tensor_name(void *t);
 void tnn_tensor_set_name(void *t, const char *name);
 int tnn_tensor_dtype(void *t);
+
+/* ===================================================================== */
+/* Decode with a KV cache (inference forward)                            */
+/* ===================================================================== */
+/* The per-token forward toy's KV engine runs for `toy infer` / `serve`
+ * (lib/toy/llm/engine/llama_kv_engine.rb: build_block_step :1687,
+ * build_attention_qhead_step :2132, SmolLM2KVStepResult.decode_step :2350 /
+ * decode_batch :2381, enable_kv_q8! :359; its fused attention is
+ * tnn_flash_attn_ext, tinynn/tinynn_ggml.c:1583-1598) on the weights of the
+ * session's realised step engine (Q8_0 base or f32, as realised; adapters are
+ * not applied). n_seq sequences (1-8 or 16) decode in lockstep, each with its
+ * own cache of max_T positions; kv_type 0 keeps K and V in f32, 8 in Q8_0
+ * (ggml's quantiser, per head and position in blocks of 32).
+ * Returns 0, -1 for a bad argument, -2 without tb2_llama_realize. */
+int tb2_kv_realize(void *sess, int max_T, int n_seq, int kv_type);
+/* Clear every cache (a new set of sequences). */
+int tb2_kv_reset(void *sess);
+/* One decode step: token[b] at position positions[b] of sequence b (its
+ * cache holds positions 0 .. positions[b] - 1), K / V appended, logits of the
+ * next token for every sequence; copied to logits [n_seq][vocab] when
+ * non-NULL. The first call captures the step as a CUDA graph. */
+int tb2_kv_decode(void *sess, const long long *tokens, const long long *positions, int n_seq, float *logits);
+/* The last step's logits [n_seq][vocab] (n = n_seq * vocab). */
+int tb2_kv_logits(void *sess, float *out, long long n);
+/* steps replays of the last decode step's graph timed by CUDA events (ms);
+ * the kernels launched per step. */
+int tb2_kv_run(void *sess, int steps, float *ms);
+int tb2_kv_launches(void *sess);
+int tb2_kv_free(void *sess);
+
+/* ===================================================================== */
+/* GGUF files (tinynn/tinynn_gguf.h; writer tinynn/tinynn_ggml.h:538-545) */
+/* ===================================================================== */
+/* Host-side: a GGUF v2/v3 reader that maps the file read-only in place and a
+ * writer. The loaders and the checkpoint writer of toy's training runs
+ * (lib/toy/train/toy_gguf_writer.rb) make these calls. */
+
+/* tinynn_gguf.h:89-94 -- the mapping returned by tnn_gguf_mmap_base is
+ * followed by at least this many readable zero bytes past tnn_gguf_mmap_size. */
+#define TNN_GGUF_MMAP_TAIL 4096
+/* tinynn_gguf.h:15 (tinynn_gguf.c:198-280): parse and map; NULL on error. */
+void *tnn_gguf_load(const char *path);
+void tnn_gguf_free(void *handle);
+/* tinynn_gguf.h:45-51: tensor directory (ne0 fastest; ggml type ids: 0 F32,
+ * 1 F16, 8 Q8_0, 30 BF16). */
+int tnn_gguf_n_tensors(void *handle);
+const char *tnn_gguf_tensor_name(void *handle, int i);
+int tnn_gguf_tensor_ne(void *handle, int i, int dim);
+int tnn_gguf_tensor_type(void *handle, int i);
+size_t tnn_gguf_tensor_nbytes(void *handle, int i);
+/* tinynn_gguf.h:61-62: values as doubles (F32, F16, BF16, Q8_0 dequantised:
+ * scale * quant); 0, or -1 on a bad index, type or element count n. */
+int tnn_gguf_read_f32_to_doubles(void *handle, int i, double *out, size_t n);
+int tnn_gguf_tensor_is_quantized(void *handle, int i);
+/* tinynn_gguf.h:67-86: metadata (-1 / 0.0 / NULL when missing or of another type). */
+int tnn_gguf_get_u32(void *handle, const char *key);
+double tnn_gguf_get_f32(void *handle, const char *key);
+int tnn_gguf_get_bool(void *handle, const char *key);
+const char *tnn_gguf_get_str(void *handle, const char *key);
+const char *tnn_gguf_arch_prefix(void *handle);
+/* tinynn_gguf.c:520-554: 1 when 2-D linears are stored ne=[in, out] (the
+ * toy.ggml_native flag, else the stored shape of blk.0.ffn_gate.weight). */
+int tnn_gguf_is_native_layout(void *handle);
+int tnn_gguf_arr_n(void *handle, const char *key);
+const char *tnn_gguf_arr_str(void *handle, const char *key, int i);
+int tnn_gguf_arr_i32(void *handle, const char *key, int i);
+/* tinynn_gguf.h:95-97: the mapped file, its size, a tensor's absolute offset. */
+void *tnn_gguf_mmap_base(void *handle);
+size_t tnn_gguf_mmap_size(void *handle);
+size_t tnn_gguf_tensor_file_offset(void *handle, int i);
+/* tinynn_gguf.h:197: index of a tensor by name, or -1. */
+int tnn_gguf_find_index(void *handle, const char *name);
+/* tinynn_gguf.h:103: a GGUF with one 2x3 f32 tensor "demo.tensor" = 1..6. */
+int tnn_gguf_write_demo_file(const char *path);
+
+/* tinynn_ggml.h:538-545: the checkpoint writer. add_tensor copies a session
+ * tensor to the host when called: a step-program parameter (f32 values, or a
+ * frozen projection's Q8_0 blocks verbatim) or an f32 primitive-graph node. */
+void *tnn_gguf_w_init(void);
+void tnn_gguf_w_set_str(void *ctx, const char *key, const char *val);
+void tnn_gguf_w_set_u32(void *ctx, const char *key, int val);
+void tnn_gguf_w_set_f32(void *ctx, const char *key, double val);
+void tnn_gguf_w_set_bool(void *ctx, const char *key, int val);
+void tnn_gguf_w_add_tensor(void *ctx, void *t);
+int tnn_gguf_w_finalize(void *ctx, const char *path);
+void tnn_gguf_w_free(void *ctx);
+/* Host-data tensors for the writer (no counterpart in the reference): f32
+ * [ne1][ne0], or Q8_0 blocks [ne1][ne0/32*34]. 0 or -1. */
+int tb2_gguf_w_add_f32(void *ctx, const char *name, int ne0, int ne1, const float *data);
+int tb2_gguf_w_add_q8_0(void *ctx, const char *name, int ne0, int ne1, const void *blocks);
+
+/* The step engine's weights from a GGUF (replaces realize_for_mmap's
+ * per-tensor copies, tinynn_gguf.c:612-682, for the fused step): every
+ * parameter is found by its GGUF name; a frozen Q8_0 projection takes the
+ * file's blocks verbatim (split once into the GEMM's quant / scale layout),
+ * f32 / f16 / bf16 / Q8_0 values go to the f32 arenas (Q8_0 dequantised
+ * where the step trains the tensor), toy's legacy transposed layout is
+ * transposed back, adapters absent from the file keep their init, and the
+ * per-head LoRA-Q tensors may come under toy's per-head names
+ * (blk.N.attn_q.head_H.lora_{a,b}.weight). flags bit 0: also load Adam
+ * moments from "<name>.m" / "<name>.v"; bit 1: a partial file (a checkpoint):
+ * tensors it lacks keep their values. Returns the tensor count loaded, -1 for
+ * a missing or mis-shaped tensor (named on stderr), -2 before realize. */
+int tb2_llama_load_gguf(void *sess, void *gguf, int flags);
+/* A checkpoint of the step engine as GGUF v3 with the metadata toy's writer
+ * records: what bit 0 is implied (trainable tensors); bit 1 adds the frozen
+ * tensors (Q8_0 blocks verbatim); bit 2 adds Adam moments as "<name>.m" /
+ * "<name>.v"; bit 3 writes per-head LoRA-Q stacked instead of one pair per
+ * head under toy's names. 0 or negative. */
+int tb2_llama_save_gguf(void *sess, const char *path, int what);
 
 #ifdef __cplusplus
 }

@@ -424,7 +424,8 @@ def qlora_model(cfg: LlamaCfg, lcfg: LoraCfg, seed: int = 42, base_std: float = 
             k = f"blk.{l}.{PNAME[p]}.weight"
             q8[k] = q8_0_quantize(P[k])
             P[k] = q8_0_dequantize(q8[k], P[k].shape[1])
-    L = lora_init(cfg, lcfg, st, seed)
+    # per-head LoRA-Q draws A with init_scale = a_std (upload_lora_q_init!'s init_scale)
+    L = lora_init(cfg, lcfg, st, seed, init_scale=lcfg.a_std if lcfg.per_head_q else 0.01)
     P.update(L)
     mdl = Model(cfg, P, sorted(L.keys()), lora=lcfg, q8=q8)
     mdl.zero_moments()
@@ -474,11 +475,22 @@ def _lora_back(mdl: Model, l: int, p: str, h1, u, dy, grads):
     return du @ A
 
 
+def q8_0_roundtrip(x: np.ndarray) -> np.ndarray:
+    """The values a Q8_0 cache holds for x [..., n] (n % 32 == 0): x narrowed
+    to f32, quantised (ggml's quantiser) and dequantised."""
+    xf = np.ascontiguousarray(x, np.float32)
+    n = xf.shape[-1]
+    return q8_0_dequantize(q8_0_quantize(xf.reshape(-1, n)), n).reshape(x.shape).astype(np.float64)
+
+
 def forward_backward(mdl: Model, ids: np.ndarray, pos: np.ndarray, labels: np.ndarray, T: int, B: int,
-                     want_grads: bool = True, trace: Optional[dict] = None):
+                     want_grads: bool = True, trace: Optional[dict] = None, kv_q8: bool = False):
     """Loss and gradients (float64) of one step. ids/pos/labels have T*B entries,
     token (b, t) at b*T + t; labels are ids (-1 = none) or a dense [N, V] array.
-    When `trace` is a dict it receives the per-layer forward caches and logits."""
+    When `trace` is a dict it receives the per-layer forward caches and logits.
+    kv_q8 (forward only): K (after RoPE) and V pass through a Q8_0 round trip
+    per token and head, as a Q8_0 KV cache stores them (llama_kv_engine.rb
+    enable_kv_q8!)."""
     cfg, P = mdl.cfg, mdl.params
     N, d, H, KV, dh, G = T * B, cfg.d_model, cfg.n_heads, cfg.n_kv, cfg.d_head, cfg.group
     eps = cfg.rms_eps
@@ -509,6 +521,8 @@ def forward_backward(mdl: Model, ids: np.ndarray, pos: np.ndarray, labels: np.nd
         q = rope(qkv["q"].reshape(N, H, dh), cos, sin)
         k = rope(qkv["k"].reshape(N, KV, dh), cos, sin)
         v = qkv["v"].reshape(N, KV, dh)
+        if kv_q8:
+            k, v = q8_0_roundtrip(k).astype(dt), q8_0_roundtrip(v).astype(dt)
         o = np.empty((N, H, dh), dt)
         probs = np.empty((B, H, T, T), dt)
         for b in range(B):

@@ -32,7 +32,7 @@ class LlamaConfigC(C.Structure):
                 ("rms_eps", C.c_double), ("freq_scale", C.c_double), ("tied", C.c_int), ("qkv_bias", C.c_int),
                 ("t_seq", C.c_int), ("t_batch", C.c_int), ("mode", C.c_int), ("lora_rank", C.c_int),
                 ("lora_alpha", C.c_double), ("lora_targets", C.c_int),
-                ("rope_freq_factors", C.POINTER(C.c_double)), ("attn_impl", C.c_int)]
+                ("rope_freq_factors", C.POINTER(C.c_double)), ("attn_impl", C.c_int), ("lora_per_head_q", C.c_int)]
 
 
 _lib = None
@@ -66,10 +66,17 @@ _SIGS = [
     ("tb2_sync", I, [VP]),
     ("tb2_debug_activation", LL, [VP, I, I, C.POINTER(C.c_float), LL]),
     ("tb2_run_steps", I, [VP, I, C.POINTER(C.c_float)]),
+    ("tb2_llama_set_grad_accumulation", I, [VP, I]),
     ("tb2_nccl_unique_id", I, [VP, SZ]),
     ("tb2_dp_init", I, [VP, VP, I, I]),
     ("tb2_dp_free", I, [VP]),
     ("tb2_dp_set_bucket_floats", I, [VP, LL]),
+    ("tb2_dp_set_timeout_ms", I, [LL]),
+    ("tb2_dp_wait", I, [VP]),
+    ("tb2_dp_status", I, [VP]),
+    ("tb2_dp_abort", I, [VP]),
+    ("tb2_dp_bucket_plan", LL, [C.POINTER(C.c_longlong), I, LL, LL, C.POINTER(C.c_longlong), LL]),
+    ("tb2_dp_session_bucket_plan", LL, [VP, C.POINTER(C.c_longlong), LL]),
     ("tb2_profile_step", I, [VP, I, C.POINTER(C.c_int), C.POINTER(C.c_float), C.POINTER(C.c_double), I]),
     ("tnn_graph_reset", I, [VP]),
     ("tnn_graph_reset_grads_only", I, [VP]),
@@ -90,6 +97,7 @@ _SIGS = [
                            C.POINTER(Epilogue), C.c_int, C.c_int, C.c_void_p]),
     ("tb2_gemm_noalloc", C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(Operand),
                                    C.POINTER(Operand), C.POINTER(Epilogue), C.c_int, C.c_int, C.c_void_p]),
+    ("tb2_gemm_noalloc_error", C.c_int, []),
     ("tb2_split_f32", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
     ("tb2_gemm_set_pair_mode", C.c_int, [C.c_int]),
     ("tb2_set_q8_base_mode", C.c_int, [C.c_int]),
@@ -186,6 +194,49 @@ _SIGS = [
     ("tnn_scratch_sum_abs_f32", D, [VP, I]),
     ("tnn_scratch_nan_count_f32", I, [VP, I]),
     ("tnn_upload_transposed_f64", I, [VP, VP, DP, I, I]),
+    # GGUF files
+    ("tnn_gguf_load", VP, [C.c_char_p]),
+    ("tnn_gguf_free", None, [VP]),
+    ("tnn_gguf_n_tensors", I, [VP]),
+    ("tnn_gguf_tensor_name", C.c_char_p, [VP, I]),
+    ("tnn_gguf_tensor_ne", I, [VP, I, I]),
+    ("tnn_gguf_tensor_type", I, [VP, I]),
+    ("tnn_gguf_tensor_nbytes", SZ, [VP, I]),
+    ("tnn_gguf_read_f32_to_doubles", I, [VP, I, DP, SZ]),
+    ("tnn_gguf_tensor_is_quantized", I, [VP, I]),
+    ("tnn_gguf_get_u32", I, [VP, C.c_char_p]),
+    ("tnn_gguf_get_f32", D, [VP, C.c_char_p]),
+    ("tnn_gguf_get_bool", I, [VP, C.c_char_p]),
+    ("tnn_gguf_get_str", C.c_char_p, [VP, C.c_char_p]),
+    ("tnn_gguf_arch_prefix", C.c_char_p, [VP]),
+    ("tnn_gguf_is_native_layout", I, [VP]),
+    ("tnn_gguf_arr_n", I, [VP, C.c_char_p]),
+    ("tnn_gguf_arr_str", C.c_char_p, [VP, C.c_char_p, I]),
+    ("tnn_gguf_arr_i32", I, [VP, C.c_char_p, I]),
+    ("tnn_gguf_mmap_base", VP, [VP]),
+    ("tnn_gguf_mmap_size", SZ, [VP]),
+    ("tnn_gguf_tensor_file_offset", SZ, [VP, I]),
+    ("tnn_gguf_find_index", I, [VP, C.c_char_p]),
+    ("tnn_gguf_write_demo_file", I, [C.c_char_p]),
+    ("tnn_gguf_w_init", VP, []),
+    ("tnn_gguf_w_set_str", None, [VP, C.c_char_p, C.c_char_p]),
+    ("tnn_gguf_w_set_u32", None, [VP, C.c_char_p, I]),
+    ("tnn_gguf_w_set_f32", None, [VP, C.c_char_p, D]),
+    ("tnn_gguf_w_set_bool", None, [VP, C.c_char_p, I]),
+    ("tnn_gguf_w_add_tensor", None, [VP, VP]),
+    ("tnn_gguf_w_finalize", I, [VP, C.c_char_p]),
+    ("tnn_gguf_w_free", None, [VP]),
+    ("tb2_gguf_w_add_f32", I, [VP, C.c_char_p, I, I, C.POINTER(C.c_float)]),
+    ("tb2_gguf_w_add_q8_0", I, [VP, C.c_char_p, I, I, VP]),
+    ("tb2_llama_load_gguf", I, [VP, VP, I]),
+    ("tb2_kv_realize", I, [VP, I, I, I]),
+    ("tb2_kv_reset", I, [VP]),
+    ("tb2_kv_decode", I, [VP, C.POINTER(C.c_longlong), C.POINTER(C.c_longlong), I, C.POINTER(C.c_float)]),
+    ("tb2_kv_logits", I, [VP, C.POINTER(C.c_float), LL]),
+    ("tb2_kv_run", I, [VP, I, C.POINTER(C.c_float)]),
+    ("tb2_kv_launches", I, [VP]),
+    ("tb2_kv_free", I, [VP]),
+    ("tb2_llama_save_gguf", I, [VP, C.c_char_p, I]),
 ]
 
 

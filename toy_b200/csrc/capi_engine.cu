@@ -85,6 +85,7 @@ int tb2_llama_realize(void* sess, const tb2_llama_config* cfg) {
   c.tied = cfg->tied; c.qkv_bias = cfg->qkv_bias; c.T = cfg->t_seq; c.B = cfg->t_batch; c.mode = cfg->mode;
   c.lora_rank = cfg->lora_rank; c.lora_alpha = (float)cfg->lora_alpha; c.lora_targets = cfg->lora_targets;
   c.attn_impl = cfg->attn_impl;
+  c.lora_per_head_q = cfg->lora_per_head_q;
   if (cfg->rope_freq_factors)
     for (int i = 0; i < cfg->d_head / 2; ++i) c.freq_factors.push_back((float)cfg->rope_freq_factors[i]);
   if (cudaSetDevice(s->device) != cudaSuccess) return -3;
@@ -203,6 +204,11 @@ int tb2_forward_only(void* sess) {
   return S(sess)->eng->forward_only();
 }
 
+int tb2_llama_set_grad_accumulation(void* sess, int n_micro) {
+  if (!sess || !S(sess)->eng) return -2;
+  return S(sess)->eng->set_grad_accumulation(n_micro);
+}
+
 int tb2_run_steps(void* sess, int n, float* ms) {
   if (!sess || !S(sess)->eng) return -2;
   return S(sess)->eng->run_steps(n, ms);
@@ -238,9 +244,13 @@ int tnn_compute_backward(void* sess) {
   if (!sess) return -1;
   Session* s = S(sess);
   if (!s->eng) return s->bwd_built ? tb2::prim_compute_backward(s) : -2;
+  if (s->dp && tb2::dp_status(s)) return -2;   // its communicator was aborted: no more steps
   const bool first = s->first_pending;
   s->first_pending = false;
-  return s->eng->step(first, true);
+  const int rc = s->eng->step(first, true);
+  // a data-parallel step waits for its collectives with a time limit, so a
+  // rank that never joins ends the step with an error instead of a hang
+  return rc ? rc : (s->dp ? tb2::dp_wait_step(s) : 0);
 }
 
 // ------------------------------------------------------------------ tensor I/O

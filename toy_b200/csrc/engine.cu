@@ -119,7 +119,8 @@ LlamaEngine::LlamaEngine(const LlamaConfig& cfg, int device) : cfg_(cfg), device
 LlamaEngine::~LlamaEngine() {
   cudaSetDevice(device_);
   if (graph_) cudaGraphExecDestroy(graph_);
-  for (DeviceBuf* b : {&p32_, &phi_, &plo_, &g_, &m_, &v_, &q8_, &q8v_, &q8s_, &q8pl_, &wsc_ws_})
+  if (graph_acc_) cudaGraphExecDestroy(graph_acc_);
+  for (DeviceBuf* b : {&p32_, &phi_, &plo_, &g_, &m_, &v_, &q8_, &q8v_, &q8s_, &q8pl_, &wsc_ws_, &acc_})
     if (b->p) cudaFree(b->p);
   for (auto& b : bufs_)
     if (b.p) cudaFree(b.p);
@@ -151,11 +152,10 @@ int LlamaEngine::bucket_begin() {
 // the step stream itself. Every rank runs the same bucket sequence.
 int LlamaEngine::bucket_ready(long long lo, bool flush) {
   if (!allreduce_fn_) return 0;
-  pend_lo_ = std::min(pend_lo_, lo);
-  if (pend_hi_ <= pend_lo_ || (!flush && pend_hi_ - pend_lo_ < bucket_floats_)) return 0;
-  float* buf = grad_arena() + pend_lo_;
-  const long long n = pend_hi_ - pend_lo_;
-  pend_hi_ = pend_lo_;
+  long long b_lo = 0, b_hi = 0;
+  if (!bucket_take(pend_lo_, pend_hi_, lo, flush, bucket_floats_, b_lo, b_hi)) return 0;
+  float* buf = grad_arena() + b_lo;
+  const long long n = b_hi - b_lo;
   if (profiling_) {
     prof_begin(kKAllreduce, 0.0);
     const int rc = allreduce_fn_(allreduce_ctx_, buf, n, stream_);
@@ -227,6 +227,8 @@ int LlamaEngine::realize() {
   // fused attention masks ragged tiles and takes any T
   if (c.T % 64 && !(c.attn_impl == 0 && flash_supported(c.d_head))) return -1;
   if (c.mode == 1 && (c.lora_rank <= 0 || c.lora_rank > kLoraMaxRank || c.lora_targets == 0)) return -1;
+  per_head_ = c.mode == 1 && c.lora_per_head_q;
+  if (per_head_ && (c.lora_targets != (1 << kLoraQ) || g_q8_base_mode != 1)) return -1;
   CU(cudaSetDevice(device_));
   // Adapter steps: the activation / activation-gradient chain is the critical
   // path and the second stream carries light work (adapter weight gradients,
@@ -258,7 +260,7 @@ int LlamaEngine::realize() {
                              : (t == kLoraO || t == kLoraDown) ? d : ff;
         const int cols_in = t == kLoraO ? H * dh : t == kLoraDown ? ff : d;
         const std::string pre = "blk." + std::to_string(l) + "." + kProjName[t];
-        add_param(pre + ".lora_a", r, cols_in, true, false);
+        add_param(pre + ".lora_a", (per_head_ && t == kLoraQ) ? H * r : r, cols_in, true, false);
         add_param(pre + ".lora_b", rows_out, r, true, false);
       }
   }
@@ -328,6 +330,7 @@ int LlamaEngine::realize() {
       const LoraGroup G = lora_group(g);
       const bool fold = G.n && lora_grouped(rg.d_in);
       rg.ext = fold ? 64 : 0;
+      if (per_head_ && g == kGroupQKV) rg.ext = (H * r + 63) / 64 * 64;   // the H r columns of u
       ext_[g] = rg.ext;
       rg.off = slot;
       slot += ((long long)(rg.d_out + rg.ext) * (rg.d_in + rg.ext) + 127) / 128 * 128;
@@ -372,7 +375,7 @@ int LlamaEngine::realize() {
   }
 
   const int N = this->N(), T = c.T, B = c.B, W = (H + 2 * KV) * dh;
-  if (full) {   // split-K workspace of the weight-gradient GEMMs on wst_
+  if (full || per_head_) {   // split-K workspace of the weight-gradient GEMMs on wst_
     wsc_.ws_floats = gemm_scratch().ws_floats;
     CK(alloc(wsc_ws_, (size_t)wsc_.ws_floats * sizeof(float)));
     wsc_.ws = static_cast<float*>(wsc_ws_.p);
@@ -461,6 +464,7 @@ int LlamaEngine::realize() {
     lora_part_ = f32(part);
     lora_part2_ = f32(part);
   }
+  if (per_head_) bd_dense_ = f32((long long)H * dh * H * r);
   hp_ = f32(8);
   bufs_.emplace_back();
   CK(alloc(bufs_.back(), (size_t)N * 4 * 5 + 64));
@@ -573,6 +577,14 @@ Operand LlamaEngine::wop(const Param& p, int rows, int cols, long long ld, int m
   return o;
 }
 
+Planes LlamaEngine::ring_ext_b(int l) const {
+  const int slot = l & 1;
+  if (!q8_planes_ || ring_layer_[slot] != l) return Planes{};
+  const RingGroup& rg = ring_[kGroupQKV];
+  bf16* base = static_cast<bf16*>(q8pl_.p) + (long long)slot * 2 * q8_slot_elems_ + rg.off + rg.d_in;
+  return Planes{base, base + q8_slot_elems_};
+}
+
 int LlamaEngine::set_param_q8(const std::string& name, const uint8_t* blocks, long long nbytes) {
   const Param* p = find(name);
   if (!p || !p->q8 || !blocks || nbytes != p->numel() / 32 * 34) return -1;
@@ -626,6 +638,16 @@ int LlamaEngine::get_moment(const std::string& name, int which, float* host, lon
   CU(cudaStreamSynchronize(stream_));
   const float* src = static_cast<float*>(which == 0 ? m_.p : v_.p) + p->offset;
   CU(cudaMemcpy(host, src, n * 4, cudaMemcpyDeviceToHost));
+  return 0;
+}
+
+int LlamaEngine::set_moment(const std::string& name, int which, const float* host, long long n) {
+  const Param* p = find(name);
+  if (!p || !host || n != p->numel() || !p->trainable || which < 0 || which > 1) return -1;
+  CU(cudaStreamSynchronize(stream_));
+  float* dst = static_cast<float*>(which == 0 ? m_.p : v_.p) + p->offset;
+  CU(cudaMemcpyAsync(dst, host, n * 4, cudaMemcpyHostToDevice, stream_));
+  CU(cudaStreamSynchronize(stream_));
   return 0;
 }
 
@@ -683,7 +705,26 @@ int LlamaEngine::init_random(long long seed, double init_scale, double std_all, 
       CK(fill(pre + "attn_v.bias", sb));
     }
   }
-  if (c.mode == 1) {
+  if (per_head_) {
+    // upload_lora_q_init! (llama_seq_engine.rb:2545-2575): the raw seed drives
+    // the LCG (no fold, no warm-up), two draws per A element, cos branch only,
+    // A = init_scale N(0, 1) (init_scale arrives as lora_a_std), every B_h = 0
+    const int r = c.lora_rank;
+    uint64_t s = (uint64_t)seed & kMask;
+    for (int l = 0; l < c.n_layers; ++l) {
+      const std::string pre = "blk." + std::to_string(l) + ".attn_q";
+      std::vector<float> A((size_t)H * r * d), Bz((size_t)H * dh * r, 0.0f);
+      for (size_t i = 0; i < A.size(); ++i) {
+        s = lcg_next(s);
+        const double u1 = ((double)s + 1.0) / 2147483648.0;
+        s = lcg_next(s);
+        const double u2 = ((double)s + 1.0) / 2147483648.0;
+        A[i] = (float)(lora_a_std * std::sqrt(-2.0 * std::log(u1)) * std::cos(2.0 * M_PI * u2));
+      }
+      CK(set_param(pre + ".lora_a", A.data(), (long long)A.size()));
+      CK(set_param(pre + ".lora_b", Bz.data(), (long long)Bz.size()));
+    }
+  } else if (c.mode == 1) {
     for (int l = 0; l < c.n_layers; ++l)
       for (int t = 0; t < kLoraCount; ++t) {
         if (!(c.lora_targets & (1 << t))) continue;
@@ -1003,7 +1044,17 @@ int LlamaEngine::build_ring(long long qvoff) {
       M.d_out = rg.d_out; M.d_in = rg.d_in; M.ext = rg.ext; M.r = c.lora_rank; M.s = s;
       M.chunk0 = chunk;
       chunk += (long long)(rg.d_out + rg.ext) * (rg.d_in + rg.ext) / 16;
-      if (rg.ext) {
+      if (per_head_ && g == kGroupQKV) {   // the per-head LoRA-Q pairs as one block-diagonal adapter
+        const std::string pre = "blk." + std::to_string(l) + ".attn_q";
+        RingAdapter& a = M.ad[M.n_ad++];
+        a.A = P32(P(pre + ".lora_a"));
+        a.B = P32(P(pre + ".lora_b"));
+        a.c0 = 0;
+        a.width = c.n_heads * c.d_head;
+        M.bd_r = c.lora_rank;
+        M.bd_w = c.d_head;
+        M.s = 1.0f;
+      } else if (rg.ext) {
         const LoraGroup G = lora_group(g);
         if (G.n > 3 || c.lora_rank > 16) return -1;
         for (int i = 0; i < G.n; ++i) {
@@ -1066,7 +1117,7 @@ LlamaEngine::LoraGroup LlamaEngine::lora_group(int g) const {
   const int d = c.d_model, H = c.n_heads, KV = c.n_kv, dh = c.d_head, ff = c.d_ff;
   LoraGroup G;
   auto add = [&](int t, int c0, int w) {
-    if (c.mode == 1 && (c.lora_targets & (1 << t))) {
+    if (c.mode == 1 && (c.lora_targets & (1 << t)) && !(per_head_ && t == kLoraQ)) {
       G.t[G.n] = t; G.c0[G.n] = c0; G.w[G.n] = w;
       ++G.n;
     }
@@ -1202,6 +1253,16 @@ int LlamaEngine::enqueue_forward() {
     const LoraGroup Gq = lora_group(kGroupQKV);
     const int eq = ext_[kGroupQKV];   // q|k|v adapters folded into the GEMM as extra reduction columns
     CK(rmsnorm_lora(l, x_[l], P32(P(pre + "attn_norm.weight")), h1_[l], Gq, d + eq));   // + the adapters' u
+    if (per_head_) {   // u = h A^T of every head's pair, as planes into h's extension columns
+      GemmDesc gu;
+      gu.M = N; gu.N = H * c.lora_rank; gu.K = d;
+      gu.a = op(h1_[l], N, d, d + eq, 0);
+      gu.b = op(PP(P(pre + "attn_q.lora_a")), H * c.lora_rank, d, d, 0);
+      gu.epi = epi_rowmajor(kEpiStoreSplit, nullptr, d + eq);
+      gu.epi.out_hi = h1_[l].hi + d;
+      gu.epi.out_lo = h1_[l].lo + d;
+      CK(gemm(gu));
+    }
     GemmDesc g;
     g.M = N; g.N = W; g.K = d + eq;
     g.a = op(h1_[l], N, d + eq, d + eq, 0);
@@ -1499,7 +1560,35 @@ int LlamaEngine::enqueue_backward() {
     const LoraGroup Gq = lora_group(kGroupQKV);
     const bool gq_grp = Gq.n && lora_grouped(d);
     if (gq_grp) CK(lora_group_du(l, Gq, dqkv_, W + eq, d, gx.epi, eq ? W : -1));
+    const int Rq = H * c.lora_rank;
+    if (per_head_) {   // du = dY_q B (block-diagonal B from the ring operand) into dY's extension columns
+      GemmDesc gdu;
+      gdu.M = N; gdu.N = Rq; gdu.K = H * dh;
+      gdu.a = op(dqkv_, N, H * dh, W + eq, 0);
+      gdu.b = op(ring_ext_b(l), H * dh, Rq, d + eq, 1);
+      gdu.epi = epi_rowmajor(kEpiStoreSplit, nullptr, W + eq);
+      gdu.epi.out_hi = dqkv_.hi + W;
+      gdu.epi.out_lo = dqkv_.lo + W;
+      CK(gemm(gdu));
+    }
     CK(gemm(gx));
+    if (per_head_) {   // dA = du^T h and the diagonal blocks of dY_q^T u, on the weight-gradient stream
+      CK(fork_side());
+      GemmDesc ga;
+      ga.M = Rq; ga.N = d; ga.K = N;
+      ga.a = op(offset(dqkv_, W), N, Rq, W + eq, 1);
+      ga.b = op(h1_[l], N, d, d + eq, 1);
+      ga.epi = epi_rowmajor(kEpiStoreF32, G32(P(pre + "attn_q.lora_a")), d);
+      CK(gemm_side(ga));
+      GemmDesc gb;
+      gb.M = H * dh; gb.N = Rq; gb.K = N;
+      gb.a = op(dqkv_, N, H * dh, W + eq, 1);
+      gb.b = op(offset(h1_[l], d), N, Rq, d + eq, 1);
+      gb.epi = epi_rowmajor(kEpiStoreF32, bd_dense_, Rq);
+      CK(gemm_side(gb));
+      KL(launch_lora_blockdiag_take(bd_dense_, H, dh, c.lora_rank, G32(P(pre + "attn_q.lora_b")), sst()));
+      CK(side_read(t_dqkv_));
+    }
     if (gq_grp || full) {
       CK(fork_side());
       if (gq_grp) CK(lora_group_wgrad(l, Gq, h1_[l], d + eq, d, dqkv_, W + eq));
@@ -1520,7 +1609,12 @@ int LlamaEngine::enqueue_backward() {
     CK(bucket_ready(layer_grad_lo_[l], false));   // this layer's gradients are final
   }
   CK(join_side());   // the embedding scatter adds to the LM head's (tied) gradient
-  if (full) KL(launch_embed_scatter(dx_, ord_, seg_start_, seg_id_, nseg_dev_, N, G32(E), d, stream_));
+  if (full) {
+    // the scatter adds onto the embedding's gradient: the tied LM head's dW
+    // GEMM wrote it above; an untied embedding starts from zero every step
+    if (!c.tied) CU(cudaMemsetAsync(G32(E), 0, (size_t)E.numel() * 4, stream_));
+    KL(launch_embed_scatter(dx_, ord_, seg_start_, seg_id_, nseg_dev_, N, G32(E), d, stream_));
+  }
   CK(bucket_ready(0, true));
   CK(bucket_join());
   side_ = false;
@@ -1529,18 +1623,35 @@ int LlamaEngine::enqueue_backward() {
 
 int LlamaEngine::enqueue_optimizer() {
   Planes pp{static_cast<bf16*>(phi_.p), static_cast<bf16*>(plo_.p)};
-  KL(launch_adamw(static_cast<float*>(p32_.p), static_cast<float*>(g_.p), static_cast<float*>(m_.p),
-                  static_cast<float*>(v_.p), pp, n_train_, hp_, grad_scale_, stream_));
+  const bool acc = accum_ > 1;
+  float* g = static_cast<float*>(acc ? acc_.p : g_.p);
+  KL(launch_adamw(static_cast<float*>(p32_.p), g, static_cast<float*>(m_.p), static_cast<float*>(v_.p), pp, n_train_,
+                  hp_, grad_scale_ / (float)accum_, stream_));
+  if (acc) CU(cudaMemsetAsync(acc_.p, 0, acc_.bytes, stream_));   // the next window starts empty
   return 0;
 }
 
-int LlamaEngine::enqueue_step(bool run_optimizer) {
+int LlamaEngine::enqueue_step(bool run_optimizer, bool accumulate) {
   counting_ = 0;
   CK(bucket_begin());
   CK(enqueue_forward());
   CK(enqueue_backward());
+  if (accumulate)
+    KL(launch_add_inplace(static_cast<float*>(acc_.p), static_cast<const float*>(g_.p), n_train_, stream_));
   if (run_optimizer) CK(enqueue_optimizer());
   launches_ = counting_;
+  return 0;
+}
+
+int LlamaEngine::set_grad_accumulation(int n) {
+  if (!realized_ || n < 1) return -1;
+  CU(cudaSetDevice(device_));
+  if (n > 1 && !acc_.p) CK(alloc(acc_, (size_t)std::max<long long>(n_train_, 64) * 4));
+  if (acc_.p) CU(cudaMemsetAsync(acc_.p, 0, acc_.bytes, stream_));
+  accum_ = n;
+  micro_ = 0;
+  graph_valid_ = graph_acc_valid_ = false;
+  CU(cudaStreamSynchronize(stream_));
   return 0;
 }
 
@@ -1550,32 +1661,44 @@ int LlamaEngine::step(bool is_first, bool run_optimizer) {
   if (is_first) {
     CU(cudaMemsetAsync(m_.p, 0, m_.bytes, stream_));
     CU(cudaMemsetAsync(v_.p, 0, v_.bytes, stream_));
+    if (accum_ > 1) {   // a new accumulation window
+      CU(cudaMemsetAsync(acc_.p, 0, acc_.bytes, stream_));
+      micro_ = 0;
+    }
   }
-  // The embedding scatter's segment count is baked into a captured graph.
+  // With gradient accumulation every step adds into the arena and the last
+  // micro-batch of the window runs the optimiser; the accumulating steps
+  // replay a graph of their own.
+  const bool acc = accum_ > 1 && run_optimizer;
+  const bool opt = run_optimizer && (!acc || micro_ == accum_ - 1);
+  if (acc) micro_ = opt ? 0 : micro_ + 1;
+  cudaGraphExec_t& gx = (acc && !opt) ? graph_acc_ : graph_;
+  bool& gvalid = (acc && !opt) ? graph_acc_valid_ : graph_valid_;
+  bool& gdense = (acc && !opt) ? graph_acc_dense_ : graph_dense_;
   const bool can_graph = use_graph_ && run_optimizer;
-  if (can_graph && graph_valid_ && graph_dense_ == dense_labels_) {
-    CU(cudaGraphLaunch(graph_, stream_));
+  if (can_graph && gvalid && gdense == dense_labels_) {
+    CU(cudaGraphLaunch(gx, stream_));
     return 0;
   }
-  if (!can_graph) return enqueue_step(run_optimizer);
+  if (!can_graph) return enqueue_step(opt, acc);
   // First use of this configuration: run eagerly once (validates every launch),
   // then capture the same program for replay.
-  CK(enqueue_step(run_optimizer));
+  CK(enqueue_step(opt, acc));
   cudaGraph_t g = nullptr;
   CU(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
-  const int rc = enqueue_step(run_optimizer);
+  const int rc = enqueue_step(opt, acc);
   cudaError_t ce = cudaStreamEndCapture(stream_, &g);
   if (rc || ce != cudaSuccess) {
     if (g) cudaGraphDestroy(g);
     return rc ? rc : -3;
   }
-  if (graph_) cudaGraphExecDestroy(graph_);
-  graph_ = nullptr;
-  ce = cudaGraphInstantiate(&graph_, g, cudaGraphInstantiateFlagUseNodePriority);
+  if (gx) cudaGraphExecDestroy(gx);
+  gx = nullptr;
+  ce = cudaGraphInstantiate(&gx, g, cudaGraphInstantiateFlagUseNodePriority);
   cudaGraphDestroy(g);
   CU(ce);
-  graph_valid_ = true;
-  graph_dense_ = dense_labels_;
+  gvalid = true;
+  gdense = dense_labels_;
   return 0;
 }
 
@@ -1589,6 +1712,14 @@ int LlamaEngine::run_steps(int n, float* ms) {
   CU(cudaEventRecord(a, stream_));
   for (int i = 0; i < n; ++i) CK(step(false, true));
   CU(cudaEventRecord(b, stream_));
+  if (wait_fn_) {
+    const int rc = wait_fn_(wait_ctx_, b);
+    if (rc) {
+      cudaEventDestroy(a);
+      cudaEventDestroy(b);
+      return rc;
+    }
+  }
   CU(cudaEventSynchronize(b));
   CU(cudaEventElapsedTime(ms, a, b));
   cudaEventDestroy(a);
@@ -1606,7 +1737,7 @@ int LlamaEngine::profile_step(bool is_first, int* kinds, float* ms, double* flop
   profiling_ = true;
   recs_.clear();
   evnext_ = 0;
-  const int rc = enqueue_step(true);
+  const int rc = enqueue_step(true, accum_ > 1);
   profiling_ = false;
   CK(rc);
   CU(cudaStreamSynchronize(stream_));

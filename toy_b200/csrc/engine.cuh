@@ -27,6 +27,11 @@ struct LlamaConfig {
   int lora_targets = 0;   // bitmask over LoraTarget
   std::vector<float> freq_factors;   // d_head/2 llama3-style factors, or empty
   int attn_impl = 0;      // 0: fused flash attention where supported, 1: materialised scores
+  // 1: the reference's LoRA-Q (lora_targets = q only): one (A_h [r][d], B_h
+  // [d_head][r]) pair per query head, no alpha / r scale, stored stacked as
+  // attn_q.lora_a [H r][d] and attn_q.lora_b [H d_head][r]; needs the Q8_0
+  // plane ring (base mode 1)
+  int lora_per_head_q = 0;
 };
 
 // One named parameter inside the arenas.
@@ -78,6 +83,7 @@ class LlamaEngine {
   int get_param(const std::string& name, float* host, long long n);
   int get_grad(const std::string& name, float* host, long long n);
   int get_moment(const std::string& name, int which, float* host, long long n);
+  int set_moment(const std::string& name, int which, const float* host, long long n);
   int set_param_q8(const std::string& name, const uint8_t* blocks, long long nbytes);
   int get_param_q8(const std::string& name, uint8_t* blocks, long long nbytes);
   // Standard deviations stay f64 end to end: the reference draws in f64 and
@@ -104,17 +110,78 @@ class LlamaEngine {
   void set_allreduce_hook(int (*fn)(void*, float*, long long, cudaStream_t), void* ctx) {
     allreduce_fn_ = fn;
     allreduce_ctx_ = ctx;
-    graph_valid_ = false;
+    graph_valid_ = graph_acc_valid_ = false;
   }
-  void set_use_graph(bool on) { use_graph_ = on; graph_valid_ = false; }
+  // Host wait for the end of a timed run when collectives are in flight: the
+  // data-parallel layer polls the event next to its communicator, with a time
+  // limit, instead of blocking (0 done, else an error code).
+  void set_wait_hook(int (*fn)(void*, cudaEvent_t), void* ctx) {
+    wait_fn_ = fn;
+    wait_ctx_ = ctx;
+  }
+  void set_use_graph(bool on) {
+    use_graph_ = on;
+    graph_valid_ = graph_acc_valid_ = false;
+  }
+  // Gradient accumulation over n micro-batches (n >= 1; 1 = off): every step
+  // adds its gradients into an accumulation arena and only every n-th step
+  // runs AdamW, on the accumulated sum times 1/n (times 1/world with data
+  // parallelism), then clears the arena. With equal token counts per
+  // micro-batch this is the step on the joined batch. A first step
+  // (is_first) starts a new window.
+  int set_grad_accumulation(int n);
+  int grad_accumulation() const { return accum_; }
+  int micro_index() const { return micro_; }
+  // Gradient buckets. bucket_take is the decision rule of the backward: the
+  // gradients at arena offsets >= lo are final; the pending range [pend_lo,
+  // pend_hi) becomes a bucket [b_lo, b_hi) once it holds min_floats (or on the
+  // final flush). Pure host logic, shared with the data-parallel layer's plan.
+  static bool bucket_take(long long& pend_lo, long long& pend_hi, long long lo, bool flush, long long min_floats,
+                          long long& b_lo, long long& b_hi) {
+    pend_lo = pend_lo < lo ? pend_lo : lo;
+    if (pend_hi <= pend_lo || (!flush && pend_hi - pend_lo < min_floats)) return false;
+    b_lo = pend_lo;
+    b_hi = pend_hi;
+    pend_hi = pend_lo;
+    return true;
+  }
+  const std::vector<long long>& layer_grad_lo() const { return layer_grad_lo_; }
+  // Read-only views for the decode engine, which shares this engine's weights:
+  // a frozen Q8_0 projection as its quants [rows][cols] and fp16 scale bits
+  // [rows][cols / 32], any other parameter as its f32 values.
+  struct WeightView {
+    const float* f32 = nullptr;
+    const int8_t* qv = nullptr;
+    const uint16_t* qs = nullptr;
+    int rows = 0, cols = 0;
+  };
+  WeightView weight(const std::string& name) const {
+    WeightView w;
+    const Param* p = find(name);
+    if (!p) return w;
+    w.rows = p->rows;
+    w.cols = p->cols;
+    if (p->q8) {
+      w.qv = static_cast<const int8_t*>(q8v_.p) + p->q8v_offset;
+      w.qs = static_cast<const uint16_t*>(q8s_.p) + p->q8s_offset;
+    } else {
+      w.f32 = static_cast<const float*>(p32_.p) + p->offset;
+    }
+    return w;
+  }
+  const float* rope_table() const { return cs_; }   // [rope_rows][d_head / 2] (cos, sin) pairs
+  int rope_rows() const { return cs_rows_; }
+  int device() const { return device_; }
+  long long bucket_floats() const { return bucket_floats_; }
   void set_bucket_floats(long long n) {
     bucket_floats_ = n;
-    graph_valid_ = false;
+    graph_valid_ = graph_acc_valid_ = false;
   }
   void drop_graph() {
     if (graph_) cudaGraphExecDestroy(graph_);
-    graph_ = nullptr;
-    graph_valid_ = false;
+    if (graph_acc_) cudaGraphExecDestroy(graph_acc_);
+    graph_ = graph_acc_ = nullptr;
+    graph_valid_ = graph_acc_valid_ = false;
   }
   int launches_per_step() const { return launches_; }
   // Copy a saved activation of the last step to the host as f32 (planes are
@@ -136,7 +203,9 @@ class LlamaEngine {
   int enqueue_forward();
   int enqueue_backward();
   int enqueue_optimizer();
-  int enqueue_step(bool run_optimizer);
+  // accumulate: add this step's gradients into the accumulation arena;
+  // run_optimizer: AdamW (on the arena when accumulating)
+  int enqueue_step(bool run_optimizer, bool accumulate = false);
   int gemm(const GemmDesc& d);
   // Weight gradients (dW GEMMs, adapter dA / dB) feed only the optimiser, so
   // the backward runs them on a second stream, side by side with the chain of
@@ -185,6 +254,13 @@ class LlamaEngine {
   // backward, after it: dB and dA of every adapter (partials + fixed-order sum)
   int lora_group_wgrad(int l, const LoraGroup& G, Planes X, long long ldx, int d_in, Planes dY, long long ld_dy);
   bool lora_grouped(int d_in) const { return cfg_.lora_rank <= 16 && d_in % 32 == 0; }
+  // Per-head LoRA-Q: the block-diagonal adapter rides the q|k|v GEMMs as extra
+  // reduction columns (u = h A^T into h's, du = dY_q B into dY's); dA and dB
+  // are tensor-core products on the weight-gradient stream, dB through a dense
+  // [H d_head][H r] product whose diagonal blocks are kept.
+  bool per_head_ = false;
+  float* bd_dense_ = nullptr;
+  Planes ring_ext_b(int l) const;   // B's extension block of block l's q|k|v ring operand
   float* P32(const Param& p) { return static_cast<float*>(p32_.p) + p.offset; }
   float* G32(const Param& p) { return static_cast<float*>(g_.p) + p.offset; }
   Planes PP(const Param& p) {
@@ -282,6 +358,8 @@ class LlamaEngine {
   float grad_scale_ = 1.0f;
   int (*allreduce_fn_)(void*, float*, long long, cudaStream_t) = nullptr;
   void* allreduce_ctx_ = nullptr;
+  int (*wait_fn_)(void*, cudaEvent_t) = nullptr;
+  void* wait_ctx_ = nullptr;
   // Gradient buckets: the backward finalises the arena from the top down (layer
   // L-1 first); every range of at least bucket_floats_ finished floats is reduced
   // on comm_stream_ while the backward continues, the rest after the backward.
@@ -300,6 +378,12 @@ class LlamaEngine {
   cudaGraphExec_t graph_ = nullptr;
   bool graph_valid_ = false;
   bool graph_dense_ = false;
+  // gradient accumulation: the arena, the window length and the position in it;
+  // the steps that only accumulate replay their own graph
+  int accum_ = 1, micro_ = 0;
+  DeviceBuf acc_;
+  cudaGraphExec_t graph_acc_ = nullptr;
+  bool graph_acc_valid_ = false, graph_acc_dense_ = false;
   int launches_ = 0;
   int counting_ = 0;
   int staged(size_t bytes);

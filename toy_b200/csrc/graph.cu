@@ -36,6 +36,7 @@ namespace tb2 {
 
 Session::~Session() {
   if (device >= 0) cudaSetDevice(device);
+  kv_free(this);   // the decode engine reads the step engine's weights: it goes first
   dp_free(this);
   for (auto& t : tensors) {
     if (t->data && !t->view_of) cudaFree(t->data);

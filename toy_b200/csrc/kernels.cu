@@ -785,8 +785,11 @@ __global__ void __launch_bounds__(256) q8_0_ring_kernel(const __grid_constant__ 
         q[u] = __ldg(reinterpret_cast<const int4*>(M.qv + e));
         sc[u] = __half2float(__ushort_as_half(__ldg(M.qs + e / 32)));
       } else if (rr[u] >= M.d_out) {
-        const int t = rr[u] - M.d_out, a = t / 16, j = t % 16;
-        if (cc[u] < M.d_in && a < M.n_ad && j < M.r) {
+        const int t = rr[u] - M.d_out;
+        const bool bd = M.bd_r > 0;
+        const int a = bd ? 0 : t / 16, j = bd ? t : t % 16;
+        const int jmax = bd ? M.ad[0].width / M.bd_w * M.bd_r : M.r;
+        if (cc[u] < M.d_in && a < M.n_ad && j < jmax) {
           const float4* src = reinterpret_cast<const float4*>(M.ad[a].A + (long long)j * M.d_in + cc[u]);
 #pragma unroll
           for (int v = 0; v < 4; ++v) av[u][v] = __ldg(src + v);
@@ -806,6 +809,15 @@ __global__ void __launch_bounds__(256) q8_0_ring_kernel(const __grid_constant__ 
         const int8_t* b = reinterpret_cast<const int8_t*>(&q[u]);
 #pragma unroll
         for (int t = 0; t < 16; ++t) v[t] = sc[u] * (float)b[t];
+      } else if (row < M.d_out && M.bd_r > 0) {
+        // block-diagonal adapter: row's block h owns extension columns [h bd_r, (h + 1) bd_r)
+        const RingAdapter& ad = M.ad[0];
+        const bool on = row >= ad.c0 && row < ad.c0 + ad.width;
+        const int h = on ? (row - ad.c0) / M.bd_w : 0;
+        const int e0 = col - M.d_in - h * M.bd_r;
+        const float* br = on ? ad.B + (long long)(row - ad.c0) * M.bd_r : nullptr;
+#pragma unroll
+        for (int t = 0; t < 16; ++t) v[t] = (on && e0 + t >= 0 && e0 + t < M.bd_r) ? M.s * br[e0 + t] : 0.f;
       } else if (row < M.d_out) {
         const int a = (col - M.d_in) / 16;
         const bool on = a < M.n_ad && row >= M.ad[a].c0 && row < M.ad[a].c0 + M.ad[a].width;
@@ -892,6 +904,19 @@ __global__ void add_inplace_kernel(float* __restrict__ y, const float* __restric
   griddep_wait();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
     y[i] += x[i];
+}
+
+__global__ void blockdiag_take_kernel(const float* __restrict__ dense, int nb, int bw, int r,
+                                      float* __restrict__ out) {
+  griddep_wait();
+  const long long n = (long long)nb * bw * r;
+  const long long R = (long long)nb * r;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long row = i / r;
+    const int j = (int)(i % r);
+    const int h = (int)(row / bw);
+    out[i] = dense[row * R + (long long)h * r + j];
+  }
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -1050,11 +1075,11 @@ struct RmsFwdLora {
                 const LoraSegs& g, cudaStream_t st) {
     constexpr int RW = NS * RT <= 32 ? 2 : 1;
     auto* kern = rmsnorm_fwd_lora_kernel<NC, RT, NS, RW>;
-    static bool attr = false;
-    if (!attr) {
+    static DeviceOnce setup;
+    setup.ensure([&](int) {
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-      attr = true;
-    }
+      return 0;
+    });
     const size_t smem = 16 + (size_t)NS * r * d * sizeof(float);
     launch_pdl(kern, dim3(grid_for(((long long)N + RW - 1) / RW * 32, 256)), dim3(256), smem, st, x, gamma, h, ldh, N,
                d, eps, r, g, device_error_word());
@@ -1088,11 +1113,11 @@ struct RmsBwd {
   static int run(const float* x, const float* dh, const float* gamma, const float* dres, float* dx, Planes dxp,
                  long long ldp, float* gpart, int nblk, int N, int d, float eps, cudaStream_t st) {
     const size_t smem = (size_t)8 * d * sizeof(float);
-    static bool attr = false;
-    if (!attr) {
+    static DeviceOnce setup;
+    setup.ensure([](int) {
       cudaFuncSetAttribute(rmsnorm_bwd_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-      attr = true;
-    }
+      return 0;
+    });
     launch_pdl(rmsnorm_bwd_kernel<NC>, dim3(nblk), dim3(256), smem, st, x, dh, gamma, dres, dx, dxp, ldp, gpart, N, d,
                eps);
     return ok();
@@ -1298,6 +1323,13 @@ int launch_q8_0_quantize(const float* x, uint8_t* q, long long rows, int K, cuda
 
 int launch_colsum_rows(const float* x, int N, int W, float* out, cudaStream_t st) {
   launch_pdl(colsum_rows_kernel, dim3((W + 127) / 128), dim3(128), 0, st, x, N, W, out);
+  return ok();
+}
+
+int launch_lora_blockdiag_take(const float* dense, int nb, int bw, int r, float* out, cudaStream_t st) {
+  if (!dense || !out || nb < 1 || bw < 1 || r < 1) return -1;
+  launch_pdl(blockdiag_take_kernel, dim3(grid_for((long long)nb * bw * r, 256)), dim3(256), 0, st, dense, nb, bw, r,
+             out);
   return ok();
 }
 

@@ -120,12 +120,20 @@ struct RingAdapter {
   const float* B = nullptr;   // [width][r]
   int c0 = 0, width = 0;
 };
+//
+// Block-diagonal adapter (bd_r > 0, one RingAdapter): the reference's LoRA-Q
+// with one (A_h [bd_r][d_in], B_h [bd_w][bd_r]) pair per block of bd_w output
+// rows. A is the blocks' A_h stacked ([R][d_in], R = width / bd_w * bd_r), B
+// the B_h stacked ([width][bd_r]); extension column d_in + e of row c
+// (h = (c - c0) / bd_w) holds s * B[c - c0][e - h bd_r] for e in
+// [h bd_r, (h + 1) bd_r), extension row d_out + e holds A[e][:].
 struct RingMat {
   const int8_t* qv = nullptr;     // quants [d_out][d_in]
   const uint16_t* qs = nullptr;   // fp16 scale bits [d_out * d_in / 32]
   bf16* hi = nullptr;
   bf16* lo = nullptr;
   int d_out = 0, d_in = 0, ext = 0, n_ad = 0, r = 0;
+  int bd_r = 0, bd_w = 0;         // block-diagonal adapter: rank per block, rows per block
   float s = 0.f;
   long long chunk0 = 0;           // first 16-value chunk of this matrix in the launch
   RingAdapter ad[3];
@@ -143,6 +151,11 @@ int launch_q8_0_ring(const RingLayer& desc, cudaStream_t st);
 // qv[32 b ..] and its fp16 scale bits at qs[b] (the same Q8_0 content, scales
 // split off so quant tiles are TMA-loadable).
 int launch_q8_0_split(const uint8_t* blocks, int8_t* qv, uint16_t* qs, long long nblocks, cudaStream_t st);
+
+// The diagonal blocks of a block-diagonal adapter's dense gradient:
+// out[h bw + c][j] = dense[h bw + c][h r + j] (dense [nb bw][nb r], out
+// [nb bw][r]), h < nb, c < bw, j < r.
+int launch_lora_blockdiag_take(const float* dense, int nb, int bw, int r, float* out, cudaStream_t st);
 
 // out[c] = sum over rows of x[N][W] (fixed order), e.g. bias gradients.
 int launch_colsum_rows(const float* x, int N, int W, float* out, cudaStream_t st);

@@ -13,10 +13,19 @@ namespace tb2 {
 
 struct Session;
 struct DpState;
+class KvEngine;
+
+// The decode engine of a session (kv.cu), freed before the step engine whose weights it reads.
+void kv_free(Session* s);
 
 // Data-parallel gradient reduction (dp.cu).
 void dp_free(Session* s);
 int nccl_allreduce_entry(void* ctx, float* buf, long long n, cudaStream_t st);
+// 0, or the code that ended the session's communicator
+int dp_status(const Session* s);
+// Wait (host, bounded, next to the communicator's error state) for the step
+// stream of a data-parallel session; 0 when it is idle.
+int dp_wait_step(Session* s);
 
 struct Tensor {
   enum Role : int { kPrim = 0, kIds, kPos, kLabels, kHp, kLoss, kParam };
@@ -57,6 +66,7 @@ struct Session {
   Tensor* io[TB2_IO_COUNT] = {nullptr};
   bool first_pending = false;
   DpState* dp = nullptr;
+  KvEngine* kv = nullptr;
   // primitive op graph
   std::vector<Tensor*> nodes;     // forward program (topological order)
   std::vector<Tensor*> bwd;       // backward program (creation order)

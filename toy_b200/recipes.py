@@ -76,13 +76,27 @@ class RecipeOptions:
 
 @dataclass
 class LoraOptions:
-    """Adapter placement and synthetic init (rank r, scale alpha / r)."""
+    """Adapter placement and synthetic init.
+
+    Per-projection adapters (the benchmark configurations): rank r, scale
+    alpha / r, A ~ N(0, a_std), B ~ N(0, b_std), drawn after the base from the
+    seeded stream. per_head_q=True is toy's own LoRA-Q recipe instead
+    (transformer_block.rb:522-579,861-871): one (A_h, B_h) pair per query head,
+    no scale, A = a_std * N(0, 1) from upload_lora_q_init!'s raw-seed stream
+    (a_std plays init_scale), B = 0; targets must be ("q",)."""
     rank: int = 8
     alpha: float = 16.0
     targets: Sequence[str] = ("q", "v")
     a_std: float = 0.125
     b_std: float = 0.01
     base_std: float = 0.02   # synthetic frozen base N(0, base_std), quantised to Q8_0
+    per_head_q: bool = False
+
+    @staticmethod
+    def lora_q(rank: int, init_scale: float = 1.0, base_std: float = 0.02) -> "LoraOptions":
+        """toy's LoRA recipe: enable_lora_q!(rank) + upload_lora_q_init!(seed, init_scale)."""
+        return LoraOptions(rank=rank, alpha=float(rank), targets=("q",), a_std=init_scale, b_std=0.0,
+                           base_std=base_std, per_head_q=True)
 
 
 class LlamaSeqEngine:
@@ -123,6 +137,9 @@ class LlamaSeqEngine:
         if lora is not None:
             c.lora_rank, c.lora_alpha = lora.rank, lora.alpha
             c.lora_targets = sum(LORA_BITS[t] for t in lora.targets)
+            c.lora_per_head_q = 1 if lora.per_head_q else 0
+            if lora.per_head_q and tuple(lora.targets) != ("q",):
+                raise ValueError("per-head LoRA-Q adapts the query projection only: targets must be ('q',)")
         self._ff = None
         if cfg.rope_freq_factors is not None:
             self._ff = np.ascontiguousarray(np.asarray(cfg.rope_freq_factors, np.float64))
@@ -201,6 +218,37 @@ class LlamaSeqEngine:
     def launches_per_step(self) -> int:
         return lib().tb2_step_launches(self.sess)
 
+    # ---- GGUF weights and checkpoints
+    def load_gguf(self, path: str, moments: bool = False, partial: bool = False) -> int:
+        """Load every parameter found in a GGUF file (toy's converter layout or
+        its legacy transposed one; Q8_0 blocks verbatim into the frozen base);
+        with moments, also the Adam state a checkpoint carries; partial: a
+        checkpoint that holds only some tensors (the rest keep their values).
+        Returns the number of tensors loaded."""
+        L = lib()
+        h = L.tnn_gguf_load(path.encode())
+        if not h:
+            raise RuntimeError(f"toy_b200: cannot read GGUF {path}")
+        try:
+            n = L.tb2_llama_load_gguf(self.sess, h, (1 if moments else 0) | (2 if partial else 0))
+        finally:
+            L.tnn_gguf_free(h)
+        if n < 0:
+            raise RuntimeError(f"toy_b200: tb2_llama_load_gguf failed with code {n}")
+        return n
+
+    def save_gguf(self, path: str, frozen: bool = False, moments: bool = False, stacked: bool = False) -> None:
+        """Checkpoint the trainable tensors (plus the frozen ones, plus Adam
+        moments) as GGUF; per-head LoRA-Q goes under toy's per-head names unless
+        stacked."""
+        what = 1 | (2 if frozen else 0) | (4 if moments else 0) | (8 if stacked else 0)
+        check(lib().tb2_llama_save_gguf(self.sess, path.encode(), what), "tb2_llama_save_gguf")
+
+    def set_grad_accumulation(self, n_micro: int) -> None:
+        """Accumulate gradients over n_micro step calls; AdamW runs on every
+        n_micro-th call with the mean gradient (the joined-batch step)."""
+        check(lib().tb2_llama_set_grad_accumulation(self.sess, int(n_micro)), "tb2_llama_set_grad_accumulation")
+
 
 def _step(eng: LlamaSeqEngine, t_loss, t_labels, t_hp, seq_ids, positions, m_labels, m_hp, is_first) -> float:
     """from_scratch.rb:89-103 == lora.rb:94-107, in the same order."""
@@ -240,7 +288,12 @@ class FromScratch:
 
 
 class LoRA:
-    """Toy::LLM::Recipes::LoRA over a frozen Q8_0 base (QLoRA)."""
+    """Toy::LLM::Recipes::LoRA over a frozen Q8_0 base (QLoRA).
+
+    realize(cfg, rank, opts) with no LoraOptions runs the reference recipe's own
+    adapters: per-head LoRA-Q of the given rank, initialised by
+    upload_lora_q_init!(opts.seed, opts.init_scale) (lora.rb:71-82). A
+    LoraOptions selects per-projection adapters (q, k, v, o, gate, up, down)."""
 
     def __init__(self, device: int = 0):
         self.lora_cache = LlamaSeqEngine(device)
@@ -248,7 +301,7 @@ class LoRA:
         self.lora_step_index = 0
 
     def realize(self, cfg: LlamaConfig, rank: int, opts: RecipeOptions, lora: Optional[LoraOptions] = None) -> None:
-        lo = lora or LoraOptions(rank=rank)
+        lo = lora or LoraOptions.lora_q(rank, init_scale=opts.init_scale)
         lo.rank = rank
         self.lora_cache.realize(cfg, opts, mode=1, lora=lo)
         self.lora_t_loss, self.lora_t_labels, self.lora_t_hp = self.lora_cache.build_training_step()
