@@ -197,6 +197,20 @@ typedef struct tb2_llama_config {
                                       (transformer_block.rb:522-579,861-871); lora_targets must be q only;
                                       attn_q.lora_a is the A_h stacked [H r][d], attn_q.lora_b the B_h
                                       stacked [H d_head][r]; needs tb2_set_q8_base_mode(1) */
+  /* Mixture of experts in every block's FFN (QLoRA only; llama_kv_engine.rb
+   * build_moe_ffn :2073): a frozen f32 router (blk.N.ffn_gate_inp.weight
+   * [n_experts x d]) picks the top n_experts_used experts per token by softmax
+   * probability (norm_topk: their weights renormalised to sum 1); the experts'
+   * SwiGLU FFNs of width d_ff are frozen Q8_0, stacked as
+   * blk.N.ffn_{gate,up}_exps.weight [n_experts d_ff x d] and
+   * blk.N.ffn_down_exps.weight [n_experts d x d_ff]. Adapters only on q, k, v, o.
+   * The backward runs through the experts, the routing weights and the router's
+   * softmax. Such a step runs eagerly (one host round trip per block to order
+   * the routed tokens by expert). 0 = dense FFN. */
+  int n_experts, n_experts_used, norm_topk;
+  /* 2: RMSNorm over the whole q and k vectors before RoPE (OLMoE), frozen
+   * gammas blk.N.attn_{q,k}_norm.weight; 0 none. QLoRA only. */
+  int qk_norm;
 } tb2_llama_config;
 
 /* Realize the forward + cross-entropy + backward + AdamW program for a Llama

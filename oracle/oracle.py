@@ -125,6 +125,16 @@ class LlamaCfg:
     tied: bool = True
     qkv_bias: bool = False
     rope_freq_factors: Optional[np.ndarray] = None   # llama3-style per-dim factors (d_head/2)
+    # mixture of experts in every block's FFN (n_experts > 0): router softmax over
+    # the experts, the top n_experts_used by probability, their SwiGLU outputs
+    # (expert FFN width d_ff) weighted by the probabilities (renormalised to sum
+    # 1 with norm_topk) -- llama_kv_engine.rb build_moe_ffn :2073
+    n_experts: int = 0
+    n_experts_used: int = 0
+    norm_topk: bool = False
+    # 2: RMSNorm over the whole q and k vectors before the head split and RoPE
+    # (OLMoE / Granite, llama_kv_engine.rb build_block_step :1687)
+    qk_norm: int = 0
 
     @property
     def group(self) -> int:
@@ -190,12 +200,26 @@ def random_init(cfg: LlamaCfg, seed: int, init_scale: float, std_all: Optional[f
         P[f"blk.{l}.attn_q.weight"], P[f"blk.{l}.attn_k.weight"], P[f"blk.{l}.attn_v.weight"] = wq, wk, wv
         w, st = gaussian_fill(st, d * H * dh, s_d)
         P[f"blk.{l}.attn_output.weight"] = w.reshape(d, H * dh)
-        w, st = gaussian_fill(st, ff * d, s_d)
-        P[f"blk.{l}.ffn_gate.weight"] = w.reshape(ff, d)
-        w, st = gaussian_fill(st, ff * d, s_d)
-        P[f"blk.{l}.ffn_up.weight"] = w.reshape(ff, d)
-        w, st = gaussian_fill(st, d * ff, s_ff)
-        P[f"blk.{l}.ffn_down.weight"] = w.reshape(d, ff)
+        if cfg.n_experts:
+            E = cfg.n_experts
+            w, st = gaussian_fill(st, E * d, s_emb)
+            P[f"blk.{l}.ffn_gate_inp.weight"] = w.reshape(E, d)
+            w, st = gaussian_fill(st, E * ff * d, s_d)
+            P[f"blk.{l}.ffn_gate_exps.weight"] = w.reshape(E, ff, d)
+            w, st = gaussian_fill(st, E * ff * d, s_d)
+            P[f"blk.{l}.ffn_up_exps.weight"] = w.reshape(E, ff, d)
+            w, st = gaussian_fill(st, E * d * ff, s_ff)
+            P[f"blk.{l}.ffn_down_exps.weight"] = w.reshape(E, d, ff)
+        else:
+            w, st = gaussian_fill(st, ff * d, s_d)
+            P[f"blk.{l}.ffn_gate.weight"] = w.reshape(ff, d)
+            w, st = gaussian_fill(st, ff * d, s_d)
+            P[f"blk.{l}.ffn_up.weight"] = w.reshape(ff, d)
+            w, st = gaussian_fill(st, d * ff, s_ff)
+            P[f"blk.{l}.ffn_down.weight"] = w.reshape(d, ff)
+        if cfg.qk_norm:
+            P[f"blk.{l}.attn_q_norm.weight"] = np.ones(H * dh, np.float32)
+            P[f"blk.{l}.attn_k_norm.weight"] = np.ones(KV * dh, np.float32)
         if cfg.qkv_bias:
             for nm, rows in (("q", H * dh), ("k", KV * dh), ("v", KV * dh)):
                 w, st = gaussian_fill(st, rows, 0.02 if std_all is None else std_all)
@@ -420,10 +444,12 @@ def qlora_model(cfg: LlamaCfg, lcfg: LoraCfg, seed: int = 42, base_std: float = 
     st = int(P.pop("_state")[0])
     q8 = {}
     for l in range(cfg.n_layers):
-        for p in PROJ:
-            k = f"blk.{l}.{PNAME[p]}.weight"
+        names = [f"blk.{l}.{PNAME[p]}.weight" for p in PROJ if cfg.n_experts == 0 or p in ("q", "k", "v", "o")]
+        if cfg.n_experts:   # expert tensors quantised per expert row (along d_in), router kept in f32
+            names += [f"blk.{l}.ffn_{t}_exps.weight" for t in ("gate", "up", "down")]
+        for k in names:
             q8[k] = q8_0_quantize(P[k])
-            P[k] = q8_0_dequantize(q8[k], P[k].shape[1])
+            P[k] = q8_0_dequantize(q8[k], P[k].shape[-1])
     # per-head LoRA-Q draws A with init_scale = a_std (upload_lora_q_init!'s init_scale)
     L = lora_init(cfg, lcfg, st, seed, init_scale=lcfg.a_std if lcfg.per_head_q else 0.01)
     P.update(L)
@@ -475,6 +501,139 @@ def _lora_back(mdl: Model, l: int, p: str, h1, u, dy, grads):
     return du @ A
 
 
+def _attn_backward(mdl: Model, l: int, c: dict, dx1, cos, sin, grads, tr):
+    """Backward of one block's attention half: from d(x1) to d(x), adapters and
+    weight gradients into grads."""
+    cfg, P = mdl.cfg, mdl.params
+    N, H, KV, dh, G = c["x"].shape[0], cfg.n_heads, cfg.n_kv, cfg.d_head, cfg.group
+    B = c["probs"].shape[0]
+    T = N // B
+    eps = cfg.rms_eps
+    dt = mdl.dtype
+    scale = dt(1.0 / math.sqrt(dh))
+    f64 = lambda k: P[k].astype(dt)
+    pre = f"blk.{l}."
+    do = dx1 @ f64(pre + "attn_output.weight")
+    if pre + "attn_output.weight" in tr:
+        grads[pre + "attn_output.weight"] = dx1.T @ c["o"]
+    if "u_o" in c:
+        do = do + _lora_back(mdl, l, "o", c["o"], c["u_o"], dx1, grads)
+    do = do.reshape(N, H, dh)
+    q, k, v, probs = c["q"], c["k"], c["v"], c["probs"]
+    dq = np.zeros_like(q)
+    dk = np.zeros_like(k)
+    dv = np.zeros_like(v)
+    for b in range(B):
+        sl = slice(b * T, (b + 1) * T)
+        for h in range(H):
+            j = h // G
+            pr = probs[b, h]
+            dP = do[sl, h] @ v[sl, j].T
+            dS = pr * (dP - np.sum(dP * pr, axis=-1, keepdims=True)) * scale
+            dq[sl, h] = dS @ k[sl, j]
+            dk[sl, j] += dS.T @ q[sl, h]
+            dv[sl, j] += pr.T @ do[sl, h]
+    dq = rope_back(dq, cos, sin).reshape(N, H * dh)
+    dk = rope_back(dk, cos, sin).reshape(N, KV * dh)
+    dv = dv.reshape(N, KV * dh)
+    if cfg.qk_norm:   # through the whole-vector q / k RMSNorm
+        for nm, pre_v in (("q", "q_pre"), ("k", "k_pre")):
+            gk = pre + f"attn_{nm}_norm.weight"
+            xv = c[pre_v]
+            dpost = dq if nm == "q" else dk
+            if gk in tr:
+                rr = 1.0 / np.sqrt(np.mean(xv * xv, axis=-1, keepdims=True) + eps)
+                grads[gk] = np.sum(dpost * xv * rr, axis=0)
+            back = rms_norm_back(xv, dpost * f64(gk), eps)
+            if nm == "q":
+                dq = back
+            else:
+                dk = back
+    h1 = c["h1"]
+    dh1 = dq @ f64(pre + "attn_q.weight") + dk @ f64(pre + "attn_k.weight") + dv @ f64(pre + "attn_v.weight")
+    for p, dy in (("q", dq), ("k", dk), ("v", dv)):
+        if pre + PNAME[p] + ".weight" in tr:
+            grads[pre + PNAME[p] + ".weight"] = dy.T @ h1
+        if cfg.qkv_bias and pre + PNAME[p] + ".bias" in tr:
+            grads[pre + PNAME[p] + ".bias"] = dy.sum(axis=0)
+        if "u_" + p in c:
+            dh1 = dh1 + _lora_back(mdl, l, p, h1, c["u_" + p], dy, grads)
+    x0 = c["x"]
+    r1 = 1.0 / np.sqrt(np.mean(x0 * x0, axis=-1, keepdims=True) + eps)
+    if pre + "attn_norm.weight" in tr:
+        grads[pre + "attn_norm.weight"] = np.sum(dh1 * x0 * r1, axis=0)
+    return dx1 + rms_norm_back(x0, dh1 * f64(pre + "attn_norm.weight"), eps)
+
+
+def moe_forward(mdl: Model, l: int, h2):
+    """The FFN of an MoE block (llama_kv_engine.rb build_moe_ffn :2073) for every
+    token row of h2: probs = softmax(h2 Wr^T) over the experts, the top
+    n_experts_used by probability (ties to the lower index), weights = their
+    probabilities (renormalised with norm_topk), and the weighted sum of the
+    selected experts' SwiGLU FFNs. Returns (y, cache)."""
+    cfg, P = mdl.cfg, mdl.params
+    dt = mdl.dtype
+    E, K = cfg.n_experts, cfg.n_experts_used
+    f = lambda k: P[k].astype(dt)
+    pre = f"blk.{l}."
+    Wr, Wg, Wu, Wd = f(pre + "ffn_gate_inp.weight"), f(pre + "ffn_gate_exps.weight"), f(pre + "ffn_up_exps.weight"), \
+        f(pre + "ffn_down_exps.weight")
+    N = h2.shape[0]
+    probs = softmax(h2 @ Wr.T)
+    idx = np.argsort(-probs, axis=1, kind="stable")[:, :K]
+    w = np.take_along_axis(probs, idx, 1)
+    if cfg.norm_topk:
+        w = w / np.sum(w, axis=1, keepdims=True)
+    g = np.zeros((N, K, Wg.shape[1]), dt)
+    u = np.zeros_like(g)
+    ye = np.zeros((N, K, h2.shape[1]), dt)
+    for e in range(E):
+        n_i, k_i = np.nonzero(idx == e)
+        if n_i.size == 0:
+            continue
+        X = h2[n_i]
+        ge, ue = X @ Wg[e].T, X @ Wu[e].T
+        g[n_i, k_i], u[n_i, k_i] = ge, ue
+        ye[n_i, k_i] = (silu(ge) * ue) @ Wd[e].T
+    y = np.einsum("nk,nkd->nd", w, ye)
+    return y, {"probs": probs, "idx": idx, "w": w, "g": g, "u": u, "ye": ye}
+
+
+def moe_backward(mdl: Model, l: int, h2, mc: dict, dy):
+    """d(h2) of moe_forward for the output gradient dy, the experts and the
+    router frozen: through every selected expert (weighted by its routing
+    weight) and through the routing weights into the router's softmax."""
+    cfg, P = mdl.cfg, mdl.params
+    dt = mdl.dtype
+    E, K = cfg.n_experts, cfg.n_experts_used
+    f = lambda k: P[k].astype(dt)
+    pre = f"blk.{l}."
+    Wr, Wg, Wu, Wd = f(pre + "ffn_gate_inp.weight"), f(pre + "ffn_gate_exps.weight"), f(pre + "ffn_up_exps.weight"), \
+        f(pre + "ffn_down_exps.weight")
+    probs, idx, w, g, u, ye = mc["probs"], mc["idx"], mc["w"], mc["g"], mc["u"], mc["ye"]
+    dh2 = np.zeros_like(h2)
+    dw = np.einsum("nd,nkd->nk", dy, ye)
+    for e in range(E):
+        n_i, k_i = np.nonzero(idx == e)
+        if n_i.size == 0:
+            continue
+        dye = w[n_i, k_i][:, None] * dy[n_i]
+        da = dye @ Wd[e]
+        ge, ue = g[n_i, k_i], u[n_i, k_i]
+        dge = silu_back(ge, da * ue)
+        due = da * silu(ge)
+        np.add.at(dh2, n_i, dge @ Wg[e] + due @ Wu[e])
+    if cfg.norm_topk:   # w = p_sel / sum(p_sel)
+        ssum = np.sum(np.take_along_axis(probs, idx, 1), axis=1, keepdims=True)
+        dsel = (dw - np.sum(dw * w, axis=1, keepdims=True)) / ssum
+    else:
+        dsel = dw
+    dprobs = np.zeros_like(probs)
+    np.put_along_axis(dprobs, idx, dsel, 1)
+    dlogits = probs * (dprobs - np.sum(probs * dprobs, axis=1, keepdims=True))
+    return dh2 + dlogits @ Wr
+
+
 def q8_0_roundtrip(x: np.ndarray) -> np.ndarray:
     """The values a Q8_0 cache holds for x [..., n] (n % 32 == 0): x narrowed
     to f32, quantised (ggml's quantiser) and dequantised."""
@@ -518,6 +677,10 @@ def forward_backward(mdl: Model, ids: np.ndarray, pos: np.ndarray, labels: np.nd
             if cfg.qkv_bias:
                 y = y + f64(f"blk.{l}.{PNAME[p]}.bias")
             qkv[p] = y
+        if cfg.qk_norm:
+            c["q_pre"], c["k_pre"] = qkv["q"], qkv["k"]
+            qkv["q"] = rms_norm(qkv["q"], f64(f"blk.{l}.attn_q_norm.weight"), eps)[0]
+            qkv["k"] = rms_norm(qkv["k"], f64(f"blk.{l}.attn_k_norm.weight"), eps)[0]
         q = rope(qkv["q"].reshape(N, H, dh), cos, sin)
         k = rope(qkv["k"].reshape(N, KV, dh), cos, sin)
         v = qkv["v"].reshape(N, KV, dh)
@@ -542,6 +705,12 @@ def forward_backward(mdl: Model, ids: np.ndarray, pos: np.ndarray, labels: np.nd
         c["x1"] = x1
         h2, r2 = rms_norm(x1, f64(f"blk.{l}.ffn_norm.weight"), eps)
         c["h2"] = h2
+        if cfg.n_experts:
+            y, c["moe"] = moe_forward(mdl, l, h2)
+            x2 = x1 + y
+            caches.append(c)
+            x = x2
+            continue
         g = h2 @ f64(f"blk.{l}.ffn_gate.weight").T
         up = h2 @ f64(f"blk.{l}.ffn_up.weight").T
         for p, y in (("gate", "g"), ("up", "up")):
@@ -584,6 +753,15 @@ def forward_backward(mdl: Model, ids: np.ndarray, pos: np.ndarray, labels: np.nd
     for l in reversed(range(cfg.n_layers)):
         c = caches[l]
         pre = f"blk.{l}."
+        if cfg.n_experts:
+            dh2 = moe_backward(mdl, l, c["h2"], c["moe"], dx)
+            x1 = c["x1"]
+            r2 = 1.0 / np.sqrt(np.mean(x1 * x1, axis=-1, keepdims=True) + eps)
+            if pre + "ffn_norm.weight" in tr:
+                grads[pre + "ffn_norm.weight"] = np.sum(dh2 * x1 * r2, axis=0)
+            dx1 = dx + rms_norm_back(x1, dh2 * f64(pre + "ffn_norm.weight"), eps)
+            dx = _attn_backward(mdl, l, c, dx1, cos, sin, grads, tr)
+            continue
         # FFN
         da = dx @ f64(pre + "ffn_down.weight")
         if pre + "ffn_down.weight" in tr:
@@ -606,44 +784,7 @@ def forward_backward(mdl: Model, ids: np.ndarray, pos: np.ndarray, labels: np.nd
         if pre + "ffn_norm.weight" in tr:
             grads[pre + "ffn_norm.weight"] = np.sum(dh2 * x1 * r2, axis=0)
         dx1 = dx + rms_norm_back(x1, dh2 * f64(pre + "ffn_norm.weight"), eps)
-        # attention
-        do = dx1 @ f64(pre + "attn_output.weight")
-        if pre + "attn_output.weight" in tr:
-            grads[pre + "attn_output.weight"] = dx1.T @ c["o"]
-        if "u_o" in c:
-            do = do + _lora_back(mdl, l, "o", c["o"], c["u_o"], dx1, grads)
-        do = do.reshape(N, H, dh)
-        q, k, v, probs = c["q"], c["k"], c["v"], c["probs"]
-        dq = np.zeros_like(q)
-        dk = np.zeros_like(k)
-        dv = np.zeros_like(v)
-        for b in range(B):
-            sl = slice(b * T, (b + 1) * T)
-            for h in range(H):
-                j = h // G
-                pr = probs[b, h]
-                dP = do[sl, h] @ v[sl, j].T
-                dS = pr * (dP - np.sum(dP * pr, axis=-1, keepdims=True)) * scale
-                dq[sl, h] = dS @ k[sl, j]
-                dk[sl, j] += dS.T @ q[sl, h]
-                dv[sl, j] += pr.T @ do[sl, h]
-        dq = rope_back(dq, cos, sin).reshape(N, H * dh)
-        dk = rope_back(dk, cos, sin).reshape(N, KV * dh)
-        dv = dv.reshape(N, KV * dh)
-        h1 = c["h1"]
-        dh1 = dq @ f64(pre + "attn_q.weight") + dk @ f64(pre + "attn_k.weight") + dv @ f64(pre + "attn_v.weight")
-        for p, dy in (("q", dq), ("k", dk), ("v", dv)):
-            if pre + PNAME[p] + ".weight" in tr:
-                grads[pre + PNAME[p] + ".weight"] = dy.T @ h1
-            if cfg.qkv_bias and pre + PNAME[p] + ".bias" in tr:
-                grads[pre + PNAME[p] + ".bias"] = dy.sum(axis=0)
-            if "u_" + p in c:
-                dh1 = dh1 + _lora_back(mdl, l, p, h1, c["u_" + p], dy, grads)
-        x0 = c["x"]
-        r1 = 1.0 / np.sqrt(np.mean(x0 * x0, axis=-1, keepdims=True) + eps)
-        if pre + "attn_norm.weight" in tr:
-            grads[pre + "attn_norm.weight"] = np.sum(dh1 * x0 * r1, axis=0)
-        dx = dx1 + rms_norm_back(x0, dh1 * f64(pre + "attn_norm.weight"), eps)
+        dx = _attn_backward(mdl, l, c, dx1, cos, sin, grads, tr)
     if "token_embd.weight" in tr:
         gE = grads.get("token_embd.weight", np.zeros(E.shape, dt))
         np.add.at(gE, ids, dx)     # get_rows_back: scatter-add (tinynn_ggml.c:1683-1700)

@@ -141,8 +141,11 @@ def _torch_reference_grads(mdl, ids, pos, labels, T, B):
     mask = torch.triu(torch.full((T, T), float("-inf"), dtype=torch.float64), 1)
     for l in range(cfg.n_layers):
         h1 = rms(x, P[f"blk.{l}.attn_norm.weight"])
-        q = rope(proj(l, "q", h1).view(N, H, dh))
-        k = rope(proj(l, "k", h1).view(N, KV, dh))
+        qf, kf = proj(l, "q", h1), proj(l, "k", h1)
+        if cfg.qk_norm:
+            qf, kf = rms(qf, P[f"blk.{l}.attn_q_norm.weight"]), rms(kf, P[f"blk.{l}.attn_k_norm.weight"])
+        q = rope(qf.view(N, H, dh))
+        k = rope(kf.view(N, KV, dh))
         v = proj(l, "v", h1).view(N, KV, dh)
         outs = []
         for b in range(B):
@@ -156,6 +159,24 @@ def _torch_reference_grads(mdl, ids, pos, labels, T, B):
         o = torch.cat(outs, 0)
         x = x + proj(l, "o", o)
         h2 = rms(x, P[f"blk.{l}.ffn_norm.weight"])
+        if cfg.n_experts:
+            pr = torch.softmax(h2 @ P[f"blk.{l}.ffn_gate_inp.weight"].T, -1)
+            idx = torch.argsort(-pr.detach(), dim=1, stable=True)[:, :cfg.n_experts_used]
+            w = torch.gather(pr, 1, idx)
+            if cfg.norm_topk:
+                w = w / w.sum(1, keepdim=True)
+            y = torch.zeros_like(h2)
+            for e in range(cfg.n_experts):
+                for kk in range(cfg.n_experts_used):
+                    sel = idx[:, kk] == e
+                    if sel.any():
+                        X = h2[sel]
+                        a = torch.nn.functional.silu(X @ P[f"blk.{l}.ffn_gate_exps.weight"][e].T) * \
+                            (X @ P[f"blk.{l}.ffn_up_exps.weight"][e].T)
+                        ye = a @ P[f"blk.{l}.ffn_down_exps.weight"][e].T
+                        y = y.index_add(0, torch.nonzero(sel)[:, 0], w[sel, kk:kk + 1] * ye)
+            x = x + y
+            continue
         a = torch.nn.functional.silu(proj(l, "gate", h2)) * proj(l, "up", h2)
         x = x + proj(l, "down", a)
     xf = rms(x, P["output_norm.weight"])
@@ -172,11 +193,15 @@ def _torch_reference_grads(mdl, ids, pos, labels, T, B):
     return loss.item(), {k: P[k].grad.numpy() for k in mdl.trainable}
 
 
-@pytest.mark.parametrize("mode", ["full", "qlora", "qlora_all7", "qlora_per_head"])
+@pytest.mark.parametrize("mode", ["full", "qlora", "qlora_all7", "qlora_per_head", "qlora_moe", "qlora_moe_norm"])
 def test_backward_matches_torch_autograd(mode):
     cfg = O.LlamaCfg(vocab=96, d_model=64, n_heads=4, n_kv=2, d_head=16, d_ff=96, n_layers=2, rope_base=1e4)
     T, B = 8, 2
-    if mode == "full":
+    if mode.startswith("qlora_moe"):   # OLMoE-style block: QK-RMSNorm, 6 experts, top 3
+        cfg = O.LlamaCfg(vocab=96, d_model=64, n_heads=4, n_kv=4, d_head=16, d_ff=32, n_layers=2, rope_base=1e4,
+                         n_experts=6, n_experts_used=3, norm_topk=mode.endswith("norm"), qk_norm=2)
+        mdl = O.qlora_model(cfg, O.LoraCfg(rank=4, alpha=8, targets=("q", "k", "v", "o")), seed=3)
+    elif mode == "full":
         mdl = O.full_ft_model(cfg, seed=3, init_scale=1.0)
     elif mode == "qlora":
         mdl = O.qlora_model(cfg, O.LoraCfg(rank=4, alpha=8, targets=("q", "v")), seed=3)

@@ -32,7 +32,8 @@ class LlamaConfigC(C.Structure):
                 ("rms_eps", C.c_double), ("freq_scale", C.c_double), ("tied", C.c_int), ("qkv_bias", C.c_int),
                 ("t_seq", C.c_int), ("t_batch", C.c_int), ("mode", C.c_int), ("lora_rank", C.c_int),
                 ("lora_alpha", C.c_double), ("lora_targets", C.c_int),
-                ("rope_freq_factors", C.POINTER(C.c_double)), ("attn_impl", C.c_int), ("lora_per_head_q", C.c_int)]
+                ("rope_freq_factors", C.POINTER(C.c_double)), ("attn_impl", C.c_int), ("lora_per_head_q", C.c_int),
+                ("n_experts", C.c_int), ("n_experts_used", C.c_int), ("norm_topk", C.c_int), ("qk_norm", C.c_int)]
 
 
 _lib = None

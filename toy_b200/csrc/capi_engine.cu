@@ -86,6 +86,10 @@ int tb2_llama_realize(void* sess, const tb2_llama_config* cfg) {
   c.lora_rank = cfg->lora_rank; c.lora_alpha = (float)cfg->lora_alpha; c.lora_targets = cfg->lora_targets;
   c.attn_impl = cfg->attn_impl;
   c.lora_per_head_q = cfg->lora_per_head_q;
+  c.n_experts = cfg->n_experts;
+  c.n_experts_used = cfg->n_experts_used;
+  c.norm_topk = cfg->norm_topk;
+  c.qk_norm = cfg->qk_norm;
   if (cfg->rope_freq_factors)
     for (int i = 0; i < cfg->d_head / 2; ++i) c.freq_factors.push_back((float)cfg->rope_freq_factors[i]);
   if (cudaSetDevice(s->device) != cudaSuccess) return -3;

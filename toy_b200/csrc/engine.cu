@@ -229,6 +229,15 @@ int LlamaEngine::realize() {
   if (c.mode == 1 && (c.lora_rank <= 0 || c.lora_rank > kLoraMaxRank || c.lora_targets == 0)) return -1;
   per_head_ = c.mode == 1 && c.lora_per_head_q;
   if (per_head_ && (c.lora_targets != (1 << kLoraQ) || g_q8_base_mode != 1)) return -1;
+  moe_ = c.n_experts > 0;
+  if (moe_) {
+    // QLoRA over frozen experts; adapters on the attention projections only
+    const int ffn_bits = (1 << kLoraGate) | (1 << kLoraUp) | (1 << kLoraDown);
+    if (c.mode != 1 || per_head_ || c.n_experts > 256 || c.n_experts % 8 || c.n_experts_used < 1 ||
+        c.n_experts_used > 16 || c.n_experts_used > c.n_experts || (c.lora_targets & ffn_bits))
+      return -1;
+  }
+  if (c.qk_norm && (c.qk_norm != 2 || c.mode != 1 || c.qkv_bias)) return -1;
   CU(cudaSetDevice(device_));
   // Adapter steps: the activation / activation-gradient chain is the critical
   // path and the second stream carries light work (adapter weight gradients,
@@ -277,7 +286,19 @@ int LlamaEngine::realize() {
       add_param(pre + "attn_v.bias", 1, KV * dh, full, false);
     }
     add_param(pre + "attn_output.weight", d, H * dh, full, q8);
+    if (c.qk_norm) {
+      add_param(pre + "attn_q_norm.weight", 1, H * dh, false, false);
+      add_param(pre + "attn_k_norm.weight", 1, KV * dh, false, false);
+    }
     add_param(pre + "ffn_norm.weight", 1, d, full, false);
+    if (moe_) {   // router (f32) and the experts stacked, [expert][rows][cols] (GGUF ne = [cols, rows, experts])
+      const int E = c.n_experts;
+      add_param(pre + "ffn_gate_inp.weight", E, d, false, false);
+      add_param(pre + "ffn_gate_exps.weight", E * ff, d, false, true);
+      add_param(pre + "ffn_up_exps.weight", E * ff, d, false, true);
+      add_param(pre + "ffn_down_exps.weight", E * d, ff, false, true);
+      continue;
+    }
     add_param(pre + "ffn_gate.weight", ff, d, full, q8);      // gate | up contiguous
     add_param(pre + "ffn_up.weight", ff, d, full, q8);
     add_param(pre + "ffn_down.weight", d, ff, full, q8);
@@ -309,7 +330,7 @@ int LlamaEngine::realize() {
   q8_bytes_ = qoff;
   // Q8_0 base as ring planes: the four group operands of a block, each with
   // 64 extra reduction columns / rows when its adapters are folded in
-  q8_planes_ = q8_bytes_ && g_q8_base_mode == 1;
+  q8_planes_ = q8_bytes_ && g_q8_base_mode == 1 && !moe_;   // expert blocks dequantise inside their GEMMs
   for (auto& p : params_) {
     if (!p.q8) continue;
     p.layer = std::atoi(p.name.c_str() + 4);
@@ -356,7 +377,7 @@ int LlamaEngine::realize() {
     const std::string pre = "blk." + std::to_string(l) + ".";
     if (!follows(P(pre + "attn_q.weight"), P(pre + "attn_k.weight"))) return -1;
     if (!follows(P(pre + "attn_k.weight"), P(pre + "attn_v.weight"))) return -1;
-    if (!follows(P(pre + "ffn_gate.weight"), P(pre + "ffn_up.weight"))) return -1;
+    if (!moe_ && !follows(P(pre + "ffn_gate.weight"), P(pre + "ffn_up.weight"))) return -1;
   }
   CK(alloc(p32_, n_total_ * 4));
   CK(alloc(phi_, n_total_ * 2));
@@ -399,10 +420,10 @@ int LlamaEngine::realize() {
   lora_bt_.resize(c.n_layers);
   for (int l = 0; l < c.n_layers; ++l) {
     x1_.push_back(f32((long long)N * d));
-    gu_.push_back(f32((long long)N * 2 * ff));
+    gu_.push_back(moe_ ? nullptr : f32((long long)N * 2 * ff));
     h1_.push_back(pl((long long)N * (d + ext_[kGroupQKV])));   // + the q|k|v adapters' u columns
     h2_.push_back(pl((long long)N * (d + ext_[kGroupGU])));    // + the gate|up adapters' u columns
-    a_.push_back(pl((long long)N * a_ld_));   // + the down adapters' u columns
+    a_.push_back(moe_ ? Planes{} : pl((long long)N * a_ld_));   // + the down adapters' u columns
     Qh_.push_back(pl((long long)N * H * dh));
     Kh_.push_back(pl((long long)N * KV * dh));
     Vh_.push_back(pl((long long)N * KV * dh));
@@ -418,6 +439,35 @@ int LlamaEngine::realize() {
       }
   }
   qkv_ = f32((long long)N * W);
+  if (c.qk_norm)
+    for (int l = 0; l < c.n_layers; ++l) qkpre_.push_back(f32((long long)N * (H + KV) * dh));
+  if (moe_) {
+    const int E = c.n_experts, K = c.n_experts_used;
+    const long long NK = (long long)N * K;
+    moe_l_.resize(c.n_layers);
+    for (auto& M : moe_l_) {
+      M.probs = f32((long long)N * E);
+      M.w = f32(NK);
+      M.idx = reinterpret_cast<int*>(f32(NK));
+      M.perm = reinterpret_cast<int*>(f32(NK));
+      M.pos = reinterpret_cast<int*>(f32(NK));
+      M.gu = f32(NK * 2 * ff);
+      M.a = pl(NK * ff);
+      M.ye = f32(NK * d);
+    }
+    moe_logits_ = f32((long long)N * E);
+    moe_xs_ = pl(NK * d);
+    moe_dye_ = pl(NK * d);
+    moe_das_ = f32(NK * ff);
+    moe_dgu_ = pl(NK * 2 * ff);
+    moe_dxs_ = f32(NK * d);
+    moe_dw_ = f32(NK);
+    moe_dlog_ = pl((long long)N * E);
+    moe_hidx_.resize(NK);
+    moe_hperm_.resize(NK);
+    moe_hpos_.resize(NK);
+    use_graph_ = false;   // host round trip per block: eager steps
+  }
   if (!flash_) S_ = f32(att);
   logits_ = f32((long long)N * V);
   loss_rows_ = f32(N);
@@ -695,9 +745,20 @@ int LlamaEngine::init_random(long long seed, double init_scale, double std_all, 
     CK(set_param(pre + "attn_k.weight", wk.data(), (long long)wk.size()));
     CK(set_param(pre + "attn_v.weight", wv.data(), (long long)wv.size()));
     CK(fill(pre + "attn_output.weight", s_d));
-    CK(fill(pre + "ffn_gate.weight", s_d));
-    CK(fill(pre + "ffn_up.weight", s_d));
-    CK(fill(pre + "ffn_down.weight", s_ff));
+    if (moe_) {   // router, then the stacked experts' gate, up and down
+      CK(fill(pre + "ffn_gate_inp.weight", s_emb));
+      CK(fill(pre + "ffn_gate_exps.weight", s_d));
+      CK(fill(pre + "ffn_up_exps.weight", s_d));
+      CK(fill(pre + "ffn_down_exps.weight", s_ff));
+    } else {
+      CK(fill(pre + "ffn_gate.weight", s_d));
+      CK(fill(pre + "ffn_up.weight", s_d));
+      CK(fill(pre + "ffn_down.weight", s_ff));
+    }
+    if (c.qk_norm) {
+      CK(ones(pre + "attn_q_norm.weight"));
+      CK(ones(pre + "attn_k_norm.weight"));
+    }
     if (c.qkv_bias) {
       const double sb = all ? std_all : 0.02;
       CK(fill(pre + "attn_q.bias", sb));
@@ -931,7 +992,8 @@ int kind_of(const char* call) {
       {"launch_adamw", LlamaEngine::kKAdamw},        {"launch_embed", LlamaEngine::kKEmbed},
       {"launch_split", LlamaEngine::kKSplit},        {"launch_q8_0_ring", LlamaEngine::kKSplit},        {"launch_flash_fwd", LlamaEngine::kKFlashFwd},
       {"launch_flash_bwd_prep", LlamaEngine::kKFlashPrep}, {"launch_flash_bwd", LlamaEngine::kKFlashBwd},
-      {"launch_flash_rope", LlamaEngine::kKRope},   {"launch_lora", LlamaEngine::kKLora}};
+      {"launch_flash_rope", LlamaEngine::kKRope},   {"launch_lora", LlamaEngine::kKLora},
+      {"launch_moe", LlamaEngine::kKSwiglu},         {"launch_rms_cols", LlamaEngine::kKRmsFwd}};
   for (const auto& t : table)
     if (strncmp(call, t.prefix, strlen(t.prefix)) == 0) return t.kind;
   return LlamaEngine::kKCount;
@@ -1233,6 +1295,134 @@ int LlamaEngine::lora_group_wgrad(int l, const LoraGroup& G, Planes X, long long
   return 0;
 }
 
+Operand LlamaEngine::expert_op(const Param& p, int e, int rows, int cols, int mn) {
+  // expert e of a stacked Q8_0 tensor: rows x cols quants (row-major) and their scales
+  Operand o = op(Planes{}, rows, cols, cols, mn);
+  const long long first = (long long)e * rows * cols;
+  o.q8 = static_cast<const int8_t*>(q8v_.p) + p.q8v_offset + first;
+  o.q8_scale = static_cast<const uint16_t*>(q8s_.p) + p.q8s_offset + first / 32;
+  return o;
+}
+
+// The MoE FFN of block l: router GEMM, routing, slots ordered by expert on the
+// host, the experts' gate / up GEMMs over their slot rows (Q8_0 dequantised in
+// the GEMM), SwiGLU, down GEMMs, and the weighted sum back onto the tokens
+// with the residual: x[l + 1] = x1 + sum_k w_k y_k.
+int LlamaEngine::moe_forward(int l) {
+  const LlamaConfig& c = cfg_;
+  const int N = this->N(), d = c.d_model, ff = c.d_ff, E = c.n_experts, K = c.n_experts_used;
+  const long long NK = (long long)N * K;
+  const std::string pre = "blk." + std::to_string(l) + ".";
+  MoeLayer& M = moe_l_[l];
+  GemmDesc gr;
+  gr.M = N; gr.N = E; gr.K = d;
+  gr.a = op(h2_[l], N, d, d, 0);
+  gr.b = op(PP(P(pre + "ffn_gate_inp.weight")), E, d, d, 0);
+  gr.epi = epi_rowmajor(kEpiStoreF32, moe_logits_, E);
+  CK(gemm(gr));
+  KL(launch_moe_route(moe_logits_, N, E, K, c.norm_topk, M.probs, M.idx, M.w, stream_));
+  // slots (token * K + choice) in expert order, ascending within an expert
+  CU(cudaMemcpyAsync(moe_hidx_.data(), M.idx, NK * 4, cudaMemcpyDeviceToHost, stream_));
+  CU(cudaStreamSynchronize(stream_));
+  M.count.assign(E, 0);
+  for (long long i = 0; i < NK; ++i) {
+    const int e = moe_hidx_[i];
+    if (e < 0 || e >= E) return -3;
+    ++M.count[e];
+  }
+  M.offset.assign(E + 1, 0);
+  for (int e = 0; e < E; ++e) M.offset[e + 1] = M.offset[e] + M.count[e];
+  std::vector<int> fill(M.offset.begin(), M.offset.end() - 1);
+  for (long long i = 0; i < NK; ++i) {
+    const int at = fill[moe_hidx_[i]]++;
+    moe_hperm_[at] = (int)i;
+    moe_hpos_[i] = at;
+  }
+  CU(cudaMemcpyAsync(M.perm, moe_hperm_.data(), NK * 4, cudaMemcpyHostToDevice, stream_));
+  CU(cudaMemcpyAsync(M.pos, moe_hpos_.data(), NK * 4, cudaMemcpyHostToDevice, stream_));
+  KL(launch_moe_gather(h2_[l], d, M.perm, NK, K, d, moe_xs_, stream_));
+  const Param& Wg = P(pre + "ffn_gate_exps.weight");
+  const Param& Wu = P(pre + "ffn_up_exps.weight");
+  const Param& Wd = P(pre + "ffn_down_exps.weight");
+  for (int e = 0; e < E; ++e) {
+    const int cnt = M.count[e];
+    if (!cnt) continue;
+    const long long off = M.offset[e];
+    for (int h = 0; h < 2; ++h) {   // gate into columns [0, ff), up into [ff, 2 ff)
+      GemmDesc g;
+      g.M = cnt; g.N = ff; g.K = d;
+      g.a = op(offset(moe_xs_, off * d), cnt, d, d, 0);
+      g.b = expert_op(h ? Wu : Wg, e, ff, d, 0);
+      g.epi = epi_rowmajor(kEpiStoreF32, M.gu + off * 2 * ff + h * ff, 2 * ff);
+      CK(gemm(g));
+    }
+  }
+  KL(launch_swiglu_fwd(M.gu, M.a, (int)NK, ff, stream_, ff));
+  for (int e = 0; e < E; ++e) {
+    const int cnt = M.count[e];
+    if (!cnt) continue;
+    const long long off = M.offset[e];
+    GemmDesc g;
+    g.M = cnt; g.N = d; g.K = ff;
+    g.a = op(offset(M.a, off * ff), cnt, ff, ff, 0);
+    g.b = expert_op(Wd, e, d, ff, 0);
+    g.epi = epi_rowmajor(kEpiStoreF32, M.ye + off * d, d);
+    CK(gemm(g));
+  }
+  KL(launch_moe_combine(x1_[l], M.ye, M.pos, M.w, N, K, d, x_[l + 1], stream_));
+  return 0;
+}
+
+// d(h2) of block l's MoE FFN into dh_ from the output gradient dx_: per slot
+// dw = <dy, y> and w dy, back through each expert (down, SwiGLU, gate / up,
+// the frozen Q8_0 weights read MN-major), the router's softmax backward, and
+// the fixed-order sum of the slots' input gradients onto their tokens.
+int LlamaEngine::moe_backward(int l) {
+  const LlamaConfig& c = cfg_;
+  const int N = this->N(), d = c.d_model, ff = c.d_ff, E = c.n_experts, K = c.n_experts_used;
+  const long long NK = (long long)N * K;
+  const std::string pre = "blk." + std::to_string(l) + ".";
+  MoeLayer& M = moe_l_[l];
+  const Param& Wg = P(pre + "ffn_gate_exps.weight");
+  const Param& Wu = P(pre + "ffn_up_exps.weight");
+  const Param& Wd = P(pre + "ffn_down_exps.weight");
+  KL(launch_moe_dy(dx_, M.ye, M.perm, M.w, NK, K, d, moe_dw_, moe_dye_, stream_));
+  for (int e = 0; e < E; ++e) {
+    const int cnt = M.count[e];
+    if (!cnt) continue;
+    const long long off = M.offset[e];
+    GemmDesc g;
+    g.M = cnt; g.N = ff; g.K = d;
+    g.a = op(offset(moe_dye_, off * d), cnt, d, d, 0);
+    g.b = expert_op(Wd, e, d, ff, 1);
+    g.epi = epi_rowmajor(kEpiStoreF32, moe_das_ + off * ff, ff);
+    CK(gemm(g));
+  }
+  KL(launch_swiglu_bwd(M.gu, moe_das_, moe_dgu_, (int)NK, ff, stream_, 2 * ff));
+  for (int e = 0; e < E; ++e) {
+    const int cnt = M.count[e];
+    if (!cnt) continue;
+    const long long off = M.offset[e];
+    for (int h = 0; h < 2; ++h) {   // dxs = dgate Wg_e + dup Wu_e
+      GemmDesc g;
+      g.M = cnt; g.N = d; g.K = ff;
+      g.a = op(offset(moe_dgu_, off * 2 * ff + h * ff), cnt, ff, 2 * ff, 0);
+      g.b = expert_op(h ? Wu : Wg, e, ff, d, 1);
+      g.epi = epi_rowmajor(h ? kEpiAccumF32 : kEpiStoreF32, moe_dxs_ + off * d, d);
+      CK(gemm(g));
+    }
+  }
+  KL(launch_moe_router_bwd(M.probs, M.idx, M.w, moe_dw_, N, E, K, c.norm_topk, moe_dlog_, stream_));
+  GemmDesc gr;
+  gr.M = N; gr.N = d; gr.K = E;
+  gr.a = op(moe_dlog_, N, E, E, 0);
+  gr.b = op(PP(P(pre + "ffn_gate_inp.weight")), E, d, d, 1);
+  gr.epi = epi_rowmajor(kEpiStoreF32, dh_, d);
+  CK(gemm(gr));
+  KL(launch_moe_gather_sum(moe_dxs_, M.pos, N, K, d, dh_, stream_));
+  return 0;
+}
+
 int LlamaEngine::enqueue_forward() {
   const LlamaConfig& c = cfg_;
   const int N = this->N(), d = c.d_model, H = c.n_heads, KV = c.n_kv, dh = c.d_head, ff = c.d_ff, T = c.T, B = c.B;
@@ -1270,7 +1460,7 @@ int LlamaEngine::enqueue_forward() {
     const float* bias = c.qkv_bias ? P32(P(pre + "attn_q.bias")) : nullptr;
     const int qkv_t[3] = {kLoraQ, kLoraK, kLoraV};
     const int qkv_c0[3] = {0, H * dh, (H + KV) * dh}, qkv_w[3] = {H * dh, KV * dh, KV * dh};
-    if (dh == 64) {
+    if (dh == 64 && !c.qk_norm) {
       // one launch: q|k|v projection, adapters, bias, RoPE, head-major Q / K / V planes
       g.epi.mode = kEpiRopeQKV;
       RopeOut& ro = g.epi.rope;
@@ -1284,6 +1474,12 @@ int LlamaEngine::enqueue_forward() {
       g.epi = epi_rowmajor(kEpiStoreF32, qkv_, W);
       CK(gemm(g));
       for (int i = 0; i < Gq.n && !eq; ++i) CK(lora_forward(l, Gq.t[i], qkv_, W, Gq.c0[i], Gq.w[i]));
+      if (c.qk_norm) {   // RMSNorm over the whole q and k vectors, before RoPE; pre-norm values kept
+        KL(launch_rms_cols_fwd(qkv_, W, 0, H * dh, P32(P(pre + "attn_q_norm.weight")), c.rms_eps, N, qkpre_[l],
+                               stream_));
+        KL(launch_rms_cols_fwd(qkv_, W, H * dh, KV * dh, P32(P(pre + "attn_k_norm.weight")), c.rms_eps, N,
+                               qkpre_[l] + (long long)N * H * dh, stream_));
+      }
       KL(launch_rope_qkv_fwd(qkv_, bias, pos_, cs_, cs_rows_, Qh_[l], Kh_[l], Vh_[l], B, T, H, KV, dh, stream_));
     }
     if (flash_) {
@@ -1327,6 +1523,10 @@ int LlamaEngine::enqueue_forward() {
     const LoraGroup Gg = lora_group(kGroupGU);
     const int eg = ext_[kGroupGU];
     CK(rmsnorm_lora(l, x1_[l], P32(P(pre + "ffn_norm.weight")), h2_[l], Gg, d + eg));   // + the adapters' u
+    if (moe_) {
+      CK(moe_forward(l));
+      continue;
+    }
     GemmDesc gg;
     gg.M = N; gg.N = 2 * ff; gg.K = d + eg;
     gg.a = op(h2_[l], N, d + eg, d + eg, 0);
@@ -1420,11 +1620,14 @@ int LlamaEngine::enqueue_backward() {
     const std::string pre = "blk." + std::to_string(l) + ".";
     CK(dequant_layer(l));   // the forward's last two blocks are still in the ring
     CK(fill_ahead(l - 1));
-    const Param& Wd = P(pre + "ffn_down.weight");
-    const Param& Wg = P(pre + "ffn_gate.weight");
     const Param& Wo = P(pre + "attn_output.weight");
     const Param& Wq = P(pre + "attn_q.weight");
     // ---- FFN
+    if (moe_) {
+      CK(moe_backward(l));
+    } else {
+    const Param& Wd = P(pre + "ffn_down.weight");
+    const Param& Wg = P(pre + "ffn_gate.weight");
     const int ed = ext_[kGroupDown];   // dY carries du of the down adapter in its extra columns
     GemmDesc gda;
     gda.M = N; gda.N = ff; gda.K = d + ed;
@@ -1477,6 +1680,7 @@ int LlamaEngine::enqueue_backward() {
     }
     for (int i = 0; i < Gg.n && !gg_grp; ++i)
       CK(lora_backward(l, Gg.t[i], h2_[l], d, dgu_, 2 * ff, Gg.c0[i], Gg.w[i], dh_, nullptr));
+    }
     const Param& g2 = P(pre + "ffn_norm.weight");
     CK(norm_bwd(x1_[l], P32(g2), dx_, g2));
     // ---- attention output projection: dO (head-major f32), dWo
@@ -1548,6 +1752,12 @@ int LlamaEngine::enqueue_backward() {
       CK(gemm(gv));
       KL(launch_rope_qkv_bwd(dQ_, dK_, dV_, pos_, cs_, cs_rows_, dqkv_, c.qkv_bias ? qkv_ : nullptr, B, T, H, KV, dh,
                              stream_, W + ext_[kGroupQKV]));
+    }
+    if (c.qk_norm) {   // back through the whole-vector q / k RMSNorm, on the gradient planes in place
+      KL(launch_rms_cols_bwd(dqkv_, W + ext_[kGroupQKV], 0, H * dh, P32(P(pre + "attn_q_norm.weight")), qkpre_[l],
+                             c.rms_eps, N, stream_));
+      KL(launch_rms_cols_bwd(dqkv_, W + ext_[kGroupQKV], H * dh, KV * dh, P32(P(pre + "attn_k_norm.weight")),
+                             qkpre_[l] + (long long)N * H * dh, c.rms_eps, N, stream_));
     }
     if (c.qkv_bias && full) KL(launch_colsum_rows(qkv_, N, W, G32(P(pre + "attn_q.bias")), stream_));
     // ---- QKV projection

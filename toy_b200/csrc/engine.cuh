@@ -32,6 +32,13 @@ struct LlamaConfig {
   // attn_q.lora_a [H r][d] and attn_q.lora_b [H d_head][r]; needs the Q8_0
   // plane ring (base mode 1)
   int lora_per_head_q = 0;
+  // mixture of experts in every block's FFN (QLoRA only): n_experts routed by
+  // a frozen f32 router, the top n_experts_used per token (norm_topk: their
+  // weights renormalised to sum 1), expert SwiGLU FFNs of width d_ff as frozen
+  // Q8_0 -- the OLMoE block (llama_kv_engine.rb build_moe_ffn :2073)
+  int n_experts = 0, n_experts_used = 0, norm_topk = 0;
+  // 2: RMSNorm over the whole q and k vectors before RoPE (frozen gammas)
+  int qk_norm = 0;
 };
 
 // One named parameter inside the arenas.
@@ -260,6 +267,26 @@ class LlamaEngine {
   // [H d_head][H r] product whose diagonal blocks are kept.
   bool per_head_ = false;
   float* bd_dense_ = nullptr;
+  // Mixture of experts: the step runs eagerly (each block's expert counts come
+  // back to the host, which orders the (token, choice) slots by expert and
+  // sizes one Q8_0 GEMM per expert and projection). Per block the router's
+  // probabilities, the choices and weights, the slot order and its inverse,
+  // the experts' gate|up (f32), SwiGLU (planes) and output (f32) per slot.
+  bool moe_ = false;
+  struct MoeLayer {
+    float *probs = nullptr, *w = nullptr, *gu = nullptr, *ye = nullptr;
+    int *idx = nullptr, *perm = nullptr, *pos = nullptr;
+    Planes a;
+    std::vector<int> count, offset;
+  };
+  std::vector<MoeLayer> moe_l_;
+  float *moe_logits_ = nullptr, *moe_das_ = nullptr, *moe_dxs_ = nullptr, *moe_dw_ = nullptr;
+  Planes moe_xs_, moe_dye_, moe_dgu_, moe_dlog_;
+  std::vector<int> moe_hidx_, moe_hperm_, moe_hpos_;
+  std::vector<float*> qkpre_;   // QK-norm: per block the pre-norm q | k [N][(H + KV) d_head]
+  int moe_forward(int l);
+  int moe_backward(int l);
+  Operand expert_op(const Param& p, int e, int rows, int cols, int mn);
   Planes ring_ext_b(int l) const;   // B's extension block of block l's q|k|v ring operand
   float* P32(const Param& p) { return static_cast<float*>(p32_.p) + p.offset; }
   float* G32(const Param& p) { return static_cast<float*>(g_.p) + p.offset; }

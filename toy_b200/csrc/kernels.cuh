@@ -164,3 +164,21 @@ int launch_colsum_rows(const float* x, int N, int W, float* out, cudaStream_t st
 int launch_add_inplace(float* y, const float* x, long long n, cudaStream_t st);
 
 }  // namespace tb2
+
+namespace tb2 {
+// ---- mixture-of-experts FFN and QK-RMSNorm (moe.cu)
+int launch_moe_route(const float* logits, int N, int E, int K, int norm_topk, float* probs, int* idx, float* w,
+                     cudaStream_t st);
+int launch_moe_gather(Planes h, long long ldh, const int* perm, long long NK, int K, int d, Planes xs, cudaStream_t st);
+int launch_moe_combine(const float* x1, const float* ye, const int* pos, const float* w, int N, int K, int d, float* x2,
+                       cudaStream_t st);
+int launch_moe_dy(const float* dy, const float* ye, const int* perm, const float* w, long long NK, int K, int d,
+                  float* dw, Planes dye, cudaStream_t st);
+int launch_moe_router_bwd(const float* probs, const int* idx, const float* w, const float* dw, int N, int E, int K,
+                          int norm_topk, Planes dlog, cudaStream_t st);
+int launch_moe_gather_sum(const float* dxs, const int* pos, int N, int K, int d, float* dh, cudaStream_t st);
+int launch_rms_cols_fwd(float* x, long long ld, int c0, int width, const float* g, float eps, int N, float* pre,
+                        cudaStream_t st);
+int launch_rms_cols_bwd(Planes dy, long long ld, int c0, int width, const float* g, const float* pre, float eps, int N,
+                        cudaStream_t st);
+}  // namespace tb2

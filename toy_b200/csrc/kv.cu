@@ -14,8 +14,9 @@
 // an append kernel (bias, NEOX RoPE from the training engine's table, K / V
 // written into the cache -- quantised to Q8_0 with ggml's quantiser when the
 // cache is Q8_0), a split-history flash-decode attention (per query head and
-// 256-key chunk: online softmax over the chunk, GQA by reading KV head h / G),
-// the combine of the chunks, the o GEMV with the residual add, the gate|up
+// 128-key chunk, one key per thread; GQA by reading KV head h / G), the o GEMV
+// that assembles the chunks' partial softmax sums while it stages its input and
+// adds the residual, the gate|up
 // GEMV (RMSNorm folded, SwiGLU on the paired rows) and the down GEMV with the
 // residual add; then the final norm folded into the LM-head GEMV. The whole
 // step is one CUDA graph; tokens and positions are copied in before it.
@@ -41,7 +42,7 @@ namespace tb2 {
 namespace {
 
 constexpr int kGemvWarps = 8;
-constexpr int kChunk = 256;   // keys per attention CTA
+constexpr int kChunk = 128;   // keys per attention CTA (one per thread)
 constexpr int kMaxSeq = 16;
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -73,6 +74,10 @@ struct GemvArgs {
   long long ldo = 0;
   const float* res = nullptr;      // [n_seq][ldo]
   int mode = 0, pair = 0;
+  // x is the attention output to assemble from the chunks' partials
+  // [n_seq][H][nsplit][dh + 2] (o, m, l): x[b][h dh + d] = sum_s o_s e^(m_s - m) / sum_s l_s e^(m_s - m)
+  const float* part = nullptr;
+  int nsplit = 0, dh = 0;
 };
 
 template <int NB, bool Q8>
@@ -81,9 +86,28 @@ __global__ void __launch_bounds__(256) kv_gemv_kernel(const GemvArgs a) {
   __shared__ float rs[NB];
   griddep_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = threadIdx.x; i < NB * a.K; i += blockDim.x) {
-    const int b = i / a.K, k = i % a.K;
-    xs[i] = a.x[(long long)b * a.ldx + k] * (a.gamma ? a.gamma[k] : 1.0f);
+  if (a.part) {
+    const int H = a.K / a.dh;
+    for (int i = threadIdx.x; i < NB * a.K; i += blockDim.x) {
+      const int b = i / a.K, k = i % a.K, hh = k / a.dh, dd = k % a.dh;
+      const float* p = a.part + ((long long)b * H + hh) * a.nsplit * (a.dh + 2);
+      float m = -INFINITY;
+      for (int sp = 0; sp < a.nsplit; ++sp) m = fmaxf(m, p[sp * (a.dh + 2) + a.dh]);
+      float l = 0.f, o = 0.f;
+      for (int sp = 0; sp < a.nsplit; ++sp) {
+        const float ms = p[sp * (a.dh + 2) + a.dh];
+        if (ms == -INFINITY) continue;
+        const float f = expf(ms - m);
+        l += p[sp * (a.dh + 2) + a.dh + 1] * f;
+        o += p[sp * (a.dh + 2) + dd] * f;
+      }
+      xs[i] = o / l;
+    }
+  } else {
+    for (int i = threadIdx.x; i < NB * a.K; i += blockDim.x) {
+      const int b = i / a.K, k = i % a.K;
+      xs[i] = a.x[(long long)b * a.ldx + k] * (a.gamma ? a.gamma[k] : 1.0f);
+    }
   }
   if (a.gamma) {   // per-sequence rsqrt(mean x^2 + eps): one warp per sequence
     for (int b = warp; b < NB; b += kGemvWarps) {
@@ -112,6 +136,7 @@ __global__ void __launch_bounds__(256) kv_gemv_kernel(const GemvArgs a) {
       if (Q8) {
         const int8_t* q = a.wq + row * a.K;
         const uint16_t* sc = a.ws + row * (a.K / 32);
+#pragma unroll 3
         for (int c = lane; c < a.K / 16; c += 32) {
           const int4 raw = __ldg(reinterpret_cast<const int4*>(q + c * 16));
           const float d = __half2float(__ushort_as_half(__ldg(sc + c / 2)));
@@ -125,6 +150,7 @@ __global__ void __launch_bounds__(256) kv_gemv_kernel(const GemvArgs a) {
         }
       } else {
         const float* wr = a.w32 + row * a.K;
+#pragma unroll 5
         for (int c = lane; c < a.K / 4; c += 32) {
           const float4 wv = __ldg(reinterpret_cast<const float4*>(wr + c * 4));
 #pragma unroll
@@ -248,80 +274,101 @@ __device__ __forceinline__ float cache_val(const KvCache& c, bool v, long long s
   return __half2float(__ushort_as_half(s[slot * (dh / 32) + d / 32])) * (float)q[slot * dh + d];
 }
 
-// grid (n_seq * H, nsplit), block 128: keys [split * kChunk, ...) of the history
-template <int DPL>   // head dims per lane (dh / 32)
-__global__ void __launch_bounds__(128) kv_attn_kernel(const AttnArgs a) {
-  __shared__ float sm[4][2 + 32 * DPL];
+// grid (n_seq * H, nsplit), block 128: keys [split * kChunk, ...) of the
+// history. Scores: one key per thread (its K row read as 16-byte vectors, q
+// from shared memory); the chunk's max and sum by block reductions; P V: each
+// thread owns one head dimension for a slice of the keys, reading V rows
+// coalesced across threads, P from shared memory. Writes the chunk's
+// unnormalised o, its max m and its sum l.
+__global__ void __launch_bounds__(kChunk) kv_attn_kernel(const AttnArgs a) {
+  __shared__ float qs[128];
+  __shared__ float ps[kChunk];
+  __shared__ float red[kChunk / 32];
+  __shared__ float osum[kChunk];
   griddep_wait();
   const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H, j = h / (a.H / a.KV), split = blockIdx.y;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, dh = a.dh;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, dh = a.dh;
   const int hist = a.pos[b] + 1;
   const int t0 = split * kChunk, t1 = min(t0 + kChunk, hist);
-  const float* q = a.qkv + (long long)b * (a.H + 2 * a.KV) * dh + h * dh;
-  float qv[DPL], o[DPL];
-#pragma unroll
-  for (int e = 0; e < DPL; ++e) {
-    qv[e] = q[lane + 32 * e];
-    o[e] = 0.f;
-  }
-  float m = -INFINITY, l = 0.f;
-  const long long base = ((long long)b * a.KV + j) * a.max_T;
-  for (int t = t0 + warp; t < t1; t += 4) {
-    float s = 0.f;
-#pragma unroll
-    for (int e = 0; e < DPL; ++e) s += qv[e] * cache_val(a.c, false, base + t, dh, lane + 32 * e);
-    s = warp_sum(s) * a.scale;
-    const float mn = fmaxf(m, s);
-    const float corr = expf(m - mn), pe = expf(s - mn);
-    l = l * corr + pe;
-#pragma unroll
-    for (int e = 0; e < DPL; ++e) o[e] = o[e] * corr + pe * cache_val(a.c, true, base + t, dh, lane + 32 * e);
-    m = mn;
-  }
-  if (lane == 0) {
-    sm[warp][0] = m;
-    sm[warp][1] = l;
-  }
-#pragma unroll
-  for (int e = 0; e < DPL; ++e) sm[warp][2 + lane + 32 * e] = o[e];
-  __syncthreads();
-  if (warp) return;
-  float mm = -INFINITY;
-  for (int w = 0; w < 4; ++w) mm = fmaxf(mm, sm[w][0]);
   float* out = a.part + ((long long)bh * a.nsplit + split) * (dh + 2);
-  float lt = 0.f, ot[DPL];
-#pragma unroll
-  for (int e = 0; e < DPL; ++e) ot[e] = 0.f;
-  for (int w = 0; w < 4; ++w) {
-    const float f = sm[w][0] == -INFINITY ? 0.f : expf(sm[w][0] - mm);
-    lt += sm[w][1] * f;
-#pragma unroll
-    for (int e = 0; e < DPL; ++e) ot[e] += sm[w][2 + lane + 32 * e] * f;
+  if (t0 >= t1) {   // this chunk is past the history
+    for (int d = tid; d < dh; d += blockDim.x) out[d] = 0.f;
+    if (tid == 0) {
+      out[dh] = -INFINITY;
+      out[dh + 1] = 0.f;
+    }
+    return;
   }
+  const float* q = a.qkv + (long long)b * (a.H + 2 * a.KV) * dh + h * dh;
+  for (int d = tid; d < dh; d += blockDim.x) qs[d] = q[d];
+  __syncthreads();
+  const long long base = ((long long)b * a.KV + j) * a.max_T;
+  const int t = t0 + tid;
+  float s = -INFINITY;
+  if (t < t1) {
+    float acc = 0.f;
+    const long long slot = base + t;
+    if (a.c.k32) {
+      const float4* kr = reinterpret_cast<const float4*>(a.c.k32 + slot * dh);
+#pragma unroll 8
+      for (int c = 0; c < dh / 4; ++c) {
+        const float4 kv = __ldg(kr + c);
+        acc += kv.x * qs[4 * c] + kv.y * qs[4 * c + 1] + kv.z * qs[4 * c + 2] + kv.w * qs[4 * c + 3];
+      }
+    } else {
+      const int4* kr = reinterpret_cast<const int4*>(a.c.kq + slot * dh);
+      const uint16_t* ks = a.c.ks + slot * (dh / 32);
+#pragma unroll 4
+      for (int c = 0; c < dh / 16; ++c) {
+        const int4 raw = __ldg(kr + c);
+        const int8_t* qb = reinterpret_cast<const int8_t*>(&raw);
+        const float sc = __half2float(__ushort_as_half(__ldg(ks + c / 2)));
+        float part = 0.f;
 #pragma unroll
-  for (int e = 0; e < DPL; ++e) out[lane + 32 * e] = ot[e];
-  if (lane == 0) {
-    out[dh] = mm;
-    out[dh + 1] = lt;
+        for (int e = 0; e < 16; ++e) part += (float)qb[e] * qs[16 * c + e];
+        acc += sc * part;
+      }
+    }
+    s = acc * a.scale;
   }
-}
-
-// grid n_seq * H, block dh: att[b][h dh + d] = sum_s o_s e^(m_s - m) / sum_s l_s e^(m_s - m)
-__global__ void kv_combine_kernel(const float* __restrict__ part, int H, int nsplit, int dh, float* __restrict__ att) {
-  griddep_wait();
-  const int bh = blockIdx.x, d = threadIdx.x;
-  const float* p = part + (long long)bh * nsplit * (dh + 2);
-  float m = -INFINITY;
-  for (int s = 0; s < nsplit; ++s) m = fmaxf(m, p[s * (dh + 2) + dh]);
-  float l = 0.f, o = 0.f;
-  for (int s = 0; s < nsplit; ++s) {
-    const float ms = p[s * (dh + 2) + dh];
-    if (ms == -INFINITY) continue;
-    const float f = expf(ms - m);
-    l += p[s * (dh + 2) + dh + 1] * f;
-    o += p[s * (dh + 2) + d] * f;
+  float m = warp_max(s);
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  m = red[0];
+  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
+  const float p = t < t1 ? expf(s - m) : 0.f;
+  ps[tid] = p;
+  __syncthreads();   // red is read above before it is reused below
+  float l = warp_sum(p);
+  if (lane == 0) red[warp] = l;
+  __syncthreads();
+  l = 0.f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) l += red[w];
+  // P V: thread (g, d) sums keys g, g + G, ... of the chunk for dimension d (G = blockDim / dh groups)
+  const int groups = blockDim.x / dh, g = tid / dh, d = tid % dh;
+  float o = 0.f;
+  if (g < groups) {
+    const int n = t1 - t0;
+#pragma unroll 8
+    for (int k = g; k < n; k += groups) {
+      const long long slot = base + t0 + k;
+      const float v = a.c.v32 ? __ldg(a.c.v32 + slot * dh + d)
+                              : __half2float(__ushort_as_half(__ldg(a.c.vs + slot * (dh / 32) + d / 32))) *
+                                    (float)__ldg(a.c.vq + slot * dh + d);
+      o += ps[k] * v;
+    }
   }
-  att[(long long)bh * dh + d] = o / l;
+  osum[tid] = o;
+  __syncthreads();
+  if (tid < dh) {
+    float acc = 0.f;
+    for (int gg = 0; gg < groups; ++gg) acc += osum[gg * dh + tid];
+    out[tid] = acc;
+  }
+  if (tid == 0) {
+    out[dh] = m;
+    out[dh + 1] = l;
+  }
 }
 
 }  // namespace
@@ -358,7 +405,6 @@ class KvEngine {
     x_ = f32((long long)nb_ * d);
     x1_ = f32((long long)nb_ * d);
     qkv_ = f32((long long)nb_ * W);
-    att_ = f32((long long)nb_ * H * dh);
     a_ = f32((long long)nb_ * ff);
     part_ = f32((long long)nb_ * H * nsplit_ * (dh + 2));
     logits_ = f32((long long)nb_ * V);
@@ -543,18 +589,11 @@ class KvEngine {
       at.qkv = qkv_; at.pos = pos_; at.c = cache; at.H = H; at.KV = KV; at.dh = dh; at.max_T = max_T_;
       at.nsplit = nsplit_; at.scale = 1.0f / std::sqrt((float)dh); at.part = part_;
       ++launches_;
-      const dim3 ag(nb_ * H, nsplit_);
-      const int rc_a = dh == 32 ? launch_pdl(kv_attn_kernel<1>, ag, dim3(128), 0, st_, at)
-                       : dh == 64 ? launch_pdl(kv_attn_kernel<2>, ag, dim3(128), 0, st_, at)
-                       : dh == 96 ? launch_pdl(kv_attn_kernel<3>, ag, dim3(128), 0, st_, at)
-                                  : launch_pdl(kv_attn_kernel<4>, ag, dim3(128), 0, st_, at);
-      if (rc_a) return -3;
-      ++launches_;
-      if (launch_pdl(kv_combine_kernel, dim3(nb_ * H), dim3(dh), 0, st_, (const float*)part_, H, nsplit_, dh, att_))
-        return -3;
-      // x1 = x + att Wo^T
+      if (launch_pdl(kv_attn_kernel, dim3(nb_ * H, nsplit_), dim3(kChunk), 0, st_, at)) return -3;
+      // x1 = x + att Wo^T, the attention output assembled from the chunks while staging
       g = wargs(pre + "attn_output.weight", d, H * dh);
-      g.x = att_; g.ldx = H * dh; g.out = x1_; g.ldo = d; g.res = x_; g.mode = 1;
+      g.part = part_; g.nsplit = nsplit_; g.dh = dh;
+      g.ldx = H * dh; g.out = x1_; g.ldo = d; g.res = x_; g.mode = 1;
       if (int rc = gemv(g)) return rc;
       // a = silu(h2 Wg^T) * (h2 Wu^T), the FFN RMSNorm folded in (gate | up rows paired)
       g = wargs(pre + "ffn_gate.weight", 2 * ff, d);
@@ -580,7 +619,7 @@ class KvEngine {
   cudaStream_t st_ = nullptr;
   cudaGraphExec_t graph_ = nullptr;
   std::vector<void*> bufs_;
-  float *x_ = nullptr, *x1_ = nullptr, *qkv_ = nullptr, *att_ = nullptr, *a_ = nullptr, *part_ = nullptr,
+  float *x_ = nullptr, *x1_ = nullptr, *qkv_ = nullptr, *a_ = nullptr, *part_ = nullptr,
         *logits_ = nullptr;
   float *k32_ = nullptr, *v32_ = nullptr;
   int8_t *kq_ = nullptr, *vq_ = nullptr;

@@ -41,6 +41,18 @@ class LlamaConfig:
     tied: bool = True
     qkv_bias: bool = False
     rope_freq_factors: Optional[Sequence[float]] = None
+    # mixture-of-experts FFN (QLoRA): n_experts, the top n_experts_used per token,
+    # expert width d_ff; qk_norm 2 = RMSNorm over the whole q and k vectors
+    n_experts: int = 0
+    n_experts_used: int = 0
+    norm_topk: bool = False
+    qk_norm: int = 0
+
+    @staticmethod
+    def olmoe_1b_7b() -> "LlamaConfig":
+        """OLMoE-1B-7B shape: 64 experts, top 8, expert FFN 1024, QK-RMSNorm."""
+        return LlamaConfig(50304, 2048, 16, 16, 128, 1024, 16, 1.0e4, 1.0e-5, n_experts=64, n_experts_used=8,
+                           qk_norm=2)
 
     @staticmethod
     def smollm2_135m() -> "LlamaConfig":
@@ -134,6 +146,8 @@ class LlamaSeqEngine:
         if opts.attention not in ("flash", "materialized"):
             raise ValueError(f"unknown attention implementation {opts.attention!r}")
         c.attn_impl = 0 if opts.attention == "flash" else 1
+        c.n_experts, c.n_experts_used = cfg.n_experts, cfg.n_experts_used
+        c.norm_topk, c.qk_norm = 1 if cfg.norm_topk else 0, cfg.qk_norm
         if lora is not None:
             c.lora_rank, c.lora_alpha = lora.rank, lora.alpha
             c.lora_targets = sum(LORA_BITS[t] for t in lora.targets)
