@@ -82,47 +82,61 @@ struct GemvArgs {
 
 template <int NB, bool Q8>
 __global__ void __launch_bounds__(256) kv_gemv_kernel(const GemvArgs a) {
-  extern __shared__ float xs[];   // [NB][K]: x * gamma
+  // xs [NB][K]: the input rows (times gamma when a norm is folded in); with the
+  // attention partials, fs [NB][H][nsplit] holds each chunk's factor e^(m_s - m) / L
+  extern __shared__ float xs[];
   __shared__ float rs[NB];
   griddep_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (a.part) {
-    const int H = a.K / a.dh;
+    const int H = a.K / a.dh, ns = a.nsplit, stride = a.dh + 2;
+    float* fs = xs + NB * a.K;
+    for (int j = threadIdx.x; j < NB * H; j += blockDim.x) {
+      const float* p = a.part + (long long)j * ns * stride;
+      float m = -INFINITY;
+      for (int sp = 0; sp < ns; ++sp) m = fmaxf(m, p[sp * stride + a.dh]);
+      float l = 0.f;
+      for (int sp = 0; sp < ns; ++sp) {
+        const float ms = p[sp * stride + a.dh];
+        const float f = ms == -INFINITY ? 0.f : expf(ms - m);
+        fs[j * ns + sp] = f;
+        l += p[sp * stride + a.dh + 1] * f;
+      }
+      for (int sp = 0; sp < ns; ++sp) fs[j * ns + sp] /= l;
+    }
+    __syncthreads();
     for (int i = threadIdx.x; i < NB * a.K; i += blockDim.x) {
       const int b = i / a.K, k = i % a.K, hh = k / a.dh, dd = k % a.dh;
-      const float* p = a.part + ((long long)b * H + hh) * a.nsplit * (a.dh + 2);
-      float m = -INFINITY;
-      for (int sp = 0; sp < a.nsplit; ++sp) m = fmaxf(m, p[sp * (a.dh + 2) + a.dh]);
-      float l = 0.f, o = 0.f;
-      for (int sp = 0; sp < a.nsplit; ++sp) {
-        const float ms = p[sp * (a.dh + 2) + a.dh];
-        if (ms == -INFINITY) continue;
-        const float f = expf(ms - m);
-        l += p[sp * (a.dh + 2) + a.dh + 1] * f;
-        o += p[sp * (a.dh + 2) + dd] * f;
-      }
-      xs[i] = o / l;
+      const float* p = a.part + ((long long)b * H + hh) * ns * stride + dd;
+      const float* f = fs + (b * H + hh) * ns;
+      float o = 0.f;
+#pragma unroll 4
+      for (int sp = 0; sp < ns; ++sp) o += p[sp * stride] * f[sp];
+      xs[i] = o;
     }
   } else {
+#pragma unroll 4
     for (int i = threadIdx.x; i < NB * a.K; i += blockDim.x) {
       const int b = i / a.K, k = i % a.K;
-      xs[i] = a.x[(long long)b * a.ldx + k] * (a.gamma ? a.gamma[k] : 1.0f);
+      xs[i] = a.x[(long long)b * a.ldx + k];
     }
   }
-  if (a.gamma) {   // per-sequence rsqrt(mean x^2 + eps): one warp per sequence
+  if (!a.gamma && threadIdx.x < NB) rs[threadIdx.x] = 1.0f;
+  __syncthreads();
+  if (a.gamma) {   // per-sequence rsqrt(mean x^2 + eps) from shared memory, then x * gamma in place
     for (int b = warp; b < NB; b += kGemvWarps) {
       float s = 0.f;
       for (int k = lane; k < a.K; k += 32) {
-        const float v = a.x[(long long)b * a.ldx + k];
+        const float v = xs[b * a.K + k];
         s += v * v;
       }
       s = warp_sum(s);
       if (lane == 0) rs[b] = rsqrtf(s / (float)a.K + a.eps);
     }
-  } else if (threadIdx.x < NB) {
-    rs[threadIdx.x] = 1.0f;
+    __syncthreads();
+    for (int i = threadIdx.x; i < NB * a.K; i += blockDim.x) xs[i] *= a.gamma[i % a.K];
+    __syncthreads();
   }
-  __syncthreads();
   const int n_out = a.mode == 2 ? a.pair : a.rows;
   for (int n = blockIdx.x * kGemvWarps + warp; n < n_out; n += gridDim.x * kGemvWarps) {
     float acc[2][NB];
@@ -389,7 +403,10 @@ class KvEngine {
     const LlamaConfig& c = e_.cfg();
     if (max_T_ < 1 || max_T_ > e_.rope_rows() || nb_ < 1 || (nb_ > 8 && nb_ != kMaxSeq)) return -1;
     if (c.d_head % 32 || c.d_head > 128 || c.d_model % 16 || c.d_ff % 16) return -1;
-    if ((long long)nb_ * std::max(c.d_ff, std::max(c.d_model, c.n_heads * c.d_head)) * 4 > 200 * 1024) return -1;
+    const long long nsplit = (max_T_ + kChunk - 1) / kChunk;
+    if (((long long)nb_ * std::max(c.d_ff, std::max(c.d_model, c.n_heads * c.d_head)) +
+         (long long)nb_ * c.n_heads * nsplit) * 4 > 200 * 1024)
+      return -1;
     if (cudaSetDevice(e_.device()) != cudaSuccess) return -3;
     if (cudaStreamCreateWithFlags(&st_, cudaStreamNonBlocking) != cudaSuccess) return -3;
     const int d = c.d_model, H = c.n_heads, KV = c.n_kv, dh = c.d_head, ff = c.d_ff, V = c.vocab, L = c.n_layers;
@@ -515,7 +532,7 @@ class KvEngine {
   template <int NB>
   int gemv_nb(const GemvArgs& g) {
     const bool q8 = g.wq != nullptr;
-    const size_t smem = (size_t)NB * g.K * 4;
+    const size_t smem = ((size_t)NB * g.K + (g.part ? (size_t)NB * (g.K / g.dh) * g.nsplit : 0)) * 4;
     auto* k = q8 ? kv_gemv_kernel<NB, true> : kv_gemv_kernel<NB, false>;
     static DeviceOnce setup[2];
     if (setup[q8].ensure([&](int) {
