@@ -53,7 +53,6 @@ struct KArgs {
   int tiles_m, tiles_n, splits, units, kb_total, causal;
   Epilogue epi;
   float* ws;
-  int* sem;
   int* err;
   const uint16_t* q8_scale;   // Q8_0 B operand: scales and stored extent
   int q8_rows, q8_cols;
@@ -1061,7 +1060,6 @@ int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream
   k.units = (int)(tiles * splits);
   k.epi = d.epi;
   k.ws = sc.ws;
-  k.sem = sc.sem;
   k.err = dev_err;
   k.q8_scale = d.b.q8_scale;
   k.q8_rows = d.b.rows;

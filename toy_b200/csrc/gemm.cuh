@@ -120,13 +120,11 @@ struct GemmDesc {
   Epilogue epi;
 };
 
-// Split-K workspace: f32 partial tiles and per-tile arrival counters (zero at
-// rest; the reducing CTA resets its counter). One GEMM at a time may use it.
+// Split-K workspace: f32 partial tiles, summed by a separate reduce launch.
+// One GEMM at a time may use it.
 struct GemmScratch {
   float* ws = nullptr;
   long long ws_floats = 0;
-  int* sem = nullptr;
-  long long sem_count = 0;
 };
 
 // Enqueue the GEMM on `stream`. Returns 0 on success, negative on a rejected

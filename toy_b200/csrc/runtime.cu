@@ -11,7 +11,6 @@ std::mutex g_mu;
 int* g_err[64] = {nullptr};
 GemmScratch g_scratch[64];
 constexpr long long kWsFloats = 16LL << 20;   // 64 MiB
-constexpr long long kSemCount = 64LL << 10;
 }  // namespace
 
 const GemmScratch& gemm_scratch() {
@@ -22,16 +21,9 @@ const GemmScratch& gemm_scratch() {
   GemmScratch& s = g_scratch[dev];
   if (!s.ws) {
     float* ws = nullptr;
-    int* sem = nullptr;
     if (cudaMalloc(&ws, kWsFloats * sizeof(float)) != cudaSuccess) return none;
-    if (cudaMalloc(&sem, kSemCount * sizeof(int)) != cudaSuccess || cudaMemset(sem, 0, kSemCount * sizeof(int)) != cudaSuccess) {
-      cudaFree(ws);
-      return none;
-    }
     s.ws = ws;
     s.ws_floats = kWsFloats;
-    s.sem = sem;
-    s.sem_count = kSemCount;
   }
   return s;
 }
