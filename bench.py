@@ -363,6 +363,8 @@ def main():
     ap.add_argument("--batch", type=int, default=0, help="override sequences per GPU (small profiling cases)")
     ap.add_argument("--layers", type=int, default=0,
                     help="override the decoder depth (small profiling cases; recorded in config)")
+    ap.add_argument("--q8-ring-l2", type=int, default=1, choices=[0, 1],
+                    help="QLoRA plane ring kept resident in the L2 (1, the library default) or not")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     wl = dict(WORKLOADS[args.workload])
@@ -375,6 +377,8 @@ def main():
 
     rank, world, local = dist_env()
     from toy_b200 import LlamaConfig
+    from toy_b200._lib import lib
+    lib().tb2_set_q8_ring_l2(args.q8_ring_l2)
     cfg = LlamaConfig.smollm2_135m()
     if args.layers:
         cfg.n_layers = args.layers
@@ -450,6 +454,7 @@ def main():
             N * world / (qlora["step_ms"] * 1e-3)
         line["north_star_qlora"] = {
             "workload": "smollm2_qlora_b8_t512", "lora": "q,v rank 8 alpha 16 over a frozen Q8_0 base",
+            "q8_ring_l2_resident": bool(args.q8_ring_l2),
             "value": qv, "unit": "tokens/s", "ms_per_step": qlora["step_ms"], "steps": args.steps,
             "step_roofline": {"tflops_algorithmic": qf * qv / world / 1e12, "peak_tflops": sustained,
                               "frac": qf * qv / world / 1e12 / sustained, "flops_per_token": qf},

@@ -132,6 +132,18 @@ int tb2_gemm_set_pair_mode(int mode);
  * Returns the previous mode, or -1 for an unknown mode. */
 int tb2_set_q8_base_mode(int mode);
 
+/* With the ring of tb2_set_q8_base_mode(1): 1 (the default) keeps each
+ * session's ring resident in the L2 -- the session reserves an L2 persisting
+ * set-aside of the ring's size (a limit of this process's CUDA context,
+ * released with the last session that holds one; nothing when the device
+ * offers no set-aside that large) and the ring's planes are written and read
+ * with the L2 evict-last policy, so the dequantised weights are read back from
+ * the L2 and not written back to HBM; 0 writes and reads them as ordinary
+ * data. Applies to engines realised afterwards; results are identical either
+ * way. No counterpart in the reference.
+ * Returns the previous setting, or -1 for an unknown one. */
+int tb2_set_q8_ring_l2(int on);
+
 /* hi = rn_bf16(x), lo = rn_bf16(x - hi) for n f32 values. */
 int tb2_split_f32(const float *x, void *hi, void *lo, size_t n, void *stream);
 

@@ -62,6 +62,8 @@ int tb2_gemm_set_pair_mode(int mode) { return tb2::gemm_set_pair_mode(mode); }
 
 int tb2_set_q8_base_mode(int mode) { return tb2::engine_set_q8_base_mode(mode); }
 
+int tb2_set_q8_ring_l2(int on) { return tb2::engine_set_q8_ring_l2(on); }
+
 int tb2_split_f32(const float* x, void* hi, void* lo, size_t n, void* stream) {
   if (!x || !hi || !lo) return -1;
   return tb2::launch_split_f32(x, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo), (long long)n,

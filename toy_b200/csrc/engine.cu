@@ -25,6 +25,14 @@ namespace tb2 {
   } while (0)
 
 int g_q8_base_mode = 1;
+int g_ring_l2 = 1;
+
+int engine_set_q8_ring_l2(int on) {
+  if (on < 0 || on > 1) return -1;
+  const int prev = g_ring_l2;
+  g_ring_l2 = on;
+  return prev;
+}
 
 int engine_set_q8_base_mode(int mode) {
   if (mode < 0 || mode > 1) return -1;
@@ -118,6 +126,7 @@ LlamaEngine::LlamaEngine(const LlamaConfig& cfg, int device) : cfg_(cfg), device
 
 LlamaEngine::~LlamaEngine() {
   cudaSetDevice(device_);
+  if (ring_keep_) l2_keep_release((size_t)q8pl_.bytes);
   if (graph_) cudaGraphExecDestroy(graph_);
   if (graph_acc_) cudaGraphExecDestroy(graph_acc_);
   for (DeviceBuf* b : {&p32_, &phi_, &plo_, &g_, &m_, &v_, &q8_, &q8v_, &q8s_, &q8pl_, &wsc_ws_, &acc_})
@@ -392,6 +401,13 @@ int LlamaEngine::realize() {
     if (q8_planes_) {
       CK(alloc(q8pl_, q8_slot_elems_ * 2 * 2 * 2));   // 2 slots x (hi, lo) x bf16
       CK(build_ring(qvoff));
+      // keep the ring in the L2's persisting set-aside: its planes are written
+      // and read with the evict-last policy, so they stay on chip between the
+      // fill and the GEMMs that read them instead of being written back to HBM
+      if (g_ring_l2 && l2_keep_acquire((size_t)q8pl_.bytes)) {
+        ring_keep_ = true;
+        for (RingLayer& L : ring_desc_) L.keep = 1;
+      }
     }
   }
 
@@ -619,7 +635,9 @@ Operand LlamaEngine::wop(const Param& p, int rows, int cols, long long ld, int m
     bf16* base = static_cast<bf16*>(q8pl_.p) + (long long)slot * 2 * q8_slot_elems_ + rg.off;
     const Planes pl{base, base + q8_slot_elems_};
     const int e = rg.ext;
-    return mn ? op(pl, rows + e, cols, rg.d_in + e, 1) : op(pl, rows, cols + e, rg.d_in + e, 0);
+    Operand o = mn ? op(pl, rows + e, cols, rg.d_in + e, 1) : op(pl, rows, cols + e, rg.d_in + e, 0);
+    o.l2_keep = ring_keep_;
+    return o;
   }
   Operand o = op(Planes{}, rows, cols, ld, mn);
   o.q8 = static_cast<const int8_t*>(q8v_.p) + p.q8v_offset;
@@ -1776,6 +1794,7 @@ int LlamaEngine::enqueue_backward() {
       gdu.M = N; gdu.N = Rq; gdu.K = H * dh;
       gdu.a = op(dqkv_, N, H * dh, W + eq, 0);
       gdu.b = op(ring_ext_b(l), H * dh, Rq, d + eq, 1);
+      gdu.b.l2_keep = ring_keep_;
       gdu.epi = epi_rowmajor(kEpiStoreSplit, nullptr, W + eq);
       gdu.epi.out_hi = dqkv_.hi + W;
       gdu.epi.out_lo = dqkv_.lo + W;

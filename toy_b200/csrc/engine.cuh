@@ -65,6 +65,11 @@ struct Param {
 // the adapters in GEMM epilogues. Same values either way. Returns the previous
 // mode, or -1 for a mode out of range.
 int engine_set_q8_base_mode(int mode);
+// 1 (default): engines realised afterwards keep their plane ring resident in
+// the L2 (a persisting set-aside of the ring's size, when the device offers
+// one); 0: the ring is written and read as ordinary data. Returns the previous
+// setting, or -1.
+int engine_set_q8_ring_l2(int on);
 
 struct DeviceBuf {
   void* p = nullptr;
@@ -316,6 +321,7 @@ class LlamaEngine {
   // Q8_0 base as planes: per block the first quant / scale index and the count
   // of its projections' elements; two slots of slot_elems hi then lo values
   bool q8_planes_ = false;
+  bool ring_keep_ = false;   // the ring holds an L2 persisting set-aside (evict-last writes and reads)
   DeviceBuf q8pl_;
   long long q8_slot_elems_ = 0;
   int ring_layer_[2] = {-1, -1};

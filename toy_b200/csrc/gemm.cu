@@ -53,6 +53,7 @@ struct KArgs {
   int tiles_m, tiles_n, splits, units, kb_total, causal;
   Epilogue epi;
   float* ws;
+  int b_keep;   // B is an operand kept resident in the L2: evict-last loads
   int* err;
   const uint16_t* q8_scale;   // Q8_0 B operand: scales and stored extent
   int q8_rows, q8_cols;
@@ -435,6 +436,7 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
     if (lane == 0) {
       tma_prefetch_desc(&map_a_hi);
       tma_prefetch_desc(&map_b_hi);
+      const uint64_t keep_pol = args.b_keep ? l2_policy_evict_last() : 0ull;
       uint32_t it = 0;
       bool ok = true;
       for (int u = walker; u < args.units && ok; u += walkers) {
@@ -458,6 +460,17 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
           auto ld = [&](void* dst, const CUtensorMap* map, int c0, int c1, int c2) {
             if constexpr (PAIR) tma_load_3d_pair(dst, map, fc, c0, c1, c2);
             else tma_load_3d(dst, map, &full[s], c0, c1, c2);
+          };
+          // B plane tiles of an operand kept resident in the L2 (args.b_keep):
+          // loaded with the evict-last policy, so reading them does not demote them
+          auto ldb = [&](void* dst, const CUtensorMap* map, int c0, int c1, int c2) {
+            if (!args.b_keep) {
+              ld(dst, map, c0, c1, c2);
+            } else if constexpr (PAIR) {
+              tma_load_3d_pair_hint(dst, map, fc, c0, c1, c2, keep_pol);
+            } else {
+              tma_load_3d_hint(dst, map, &full[s], c0, c1, c2, keep_pol);
+            }
           };
           if (!PAIR || rank == 0) mbar_arrive_expect_tx(&full[s], kTxBytes);
           if (Q8) mbar_arrive_expect_tx(&qfull[s], St::kQBytes);
@@ -497,25 +510,25 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
             }
           } else if (args.epi.pair_off) {
             if (PAIR) {
-              ld(b_hi, &map_b_hi, k0, pr, zb);
-              ld(b_lo, &map_b_lo, k0, pr, zb);
+              ldb(b_hi, &map_b_hi, k0, pr, zb);
+              ldb(b_lo, &map_b_lo, k0, pr, zb);
             } else {   // gate rows, then the matching up rows
               const int r0 = w.n0 / 2, r1 = args.epi.pair_off + w.n0 / 2;
-              ld(b_hi, &map_b_hi, k0, r0, zb);
-              ld(b_hi + (BN / 2) * 128, &map_b_hi, k0, r1, zb);
+              ldb(b_hi, &map_b_hi, k0, r0, zb);
+              ldb(b_hi + (BN / 2) * 128, &map_b_hi, k0, r1, zb);
               if (SPLIT) {
-                ld(b_lo, &map_b_lo, k0, r0, zb);
-                ld(b_lo + (BN / 2) * 128, &map_b_lo, k0, r1, zb);
+                ldb(b_lo, &map_b_lo, k0, r0, zb);
+                ldb(b_lo + (BN / 2) * 128, &map_b_lo, k0, r1, zb);
               }
             }
           } else if (!args.b_mn) {
-            ld(b_hi, &map_b_hi, k0, nb, zb);
-            if (SPLIT) ld(b_lo, &map_b_lo, k0, nb, zb);
+            ldb(b_hi, &map_b_hi, k0, nb, zb);
+            if (SPLIT) ldb(b_lo, &map_b_lo, k0, nb, zb);
           } else {
 #pragma unroll
             for (int j = 0; j < RB / 64; ++j) {
-              ld(b_hi + j * 64 * 128, &map_b_hi, nb + 64 * j, k0, zb);
-              if (SPLIT) ld(b_lo + j * 64 * 128, &map_b_lo, nb + 64 * j, k0, zb);
+              ldb(b_hi + j * 64 * 128, &map_b_hi, nb + 64 * j, k0, zb);
+              if (SPLIT) ldb(b_lo + j * 64 * 128, &map_b_lo, nb + 64 * j, k0, zb);
             }
           }
         }
@@ -1060,6 +1073,7 @@ int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream
   k.units = (int)(tiles * splits);
   k.epi = d.epi;
   k.ws = sc.ws;
+  k.b_keep = d.b.l2_keep && !Q8;
   k.err = dev_err;
   k.q8_scale = d.b.q8_scale;
   k.q8_rows = d.b.rows;

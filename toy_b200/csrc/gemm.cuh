@@ -40,6 +40,10 @@ struct Operand {
   // off. The GEMM dequantises tiles in shared memory.
   const int8_t* q8 = nullptr;
   const uint16_t* q8_scale = nullptr;
+  // B operand only: the planes are kept resident in the L2's persisting
+  // set-aside by their producer (written with the evict-last policy); the GEMM
+  // loads them with the same policy so reading does not demote them.
+  int l2_keep = 0;
 };
 
 enum EpiMode : int {

@@ -764,8 +764,16 @@ __device__ __forceinline__ void ring_chunk_loc(const RingLayer& L, long long i, 
   col = (int)(c % cpr) * 16;
 }
 
+// 16-byte global store with an L2 cache-policy hint
+__device__ __forceinline__ void st_keep(uint4* p, uint4 v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w), "l"(pol)
+               : "memory");
+}
+
 __global__ void __launch_bounds__(256) q8_0_ring_kernel(const __grid_constant__ RingLayer L) {
   griddep_wait();
+  const uint64_t pol = L.keep ? l2_policy_evict_last() : 0ull;
   const long long total = L.chunks;
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i0 = blockIdx.x * (long long)blockDim.x + threadIdx.x; i0 < total; i0 += stride * kRingPer) {
@@ -836,10 +844,17 @@ __global__ void __launch_bounds__(256) q8_0_ring_kernel(const __grid_constant__ 
       const long long o = (long long)row * (M.d_in + M.ext) + col;
       uint4* ph = reinterpret_cast<uint4*>(M.hi + o);
       uint4* pl = reinterpret_cast<uint4*>(M.lo + o);
-      ph[0] = reinterpret_cast<const uint4*>(h)[0];
-      ph[1] = reinterpret_cast<const uint4*>(h)[1];
-      pl[0] = reinterpret_cast<const uint4*>(l)[0];
-      pl[1] = reinterpret_cast<const uint4*>(l)[1];
+      if (L.keep) {
+        st_keep(ph, reinterpret_cast<const uint4*>(h)[0], pol);
+        st_keep(ph + 1, reinterpret_cast<const uint4*>(h)[1], pol);
+        st_keep(pl, reinterpret_cast<const uint4*>(l)[0], pol);
+        st_keep(pl + 1, reinterpret_cast<const uint4*>(l)[1], pol);
+      } else {
+        ph[0] = reinterpret_cast<const uint4*>(h)[0];
+        ph[1] = reinterpret_cast<const uint4*>(h)[1];
+        pl[0] = reinterpret_cast<const uint4*>(l)[0];
+        pl[1] = reinterpret_cast<const uint4*>(l)[1];
+      }
     }
   }
 }

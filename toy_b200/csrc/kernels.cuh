@@ -143,6 +143,7 @@ struct RingLayer {
   RingMat m[kRingMats];
   int n = 0;
   long long chunks = 0;           // 16-value chunks of all n matrices
+  int keep = 0;                   // write the planes with the L2 evict-last policy (the ring stays L2-resident)
 };
 // Fills the matrices of one transformer block (the descriptors travel with
 // the launch).

@@ -1,7 +1,9 @@
 // Process-wide device state shared by every entry point: one device error
-// word per GPU (written by kernels whose bounded waits give up).
+// word per GPU (written by kernels whose bounded waits give up), the split-K
+// workspace, and the L2 persisting set-aside the engines' plane rings use.
 #include "runtime.cuh"
 
+#include <algorithm>
 #include <mutex>
 
 namespace tb2 {
@@ -11,7 +13,46 @@ std::mutex g_mu;
 int* g_err[64] = {nullptr};
 GemmScratch g_scratch[64];
 constexpr long long kWsFloats = 16LL << 20;   // 64 MiB
+struct L2Keep {
+  int users = 0;
+  size_t held = 0;   // sum of the users' bytes
+  size_t prev = 0;   // the context's limit before the first user
+};
+L2Keep g_l2[64];
 }  // namespace
+
+bool l2_keep_acquire(size_t bytes) {
+  int dev = 0;
+  if (bytes == 0 || cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  int maxp = 0;
+  if (cudaDeviceGetAttribute(&maxp, cudaDevAttrMaxPersistingL2CacheSize, dev) != cudaSuccess || maxp <= 0 ||
+      bytes > (size_t)maxp)
+    return false;
+  std::lock_guard<std::mutex> lk(g_mu);
+  L2Keep& k = g_l2[dev];
+  size_t cur = 0;
+  if (cudaDeviceGetLimit(&cur, cudaLimitPersistingL2CacheSize) != cudaSuccess) return false;
+  const size_t want = std::min(k.held + bytes, (size_t)maxp);
+  if (want > cur && cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, want) != cudaSuccess) return false;
+  if (k.users == 0) k.prev = cur;
+  ++k.users;
+  k.held += bytes;
+  return true;
+}
+
+void l2_keep_release(size_t bytes) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return;
+  std::lock_guard<std::mutex> lk(g_mu);
+  L2Keep& k = g_l2[dev];
+  if (k.users <= 0) return;
+  --k.users;
+  k.held = k.held > bytes ? k.held - bytes : 0;
+  if (k.users == 0) {
+    cudaCtxResetPersistingL2Cache();
+    cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, k.prev);
+  }
+}
 
 const GemmScratch& gemm_scratch() {
   static const GemmScratch none;

@@ -35,7 +35,16 @@ int* device_error_word();
 // Synchronise, read the word, clear it. Returns the code (0 = none) or -3.
 int read_and_clear_device_error();
 // Split-K workspace of the current device (allocated on first use: 64 MiB of
-// partial tiles and 64 Ki tile counters). Shared by every GEMM of the device,
-// so GEMMs that use it must run on one stream at a time.
+// partial tiles). Shared by every GEMM of the device, so GEMMs that use it
+// must run on one stream at a time.
 const GemmScratch& gemm_scratch();
+
+// L2 persisting set-aside of the current device (a limit of this process's
+// context, gone with it): l2_keep_acquire(bytes) grows the set-aside to hold
+// the sum of its users' bytes (at most the device's maximum) and returns true
+// when `bytes` fit, false (nothing reserved) otherwise; l2_keep_release(bytes)
+// gives them back, and the last user restores the context's previous limit and
+// returns every persisting line to normal status.
+bool l2_keep_acquire(size_t bytes);
+void l2_keep_release(size_t bytes);
 }  // namespace tb2
