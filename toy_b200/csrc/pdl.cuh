@@ -1,7 +1,7 @@
 // Programmatic dependent launch: every kernel of the step is launched with
 // programmatic stream serialisation, so the next kernel's launch and its
-// data-independent prologue overlap the tail of the previous one. Each kernel
-// calls griddep_wait() before it touches global memory, which waits for the
+// data-independent prologue overlap the previous one. Each kernel calls
+// griddep_wait() before it touches global memory, which waits for the
 // previous kernel to complete and its writes to be visible; since every kernel
 // waits, completion is ordered transitively down the stream.
 #pragma once
@@ -11,7 +11,17 @@
 
 namespace tb2 {
 
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Wait for the previous kernel, then let the next one launch: its CTAs are
+// scheduled once every CTA of this grid has passed this point (so all of this
+// grid's CTAs are already resident and none can be starved by the waiting
+// ones), run their data-independent prologue (barrier set-up, TMEM
+// allocation) beside this kernel and block in their own griddep_wait until it
+// completes. Kernels that hold TMEM (the GEMM and flash kernels) need more
+// than half an SM's shared memory, so two of them never share an SM.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 template <typename... KParams, typename... Args>
 int launch_pdl(void (*kernel)(KParams...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
