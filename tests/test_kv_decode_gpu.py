@@ -3,8 +3,11 @@ full-sequence forward: the logits after each teacher-forced token equal the
 oracle's logits row for that position (f32 cache: 1e-4 relative L2 per row;
 Q8_0 cache: the oracle with the same Q8_0 round trip of K and V, median row
 1e-3, every row 1e-2), for
-several sequences in lockstep, over the Q8_0 base and over f32 weights, at
-SmolLM2-135M's full shape, plus a greedy continuation and argument checks."""
+several sequences in lockstep, over the Q8_0 base with its LoRA adapters
+(plain adapters on q and v, on all seven projections, and toy's per-head
+LoRA-Q, each with nonzero B so that the adapters change the logits) and over
+f32 weights, at SmolLM2-135M's full shape, plus a greedy continuation and
+argument checks."""
 import numpy as np
 import pytest
 
@@ -24,15 +27,33 @@ def tiny():
     return oc, LlamaConfig(512, 128, 4, 2, 32, 256, 2, 1e4, 1e-5)
 
 
-def base_model(mode, oc, gc, seed):
+def set_adapters_b(eng, mdl, seed):
+    """B starts at zero; give every adapter B seeded N(0, 0.05) values on both sides."""
+    rng = np.random.default_rng(seed)
+    for k in mdl.trainable:
+        if k.endswith(".lora_b"):
+            v = (rng.standard_normal(mdl.params[k].shape) * 0.05).astype(np.float32)
+            mdl.params[k] = v
+            eng.set_param(k, v)
+
+
+def base_model(mode, oc, gc, seed, targets=("q", "v")):
     """A realised step engine (its weights feed the decoder) and the oracle model
-    of the same weights without adapters (decoding applies none)."""
+    of the same weights, adapters included ("q8": plain adapters on `targets`;
+    "lora_q": toy's per-head LoRA-Q)."""
     from toy_b200 import FromScratch, LoRA, LoraOptions, RecipeOptions
     if mode == "q8":
         rec = LoRA()
-        rec.realize(gc, 8, RecipeOptions(t_seq=64, t_batch=1, seed=seed), LoraOptions(rank=8, targets=("q", "v")))
-        mdl = O.qlora_model(oc, O.LoraCfg(rank=8, alpha=16.0, targets=("q", "v")), seed=seed)
-        mdl.lora = None
+        rec.realize(gc, 8, RecipeOptions(t_seq=64, t_batch=1, seed=seed), LoraOptions(rank=8, targets=targets))
+        mdl = O.qlora_model(oc, O.LoraCfg(rank=8, alpha=16.0, targets=targets), seed=seed)
+        set_adapters_b(rec.lora_cache, mdl, seed + 100)
+        return rec.lora_cache, mdl
+    if mode == "lora_q":
+        rec = LoRA()
+        rec.realize(gc, 4, RecipeOptions(t_seq=64, t_batch=1, seed=seed, init_scale=0.05))
+        mdl = O.qlora_model(oc, O.LoraCfg(rank=4, per_head_q=True, targets=("q",), a_std=0.05), seed=seed,
+                            base_std=0.02)
+        set_adapters_b(rec.lora_cache, mdl, seed + 100)
         return rec.lora_cache, mdl
     rec = FromScratch()
     rec.realize(gc, RecipeOptions(t_seq=64, t_batch=1, seed=seed))
@@ -70,6 +91,19 @@ def test_decode_tiny(cuda, mode, kv_q8):
     oc, gc = tiny()
     eng, mdl = base_model(mode, oc, gc, 3)
     check_decode(eng, mdl, oc, 40, 3, kv_q8, 1e-3 if kv_q8 else 1e-4)
+
+
+@pytest.mark.parametrize("mode", ["lora_q", "all7"])
+def test_decode_adapters(cuda, mode):
+    """toy's per-head LoRA-Q (its KV engine adds B_h A_h h to each query head
+    before the bias, llama_kv_engine.rb:2157-2167) and plain adapters on all
+    seven projections."""
+    oc, gc = tiny()
+    if mode == "lora_q":
+        eng, mdl = base_model("lora_q", oc, gc, 4)
+    else:
+        eng, mdl = base_model("q8", oc, gc, 4, targets=("q", "k", "v", "o", "gate", "up", "down"))
+    check_decode(eng, mdl, oc, 24, 2, False, 1e-4)
 
 
 def test_decode_history_longer_than_a_chunk(cuda):

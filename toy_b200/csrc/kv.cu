@@ -60,6 +60,21 @@ __device__ __forceinline__ float warp_max(float v) {
 // out(b, n) for the n_seq rows of x: y = r_b * sum_k W[n][k] x[b][k] g[k]
 // (r_b = 1 and g = 1 without a norm). mode 0 store (+ bias), 1 residual
 // (out = res + y), 2 SwiGLU over paired rows (n and n + pair: out = silu(y_n) y_{n+pair}).
+
+// A LoRA adapter on the output rows [c0, c0 + width) of a GEMV (in pair mode:
+// of the gate rows, on = 0, or of the up rows, on = 1): y(b, n) +=
+// s * sum_j B[n - c0][j] u[b][o(n) + j], with u = A x computed by an earlier
+// GEMV and o(n) = ((n - c0) / bd_w) r for toy's per-head LoRA-Q (one adapter
+// pair per block of bd_w rows), 0 for a plain adapter.
+struct GemvLora {
+  const float* B = nullptr;        // [width][r]
+  const float* u = nullptr;        // [n_seq][ldu]
+  long long ldu = 0;
+  int c0 = 0, width = 0, r = 0, bd_w = 0, on = 0;
+  float s = 1.f;
+};
+constexpr int kGemvLoras = 3;
+
 struct GemvArgs {
   const float* w32 = nullptr;      // f32 weights [rows][K], or
   const int8_t* wq = nullptr;      // Q8_0 quants [rows][K] and
@@ -78,19 +93,114 @@ struct GemvArgs {
   // [n_seq][H][nsplit][dh + 2] (o, m, l): x[b][h dh + d] = sum_s o_s e^(m_s - m) / sum_s l_s e^(m_s - m)
   const float* part = nullptr;
   int nsplit = 0, dh = 0;
+  // low-rank adapters added to the product before the mode's epilogue
+  GemvLora lora[kGemvLoras];
+  int n_lora = 0;
 };
+
+// One output row (or gate / up pair) of weights held in registers: lane l
+// holds 16-value chunks l, l + 32, ... (Q8_0: int8 quants and the block
+// scale) or 4-value chunks (f32). Rows up to kRegK columns are read this way,
+// the next row's loads issued before the current row's arithmetic; the first
+// row's before the grid wait, beside the previous kernel.
+constexpr int kQ8Chunks = 3;   // Q8_0 rows of K <= 1536
+constexpr int kF32Chunks = 5;  // f32 rows of K <= 640
+
+template <bool Q8>
+struct RowRegs {
+  static constexpr int kC = Q8 ? kQ8Chunks : kF32Chunks;
+  static constexpr int kRows = Q8 ? 2 : 1;   // f32 rows: single rows only (not the gate / up pairs)
+  int4 v[kRows][kC];
+  float d[kRows][kC];
+};
+
+template <bool Q8>
+__device__ __forceinline__ bool row_fits(int K, int mode) {
+  return Q8 ? K <= kQ8Chunks * 32 * 16 : (K <= kF32Chunks * 32 * 4 && mode != 2);
+}
+
+template <bool Q8>
+__device__ __forceinline__ void row_load(const GemvArgs& a, int n, int nrow, int lane, RowRegs<Q8>& r) {
+  constexpr int kC = RowRegs<Q8>::kC;
+  const int nch = Q8 ? a.K / 16 : a.K / 4;
+#pragma unroll
+  for (int h = 0; h < RowRegs<Q8>::kRows; ++h) {
+#pragma unroll
+    for (int i = 0; i < kC; ++i) {
+      const int c = lane + 32 * i;
+      r.v[h][i] = make_int4(0, 0, 0, 0);
+      r.d[h][i] = 0.f;
+      if (h >= nrow || c >= nch) continue;
+      const long long row = n + (long long)h * a.pair;
+      if (Q8) {
+        r.v[h][i] = __ldg(reinterpret_cast<const int4*>(a.wq + row * a.K) + c);
+        r.d[h][i] = __half2float(__ushort_as_half(__ldg(a.ws + row * (a.K / 32) + c / 2)));
+      } else {
+        r.v[h][i] = __ldg(reinterpret_cast<const int4*>(a.w32 + row * a.K) + c);
+      }
+    }
+  }
+}
+
+template <int NB, bool Q8>
+__device__ __forceinline__ void row_dot(const GemvArgs& a, const float* xs, int lane, const RowRegs<Q8>& r,
+                                        float (&acc)[2][NB]) {
+  constexpr int kC = RowRegs<Q8>::kC;
+  const int nch = Q8 ? a.K / 16 : a.K / 4;
+#pragma unroll
+  for (int h = 0; h < RowRegs<Q8>::kRows; ++h) {
+#pragma unroll
+    for (int i = 0; i < kC; ++i) {
+      const int c = lane + 32 * i;
+      if (c >= nch) continue;
+      if (Q8) {
+        const int8_t* qb = reinterpret_cast<const int8_t*>(&r.v[h][i]);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float wv = r.d[h][i] * (float)qb[j];
+#pragma unroll
+          for (int b = 0; b < NB; ++b) acc[h][b] = fmaf(wv, xs[b * a.K + c * 16 + j], acc[h][b]);
+        }
+      } else {
+        const int4 wi = r.v[h][i];
+        const float4 wv = make_float4(__int_as_float(wi.x), __int_as_float(wi.y), __int_as_float(wi.z),
+                                      __int_as_float(wi.w));
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          const float* xb = xs + b * a.K + c * 4;
+          acc[h][b] = fmaf(wv.x, xb[0], fmaf(wv.y, xb[1], fmaf(wv.z, xb[2], fmaf(wv.w, xb[3], acc[h][b]))));
+        }
+      }
+    }
+  }
+}
 
 template <int NB, bool Q8>
 __global__ void __launch_bounds__(256) kv_gemv_kernel(const GemvArgs a) {
-  // xs [NB][K]: the input rows (times gamma when a norm is folded in); with the
-  // attention partials, fs [NB][H][nsplit] holds each chunk's factor e^(m_s - m) / L
+  // xs [NB][K]: the input rows (times gamma when a norm is folded in); with
+  // the attention partials, fs [NB][H][nsplit] holds each chunk's factor
+  // e^(m_s - m) / L; then gs [K]: gamma
   extern __shared__ float xs[];
   __shared__ float rs[NB];
-  griddep_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_out = a.mode == 2 ? a.pair : a.rows;
+  const int nrow = a.mode == 2 ? 2 : 1;
+  const int H = a.part ? a.K / a.dh : 0;
+  float* fs = xs + NB * a.K;
+  float* gs = fs + NB * H * a.nsplit;
+  // prologue on weights only (nothing the previous kernels write): gamma into
+  // shared memory, this warp's first row into registers
+  if (a.gamma)
+    for (int k = threadIdx.x; k < a.K; k += blockDim.x) gs[k] = __ldg(a.gamma + k);
+  // (wider batches keep the streaming loop: their per-row arithmetic hides the
+  // loads, and the row registers would cost occupancy)
+  const bool regs = NB <= 4 && row_fits<Q8>(a.K, a.mode);
+  const int n_first = blockIdx.x * kGemvWarps + warp, n_step = gridDim.x * kGemvWarps;
+  RowRegs<Q8> cur;
+  if (NB <= 4 && regs && n_first < n_out) row_load<Q8>(a, n_first, nrow, lane, cur);
+  griddep_wait_release();
   if (a.part) {
-    const int H = a.K / a.dh, ns = a.nsplit, stride = a.dh + 2;
-    float* fs = xs + NB * a.K;
+    const int ns = a.nsplit, stride = a.dh + 2;
     for (int j = threadIdx.x; j < NB * H; j += blockDim.x) {
       const float* p = a.part + (long long)j * ns * stride;
       float m = -INFINITY;
@@ -134,51 +244,73 @@ __global__ void __launch_bounds__(256) kv_gemv_kernel(const GemvArgs a) {
       if (lane == 0) rs[b] = rsqrtf(s / (float)a.K + a.eps);
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < NB * a.K; i += blockDim.x) xs[i] *= a.gamma[i % a.K];
+    for (int i = threadIdx.x; i < NB * a.K; i += blockDim.x) xs[i] *= gs[i % a.K];
     __syncthreads();
   }
-  const int n_out = a.mode == 2 ? a.pair : a.rows;
-  for (int n = blockIdx.x * kGemvWarps + warp; n < n_out; n += gridDim.x * kGemvWarps) {
+  for (int n = n_first; n < n_out; n += n_step) {
     float acc[2][NB];
 #pragma unroll
     for (int h = 0; h < 2; ++h)
 #pragma unroll
       for (int b = 0; b < NB; ++b) acc[h][b] = 0.f;
-    const int nrow = a.mode == 2 ? 2 : 1;
-    for (int h = 0; h < nrow; ++h) {
-      const long long row = n + (long long)h * a.pair;
-      if (Q8) {
-        const int8_t* q = a.wq + row * a.K;
-        const uint16_t* sc = a.ws + row * (a.K / 32);
+    if (NB <= 4 && regs) {
+      RowRegs<Q8> nxt;
+      const bool more = n + n_step < n_out;
+      if (more) row_load<Q8>(a, n + n_step, nrow, lane, nxt);   // in flight during this row's arithmetic
+      row_dot<NB, Q8>(a, xs, lane, cur, acc);
+      if (more) cur = nxt;
+    } else {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {   // (unrolled: acc is indexed by constants)
+        if (h >= nrow) break;
+        const long long row = n + (long long)h * a.pair;
+        if (Q8) {
+          const int8_t* q = a.wq + row * a.K;
+          const uint16_t* sc = a.ws + row * (a.K / 32);
 #pragma unroll 3
-        for (int c = lane; c < a.K / 16; c += 32) {
-          const int4 raw = __ldg(reinterpret_cast<const int4*>(q + c * 16));
-          const float d = __half2float(__ushort_as_half(__ldg(sc + c / 2)));
-          const int8_t* qb = reinterpret_cast<const int8_t*>(&raw);
+          for (int c = lane; c < a.K / 16; c += 32) {
+            const int4 raw = __ldg(reinterpret_cast<const int4*>(q + c * 16));
+            const float d = __half2float(__ushort_as_half(__ldg(sc + c / 2)));
+            const int8_t* qb = reinterpret_cast<const int8_t*>(&raw);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float wv = d * (float)qb[j];
+            for (int j = 0; j < 16; ++j) {
+              const float wv = d * (float)qb[j];
 #pragma unroll
-            for (int b = 0; b < NB; ++b) acc[h][b] = fmaf(wv, xs[b * a.K + c * 16 + j], acc[h][b]);
+              for (int b = 0; b < NB; ++b) acc[h][b] = fmaf(wv, xs[b * a.K + c * 16 + j], acc[h][b]);
+            }
           }
-        }
-      } else {
-        const float* wr = a.w32 + row * a.K;
+        } else {
+          const float* wr = a.w32 + row * a.K;
 #pragma unroll 5
-        for (int c = lane; c < a.K / 4; c += 32) {
-          const float4 wv = __ldg(reinterpret_cast<const float4*>(wr + c * 4));
+          for (int c = lane; c < a.K / 4; c += 32) {
+            const float4 wv = __ldg(reinterpret_cast<const float4*>(wr + c * 4));
 #pragma unroll
-          for (int b = 0; b < NB; ++b) {
-            const float* xb = xs + b * a.K + c * 4;
-            acc[h][b] = fmaf(wv.x, xb[0], fmaf(wv.y, xb[1], fmaf(wv.z, xb[2], fmaf(wv.w, xb[3], acc[h][b]))));
+            for (int b = 0; b < NB; ++b) {
+              const float* xb = xs + b * a.K + c * 4;
+              acc[h][b] = fmaf(wv.x, xb[0], fmaf(wv.y, xb[1], fmaf(wv.z, xb[2], fmaf(wv.w, xb[3], acc[h][b]))));
+            }
           }
         }
       }
     }
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
-      const float y0 = warp_sum(acc[0][b]) * rs[b];
-      const float y1 = a.mode == 2 ? warp_sum(acc[1][b]) * rs[b] : 0.f;
+      float y0 = warp_sum(acc[0][b]) * rs[b];
+      float y1 = a.mode == 2 ? warp_sum(acc[1][b]) * rs[b] : 0.f;
+#pragma unroll
+      for (int i = 0; i < kGemvLoras; ++i) {   // adapters, before the bias / residual / SwiGLU
+        if (i >= a.n_lora) break;
+        const GemvLora& L = a.lora[i];
+        if (n < L.c0 || n >= L.c0 + L.width) continue;
+        const int rr = n - L.c0;
+        const float* ur = L.u + b * L.ldu + (L.bd_w ? (rr / L.bd_w) * L.r : 0);
+        const float* br = L.B + (long long)rr * L.r;
+        float t = 0.f;
+        for (int j = lane; j < L.r; j += 32) t = fmaf(br[j], ur[j], t);
+        t = warp_sum(t) * L.s;
+        if (L.on) y1 += t;
+        else y0 += t;
+      }
       if (lane == 0) {
         float* o = a.out + (long long)b * a.ldo + n;
         if (a.mode == 0) *o = y0 + (a.bias ? a.bias[n] : 0.f);
@@ -191,7 +323,7 @@ __global__ void __launch_bounds__(256) kv_gemv_kernel(const GemvArgs a) {
 
 // ---------------------------------------------------------------- embedding
 __global__ void kv_embed_kernel(const float* __restrict__ E, const int* __restrict__ tok, int d, float* __restrict__ x) {
-  griddep_wait();
+  griddep_wait_release();
   const int b = blockIdx.x;
   const float* src = E + (long long)tok[b] * d;
   for (int k = threadIdx.x; k < d; k += blockDim.x) x[(long long)b * d + k] = src[k];
@@ -228,7 +360,7 @@ __device__ __forceinline__ int round_away(float v) {
 // head j rotates k and writes k and v at the sequence's position.
 __global__ void kv_append_kernel(const AppendArgs a) {
   extern __shared__ float sh[];   // [2][dh]
-  griddep_wait();
+  griddep_wait_release();
   const int b = blockIdx.x, hh = blockIdx.y, t = threadIdx.x, dh = a.dh, half = dh / 2;
   const int W = (a.H + 2 * a.KV) * dh;
   float* row = a.qkv + (long long)b * W;
@@ -295,15 +427,35 @@ __device__ __forceinline__ float cache_val(const KvCache& c, bool v, long long s
 // coalesced across threads, P from shared memory. Writes the chunk's
 // unnormalised o, its max m and its sum l.
 __global__ void __launch_bounds__(kChunk) kv_attn_kernel(const AttnArgs a) {
+  // the chunk's V rows as stored: f32 [kChunk][dh], or Q8_0 quants
+  // [kChunk][dh] followed by their fp16 scales [kChunk][dh / 32]
+  extern __shared__ __align__(16) uint8_t vsm[];
   __shared__ float qs[128];
   __shared__ float ps[kChunk];
   __shared__ float red[kChunk / 32];
   __shared__ float osum[kChunk];
-  griddep_wait();
   const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H, j = h / (a.H / a.KV), split = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, dh = a.dh;
+  // positions are copied in before the step's first kernel, so the chunk's
+  // extent is known before the grid wait: its K and V rows are pulled toward
+  // the L2 while the previous kernel (the append of the new row) runs
   const int hist = a.pos[b] + 1;
   const int t0 = split * kChunk, t1 = min(t0 + kChunk, hist);
+  const long long base = ((long long)b * a.KV + j) * a.max_T;
+  const bool f32c = a.c.k32 != nullptr;
+  const int row_bytes = f32c ? dh * 4 : dh;
+  if (t0 + tid < t1) {
+    const long long slot = base + t0 + tid;
+    const uint8_t* kr = f32c ? reinterpret_cast<const uint8_t*>(a.c.k32 + slot * dh)
+                             : reinterpret_cast<const uint8_t*>(a.c.kq + slot * dh);
+    const uint8_t* vr = f32c ? reinterpret_cast<const uint8_t*>(a.c.v32 + slot * dh)
+                             : reinterpret_cast<const uint8_t*>(a.c.vq + slot * dh);
+    for (int o = 0; o < row_bytes; o += 128) {
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(kr + o));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(vr + o));
+    }
+  }
+  griddep_wait_release();
   float* out = a.part + ((long long)bh * a.nsplit + split) * (dh + 2);
   if (t0 >= t1) {   // this chunk is past the history
     for (int d = tid; d < dh; d += blockDim.x) out[d] = 0.f;
@@ -313,10 +465,26 @@ __global__ void __launch_bounds__(kChunk) kv_attn_kernel(const AttnArgs a) {
     }
     return;
   }
+  // V rows of the chunk into shared memory by 16-byte async copies (rows are
+  // contiguous in the cache), in flight while the scores are computed
+  {
+    const uint8_t* src = f32c ? reinterpret_cast<const uint8_t*>(a.c.v32 + (base + t0) * dh)
+                              : reinterpret_cast<const uint8_t*>(a.c.vq + (base + t0) * dh);
+    const int n16 = (t1 - t0) * row_bytes / 16;
+    for (int i = tid; i < n16; i += blockDim.x)
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(vsm + 16 * i)),
+                   "l"(src + 16 * i)
+                   : "memory");
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    if (!f32c) {   // the rows' scales after the quants
+      uint16_t* vsc = reinterpret_cast<uint16_t*>(vsm + kChunk * dh);
+      const int ns = (t1 - t0) * (dh / 32);
+      for (int i = tid; i < ns; i += blockDim.x) vsc[i] = a.c.vs[(base + t0) * (dh / 32) + i];
+    }
+  }
   const float* q = a.qkv + (long long)b * (a.H + 2 * a.KV) * dh + h * dh;
   for (int d = tid; d < dh; d += blockDim.x) qs[d] = q[d];
   __syncthreads();
-  const long long base = ((long long)b * a.KV + j) * a.max_T;
   const int t = t0 + tid;
   float s = -INFINITY;
   if (t < t1) {
@@ -359,17 +527,22 @@ __global__ void __launch_bounds__(kChunk) kv_attn_kernel(const AttnArgs a) {
   l = 0.f;
   for (int w = 0; w < (int)(blockDim.x >> 5); ++w) l += red[w];
   // P V: thread (g, d) sums keys g, g + G, ... of the chunk for dimension d (G = blockDim / dh groups)
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
   const int groups = blockDim.x / dh, g = tid / dh, d = tid % dh;
   float o = 0.f;
   if (g < groups) {
     const int n = t1 - t0;
+    if (f32c) {
+      const float* vs32 = reinterpret_cast<const float*>(vsm);
 #pragma unroll 8
-    for (int k = g; k < n; k += groups) {
-      const long long slot = base + t0 + k;
-      const float v = a.c.v32 ? __ldg(a.c.v32 + slot * dh + d)
-                              : __half2float(__ushort_as_half(__ldg(a.c.vs + slot * (dh / 32) + d / 32))) *
-                                    (float)__ldg(a.c.vq + slot * dh + d);
-      o += ps[k] * v;
+      for (int k = g; k < n; k += groups) o += ps[k] * vs32[k * dh + d];
+    } else {
+      const int8_t* vq = reinterpret_cast<const int8_t*>(vsm);
+      const uint16_t* vsc = reinterpret_cast<const uint16_t*>(vsm + kChunk * dh);
+#pragma unroll 8
+      for (int k = g; k < n; k += groups)
+        o += ps[k] * (__half2float(__ushort_as_half(vsc[k * (dh / 32) + d / 32])) * (float)vq[k * dh + d]);
     }
   }
   osum[tid] = o;
@@ -388,6 +561,9 @@ __global__ void __launch_bounds__(kChunk) kv_attn_kernel(const AttnArgs a) {
 }  // namespace
 
 // ---------------------------------------------------------------- the decode engine
+// adapter parameter names by target, in the training engine's order (q, k, v, o, gate, up, down)
+const char* const kAdName[7] = {"attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"};
+
 class KvEngine {
  public:
   KvEngine(LlamaEngine& e, int max_T, int n_seq, int kv_type) : e_(e), max_T_(max_T), nb_(n_seq), q8_(kv_type == 8) {}
@@ -403,15 +579,25 @@ class KvEngine {
     const LlamaConfig& c = e_.cfg();
     if (max_T_ < 1 || max_T_ > e_.rope_rows() || nb_ < 1 || (nb_ > 8 && nb_ != kMaxSeq)) return -1;
     if (c.d_head % 32 || c.d_head > 128 || c.d_model % 16 || c.d_ff % 16) return -1;
+    if (c.qk_norm || c.n_experts) return -1;   // QK-RMSNorm and expert blocks: training-step only
     const long long nsplit = (max_T_ + kChunk - 1) / kChunk;
-    if (((long long)nb_ * std::max(c.d_ff, std::max(c.d_model, c.n_heads * c.d_head)) +
-         (long long)nb_ * c.n_heads * nsplit) * 4 > 200 * 1024)
+    const long long max_k = std::max(c.d_ff, std::max(c.d_model, c.n_heads * c.d_head));
+    if (((long long)nb_ * max_k + (long long)nb_ * c.n_heads * nsplit + max_k) * 4 > 200 * 1024)
       return -1;
     if (cudaSetDevice(e_.device()) != cudaSuccess) return -3;
     if (cudaStreamCreateWithFlags(&st_, cudaStreamNonBlocking) != cudaSuccess) return -3;
     const int d = c.d_model, H = c.n_heads, KV = c.n_kv, dh = c.d_head, ff = c.d_ff, V = c.vocab, L = c.n_layers;
     const int W = (H + 2 * KV) * dh;
     nsplit_ = (max_T_ + kChunk - 1) / kChunk;
+    attn_smem_ = q8_ ? (size_t)kChunk * dh + (size_t)kChunk * (dh / 32) * 2 : (size_t)kChunk * dh * 4;
+    static DeviceOnce attn_setup;   // the largest chunk any engine stages: f32 rows of d_head 128
+    if (attn_setup.ensure([](int) {
+          return cudaFuncSetAttribute(kv_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kChunk * 128 * 4) ==
+                         cudaSuccess
+                     ? 0
+                     : -3;
+        }))
+      return -3;
     auto f32 = [&](long long n) -> float* {
       void* p = nullptr;
       if (cudaMalloc(&p, (size_t)std::max<long long>(n, 1) * 4) != cudaSuccess) return nullptr;
@@ -442,6 +628,21 @@ class KvEngine {
     } else {
       k32_ = f32(cache);
       v32_ = f32(cache);
+    }
+    // the recipe's adapters, applied as the training step applies them
+    if (c.mode == 1 && c.lora_rank > 0) {
+      const float s = c.lora_per_head_q ? 1.0f : c.lora_alpha / (float)c.lora_rank;
+      for (int t = 0; t < kAdapters; ++t) {
+        if (!(c.lora_targets & (1 << t))) continue;
+        const LlamaEngine::WeightView A = e_.weight(std::string("blk.0.") + kAdName[t] + ".lora_a");
+        if (!A.f32) return -1;
+        Adapter& ad = ad_[t];
+        ad.on = true;
+        ad.rows = A.rows;
+        ad.u = f32((long long)nb_ * A.rows);
+        ad.s = s;
+        ad.bd_w = c.lora_per_head_q && t == 0 ? dh : 0;
+      }
     }
     for (void* p : bufs_)
       if (!p) return -3;
@@ -532,7 +733,8 @@ class KvEngine {
   template <int NB>
   int gemv_nb(const GemvArgs& g) {
     const bool q8 = g.wq != nullptr;
-    const size_t smem = ((size_t)NB * g.K + (g.part ? (size_t)NB * (g.K / g.dh) * g.nsplit : 0)) * 4;
+    const size_t smem =
+        ((size_t)NB * g.K + (g.part ? (size_t)NB * (g.K / g.dh) * g.nsplit : 0) + (g.gamma ? g.K : 0)) * 4;
     auto* k = q8 ? kv_gemv_kernel<NB, true> : kv_gemv_kernel<NB, false>;
     static DeviceOnce setup[2];
     if (setup[q8].ensure([&](int) {
@@ -560,6 +762,26 @@ class KvEngine {
       case 16: return gemv_nb<16>(g);
       default: return -1;
     }
+  }
+
+  // u = A x of adapter t of block l into its buffer; `in` carries the input of
+  // the GEMV the adapter belongs to (rows and folded norm, or the partials)
+  int adapter_u(int l, int t, const GemvArgs& in) {
+    if (!ad_[t].on) return 0;
+    const LlamaEngine::WeightView A = e_.weight("blk." + std::to_string(l) + "." + kAdName[t] + ".lora_a");
+    if (!A.f32) return -1;
+    GemvArgs g = in;
+    g.w32 = A.f32; g.wq = nullptr; g.ws = nullptr; g.rows = A.rows; g.K = A.cols;
+    g.out = ad_[t].u; g.ldo = A.rows; g.mode = 0; g.pair = 0; g.res = nullptr; g.bias = nullptr; g.n_lora = 0;
+    return gemv(g);
+  }
+
+  void add_lora(GemvArgs& g, int l, int t, int c0, int width, int on) {
+    if (!ad_[t].on) return;
+    GemvLora& L = g.lora[g.n_lora++];
+    L.B = e_.weight("blk." + std::to_string(l) + "." + kAdName[t] + ".lora_b").f32;
+    L.u = ad_[t].u; L.ldu = ad_[t].rows;
+    L.c0 = c0; L.width = width; L.r = e_.cfg().lora_rank; L.bd_w = ad_[t].bd_w; L.on = on; L.s = ad_[t].s;
   }
 
   GemvArgs wargs(const std::string& name, int rows, int K) {
@@ -590,10 +812,15 @@ class KvEngine {
       } else {
         cache.k32 = k32_ + loff; cache.v32 = v32_ + loff;
       }
-      // q | k | v with the attention RMSNorm folded in
+      // q | k | v with the attention RMSNorm folded in (and their adapters)
       GemvArgs g = wargs(pre + "attn_q.weight", W, d);
       g.x = x_; g.ldx = d; g.gamma = e_.weight(pre + "attn_norm.weight").f32; g.eps = c.rms_eps;
       g.out = qkv_; g.ldo = W;
+      for (int t = 0; t < 3; ++t)
+        if (int rc = adapter_u(l, t, g)) return rc;
+      add_lora(g, l, 0, 0, H * dh, 0);
+      add_lora(g, l, 1, H * dh, KV * dh, 0);
+      add_lora(g, l, 2, (H + KV) * dh, KV * dh, 0);
       if (int rc = gemv(g)) return rc;
       AppendArgs ap;
       ap.qkv = qkv_;
@@ -606,20 +833,28 @@ class KvEngine {
       at.qkv = qkv_; at.pos = pos_; at.c = cache; at.H = H; at.KV = KV; at.dh = dh; at.max_T = max_T_;
       at.nsplit = nsplit_; at.scale = 1.0f / std::sqrt((float)dh); at.part = part_;
       ++launches_;
-      if (launch_pdl(kv_attn_kernel, dim3(nb_ * H, nsplit_), dim3(kChunk), 0, st_, at)) return -3;
+      if (launch_pdl(kv_attn_kernel, dim3(nb_ * H, nsplit_), dim3(kChunk), attn_smem_, st_, at)) return -3;
       // x1 = x + att Wo^T, the attention output assembled from the chunks while staging
       g = wargs(pre + "attn_output.weight", d, H * dh);
       g.part = part_; g.nsplit = nsplit_; g.dh = dh;
       g.ldx = H * dh; g.out = x1_; g.ldo = d; g.res = x_; g.mode = 1;
+      if (int rc = adapter_u(l, 3, g)) return rc;
+      add_lora(g, l, 3, 0, d, 0);
       if (int rc = gemv(g)) return rc;
       // a = silu(h2 Wg^T) * (h2 Wu^T), the FFN RMSNorm folded in (gate | up rows paired)
       g = wargs(pre + "ffn_gate.weight", 2 * ff, d);
       g.x = x1_; g.ldx = d; g.gamma = e_.weight(pre + "ffn_norm.weight").f32; g.eps = c.rms_eps;
       g.out = a_; g.ldo = ff; g.mode = 2; g.pair = ff;
+      for (int t = 4; t < 6; ++t)
+        if (int rc = adapter_u(l, t, g)) return rc;
+      add_lora(g, l, 4, 0, ff, 0);
+      add_lora(g, l, 5, 0, ff, 1);
       if (int rc = gemv(g)) return rc;
       // x = x1 + a Wd^T
       g = wargs(pre + "ffn_down.weight", d, ff);
       g.x = a_; g.ldx = ff; g.out = x_; g.ldo = d; g.res = x1_; g.mode = 1;
+      if (int rc = adapter_u(l, 6, g)) return rc;
+      add_lora(g, l, 6, 0, d, 0);
       if (int rc = gemv(g)) return rc;
     }
     // logits = norm(x) W_out^T (tied: the embedding)
@@ -633,6 +868,16 @@ class KvEngine {
   int max_T_, nb_;
   bool q8_;
   int nsplit_ = 1, launches_ = 0;
+  size_t attn_smem_ = 0;   // dynamic shared memory of the attention kernel (the chunk's V rows)
+  // adapters by target (q, k, v, o, gate, up, down): u = A x buffer [n_seq][rows]
+  struct Adapter {
+    bool on = false;
+    int rows = 0, bd_w = 0;
+    float s = 1.f;
+    float* u = nullptr;
+  };
+  static constexpr int kAdapters = 7;
+  Adapter ad_[kAdapters];
   cudaStream_t st_ = nullptr;
   cudaGraphExec_t graph_ = nullptr;
   std::vector<void*> bufs_;

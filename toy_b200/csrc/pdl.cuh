@@ -11,14 +11,25 @@
 
 namespace tb2 {
 
-// Wait for the previous kernel, then let the next one launch: its CTAs are
-// scheduled once every CTA of this grid has passed this point (so all of this
-// grid's CTAs are already resident and none can be starved by the waiting
-// ones), run their data-independent prologue (barrier set-up, TMEM
-// allocation) beside this kernel and block in their own griddep_wait until it
-// completes. Kernels that hold TMEM (the GEMM and flash kernels) need more
-// than half an SM's shared memory, so two of them never share an SM.
-__device__ __forceinline__ void griddep_wait() {
+// Every kernel of the library asks for the same L1 / shared-memory split, the
+// largest shared-memory carveout: CTAs of kernels with different splits cannot
+// share an SM (which would keep the second stream's kernels off SMs that a
+// GEMM of the first holds), and a change of split between consecutive kernels
+// waits for the SM to drain. Called before each launch; sets the attribute
+// once per (device, kernel).
+void prefer_max_shared(const void* kernel);
+
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// griddep_wait, then let the next kernel launch: its CTAs are scheduled once
+// every CTA of this grid has passed this point (so all of this grid's CTAs
+// are already resident and none can be starved by the waiting ones), run
+// their prologue on data no running kernel writes (weights) beside this one
+// and block in their own wait until it completes. Used by the decode kernels,
+// whose prologues load weight rows; in the training step the early-launched
+// CTAs held shared memory the other stream's kernels needed and measured 2.5 %
+// slower, so its kernels let the next one launch at their exit.
+__device__ __forceinline__ void griddep_wait_release() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
@@ -35,6 +46,7 @@ int launch_pdl(void (*kernel)(KParams...), dim3 grid, dim3 block, size_t smem, c
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  prefer_max_shared(reinterpret_cast<const void*>(kernel));
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...) == cudaSuccess ? 0 : -3;
 }
 
@@ -56,6 +68,7 @@ int launch_pdl_cluster(void (*kernel)(KParams...), dim3 grid, dim3 block, size_t
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
+  prefer_max_shared(reinterpret_cast<const void*>(kernel));
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...) == cudaSuccess ? 0 : -3;
 }
 
