@@ -120,6 +120,15 @@ int tb2_gemm_noalloc_error(void);
  * Returns 0, or -1 for an unknown mode. */
 int tb2_gemm_set_pair_mode(int mode);
 
+/* Output tile width (columns of a CTA's tile) of every GEMM launched
+ * afterwards: 0 (the default) lets the launch plan's cost model choose; 64,
+ * 128, 192 or 256 forces that width wherever the shape and epilogue allow it
+ * (the cost model decides otherwise). For measuring the plan; at the same K
+ * split count the results are the same sums in the same order at every
+ * width. No counterpart in the reference.
+ * Returns the previous width, or -1 for another value. */
+int tb2_gemm_set_tile_width(int bn);
+
 /* How a QLoRA step feeds its frozen Q8_0 projections to the tensor cores,
  * fixed for each session when its engine is realised: 1 (the default)
  * dequantises each transformer block's projections once per use (once in the
@@ -143,6 +152,15 @@ int tb2_set_q8_base_mode(int mode);
  * way. No counterpart in the reference.
  * Returns the previous setting, or -1 for an unknown one. */
 int tb2_set_q8_ring_l2(int on);
+
+/* Persistent CTAs of each weight-gradient GEMM the step runs on its second
+ * stream: 0 (the default) one per SM; n > 0 at most n, the same tiles and K
+ * splits walked by fewer CTAs so that more SMs stay with the activation
+ * gradient chain. Results are identical. Read when a session enqueues its
+ * step program (its first step, which also captures the step's CUDA graph).
+ * No counterpart in the reference.
+ * Returns the previous setting, or -1 for n outside 0..148. */
+int tb2_set_side_gemm_ctas(int n);
 
 /* hi = rn_bf16(x), lo = rn_bf16(x - hi) for n f32 values. */
 int tb2_split_f32(const float *x, void *hi, void *lo, size_t n, void *stream);

@@ -60,9 +60,13 @@ int tb2_gemm(int M, int N, int K, int batch, int split, const tb2_operand* a, co
 
 int tb2_gemm_set_pair_mode(int mode) { return tb2::gemm_set_pair_mode(mode); }
 
+int tb2_gemm_set_tile_width(int bn) { return tb2::gemm_set_tile_width(bn); }
+
 int tb2_set_q8_base_mode(int mode) { return tb2::engine_set_q8_base_mode(mode); }
 
 int tb2_set_q8_ring_l2(int on) { return tb2::engine_set_q8_ring_l2(on); }
+
+int tb2_set_side_gemm_ctas(int n) { return tb2::engine_set_side_gemm_ctas(n); }
 
 int tb2_split_f32(const float* x, void* hi, void* lo, size_t n, void* stream) {
   if (!x || !hi || !lo) return -1;

@@ -26,6 +26,14 @@ namespace tb2 {
 
 int g_q8_base_mode = 1;
 int g_ring_l2 = 1;
+int g_side_gemm_ctas = 0;
+
+int engine_set_side_gemm_ctas(int n) {
+  if (n < 0 || n > 148) return -1;
+  const int prev = g_side_gemm_ctas;
+  g_side_gemm_ctas = n;
+  return prev;
+}
 
 int engine_set_q8_ring_l2(int on) {
   if (on < 0 || on > 1) return -1;
@@ -942,9 +950,11 @@ int LlamaEngine::gemm(const GemmDesc& d) {
   return rc;
 }
 
-int LlamaEngine::gemm_side(const GemmDesc& d) {
-  if (!side_ || !wsc_.ws) return gemm(d);
+int LlamaEngine::gemm_side(const GemmDesc& d0) {
+  if (!side_ || !wsc_.ws) return gemm(d0);
   ++counting_;
+  GemmDesc d = d0;
+  d.max_ctas = g_side_gemm_ctas;
   const int rc = gemm_launch(d, wsc_.ws ? wsc_ : gemm_scratch(), err_, wst_);
   if (rc) fprintf(stderr, "[toy_b200] gemm launch rejected (%d): M=%d N=%d K=%d batch=%d\n", rc, d.M, d.N, d.K, d.batch);
   return rc;

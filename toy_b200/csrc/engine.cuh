@@ -70,6 +70,11 @@ int engine_set_q8_base_mode(int mode);
 // one); 0: the ring is written and read as ordinary data. Returns the previous
 // setting, or -1.
 int engine_set_q8_ring_l2(int on);
+// Persistent CTAs of each weight-gradient GEMM on the second stream of engines
+// realised afterwards: 0 (default) one per SM, n > 0 at most n (the same work
+// walked by fewer CTAs, leaving SMs to the activation chain). Returns the
+// previous setting, or -1.
+int engine_set_side_gemm_ctas(int n);
 
 struct DeviceBuf {
   void* p = nullptr;

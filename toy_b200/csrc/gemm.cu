@@ -904,6 +904,11 @@ int make_q8_map(CUtensorMap* map, const Operand& o, int box_rows) {
 // streams the partial slabs once. A k-block also cannot finish faster than
 // its operand tiles arrive: ~82 GB/s per SM from L2 (~12 TB/s over the chip),
 // which is what makes narrow tiles slow.
+//
+// The model prices a GEMM running alone. Refitting it to in-graph times of
+// each of the step's shapes alone (every tile width x K splits 1..8) made its
+// picks 4.5 % faster in isolation but the two-stream step 0.7 % slower: the
+// 96-CTA tiles it gave up leave SMs to the weight-gradient stream.
 constexpr double kSmFlopsPerUs = 1310.0e6 / kNumSMs;
 constexpr double kSmOperandBytesPerUs = 82.0e3;
 
@@ -949,6 +954,8 @@ struct Plan {
 
 // CTA pairs: -1 by shape (below), 0 never, 1 wherever the shape allows
 int g_pair_mode = -1;
+// output tile width: 0 by the cost model, else 64 / 128 / 192 / 256 wherever the shape allows it
+int g_tile_bn = 0;
 
 // Measured on B200 (SmolLM2 step shapes, M = 4096 tokens): a pair beats two
 // single CTAs when both operands are K-major and N is wide -- the LM head
@@ -971,11 +978,13 @@ Plan choose_plan(const GemmDesc& d, long long ws_floats, bool q8) {
   const bool pair_ok = g_pair_mode != 0 && d.split && !d.causal && (g_pair_mode == 1 || pair_wins(d));
   Plan best;
   double best_t = 1e30;
+  auto search = [&](int force_bn) {
   for (int pr = 0; pr < 2; ++pr) {
     const bool pair = pr == 1;
     if (pair && !pair_ok) continue;
     if (!pair && pair_ok) continue;   // a shape that qualifies runs on pairs
     for (int bn : kBn) {
+      if (force_bn && bn != force_bn) continue;
       if (pair && bn != 128 && bn != 256) continue;
       if (q8 && !pair && bn > 128) break;
       if (bn > 64 && bn - 64 >= d.N && !(pair && bn == 128)) break;   // a narrower tile already covers N
@@ -1000,6 +1009,9 @@ Plan choose_plan(const GemmDesc& d, long long ws_floats, bool q8) {
       }
     }
   }
+  };
+  search(g_tile_bn);
+  if (best_t >= 1e30) search(0);   // the forced width does not fit this shape
   return best;
 }
 
@@ -1079,12 +1091,14 @@ int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream
   k.q8_rows = d.b.rows;
   k.q8_cols = d.b.cols;
   if constexpr (PAIR) {
-    const int pairs = k.units < max_pairs ? k.units : max_pairs;
+    int pairs = k.units < max_pairs ? k.units : max_pairs;
+    if (d.max_ctas >= 2 && pairs > d.max_ctas / 2) pairs = d.max_ctas / 2;
     if (launch_pdl_cluster(kern, dim3(2 * pairs), dim3(threads_of<Q8>()), S::kSmemBytes, stream, 2, ma_hi, ma_lo, mb_hi,
                            mb_lo, k) != 0)
       return -21;
   } else {
-    const int grid = k.units < kNumSMs ? k.units : kNumSMs;
+    int grid = k.units < kNumSMs ? k.units : kNumSMs;
+    if (d.max_ctas > 0 && grid > d.max_ctas) grid = d.max_ctas;
     if (launch_pdl(kern, dim3(grid), dim3(threads_of<Q8>()), S::kSmemBytes, stream, ma_hi, ma_lo, mb_hi, mb_lo, k) != 0)
       return -21;
   }
@@ -1104,6 +1118,13 @@ int gemm_set_pair_mode(int mode) {
   if (mode < -1 || mode > 1) return -1;
   g_pair_mode = mode;
   return 0;
+}
+
+int gemm_set_tile_width(int bn) {
+  if (bn != 0 && bn != 64 && bn != 128 && bn != 192 && bn != 256) return -1;
+  const int prev = g_tile_bn;
+  g_tile_bn = bn;
+  return prev;
 }
 
 int make_plane_map(CUtensorMap* map, const __nv_bfloat16* base, const Operand& o, int box_rows) {

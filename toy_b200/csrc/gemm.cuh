@@ -120,6 +120,7 @@ struct GemmDesc {
   bool split = true;
   int splits = 0;   // K ranges reduced through the workspace; 0 = choose from the tile count
   int causal = 0;   // 1: skip tiles with n0 > m0 + 127; 2: clamp K to m0 + 128 (zero beyond)
+  int max_ctas = 0; // persistent CTAs at most (0: one per SM); the units are the same, walked by fewer CTAs
   Operand a, b;
   Epilogue epi;
 };
@@ -146,6 +147,10 @@ int gemm_effective_splits(const GemmDesc& d, int ksplits);
 // (both operands K-major, N >= 2048), 0 never, 1 wherever the shape allows.
 // Process-wide; returns 0 or -1 for a bad mode.
 int gemm_set_pair_mode(int mode);
+// Output tile width of every later GEMM: 0 (default) by the cost model, else
+// 64 / 128 / 192 / 256 wherever the shape allows it. Returns the previous
+// width, or -1 for another value.
+int gemm_set_tile_width(int bn);
 
 // TMA map over one bf16 plane laid out as `o` describes: dims {cols, rows,
 // nbatch}, box {64, box_rows, 1}, 128-byte swizzle. Rows past `rows` inside a

@@ -11,14 +11,6 @@
 
 namespace tb2 {
 
-// Every kernel of the library asks for the same L1 / shared-memory split, the
-// largest shared-memory carveout: CTAs of kernels with different splits cannot
-// share an SM (which would keep the second stream's kernels off SMs that a
-// GEMM of the first holds), and a change of split between consecutive kernels
-// waits for the SM to drain. Called before each launch; sets the attribute
-// once per (device, kernel).
-void prefer_max_shared(const void* kernel);
-
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // griddep_wait, then let the next kernel launch: its CTAs are scheduled once
@@ -46,7 +38,6 @@ int launch_pdl(void (*kernel)(KParams...), dim3 grid, dim3 block, size_t smem, c
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  prefer_max_shared(reinterpret_cast<const void*>(kernel));
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...) == cudaSuccess ? 0 : -3;
 }
 
@@ -68,7 +59,6 @@ int launch_pdl_cluster(void (*kernel)(KParams...), dim3 grid, dim3 block, size_t
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  prefer_max_shared(reinterpret_cast<const void*>(kernel));
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...) == cudaSuccess ? 0 : -3;
 }
 

@@ -5,7 +5,6 @@
 
 #include <algorithm>
 #include <mutex>
-#include <unordered_set>
 
 namespace tb2 {
 
@@ -21,17 +20,6 @@ struct L2Keep {
 };
 L2Keep g_l2[64];
 }  // namespace
-
-void prefer_max_shared(const void* kernel) {
-  static std::mutex mu;
-  static std::unordered_set<const void*> done[64];
-  int dev = 0;
-  if (!kernel || cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return;
-  std::lock_guard<std::mutex> lk(mu);
-  if (done[dev].count(kernel)) return;
-  cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
-  done[dev].insert(kernel);
-}
 
 bool l2_keep_acquire(size_t bytes) {
   int dev = 0;
