@@ -162,6 +162,13 @@ int tb2_set_q8_ring_l2(int on);
  * Returns the previous setting, or -1 for n outside 0..148. */
 int tb2_set_side_gemm_ctas(int n);
 
+/* Output tile width of those weight-gradient GEMMs: 0 lets the launch plan
+ * choose, 64 / 128 / 192 / 256 forces it where the shape allows (as
+ * tb2_gemm_set_tile_width, for these GEMMs only). Read when a session
+ * enqueues its step program. No counterpart in the reference.
+ * Returns the previous width, or -1 for another value. */
+int tb2_set_side_gemm_tile_width(int bn);
+
 /* hi = rn_bf16(x), lo = rn_bf16(x - hi) for n f32 values. */
 int tb2_split_f32(const float *x, void *hi, void *lo, size_t n, void *stream);
 

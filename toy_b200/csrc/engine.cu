@@ -27,6 +27,14 @@ namespace tb2 {
 int g_q8_base_mode = 1;
 int g_ring_l2 = 1;
 int g_side_gemm_ctas = 0;
+int g_side_gemm_bn = 128;   // measured in the step: 223.2k vs 222.1k (plan's choice), 216.1k (256), 210.0k (64)
+
+int engine_set_side_gemm_tile_width(int bn) {
+  if (bn != 0 && bn != 64 && bn != 128 && bn != 192 && bn != 256) return -1;
+  const int prev = g_side_gemm_bn;
+  g_side_gemm_bn = bn;
+  return prev;
+}
 
 int engine_set_side_gemm_ctas(int n) {
   if (n < 0 || n > 148) return -1;
@@ -955,6 +963,7 @@ int LlamaEngine::gemm_side(const GemmDesc& d0) {
   ++counting_;
   GemmDesc d = d0;
   d.max_ctas = g_side_gemm_ctas;
+  d.tile_bn = g_side_gemm_bn;
   const int rc = gemm_launch(d, wsc_.ws ? wsc_ : gemm_scratch(), err_, wst_);
   if (rc) fprintf(stderr, "[toy_b200] gemm launch rejected (%d): M=%d N=%d K=%d batch=%d\n", rc, d.M, d.N, d.K, d.batch);
   return rc;

@@ -75,6 +75,9 @@ int engine_set_q8_ring_l2(int on);
 // walked by fewer CTAs, leaving SMs to the activation chain). Returns the
 // previous setting, or -1.
 int engine_set_side_gemm_ctas(int n);
+// Output tile width of the weight-gradient GEMMs on the second stream (0: the
+// launch plan's choice). Returns the previous width, or -1.
+int engine_set_side_gemm_tile_width(int bn);
 
 struct DeviceBuf {
   void* p = nullptr;

@@ -1010,7 +1010,7 @@ Plan choose_plan(const GemmDesc& d, long long ws_floats, bool q8) {
     }
   }
   };
-  search(g_tile_bn);
+  search(d.tile_bn ? d.tile_bn : g_tile_bn);
   if (best_t >= 1e30) search(0);   // the forced width does not fit this shape
   return best;
 }

@@ -121,6 +121,7 @@ struct GemmDesc {
   int splits = 0;   // K ranges reduced through the workspace; 0 = choose from the tile count
   int causal = 0;   // 1: skip tiles with n0 > m0 + 127; 2: clamp K to m0 + 128 (zero beyond)
   int max_ctas = 0; // persistent CTAs at most (0: one per SM); the units are the same, walked by fewer CTAs
+  int tile_bn = 0;  // output tile width for this GEMM (0: the launch plan's choice; else as gemm_set_tile_width)
   Operand a, b;
   Epilogue epi;
 };
