@@ -169,6 +169,15 @@ int tb2_set_side_gemm_ctas(int n);
  * Returns the previous width, or -1 for another value. */
 int tb2_set_side_gemm_tile_width(int bn);
 
+/* 1: the backward's GEMMs of an adapter recipe, which have the GPU to
+ * themselves, use the launch plan for a GEMM running alone; 0 (the default,
+ * which measured the same within noise): every GEMM uses the plan for a GPU
+ * shared with the weight-gradient stream. K-split counts may differ between the two, so
+ * the last bits of a step may too; each is deterministic. Read when a session
+ * enqueues its step program. No counterpart in the reference.
+ * Returns the previous setting, or -1 for another value. */
+int tb2_set_plan_alone(int on);
+
 /* hi = rn_bf16(x), lo = rn_bf16(x - hi) for n f32 values. */
 int tb2_split_f32(const float *x, void *hi, void *lo, size_t n, void *stream);
 

@@ -70,6 +70,8 @@ int tb2_set_side_gemm_ctas(int n) { return tb2::engine_set_side_gemm_ctas(n); }
 
 int tb2_set_side_gemm_tile_width(int bn) { return tb2::engine_set_side_gemm_tile_width(bn); }
 
+int tb2_set_plan_alone(int on) { return tb2::engine_set_plan_alone(on); }
+
 int tb2_split_f32(const float* x, void* hi, void* lo, size_t n, void* stream) {
   if (!x || !hi || !lo) return -1;
   return tb2::launch_split_f32(x, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo), (long long)n,

@@ -27,6 +27,13 @@ namespace tb2 {
 int g_q8_base_mode = 1;
 int g_ring_l2 = 1;
 int g_side_gemm_ctas = 0;
+int g_plan_alone = 0;   // measured neutral for QLoRA (270.4k alone vs 270.8k shared, two runs each)
+int engine_set_plan_alone(int on) {
+  if (on < 0 || on > 1) return -1;
+  const int prev = g_plan_alone;
+  g_plan_alone = on;
+  return prev;
+}
 int g_side_gemm_bn = 128;   // measured in the step: 223.2k vs 222.1k (plan's choice), 216.1k (256), 210.0k (64)
 
 int engine_set_side_gemm_tile_width(int bn) {
@@ -949,9 +956,11 @@ void LlamaEngine::prof_end() {
   evnext_ += 2;
 }
 
-int LlamaEngine::gemm(const GemmDesc& d) {
+int LlamaEngine::gemm(const GemmDesc& d0) {
   ++counting_;
-  if (profiling_) prof_begin(kKGemm, 2.0 * d.M * d.N * d.K * d.batch);
+  if (profiling_) prof_begin(kKGemm, 2.0 * d0.M * d0.N * d0.K * d0.batch);
+  GemmDesc d = d0;
+  d.alone = d0.alone || (gemm_alone_ && g_plan_alone);
   const int rc = gemm_launch(d, gemm_scratch(), err_, stream_);
   if (profiling_) prof_end();
   if (rc) fprintf(stderr, "[toy_b200] gemm launch rejected (%d): M=%d N=%d K=%d batch=%d\n", rc, d.M, d.N, d.K, d.batch);
@@ -1882,8 +1891,16 @@ int LlamaEngine::enqueue_optimizer() {
 int LlamaEngine::enqueue_step(bool run_optimizer, bool accumulate) {
   counting_ = 0;
   CK(bucket_begin());
+  // the backward's GEMMs of an adapter recipe have the GPU to themselves (its
+  // second stream carries only CUDA-core adapter work): planned as such. The
+  // forward's keep the shared plan, which measured faster there (full FT
+  // 222.4k vs 220.1k with the forward planned alone; the isolated timings the
+  // alone plan is fitted to lack the forward's L2 reuse between kernels).
+  gemm_alone_ = false;
   CK(enqueue_forward());
+  gemm_alone_ = cfg_.mode != 0;
   CK(enqueue_backward());
+  gemm_alone_ = false;
   if (accumulate)
     KL(launch_add_inplace(static_cast<float*>(acc_.p), static_cast<const float*>(g_.p), n_train_, stream_));
   if (run_optimizer) CK(enqueue_optimizer());

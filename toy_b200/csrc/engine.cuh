@@ -78,6 +78,10 @@ int engine_set_side_gemm_ctas(int n);
 // Output tile width of the weight-gradient GEMMs on the second stream (0: the
 // launch plan's choice). Returns the previous width, or -1.
 int engine_set_side_gemm_tile_width(int bn);
+// 1: an adapter recipe's backward GEMMs (the GPU to themselves) are planned as
+// such; 0 (default): every GEMM with the shared-GPU launch plan. Read when a session enqueues its step program.
+// Returns the previous setting, or -1.
+int engine_set_plan_alone(int on);
 
 struct DeviceBuf {
   void* p = nullptr;
@@ -329,7 +333,8 @@ class LlamaEngine {
   // Q8_0 base as planes: per block the first quant / scale index and the count
   // of its projections' elements; two slots of slot_elems hi then lo values
   bool q8_planes_ = false;
-  bool ring_keep_ = false;   // the ring holds an L2 persisting set-aside (evict-last writes and reads)
+  bool ring_keep_ = false;
+  bool gemm_alone_ = false;   // main-stream GEMMs enqueued now have the GPU to themselves (launch plan)   // the ring holds an L2 persisting set-aside (evict-last writes and reads)
   DeviceBuf q8pl_;
   long long q8_slot_elems_ = 0;
   int ring_layer_[2] = {-1, -1};

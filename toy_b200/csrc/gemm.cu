@@ -905,17 +905,30 @@ int make_q8_map(CUtensorMap* map, const Operand& o, int box_rows) {
 // its operand tiles arrive: ~82 GB/s per SM from L2 (~12 TB/s over the chip),
 // which is what makes narrow tiles slow.
 //
-// The model prices a GEMM running alone. Refitting it to in-graph times of
-// each of the step's shapes alone (every tile width x K splits 1..8) made its
-// picks 4.5 % faster in isolation but the two-stream step 0.7 % slower: the
-// 96-CTA tiles it gave up leave SMs to the weight-gradient stream.
-constexpr double kSmFlopsPerUs = 1310.0e6 / kNumSMs;
-constexpr double kSmOperandBytesPerUs = 82.0e3;
+// These constants price a GEMM that shares the GPU with the weight-gradient
+// stream of a full fine-tune's backward: the 96-CTA tiles they prefer for
+// N = 576 leave SMs to that stream. A GEMM that has the GPU to itself (the
+// forward, the backward of an adapter recipe: GemmDesc::alone) is priced with
+// constants fitted to in-graph times of each of the step's shapes alone (M =
+// 4096 tokens; forward, dX and dW products of the SmolLM2 projections; every
+// tile width x K splits 1..8): ~8 us before the first k-block, up to ~1880
+// TFLOP/s executed, ~121 GB/s of operand tiles per SM (MN-major ~12 %
+// cheaper), 0.12 us per tile switch, an epilogue drain of ~44 GB/s per CTA
+// (~4.3 TB/s over the chip), K-split reductions at ~2.7 TB/s + 0.5 us. Their
+// picks are 4.5 % faster than these constants' on those shapes timed alone,
+// but the full fine-tune's two-stream backward ran 0.7 % slower with them.
+struct CostModel {
+  double sm_flops_per_us, operand_bytes_per_us, mn_major_bytes, fill_us, switch_us, drain_cta, drain_total,
+      split_bw, split_us;
+};
+constexpr CostModel kShared = {1310.0e6 / kNumSMs, 82.0e3, 1.0, 1.2, 0.5, 100.0e3, 6.5e6, 5.0e6, 2.5};
+constexpr CostModel kAlone = {1880.0e6 / kNumSMs, 121.0e3, 0.88, 8.2, 0.12, 44.0e3, 4.25e6, 2.7e6, 0.5};
 
 // Q8_0 B operand: elements the 8 converter warps dequantise and split per us
 constexpr double kConvElemsPerUs = 6000.0;
 
 double estimate_us(const GemmDesc& d, int bn, int s, bool pair, bool q8) {
+  const CostModel& cm = d.alone ? kAlone : kShared;
   const int bmt = pair ? 2 * BM : BM;            // output rows of a unit
   const double slots = pair ? kNumSMs / 2 : kNumSMs;   // units in flight
   const int rb = pair ? bn / 2 : bn;              // B rows per CTA
@@ -935,15 +948,16 @@ double estimate_us(const GemmDesc& d, int bn, int s, bool pair, bool q8) {
   const double tile_bytes = (double)BM * bn * out_b;
   const double kb_unit = std::ceil((double)kb / s);
   const double planes = d.split ? 2.0 : 1.0;
-  const double t_mma = (d.split ? 3.0 : 1.0) * 2.0 * BM * bn * BK / kSmFlopsPerUs;
-  const double b_bytes = q8 ? (double)rb * BK : planes * rb * BK * 2.0;
-  const double t_feed = (planes * BM * BK * 2.0 + b_bytes + tile_bytes / kb_unit) / kSmOperandBytesPerUs;
+  const double t_mma = (d.split ? 3.0 : 1.0) * 2.0 * BM * bn * BK / cm.sm_flops_per_us;
+  const double b_bytes = (q8 ? (double)rb * BK : planes * rb * BK * 2.0) * (d.b.mn_major ? cm.mn_major_bytes : 1.0);
+  const double a_bytes = planes * BM * BK * 2.0 * (d.a.mn_major ? cm.mn_major_bytes : 1.0);
+  const double t_feed = (a_bytes + b_bytes + tile_bytes / kb_unit) / cm.operand_bytes_per_us;
   const double t_conv = q8 ? (double)rb * BK / kConvElemsPerUs : 0.0;
   const double t_kb = std::max(t_mma, std::max(t_feed, t_conv));
   const double active = (units < slots ? units : slots) * (pair ? 2 : 1);
-  const double drain_bw = std::min(100.0e3, 6.5e6 / active);   // bytes per us per CTA
-  double t = 1.2 + per_cta * (kb_unit * t_kb + 0.5) + tile_bytes / drain_bw;
-  if (s > 1) t += ((s + 1.0) * d.M * d.N * 4.0 + (reads_out ? d.M * d.N * 4.0 : 0.0)) / 5.0e6 + 2.5;
+  const double drain_bw = std::min(cm.drain_cta, cm.drain_total / active);   // bytes per us per CTA
+  double t = cm.fill_us + per_cta * (kb_unit * t_kb + cm.switch_us) + tile_bytes / drain_bw;
+  if (s > 1) t += ((s + 1.0) * d.M * d.N * 4.0 + (reads_out ? d.M * d.N * 4.0 : 0.0)) / cm.split_bw + cm.split_us;
   return t;
 }
 

@@ -122,6 +122,7 @@ struct GemmDesc {
   int causal = 0;   // 1: skip tiles with n0 > m0 + 127; 2: clamp K to m0 + 128 (zero beyond)
   int max_ctas = 0; // persistent CTAs at most (0: one per SM); the units are the same, walked by fewer CTAs
   int tile_bn = 0;  // output tile width for this GEMM (0: the launch plan's choice; else as gemm_set_tile_width)
+  int alone = 0;    // 1: nothing heavy runs beside it -- plan for a GEMM that has the GPU to itself
   Operand a, b;
   Epilogue epi;
 };
