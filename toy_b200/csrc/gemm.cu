@@ -35,14 +35,21 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;          // one 128-byte swizzle atom of bf16 along K
-constexpr int kThreads = 192;   // producer, MMA issuer, 4 epilogue warps
+constexpr int kThreads = 192;   // producer, MMA issuer, 4 epilogue warps (the role warps of a 4-warp epilogue)
 constexpr int kConvWarps = 8;   // Q8_0 B operand: warps 6.. dequantise into the B tiles
 constexpr int kSmemBudget = 200 * 1024;
 constexpr int kNumSMs = 148;
 
-template <bool Q8>
-constexpr int threads_of() {
-  return Q8 ? kThreads + 32 * kConvWarps : kThreads;
+// Epilogue warps: 8 (two per TMEM lane quarter, one per column half) for the
+// plain instantiations whose tile splits into halves of whole 64-column
+// groups; 4 for the fused epilogues, the Q8_0 B operand and 64-wide tiles.
+template <int BN, bool Q8, bool FUSED>
+__host__ __device__ constexpr int epi_warps() {
+  return (Q8 || FUSED || BN == 64) ? 4 : 8;
+}
+template <int BN, bool Q8, bool FUSED>
+__host__ __device__ constexpr int threads_of() {
+  return 64 + 32 * epi_warps<BN, Q8, FUSED>() + (Q8 ? 32 * kConvWarps : 0);
 }
 
 struct KArgs {
@@ -365,7 +372,7 @@ __device__ __forceinline__ void epi_swiglu(const Epilogue& e, int m, int n0, boo
 // FUSED instantiations carry the fused epilogues (LoRA addends, RoPE / SwiGLU
 // modes); the others leave that code out so they keep their register budget.
 template <int BN, bool SPLIT, bool Q8, bool FUSED, bool PAIR>
-__global__ void __launch_bounds__(threads_of<Q8>(), 1)
+__global__ void __launch_bounds__(threads_of<BN, Q8, FUSED>(), 1)
     gemm_split_bf16_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_constant__ CUtensorMap map_a_lo,
                            const __grid_constant__ CUtensorMap map_b_hi, const __grid_constant__ CUtensorMap map_b_lo,
                            const KArgs args) {
@@ -409,7 +416,7 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], PAIR ? 8 : 4);
+      mbar_init(&tempty[b], (PAIR ? 2 : 1) * epi_warps<BN, Q8, FUSED>());
     }
     fence_barrier_init();
   }
@@ -612,7 +619,7 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
         ++local;
       }
     }
-  } else if (warp >= kThreads / 32) {
+  } else if (warp >= 2 + epi_warps<BN, Q8, FUSED>()) {
     // ------------------------------------------------ Q8_0 dequantisation
     // Each item is one Q8_0 block (32 quants of a stored row, one scale): value
     // = scale * q, split into hi / lo bf16 and written to the B plane tiles in
@@ -704,8 +711,13 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // warp w reads TMEM lanes 32 (w % 4) ..; with 8 epilogue warps, warps 2..5
+    // take the tile's first half of 32-column chunks and warps 6..9 the second
+    constexpr int EW = epi_warps<BN, Q8, FUSED>();
+    constexpr int kCh = BN / 32 / (EW / 4);   // chunks per warp
     const int q = warp & 3;
     const int row = q * 32 + lane;
+    const int c_begin = EW == 8 ? ((warp - 2) >> 2) * kCh : 0, c_end = c_begin + kCh;
     const Epilogue& e = args.epi;
     uint32_t local = 0;
     for (int u = walker; u < args.units; u += walkers) {
@@ -721,8 +733,9 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
       // is ready, the next chunk's while the current one is stored
       const long long rowoff = row_in && direct ? epi_offset(e, w.z, m, 0) : 0;
       float4 pre[2][8];
-      if (row_in && direct && w.n0 < args.N)
-        epi_prefetch(e, args.N, rowoff + (w.n0 / e.n_div) * e.n_s1 + (w.n0 % e.n_div), w.n0, pre[0]);
+      const int n_first = w.n0 + c_begin * 32;
+      if (row_in && direct && n_first < args.N)
+        epi_prefetch(e, args.N, rowoff + (n_first / e.n_div) * e.n_s1 + (n_first % e.n_div), n_first, pre[0]);
       const bool ok = mbar_wait(&tfull[b], tph, args.err, kErrWaitAccum);
       tc_fence_after();
       const bool row_ok = ok && row_in;
@@ -745,7 +758,7 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
       auto chunk = [&](int c, const float4 (&cur)[8], float4 (&next)[8]) {
         float v[32];
         tmem_ld32(acc_tmem + (uint32_t)(c * 32), v);
-        if (c == BN / 32 - 1) release_acc<PAIR>(&tempty[b], lane);   // accumulator read: back to the MMA issuer
+        if (c == c_end - 1) release_acc<PAIR>(&tempty[b], lane);   // accumulator read: back to the MMA issuer
         const int nc = w.n0 + c * 32;
         if (!row_ok || nc >= args.N) return;
         if constexpr (!Q8) {   // (the LM head's operands are planes; Q8_0 kernels keep their registers)
@@ -786,7 +799,7 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
               if (nc + i < args.N) part[nc + i] = v[i];
           }
         } else {
-          if (c + 1 < BN / 32 && nc + 32 < args.N)
+          if (c + 1 < c_end && nc + 32 < args.N)
             epi_prefetch(e, args.N, rowoff + ((nc + 32) / e.n_div) * e.n_s1 + ((nc + 32) % e.n_div), nc + 32, next);
           if constexpr (FUSED) {
             if (e.n_lora) lora_add(e, m, nc, v);
@@ -795,9 +808,9 @@ __global__ void __launch_bounds__(threads_of<Q8>(), 1)
         }
       };
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; c += 2) {   // BN / 32 is even for every BN
+      for (int c = c_begin; c < c_end; c += 2) {   // (a warp's chunk count is odd for 192-wide tiles)
         chunk(c, pre[0], pre[1]);
-        chunk(c + 1, pre[1], pre[0]);
+        if (c + 1 < c_end) chunk(c + 1, pre[1], pre[0]);
       }
     }
   }
@@ -1005,6 +1018,9 @@ Plan choose_plan(const GemmDesc& d, long long ws_floats, bool q8) {
       if (d.epi.mode == kEpiSwiGLU && bn != 128 && bn != 256) continue;   // BN/2 gate + BN/2 up columns
       if (d.epi.mode == kEpiSwiGLU && q8 && !pair && bn != 128) continue;
       if (d.epi.mode == kEpiRopeQKV && bn % d.epi.rope.dh) continue;       // whole heads per tile
+      // the logsumexp pairs 32-column chunks into 64-column groups: a 192-wide
+      // tile's 8 epilogue warps would split a group between two warps
+      if (d.epi.mode == kEpiStoreLse && bn == 192) continue;
       int s_lo = 1, s_hi = 1;
       if (d.splits > 0 && !fused && d.epi.mode != kEpiStoreLse) {
         s_lo = s_hi = d.splits;
@@ -1041,7 +1057,7 @@ int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream
     if (PAIR) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(2 * kNumSMs);
-      cfg.blockDim = dim3(threads_of<Q8>());
+      cfg.blockDim = dim3(threads_of<BN, Q8, FUSED>());
       cfg.dynamicSmemBytes = S::kSmemBytes;
       cudaLaunchAttribute at[1];
       at[0].id = cudaLaunchAttributeClusterDimension;
@@ -1107,13 +1123,14 @@ int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream
   if constexpr (PAIR) {
     int pairs = k.units < max_pairs ? k.units : max_pairs;
     if (d.max_ctas >= 2 && pairs > d.max_ctas / 2) pairs = d.max_ctas / 2;
-    if (launch_pdl_cluster(kern, dim3(2 * pairs), dim3(threads_of<Q8>()), S::kSmemBytes, stream, 2, ma_hi, ma_lo, mb_hi,
-                           mb_lo, k) != 0)
+    if (launch_pdl_cluster(kern, dim3(2 * pairs), dim3(threads_of<BN, Q8, FUSED>()), S::kSmemBytes, stream, 2, ma_hi,
+                           ma_lo, mb_hi, mb_lo, k) != 0)
       return -21;
   } else {
     int grid = k.units < kNumSMs ? k.units : kNumSMs;
     if (d.max_ctas > 0 && grid > d.max_ctas) grid = d.max_ctas;
-    if (launch_pdl(kern, dim3(grid), dim3(threads_of<Q8>()), S::kSmemBytes, stream, ma_hi, ma_lo, mb_hi, mb_lo, k) != 0)
+    if (launch_pdl(kern, dim3(grid), dim3(threads_of<BN, Q8, FUSED>()), S::kSmemBytes, stream, ma_hi, ma_lo, mb_hi, mb_lo,
+                   k) != 0)
       return -21;
   }
   if (splits > 1) {
