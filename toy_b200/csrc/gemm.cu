@@ -2,8 +2,10 @@
 // shared-memory pipeline, single-thread tcgen05.mma issue into one of two TMEM
 // accumulators, 4-warp epilogue.
 //
-// CTA = 6 warps: warp 0 TMA producer, warp 1 TMEM owner + MMA issuer,
-// warps 2..5 epilogue (warp w reads TMEM lanes 32*(w%4) .. 32*(w%4)+31).
+// CTA = warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, then 4 or 8
+// epilogue warps (warp w reads TMEM lanes 32*(w%4) .. 32*(w%4)+31; with 8,
+// the two warps of a lane quarter take one column half of the tile each),
+// plus 8 converter warps for a Q8_0 B operand.
 // Each CTA walks the work units u = blockIdx.x, blockIdx.x + gridDim.x, ...;
 // a unit is one 128 x BN output tile (of one batch entry) over a range of K.
 // The producer's stage ring runs across units; the MMA issuer alternates
