@@ -49,7 +49,18 @@ WORKLOADS = {
     # toy's own LoRA recipe: per-head LoRA-Q (one rank-8 pair per query head, scale 1) over the Q8_0 base
     "smollm2_lora_q_b8_t512": dict(mode=1, B=8, T=512, lora=("q",), per_head=True, lr=1e-4, wd=0.01,
                                    init_std=0.0),
+    # the other benchmark configurations' shapes (QLoRA over a Q8_0 base), one GPU each
+    "llama32_1b_qlora_r16_b16_t1024": dict(model="llama32_1b", mode=1, B=16, T=1024, rank=16,
+                                           lora=("q", "k", "v", "o", "gate", "up", "down"), lr=1e-4, wd=0.01,
+                                           init_std=0.0),
+    "qwen25_7b_qlora_r16_b4_t2048": dict(model="qwen25_7b", mode=1, B=4, T=2048, rank=16,
+                                         lora=("q", "k", "v", "o", "gate", "up", "down"), lr=1e-4, wd=0.01,
+                                         init_std=0.0),
+    "olmoe_1b_7b_qlora_r8_b8_t1024": dict(model="olmoe_1b_7b", mode=1, B=8, T=1024, rank=8,
+                                          lora=("q", "k", "v", "o"), lr=1e-4, wd=0.01, init_std=0.0),
 }
+MODEL_NAMES = {"smollm2": "SmolLM2-135M shape", "llama32_1b": "Llama-3.2-1B shape", "qwen25_7b": "Qwen2.5-7B shape",
+               "olmoe_1b_7b": "OLMoE-1B-7B shape"}
 
 # DRAM traffic of the step's GEMM launches, from one ncu capture of the full
 # workload (dram__bytes_read.sum + dram__bytes_write.sum summed over the 363
@@ -79,10 +90,12 @@ def peaks():
 
 def step_flops_per_token(cfg, T, mode, lora_targets, rank, per_head=False):
     """Algorithmic FLOPs per token: full FT 6*P_mm + 3*A; QLoRA 4*P_mm + 3*A + 6*P_lora,
-    P_mm = projection + LM-head parameters touched per token, A = 4*L*H*dh*(T+1)/2
+    P_mm = projection + LM-head parameters touched per token (an expert block: the
+    router and the n_experts_used experts a token visits), A = 4*L*H*dh*(T+1)/2
     (per-head LoRA-Q: P_lora = L*H*r*(d + dh))."""
     d, H, KV, dh, ff, L, V = cfg.d_model, cfg.n_heads, cfg.n_kv, cfg.d_head, cfg.d_ff, cfg.n_layers, cfg.vocab
-    per_layer = d * (H + 2 * KV) * dh + H * dh * d + 2 * ff * d + ff * d
+    ffn = 3 * ff * d * (cfg.n_experts_used if cfg.n_experts else 1) + (cfg.n_experts * d if cfg.n_experts else 0)
+    per_layer = d * (H + 2 * KV) * dh + H * dh * d + ffn
     p_mm = L * per_layer + V * d
     A = 4 * L * H * dh * (T + 1) / 2
     if mode == 0:
@@ -202,6 +215,10 @@ def run_reference(args, wl):
     rank, world, _ = dist_env()
     if rank != 0:
         return
+    if wl.get("model", "smollm2") != "smollm2":
+        print(json.dumps({"impl": "reference", "unavailable": "the CPU port of this shape takes hours per step; "
+                          "the reference arm runs the SmolLM2-135M workloads"}), flush=True)
+        return
     # one full step of the workload takes ~0.5-1 min on the host: time one, a second when the first was quick
     value, n = cpu_port_step_rate(wl, 1)
     if wl["B"] * wl["T"] / value < 45.0 and args.steps > 1:
@@ -225,8 +242,9 @@ def realize(wl, cfg, device):
         rec.realize(cfg, RecipeOptions(t_seq=T, t_batch=B, seed=42, init_std=wl["init_std"]))
         return rec, rec.fs_cache
     rec = LoRA(device=device)
-    lo = None if wl.get("per_head") else LoraOptions(rank=8, alpha=16.0, targets=wl["lora"])
-    rec.realize(cfg, 8, RecipeOptions(t_seq=T, t_batch=B, seed=42), lo)   # None: the recipe's per-head LoRA-Q
+    r = wl.get("rank", 8)
+    lo = None if wl.get("per_head") else LoraOptions(rank=r, alpha=2.0 * r, targets=wl["lora"])
+    rec.realize(cfg, r, RecipeOptions(t_seq=T, t_batch=B, seed=42), lo)   # None: the recipe's per-head LoRA-Q
     return rec, rec.lora_cache
 
 
@@ -379,7 +397,8 @@ def main():
     from toy_b200 import LlamaConfig
     from toy_b200._lib import lib
     lib().tb2_set_q8_ring_l2(args.q8_ring_l2)
-    cfg = LlamaConfig.smollm2_135m()
+    cfg = getattr(LlamaConfig, {"smollm2": "smollm2_135m"}.get(wl.get("model", "smollm2"),
+                                                               wl.get("model", "smollm2")))()
     if args.layers:
         cfg.n_layers = args.layers
     if args.batch:
@@ -392,7 +411,7 @@ def main():
         dp = DataParallel(rank, world, local)
     r = measure(wl, cfg, args, dp, rank, world, local)
     qlora = None
-    if not args.no_qlora and wl["mode"] == 0:
+    if not args.no_qlora and wl["mode"] == 0 and wl.get("model", "smollm2") == "smollm2":
         qwl = dict(WORKLOADS["smollm2_qlora_b8_t512"])
         if args.batch:
             qwl["B"] = args.batch
@@ -400,7 +419,7 @@ def main():
     burst, sustained, hbm, src = peaks()
     step_ms = r["step_ms"]
     gemm_tflops = r["gemm_flops"] / (r["gemm_ms"] * 1e-3) / 1e12 if r["gemm_ms"] > 0 else 0.0
-    f_tok = step_flops_per_token(cfg, T, wl["mode"], wl["lora"] or (), 8, wl.get("per_head", False))
+    f_tok = step_flops_per_token(cfg, T, wl["mode"], wl["lora"] or (), wl.get("rank", 8), wl.get("per_head", False))
     tokens = N * world
     value = tokens / (step_ms * 1e-3)
     step_tflops = f_tok * N / (step_ms * 1e-3) / 1e12
@@ -409,7 +428,8 @@ def main():
             dp.close()
         return
     cpu = None
-    if world == 1 and not args.no_cpu_baseline and not args.layers and not args.batch:
+    if world == 1 and not args.no_cpu_baseline and not args.layers and not args.batch and \
+            wl.get("model", "smollm2") == "smollm2":
         v, nsteps = cpu_port_step_rate(wl, 1)
         cpu = {"value": v, "unit": "tokens/s", "cores": cores(), "kind": "port", "sample": cpu_sample_text(wl, nsteps)}
     tot = sum(r["per_kind"].values())
@@ -419,11 +439,11 @@ def main():
         "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32 (tensor-core products on split-bf16 pairs, f32 accumulate)",
         "data": "synthetic (uniform ids, seeded init)",
-        "config": {"workload": args.workload, "model": "SmolLM2-135M shape", "global_batch": B * world,
+        "config": {"workload": args.workload, "model": MODEL_NAMES[wl.get("model", "smollm2")], "global_batch": B * world,
                    "seq_len": T, "parallelism": f"dp{world}", "tokens_per_step": tokens,
                    "init": "every weight N(0, 0.02) f32" if wl["mode"] == 0 else "Q8_0 base from N(0, 0.02)",
-                   "l2": "inputs larger than L2: working set (activations ~6 GB, weights+moments 2 GB) far "
-                         "exceeds the 126 MB L2",
+                   "l2": "inputs larger than L2: the step's working set (activations and weights, several GB) "
+                         "far exceeds the 126 MB L2",
                    **({"layers_override": cfg.n_layers} if args.layers else {})},
         "step_roofline": {"tflops_algorithmic": step_tflops, "peak_tflops": sustained,
                           "frac": step_tflops / sustained, "peak_source": f"bf16 sustained, {src}",

@@ -6,7 +6,9 @@ at reduced width / depth so the float64 oracle finishes in seconds:
   QLoRA rank 16 on all seven projections;
 * Qwen2.5-7B family: d_head 128 (the materialised attention path), q/k/v bias,
   RoPE base 1e6, RMSNorm eps 1e-6, QLoRA rank 16 on all seven projections, and
-  the same shape fully fine-tuned (bias gradients included).
+  the same shape fully fine-tuned (bias gradients included);
+* both at their full layer width (one layer, small vocabulary), where the
+  adapters' down passes run over column chunks.
 
 Same contract as the SmolLM2 tests: loss 1e-4 relative; gradients, post-AdamW
 parameters and moments 1e-3 relative L2; Q8_0 blocks bit-exact.
@@ -37,6 +39,25 @@ def qwen_family():
     return oc, gc
 
 
+def llama3_full_width():
+    """Llama-3.2-1B's full layer width (d 2048, 32 / 8 heads, d_ff 8192), one layer, a small vocabulary."""
+    from toy_b200 import LlamaConfig
+    ff = O.llama3_freq_factors(64, 5.0e5, 8192, 32.0, 1.0, 4.0)
+    oc = O.LlamaCfg(vocab=1024, d_model=2048, n_heads=32, n_kv=8, d_head=64, d_ff=8192, n_layers=1,
+                    rope_base=5.0e5, rope_freq_factors=ff)
+    gc = LlamaConfig(1024, 2048, 32, 8, 64, 8192, 1, 5.0e5, 1e-5, rope_freq_factors=list(ff))
+    return oc, gc
+
+
+def qwen_full_width():
+    """Qwen2.5-7B's full layer width (d 3584, 28 / 4 heads of 128, d_ff 18944), one layer, a small vocabulary."""
+    from toy_b200 import LlamaConfig
+    oc = O.LlamaCfg(vocab=1024, d_model=3584, n_heads=28, n_kv=4, d_head=128, d_ff=18944, n_layers=1,
+                    rope_base=1.0e6, rms_eps=1e-6, qkv_bias=True)
+    gc = LlamaConfig(1024, 3584, 28, 4, 128, 18944, 1, 1.0e6, 1e-6, qkv_bias=True)
+    return oc, gc
+
+
 ALL = ("q", "k", "v", "o", "gate", "up", "down")
 
 
@@ -57,6 +78,28 @@ def test_qlora_rank16_all_targets(cuda, family):
     for k, blocks in mdl.q8.items():
         assert np.array_equal(eng.q8_0_blocks(k).reshape(-1), blocks.reshape(-1)), k
     ids, pos, lab = inputs(oc, T, B, seed=8)
+    for step in (1, 2):
+        hp = O.hp_lora(1e-4, step, wd=0.01)
+        loss_g = rec.step(ids, pos, lab, hp, step == 1)
+        loss_r, grads = O.train_step(mdl, ids, pos, lab, T, B, hp, step == 1)
+        compare_step(eng, mdl, loss_g, loss_r, grads)
+
+
+@pytest.mark.parametrize("family", [llama3_full_width, qwen_full_width])
+def test_qlora_rank16_full_width(cuda, family):
+    """At the real layer widths the adapters' A (rank 16 x d_in, up to three per
+    group) no longer fit in shared memory: the adapter down passes run over
+    column chunks, summed in order. One layer, T = 64, one sequence."""
+    from toy_b200 import LoRA, LoraOptions, RecipeOptions
+    oc, gc = family()
+    T, B = 64, 1
+    rec = LoRA()
+    lo = LoraOptions(rank=16, alpha=32.0, targets=ALL, a_std=0.125, b_std=0.01, base_std=0.02)
+    rec.realize(gc, 16, RecipeOptions(t_seq=T, t_batch=B, seed=23), lo)
+    mdl = O.qlora_model(oc, O.LoraCfg(rank=16, alpha=32.0, targets=ALL, a_std=0.125, b_std=0.01), seed=23,
+                        base_std=0.02)
+    eng = rec.lora_cache
+    ids, pos, lab = inputs(oc, T, B, seed=9)
     for step in (1, 2):
         hp = O.hp_lora(1e-4, step, wd=0.01)
         loss_g = rec.step(ids, pos, lab, hp, step == 1)

@@ -439,14 +439,16 @@ __global__ void __launch_bounds__(256) lora_down_group_kernel(Planes X, long lon
 #pragma unroll
   for (int a = 0; a < NS; ++a) {
     const LoraSeg& sg = g.s[a];
-    const int n4 = r * sg.width / 4;
+    const int n4 = r * sg.width / 4, w4 = sg.width / 4, ld4 = (g.ldw ? g.ldw : sg.width) / 4;
     const float4* src = reinterpret_cast<const float4*>(sg.w);
     float4* dst = wsm4 + wofs[a] / 4;
     for (int i0 = threadIdx.x; i0 < n4; i0 += 4 * 256) {   // four loads in flight per thread
       float4 t[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
-        if (i0 + u * 256 < n4) t[u] = __ldg(src + i0 + u * 256);
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * 256;
+        if (i < n4) t[u] = __ldg(src + (long long)(i / w4) * ld4 + i % w4);
+      }
 #pragma unroll
       for (int u = 0; u < 4; ++u)
         if (i0 + u * 256 < n4) dst[i0 + u * 256] = t[u];
@@ -511,12 +513,16 @@ __global__ void __launch_bounds__(256) lora_down_group_kernel(Planes X, long lon
 #pragma unroll
     for (int a = 0; a < NS; ++a) {
       const LoraSeg& sg = g.s[a];
-      const float v0 = sg.alpha * warp_sum_multi<RT>(acc0[a], lane);
-      const float v1 = sg.alpha * warp_sum_multi<RT>(acc1[a], lane);
+      float v0 = sg.alpha * warp_sum_multi<RT>(acc0[a], lane);
+      float v1 = sg.alpha * warp_sum_multi<RT>(acc1[a], lane);
       if (lead) {
+        if (g.accumulate) {   // a later column chunk: add to the earlier chunks' sum
+          v0 += sg.out[(long long)n * r + j];
+          if (two) v1 += sg.out[(long long)(n + 1) * r + j];
+        }
         sg.out[(long long)n * r + j] = v0;
         if (two) sg.out[(long long)(n + 1) * r + j] = v1;
-        if (sg.ext_col >= 0) {
+        if (sg.ext_col >= 0 && g.write_ext) {
           const long long e0 = (long long)n * ldx + sg.ext_col + j;
           __nv_bfloat16 h, l;
           h = __float2bfloat16_rn(v0);
@@ -962,7 +968,43 @@ int launch_lora_down_group(Planes X, long long ldx, int N, int r, const LoraSegs
     shared = shared && sg.col_off == segs.s[0].col_off && sg.width == segs.s[0].width;
   }
   const size_t smem = wfloats * sizeof(float);
-  if (smem > 200 * 1024) return -1;
+  if (smem > 200 * 1024) {
+    // w of the whole set does not fit: column chunks of one width (a multiple
+    // of 4), each staged in shared memory, added in chunk order into out
+    int w_all = segs.s[0].width;
+    bool same = true;
+    for (int a = 1; a < segs.n; ++a) same = same && segs.s[a].width == w_all;
+    if (!same) {   // adapters of different widths: one set each
+      for (int a = 0; a < segs.n; ++a) {
+        LoraSegs one;
+        one.s[0] = segs.s[a];
+        one.n = 1;
+        if (const int rc = launch_lora_down_group(X, ldx, N, r, one, st)) return rc;
+      }
+      return 0;
+    }
+    const size_t per_col = (size_t)r * segs.n * sizeof(float);
+    int wc = (int)((200 * 1024) / per_col) / 4 * 4;
+    if (wc < 4) return -1;
+    for (int c0 = 0; c0 < w_all; c0 += wc) {
+      LoraSegs part = segs;
+      part.ldw = w_all;
+      part.accumulate = c0 > 0;
+      part.write_ext = c0 + wc >= w_all;
+      const int width = std::min(wc, w_all - c0);
+      for (int a = 0; a < segs.n; ++a) {
+        part.s[a].col_off = segs.s[a].col_off + c0;
+        part.s[a].width = width;
+        part.s[a].w = segs.s[a].w + c0;
+        if (c0 > 0) part.s[a].bt = nullptr;   // the B^T copy once
+      }
+      const size_t psmem = (size_t)r * segs.n * width * sizeof(float);
+      const int rc = r <= 8 ? down_group_ns<8>(X, ldx, N, r, part, shared, psmem, st)
+                            : down_group_ns<16>(X, ldx, N, r, part, shared, psmem, st);
+      if (rc) return -3;
+    }
+    return 0;
+  }
   // bulk-staged variant: 16-byte aligned rows, segments and w; its shared
   // memory holds w plus kDownRows rows of the staged segments
   bool bulk = ldx % 8 == 0 && (reinterpret_cast<uintptr_t>(X.hi) & 15) == 0 &&

@@ -59,8 +59,14 @@ struct LoraSeg {
 struct LoraSegs {
   LoraSeg s[kLoraMaxSegs];
   int n = 0;
+  // launch_lora_down_group internals for adapters whose w exceeds shared
+  // memory (the pass then runs over column chunks): w's row stride (0: width),
+  // add into out instead of storing, write the extra-column planes (last chunk)
+  int ldw = 0, accumulate = 0, write_ext = 1;
 };
-// Every adapter of the group in one launch (r <= 16; X planes [N][ldx]).
+// Every adapter of the group in one launch (r <= 16; X planes [N][ldx]); an
+// adapter set whose w does not fit in shared memory runs as several launches
+// over column chunks of the same width, summed in chunk order.
 int launch_lora_down_group(Planes X, long long ldx, int N, int r, const LoraSegs& segs, cudaStream_t st);
 
 // Weight gradients of a group: for adapter i, dB_i[c][j] = s sum_n
