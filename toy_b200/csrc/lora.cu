@@ -968,9 +968,13 @@ int launch_lora_down_group(Planes X, long long ldx, int N, int r, const LoraSegs
     shared = shared && sg.col_off == segs.s[0].col_off && sg.width == segs.s[0].width;
   }
   const size_t smem = wfloats * sizeof(float);
-  if (smem > 200 * 1024) {
-    // w of the whole set does not fit: column chunks of one width (a multiple
-    // of 4), each staged in shared memory, added in chunk order into out
+  // w of more than 100 KB (the wide layers of 1B+ models): column chunks of
+  // at most 48 KB of w, so that four blocks share an SM and hide the row
+  // loads' latency
+  constexpr size_t kChunkSmem = 48 * 1024;
+  if (smem > 100 * 1024) {
+    // w of the whole set in column chunks of one width (a multiple of 4), each
+    // staged in shared memory, added in chunk order into out
     int w_all = segs.s[0].width;
     bool same = true;
     for (int a = 1; a < segs.n; ++a) same = same && segs.s[a].width == w_all;
@@ -984,7 +988,7 @@ int launch_lora_down_group(Planes X, long long ldx, int N, int r, const LoraSegs
       return 0;
     }
     const size_t per_col = (size_t)r * segs.n * sizeof(float);
-    int wc = (int)((200 * 1024) / per_col) / 4 * 4;
+    int wc = (int)(kChunkSmem / per_col) / 4 * 4;
     if (wc < 4) return -1;
     for (int c0 = 0; c0 < w_all; c0 += wc) {
       LoraSegs part = segs;
