@@ -277,6 +277,14 @@ class LlamaEngine {
                     int ext_base);
   // backward, after it: dB and dA of every adapter (partials + fixed-order sum)
   int lora_group_wgrad(int l, const LoraGroup& G, Planes X, long long ldx, int d_in, Planes dY, long long ld_dy);
+  // the same on tensor cores, for groups whose input is at least kWgTcMinWidth wide
+  int lora_group_wgrad_tc(int l, const LoraGroup& G, Planes X, long long ldx, int d_in, Planes dY, long long ld_dy);
+  static constexpr int kWgTcMinWidth = 2048;
+  static constexpr int kWgTcCols = 64;   // columns of the packed u / du planes and of the DA / DB products
+  bool wg_tc_ = false;
+  Planes wg_ubp_{}, wg_dubp_{};
+  float* wg_da_ = nullptr;
+  float* wg_db_ = nullptr;
   bool lora_grouped(int d_in) const { return cfg_.lora_rank <= 16 && d_in % 32 == 0; }
   // Per-head LoRA-Q: the block-diagonal adapter rides the q|k|v GEMMs as extra
   // reduction columns (u = h A^T into h's, du = dY_q B into dY's); dA and dB

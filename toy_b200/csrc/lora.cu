@@ -235,6 +235,58 @@ __global__ void lora_transpose_kernel(const float* __restrict__ W, int C, int r,
   }
 }
 
+// Tensor-core weight gradients of a wide adapter group (lora.cuh): the group's
+// u (or du) vectors side by side as split planes, out[n][i r + j] = src_i[n][j],
+// zero in the columns past n_src r.
+__global__ void lora_pack_planes_kernel(LoraPackSrc src, int N, int r, int R, Planes out) {
+  griddep_wait();
+  const long long total = (long long)N * (R / 2);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long n = i / (R / 2);
+    const int c = (int)(i % (R / 2)) * 2;
+    float v[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int seg = (c + e) / r, j = (c + e) % r;
+      v[e] = seg < src.n ? src.p[seg][n * r + j] : 0.f;
+    }
+    uint32_t h, l;
+    split_pair(v[0], v[1], h, l);
+    *reinterpret_cast<uint32_t*>(out.hi + n * R + c) = h;
+    *reinterpret_cast<uint32_t*>(out.lo + n * R + c) = l;
+  }
+}
+
+// dA_i[j][k] = DA[k][i r + j] (DA = X^T [du_0 | du_1 | ..], [d_in][R]) and
+// dB_i[c][j] = s DB[o_i + c][i r + j] (DB = dY^T [u_0 | u_1 | ..] over the
+// group's contiguous output columns, [sum w][R]; only the diagonal blocks).
+__global__ void lora_wg_extract_kernel(const float* __restrict__ DA, const float* __restrict__ DB, int d_in, int r,
+                                       int R, float s, LoraWgGroup g) {
+  griddep_wait();
+  long long na = (long long)g.n * r * d_in, nb = 0;
+  for (int a = 0; a < g.n; ++a) nb += (long long)g.s[a].width * r;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < na + nb;
+       i += (long long)gridDim.x * blockDim.x) {
+    if (i < na) {
+      const int a = (int)(i / ((long long)r * d_in));
+      const long long t = i % ((long long)r * d_in);
+      const int j = (int)(t / d_in), k = (int)(t % d_in);
+      g.s[a].dA[t] = DA[(long long)k * R + a * r + j];
+    } else {
+      long long t = i - na;
+      int a = 0, off = 0;
+      while (t >= (long long)g.s[a].width * r) {
+        t -= (long long)g.s[a].width * r;
+        off += g.s[a].width;
+        ++a;
+      }
+      const int c = (int)(t / r), j = (int)(t % r);
+      g.s[a].dB[t] = s * DB[(long long)(off + c) * R + a * r + j];
+    }
+  }
+}
+
 // Adapter backward, row pass: one warp per token row (two rows in flight)
 //   du[n][j] = s sum_c dY[n][c] bt[j][c]     (saved for the weight gradients)
 //   dX(n, k) += sum_j du[n][j] A[j][k]        (epilogue addressing, as lora_up)
@@ -1119,6 +1171,29 @@ int launch_lora_wgrad_group(Planes dY, long long ldy, Planes X, long long ldx, i
   int rs_max = r;
   for (int f = 0; f < p.nf; ++f) rs_max = std::max(rs_max, p.f[f].n_src * r);
   return rs_max <= 8 ? wgrad2<8>(dY, ldy, X, ldx, N, p, part, st) : wgrad2<16>(dY, ldy, X, ldx, N, p, part, st);
+}
+
+int launch_lora_pack_planes(const LoraPackSrc& src, int N, int r, int R, Planes out, cudaStream_t st) {
+  if (src.n < 1 || src.n > kLoraMaxSegs || r < 1 || R % 2 || src.n * r > R || N <= 0 || !out.hi || !out.lo) return -1;
+  for (int a = 0; a < src.n; ++a)
+    if (!src.p[a]) return -1;
+  long long blocks = ((long long)N * (R / 2) + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  return launch_pdl(lora_pack_planes_kernel, dim3((unsigned)blocks), dim3(256), 0, st, src, N, r, R, out) ? -3 : 0;
+}
+
+int launch_lora_wg_extract(const float* DA, const float* DB, int d_in, int r, int R, float s, const LoraWgGroup& g,
+                           cudaStream_t st) {
+  if (!DA || !DB || g.n < 1 || g.n > kLoraMaxSegs || g.n * r > R || d_in <= 0) return -1;
+  long long total = (long long)g.n * r * d_in;
+  for (int a = 0; a < g.n; ++a) {
+    if (!g.s[a].dA || !g.s[a].dB || g.s[a].width <= 0) return -1;
+    total += (long long)g.s[a].width * r;
+  }
+  long long blocks = (total + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  return launch_pdl(lora_wg_extract_kernel, dim3((unsigned)blocks), dim3(256), 0, st, DA, DB, d_in, r, R, s, g) ? -3
+                                                                                                                 : 0;
 }
 
 int launch_lora_transpose(const float* W, int C, int r, float* Wt, cudaStream_t st) {

@@ -85,6 +85,21 @@ struct LoraWgGroup {
   int n = 0;
 };
 long long lora_group_partial_floats(int N, int r, int d_in, int total_width, int n_adapters);
+
+// The same weight gradients on tensor cores for wide groups (the GEMMs
+// DA = X^T [du_0 | ..] and DB = dY^T [u_0 | ..] run by the caller):
+// launch_lora_pack_planes lays the group's u or du vectors ([N][r] f32 each)
+// side by side as split planes [N][R] (zero past n r columns, R even);
+// launch_lora_wg_extract scatters DA [d_in][R] into every dA [r][d_in] and the
+// diagonal blocks of DB [sum of widths][R] (the group's output columns in
+// order) into every dB [width][r], times s.
+struct LoraPackSrc {
+  const float* p[kLoraMaxSegs] = {};
+  int n = 0;
+};
+int launch_lora_pack_planes(const LoraPackSrc& src, int N, int r, int R, Planes out, cudaStream_t st);
+int launch_lora_wg_extract(const float* DA, const float* DB, int d_in, int r, int R, float s, const LoraWgGroup& g,
+                           cudaStream_t st);
 int launch_lora_wgrad_group(Planes dY, long long ldy, Planes X, long long ldx, int d_in, int N, int r, float s,
                             const LoraWgGroup& g, float* part, cudaStream_t st);
 
