@@ -561,6 +561,8 @@ int LlamaEngine::realize() {
     wg_dubp_ = pl((long long)N * kWgTcCols);
     wg_da_ = f32((long long)std::max(std::max(d, H * dh), ff) * kWgTcCols);
     wg_db_ = f32((long long)std::max(std::max(W, 2 * ff), d) * kWgTcCols);
+    wg_u_ = f32((long long)N * kWgTcCols);
+    wg_wp_ = pl((long long)kWgTcCols * std::max(std::max(std::max(d, H * dh), ff), std::max(std::max(W, 2 * ff), d)));
   }
   hp_ = f32(8);
   bufs_.emplace_back();
@@ -1296,6 +1298,32 @@ int LlamaEngine::lora_group_prep(int l, const LoraGroup& G, Planes X, int d_in, 
     for (int i = 0; i < G.n; ++i) CK(lora_prep(l, G.t[i], X, d_in, G.w[i]));
     return 0;
   }
+  if (wg_tc_ && d_in >= kWgTcMinWidth && d_in % 8 == 0 && ldx % 8 == 0) {
+    // u = X A^T for the whole group as one tensor-core GEMM against the packed A's
+    LoraPackW pw;
+    LoraScatterU sc;
+    pw.r = sc.r = r;
+    sc.X = X;
+    sc.ldx = ldx;
+    for (int i = 0; i < G.n; ++i) {
+      const std::string pre = "blk." + std::to_string(l) + "." + kProjName[G.t[i]];
+      pw.p[pw.n] = P32(P(pre + ".lora_a"));
+      pw.koff[pw.n] = 0;
+      pw.w[pw.n++] = d_in;
+      sc.out[sc.n] = lora_u_[l][G.t[i]];
+      sc.ext_col[sc.n++] = ldx > d_in ? d_in + 16 * i : -1;
+      KL(launch_lora_transpose(P32(P(pre + ".lora_b")), G.w[i], r, lora_bt_[l][G.t[i]], stream_));
+    }
+    KL(launch_lora_pack_w(pw, kWgTcCols, d_in, wg_wp_, stream_));
+    GemmDesc g;
+    g.M = N; g.N = kWgTcCols; g.K = d_in;
+    g.a = op(X, N, d_in, ldx, 0);
+    g.b = op(wg_wp_, kWgTcCols, d_in, d_in, 0);
+    g.epi = epi_rowmajor(kEpiStoreF32, wg_u_, kWgTcCols);
+    CK(gemm(g));
+    KL(launch_lora_scatter_u(wg_u_, N, kWgTcCols, sc, stream_));
+    return 0;
+  }
   const LoraSegs segs = lora_group_segs(l, G, d_in, ldx > d_in ? d_in : -1);
   KL(launch_lora_down_group(X, ldx, N, r, segs, stream_));
   return 0;
@@ -1307,16 +1335,50 @@ int LlamaEngine::lora_group_du(int l, const LoraGroup& G, Planes dY, long long l
   const float s = cfg_.lora_alpha / (float)r;
   CK(flip(t_du_));
   du32_ = du2_[t_du_.cur];
-  LoraSegs segs;
+  int sw = 0;
+  bool contiguous = true;
   for (int i = 0; i < G.n; ++i) {
-    LoraSeg& sg = segs.s[segs.n++];
-    sg.col_off = G.c0[i]; sg.width = G.w[i];
-    sg.w = lora_bt_[l][G.t[i]];
-    sg.alpha = s;
-    sg.out = du32_ + (long long)i * N * r;
-    sg.ext_col = ext_base >= 0 ? ext_base + 16 * i : -1;
+    sw += G.w[i];
+    if (i) contiguous = contiguous && G.c0[i] == G.c0[i - 1] + G.w[i - 1];
   }
-  KL(launch_lora_down_group(dY, ld_dy, N, r, segs, stream_));
+  if (wg_tc_ && contiguous && sw >= kWgTcMinWidth && sw % 8 == 0 && G.c0[0] % 8 == 0 && ld_dy % 8 == 0) {
+    // du = s dY B for the whole group as one tensor-core GEMM against the
+    // block-diagonal packed B's (adapter i's rows only see its own columns)
+    LoraPackW pw;
+    LoraScatterU sc;
+    pw.r = sc.r = r;
+    pw.trans = 1;
+    sc.alpha = s;
+    sc.X = dY;
+    sc.ldx = ld_dy;
+    for (int i = 0; i < G.n; ++i) {
+      const std::string pre = "blk." + std::to_string(l) + "." + kProjName[G.t[i]];
+      pw.p[pw.n] = P32(P(pre + ".lora_b"));
+      pw.koff[pw.n] = G.c0[i] - G.c0[0];
+      pw.w[pw.n++] = G.w[i];
+      sc.out[sc.n] = du32_ + (long long)i * N * r;
+      sc.ext_col[sc.n++] = ext_base >= 0 ? ext_base + 16 * i : -1;
+    }
+    KL(launch_lora_pack_w(pw, kWgTcCols, sw, wg_wp_, stream_));
+    GemmDesc g;
+    g.M = N; g.N = kWgTcCols; g.K = sw;
+    g.a = op(Planes{dY.hi + G.c0[0], dY.lo + G.c0[0]}, N, sw, ld_dy, 0);
+    g.b = op(wg_wp_, kWgTcCols, sw, sw, 0);
+    g.epi = epi_rowmajor(kEpiStoreF32, wg_u_, kWgTcCols);
+    CK(gemm(g));
+    KL(launch_lora_scatter_u(wg_u_, N, kWgTcCols, sc, stream_));
+  } else {
+    LoraSegs segs;
+    for (int i = 0; i < G.n; ++i) {
+      LoraSeg& sg = segs.s[segs.n++];
+      sg.col_off = G.c0[i]; sg.width = G.w[i];
+      sg.w = lora_bt_[l][G.t[i]];
+      sg.alpha = s;
+      sg.out = du32_ + (long long)i * N * r;
+      sg.ext_col = ext_base >= 0 ? ext_base + 16 * i : -1;
+    }
+    KL(launch_lora_down_group(dY, ld_dy, N, r, segs, stream_));
+  }
   if (ext_base >= 0) return 0;   // the dX GEMM reads du from dY's extra columns
   for (int i = 0; i < G.n; ++i) {
     const std::string pre = "blk." + std::to_string(l) + "." + kProjName[G.t[i]];

@@ -285,6 +285,8 @@ class LlamaEngine {
   Planes wg_ubp_{}, wg_dubp_{};
   float* wg_da_ = nullptr;
   float* wg_db_ = nullptr;
+  float* wg_u_ = nullptr;    // [N][64]: u or du of a wide group before its scatter
+  Planes wg_wp_{};           // [64][K]: a wide group's packed A (or block-diagonal B) planes
   bool lora_grouped(int d_in) const { return cfg_.lora_rank <= 16 && d_in % 32 == 0; }
   // Per-head LoRA-Q: the block-diagonal adapter rides the q|k|v GEMMs as extra
   // reduction columns (u = h A^T into h's, du = dY_q B into dY's); dA and dB

@@ -258,6 +258,49 @@ __global__ void lora_pack_planes_kernel(LoraPackSrc src, int N, int r, int R, Pl
   }
 }
 
+// Packed adapter weights W [R][K] as split planes (lora.cuh launch_lora_pack_w).
+__global__ void lora_pack_w_kernel(LoraPackW src, int R, int K, Planes out) {
+  griddep_wait();
+  const long long total = (long long)R * (K / 2);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int row = (int)(i / (K / 2)), k0 = (int)(i % (K / 2)) * 2;
+    const int a = row / src.r, j = row % src.r;
+    float v[2] = {0.f, 0.f};
+    if (a < src.n) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int c = k0 + e - src.koff[a];
+        if (c >= 0 && c < src.w[a])
+          v[e] = src.trans ? src.p[a][(long long)c * src.r + j] : src.p[a][(long long)j * src.w[a] + c];
+      }
+    }
+    uint32_t h, l;
+    split_pair(v[0], v[1], h, l);
+    *reinterpret_cast<uint32_t*>(out.hi + (long long)row * K + k0) = h;
+    *reinterpret_cast<uint32_t*>(out.lo + (long long)row * K + k0) = l;
+  }
+}
+
+// u of each adapter from D [N][R] (lora.cuh launch_lora_scatter_u).
+__global__ void lora_scatter_u_kernel(const float* __restrict__ D, int N, int R, LoraScatterU dst) {
+  griddep_wait();
+  const long long total = (long long)N * dst.n * dst.r;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long n = i / (dst.n * dst.r);
+    const int c = (int)(i % (dst.n * dst.r)), a = c / dst.r, j = c % dst.r;
+    const float v = dst.alpha * D[n * R + c];
+    dst.out[a][n * dst.r + j] = v;
+    if (dst.ext_col[a] >= 0) {
+      const __nv_bfloat16 h = __float2bfloat16_rn(v);
+      const long long e = n * dst.ldx + dst.ext_col[a] + j;
+      dst.X.hi[e] = h;
+      dst.X.lo[e] = __float2bfloat16_rn(v - __bfloat162float(h));
+    }
+  }
+}
+
 // dA_i[j][k] = DA[k][i r + j] (DA = X^T [du_0 | du_1 | ..], [d_in][R]) and
 // dB_i[c][j] = s DB[o_i + c][i r + j] (DB = dY^T [u_0 | u_1 | ..] over the
 // group's contiguous output columns, [sum w][R]; only the diagonal blocks).
@@ -1180,6 +1223,25 @@ int launch_lora_pack_planes(const LoraPackSrc& src, int N, int r, int R, Planes 
   long long blocks = ((long long)N * (R / 2) + 255) / 256;
   if (blocks > 148 * 8) blocks = 148 * 8;
   return launch_pdl(lora_pack_planes_kernel, dim3((unsigned)blocks), dim3(256), 0, st, src, N, r, R, out) ? -3 : 0;
+}
+
+int launch_lora_pack_w(const LoraPackW& src, int R, int K, Planes out, cudaStream_t st) {
+  if (src.n < 1 || src.n > kLoraMaxSegs || src.r < 1 || src.n * src.r > R || K <= 0 || K % 2 || !out.hi || !out.lo)
+    return -1;
+  for (int a = 0; a < src.n; ++a)
+    if (!src.p[a] || src.w[a] <= 0 || src.koff[a] < 0 || src.koff[a] + src.w[a] > K) return -1;
+  long long blocks = ((long long)R * (K / 2) + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  return launch_pdl(lora_pack_w_kernel, dim3((unsigned)blocks), dim3(256), 0, st, src, R, K, out) ? -3 : 0;
+}
+
+int launch_lora_scatter_u(const float* D, int N, int R, const LoraScatterU& dst, cudaStream_t st) {
+  if (!D || N <= 0 || dst.n < 1 || dst.n > kLoraMaxSegs || dst.r < 1 || dst.n * dst.r > R) return -1;
+  for (int a = 0; a < dst.n; ++a)
+    if (!dst.out[a] || (dst.ext_col[a] >= 0 && (!dst.X.hi || !dst.X.lo || dst.ext_col[a] + dst.r > dst.ldx))) return -1;
+  long long blocks = ((long long)N * dst.n * dst.r + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  return launch_pdl(lora_scatter_u_kernel, dim3((unsigned)blocks), dim3(256), 0, st, D, N, R, dst) ? -3 : 0;
 }
 
 int launch_lora_wg_extract(const float* DA, const float* DB, int d_in, int r, int R, float s, const LoraWgGroup& g,

@@ -98,6 +98,30 @@ struct LoraPackSrc {
   int n = 0;
 };
 int launch_lora_pack_planes(const LoraPackSrc& src, int N, int r, int R, Planes out, cudaStream_t st);
+
+// Tensor-core down passes of a wide group (the caller runs D = X W^T with the
+// packed W): launch_lora_pack_w writes split planes W [R][K] whose rows
+// i r + j hold adapter i's row j over columns [koff_i, koff_i + w_i) -- from
+// A_i [r][w_i] (trans = 0) or from B_i [w_i][r] read transposed (trans = 1) --
+// and zero elsewhere; launch_lora_scatter_u writes out_i[n][j] =
+// alpha D[n][i r + j] ([N][r] each) and, with ext_col_i >= 0, the same values
+// as planes into X[n][ext_col_i + j].
+struct LoraPackW {
+  const float* p[kLoraMaxSegs] = {};
+  int koff[kLoraMaxSegs] = {}, w[kLoraMaxSegs] = {};
+  int n = 0, r = 0, trans = 0;
+};
+int launch_lora_pack_w(const LoraPackW& src, int R, int K, Planes out, cudaStream_t st);
+struct LoraScatterU {
+  float* out[kLoraMaxSegs] = {};
+  int ext_col[kLoraMaxSegs] = {-1, -1, -1};
+  int n = 0, r = 0;
+  float alpha = 1.f;
+  Planes X{};
+  long long ldx = 0;
+};
+int launch_lora_scatter_u(const float* D, int N, int R, const LoraScatterU& dst, cudaStream_t st);
+static_assert(kLoraMaxSegs == 3, "LoraScatterU::ext_col lists one initialiser per segment");
 int launch_lora_wg_extract(const float* DA, const float* DB, int d_in, int r, int R, float s, const LoraWgGroup& g,
                            cudaStream_t st);
 int launch_lora_wgrad_group(Planes dY, long long ldy, Planes X, long long ldx, int d_in, int N, int r, float s,
