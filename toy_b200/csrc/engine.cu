@@ -495,6 +495,7 @@ int LlamaEngine::realize() {
       M.gu = f32(NK * 2 * ff);
       M.a = pl(NK * ff);
       M.ye = f32(NK * d);
+      M.gtab = reinterpret_cast<int*>(f32(3 * (NK / 128 + E + 1)));
     }
     moe_logits_ = f32((long long)N * E);
     moe_xs_ = pl(NK * d);
@@ -1459,6 +1460,14 @@ int LlamaEngine::lora_group_wgrad_tc(int l, const LoraGroup& G, Planes X, long l
   return 0;
 }
 
+Operand LlamaEngine::experts_op(const Param& p, int rows, int cols, int mn) {
+  Operand o = expert_op(p, 0, rows, cols, mn);
+  o.nbatch = cfg_.n_experts;   // batch z = expert z of the stacked tensor
+  o.bdiv1 = 1;
+  o.bmul1 = 1;
+  return o;
+}
+
 Operand LlamaEngine::expert_op(const Param& p, int e, int rows, int cols, int mn) {
   // expert e of a stacked Q8_0 tensor: rows x cols quants (row-major) and their scales
   Operand o = op(Planes{}, rows, cols, cols, mn);
@@ -1504,33 +1513,40 @@ int LlamaEngine::moe_forward(int l) {
   }
   CU(cudaMemcpyAsync(M.perm, moe_hperm_.data(), NK * 4, cudaMemcpyHostToDevice, stream_));
   CU(cudaMemcpyAsync(M.pos, moe_hpos_.data(), NK * 4, cudaMemcpyHostToDevice, stream_));
+  // the experts' 128-slot M tiles for the grouped GEMMs (one launch per product for all experts)
+  M.htab.clear();
+  for (int e = 0; e < E; ++e)
+    for (int t0 = 0; t0 < M.count[e]; t0 += 128) {
+      M.htab.push_back(e);
+      M.htab.push_back(M.offset[e] + t0);
+      M.htab.push_back(M.offset[e] + std::min(M.count[e], t0 + 128));
+    }
+  M.ntiles = (int)(M.htab.size() / 3);
+  if (M.ntiles > NK / 128 + E + 1) return -3;
+  CU(cudaMemcpyAsync(M.gtab, M.htab.data(), M.htab.size() * 4, cudaMemcpyHostToDevice, stream_));
   KL(launch_moe_gather(h2_[l], d, M.perm, NK, K, d, moe_xs_, stream_));
   const Param& Wg = P(pre + "ffn_gate_exps.weight");
   const Param& Wu = P(pre + "ffn_up_exps.weight");
   const Param& Wd = P(pre + "ffn_down_exps.weight");
-  for (int e = 0; e < E; ++e) {
-    const int cnt = M.count[e];
-    if (!cnt) continue;
-    const long long off = M.offset[e];
-    for (int h = 0; h < 2; ++h) {   // gate into columns [0, ff), up into [ff, 2 ff)
-      GemmDesc g;
-      g.M = cnt; g.N = ff; g.K = d;
-      g.a = op(offset(moe_xs_, off * d), cnt, d, d, 0);
-      g.b = expert_op(h ? Wu : Wg, e, ff, d, 0);
-      g.epi = epi_rowmajor(kEpiStoreF32, M.gu + off * 2 * ff + h * ff, 2 * ff);
-      CK(gemm(g));
-    }
+  for (int h = 0; h < 2; ++h) {   // gate into columns [0, ff), up into [ff, 2 ff), every expert's slots at once
+    GemmDesc g;
+    g.M = (int)NK; g.N = ff; g.K = d;
+    g.a = op(moe_xs_, (int)NK, d, d, 0);
+    g.b = experts_op(h ? Wu : Wg, ff, d, 0);
+    g.epi = epi_rowmajor(kEpiStoreF32, M.gu + h * ff, 2 * ff);
+    g.group_tiles = M.gtab;
+    g.group_mtiles = M.ntiles;
+    CK(gemm(g));
   }
   KL(launch_swiglu_fwd(M.gu, M.a, (int)NK, ff, stream_, ff));
-  for (int e = 0; e < E; ++e) {
-    const int cnt = M.count[e];
-    if (!cnt) continue;
-    const long long off = M.offset[e];
+  {
     GemmDesc g;
-    g.M = cnt; g.N = d; g.K = ff;
-    g.a = op(offset(M.a, off * ff), cnt, ff, ff, 0);
-    g.b = expert_op(Wd, e, d, ff, 0);
-    g.epi = epi_rowmajor(kEpiStoreF32, M.ye + off * d, d);
+    g.M = (int)NK; g.N = d; g.K = ff;
+    g.a = op(M.a, (int)NK, ff, ff, 0);
+    g.b = experts_op(Wd, d, ff, 0);
+    g.epi = epi_rowmajor(kEpiStoreF32, M.ye, d);
+    g.group_tiles = M.gtab;
+    g.group_mtiles = M.ntiles;
     CK(gemm(g));
   }
   KL(launch_moe_combine(x1_[l], M.ye, M.pos, M.w, N, K, d, x_[l + 1], stream_));
@@ -1551,30 +1567,26 @@ int LlamaEngine::moe_backward(int l) {
   const Param& Wu = P(pre + "ffn_up_exps.weight");
   const Param& Wd = P(pre + "ffn_down_exps.weight");
   KL(launch_moe_dy(dx_, M.ye, M.perm, M.w, NK, K, d, moe_dw_, moe_dye_, stream_));
-  for (int e = 0; e < E; ++e) {
-    const int cnt = M.count[e];
-    if (!cnt) continue;
-    const long long off = M.offset[e];
-    GemmDesc g;
-    g.M = cnt; g.N = ff; g.K = d;
-    g.a = op(offset(moe_dye_, off * d), cnt, d, d, 0);
-    g.b = expert_op(Wd, e, d, ff, 1);
-    g.epi = epi_rowmajor(kEpiStoreF32, moe_das_ + off * ff, ff);
+  {
+    GemmDesc g;   // through every expert's down projection at once
+    g.M = (int)NK; g.N = ff; g.K = d;
+    g.a = op(moe_dye_, (int)NK, d, d, 0);
+    g.b = experts_op(Wd, d, ff, 1);
+    g.epi = epi_rowmajor(kEpiStoreF32, moe_das_, ff);
+    g.group_tiles = M.gtab;
+    g.group_mtiles = M.ntiles;
     CK(gemm(g));
   }
   KL(launch_swiglu_bwd(M.gu, moe_das_, moe_dgu_, (int)NK, ff, stream_, 2 * ff));
-  for (int e = 0; e < E; ++e) {
-    const int cnt = M.count[e];
-    if (!cnt) continue;
-    const long long off = M.offset[e];
-    for (int h = 0; h < 2; ++h) {   // dxs = dgate Wg_e + dup Wu_e
-      GemmDesc g;
-      g.M = cnt; g.N = d; g.K = ff;
-      g.a = op(offset(moe_dgu_, off * 2 * ff + h * ff), cnt, ff, 2 * ff, 0);
-      g.b = expert_op(h ? Wu : Wg, e, ff, d, 1);
-      g.epi = epi_rowmajor(h ? kEpiAccumF32 : kEpiStoreF32, moe_dxs_ + off * d, d);
-      CK(gemm(g));
-    }
+  for (int h = 0; h < 2; ++h) {   // dxs = dgate Wg_e + dup Wu_e
+    GemmDesc g;
+    g.M = (int)NK; g.N = d; g.K = ff;
+    g.a = op(offset(moe_dgu_, (long long)h * ff), (int)NK, ff, 2 * ff, 0);
+    g.b = experts_op(h ? Wu : Wg, ff, d, 1);
+    g.epi = epi_rowmajor(h ? kEpiAccumF32 : kEpiStoreF32, moe_dxs_, d);
+    g.group_tiles = M.gtab;
+    g.group_mtiles = M.ntiles;
+    CK(gemm(g));
   }
   KL(launch_moe_router_bwd(M.probs, M.idx, M.w, moe_dw_, N, E, K, c.norm_topk, moe_dlog_, stream_));
   GemmDesc gr;

@@ -303,6 +303,9 @@ class LlamaEngine {
   struct MoeLayer {
     float *probs = nullptr, *w = nullptr, *gu = nullptr, *ye = nullptr;
     int *idx = nullptr, *perm = nullptr, *pos = nullptr;
+    int* gtab = nullptr;            // the experts' M tiles (expert, first slot, end slot) for the grouped GEMMs
+    int ntiles = 0;
+    std::vector<int> htab;
     Planes a;
     std::vector<int> count, offset;
   };
@@ -314,6 +317,7 @@ class LlamaEngine {
   int moe_forward(int l);
   int moe_backward(int l);
   Operand expert_op(const Param& p, int e, int rows, int cols, int mn);
+  Operand experts_op(const Param& p, int rows, int cols, int mn);   // all experts, batch = expert
   Planes ring_ext_b(int l) const;   // B's extension block of block l's q|k|v ring operand
   float* P32(const Param& p) { return static_cast<float*>(p32_.p) + p.offset; }
   float* G32(const Param& p) { return static_cast<float*>(g_.p) + p.offset; }

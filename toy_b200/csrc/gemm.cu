@@ -62,6 +62,7 @@ struct KArgs {
   int tiles_m, tiles_n, splits, units, kb_total, causal;
   Epilogue epi;
   float* ws;
+  const int* gtab;   // grouped product: per M tile (group, first row, end row); null otherwise
   int b_keep;   // B is an operand kept resident in the L2: evict-last loads
   int* err;
   const uint16_t* q8_scale;   // Q8_0 B operand: scales and stored extent
@@ -98,7 +99,7 @@ struct Stages {
 };
 
 struct Unit {
-  int z, m0, n0, kb0, kb1, tile;
+  int z, m0, m1, n0, kb0, kb1, tile;   // m1: end of the rows this unit may write
   bool skip;
 };
 
@@ -112,8 +113,16 @@ __device__ __forceinline__ Unit decode(const KArgs& a, int u) {
   r.tile = t;
   r.n0 = (t % a.tiles_n) * BN;
   t /= a.tiles_n;
-  r.m0 = (t % a.tiles_m) * BMT;
-  r.z = t / a.tiles_m;
+  if (a.gtab) {   // grouped product: the M tile's group (its B batch) and row range
+    const int* g = a.gtab + 3 * (t % a.tiles_m);
+    r.z = g[0];
+    r.m0 = g[1];
+    r.m1 = g[2];
+  } else {
+    r.m0 = (t % a.tiles_m) * BMT;
+    r.z = t / a.tiles_m;
+    r.m1 = a.M;
+  }
   r.skip = a.causal == 1 && r.n0 > r.m0 + BM - 1;
   int kbt = a.kb_total;
   if (a.causal == 2) {
@@ -451,7 +460,7 @@ __global__ void __launch_bounds__(threads_of<BN, Q8, FUSED>(), 1)
       for (int u = walker; u < args.units && ok; u += walkers) {
         const Unit w = decode<BN, BMT>(args, u);
         if (w.skip) continue;
-        const int za = batch_index(w.z, args.a_bdiv1, args.a_bmul1, args.a_bdiv2, args.a_bmul2);
+        const int za = args.gtab ? 0 : batch_index(w.z, args.a_bdiv1, args.a_bmul1, args.a_bdiv2, args.a_bmul2);
         const int zb = batch_index(w.z, args.b_bdiv1, args.b_bmul1, args.b_bdiv2, args.b_bmul2);
         const int m0 = w.m0 + (int)rank * BM;   // this CTA's A rows
         const int nb = w.n0 + (int)rank * RB;   // this CTA's B rows (unpaired)
@@ -506,16 +515,16 @@ __global__ void __launch_bounds__(threads_of<BN, Q8, FUSED>(), 1)
             uint64_t* qb = &qfull[s];
             if (args.epi.pair_off) {
               if (PAIR) {
-                tma_load_3d(qd, &map_b_hi, qb, k0, pr, 0);
+                tma_load_3d(qd, &map_b_hi, qb, k0, pr, zb);
               } else {   // gate rows, then the matching up rows
-                tma_load_3d(qd, &map_b_hi, qb, k0, w.n0 / 2, 0);
-                tma_load_3d(qd + (BN / 2) * 64, &map_b_hi, qb, k0, args.epi.pair_off + w.n0 / 2, 0);
+                tma_load_3d(qd, &map_b_hi, qb, k0, w.n0 / 2, zb);
+                tma_load_3d(qd + (BN / 2) * 64, &map_b_hi, qb, k0, args.epi.pair_off + w.n0 / 2, zb);
               }
             } else if (!args.b_mn) {
-              tma_load_3d(qd, &map_b_hi, qb, k0, nb, 0);
+              tma_load_3d(qd, &map_b_hi, qb, k0, nb, zb);
             } else {
 #pragma unroll
-              for (int j = 0; j < RB / 64; ++j) tma_load_3d(qd + j * 64 * 64, &map_b_hi, qb, nb + 64 * j, k0, 0);
+              for (int j = 0; j < RB / 64; ++j) tma_load_3d(qd + j * 64 * 64, &map_b_hi, qb, nb + 64 * j, k0, zb);
             }
           } else if (args.epi.pair_off) {
             if (PAIR) {
@@ -643,6 +652,7 @@ __global__ void __launch_bounds__(threads_of<BN, Q8, FUSED>(), 1)
         const Unit w = decode<BN, BMT>(args, u);
         if (w.skip) continue;
         const int nb = w.n0 + (int)rank * RB;
+        const int zq = batch_index(w.z, args.b_bdiv1, args.b_bmul1, args.b_bdiv2, args.b_bmul2);   // B batch
         // this item's scale for k-block kb (a global load, issued ahead of
         // the stage wait so its latency overlaps the wait and the conversion)
         auto scale_of = [&](int kb) -> float {
@@ -658,7 +668,7 @@ __global__ void __launch_bounds__(threads_of<BN, Q8, FUSED>(), 1)
             sb = ((nb + 64 * tj) >> 5) + c32;
           }
           return (has_item && srow < args.q8_rows && sb < sblk)
-                     ? __half2float(__ushort_as_half(args.q8_scale[(long long)srow * sblk + sb]))
+                     ? __half2float(__ushort_as_half(args.q8_scale[((long long)zq * args.q8_rows + srow) * sblk + sb]))
                      : 0.f;
         };
         float sc_next = scale_of(w.kb0);
@@ -728,7 +738,7 @@ __global__ void __launch_bounds__(threads_of<BN, Q8, FUSED>(), 1)
       const uint32_t b = local & 1, tph = (local >> 1) & 1;
       ++local;
       const int m = w.m0 + (int)rank * BM + row;
-      const bool row_in = m < args.M;
+      const bool row_in = m < w.m1;
       const bool direct = args.splits == 1;
       // output offset of this row (without the column part); the residual /
       // accumulate addend of the first chunk is loaded before the accumulator
@@ -899,8 +909,8 @@ int make_q8_map(CUtensorMap* map, const Operand& o, int box_rows) {
   auto fn = encode_fn();
   if (!fn) return -10;
   if (reinterpret_cast<uintptr_t>(o.q8) % 16 != 0 || o.ld % 16 != 0) return -11;
-  cuuint64_t dims[3] = {(cuuint64_t)o.cols, (cuuint64_t)o.rows, 1};
-  cuuint64_t strides[2] = {(cuuint64_t)o.ld, (cuuint64_t)o.ld * o.rows};
+  cuuint64_t dims[3] = {(cuuint64_t)o.cols, (cuuint64_t)o.rows, (cuuint64_t)(o.nbatch > 0 ? o.nbatch : 1)};
+  cuuint64_t strides[2] = {(cuuint64_t)o.ld, (cuuint64_t)o.ld * o.rows};   // batches (experts) back to back
   cuuint32_t box[3] = {64u, (cuuint32_t)box_rows, 1u};
   cuuint32_t estr[3] = {1u, 1u, 1u};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(o.q8), dims, strides, box, estr,
@@ -1003,8 +1013,9 @@ Plan choose_plan(const GemmDesc& d, long long ws_floats, bool q8) {
   // fused epilogues act on whole output rows of a tile: no K splits
   const bool fused = d.epi.mode == kEpiRopeQKV || d.epi.mode == kEpiSwiGLU || d.epi.n_lora > 0;
   // the logsumexp epilogue reduces whole tile rows: no K splits either
-  const bool can_split = !d.causal && d.batch == 1 && ws_floats > 0 && !fused && d.epi.mode != kEpiStoreLse;
-  const bool pair_ok = g_pair_mode != 0 && d.split && !d.causal && (g_pair_mode == 1 || pair_wins(d));
+  const bool can_split =
+      !d.causal && d.batch == 1 && ws_floats > 0 && !fused && d.epi.mode != kEpiStoreLse && !d.group_tiles;
+  const bool pair_ok = g_pair_mode != 0 && d.split && !d.causal && !d.group_tiles && (g_pair_mode == 1 || pair_wins(d));
   Plan best;
   double best_t = 1e30;
   auto search = [&](int force_bn) {
@@ -1024,7 +1035,7 @@ Plan choose_plan(const GemmDesc& d, long long ws_floats, bool q8) {
       // tile's 8 epilogue warps would split a group between two warps
       if (d.epi.mode == kEpiStoreLse && bn == 192) continue;
       int s_lo = 1, s_hi = 1;
-      if (d.splits > 0 && !fused && d.epi.mode != kEpiStoreLse) {
+      if (d.splits > 0 && !fused && d.epi.mode != kEpiStoreLse && !d.group_tiles) {
         s_lo = s_hi = d.splits;
       } else if (can_split && kb >= 8) {
         s_hi = std::min(16, kb / 2);
@@ -1103,12 +1114,13 @@ int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream
   k.a_mn = d.a.mn_major; k.b_mn = d.b.mn_major;
   k.a_bdiv1 = d.a.bdiv1; k.a_bmul1 = d.a.bmul1; k.a_bdiv2 = d.a.bdiv2; k.a_bmul2 = d.a.bmul2;
   k.b_bdiv1 = d.b.bdiv1; k.b_bmul1 = d.b.bmul1; k.b_bdiv2 = d.b.bdiv2; k.b_bmul2 = d.b.bmul2;
-  k.tiles_m = (d.M + (PAIR ? 2 : 1) * BM - 1) / ((PAIR ? 2 : 1) * BM);
+  k.tiles_m = d.group_tiles ? d.group_mtiles : (d.M + (PAIR ? 2 : 1) * BM - 1) / ((PAIR ? 2 : 1) * BM);
+  k.gtab = d.group_tiles;
   k.tiles_n = (d.N + BN - 1) / BN;
   k.kb_total = (d.K + BK - 1) / BK;
   k.causal = d.causal;
   const long long tiles = (long long)d.batch * k.tiles_m * k.tiles_n;
-  if (splits < 1 || d.epi.mode == kEpiStoreLse) splits = 1;
+  if (splits < 1 || d.epi.mode == kEpiStoreLse || d.group_tiles) splits = 1;
   if (splits > k.kb_total) splits = k.kb_total;
   if (splits > 1 && (d.causal || d.batch != 1 || !sc.ws || (long long)splits * d.M * d.N > sc.ws_floats))
     splits = 1;
@@ -1175,6 +1187,8 @@ int gemm_effective_splits(const GemmDesc& d, int ksplits) {
 int gemm_launch(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream_t stream) {
   if (d.M <= 0 || d.N <= 0 || d.K <= 0 || d.batch <= 0) return -1;
   if (d.causal < 0 || d.causal > 2) return -1;
+  if (d.group_tiles && (d.group_mtiles < 1 || d.causal || d.batch != 1 || d.a.mn_major)) return -1;
+  if (!d.group_tiles && d.group_mtiles) return -1;
   // Epilogue vector stores need 16-byte aligned rows.
   const Epilogue& e = d.epi;
   const int al = (e.mode == kEpiStoreSplit || e.mode == kEpiStoreBoth) ? 8 : 4;

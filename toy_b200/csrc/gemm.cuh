@@ -123,6 +123,13 @@ struct GemmDesc {
   int max_ctas = 0; // persistent CTAs at most (0: one per SM); the units are the same, walked by fewer CTAs
   int tile_bn = 0;  // output tile width for this GEMM (0: the launch plan's choice; else as gemm_set_tile_width)
   int alone = 0;    // 1: nothing heavy runs beside it -- plan for a GEMM that has the GPU to itself
+  // Grouped product (the experts of a mixture-of-experts block): group_mtiles
+  // M tiles listed in device memory as triples (group, first row, end row),
+  // rows of at most 128 per tile; a tile's rows read A (unbatched, rows of the
+  // whole product) and batch `group` of B, and write only rows below its end.
+  // M is the total row count; no K splits, no CTA pairs, batch 1.
+  const int* group_tiles = nullptr;
+  int group_mtiles = 0;
   Operand a, b;
   Epilogue epi;
 };
