@@ -471,6 +471,19 @@ void *tnn_view_3d(void *sess, void *a, int ne0, int ne1, int ne2, long nb1, long
 void *tnn_concat(void *sess, void *a, void *b, int dim);
 void *tnn_get_rows(void *sess, void *table, void *idx);
 void *tnn_get_rows_back(void *sess, void *d_out, void *idx, void *table_shape);
+/* MoE primitives (tinynn_ggml.h:161-175, ggml semantics; forward only, as the
+ * reference's graphs use them). tnn_mul_mat_id: as [d_in, d_out, n_experts]
+ * (f32 or Q8_0), b [d_in, 1 or n_used, T] f32, ids i32 [n_used, T] ->
+ * [d_out, n_used, T], one product with expert ids[u, t] per (u, t); an id
+ * outside [0, n_experts) gives zeros. tnn_add_id: a [n0, n1, n2] + b[:, ids]
+ * with ids i32 [n1, n2]. tnn_argsort: i32 indices that sort each row of a
+ * (descending != 0: largest first), equal values by index; tnn_top_k: the
+ * indices of each row's k largest values, largest first. NULL on a shape or
+ * type mismatch. */
+void *tnn_mul_mat_id(void *sess, void *as, void *b, void *ids);
+void *tnn_add_id(void *sess, void *a, void *b, void *ids);
+void *tnn_argsort(void *sess, void *a, int descending);
+void *tnn_top_k(void *sess, void *a, int k);
 void *tnn_cross_entropy_loss(void *sess, void *a, void *b);
 void *tnn_sum(void *sess, void *a);
 void *tnn_sum_rows(void *sess, void *a);

@@ -511,3 +511,46 @@ def test_scratch_mmap_and_transposed_upload(cuda):
     assert rel(g.get(tt), np.float32(M).T) == 0
     assert L.tnn_pin_all_graph_b_nodes(s) == 0
     g.close()
+
+
+def test_moe_primitives(cuda):
+    """tnn_mul_mat_id (f32 and Q8_0 experts, shared and per-slot inputs),
+    tnn_add_id, tnn_argsort and tnn_top_k against numpy, ggml semantics
+    (tinynn_ggml.h:161-175)."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(11)
+    E, d_in, d_out, nu, T = 4, 64, 48, 2, 5
+    W = 0.1 * rng.standard_normal((E, d_out, d_in))
+    X = rng.standard_normal((T, 1, d_in))
+    Xu = rng.standard_normal((T, nu, d_in))
+    ids = rng.integers(0, E, size=(T, nu))
+    bias = rng.standard_normal((E, d_out))
+    g = Graph()
+    L, s = g.L, g.s
+    tid = L.tnn_reshape_2d(s, g.i32(ids.reshape(-1)), nu, T)
+    wf = g.f32(W)
+    y = L.tnn_mul_mat_id(s, wf, g.f32(X), tid)
+    yu = L.tnn_mul_mat_id(s, wf, g.f32(Xu), tid)
+    # Q8_0 experts: the blocks of every expert row, dequantised for the reference
+    blocks = O.q8_0_quantize(W.reshape(E * d_out, d_in).astype(np.float32))
+    wq = L.tnn_input_3d_persistent_typed(s, d_in, d_out, E, 8)
+    assert wq and L.tnn_upload_q8_0_blocks(s, wq, blocks.ctypes.data, blocks.nbytes) == 0
+    Wd = O.q8_0_dequantize(blocks, d_in).reshape(E, d_out, d_in)
+    yq = L.tnn_mul_mat_id(s, wq, g.f32(X), tid)
+    ya = L.tnn_add_id(s, yu, g.f32(bias), tid)
+    v = np.array([[3.0, 1.0, 2.0, 1.0, 5.0, 0.0, 2.0], [1.0, 1.0, 1.0, 0.5, 4.0, 4.0, -1.0]])
+    tv = g.f32(v)
+    asc, desc, top = L.tnn_argsort(s, tv, 0), L.tnn_argsort(s, tv, 1), L.tnn_top_k(s, tv, 3)
+    r_y, r_yu, r_yq, r_ya, r_asc, r_desc, r_top = g.run([y, yu, yq, ya, asc, desc, top])
+    ref = np.stack([np.stack([W[ids[t, u]] @ X[t, 0] for u in range(nu)]) for t in range(T)])
+    refu = np.stack([np.stack([W[ids[t, u]] @ Xu[t, u] for u in range(nu)]) for t in range(T)])
+    refq = np.stack([np.stack([Wd[ids[t, u]] @ X[t, 0] for u in range(nu)]) for t in range(T)])
+    assert rel(r_y, ref) < 1e-6 and rel(r_yu, refu) < 1e-6 and rel(r_yq, refq) < 1e-6
+    assert rel(r_ya, refu + bias[ids]) < 1e-6
+    stable = lambda row, sign: sorted(range(len(row)), key=lambda i: (sign * row[i], i))
+    assert np.array_equal(r_asc, [stable(r, 1) for r in v])
+    assert np.array_equal(r_desc, [stable(r, -1) for r in v])
+    assert np.array_equal(r_top, [stable(r, -1)[:3] for r in v])
+    assert L.tnn_mul_mat_id(s, wf, g.f32(rng.standard_normal((T, 3, d_in))), tid) is None   # n_used mismatch
+    assert L.tnn_top_k(s, tv, 8) is None
+    g.close()

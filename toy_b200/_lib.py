@@ -157,6 +157,10 @@ _SIGS = [
     ("tnn_concat", VP, [VP, VP, VP, I]),
     ("tnn_get_rows", VP, [VP, VP, VP]),
     ("tnn_get_rows_back", VP, [VP, VP, VP, VP]),
+    ("tnn_mul_mat_id", VP, [VP, VP, VP, VP]),
+    ("tnn_add_id", VP, [VP, VP, VP, VP]),
+    ("tnn_argsort", VP, [VP, VP, C.c_int]),
+    ("tnn_top_k", VP, [VP, VP, C.c_int]),
     ("tnn_cross_entropy_loss", VP, [VP, VP, VP]),
     ("tnn_sum", VP, [VP, VP]),
     ("tnn_sum_rows", VP, [VP, VP]),

@@ -202,6 +202,22 @@ void* tnn_get_rows(void* sess, void* table, void* idx) {
   Session* s = graph_session(sess);
   return s && mine(s, table) && mine(s, idx) ? tb2::prim_get_rows(s, T(table), T(idx)) : nullptr;
 }
+void* tnn_mul_mat_id(void* sess, void* as, void* b, void* ids) {
+  Session* s = graph_session(sess);
+  return s && mine(s, as) && mine(s, b) && mine(s, ids) ? tb2::prim_mul_mat_id(s, T(as), T(b), T(ids)) : nullptr;
+}
+void* tnn_add_id(void* sess, void* a, void* b, void* ids) {
+  Session* s = graph_session(sess);
+  return s && mine(s, a) && mine(s, b) && mine(s, ids) ? tb2::prim_add_id(s, T(a), T(b), T(ids)) : nullptr;
+}
+void* tnn_argsort(void* sess, void* a, int descending) {
+  Session* s = graph_session(sess);
+  return s && mine(s, a) ? tb2::prim_argsort(s, T(a), descending, 0) : nullptr;
+}
+void* tnn_top_k(void* sess, void* a, int k) {
+  Session* s = graph_session(sess);
+  return s && mine(s, a) && k > 0 ? tb2::prim_argsort(s, T(a), 1, k) : nullptr;
+}
 void* tnn_get_rows_back(void* sess, void* d_out, void* idx, void* table_shape) {
   Session* s = graph_session(sess);
   if (!s || !mine(s, d_out) || !mine(s, idx) || !mine(s, table_shape)) return nullptr;

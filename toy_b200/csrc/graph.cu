@@ -370,6 +370,67 @@ __global__ void k_get_rows(const float* __restrict__ table, const int* __restric
   }
 }
 
+// ggml_mul_mat_id: o[t][u][r] = sum_k W[e][r][k] x[t][u or 0][k], e = ids[t][u]
+// (W [E][d_out][d_in] f32, or Q8_0 quants and fp16 scales); one warp per
+// output element, lanes along k, an expert index outside [0, E) gives 0.
+__global__ void k_mul_mat_id(const float* __restrict__ w32, const int8_t* __restrict__ wq,
+                             const uint16_t* __restrict__ ws, const float* __restrict__ x, const int* __restrict__ ids,
+                             float* __restrict__ o, int d_in, int d_out, int E, int n_used, int nx1, long long nout) {
+  griddep_wait();
+  const int lane = threadIdx.x & 31;
+  for (long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) / 32; w < nout;
+       w += (long long)gridDim.x * blockDim.x / 32) {
+    const long long slot = w / d_out;   // t * n_used + u
+    const int r = (int)(w % d_out), u = (int)(slot % n_used);
+    const long long t = slot / n_used;
+    const int e = ids[slot];
+    float acc = 0.f;
+    if (e >= 0 && e < E) {
+      const float* xr = x + (t * nx1 + (nx1 == 1 ? 0 : u)) * d_in;
+      const long long row = (long long)e * d_out + r;
+      for (int k = lane; k < d_in; k += 32) {
+        const float wv = w32 ? w32[row * d_in + k]
+                             : __half2float(__ushort_as_half(ws[row * (d_in / 32) + k / 32])) * (float)wq[row * d_in + k];
+        acc = fmaf(wv, xr[k], acc);
+      }
+    }
+#pragma unroll
+    for (int m = 16; m; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
+    if (lane == 0) o[w] = acc;
+  }
+}
+
+// ggml_add_id: o[i2][i1][i0] = a[i2][i1][i0] + b[ids[i2][i1]][i0]
+__global__ void k_add_id(const float* __restrict__ a, const float* __restrict__ b, const int* __restrict__ ids,
+                         float* __restrict__ o, int ne0, int nb_rows, long long n) {
+  griddep_wait();
+  GRID_LOOP(i, n) {
+    int id = ids[i / ne0];
+    id = id < 0 ? 0 : (id >= nb_rows ? nb_rows - 1 : id);
+    o[i] = a[i] + b[(long long)id * ne0 + i % ne0];
+  }
+}
+
+// ggml_argsort / ggml_top_k over each row of ne0 values: o[row][rank] = i for
+// the rank of element i (ascending, or descending), ties by the lower index
+// first; top_k keeps the k leading ranks of a descending sort. One block per row.
+__global__ void k_argsort(const float* __restrict__ a, int* __restrict__ o, int ne0, long long rows, int desc,
+                          int keep) {
+  griddep_wait();
+  for (long long row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float* v = a + row * ne0;
+    for (int i = threadIdx.x; i < ne0; i += blockDim.x) {
+      const float vi = v[i];
+      int rank = 0;
+      for (int j = 0; j < ne0; ++j) {
+        const float vj = v[j];
+        rank += (desc ? vj > vi : vj < vi) || (vj == vi && j < i);
+      }
+      if (rank < keep) o[row * keep + rank] = i;
+    }
+  }
+}
+
 __global__ void k_get_rows_back(const float* __restrict__ g, const int* __restrict__ idx, float* __restrict__ o,
                                 int ne0, int nrows_table, long long n) {
   griddep_wait();
@@ -878,6 +939,39 @@ Tensor* prim_slice(Session* s, Tensor* a, int dim, int start, int len) {
   return t;
 }
 
+// ggml_mul_mat_id: as [d_in][d_out][E] (ne order; f32 or Q8_0), b [d_in][1 or
+// n_used][T] f32, ids [n_used][T] i32 -> [d_out][n_used][T]. No backward (as in
+// the reference, whose MoE graphs do not differentiate through it).
+Tensor* prim_mul_mat_id(Session* s, Tensor* as, Tensor* b, Tensor* ids) {
+  if (!as || !b || !ids || ids->type != 26 || !is_f32(b) || (as->type != 0 && as->type != 8)) return nullptr;
+  const int d_in = as->ne[0], d_out = as->ne[1], n_used = ids->ne[0], T = ids->ne[1];
+  if (as->ne[3] != 1 || ids->ne[2] != 1 || ids->ne[3] != 1 || b->ne[0] != d_in || b->ne[2] != T || b->ne[3] != 1 ||
+      (b->ne[1] != 1 && b->ne[1] != n_used) || (as->type == 8 && d_in % 32))
+    return nullptr;
+  Tensor* t = prim_new(s, 0, d_out, n_used, T, 1, kOpMulMatId, false);
+  if (t) { t->src[0] = as; t->src[1] = b; t->src[2] = ids; }
+  return t;
+}
+
+// ggml_add_id: a [n0][n1][n2] f32, b [n0][rows] f32, ids [n1][n2] i32 -> a + b[ids]
+Tensor* prim_add_id(Session* s, Tensor* a, Tensor* b, Tensor* ids) {
+  if (!is_f32(a) || !is_f32(b) || !ids || ids->type != 26 || b->ne[0] != a->ne[0] || ids->ne[0] != a->ne[1] ||
+      ids->ne[1] != a->ne[2] || a->ne[3] != 1 || b->ne[2] != 1 || b->ne[3] != 1)
+    return nullptr;
+  Tensor* t = prim_new(s, 0, a->ne[0], a->ne[1], a->ne[2], 1, kOpAddId, false);
+  if (t) { t->src[0] = a; t->src[1] = b; t->src[2] = ids; }
+  return t;
+}
+
+// ggml_argsort (k = 0: every index, ascending or descending) and ggml_top_k
+// (k > 0: the indices of the k largest, largest first): i32 [k or ne0][rows]
+Tensor* prim_argsort(Session* s, Tensor* a, int descending, int k) {
+  if (!is_f32(a) || k < 0 || k > a->ne[0]) return nullptr;
+  Tensor* t = prim_new(s, 26, k ? k : a->ne[0], a->ne[1], a->ne[2], a->ne[3], k ? kOpTopK : kOpArgsort, false);
+  if (t) { t->src[0] = a; t->ip[0] = k ? 1 : (descending ? 1 : 0); }
+  return t;
+}
+
 Tensor* prim_get_rows(Session* s, Tensor* table, Tensor* idx) {
   if (!is_f32(table) || !idx || idx->type != 26) return nullptr;
   Tensor* t = prim_new(s, 0, table->ne[0], (int)idx->nel(), 1, 1, kOpGetRows, false);
@@ -1115,6 +1209,26 @@ int exec(Session* s, Tensor* t) {
     case kOpSlice:
       return launch_pdl(k_slice, dim3(grid_for(n, threads)), dim3(threads), 0, st, F(a), F(t), shape(a), shape(t),
                         t->ip[0], t->ip[1], n);
+    case kOpMulMatId: {
+      Tensor* ids = t->src[2];
+      const long long nout = t->nel();
+      long long blocks = (nout * 32 + 255) / 256;
+      if (blocks > 148 * 16) blocks = 148 * 16;
+      const bool q8 = a->type == 8;
+      return launch_pdl(k_mul_mat_id, dim3((unsigned)blocks), dim3(256), 0, st, q8 ? (const float*)nullptr : F(a),
+                        q8 ? static_cast<const int8_t*>(a->q8v) : (const int8_t*)nullptr,
+                        q8 ? static_cast<const uint16_t*>(a->q8s) : (const uint16_t*)nullptr, (const float*)F(b),
+                        (const int*)I(ids), F(t), a->ne[0], a->ne[1], a->ne[2], ids->ne[0], b->ne[1], nout);
+    }
+    case kOpAddId:
+      return launch_pdl(k_add_id, dim3(grid_for(n, threads)), dim3(threads), 0, st, (const float*)F(a),
+                        (const float*)F(b), (const int*)I(t->src[2]), F(t), t->ne[0], (int)b->rows(), n);
+    case kOpArgsort: case kOpTopK: {
+      const long long rows = a->rows();
+      const unsigned blocks = (unsigned)std::min<long long>(rows, 148 * 8);
+      return launch_pdl(k_argsort, dim3(blocks), dim3(128), 0, st, (const float*)F(a), static_cast<int*>(t->data), a->ne[0], rows,
+                        t->ip[0], t->ne[0]);
+    }
     case kOpGetRows:
       return launch_pdl(k_get_rows, dim3(grid_for(n, threads)), dim3(threads), 0, st, F(a), I(b), F(t), t->ne[0],
                         (int)a->rows(), n);

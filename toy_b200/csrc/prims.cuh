@@ -9,7 +9,8 @@ enum PrimOp : int {
   kOpNone = 0, kOpAdd, kOpSub, kOpMul, kOpScale, kOpSilu, kOpSiluBack, kOpSwiglu, kOpMulMat, kOpOutProd, kOpMulMatAT,
   kOpRmsNorm, kOpRmsNormBack, kOpRope, kOpRopeBack, kOpSoftMax, kOpSoftMaxBack, kOpDiagMaskInf, kOpDiagMaskZero,
   kOpTranspose, kOpCont, kOpReshape, kOpView, kOpConcat, kOpSlice, kOpGetRows, kOpGetRowsBack, kOpCrossEntropy,
-  kOpCrossEntropyBack, kOpSum, kOpSumRows, kOpRepeat, kOpRepeatBack, kOpOptAdamw, kOpAccView, kOpDequant, kOpOptSgd, kOpCount
+  kOpCrossEntropyBack, kOpSum, kOpSumRows, kOpRepeat, kOpRepeatBack, kOpOptAdamw, kOpAccView, kOpDequant, kOpOptSgd,
+  kOpMulMatId, kOpAddId, kOpArgsort, kOpTopK, kOpCount
 };
 const char* prim_op_name(int op);
 
@@ -41,6 +42,9 @@ Tensor* prim_cont(Session* s, Tensor* a, int ne0, int ne1, int ne2, int ne3);
 Tensor* prim_view(Session* s, Tensor* a, int ne0, int ne1, int ne2, size_t nb1, size_t nb2, size_t offset);
 Tensor* prim_concat(Session* s, Tensor* a, Tensor* b, int dim);
 Tensor* prim_get_rows(Session* s, Tensor* table, Tensor* idx);
+Tensor* prim_mul_mat_id(Session* s, Tensor* as, Tensor* b, Tensor* ids);   // ggml_mul_mat_id (forward)
+Tensor* prim_add_id(Session* s, Tensor* a, Tensor* b, Tensor* ids);        // ggml_add_id (forward)
+Tensor* prim_argsort(Session* s, Tensor* a, int descending, int k);        // k = 0: argsort; k > 0: top_k
 Tensor* prim_get_rows_back(Session* s, Tensor* g, Tensor* idx, Tensor* like);
 Tensor* prim_cross_entropy(Session* s, Tensor* a, Tensor* b);
 Tensor* prim_sum(Session* s, int op, Tensor* a);                        // kOpSum / kOpSumRows
