@@ -481,6 +481,23 @@ void *tnn_get_rows_back(void *sess, void *d_out, void *idx, void *table_shape);
  * indices of each row's k largest values, largest first. NULL on a shape or
  * type mismatch. */
 void *tnn_mul_mat_id(void *sess, void *as, void *b, void *ids);
+/* KV-cache graph primitives (tinynn_ggml.h:311-342, 574). tnn_null_ptr: NULL.
+ * tnn_detach: a itself for the forward, a cut for the backward.
+ * tnn_cpy: a's elements (f32 or i32) written into b's storage; returns b's
+ * view, so reads of b that run after it see them. tnn_set_rows: rows idx[i]
+ * (i32) of a := rows i of b; returns a's view. tnn_upload_causal_mask: fills
+ * f32 [hist, n_tok] with 0 where key j <= pos0 + token i, -inf elsewhere
+ * (hist == pos0 + n_tok, else -2; wrong shape or type -3).
+ * tnn_upload_cell_mask: the same over a pool of KV cells -- cell c is open
+ * to token t when it belongs to t's sequence at a position <= t's, or is a
+ * shared-prefix cell (owner -1) below t's shared length; owner -2 is free. */
+void *tnn_null_ptr(void);
+void *tnn_detach(void *sess, void *a);
+void *tnn_cpy(void *sess, void *a, void *b);
+void *tnn_set_rows(void *sess, void *a, void *b, void *idx);
+int tnn_upload_causal_mask(void *sess, void *tensor, int hist, int n_tok, int pos0);
+int tnn_upload_cell_mask(void *sess, void *tensor, int hi, int n_tok, const long *cell_owner, const long *cell_pos,
+                         const long *tok_owner, const long *tok_pos, const long *tok_shared);
 void *tnn_add_id(void *sess, void *a, void *b, void *ids);
 void *tnn_argsort(void *sess, void *a, int descending);
 void *tnn_top_k(void *sess, void *a, int k);

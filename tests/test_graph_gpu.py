@@ -554,3 +554,42 @@ def test_moe_primitives(cuda):
     assert L.tnn_mul_mat_id(s, wf, g.f32(rng.standard_normal((T, 3, d_in))), tid) is None   # n_used mismatch
     assert L.tnn_top_k(s, tv, 8) is None
     g.close()
+
+
+def test_kv_cache_primitives(cuda):
+    """tnn_set_rows / tnn_cpy write into their destination's storage, tnn_detach
+    is the identity forward, and the causal and cell masks are filled as
+    tinynn_ggml.c fills them."""
+    rng = np.random.default_rng(12)
+    g = Graph()
+    L, s = g.L, g.s
+    assert L.tnn_null_ptr() is None
+    C0 = rng.standard_normal((6, 8))
+    R = rng.standard_normal((2, 8))
+    Nw = rng.standard_normal((6, 8))
+    V = rng.standard_normal((3, 4))
+    cache, dst = g.f32(C0), g.f32(np.zeros((6, 8)))
+    sr = L.tnn_set_rows(s, cache, g.f32(R), g.i32(np.array([4, 1])))
+    cp = L.tnn_cpy(s, g.f32(Nw), dst)
+    det = L.tnn_detach(s, g.f32(V))
+    r_sr, r_cp, r_det = g.run([sr, cp, det])
+    want = C0.copy()
+    want[4], want[1] = R[0], R[1]
+    assert rel(r_sr, want) < 1e-7 and rel(g.get(cache), want) < 1e-7
+    assert rel(r_cp, Nw) < 1e-7 and rel(g.get(dst), Nw) < 1e-7
+    assert rel(r_det, V) < 1e-7
+    hist, n_tok, pos0 = 7, 3, 4
+    m = L.tnn_input_2d_f32_persistent(s, n_tok, hist)
+    assert L.tnn_upload_causal_mask(s, m, hist, n_tok, pos0) == 0
+    ref = np.array([[0.0 if j <= pos0 + i else -np.inf for j in range(hist)] for i in range(n_tok)])
+    assert np.array_equal(g.get(m), ref)
+    assert L.tnn_upload_causal_mask(s, m, hist, n_tok, pos0 + 1) == -2
+    hi = 5
+    cm = L.tnn_input_2d_f32_persistent(s, 2, hi)
+    arr = lambda *v: (C.c_long * len(v))(*v)
+    owner, cpos = arr(0, 0, -1, 1, -2), arr(0, 3, 1, 0, 0)
+    assert L.tnn_upload_cell_mask(s, cm, hi, 2, owner, cpos, arr(0, 1), arr(2, 5), arr(2, 0)) == 0
+    vis = [[(o == to and p <= tp) or (o == -1 and p < sh) for o, p in zip([0, 0, -1, 1, -2], [0, 3, 1, 0, 0])]
+           for to, tp, sh in ((0, 2, 2), (1, 5, 0))]
+    assert np.array_equal(g.get(cm), np.where(vis, 0.0, -np.inf))
+    g.close()

@@ -158,6 +158,13 @@ _SIGS = [
     ("tnn_get_rows", VP, [VP, VP, VP]),
     ("tnn_get_rows_back", VP, [VP, VP, VP, VP]),
     ("tnn_mul_mat_id", VP, [VP, VP, VP, VP]),
+    ("tnn_null_ptr", VP, []),
+    ("tnn_detach", VP, [VP, VP]),
+    ("tnn_cpy", VP, [VP, VP, VP]),
+    ("tnn_set_rows", VP, [VP, VP, VP, VP]),
+    ("tnn_upload_causal_mask", C.c_int, [VP, VP, C.c_int, C.c_int, C.c_int]),
+    ("tnn_upload_cell_mask", C.c_int, [VP, VP, C.c_int, C.c_int, C.POINTER(C.c_long), C.POINTER(C.c_long),
+                                       C.POINTER(C.c_long), C.POINTER(C.c_long), C.POINTER(C.c_long)]),
     ("tnn_add_id", VP, [VP, VP, VP, VP]),
     ("tnn_argsort", VP, [VP, VP, C.c_int]),
     ("tnn_top_k", VP, [VP, VP, C.c_int]),

@@ -202,6 +202,57 @@ void* tnn_get_rows(void* sess, void* table, void* idx) {
   Session* s = graph_session(sess);
   return s && mine(s, table) && mine(s, idx) ? tb2::prim_get_rows(s, T(table), T(idx)) : nullptr;
 }
+void* tnn_null_ptr(void) { return nullptr; }
+
+// tinynn_ggml.c tnn_upload_causal_mask semantics: f32 [hist][n_tok] (ne0 =
+// hist), column i open (0) for keys j <= pos0 + i, -inf beyond; hist must be
+// pos0 + n_tok (-2 otherwise), a tensor of another shape or type gives -3.
+int tnn_upload_causal_mask(void* sess, void* tensor, int hist, int n_tok, int pos0) {
+  if (!sess || !tensor) return -1;
+  if (hist <= 0 || n_tok <= 0 || pos0 < 0 || hist != pos0 + n_tok) return -2;
+  Session* s = graph_session(sess);
+  if (!s || !mine(s, tensor)) return -1;
+  Tensor* t = T(tensor);
+  if (t->type != 0 || t->ne[0] != hist || t->ne[1] != n_tok || t->ne[2] != 1 || t->ne[3] != 1) return -3;
+  std::vector<double> m((size_t)hist * n_tok);
+  for (int i = 0; i < n_tok; ++i)
+    for (int j = 0; j < hist; ++j) m[(size_t)i * hist + j] = j <= pos0 + i ? 0.0 : -INFINITY;
+  return tb2::prim_upload_f64(s, t, m.data(), m.size());
+}
+
+// tinynn_ggml.c tnn_upload_cell_mask semantics: f32 [hi][n_tok], cell c open to
+// token t when it holds an earlier-or-equal position of t's sequence
+// (cell_owner[c] == tok_owner[t] && cell_pos[c] <= tok_pos[t]) or is a shared
+// prefix cell (owner -1) below t's shared-prefix length; owner -2 is free.
+int tnn_upload_cell_mask(void* sess, void* tensor, int hi, int n_tok, const long* cell_owner, const long* cell_pos,
+                         const long* tok_owner, const long* tok_pos, const long* tok_shared) {
+  if (!sess || !tensor || !cell_owner || !cell_pos || !tok_owner || !tok_pos || !tok_shared) return -1;
+  if (hi <= 0 || n_tok <= 0) return -2;
+  Session* s = graph_session(sess);
+  if (!s || !mine(s, tensor)) return -1;
+  Tensor* t = T(tensor);
+  if (t->type != 0 || t->ne[0] != hi || t->ne[1] != n_tok || t->ne[2] != 1 || t->ne[3] != 1) return -3;
+  std::vector<double> m((size_t)hi * n_tok);
+  for (int k = 0; k < n_tok; ++k)
+    for (int c = 0; c < hi; ++c) {
+      const bool own = cell_owner[c] == tok_owner[k] && cell_pos[c] <= tok_pos[k];
+      const bool shared = cell_owner[c] == -1 && cell_pos[c] < tok_shared[k];
+      m[(size_t)k * hi + c] = own || shared ? 0.0 : -INFINITY;
+    }
+  return tb2::prim_upload_f64(s, t, m.data(), m.size());
+}
+void* tnn_detach(void* sess, void* a) {
+  Session* s = graph_session(sess);
+  return s && mine(s, a) ? tb2::prim_detach(s, T(a)) : nullptr;
+}
+void* tnn_cpy(void* sess, void* a, void* b) {
+  Session* s = graph_session(sess);
+  return s && mine(s, a) && mine(s, b) ? tb2::prim_cpy(s, T(a), T(b)) : nullptr;
+}
+void* tnn_set_rows(void* sess, void* a, void* b, void* idx) {
+  Session* s = graph_session(sess);
+  return s && mine(s, a) && mine(s, b) && mine(s, idx) ? tb2::prim_set_rows(s, T(a), T(b), T(idx)) : nullptr;
+}
 void* tnn_mul_mat_id(void* sess, void* as, void* b, void* ids) {
   Session* s = graph_session(sess);
   return s && mine(s, as) && mine(s, b) && mine(s, ids) ? tb2::prim_mul_mat_id(s, T(as), T(b), T(ids)) : nullptr;

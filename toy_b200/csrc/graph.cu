@@ -400,6 +400,16 @@ __global__ void k_mul_mat_id(const float* __restrict__ w32, const int8_t* __rest
   }
 }
 
+// ggml_set_rows: o[idx[r]][c] = b[r][c] for the rows of b (indices outside o skipped)
+__global__ void k_set_rows(const float* __restrict__ b, const int* __restrict__ idx, float* __restrict__ o, int ne0,
+                           int o_rows, long long n) {
+  griddep_wait();
+  GRID_LOOP(i, n) {
+    const int r = idx[i / ne0];
+    if (r >= 0 && r < o_rows) o[(long long)r * ne0 + i % ne0] = b[i];
+  }
+}
+
 // ggml_add_id: o[i2][i1][i0] = a[i2][i1][i0] + b[ids[i2][i1]][i0]
 __global__ void k_add_id(const float* __restrict__ a, const float* __restrict__ b, const int* __restrict__ ids,
                          float* __restrict__ o, int ne0, int nb_rows, long long n) {
@@ -972,6 +982,48 @@ Tensor* prim_argsort(Session* s, Tensor* a, int descending, int k) {
   return t;
 }
 
+// ggml_detach-style cut: an alias of a that the backward does not pass through
+Tensor* prim_detach(Session* s, Tensor* a) {
+  if (!a || a->type == 8) return nullptr;
+  Tensor* t = prim_new(s, a->type, a->ne[0], a->ne[1], a->ne[2], a->ne[3], kOpDetach, false);
+  if (t) {
+    t->src[0] = a;
+    t->view_of = a->view_of ? a->view_of : a;
+    t->view_off = a->view_of ? a->view_off : 0;
+  }
+  return t;
+}
+
+// ggml_cpy: the elements of a written into b's storage (same count, same type,
+// f32 or i32); the result is b's view, so later reads of b see them
+Tensor* prim_cpy(Session* s, Tensor* a, Tensor* b) {
+  if (!a || !b || a->type != b->type || (a->type != 0 && a->type != 26) || a->nel() != b->nel()) return nullptr;
+  Tensor* t = prim_new(s, b->type, b->ne[0], b->ne[1], b->ne[2], b->ne[3], kOpCpy, false);
+  if (t) {
+    t->src[0] = a;
+    t->src[1] = b;
+    t->view_of = b->view_of ? b->view_of : b;
+    t->view_off = b->view_of ? b->view_off : 0;
+  }
+  return t;
+}
+
+// ggml_set_rows: rows idx[i] of a (f32 [ne0][rows]) := rows i of b (f32 [ne0][n]),
+// idx i32 [n]; the result is a's view (indices outside a's rows are skipped)
+Tensor* prim_set_rows(Session* s, Tensor* a, Tensor* b, Tensor* idx) {
+  if (!is_f32(a) || !is_f32(b) || !idx || idx->type != 26 || a->ne[0] != b->ne[0] || b->rows() != idx->nel())
+    return nullptr;
+  Tensor* t = prim_new(s, 0, a->ne[0], a->ne[1], a->ne[2], a->ne[3], kOpSetRows, false);
+  if (t) {
+    t->src[0] = a;
+    t->src[1] = b;
+    t->src[2] = idx;
+    t->view_of = a->view_of ? a->view_of : a;
+    t->view_off = a->view_of ? a->view_off : 0;
+  }
+  return t;
+}
+
 Tensor* prim_get_rows(Session* s, Tensor* table, Tensor* idx) {
   if (!is_f32(table) || !idx || idx->type != 26) return nullptr;
   Tensor* t = prim_new(s, 0, table->ne[0], (int)idx->nel(), 1, 1, kOpGetRows, false);
@@ -1209,6 +1261,13 @@ int exec(Session* s, Tensor* t) {
     case kOpSlice:
       return launch_pdl(k_slice, dim3(grid_for(n, threads)), dim3(threads), 0, st, F(a), F(t), shape(a), shape(t),
                         t->ip[0], t->ip[1], n);
+    case kOpDetach:
+      return 0;
+    case kOpCpy:
+      return cudaMemcpyAsync(t->data, a->data, (size_t)n * 4, cudaMemcpyDeviceToDevice, st) == cudaSuccess ? 0 : -3;
+    case kOpSetRows:
+      return launch_pdl(k_set_rows, dim3(grid_for(b->nel(), threads)), dim3(threads), 0, st, (const float*)F(b),
+                        (const int*)I(t->src[2]), F(t), t->ne[0], (int)t->rows(), b->nel());
     case kOpMulMatId: {
       Tensor* ids = t->src[2];
       const long long nout = t->nel();

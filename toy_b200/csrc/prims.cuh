@@ -10,7 +10,7 @@ enum PrimOp : int {
   kOpRmsNorm, kOpRmsNormBack, kOpRope, kOpRopeBack, kOpSoftMax, kOpSoftMaxBack, kOpDiagMaskInf, kOpDiagMaskZero,
   kOpTranspose, kOpCont, kOpReshape, kOpView, kOpConcat, kOpSlice, kOpGetRows, kOpGetRowsBack, kOpCrossEntropy,
   kOpCrossEntropyBack, kOpSum, kOpSumRows, kOpRepeat, kOpRepeatBack, kOpOptAdamw, kOpAccView, kOpDequant, kOpOptSgd,
-  kOpMulMatId, kOpAddId, kOpArgsort, kOpTopK, kOpCount
+  kOpMulMatId, kOpAddId, kOpArgsort, kOpTopK, kOpDetach, kOpCpy, kOpSetRows, kOpCount
 };
 const char* prim_op_name(int op);
 
@@ -45,6 +45,9 @@ Tensor* prim_get_rows(Session* s, Tensor* table, Tensor* idx);
 Tensor* prim_mul_mat_id(Session* s, Tensor* as, Tensor* b, Tensor* ids);   // ggml_mul_mat_id (forward)
 Tensor* prim_add_id(Session* s, Tensor* a, Tensor* b, Tensor* ids);        // ggml_add_id (forward)
 Tensor* prim_argsort(Session* s, Tensor* a, int descending, int k);        // k = 0: argsort; k > 0: top_k
+Tensor* prim_detach(Session* s, Tensor* a);                                // forward identity, no gradient
+Tensor* prim_cpy(Session* s, Tensor* a, Tensor* b);                        // b's storage := a; returns b's view
+Tensor* prim_set_rows(Session* s, Tensor* a, Tensor* b, Tensor* idx);      // a[idx[i]] := b[i]; returns a's view
 Tensor* prim_get_rows_back(Session* s, Tensor* g, Tensor* idx, Tensor* like);
 Tensor* prim_cross_entropy(Session* s, Tensor* a, Tensor* b);
 Tensor* prim_sum(Session* s, int op, Tensor* a);                        // kOpSum / kOpSumRows
