@@ -72,7 +72,7 @@ MODEL_NAMES = {"smollm2": "SmolLM2-135M shape", "llama32_1b": "Llama-3.2-1B shap
 # when its kernel ends is not counted as a DRAM write: the traffic is a lower
 # bound on writes, exact on reads.
 GEMM_TRAFFIC = {
-    "smollm2_full_ft_b8_t512": {"bytes_per_step": 14067009280, "launches": 363,
+    "smollm2_full_ft_b8_t512": {"bytes_per_step": 14233990912, "launches": 363,
                                 "algorithmic_bytes_per_step": 17081303040,
                                 "source": "ncu, full workload, -s 272 -c 900 (one complete step)"},
 }
