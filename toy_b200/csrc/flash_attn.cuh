@@ -7,7 +7,7 @@
 //   lse2 [B][H][T]  log2-domain softmax normaliser of the scaled scores:
 //                   P[q, k] = exp2(S[q, k] * scale * log2(e) - lse2[q])
 // Query head h reads key/value head h / (H / KV) (grouped-query attention).
-// Supported head width: dh = 64.
+// Supported head widths: dh = 64 and 128.
 #pragma once
 #include "kernels.cuh"
 

@@ -81,8 +81,8 @@ class RecipeOptions:
     # > 0: every weight N(0, init_std) instead of the reference's fan-in scaled
     # init (the benchmark configurations' "all weights N(0, 0.02)")
     init_std: float = 0.0
-    # attention core: "flash" (fused kernels, d_head 64; other widths use the
-    # materialised path) or "materialized" (score GEMM + softmax + PV GEMM)
+    # attention core: "flash" (fused kernels, d_head 64 or 128; other widths
+    # use the materialised path) or "materialized" (score GEMM + softmax + PV GEMM)
     attention: str = "flash"
 
 
