@@ -76,7 +76,8 @@ typedef struct tb2_epilogue {
 
 /* D_z[m,n] = epilogue(sum_k A_z[m,k] B_z[n,k]) on tcgen05 tensor cores.
  * split = 1: 3 MMAs per k-step over (hi, lo) planes (~fp32 accuracy);
- * split = 0: plain bf16 (hi planes only).
+ * split = 0: plain bf16 (hi planes only);
+ * split = 2: plain fp16 (the hi arrays hold fp16 values; lo unused).
  * ksplits: K ranges reduced deterministically through a per-device workspace
  * (0 = chosen from the tile count). causal: 0 none, 1 skip output tiles whose
  * columns all exceed their rows (attention scores), 2 limit K to each row
@@ -177,6 +178,13 @@ int tb2_set_side_gemm_tile_width(int bn);
  * enqueues its step program. No counterpart in the reference.
  * Returns the previous setting, or -1 for another value. */
 int tb2_set_plan_alone(int on);
+/* 1 (the default): full fine-tunes realised afterwards compute their weight
+ * gradients in one fp16 tensor-core pass (the gradient operands scaled per
+ * tensor by a power of two set from the previous step's largest magnitude;
+ * the first step of a program records those magnitudes on three split-bf16
+ * passes); 0: three split-bf16 passes. No counterpart in the reference.
+ * Returns the previous setting, or -1 for another value. */
+int tb2_set_f16_wgrad(int on);
 
 /* hi = rn_bf16(x), lo = rn_bf16(x - hi) for n f32 values. */
 int tb2_split_f32(const float *x, void *hi, void *lo, size_t n, void *stream);

@@ -9,8 +9,9 @@ streams bit-exact.
 
   * SmolLM2-135M QLoRA (q, v; rank 8, alpha 16), 30 layers, V = 49152, B=1 T=64,
     seed 42, lr 1e-4, wd 0.01, two steps;
-  * SmolLM2-135M full f32 fine-tune, every weight N(0, 0.02), B=8 T=512, one step
-    (the default throughput workload);
+  * SmolLM2-135M full f32 fine-tune, every weight N(0, 0.02), B=8 T=512, two steps
+    (the default throughput workload; the second step runs the weight gradients
+    as one fp16 pass, scaled from the first step's gradient magnitudes);
   * SmolLM2-135M QLoRA (q, v) at B=8 T=512, one step (the QLoRA throughput workload).
 
 Each test prints its three worst relative-L2 values (gradients, weights, moments).
@@ -101,7 +102,7 @@ def test_smollm2_qlora_b1_t64_two_steps(cuda, capsys):
 
 
 def test_smollm2_full_ft_b8_t512(cuda, capsys):
-    """The default throughput workload, one step: full f32 fine-tune, B=8 T=512."""
+    """The default throughput workload, two steps: full f32 fine-tune, B=8 T=512."""
     from toy_b200 import FromScratch, RecipeOptions
     oc, gc = smollm2()
     T, B = 512, 8
@@ -112,13 +113,14 @@ def test_smollm2_full_ft_b8_t512(cuda, capsys):
     for k in ("token_embd.weight", "blk.0.attn_q.weight", "blk.29.ffn_down.weight"):
         got = eng.param(k).astype(np.float32).reshape(mdl.params[k].shape)
         assert np.array_equal(got.view(np.uint32), mdl.params[k].view(np.uint32)), k
-    ids, pos, lab = batch(oc, T, B, 7)
-    hp = O.hp_lora(1e-4, 1, wd=0.01)
-    loss_g = rec.step(ids, pos, lab, hp, True)
-    loss_r, grads = O.train_step(mdl, ids, pos, lab, T, B, hp, True)
-    lerr, worst = compare(eng, mdl, loss_g, loss_r, grads)
-    report(capsys, "smollm2 full FT B8 T512", 1, lerr, worst)
-    check(lerr, worst)
+    for step, seed in ((1, 7), (2, 8)):
+        ids, pos, lab = batch(oc, T, B, seed)
+        hp = O.hp_lora(1e-4, step, wd=0.01)
+        loss_g = rec.step(ids, pos, lab, hp, step == 1)
+        loss_r, grads = O.train_step(mdl, ids, pos, lab, T, B, hp, step == 1)
+        lerr, worst = compare(eng, mdl, loss_g, loss_r, grads)
+        report(capsys, "smollm2 full FT B8 T512", step, lerr, worst)
+        check(lerr, worst)
 
 
 def test_smollm2_qlora_b8_t512(cuda, capsys):

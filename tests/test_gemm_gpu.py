@@ -85,6 +85,39 @@ def test_gemm_single_pass_bf16(cuda):
     assert _relerr(out, ref) < 1e-5
 
 
+def _operand16(store, mn_major, rows):
+    """store: f32 tensor [rows_total, cols]; its fp16 copy as a single-plane operand."""
+    from toy_b200._lib import Operand
+    h = store.half().contiguous()
+    o = Operand()
+    o.hi, o.lo = h.data_ptr(), None
+    o.mn_major = mn_major
+    o.ld = store.shape[1]
+    o.rows = rows
+    o.cols = store.shape[1]
+    o.batch_stride = rows * store.shape[1]
+    o.nbatch = 1
+    o.bdiv1, o.bmul1, o.bdiv2, o.bmul2 = 1, 0, 1, 0
+    return o, h
+
+
+@pytest.mark.parametrize("a_mn,b_mn,ksplits", [(1, 1, 0), (1, 1, 4), (0, 0, 0), (1, 0, 2)])
+def test_gemm_single_pass_f16(cuda, a_mn, b_mn, ksplits):
+    """split = 2: one kind::f16 pass on fp16 operands (the weight-gradient layout: both
+    operands MN-major, K = tokens), against fp64 of the fp16-rounded inputs; alpha applied."""
+    import torch
+    M, N, K = 576, 1536, 4096
+    g = torch.Generator(device="cuda").manual_seed(5)
+    A = torch.randn(M, K, device=cuda, generator=g) * 3.0
+    B = torch.randn(N, K, device=cuda, generator=g)
+    a, ka = _operand16(A.t().contiguous() if a_mn else A, a_mn, K if a_mn else M)
+    b, kb = _operand16(B.t().contiguous() if b_mn else B, b_mn, K if b_mn else N)
+    out = torch.full((M, N), float("nan"), device=cuda)
+    _gemm(M, N, K, 1, 2, a, b, _epi(0, out, N, alpha=0.25), ksplits=ksplits)
+    ref = 0.25 * (A.half().double() @ B.half().double().t())
+    assert _relerr(out, ref) < 1e-5
+
+
 def test_gemm_batched_gqa(cuda):
     """Scores per (sequence, query head) against a shared K head: z = b*H + h reads K batch b*KV + h/G."""
     import torch

@@ -107,6 +107,7 @@ _SIGS = [
     ("tb2_set_side_gemm_ctas", C.c_int, [C.c_int]),
     ("tb2_set_side_gemm_tile_width", C.c_int, [C.c_int]),
     ("tb2_set_plan_alone", C.c_int, [C.c_int]),
+    ("tb2_set_f16_wgrad", C.c_int, [C.c_int]),
     ("tb2_device_error", C.c_int, []),
     ("tb2_q8_0_quantize", C.c_int, [C.c_void_p, C.c_void_p, C.c_longlong, C.c_int, C.c_void_p]),
     ("tb2_q8_0_dequantize", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_longlong, C.c_int,

@@ -30,9 +30,10 @@ extern "C" {
 
 int tb2_gemm(int M, int N, int K, int batch, int split, const tb2_operand* a, const tb2_operand* b,
              const tb2_epilogue* epi, int ksplits, int causal, void* stream) {
-  if (!a || !b || !epi || ksplits < 0) return -1;
+  if (!a || !b || !epi || ksplits < 0 || split < 0 || split > 2) return -1;
   tb2::GemmDesc d;
-  d.M = M; d.N = N; d.K = K; d.batch = batch; d.split = split != 0;
+  d.M = M; d.N = N; d.K = K; d.batch = batch; d.split = split == 1;
+  d.f16 = split == 2;
   d.splits = ksplits;
   d.causal = causal;
   d.a = to_op(a);
@@ -71,6 +72,7 @@ int tb2_set_side_gemm_ctas(int n) { return tb2::engine_set_side_gemm_ctas(n); }
 int tb2_set_side_gemm_tile_width(int bn) { return tb2::engine_set_side_gemm_tile_width(bn); }
 
 int tb2_set_plan_alone(int on) { return tb2::engine_set_plan_alone(on); }
+int tb2_set_f16_wgrad(int on) { return tb2::engine_set_f16_wgrad(on); }
 
 int tb2_split_f32(const float* x, void* hi, void* lo, size_t n, void* stream) {
   if (!x || !hi || !lo) return -1;

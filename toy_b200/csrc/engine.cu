@@ -35,6 +35,14 @@ int engine_set_plan_alone(int on) {
   return prev;
 }
 int g_side_gemm_bn = 128;   // measured in the step: 223.2k vs 222.1k (plan's choice), 216.1k (256), 210.0k (64)
+int g_f16_wgrad = 1;
+
+int engine_set_f16_wgrad(int on) {
+  if (on < 0 || on > 1) return -1;
+  const int prev = g_f16_wgrad;
+  g_f16_wgrad = on;
+  return prev;
+}
 
 int engine_set_side_gemm_tile_width(int bn) {
   if (bn != 0 && bn != 64 && bn != 128 && bn != 192 && bn != 256) return -1;
@@ -71,6 +79,11 @@ Operand op(Planes p, int rows, int cols, long long ld, int mn) {
   o.hi = p.hi; o.lo = p.lo; o.mn_major = mn; o.ld = ld; o.rows = rows; o.cols = cols;
   o.batch_stride = (long long)rows * ld; o.nbatch = 1; o.bdiv1 = 1; o.bmul1 = 0; o.bdiv2 = 1; o.bmul2 = 0;
   return o;
+}
+
+// an fp16 array as a single-plane operand (GemmDesc::f16)
+Operand op16(const __half* p, int rows, int cols, long long ld, int mn) {
+  return op(Planes{reinterpret_cast<bf16*>(const_cast<__half*>(p)), nullptr}, rows, cols, ld, mn);
 }
 
 Operand bop(Planes p, int rows, int cols, long long ld, int nbatch, int mn, int d1 = 1, int m1 = 1, int d2 = 1,
@@ -540,6 +553,44 @@ int LlamaEngine::realize() {
   dxp_ = dxp2_[0];
   dgu_ = dgu2_[0];
   dqkv_ = dqkv2_[0];
+  // fp16 copies of the weight-gradient operands (full fine-tune on the fused
+  // attention, dense FFN): every activation operand in place, the gradients
+  // scaled per tensor (slots: 4 per layer + the logits' gradient)
+  f16w_ = full && flash_ && !moe_ && g_f16_wgrad;
+  f16w_ready_ = false;
+  if (f16w_) {
+    auto h16 = [&](long long n) -> __half* {
+      bufs_.emplace_back();
+      if (alloc(bufs_.back(), ((n + 127) / 128 * 128) * 2)) return nullptr;
+      return static_cast<__half*>(bufs_.back().p);
+    };
+    for (int l = 0; l < c.n_layers; ++l) {
+      h1_[l].f16 = h16((long long)N * d);
+      h2_[l].f16 = h16((long long)N * d);
+      a_[l].f16 = h16((long long)N * a_ld_);
+      O_[l].f16 = h16((long long)N * o_ld_);
+    }
+    xf_.f16 = h16((long long)N * d);
+    dlog_.f16 = h16((long long)N * V);
+    for (int k = 0; k < 2; ++k) {
+      dxp2_[k].f16 = h16((long long)N * dxp_ld_);
+      dgu2_[k].f16 = h16((long long)N * (2 * ff + ext_[kGroupGU]));
+      dqkv2_[k].f16 = h16((long long)N * (W + ext_[kGroupQKV]));
+    }
+    n16_ = 4 * c.n_layers;
+    amax16_ = reinterpret_cast<unsigned*>(f32(n16_ + 1));
+    scale16_ = f32(n16_ + 1);
+    inv16_ = f32(n16_ + 1);
+    // |dlogits| <= 1 / N: a static scale 2^(14 + floor(log2 N)) keeps them <= 2^14
+    const int e = 14 + (int)std::floor(std::log2((double)N));
+    std::vector<float> sc(n16_ + 1, 1.0f), iv(n16_ + 1, 1.0f);
+    sc[n16_] = std::ldexp(1.0f, e);
+    iv[n16_] = std::ldexp(1.0f, -e);
+    CU(cudaMemcpy(scale16_, sc.data(), sc.size() * 4, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(inv16_, iv.data(), iv.size() * 4, cudaMemcpyHostToDevice));
+    CU(cudaMemset(amax16_, 0, (n16_ + 1) * 4));
+    dlog_.f16_scale = scale16_ + n16_;
+  }
   dO_ = pl((long long)N * H * dh);
   if (!flash_) dS_ = pl(att);
   if (!full) {
@@ -1120,7 +1171,7 @@ int LlamaEngine::fill_ahead(int l) {
   return 0;
 }
 
-int LlamaEngine::norm_bwd(const float* x, const float* gamma, const float* dres, const Param& gp) {
+int LlamaEngine::norm_bwd(const float* x, const float* gamma, const float* dres, const Param& gp, int slot16) {
   const LlamaConfig& c = cfg_;
   const bool trainable = gp.trainable;
   CK(flip(t_dxp_));
@@ -1130,7 +1181,8 @@ int LlamaEngine::norm_bwd(const float* x, const float* gamma, const float* dres,
     gpart_ = gpart2_[t_gpart_.cur];
   }
   const int nblk = rmsnorm_bwd_blocks();
-  KL(launch_rmsnorm_bwd(x, dh_, gamma, dres, dx_, dxp_, trainable ? gpart_ : nullptr, nblk, N(), c.d_model, c.rms_eps,
+  KL(launch_rmsnorm_bwd(x, dh_, gamma, dres, dx_, grad16(dxp_, slot16), trainable ? gpart_ : nullptr, nblk, N(),
+                        c.d_model, c.rms_eps,
                         stream_, dxp_ld_));
   if (trainable) {   // dgamma: a weight gradient, on the side stream
     CK(fork_side());
@@ -1774,6 +1826,11 @@ int LlamaEngine::enqueue_backward() {
   side_forked_ = false;
   t_dxp_ = t_dgu_ = t_dqkv_ = t_du_ = t_gpart_ = Transient{};
   dxp_ = dxp2_[0]; dgu_ = dgu2_[0]; dqkv_ = dqkv2_[0]; du32_ = du2_[0];
+  // fp16 weight gradients from the second step a program runs on: the first
+  // records the gradients' magnitudes (three-pass products meanwhile)
+  const bool w16 = f16w_ && f16w_ready_;
+  if (f16w_) KL(launch_f16_scale_update(amax16_, scale16_, inv16_, n16_, stream_));
+  const int L = c.n_layers;
   // dxf = dlogits W_out   ([N][V] x [V][d])
   GemmDesc g;
   g.M = N; g.N = d; g.K = V;
@@ -1787,11 +1844,17 @@ int LlamaEngine::enqueue_backward() {
     ge.a = op(dlog_, N, V, V, 1);
     ge.b = op(xf_, N, d, d, 1);
     ge.epi = epi_rowmajor(kEpiStoreF32, G32(Wout), d);
+    if (w16) {
+      ge.split = false; ge.f16 = true;
+      ge.a = op16(dlog_.f16, N, V, V, 1);
+      ge.b = op16(xf_.f16, N, d, d, 1);
+      ge.epi.alpha_dev = inv16_ + n16_;
+    }
     CK(fork_side());
     CK(gemm_side(ge));
   }
   const Param& gf = P("output_norm.weight");
-  CK(norm_bwd(x_[c.n_layers], P32(gf), nullptr, gf));
+  CK(norm_bwd(x_[c.n_layers], P32(gf), nullptr, gf, 4 * (L - 1)));
   for (int l = c.n_layers - 1; l >= 0; --l) {
     const std::string pre = "blk." + std::to_string(l) + ".";
     CK(dequant_layer(l));   // the forward's last two blocks are still in the ring
@@ -1823,6 +1886,12 @@ int LlamaEngine::enqueue_backward() {
         gw.a = op(dxp_, N, d, dxp_ld_, 1);
         gw.b = op(a_[l], N, ff, a_ld_, 1);
         gw.epi = epi_rowmajor(kEpiStoreF32, G32(Wd), ff);
+        if (w16) {
+          gw.split = false; gw.f16 = true;
+          gw.a = op16(dxp_.f16, N, d, dxp_ld_, 1);
+          gw.b = op16(a_[l].f16, N, ff, a_ld_, 1);
+          gw.epi.alpha_dev = inv16_ + 4 * l;
+        }
         CK(gemm_side(gw));
       }
       CK(side_read2(t_dxp_, t_du_));
@@ -1831,7 +1900,7 @@ int LlamaEngine::enqueue_backward() {
     const int eg = ext_[kGroupGU];   // dgu carries du of the gate|up adapters in its extra columns
     CK(flip(t_dgu_));
     dgu_ = dgu2_[t_dgu_.cur];
-    KL(launch_swiglu_bwd(gu_[l], da_, dgu_, N, ff, stream_, 2 * ff + eg));
+    KL(launch_swiglu_bwd(gu_[l], da_, grad16(dgu_, 4 * l + 1), N, ff, stream_, 2 * ff + eg));
     GemmDesc gh;
     gh.M = N; gh.N = d; gh.K = 2 * ff + eg;
     gh.a = op(dgu_, N, 2 * ff + eg, 2 * ff + eg, 0);
@@ -1850,6 +1919,12 @@ int LlamaEngine::enqueue_backward() {
         gw.a = op(dgu_, N, 2 * ff, 2 * ff + eg, 1);
         gw.b = op(h2_[l], N, d, d, 1);
         gw.epi = epi_rowmajor(kEpiStoreF32, G32(Wg), d);
+        if (w16) {
+          gw.split = false; gw.f16 = true;
+          gw.a = op16(dgu_.f16, N, 2 * ff, 2 * ff + eg, 1);
+          gw.b = op16(h2_[l].f16, N, d, d, 1);
+          gw.epi.alpha_dev = inv16_ + 4 * l + 1;
+        }
         CK(gemm_side(gw));
       }
       CK(side_read2(t_dgu_, t_du_));
@@ -1858,7 +1933,7 @@ int LlamaEngine::enqueue_backward() {
       CK(lora_backward(l, Gg.t[i], h2_[l], d, dgu_, 2 * ff, Gg.c0[i], Gg.w[i], dh_, nullptr));
     }
     const Param& g2 = P(pre + "ffn_norm.weight");
-    CK(norm_bwd(x1_[l], P32(g2), dx_, g2));
+    CK(norm_bwd(x1_[l], P32(g2), dx_, g2, 4 * l + 2));
     // ---- attention output projection: dO (head-major f32), dWo
     Epilogue hm;
     hm.mode = kEpiStoreF32; hm.out = dO32_;
@@ -1882,6 +1957,12 @@ int LlamaEngine::enqueue_backward() {
         gw.a = op(dxp_, N, d, dxp_ld_, 1);
         gw.b = op(O_[l], N, H * dh, o_ld_, 1);
         gw.epi = epi_rowmajor(kEpiStoreF32, G32(Wo), H * dh);
+        if (w16) {
+          gw.split = false; gw.f16 = true;
+          gw.a = op16(dxp_.f16, N, d, dxp_ld_, 1);
+          gw.b = op16(O_[l].f16, N, H * dh, o_ld_, 1);
+          gw.epi.alpha_dev = inv16_ + 4 * l + 2;
+        }
         CK(gemm_side(gw));
       }
       CK(side_read2(t_dxp_, t_du_));
@@ -1894,8 +1975,8 @@ int LlamaEngine::enqueue_backward() {
       KL(launch_flash_bwd_prep(dO32_, O_[l], dO_, dvec_, B, T, H, dh, stream_, o_ld_));
       KL(launch_flash_bwd(Qh_[l], Kh_[l], Vh_[l], dO_, lse2_[l], dvec_, fws_, B, T, H, KV, dh, scale, err_,
                           stream_));
-      KL(launch_flash_rope_bwd(fws_, pos_, cs_, cs_rows_, dqkv_, c.qkv_bias ? qkv_ : nullptr, B, T, H, KV, dh,
-                               stream_, W + ext_[kGroupQKV]));
+      KL(launch_flash_rope_bwd(fws_, pos_, cs_, cs_rows_, grad16(dqkv_, 4 * l + 3), c.qkv_bias ? qkv_ : nullptr, B,
+                               T, H, KV, dh, stream_, W + ext_[kGroupQKV]));
     } else {
       KL(launch_split_f32(dO32_, dO_.hi, dO_.lo, (long long)N * H * dh, stream_));
       // ---- attention core
@@ -1985,6 +2066,12 @@ int LlamaEngine::enqueue_backward() {
         gw.a = op(dqkv_, N, W, W + eq, 1);
         gw.b = op(h1_[l], N, d, d, 1);
         gw.epi = epi_rowmajor(kEpiStoreF32, G32(Wq), d);
+        if (w16) {
+          gw.split = false; gw.f16 = true;
+          gw.a = op16(dqkv_.f16, N, W, W + eq, 1);
+          gw.b = op16(h1_[l].f16, N, d, d, 1);
+          gw.epi.alpha_dev = inv16_ + 4 * l + 3;
+        }
         CK(gemm_side(gw));
       }
       CK(side_read2(t_dqkv_, t_du_));
@@ -1992,7 +2079,7 @@ int LlamaEngine::enqueue_backward() {
     for (int i = 0; i < Gq.n && !gq_grp; ++i)
       CK(lora_backward(l, Gq.t[i], h1_[l], d, dqkv_, W, Gq.c0[i], Gq.w[i], dh_, nullptr));
     const Param& g1 = P(pre + "attn_norm.weight");
-    CK(norm_bwd(x_[l], P32(g1), dx_, g1));
+    CK(norm_bwd(x_[l], P32(g1), dx_, g1, l > 0 ? 4 * (l - 1) : -1));
     CK(bucket_ready(layer_grad_lo_[l], false));   // this layer's gradients are final
   }
   CK(join_side());   // the embedding scatter adds to the LM head's (tied) gradient
@@ -2005,6 +2092,7 @@ int LlamaEngine::enqueue_backward() {
   CK(bucket_ready(0, true));
   CK(bucket_join());
   side_ = false;
+  if (f16w_) f16w_ready_ = true;   // the gradient slots hold this program's magnitudes
   return 0;
 }
 

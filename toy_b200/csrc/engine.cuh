@@ -82,6 +82,12 @@ int engine_set_side_gemm_tile_width(int bn);
 // such; 0 (default): every GEMM with the shared-GPU launch plan. Read when a session enqueues its step program.
 // Returns the previous setting, or -1.
 int engine_set_plan_alone(int on);
+// 1 (default): full fine-tunes realised afterwards compute their weight
+// gradients in one fp16 tensor-core pass (fp16 copies of the operands; the
+// gradients scaled per tensor by a power of two from the previous step's
+// largest magnitude); 0: three split-bf16 passes like every other product.
+// Returns the previous setting, or -1.
+int engine_set_f16_wgrad(int on);
 
 struct DeviceBuf {
   void* p = nullptr;
@@ -385,8 +391,29 @@ class LlamaEngine {
   // ring slot (l % 2) := block l on wst_, one block ahead of its use (the
   // slot's previous block is done on the step stream); dequant_layer waits
   int fill_ahead(int l);
-  // RMSNorm backward into dx / dxp; for a trainable gamma its column sum on wst_
-  int norm_bwd(const float* x, const float* gamma, const float* dres, const Param& gp);
+  // RMSNorm backward into dx / dxp; for a trainable gamma its column sum on wst_.
+  // slot16 >= 0: dxp's fp16 copy too, scaled by that gradient slot
+  int norm_bwd(const float* x, const float* gamma, const float* dres, const Param& gp, int slot16 = -1);
+  // One-pass fp16 weight gradients (full fine-tune): the fp16 copies hang off
+  // the operands' Planes (h1_, h2_, a_, O_, xf_, dlog_, dxp2_, dgu2_, dqkv2_).
+  // Gradient slot i (4 per layer: the down projection's dY, dgate|dup, the o
+  // projection's dY, dq|dk|dv; then dlogits) is written scaled by scale16_[i]
+  // and unscaled by the GEMM epilogue with inv16_[i]; the kernels that write a
+  // slot raise amax16_[i], from which the next step's scale is set.
+  bool f16w_ = false;
+  bool f16w_ready_ = false;   // a finished step has recorded the slots' magnitudes
+  int n16_ = 0;
+  unsigned* amax16_ = nullptr;
+  float *scale16_ = nullptr, *inv16_ = nullptr;
+  Planes grad16(Planes p, int slot) const {   // p with its fp16 copy scaled and measured as slot
+    if (!f16w_ || slot < 0) {
+      p.f16 = nullptr;
+      return p;
+    }
+    p.f16_scale = scale16_ + slot;
+    p.f16_amax = amax16_ + slot;
+    return p;
+  }
   float* du2_[2] = {nullptr, nullptr};
   float* lora_part2_ = nullptr;   // the side stream's weight-gradient partials
   // activations and scratch

@@ -65,6 +65,7 @@ struct FwdArgs {
   float scale_log2;
   bf16* o_hi;
   bf16* o_lo;
+  __half* o16;      // optional fp16 copy of O (same offsets)
   long long o_ld;   // token-major O row pitch
   float* lse2;
   int* err;
@@ -119,6 +120,20 @@ __device__ __forceinline__ void store_planes32(bf16* hi, bf16* lo, const float (
     split8(v, u, h, l);
     reinterpret_cast<uint4*>(hi)[u] = h;
     reinterpret_cast<uint4*>(lo)[u] = l;
+  }
+}
+
+// 32 values as fp16 (saturated to +-65504) at a 16-byte aligned address.
+__device__ __forceinline__ void store_f16x32(__half* dst, const float (&v)[32]) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    __align__(16) __half q[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float x = v[8 * u + k];
+      q[k] = __float2half_rn(x > 65504.f ? 65504.f : (x < -65504.f ? -65504.f : x));
+    }
+    reinterpret_cast<uint4*>(dst)[u] = *reinterpret_cast<const uint4*>(q);
   }
 }
 
@@ -385,6 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (qrow < a.T) {
         const long long off = (long long)(b * a.T + qrow) * a.o_ld + h * kDh + half * 32;
         store_planes32(a.o_hi + off, a.o_lo + off, o);
+        if (a.o16) store_f16x32(a.o16 + off, o);
         if (half == 0) a.lse2[(long long)bh * a.T + qrow] = mb + log2f(lt);
       }
     }
@@ -906,7 +922,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(tmem + lanes + kO2 + half * 64 + c * 32, o);
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[e] *= inv;
-        if (qrow < a.T) store_planes32(a.o_hi + off + c * 32, a.o_lo + off + c * 32, o);
+        if (qrow < a.T) {
+          store_planes32(a.o_hi + off + c * 32, a.o_lo + off + c * 32, o);
+          if (a.o16) store_f16x32(a.o16 + off + c * 32, o);
+        }
       }
       if (qrow < a.T && half == 0) a.lse2[(long long)bh * a.T + qrow] = mb + log2f(lt);
     }
@@ -1253,7 +1272,7 @@ int launch_flash_fwd(Planes Q, Planes K, Planes V, Planes O, float* lse2, int B,
   FwdArgs a;
   a.B = B; a.T = T; a.H = H; a.KV = KV; a.G = H / KV; a.nq = (T + kTile - 1) / kTile;
   a.scale_log2 = scale * 1.4426950408889634f;
-  a.o_hi = O.hi; a.o_lo = O.lo; a.o_ld = o_ld; a.lse2 = lse2; a.err = err;
+  a.o_hi = O.hi; a.o_lo = O.lo; a.o16 = O.f16; a.o_ld = o_ld; a.lse2 = lse2; a.err = err;
   const long long grid = (long long)a.nq * B * H;
   if (grid > 0x7fffffffLL) return -5;
   if (wide)

@@ -16,7 +16,8 @@ namespace tb2 {
 bool flash_supported(int dh);
 
 // O = softmax(scale * Q K^T + causal mask) V, and lse2. O is token-major,
-// rows o_ld apart (0: H dh).
+// rows o_ld apart (0: H dh); O.f16, when set, also gets an fp16 copy (no
+// scale) at the same offsets.
 int launch_flash_fwd(Planes Q, Planes K, Planes V, Planes O, float* lse2, int B, int T, int H, int KV, int dh,
                      float scale, int* err, cudaStream_t st, long long o_ld = 0);
 

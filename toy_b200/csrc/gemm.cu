@@ -60,6 +60,7 @@ struct KArgs {
   int a_bdiv1, a_bmul1, a_bdiv2, a_bmul2;
   int b_bdiv1, b_bmul1, b_bdiv2, b_bmul2;
   int tiles_m, tiles_n, splits, units, kb_total, causal;
+  int f16;   // operands are fp16 (one pass), not bf16
   Epilogue epi;
   float* ws;
   const int* gtab;   // grouped product: per M tile (group, first row, end row); null otherwise
@@ -153,8 +154,9 @@ __device__ __forceinline__ void epi_prefetch(const Epilogue& e, int N, long long
 // `pre` holds the addend loaded by epi_prefetch (used when the chunk is full).
 __device__ __forceinline__ void epi_store(const Epilogue& e, int N, long long off, int nc, float (&v)[32],
                                           const float4 (&pre)[8]) {
+  const float alpha = e.alpha_dev ? e.alpha * __ldg(e.alpha_dev) : e.alpha;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] *= e.alpha;
+  for (int i = 0; i < 32; ++i) v[i] *= alpha;
   const bool full_chunk = nc + 32 <= N;
   if (e.mode == kEpiStoreF32 || e.mode == kEpiAccumF32 || e.mode == kEpiResidF32 || e.mode == kEpiStoreBoth ||
       e.mode == kEpiStoreLse) {
@@ -563,7 +565,7 @@ __global__ void __launch_bounds__(threads_of<BN, Q8, FUSED>(), 1)
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0 && (!PAIR || rank == 0)) {
-      const uint32_t idesc = make_idesc_f16(BMT, BN, true, args.a_mn != 0, args.b_mn != 0);
+      const uint32_t idesc = make_idesc_f16(BMT, BN, args.f16 == 0, args.a_mn != 0, args.b_mn != 0);
       // K-major: advance 32 B per 16-element k-step inside the swizzle atom.
       // MN-major: advance 16 rows of 128 B; MN atoms are 64 rows (8 KB) apart.
       const uint32_t a_kstep = args.a_mn ? 2048u : 32u;
@@ -1119,6 +1121,7 @@ int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream
   k.tiles_n = (d.N + BN - 1) / BN;
   k.kb_total = (d.K + BK - 1) / BK;
   k.causal = d.causal;
+  k.f16 = d.f16 ? 1 : 0;
   const long long tiles = (long long)d.batch * k.tiles_m * k.tiles_n;
   if (splits < 1 || d.epi.mode == kEpiStoreLse || d.group_tiles) splits = 1;
   if (splits > k.kb_total) splits = k.kb_total;
@@ -1195,6 +1198,10 @@ int gemm_launch(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStre
   if ((e.m_s0 % al) || (e.m_s1 % al) || (e.n_s1 % al) || (e.bstride % al) || (e.z_s1 % al) || (e.n_div % 32))
     return -3;
   if (e.n_lora < 0 || e.n_lora > kMaxLoraAddends || (e.n_lora && e.alpha != 1.0f)) return -3;
+  // the device factor scales the plain stores only
+  if (e.alpha_dev && (e.n_lora || e.mode == kEpiRopeQKV || e.mode == kEpiSwiGLU || e.mode == kEpiStoreLse)) return -3;
+  // fp16 operands: one pass over plain (non-Q8_0) single planes
+  if (d.f16 && (d.split || d.b.q8)) return -4;
   for (int i = 0; i < e.n_lora; ++i) {
     const LoraAddend& L = e.lora[i];
     if (!L.u || !L.bt || L.r < 1 || L.c0 % 32 || L.width % 32 || L.c0 + L.width > d.N ||

@@ -91,6 +91,9 @@ struct RopeOut {
 struct Epilogue {
   int mode = kEpiStoreF32;
   float alpha = 1.0f;
+  // optional device factor: the epilogue's multiplier is alpha * *alpha_dev
+  // (the inverse of an operand scale that changes from step to step)
+  const float* alpha_dev = nullptr;
   float* out = nullptr;
   const float* res = nullptr;
   __nv_bfloat16* out_hi = nullptr;
@@ -118,6 +121,10 @@ struct Epilogue {
 struct GemmDesc {
   int M = 0, N = 0, K = 0, batch = 1;
   bool split = true;
+  // with split = false: the operands' hi arrays hold fp16 (not bf16) values,
+  // multiplied in one kind::f16 pass with fp16 inputs (the tensor maps copy
+  // 2-byte elements either way; zero fill is 0 in both formats)
+  bool f16 = false;
   int splits = 0;   // K ranges reduced through the workspace; 0 = choose from the tile count
   int causal = 0;   // 1: skip tiles with n0 > m0 + 127; 2: clamp K to m0 + 128 (zero beyond)
   int max_ctas = 0; // persistent CTAs at most (0: one per SM); the units are the same, walked by fewer CTAs

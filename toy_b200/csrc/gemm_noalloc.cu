@@ -70,9 +70,10 @@ int resolve(DevicePtrs* out) {
 
 extern "C" int tb2_gemm_noalloc(int M, int N, int K, int batch, int split, const tb2_operand* a, const tb2_operand* b,
                                 const tb2_epilogue* epi, int ksplits, int causal, void* stream) {
-  if (!a || !b || !epi || ksplits < 0) return -1;
+  if (!a || !b || !epi || ksplits < 0 || split < 0 || split > 2) return -1;
   tb2::GemmDesc d;
-  d.M = M; d.N = N; d.K = K; d.batch = batch; d.split = split != 0;
+  d.M = M; d.N = N; d.K = K; d.batch = batch; d.split = split == 1;
+  d.f16 = split == 2;
   d.splits = ksplits;
   d.causal = causal;
   auto cvt = [](const tb2_operand* o) {

@@ -23,15 +23,28 @@ __device__ __forceinline__ void split2(float x, bf16& h, bf16& l) {
   l = __float2bfloat16_rn(x - __bfloat162float(h));
 }
 
-__device__ __forceinline__ void store_planes(const Planes& p, long long i, float x) {
+// rn_f16(x) saturated to the largest finite magnitude (NaN stays NaN)
+__device__ __forceinline__ __half f16_sat(float x) {
+  return __float2half_rn(x > 65504.f ? 65504.f : (x < -65504.f ? -65504.f : x));
+}
+
+__device__ __forceinline__ float f16_scale_of(const Planes& p) { return p.f16_scale ? __ldg(p.f16_scale) : 1.0f; }
+
+// The store helpers take the fp16 copy's scale s as loaded once by the
+// kernel (f16_scale_of); the overloads without it load it per call.
+__device__ __forceinline__ void store_planes(const Planes& p, long long i, float x, float s) {
   bf16 h, l;
   split2(x, h, l);
   p.hi[i] = h;
   p.lo[i] = l;
+  if (p.f16) p.f16[i] = f16_sat(x * s);
+}
+__device__ __forceinline__ void store_planes(const Planes& p, long long i, float x) {
+  store_planes(p, i, x, p.f16 ? f16_scale_of(p) : 1.0f);
 }
 
-// Four consecutive values (i % 4 == 0) as two 8-byte stores.
-__device__ __forceinline__ void store_planes4(const Planes& p, long long i, float4 v) {
+// Four consecutive values (i % 4 == 0) as two 8-byte stores (three with the fp16 copy).
+__device__ __forceinline__ void store_planes4(const Planes& p, long long i, float4 v, float s) {
   __align__(8) bf16 h[4], l[4];
   split2(v.x, h[0], l[0]);
   split2(v.y, h[1], l[1]);
@@ -39,15 +52,39 @@ __device__ __forceinline__ void store_planes4(const Planes& p, long long i, floa
   split2(v.w, h[3], l[3]);
   *reinterpret_cast<uint2*>(p.hi + i) = *reinterpret_cast<const uint2*>(h);
   *reinterpret_cast<uint2*>(p.lo + i) = *reinterpret_cast<const uint2*>(l);
+  if (p.f16) {
+    __align__(8) __half q[4] = {f16_sat(v.x * s), f16_sat(v.y * s), f16_sat(v.z * s), f16_sat(v.w * s)};
+    *reinterpret_cast<uint2*>(p.f16 + i) = *reinterpret_cast<const uint2*>(q);
+  }
+}
+__device__ __forceinline__ void store_planes4(const Planes& p, long long i, float4 v) {
+  store_planes4(p, i, v, p.f16 ? f16_scale_of(p) : 1.0f);
 }
 
-// Two consecutive values (i % 2 == 0) as two 4-byte stores.
+// Two consecutive values (i % 2 == 0) as two 4-byte stores (three with the fp16 copy).
 __device__ __forceinline__ void store_planes2(const Planes& p, long long i, float a, float b) {
   __align__(4) bf16 h[2], l[2];
   split2(a, h[0], l[0]);
   split2(b, h[1], l[1]);
   *reinterpret_cast<uint32_t*>(p.hi + i) = *reinterpret_cast<const uint32_t*>(h);
   *reinterpret_cast<uint32_t*>(p.lo + i) = *reinterpret_cast<const uint32_t*>(l);
+  if (p.f16) {
+    const float s = f16_scale_of(p);
+    __align__(4) __half q[2] = {f16_sat(a * s), f16_sat(b * s)};
+    *reinterpret_cast<uint32_t*>(p.f16 + i) = *reinterpret_cast<const uint32_t*>(q);
+  }
+}
+
+__device__ __forceinline__ float amax4(float m, float4 v) {
+  return fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+}
+
+// Raise *amax to the warp's largest m (non-negative floats order like their
+// bits). Every lane of the warp calls it.
+__device__ __forceinline__ void flush_amax(unsigned* amax, float m) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0 && m > 0.f) atomicMax(amax, __float_as_uint(m));
 }
 
 __device__ __forceinline__ float4 load_planes4(const Planes& p, long long i) {
@@ -181,6 +218,8 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restric
     for (int c = lane; c < d4; c += 32) my[c] = f4_zero();
   __syncwarp();
   const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  float am = 0.f;   // max |dx| written (for the fp16 copy's scale)
+  const float s16 = dxp.f16 ? f16_scale_of(dxp) : 1.0f;
   for (int n = blockIdx.x * warps + warp; n < N; n += gridDim.x * warps) {
     const long long base = (long long)n * d;
     const float4* xr = reinterpret_cast<const float4*>(x + base);
@@ -215,7 +254,8 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restric
       o.z = rs.z + (gg.z * g.z - v.z * coef) * rr;
       o.w = rs.w + (gg.w * g.w - v.w * coef) * rr;
       out[c] = o;
-      if (dxp.hi) store_planes4(dxp, (long long)n * ldp + c * 4, o);
+      if (dxp.hi) store_planes4(dxp, (long long)n * ldp + c * 4, o, s16);
+      am = amax4(am, o);
       if (gpart) {
         float4 a = my[c];
         a.x += gg.x * v.x * rr;
@@ -226,6 +266,7 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restric
       }
     }
   }
+  if (dxp.f16_amax) flush_amax(dxp.f16_amax, am);
   if (!gpart) return;   // frozen gamma: no dgamma partials
   __syncthreads();
   for (int c = threadIdx.x; c < d4; c += blockDim.x) {
@@ -317,6 +358,8 @@ __global__ void __launch_bounds__(256) rope_qkv_bwd_kernel(const float* __restri
   const int slots = H + 2 * KV;
   const int width = slots * dh;
   const long long items = (long long)N * slots * h4;
+  float am = 0.f;   // max |dq|, |dk|, |dv| written
+  const float s16 = out.f16 ? f16_scale_of(out) : 1.0f;
   for (long long it = blockIdx.x * (long long)blockDim.x + threadIdx.x; it < items;
        it += (long long)gridDim.x * blockDim.x) {
     const int n = (int)(it / (slots * h4));
@@ -369,14 +412,16 @@ __global__ void __launch_bounds__(256) rope_qkv_bwd_kernel(const float* __restri
                        -g0.w * c3.y + g1.w * c3.x);
     }
     const long long dp = (long long)n * ldo + slot * dh + j;
-    store_planes4(out, dp, y0);
-    store_planes4(out, dp + half, y1);
+    store_planes4(out, dp, y0, s16);
+    store_planes4(out, dp + half, y1, s16);
+    am = amax4(amax4(am, y0), y1);
     if (out_f32) {
       const long long dst = (long long)n * width + slot * dh + j;
       *reinterpret_cast<float4*>(out_f32 + dst) = y0;
       *reinterpret_cast<float4*>(out_f32 + dst + half) = y1;
     }
   }
+  if (out.f16_amax) flush_amax(out.f16_amax, am);
 }
 
 // ------------------------------------------------------------------ attention softmax
@@ -500,6 +545,8 @@ __global__ void __launch_bounds__(128) swiglu_bwd_kernel(const float* __restrict
                                                          Planes dgu, long long ldo, int N, int ff) {
   griddep_wait();
   const int ff4 = ff / 4;
+  float am = 0.f;   // max |dgate|, |dup| written
+  const float s16 = dgu.f16 ? f16_scale_of(dgu) : 1.0f;
   for (int n = blockIdx.x; n < N; n += gridDim.x) {
     const float4* g4 = reinterpret_cast<const float4*>(gu + (long long)n * 2 * ff);
     const float4* u4 = g4 + ff4;
@@ -511,10 +558,12 @@ __global__ void __launch_bounds__(128) swiglu_bwd_kernel(const float* __restrict
       swiglu_back1(g.y, u.y, dy.y, dg.y, du.y);
       swiglu_back1(g.z, u.z, dy.z, dg.z, du.z);
       swiglu_back1(g.w, u.w, dy.w, dg.w, du.w);
-      store_planes4(dgu, (long long)n * ldo + 4 * c, dg);
-      store_planes4(dgu, (long long)n * ldo + ff + 4 * c, du);
+      store_planes4(dgu, (long long)n * ldo + 4 * c, dg, s16);
+      store_planes4(dgu, (long long)n * ldo + ff + 4 * c, du, s16);
+      am = amax4(amax4(am, dg), du);
     }
   }
+  if (dgu.f16_amax) flush_amax(dgu.f16_amax, am);
 }
 
 // ------------------------------------------------------------------ cross-entropy
@@ -537,6 +586,7 @@ __global__ void __launch_bounds__(kCeThreads) cross_entropy_kernel(const float* 
   __shared__ float bc[2];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const float invN = 1.0f / (float)N;
+  const float s16 = dl.f16 ? f16_scale_of(dl) : 1.0f;
   const bool vec = (V % 4) == 0;
   for (int n = blockIdx.x; n < N; n += gridDim.x) {
     const float* z = logits + (long long)n * V;
@@ -593,7 +643,7 @@ __global__ void __launch_bounds__(kCeThreads) cross_entropy_kernel(const float* 
         if (k == 1) g.y -= 1.0f;
         if (k == 2) g.z -= 1.0f;
         if (k == 3) g.w -= 1.0f;
-        store_planes4(dl, (long long)n * V + 4 * v, make_float4(g.x * invN, g.y * invN, g.z * invN, g.w * invN));
+        store_planes4(dl, (long long)n * V + 4 * v, make_float4(g.x * invN, g.y * invN, g.z * invN, g.w * invN), s16);
       }
     } else {
       for (int v = threadIdx.x; v < V; v += blockDim.x) {
@@ -605,7 +655,7 @@ __global__ void __launch_bounds__(kCeThreads) cross_entropy_kernel(const float* 
         } else if (v == lab) {
           y = 1.0f;
         }
-        store_planes(dl, (long long)n * V + v, (expf(x - M) * inv - y) * invN);
+        store_planes(dl, (long long)n * V + v, (expf(x - M) * inv - y) * invN, s16);
       }
     }
     if (label_dense) {
@@ -659,6 +709,7 @@ __global__ void __launch_bounds__(kCeThreads) cross_entropy_grad_kernel(const fl
                                                                         int N, int V) {
   griddep_wait();
   const float invN = 1.0f / (float)N;
+  const float s16 = dl.f16 ? f16_scale_of(dl) : 1.0f;
   for (int n = blockIdx.x; n < N; n += gridDim.x) {
     const float2 st = ms[n];
     const float M = st.x, inv = 1.0f / st.y;
@@ -675,13 +726,34 @@ __global__ void __launch_bounds__(kCeThreads) cross_entropy_grad_kernel(const fl
         if (k == 1) g.y -= 1.0f;
         if (k == 2) g.z -= 1.0f;
         if (k == 3) g.w -= 1.0f;
-        store_planes4(dl, (long long)n * V + 4 * v, make_float4(g.x * invN, g.y * invN, g.z * invN, g.w * invN));
+        store_planes4(dl, (long long)n * V + 4 * v, make_float4(g.x * invN, g.y * invN, g.z * invN, g.w * invN), s16);
       }
     } else {
       for (int v = threadIdx.x; v < V; v += blockDim.x)
-        store_planes(dl, (long long)n * V + v, (expf(z[v] - M) * inv - (v == lab ? 1.0f : 0.0f)) * invN);
+        store_planes(dl, (long long)n * V + v, (expf(z[v] - M) * inv - (v == lab ? 1.0f : 0.0f)) * invN, s16);
     }
     if (threadIdx.x == 0) loss_rows[n] = lab >= 0 ? M + logf(st.y) - z[lab] : 0.f;
+  }
+}
+
+// Per gradient slot: the power-of-two scale of this step's fp16 copies from
+// the largest magnitude the previous step wrote (amax * scale < 2^12, a 16x
+// margin below the fp16 range) and its inverse for the GEMM epilogue; then the
+// slot's record is cleared for this step. A slot without a finite positive
+// record keeps its scale.
+__global__ void f16_scale_update_kernel(unsigned* amax, float* scale, float* inv, int n) {
+  griddep_wait();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const float a = __uint_as_float(amax[i]);
+    if (a > 0.f && a <= 3.0e38f) {
+      int e;
+      frexpf(a, &e);   // a < 2^e
+      int k = 12 - e;
+      k = k < -126 ? -126 : (k > 126 ? 126 : k);
+      scale[i] = ldexpf(1.0f, k);
+      inv[i] = ldexpf(1.0f, -k);
+    }
+    amax[i] = 0u;
   }
 }
 
@@ -1294,6 +1366,12 @@ int launch_cross_entropy_lse(const float* logits, const float2* lse_part, float2
   const int g = N < 4 * kSMs ? N : 4 * kSMs;
   launch_pdl(cross_entropy_grad_kernel, dim3(g), dim3(kCeThreads), 0, st, logits, (const float2*)ms, label_ids,
              loss_rows, dlogits, N, V);
+  return ok();
+}
+
+int launch_f16_scale_update(unsigned* amax, float* scale, float* inv, int n, cudaStream_t st) {
+  if (n <= 0) return 0;
+  launch_pdl(f16_scale_update_kernel, dim3((n + 255) / 256), dim3(256), 0, st, amax, scale, inv, n);
   return ok();
 }
 

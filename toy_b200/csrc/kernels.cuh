@@ -3,6 +3,7 @@
 // arrays carrying an f32 value as hi + lo (see gemm.cuh).
 #pragma once
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -13,6 +14,14 @@ using bf16 = __nv_bfloat16;
 struct Planes {
   bf16* hi = nullptr;
   bf16* lo = nullptr;
+  // Optional fp16 copy of the same values at the same element offsets (the
+  // operands of one-pass fp16 weight-gradient GEMMs): f16[i] = rn_f16(x *
+  // *f16_scale), saturated to +-65504 (no scale pointer: x itself). Kernels
+  // that write gradients also raise *f16_amax to max |x| of what they wrote
+  // (unscaled, as f32 bits) when it is set.
+  __half* f16 = nullptr;
+  const float* f16_scale = nullptr;
+  unsigned* f16_amax = nullptr;
 };
 
 // hi = rn_bf16(x), lo = rn_bf16(x - hi)
@@ -93,6 +102,10 @@ int launch_cross_entropy(const float* logits, const int* label_ids, const float*
 // writes the gradient planes and loss rows.
 int launch_cross_entropy_lse(const float* logits, const float2* lse_part, float2* ms, const int* label_ids,
                              float* loss_rows, Planes dlogits, int N, int V, cudaStream_t st);
+// Gradient slots of the fp16 weight-gradient operands: scale[i] = 2^k with
+// amax[i] * 2^k < 2^12 from the record of the previous step (kept when there
+// is none), inv[i] = 2^-k, then amax[i] = 0.
+int launch_f16_scale_update(unsigned* amax, float* scale, float* inv, int n, cudaStream_t st);
 // loss = sum(loss_rows) / N   (single block, fixed order)
 int launch_loss_reduce(const float* loss_rows, int N, float* loss, cudaStream_t st);
 
