@@ -73,9 +73,46 @@ MODEL_NAMES = {"smollm2": "SmolLM2-135M shape", "llama32_1b": "Llama-3.2-1B shap
 # bound on writes, exact on reads.
 GEMM_TRAFFIC = {
     "smollm2_full_ft_b8_t512": {"bytes_per_step": 14233990912, "launches": 363,
-                                "algorithmic_bytes_per_step": 17081303040,
                                 "source": "ncu, full workload, -s 272 -c 900 (one complete step)"},
 }
+
+
+def gemm_algorithmic_bytes(cfg, N, f16_wgrad):
+    """Operand and output bytes of one full fine-tune step's GEMMs (dense Llama, fused
+    flash attention): each operand read once (split planes 4 bytes per element, fp16
+    weight-gradient operands 2), each f32 output written once, residual addends read."""
+    d, H, KV, dh, ff, L, V = cfg.d_model, cfg.n_heads, cfg.n_kv, cfg.d_head, cfg.d_ff, cfg.n_layers, cfg.vocab
+    W = (H + 2 * KV) * dh
+    pl, f32 = 4, 4
+    wg = 2 if f16_wgrad else 4
+
+    def g(m_rows, k_cols, n_rows, out, a_b=pl, res=0):   # A [M][K], B [N][K], output bytes
+        return a_b * (m_rows * k_cols + n_rows * k_cols) + out + res
+    per_layer = (
+        g(N, d, W, N * W * pl)                              # q|k|v (+ RoPE, head-major planes)
+        + g(N, H * dh, d, N * d * f32, res=N * d * f32)     # o (+ residual)
+        + g(N, d, 2 * ff, N * 2 * ff * f32)                 # gate|up
+        + g(N, ff, d, N * d * f32, res=N * d * f32)         # down (+ residual)
+        + g(N, d, ff, N * ff * f32)                         # dX down
+        + g(N, 2 * ff, d, N * d * f32)                      # dX gate|up
+        + g(N, d, H * dh, N * H * dh * f32)                 # dX o
+        + g(N, W, d, N * d * f32)                           # dX q|k|v
+        + g(d, N, ff, d * ff * f32, a_b=wg)                 # dW down
+        + g(2 * ff, N, d, 2 * ff * d * f32, a_b=wg)         # dW gate|up
+        + g(d, N, H * dh, d * H * dh * f32, a_b=wg)         # dW o
+        + g(W, N, d, W * d * f32, a_b=wg))                  # dW q|k|v
+    head = (g(N, d, V, N * V * f32)                         # LM head (logits)
+            + g(N, V, d, N * d * f32)                       # dX of the LM head
+            + g(V, N, d, V * d * f32, a_b=wg))              # dW of the LM head
+    return L * per_layer + head
+
+
+def f16_wgrad_on():
+    """The library's fp16 weight-gradient setting (read by setting it back)."""
+    from toy_b200._lib import lib
+    prev = lib().tb2_set_f16_wgrad(1)
+    lib().tb2_set_f16_wgrad(prev)
+    return prev == 1
 
 
 def peaks():
@@ -434,10 +471,15 @@ def main():
         cpu = {"value": v, "unit": "tokens/s", "cores": cores(), "kind": "port", "sample": cpu_sample_text(wl, nsteps)}
     tot = sum(r["per_kind"].values())
     traffic = GEMM_TRAFFIC.get(args.workload) if not (args.layers or args.batch) else None
+    f16w = wl["mode"] == 0 and f16_wgrad_on()
+    alg_bytes = gemm_algorithmic_bytes(cfg, tokens // world, f16w) if traffic else None
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32 (tensor-core products on split-bf16 pairs, f32 accumulate)",
+        "vs_baseline": None,
+        "dtype": "f32 (tensor-core products on split-bf16 pairs, f32 accumulate" +
+                 ("; weight gradients: one fp16 pass, gradients scaled per tensor by a power of two)" if f16w
+                  else ")"),
         "data": "synthetic (uniform ids, seeded init)",
         "config": {"workload": args.workload, "model": MODEL_NAMES[wl.get("model", "smollm2")], "global_batch": B * world,
                    "seq_len": T, "parallelism": f"dp{world}", "tokens_per_step": tokens,
@@ -455,9 +497,10 @@ def main():
                      "traffic_note": (f"mean DRAM bytes per GEMM launch (ncu dram__bytes_read+write over "
                                       f"{traffic['launches']} GEMM launches of one step, {traffic['source']}); "
                                       f"algorithmic operand+output bytes per launch "
-                                      f"{traffic['algorithmic_bytes_per_step'] / r['gemm_n']:.3e}")
+                                      f"{alg_bytes / r['gemm_n']:.3e}")
                      if traffic else None,
-                     "gemm_launches_per_step": r["gemm_n"], "mma_passes": 3,
+                     "gemm_launches_per_step": r["gemm_n"],
+                     "mma_passes": "3 (forward, dX), 1 fp16 (dW)" if f16w else 3,
                      "peak_source": f"bf16 sustained, {src}"},
         "kernel_ms": {k: round(v, 4) for k, v in sorted(r["per_kind"].items(), key=lambda kv: -kv[1])},
         "kernel_share": {k: round(v / tot, 4) for k, v in r["per_kind"].items()} if tot > 0 else {},

@@ -1688,7 +1688,7 @@ int LlamaEngine::enqueue_forward() {
     const float* bias = c.qkv_bias ? P32(P(pre + "attn_q.bias")) : nullptr;
     const int qkv_t[3] = {kLoraQ, kLoraK, kLoraV};
     const int qkv_c0[3] = {0, H * dh, (H + KV) * dh}, qkv_w[3] = {H * dh, KV * dh, KV * dh};
-    if (dh == 64 && !c.qk_norm) {
+    if ((dh == 64 || dh == 128) && !c.qk_norm) {
       // one launch: q|k|v projection, adapters, bias, RoPE, head-major Q / K / V planes
       g.epi.mode = kEpiRopeQKV;
       RopeOut& ro = g.epi.rope;

@@ -755,8 +755,12 @@ __global__ void __launch_bounds__(threads_of<BN, Q8, FUSED>(), 1)
       const bool row_ok = ok && row_in;
       const uint32_t acc_tmem = tmem_base + b * kAccCols + ((uint32_t)(q * 32) << 16);
       if constexpr (FUSED) {
-        if (e.mode == kEpiRopeQKV) {
-          epi_rope<BN, 2, PAIR>(e, m, w.n0, row_ok, args.N, acc_tmem, &tempty[b], lane);
+        if (e.mode == kEpiRopeQKV) {   // whole heads of 64 or 128 columns per tile
+          if (e.rope.dh == 64) {
+            epi_rope<BN, 2, PAIR>(e, m, w.n0, row_ok, args.N, acc_tmem, &tempty[b], lane);
+          } else if constexpr (BN % 128 == 0) {
+            epi_rope<BN, 4, PAIR>(e, m, w.n0, row_ok, args.N, acc_tmem, &tempty[b], lane);
+          }
           continue;
         }
         if (e.mode == kEpiSwiGLU) {
@@ -1221,7 +1225,6 @@ int gemm_launch(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStre
   } else if (e.pair_off) {
     return -3;
   }
-  if (e.mode == kEpiRopeQKV && e.rope.dh != 64) return -3;
   if (e.mode == kEpiStoreLse && (!e.lse_part || e.alpha != 1.0f || d.batch != 1 || e.m_div != (1 << 30) ||
                                  e.n_div != (1 << 30) || d.b.q8))
     return -3;

@@ -80,11 +80,14 @@ __device__ __forceinline__ float amax4(float m, float4 v) {
 }
 
 // Raise *amax to the warp's largest m (non-negative floats order like their
-// bits). Every lane of the warp calls it.
+// bits). Every lane of the warp calls it. Thousands of warps end on the same
+// word: a warp whose maximum the word already holds skips the atomic, so the
+// atomics do not queue up on it.
 __device__ __forceinline__ void flush_amax(unsigned* amax, float m) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if ((threadIdx.x & 31) == 0 && m > 0.f) atomicMax(amax, __float_as_uint(m));
+  if ((threadIdx.x & 31) == 0 && m > 0.f && *reinterpret_cast<volatile unsigned*>(amax) < __float_as_uint(m))
+    atomicMax(amax, __float_as_uint(m));
 }
 
 __device__ __forceinline__ float4 load_planes4(const Planes& p, long long i) {
@@ -225,14 +228,17 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restric
     const float4* xr = reinterpret_cast<const float4*>(x + base);
     const float4* hr = reinterpret_cast<const float4*>(dh + base);
     const float4* rres = dres ? reinterpret_cast<const float4*>(dres + base) : nullptr;
-    float4 xv[NC], hv[NC], rv[NC];
+    // x and dh in registers; the residual gradient is read where it is added
+    // (in the first round of loads while the row is short, NC <= 8)
+    constexpr bool kRvEarly = NC <= 8;
+    float4 xv[NC], hv[NC], rv[kRvEarly ? NC : 1];
     float sxx = 0.f, sxdz = 0.f;
 #pragma unroll
-    for (int i = 0; i < NC; ++i) {   // x, dh and the residual gradient in one round of loads
+    for (int i = 0; i < NC; ++i) {
       const int c = lane + 32 * i;
       xv[i] = c < d4 ? xr[c] : f4_zero();
       hv[i] = c < d4 ? __ldcs(hr + c) : f4_zero();
-      rv[i] = (rres && c < d4) ? rres[c] : f4_zero();
+      if constexpr (kRvEarly) rv[i] = (rres && c < d4) ? rres[c] : f4_zero();
       const float4 g = c < d4 ? g4[c] : f4_zero();
       sxx += xv[i].x * xv[i].x + xv[i].y * xv[i].y + xv[i].z * xv[i].z + xv[i].w * xv[i].w;
       sxdz += xv[i].x * hv[i].x * g.x + xv[i].y * hv[i].y * g.y + xv[i].z * hv[i].z * g.z + xv[i].w * hv[i].w * g.w;
@@ -247,7 +253,9 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restric
       const int c = lane + 32 * i;
       if (c >= d4) continue;
       const float4 v = xv[i], gg = hv[i], g = g4[c];
-      const float4 rs = rv[i];
+      float4 rs;
+      if constexpr (kRvEarly) rs = rv[i];
+      else rs = rres ? rres[c] : f4_zero();
       float4 o;
       o.x = rs.x + (gg.x * g.x - v.x * coef) * rr;
       o.y = rs.y + (gg.y * g.y - v.y * coef) * rr;
