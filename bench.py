@@ -64,16 +64,16 @@ MODEL_NAMES = {"smollm2": "SmolLM2-135M shape", "llama32_1b": "Llama-3.2-1B shap
 
 # DRAM traffic of the step's GEMM launches, from one ncu capture of the full
 # workload (dram__bytes_read.sum + dram__bytes_write.sum summed over the 363
-# GEMM launches of one step, one pass per launch; the summary and its command
-# are in profiles/launches_dram_smollm2_full_ft_b8_t512.md). The algorithmic
-# bytes are each GEMM's operands (split planes, 4 bytes per element) plus its
-# output and residual addend, summed over the step's GEMMs. ncu writes back and
+# GEMM launches of one graph-replayed step, one pass per launch; the summary
+# and its command are in profiles/launches_dram_smollm2_full_ft_b8_t512.md).
+# The algorithmic bytes (gemm_algorithmic_bytes) are each GEMM's operands plus
+# its output and residual addend, summed over the step's GEMMs. ncu writes back and
 # invalidates L2 between captured kernels, so an output that still sits in L2
 # when its kernel ends is not counted as a DRAM write: the traffic is a lower
 # bound on writes, exact on reads.
 GEMM_TRAFFIC = {
-    "smollm2_full_ft_b8_t512": {"bytes_per_step": 14233990912, "launches": 363,
-                                "source": "ncu, full workload, -s 272 -c 900 (one complete step)"},
+    "smollm2_full_ft_b8_t512": {"bytes_per_step": 11705450240, "launches": 363,
+                                "source": "ncu, full workload, -s 272 -c 2000, the second step (a graph replay)"},
 }
 
 

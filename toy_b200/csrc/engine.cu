@@ -1019,11 +1019,11 @@ void LlamaEngine::prof_end() {
 }
 
 int LlamaEngine::gemm(const GemmDesc& d0) {
-  ++counting_;
   if (profiling_) prof_begin(kKGemm, 2.0 * d0.M * d0.N * d0.K * d0.batch);
   GemmDesc d = d0;
   d.alone = d0.alone || (gemm_alone_ && g_plan_alone);
   const int rc = gemm_launch(d, gemm_scratch(), err_, stream_);
+  counting_ += gemm_last_launches();
   if (profiling_) prof_end();
   if (rc) fprintf(stderr, "[toy_b200] gemm launch rejected (%d): M=%d N=%d K=%d batch=%d\n", rc, d.M, d.N, d.K, d.batch);
   return rc;
@@ -1031,11 +1031,11 @@ int LlamaEngine::gemm(const GemmDesc& d0) {
 
 int LlamaEngine::gemm_side(const GemmDesc& d0) {
   if (!side_ || !wsc_.ws) return gemm(d0);
-  ++counting_;
   GemmDesc d = d0;
   d.max_ctas = g_side_gemm_ctas;
   d.tile_bn = g_side_gemm_bn;
   const int rc = gemm_launch(d, wsc_.ws ? wsc_ : gemm_scratch(), err_, wst_);
+  counting_ += gemm_last_launches();
   if (rc) fprintf(stderr, "[toy_b200] gemm launch rejected (%d): M=%d N=%d K=%d batch=%d\n", rc, d.M, d.N, d.K, d.batch);
   return rc;
 }
@@ -1806,6 +1806,7 @@ int LlamaEngine::enqueue_forward() {
     gl.epi.lse_part = lse_part_;
     CK(gemm(gl));
     KL(launch_cross_entropy_lse(logits_, lse_part_, lse_ms_, labels_, loss_rows_, dlog_, N, V, stream_));
+    ++counting_;   // (two kernels: the logsumexp combine and the gradient pass)
   } else {
     CK(gemm(gl));
     KL(launch_cross_entropy(logits_, labels_, labels_dense_, loss_rows_, dlog_, N, V, stream_));

@@ -54,6 +54,10 @@ __host__ __device__ constexpr int threads_of() {
   return 64 + 32 * epi_warps<BN, Q8, FUSED>() + (Q8 ? 32 * kConvWarps : 0);
 }
 
+// kernels the calling thread's last gemm_launch enqueued (the product, and
+// the split-K reduction when there is one)
+thread_local int t_last_launches = 0;
+
 struct KArgs {
   int M, N, K, batch;
   int a_mn, b_mn;
@@ -1154,12 +1158,14 @@ int launch_bn(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream
                    k) != 0)
       return -21;
   }
+  t_last_launches = 1;
   if (splits > 1) {
     const long long work = (long long)d.M * ((d.N + 31) / 32);
     long long blocks = (work + 127) / 128;
     if (blocks > 8 * kNumSMs) blocks = 8 * kNumSMs;
     if (launch_pdl(splitk_reduce_kernel, dim3((int)blocks), dim3(128), 0, stream, sc.ws, splits, d.M, d.N, d.epi) != 0)
       return -21;
+    t_last_launches = 2;
   }
   return 0;
 }
@@ -1191,7 +1197,10 @@ int gemm_effective_splits(const GemmDesc& d, int ksplits) {
   return ksplits < kb ? ksplits : kb;
 }
 
+int gemm_last_launches() { return t_last_launches; }
+
 int gemm_launch(const GemmDesc& d, const GemmScratch& sc, int* dev_err, cudaStream_t stream) {
+  t_last_launches = 0;
   if (d.M <= 0 || d.N <= 0 || d.K <= 0 || d.batch <= 0) return -1;
   if (d.causal < 0 || d.causal > 2) return -1;
   if (d.group_tiles && (d.group_mtiles < 1 || d.causal || d.batch != 1 || d.a.mn_major)) return -1;

@@ -152,6 +152,9 @@ struct GemmScratch {
 // shape/alignment (nothing launched). `dev_err` is a device int the kernel sets
 // to a DeviceError code if one of its bounded waits gives up.
 int gemm_launch(const GemmDesc& d, const GemmScratch& scratch, int* dev_err, cudaStream_t stream);
+// Kernels the calling thread's last gemm_launch enqueued: 1, or 2 with a
+// split-K reduction (0 after a rejected call).
+int gemm_last_launches();
 // The number of K splits gemm_launch runs for an explicit request of
 // `ksplits` (d.splits is ignored): 1 when the shape allows no split (causal,
 // batched, fused or logsumexp epilogues), else ksplits capped at the k-block
