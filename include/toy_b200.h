@@ -155,11 +155,12 @@ int tb2_set_q8_base_mode(int mode);
 int tb2_set_q8_ring_l2(int on);
 
 /* Persistent CTAs of each weight-gradient GEMM the step runs on its second
- * stream: 0 (the default) one per SM; n > 0 at most n, the same tiles and K
- * splits walked by fewer CTAs so that more SMs stay with the activation
- * gradient chain. Results are identical. Read when a session enqueues its
- * step program (its first step, which also captures the step's CUDA graph).
- * No counterpart in the reference.
+ * stream: 0 (the default) 100 for the one-pass fp16 weight gradients of a
+ * full fine-tune, one per SM otherwise; n > 0 at most n (148: one per SM),
+ * the same tiles and K splits walked by fewer CTAs so that more SMs stay with
+ * the activation gradient chain. Results are identical. Read when a session
+ * enqueues its step program (its first step, which also captures the step's
+ * CUDA graph). No counterpart in the reference.
  * Returns the previous setting, or -1 for n outside 0..148. */
 int tb2_set_side_gemm_ctas(int n);
 

@@ -26,6 +26,9 @@ namespace tb2 {
 
 int g_q8_base_mode = 1;
 int g_ring_l2 = 1;
+// 0: 100 CTAs for the one-pass fp16 weight gradients of a full fine-tune
+// (measured in the step: 231.3k-233.7k tokens/s at 88-112 CTAs against 227.5k
+// uncapped; 225.2k at 124, 223.0k at 40), one per SM otherwise
 int g_side_gemm_ctas = 0;
 int g_plan_alone = 0;   // measured neutral for QLoRA (270.4k alone vs 270.8k shared, two runs each)
 int engine_set_plan_alone(int on) {
@@ -1032,7 +1035,7 @@ int LlamaEngine::gemm(const GemmDesc& d0) {
 int LlamaEngine::gemm_side(const GemmDesc& d0) {
   if (!side_ || !wsc_.ws) return gemm(d0);
   GemmDesc d = d0;
-  d.max_ctas = g_side_gemm_ctas;
+  d.max_ctas = g_side_gemm_ctas > 0 ? g_side_gemm_ctas : (f16w_ ? 100 : 0);
   d.tile_bn = g_side_gemm_bn;
   const int rc = gemm_launch(d, wsc_.ws ? wsc_ : gemm_scratch(), err_, wst_);
   counting_ += gemm_last_launches();

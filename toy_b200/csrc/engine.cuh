@@ -71,9 +71,10 @@ int engine_set_q8_base_mode(int mode);
 // setting, or -1.
 int engine_set_q8_ring_l2(int on);
 // Persistent CTAs of each weight-gradient GEMM on the second stream of engines
-// realised afterwards: 0 (default) one per SM, n > 0 at most n (the same work
-// walked by fewer CTAs, leaving SMs to the activation chain). Returns the
-// previous setting, or -1.
+// realised afterwards: 0 (default) 100 for a full fine-tune's one-pass fp16
+// weight gradients and one per SM otherwise, n > 0 at most n (148: one per
+// SM; the same work walked by fewer CTAs, leaving SMs to the activation
+// chain). Returns the previous setting, or -1 for n outside 0..148.
 int engine_set_side_gemm_ctas(int n);
 // Output tile width of the weight-gradient GEMMs on the second stream (0: the
 // launch plan's choice). Returns the previous width, or -1.
