@@ -24,19 +24,22 @@ def _free_port():
     return p
 
 
-def _cfgs():
+def _cfgs(dh=32):
+    """d_head 32: the materialised attention and three-pass weight gradients; d_head 64:
+    the fused attention and the one-pass fp16 weight gradients (each rank scaling its own)."""
     from toy_b200 import LlamaConfig
-    oc = O.LlamaCfg(vocab=512, d_model=128, n_heads=4, n_kv=2, d_head=32, d_ff=256, n_layers=2, rope_base=1e4)
-    return oc, LlamaConfig(512, 128, 4, 2, 32, 256, 2, 1e4, 1e-5)
+    d = 4 * dh
+    oc = O.LlamaCfg(vocab=512, d_model=d, n_heads=4, n_kv=2, d_head=dh, d_ff=256, n_layers=2, rope_base=1e4)
+    return oc, LlamaConfig(512, d, 4, 2, dh, 256, 2, 1e4, 1e-5)
 
 
-def _rank(rank, world, port, q, bucket):
+def _rank(rank, world, port, q, bucket, dh=32):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     from toy_b200 import FromScratch, RecipeOptions
     from toy_b200.parallel import DataParallel
-    oc, gc = _cfgs()
+    oc, gc = _cfgs(dh)
     T = 64
     dp = DataParallel(rank, world, rank, timeout_s=120)
     rec = FromScratch(device=rank)
@@ -52,15 +55,15 @@ def _rank(rank, world, port, q, bucket):
     rec.fs_cache.close()
 
 
-@pytest.mark.parametrize("bucket", [None, 4096])
-def test_dp2_matches_joined_batch(cuda, bucket):
+@pytest.mark.parametrize("bucket,dh", [(None, 32), (4096, 32), (4096, 64)])
+def test_dp2_matches_joined_batch(cuda, bucket, dh):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_rank, args=(r, 2, port, q, bucket)) for r in range(2)]
+    ps = [ctx.Process(target=_rank, args=(r, 2, port, q, bucket, dh)) for r in range(2)]
     for p in ps:
         p.start()
     res = sorted((q.get(timeout=300) for _ in range(2)), key=lambda r: r[0])
@@ -68,7 +71,7 @@ def test_dp2_matches_joined_batch(cuda, bucket):
         p.join(timeout=120)
         assert p.exitcode == 0
     from toy_b200 import FromScratch, RecipeOptions
-    oc, gc = _cfgs()
+    oc, gc = _cfgs(dh)
     T = 64
     rec = FromScratch(device=0)
     rec.realize(gc, RecipeOptions(t_seq=T, t_batch=2, seed=3))
