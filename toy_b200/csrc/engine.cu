@@ -915,19 +915,32 @@ int LlamaEngine::set_tokens(const long long* ids, int n) {
     if (ids[i] < 0 || ids[i] >= V) return -1;
     h[i] = (int)ids[i];
   }
-  // rows grouped by id (stable), for the deterministic embedding scatter-add
-  std::vector<int> cnt;
-  std::vector<std::pair<int, int>> kv(n);
-  for (int i = 0; i < n; ++i) kv[i] = {h[i], i};
-  std::stable_sort(kv.begin(), kv.end(), [](auto a, auto b) { return a.first < b.first; });
+  // rows grouped by id, in row order within an id (the deterministic
+  // embedding scatter-add): a stable LSD radix sort of the row indices by id,
+  // one pass per byte of the largest id (linear in n)
   int* ord = h + n;
   int* sid = h + 2 * n;
   int* sst = h + 3 * n;
+  {
+    std::vector<int>& tmp = sort_tmp_;
+    tmp.resize(n);
+    for (int i = 0; i < n; ++i) ord[i] = i;
+    int* src = ord;
+    int* dst = tmp.data();
+    for (int shift = 0; shift < 32 && (shift == 0 || (V - 1) >> shift); shift += 8) {
+      int count[257] = {0};
+      for (int i = 0; i < n; ++i) ++count[((h[src[i]] >> shift) & 255) + 1];
+      for (int d = 0; d < 256; ++d) count[d + 1] += count[d];
+      for (int i = 0; i < n; ++i) dst[count[(h[src[i]] >> shift) & 255]++] = src[i];
+      std::swap(src, dst);
+    }
+    if (src != ord) std::copy(src, src + n, ord);
+  }
   int ns = 0;
   for (int i = 0; i < n; ++i) {
-    ord[i] = kv[i].second;
-    if (i == 0 || kv[i].first != kv[i - 1].first) {
-      sid[ns] = kv[i].first;
+    const int id = h[ord[i]];
+    if (i == 0 || id != h[ord[i - 1]]) {
+      sid[ns] = id;
       sst[ns] = i;
       ++ns;
     }

@@ -439,6 +439,7 @@ class LlamaEngine {
   float *labels_dense_ = nullptr, *hp_ = nullptr, *cs_ = nullptr;
   int cs_rows_ = 0, nseg_ = 0;
   bool dense_labels_ = false;
+  std::vector<int> sort_tmp_;   // set_tokens' radix-sort buffer
   // host staging (pinned)
   void* stage_ = nullptr;
   size_t stage_bytes_ = 0;
