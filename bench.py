@@ -5,7 +5,7 @@ backward + AdamW) on B200s, with the step's roofline fraction.
 Default workload (one GPU): SmolLM2-135M shape, full f32 fine-tune with every
 weight N(0, 0.02), B=8 sequences of T=512 tokens per GPU, data-parallel over N
 GPUs (weak scaling). The same line carries the QLoRA workload (q, v adapters
-over a frozen Q8_0 base, B=8 T=512) as `north_star_qlora`. Synthetic data:
+over a frozen Q8_0 base, B=8 T=512) as `qlora_step`. Synthetic data:
 token ids uniform in [0, vocab), labels = ids shifted by one inside each
 sequence, weights from the reference's seeded init stream.
 
@@ -64,8 +64,8 @@ MODEL_NAMES = {"smollm2": "SmolLM2-135M shape", "llama32_1b": "Llama-3.2-1B shap
 
 # DRAM traffic of the step's GEMM launches, from one ncu capture of the full
 # workload (dram__bytes_read.sum + dram__bytes_write.sum summed over the 363
-# GEMM launches of one graph-replayed step, one pass per launch; the summary
-# and its command are in profiles/launches_dram_smollm2_full_ft_b8_t512.md).
+# GEMM launches of one graph-replayed step, one pass per launch; ncu with
+# gpu__time_duration, dram__bytes_read and dram__bytes_write, -s 272 -c 2000).
 # The algorithmic bytes (gemm_algorithmic_bytes) are each GEMM's operands plus
 # its output and residual addend, summed over the step's GEMMs. ncu writes back and
 # invalidates L2 between captured kernels, so an output that still sits in L2
@@ -515,7 +515,7 @@ def main():
         qf = step_flops_per_token(cfg, T, 1, qwl["lora"], 8)
         qv = qwl["B"] * qwl["T"] * world / (qlora["step_ms"] * 1e-3) if not args.batch else \
             N * world / (qlora["step_ms"] * 1e-3)
-        line["north_star_qlora"] = {
+        line["qlora_step"] = {
             "workload": "smollm2_qlora_b8_t512", "lora": "q,v rank 8 alpha 16 over a frozen Q8_0 base",
             "q8_ring_l2_resident": bool(args.q8_ring_l2),
             "value": qv, "unit": "tokens/s", "ms_per_step": qlora["step_ms"], "steps": args.steps,
